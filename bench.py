@@ -1,0 +1,231 @@
+"""Benchmark: FerrisBoost training on B200, seconds per 100 boosting rounds.
+
+Workload (the config the metric is quoted on):
+11,000,000 rows x 28 f32 features ~ N(0,1) from seed 0, labels
+~ Bernoulli(sigmoid(w.x + 0.5 x0 x1 - 0.3 x2^2)); binary:logistic,
+max_bin=256, depthwise max_depth=8, eta=0.1, gpu_math="exact".  A step is one
+boosting round over the resident quantized data.  Synthetic data of the
+config's shape stands in for HIGGS (not in this container).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--rows R]
+
+value: exact-mode s/100 rounds from CUDA events on the training stream (bins
+resident in HBM; the per-round exact-mode host step — margins D2H, glibc
+expf, exp values H2D — is inside the interval).  e2e: the same metric through
+the public train() call from host arrays (sketch, quantization, H2D of the
+bins and labels, K rounds, model download), normalised per 100 rounds.
+cpu_baseline / --impl reference: the C++ restatement of the reference CPU
+engine (oracle/), all host threads, bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_FEATURES = 28
+PARAMS = {"objective": "binary:logistic", "max_depth": 8, "eta": 0.1, "lambda": 1.0, "max_bin": 256}
+
+
+def make_data(n, seed=0):
+    """configs[0]/[1] generator."""
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, N_FEATURES), dtype=np.float32)
+    w = rng.standard_normal(N_FEATURES)
+    z = X @ w + 0.5 * X[:, 0].astype(np.float64) * X[:, 1] - 0.3 * X[:, 2].astype(np.float64) ** 2
+    y = (rng.random(n) < 1.0 / (1.0 + np.exp(-z))).astype(np.float32)
+    return X, y
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device=0):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_threads():
+    return len(os.sched_getaffinity(0))
+
+
+def reference_rounds(X, y, rounds, warmup):
+    """Oracle (C++ restatement of the reference CPU engine) on the workload:
+    per-round wall seconds of rounds after `warmup`, all host threads."""
+    from oracle import RefCPU
+    rc = RefCPU()
+    rc.train(X, y, n_rounds=warmup + rounds, nthread=0, **PARAMS)
+    setup, per_round = rc.last_timing()
+    return setup, per_round[warmup:]
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    X, y = make_data(args.rows)
+    setup, rs = reference_rounds(X, y, args.steps, args.warmup)
+    s100 = float(np.mean(rs)) * 100.0
+    line = {
+        "metric": "train s/100 rounds", "value": round(s100, 4), "unit": "s/100 rounds", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * float(np.mean(rs)), 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "configs[1] binary:logistic 11M x 28, depth 8, max_bin 256, eta 0.1",
+                   "rows": args.rows, "features": N_FEATURES},
+        "cpu_baseline": {"value": round(s100, 4), "unit": "s/100 rounds", "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{args.steps} timed rounds after {args.warmup} warm-up rounds on the full "
+                                   f"{args.rows}-row workload; setup {setup:.2f} s not included"},
+        "e2e": {"value": round(s100, 4), "unit": "s/100 rounds", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world):
+    import ferrisboost_b200 as fb
+    if world > 1:
+        raise SystemExit("multi-GPU row sharding is not wired into bench.py yet")
+    device = int(os.environ.get("LOCAL_RANK", "0"))
+    t0 = time.perf_counter()
+    X, y = make_data(args.rows)
+    gen_s = time.perf_counter() - t0
+    p = dict(PARAMS, device=f"cuda:{device}")
+
+    # e2e: the public train() from host arrays, K rounds
+    t0 = time.perf_counter()
+    m = fb.train(p, X, label=y, num_boost_round=args.steps)
+    e2e_s = time.perf_counter() - t0
+    json_bytes = len(m.to_json())
+    del m
+
+    # device-resident steps
+    t0 = time.perf_counter()
+    ds = fb.Dataset(X, max_bin=p["max_bin"])
+    sketch_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    b = fb.Booster(p, ds, y)
+    upload_s = time.perf_counter() - t0
+    b.update(args.warmup)
+    b.set_stats(True)
+    with ClockSampler(device) as clk:
+        b.update(args.steps)
+    t = b.timing()
+    ms_step = t["device_ms"] / args.steps
+    s100 = ms_step * 100.0 / 1000.0
+
+    fast = fb.Booster(dict(p, gpu_math="fast"), ds, y)
+    fast.update(args.warmup)
+    fast.update(args.steps)
+    tf = fast.timing()
+
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    launches = max(t["hist_launches"], 1.0)
+    hist_gbs = t["hist_bytes"] / (t["hist_ms"] / 1000.0) / 1e9 if t["hist_ms"] > 0 else None
+
+    n = args.rows
+    bins_bytes = n * 64
+    line = {
+        "metric": "train s/100 rounds", "value": round(s100, 4), "unit": "s/100 rounds", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": "configs[1] binary:logistic 11M x 28, depth 8, max_bin 256, eta 0.1, gpu_math exact",
+                   "rows": n, "features": N_FEATURES, "l2": "inputs larger than L2 (bins 704 MB, gradients 176 MB)"},
+        "e2e": {"value": round(e2e_s / args.steps * 100.0, 4), "unit": "s/100 rounds",
+                "h2d_bytes_per_step": int((bins_bytes + 4 * n) / args.steps + 4 * n),
+                "d2h_bytes_per_step": int(4 * n + json_bytes / args.steps),
+                "includes": "sketch + quantize + upload + K rounds + model JSON, public train()"},
+        "gpu_launches": int(t["trees"] and (9 + 8 * 9) * args.steps),
+        "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": round(hist_gbs / hbm_peak, 4) if hist_gbs else None,
+                     "traffic": None, "kernel": "k_hist (histogram)",
+                     "per_launch_ms": round(t["hist_ms"] / launches, 4),
+                     "alg_bytes_per_launch": int(t["hist_bytes"] / launches), "peak_source": peak_src},
+        "clocks": clk.summary(),
+        "breakdown": {"hist_share_of_device": round(t["hist_ms"] / t["device_ms"], 4) if t["device_ms"] else None,
+                      "host_gradient_ms_per_step": round(t["gradient_ms"] / args.steps, 3),
+                      "fast_mode_s_per_100_rounds": round(tf["device_ms"] / args.steps * 100 / 1000, 4),
+                      "setup_s": {"datagen": round(gen_s, 2), "sketch_quantize": round(sketch_s, 2),
+                                  "upload": round(upload_s, 2)}},
+    }
+    if rank == 0 and not args.no_cpu:
+        csteps = 2
+        setup, rs = reference_rounds(X, y, csteps, 1)
+        line["cpu_baseline"] = {"value": round(float(np.mean(rs)) * 100, 4), "unit": "s/100 rounds",
+                                "cores": cpu_threads(), "kind": "port",
+                                "sample": f"{csteps} rounds after 1 warm-up round on the full {n}-row workload "
+                                          f"(oracle C++ restatement, all host threads)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=11_000_000)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,388 @@
+"""ferrisboost_b200 — FerrisBoost's training and explanation engine on B200.
+
+Drop-in for the reference's Python entry points (python/ferrisboost/__init__.py
+of mdai001/FerrisBoost): ``train(params, data, label=..., num_boost_round=...)``
+returns a ``Model`` with ``predict(..., output_margin, pred_contribs)``,
+``save_model`` and the XGBoost-compatible JSON.  Parameters use the
+reference's names, aliases and defaults; unknown names raise ``ValueError``.
+
+Every training, prediction and SHAP call runs on a CUDA device through the
+in-tree library libfbgpu.so (C ABI in include/fbgpu.h and include/fb_engine.h):
+there is no CPU execution path, and a missing library or device raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import math
+import os
+from typing import Any, Mapping, Sequence
+
+import numpy as np
+
+from . import _lib
+
+__all__ = ["train", "Model", "Booster", "Dataset", "build", "lib"]
+
+_DEFAULTS: dict[str, Any] = {  # python/ferrisboost/__init__.py:47-157 (the subset this engine runs)
+    "objective": "binary:logistic",
+    "max_depth": 6,
+    "max_leaves": 0,
+    "grow_policy": "depthwise",
+    "max_bin": 255,
+    "eta": 0.3,
+    "lambda": 1.0,
+    "gamma": 0.0,
+    "alpha": 0.0,
+    "max_delta_step": None,
+    "scale_pos_weight": 1.0,
+    "min_child_weight": 1.0,
+    "subsample": 1.0,
+    "sampling_method": "uniform",
+    "colsample_bytree": 1.0,
+    "colsample_bylevel": 1.0,
+    "colsample_bynode": 1.0,
+    "cols_per_block": None,
+    "nthread": 0,
+    "hist_streams": None,
+    "resident_blocks": None,
+    "hist_nodes_per_batch": None,
+    "gpu_math": None,
+    "device": None,
+    "gpu_memory_budget": None,
+    "device_quantize": None,
+    "seed": 0,
+    "base_score": None,
+    "monotone_constraints": None,
+    "enable_categorical": False,
+    "missing": float("nan"),
+    "max_cat_to_onehot": 4,
+    "max_cat_threshold": 64,
+}
+_ALIASES = {  # python/ferrisboost/__init__.py:160-167
+    "learning_rate": "eta",
+    "reg_lambda": "lambda",
+    "reg_alpha": "alpha",
+    "n_jobs": "nthread",
+    "random_state": "seed",
+}
+# Accepted for drop-in compatibility; the device planner owns these choices
+# (every configuration is resident in HBM), so their values do not change the model.
+_PLANNER_OWNED = ("cols_per_block", "hist_streams", "resident_blocks", "hist_nodes_per_batch", "gpu_memory_budget",
+                  "device_quantize")
+_OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1}
+
+
+def lib():
+    return _lib.load()
+
+
+def build(force: bool = False):
+    """Compile libfbgpu.so in-tree (nvcc, sm_100a)."""
+    from .build import build as _build
+    return _build(force=force)
+
+
+def _err() -> str:
+    return (lib().fb_last_error() or b"").decode()
+
+
+def _normalize_params(params: Mapping[str, Any], num_boost_round: int) -> dict[str, Any]:
+    """Reference python/ferrisboost/__init__.py:180-323 rules for this engine's parameters."""
+    out = dict(_DEFAULTS)
+    for key, value in dict(params).items():
+        canon = _ALIASES.get(key, key)
+        if canon not in _DEFAULTS:
+            known = ", ".join(sorted(_DEFAULTS) + sorted(_ALIASES))
+            raise ValueError(f"unknown parameter {key!r}; supported parameters: {known}")
+        out[canon] = value
+    if out["objective"] not in _OBJECTIVES:
+        raise ValueError(f"objective {out['objective']!r} is not supported on this engine; supported objectives: "
+                         f"{', '.join(_OBJECTIVES)}")
+    if not 0 < int(out["max_bin"]) <= 65535:
+        raise ValueError(f"max_bin must be in 1..=65535, got {out['max_bin']}")
+    if num_boost_round < 1:
+        raise ValueError(f"num_boost_round must be >= 1, got {num_boost_round}")
+    for key in ("max_depth", "max_leaves", "max_bin", "nthread", "seed", "max_cat_to_onehot", "max_cat_threshold"):
+        out[key] = int(out[key])
+    if out["max_leaves"] < 0:
+        raise ValueError(f"max_leaves must be >= 0, got {out['max_leaves']}")
+    if not 0 <= out["max_depth"] <= 14:
+        raise ValueError(f"max_depth must be in 0..=14, got {out['max_depth']}; 0 means a root-only tree")
+    if out["grow_policy"] not in ("depthwise", "lossguide"):
+        raise ValueError(f"grow_policy must be depthwise or lossguide, got {out['grow_policy']!r}")
+    if out["sampling_method"] != "uniform":
+        raise ValueError("sampling_method must be uniform on this engine")
+    for key in ("colsample_bylevel", "colsample_bynode"):
+        if float(out[key]) != 1.0:
+            raise ValueError(f"{key} < 1 is not supported on this engine")
+    gm = out["gpu_math"] or "exact"
+    if gm not in ("exact", "fast"):
+        raise ValueError(f'gpu_math must be "exact" or "fast", got {gm!r}')
+    out["gpu_math"] = gm
+    dev = out["device"]
+    if dev is None or dev in ("cuda", "gpu"):
+        out["device_index"] = 0
+    elif isinstance(dev, str) and dev.startswith("cuda:"):
+        out["device_index"] = int(dev.split(":", 1)[1])
+    elif dev == "cpu":
+        raise ValueError('device="cpu": this engine runs on CUDA devices only; use "cuda" or "cuda:N"')
+    else:
+        raise ValueError(f'device must be "cuda" or "cuda:N", got {dev!r}')
+    for key in ("eta", "lambda", "gamma", "min_child_weight", "alpha", "scale_pos_weight", "subsample",
+                "colsample_bytree"):
+        out[key] = float(out[key])
+        if not math.isfinite(out[key]) or out[key] < 0:
+            raise ValueError(f"{key} must be finite and non-negative")
+    if not 0.0 < out["subsample"] <= 1.0:
+        raise ValueError(f"subsample must be in (0, 1], got {out['subsample']}")
+    if not 0.0 < out["colsample_bytree"] <= 1.0:
+        raise ValueError(f"colsample_bytree must be in (0, 1], got {out['colsample_bytree']}")
+    out["max_delta_step"] = 0.0 if out["max_delta_step"] is None else float(out["max_delta_step"])
+    if out["base_score"] is not None:
+        out["base_score"] = float(out["base_score"])
+    for key in ("max_cat_to_onehot", "max_cat_threshold"):
+        if out[key] < 1:
+            raise ValueError(f"{key} must be >= 1, got {out[key]}")
+    mc = out["monotone_constraints"]
+    if isinstance(mc, str):
+        mc = [int(t) for t in mc.strip("()[] ").split(",") if t.strip()]
+    if mc is not None:
+        mc = [int(np.sign(v)) for v in mc]
+    out["monotone_constraints"] = mc
+    out["num_boost_round"] = int(num_boost_round)
+    return out
+
+
+def _fb_params(p: Mapping[str, Any]) -> _lib.FbParams:
+    fp = _lib.FbParams()
+    lib().fb_default_params(C.byref(fp))
+    fp.objective = _OBJECTIVES[p["objective"]]
+    fp.grow_policy = 1 if p["grow_policy"] == "lossguide" else 0
+    fp.max_depth = p["max_depth"]
+    fp.max_leaves = p["max_leaves"]
+    fp.max_bin = p["max_bin"]
+    fp.eta = p["eta"]
+    fp.reg_lambda = p["lambda"]
+    fp.gamma = p["gamma"]
+    fp.min_child_weight = p["min_child_weight"]
+    fp.alpha = p["alpha"]
+    fp.max_delta_step = p["max_delta_step"]
+    fp.scale_pos_weight = p["scale_pos_weight"]
+    fp.subsample = p["subsample"]
+    fp.colsample_bytree = p["colsample_bytree"]
+    fp.base_score = float("nan") if p["base_score"] is None else p["base_score"]
+    fp.seed = p["seed"]
+    fp.max_cat_to_onehot = p["max_cat_to_onehot"]
+    fp.max_cat_threshold = p["max_cat_threshold"]
+    fp.nthread = p["nthread"]
+    fp.gpu_math = 1 if p["gpu_math"] == "fast" else 0
+    fp.device = p["device_index"]
+    return fp
+
+
+def _as_matrix(x: Any, missing: float = float("nan")) -> np.ndarray:
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    if a.ndim != 2:
+        raise ValueError(f"data must be a 2-D array, got shape {a.shape}")
+    if not math.isnan(missing):
+        a = np.where(a == np.float32(missing), np.float32("nan"), a).astype(np.float32)
+    return a
+
+
+def _feature_flags(feature_types: Sequence[str] | None, n: int) -> np.ndarray | None:
+    if feature_types is None:
+        return None
+    ft = list(feature_types)
+    if len(ft) != n:
+        raise ValueError(f"feature_types has {len(ft)} entries, the data has {n} features")
+    bad = [t for t in ft if t not in ("c", "q", "float", "int", "i")]
+    if bad:
+        raise ValueError(f"feature_types entries must be 'c' or 'q', got {bad[0]!r}")
+    flags = np.array([t == "c" for t in ft], dtype=np.uint8)
+    return flags if flags.any() else None
+
+
+class Dataset:
+    """Quantized training data: cuts from the weighted quantile sketch and
+    column blocks of u8/u16 bins (the reference's DenseSource)."""
+
+    def __init__(self, data: Any, max_bin: int = 255, weight: Any = None, feature_types=None, nthread: int = 0,
+                 missing: float = float("nan")):
+        X = _as_matrix(data, missing)
+        self.n_rows, self.n_features = X.shape
+        w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+        cat = _feature_flags(feature_types, self.n_features)
+        self.categorical = cat
+        self._h = lib().fb_dataset_from_dense(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
+                                              _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), nthread)
+        if not self._h:
+            raise ValueError(_err())
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            lib().fb_dataset_free(h)
+            self._h = None
+
+    def cuts(self):
+        n = lib().fb_dataset_cuts(self._h, None, None, 0)
+        cuts = np.zeros(max(n, 1), dtype=np.float32)
+        off = np.zeros(self.n_features + 1, dtype=np.uint32)
+        lib().fb_dataset_cuts(self._h, _lib.ptr(cuts, C.c_float), _lib.ptr(off, C.c_uint32), n)
+        return cuts[:n], off
+
+    def column(self, f: int) -> np.ndarray:
+        out = np.zeros(self.n_rows, dtype=np.uint16)
+        if lib().fb_dataset_column(self._h, f, _lib.ptr(out, C.c_uint16)):
+            raise IndexError(f)
+        return out
+
+
+class Booster:
+    """A training run on one CUDA device; ``update(k)`` adds k trees."""
+
+    def __init__(self, params: Mapping[str, Any], dataset: Dataset, label: Any, weight: Any = None):
+        p = _normalize_params(params, 1)
+        y = np.ascontiguousarray(label, dtype=np.float32)
+        if y.shape != (dataset.n_rows,):
+            raise ValueError(f"label has shape {y.shape}, expected ({dataset.n_rows},)")
+        w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+        self.params = p
+        fp = _fb_params(p)
+        mono = None
+        if p["monotone_constraints"] is not None:
+            mc = p["monotone_constraints"]
+            if len(mc) > dataset.n_features:
+                raise ValueError(f"monotone_constraints has {len(mc)} entries, but there are only "
+                                 f"{dataset.n_features} features")
+            mono = np.zeros(dataset.n_features, dtype=np.int8)
+            mono[:len(mc)] = mc
+            fp.monotone = _lib.ptr(mono, C.c_int8)
+        self._keep = (y, w, mono, dataset)
+        self._h = lib().fb_booster_create(dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), C.byref(fp))
+        if not self._h:
+            raise ValueError(_err())
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            lib().fb_booster_free(h)
+            self._h = None
+
+    def update(self, n_rounds: int = 1) -> None:
+        if lib().fb_booster_update(self._h, n_rounds):
+            raise RuntimeError(_err())
+
+    def set_stats(self, on: bool = True) -> None:
+        lib().fb_booster_set_stats(self._h, int(on))
+
+    def timing(self) -> dict:
+        t = np.zeros(8, dtype=np.float64)
+        lib().fb_booster_timing(self._h, _lib.ptr(t, C.c_double))
+        keys = ("wall_ms", "gradient_ms", "tree_ms", "device_ms", "hist_ms", "hist_launches", "hist_bytes", "trees")
+        return {k: float(v) for k, v in zip(keys, t)}
+
+    def margins(self) -> np.ndarray:
+        n = self._keep[3].n_rows
+        out = np.zeros(n, dtype=np.float32)
+        if lib().fb_booster_margins(self._h, _lib.ptr(out, C.c_float)):
+            raise RuntimeError(_err())
+        return out
+
+    def model(self) -> "Model":
+        m = Model(lib().fb_booster_model(self._h), self.params)
+        return m
+
+
+class Model:
+    """A trained model (the reference's ``Model``)."""
+
+    def __init__(self, handle, params: Mapping[str, Any] | None = None):
+        if not handle:
+            raise RuntimeError(_err())
+        self._h = handle
+        self.params = dict(params or {})
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            lib().fb_model_free(h)
+            self._h = None
+
+    @property
+    def num_trees(self) -> int:
+        return lib().fb_model_num_trees(self._h)
+
+    @property
+    def n_features(self) -> int:
+        return lib().fb_model_num_features(self._h)
+
+    def _device(self, device=None) -> int:
+        d = device if device is not None else self.params.get("device")
+        if d is None or d in ("cuda", "gpu"):
+            return int(self.params.get("device_index", 0))
+        if isinstance(d, int):
+            return d
+        return int(str(d).split(":", 1)[1])
+
+    def to_json(self) -> bytes:
+        n = lib().fb_model_json(self._h, None, 0)
+        buf = C.create_string_buffer(n)
+        lib().fb_model_json(self._h, buf, n)
+        return buf.raw[:n]
+
+    def save_model(self, path: str | os.PathLike) -> None:
+        """XGBoost-compatible JSON (reference src/model/model_io.rs: atomic write)."""
+        path = os.fspath(path)
+        tmp = path + ".tmp"
+        with open(tmp, "wb") as f:
+            f.write(self.to_json())
+        os.replace(tmp, path)
+
+    def tree(self, t: int) -> dict:
+        n = lib().fb_model_tree(self._h, t, *([None] * 10))
+        if n < 0:
+            raise IndexError(t)
+        a = {"left": np.zeros(n, np.int32), "right": np.zeros(n, np.int32), "feat": np.zeros(n, np.uint32),
+             "cond": np.zeros(n, np.float32), "default_left": np.zeros(n, np.uint8), "leaf": np.zeros(n, np.float32),
+             "is_leaf": np.zeros(n, np.uint8), "gain": np.zeros(n, np.float32), "hess": np.zeros(n, np.float32),
+             "cats": np.zeros((n, 8), np.uint32)}
+        ct = [C.c_int32, C.c_int32, C.c_uint32, C.c_float, C.c_uint8, C.c_float, C.c_uint8, C.c_float, C.c_float,
+              C.c_uint32]
+        lib().fb_model_tree(self._h, t, *[_lib.ptr(v, c) for v, c in zip(a.values(), ct)])
+        return a
+
+    def predict(self, data: Any, output_margin: bool = False, pred_contribs: bool = False, device=None):
+        """Predictions (probabilities for binary:logistic unless output_margin),
+        or SHAP contributions n x (F+1) with the bias last (pred_contribs)."""
+        X = _as_matrix(data, self.params.get("missing", float("nan")))
+        if X.shape[1] != self.n_features:
+            raise ValueError(f"data has {X.shape[1]} features, the model has {self.n_features}")
+        dev = self._device(device)
+        if pred_contribs:
+            out = np.zeros((X.shape[0], X.shape[1] + 1), dtype=np.float32)
+            if lib().fb_model_shap(self._h, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float), dev):
+                raise RuntimeError(_err())
+            return out
+        out = np.zeros(X.shape[0], dtype=np.float32)
+        if lib().fb_model_predict(self._h, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float), dev):
+            raise RuntimeError(_err())
+        if output_margin or self.params.get("objective", "binary:logistic") != "binary:logistic":
+            return out
+        return (1.0 / (1.0 + np.exp(-out.astype(np.float64)))).astype(np.float32)
+
+
+def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
+          feature_types: Sequence[str] | None = None, quiet: bool = True) -> Model:
+    """Train a model (reference python/ferrisboost/__init__.py:1090 ``train``)."""
+    p = _normalize_params(params, num_boost_round)
+    if label is None:
+        raise ValueError("label is required for array input")
+    ds = Dataset(data, max_bin=p["max_bin"], weight=weight, feature_types=feature_types, nthread=p["nthread"],
+                 missing=p["missing"])
+    b = Booster(params, ds, label, weight)
+    b.update(num_boost_round)
+    m = b.model()
+    m.params = p
+    return m

@@ -1,0 +1,918 @@
+// Training context, explanation model and the C ABI of include/fbgpu.h.
+#include "ctx.h"
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+
+namespace fbg {
+
+namespace {
+thread_local std::string g_last_error;
+
+uint32_t ceil_div(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
+}  // namespace
+
+double pow2_scale_host(double max_abs, uint64_t n_rows) {
+    if (!(max_abs > 0.0) || !std::isfinite(max_abs)) return 1.0;
+    double budget = (double)(1ull << 62) / (double)(n_rows > 0 ? n_rows : 1);
+    double raw = budget / max_abs;
+    if (!std::isfinite(raw) || raw <= 0.0) return 1.0;
+    double l = std::floor(std::log2(raw));
+    int k = l >= 2147483647.0 ? 2147483647 : (l <= -2147483648.0 ? (-2147483647 - 1) : (int)l);
+    k = std::min(1000, std::max(-1000, k));
+    return std::ldexp(1.0, k);
+}
+
+// ======================================================================= TrainCtx
+TrainCtx::TrainCtx(const fbgpu_config& cfg) : cfg_(cfg) {
+    if (cfg.n_features == 0) throw InputError("training data must have at least one feature");
+    if (cfg.n_rows > 0xffffffffull) throw InputError("a shard holds at most 2^32 - 1 rows (u32 row ids)");
+    if (cfg.max_depth > 14) throw InputError("max_depth must be in 0..=14");
+    FB_CUDA_CHECK(cudaSetDevice(cfg.device));
+    FB_CUDA_CHECK(cudaStreamCreateWithFlags(&s_, cudaStreamNonBlocking));
+    FB_CUDA_CHECK(cudaEventCreate(&ev0_));
+    FB_CUDA_CHECK(cudaEventCreate(&ev1_));
+    for (auto& e : hev_) FB_CUDA_CHECK(cudaEventCreate(&e));
+    level_stats_.alloc(16 * 16);
+    n_ = cfg.n_rows;
+    F_ = cfg.n_features;
+    if (cfg_.n_rows_global == 0) cfg_.n_rows_global = n_;
+    smem_budget_ = cfg.hist_smem_bytes ? (int)cfg.hist_smem_bytes : 200 * 1024;
+    feat_block_.assign(F_, -1);
+    feat_byte_.assign(F_, 0);
+    label_.alloc(n_ * 4);
+    weight_.alloc(16);
+    pred_.alloc(n_ * 4);
+    gpair_f32_.alloc(n_ * 8);
+    host_exp_.alloc(n_ * 4);
+    fixed_.alloc(n_ * 16);
+    sums_.alloc(64);
+    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 64, s_));
+    FB_CUDA_CHECK(cudaMemsetAsync(pred_.p, 0, n_ * 4, s_));
+    ensure_tree_buffers(cfg.max_depth, cfg.max_leaves);
+}
+
+TrainCtx::~TrainCtx() {
+    if (s_) cudaStreamSynchronize(s_);
+    if (ev0_) cudaEventDestroy(ev0_);
+    if (ev1_) cudaEventDestroy(ev1_);
+    for (auto& e : hev_) if (e) cudaEventDestroy(e);
+    if (s_) cudaStreamDestroy(s_);
+}
+
+void TrainCtx::set_features(const uint32_t* n_bins, const uint8_t* width, const uint8_t* categorical) {
+    nbins_.assign(n_bins, n_bins + F_);
+    width_.assign(width, width + F_);
+    cat_.assign(F_, 0);
+    has_cat_ = false;
+    if (categorical) {
+        for (uint32_t f = 0; f < F_; f++) {
+            cat_[f] = categorical[f] ? 1 : 0;
+            has_cat_ |= cat_[f] != 0;
+        }
+    }
+    hoff_.assign(F_ + 1, 0);
+    for (uint32_t f = 0; f < F_; f++) {
+        if (width_[f] != 1 && width_[f] != 2) throw InputError("bin width must be 1 or 2 bytes");
+        if (nbins_[f] == 0) throw InputError("a feature has at least one bin");
+        if (nbins_[f] > 1024) throw InputError("device split search supports at most 1024 bins per feature");
+        if (cat_[f] && nbins_[f] > 256) throw InputError("device categorical splits support at most 256 categories");
+        hoff_[f + 1] = hoff_[f] + nbins_[f];
+    }
+    total_bins_ = hoff_[F_];
+    d_hoff_.alloc(4 * (F_ + 1));
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_hoff_.p, hoff_.data(), 4 * (F_ + 1), cudaMemcpyHostToDevice, s_));
+    d_cat_.alloc(F_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_cat_.p, cat_.data(), F_, cudaMemcpyHostToDevice, s_));
+    d_enabled_.alloc(F_);
+    d_mono_.alloc(F_);
+    FB_CUDA_CHECK(cudaMemsetAsync(d_mono_.p, 0, F_, s_));
+    d_floc_.alloc(sizeof(FeatLoc) * F_);
+    tiles_valid_ = false;
+    buf_depth_ = 0xffffffffu;  // histogram slots depend on total_bins
+    ensure_tree_buffers(cfg_.max_depth, cfg_.max_leaves);
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void TrainCtx::ensure_features() const {
+    if (nbins_.empty()) throw InputError("fbgpu_set_features must be called before training");
+    for (uint32_t f = 0; f < F_; f++)
+        if (feat_block_[f] < 0) throw InputError("feature " + std::to_string(f) + " has no uploaded column block");
+}
+
+void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const void* data) {
+    if (nbins_.empty()) throw InputError("fbgpu_set_features must be called before fbgpu_upload_block");
+    if (width != 1 && width != 2) throw InputError("bin width must be 1 or 2 bytes");
+    if (n_feats == 0) throw InputError("a column block holds at least one feature");
+    auto b = std::make_unique<Block>();
+    b->feats.assign(feat_ids, feat_ids + n_feats);
+    for (uint32_t i = 0; i < n_feats; i++) {
+        uint32_t f = feat_ids[i];
+        if (f >= F_) throw InputError("block feature id out of range");
+        if (width_[f] != width) throw InputError("a column block must hold features of its own bin width");
+        if (i && f <= feat_ids[i - 1]) throw InputError("block feature ids must be ascending");
+        if (feat_block_[f] >= 0) throw InputError("feature uploaded twice");
+    }
+    b->width = width;
+    b->stride = ((n_feats * width + 15) / 16) * 16;
+    b->data.alloc((size_t)n_ * b->stride + 16);
+    FB_CUDA_CHECK(cudaMemsetAsync(b->data.p, 0, (size_t)n_ * b->stride + 16, s_));
+    // column-major host block -> staging -> row-major records, in row slabs
+    const uint64_t slab = std::max<uint64_t>(1, std::min<uint64_t>(n_, (256ull << 20) / ((uint64_t)n_feats * width)));
+    DevMem stage;
+    stage.alloc(slab * n_feats * width);
+    std::vector<uint8_t> host;
+    host.resize(slab * n_feats * width);
+    const uint8_t* src = static_cast<const uint8_t*>(data);
+    for (uint64_t r0 = 0; r0 < n_; r0 += slab) {
+        uint64_t rows = std::min(slab, n_ - r0);
+        for (uint32_t i = 0; i < n_feats; i++)
+            std::memcpy(host.data() + (size_t)i * rows * width, src + ((size_t)i * n_ + r0) * width, rows * width);
+        FB_CUDA_CHECK(cudaMemcpyAsync(stage.p, host.data(), rows * n_feats * width, cudaMemcpyHostToDevice, s_));
+        launch_transpose((int)width, stage.as<uint8_t>(), b->data.as<uint8_t>(), (uint32_t)rows, n_feats, b->stride,
+                         r0, s_);
+        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    }
+    std::vector<FeatLoc> floc(F_);
+    const int bi = (int)blocks_.size();
+    for (uint32_t i = 0; i < n_feats; i++) {
+        feat_block_[feat_ids[i]] = bi;
+        feat_byte_[feat_ids[i]] = i * width;
+    }
+    blocks_.push_back(std::move(b));
+    for (uint32_t f = 0; f < F_; f++) {
+        if (feat_block_[f] < 0) { floc[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
+        const Block& blk = *blocks_[feat_block_[f]];
+        floc[f] = FeatLoc{blk.data.as<uint8_t>(), blk.stride, feat_byte_[f], blk.width, blk.width == 2 ? 65535u : 255u};
+    }
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_.p, floc.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    tiles_valid_ = false;
+}
+
+void TrainCtx::set_labels(const float* labels, const float* weights, const float* base_rows, float base_margin) {
+    FB_CUDA_CHECK(cudaMemcpyAsync(label_.p, labels, n_ * 4, cudaMemcpyHostToDevice, s_));
+    has_weight_ = weights != nullptr;
+    if (weights) {
+        weight_.alloc(n_ * 4);
+        FB_CUDA_CHECK(cudaMemcpyAsync(weight_.p, weights, n_ * 4, cudaMemcpyHostToDevice, s_));
+    }
+    if (base_rows) {
+        FB_CUDA_CHECK(cudaMemcpyAsync(pred_.p, base_rows, n_ * 4, cudaMemcpyHostToDevice, s_));
+    } else {
+        std::vector<float> v(n_, base_margin);
+        FB_CUDA_CHECK(cudaMemcpyAsync(pred_.p, v.data(), n_ * 4, cudaMemcpyHostToDevice, s_));
+        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    }
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+GradArgs TrainCtx::grad_args() const {
+    GradArgs a{};
+    a.n = (uint32_t)n_;
+    a.row0 = cfg_.row_offset;
+    a.sub_th = ~0ull;
+    a.label = label_.as<float>();
+    a.weight = has_weight_ ? weight_.as<float>() : nullptr;
+    a.pred = pred_.as<float>();
+    a.host_exp = host_exp_.as<float>();
+    a.gpair_in = gpair_f32_.as<float>();
+    a.gpair_f32 = gpair_f32_.as<float>();
+    a.fixed = fixed_.as<Pair>();
+    a.sum = sums_.as<unsigned long long>();
+    a.maxbits = sums_.as<unsigned long long>() + 2;
+    a.scales = reinterpret_cast<const double*>(sums_.as<unsigned long long>() + 4);
+    return a;
+}
+
+void TrainCtx::upload_and_quantize(const float* gpair, uint64_t th, uint64_t seed, uint64_t tree,
+                                   double* scales_out, int64_t* sum_out) {
+    FB_CUDA_CHECK(cudaMemcpyAsync(gpair_f32_.p, gpair, n_ * 8, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 32, s_));
+    GradArgs a = grad_args();
+    a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
+    launch_mask_max(a, s_);
+    unsigned long long mb[2];
+    FB_CUDA_CHECK(cudaMemcpyAsync(mb, sums_.as<unsigned long long>() + 2, 16, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    double mg, mh;
+    std::memcpy(&mg, &mb[0], 8);
+    std::memcpy(&mh, &mb[1], 8);
+    if (!std::isfinite(mg) || !std::isfinite(mh))
+        throw InputError("non-finite gradient or Hessian (or invalid bounds); reduce extreme labels, weights, "
+                         "base_score or objective parameters");
+    double sc[2] = {pow2_scale_host(mg, cfg_.n_rows_global), pow2_scale_host(mh, cfg_.n_rows_global)};
+    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, sc, 16, cudaMemcpyHostToDevice, s_));
+    launch_quantize(a, s_);
+    if (scales_out) { scales_out[0] = sc[0]; scales_out[1] = sc[1]; }
+    if (sum_out) {
+        FB_CUDA_CHECK(cudaMemcpyAsync(sum_out, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
+    }
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void TrainCtx::upload_fixed(const int64_t* fixed, const double* scales, const int64_t* sum) {
+    FB_CUDA_CHECK(cudaMemcpyAsync(fixed_.p, fixed, n_ * 16, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, sum, 16, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, scales, 16, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void TrainCtx::round_from_exp(int objective, const float* host_exp, uint64_t th, uint64_t seed, uint64_t tree,
+                              const double* scales) {
+    if (host_exp) FB_CUDA_CHECK(cudaMemcpyAsync(host_exp_.p, host_exp, n_ * 4, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, scales, 16, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 16, s_));
+    GradArgs a = grad_args();
+    a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
+    a.objective = objective;
+    launch_gradient_quantize_exp(a, s_);
+}
+
+void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
+                            int64_t* sum_out) {
+    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 32, s_));
+    GradArgs a = grad_args();
+    a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
+    a.objective = objective;
+    if (!fast && objective == 1)
+        throw InputError("exact logistic gradients need the host exp (fbgpu_round_from_exp)");
+    launch_gradient_max(a, fast, s_);
+    double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
+    if (fast) {
+        launch_device_scales(a.maxbits, cfg_.n_rows_global, dscales, s_);
+    } else {
+        unsigned long long mb[2];
+        FB_CUDA_CHECK(cudaMemcpyAsync(mb, a.maxbits, 16, cudaMemcpyDeviceToHost, s_));
+        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+        double mg, mh;
+        std::memcpy(&mg, &mb[0], 8);
+        std::memcpy(&mh, &mb[1], 8);
+        if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
+        double sc[2] = {pow2_scale_host(mg, cfg_.n_rows_global), pow2_scale_host(mh, cfg_.n_rows_global)};
+        FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
+        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    }
+    launch_quantize(a, s_);
+    if (scales_out) FB_CUDA_CHECK(cudaMemcpyAsync(scales_out, dscales, 16, cudaMemcpyDeviceToHost, s_));
+    if (sum_out) FB_CUDA_CHECK(cudaMemcpyAsync(sum_out, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
+    if (scales_out || sum_out) FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
+    if (max_depth == buf_depth_ && max_leaves == buf_leaves_) return;
+    uint64_t lvl = 1ull << max_depth;                 // nodes of the deepest level
+    uint64_t split_nodes = max_depth ? (1ull << (max_depth - 1)) : 1;  // deepest split level
+    uint64_t acc = max_depth >= 2 ? (1ull << (max_depth - 2)) : 1;
+    if (max_leaves) {
+        lvl = std::min<uint64_t>(lvl, std::max<uint64_t>(max_leaves, 1));
+        split_nodes = std::min<uint64_t>(split_nodes, std::max<uint64_t>(max_leaves, 1));
+        acc = std::min<uint64_t>(acc, std::max<uint64_t>(max_leaves, 1));
+    }
+    uint64_t tree_nodes = (2ull << max_depth) - 1;
+    if (max_leaves) tree_nodes = std::min<uint64_t>(tree_nodes, 2ull * max_leaves + 1);
+    max_level_nodes_ = (uint32_t)lvl;
+    max_split_nodes_ = (uint32_t)split_nodes;
+    max_acc_ = (uint32_t)acc;
+    max_tree_nodes_ = (uint32_t)tree_nodes;
+    max_chunks_ = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_level_nodes_ + 1;
+    const uint64_t tb = std::max<uint64_t>(total_bins_, 1);
+    for (int i = 0; i < 2; i++) {
+        rows_[i].alloc(std::max<uint64_t>(n_, 1) * 4);
+        nodes_[i].alloc(sizeof(NodeInfo) * lvl);
+        acc_list_[i].alloc(4 * (lvl + 1));
+        acc_prefix_[i].alloc(8 * (lvl + 2));
+        chunk_prefix_[i].alloc(4 * (lvl + 2));
+        hist_[i].alloc(16 * tb * split_nodes);
+    }
+    hist_acc_.alloc(16 * tb * acc);
+    feat_best_.alloc(sizeof(SplitRec) * split_nodes * F_);
+    feat_cats_.alloc(32 * split_nodes * F_);
+    node_best_.alloc(sizeof(SplitRec) * split_nodes);
+    node_cats_.alloc(32 * std::max<uint64_t>(lvl, 1));
+    FB_CUDA_CHECK(cudaMemsetAsync(node_cats_.p, 0, node_cats_.bytes, s_));
+    split_.alloc(sizeof(SplitDesc) * lvl);
+    chunk_left_.alloc(4 * (uint64_t)max_chunks_);
+    chunk_off_.alloc(4 * (uint64_t)max_chunks_);
+    node_left_.alloc(4 * lvl);
+    trec_.alloc(sizeof(TreeRec) * tree_nodes);
+    tcats_.alloc(32 * tree_nodes);
+    state_.alloc(sizeof(TreeState));
+    h_tree_.reserve(sizeof(TreeRec) * tree_nodes + 32 * tree_nodes + sizeof(TreeState));
+    buf_depth_ = max_depth;
+    buf_leaves_ = max_leaves;
+}
+
+// Histogram tiles: the enabled features of every block, greedily grouped so
+// that a tile's four 32-bit planes fit the shared-memory budget.
+void TrainCtx::plan_tiles(const uint8_t* enabled) {
+    std::vector<uint8_t> en(F_, 1);
+    if (enabled) for (uint32_t f = 0; f < F_; f++) en[f] = enabled[f] ? 1 : 0;
+    if (tiles_valid_ && en == last_enabled_) return;
+    std::vector<TileDesc> tiles[2];
+    std::vector<TileFeat> tf;
+    size_t smem = 0;
+    const uint32_t max_local = (uint32_t)((smem_budget_ - 64 * sizeof(TileFeat)) / 16);
+    for (int wpass = 1; wpass <= 2; wpass++) {
+        for (const auto& bp : blocks_) {
+            const Block& b = *bp;
+            if ((int)b.width != wpass) continue;
+            TileDesc cur{b.data.as<uint8_t>(), b.stride, b.width, (uint32_t)tf.size(), 0, 0, b.width == 2 ? 65535u : 255u};
+            auto flush = [&]() {
+                if (cur.n_feat == 0) return;
+                tiles[wpass - 1].push_back(cur);
+                smem = std::max(smem, (size_t)cur.local_bins * 16 + (size_t)cur.n_feat * sizeof(TileFeat));
+                cur.feat_begin = (uint32_t)tf.size();
+                cur.n_feat = 0;
+                cur.local_bins = 0;
+            };
+            for (uint32_t i = 0; i < b.feats.size(); i++) {
+                uint32_t f = b.feats[i];
+                if (!en[f]) continue;
+                if (cur.n_feat == 64 || cur.local_bins + nbins_[f] > max_local) flush();
+                tf.push_back(TileFeat{feat_byte_[f], cur.local_bins, nbins_[f], hoff_[f]});
+                cur.local_bins += nbins_[f];
+                cur.n_feat++;
+            }
+            flush();
+        }
+    }
+    n_tiles_w1_ = (uint32_t)tiles[0].size();
+    n_tiles_w2_ = (uint32_t)tiles[1].size();
+    std::vector<TileDesc> all = tiles[0];
+    all.insert(all.end(), tiles[1].begin(), tiles[1].end());
+    d_tiles_.alloc(sizeof(TileDesc) * std::max<size_t>(all.size(), 1));
+    d_tfeat_.alloc(sizeof(TileFeat) * std::max<size_t>(tf.size(), 1));
+    if (!all.empty())
+        FB_CUDA_CHECK(cudaMemcpyAsync(d_tiles_.p, all.data(), sizeof(TileDesc) * all.size(), cudaMemcpyHostToDevice, s_));
+    if (!tf.empty())
+        FB_CUDA_CHECK(cudaMemcpyAsync(d_tfeat_.p, tf.data(), sizeof(TileFeat) * tf.size(), cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_enabled_.p, en.data(), F_, cudaMemcpyHostToDevice, s_));
+    tile_smem_ = std::max<size_t>(smem, 16);
+    set_hist_smem_limit((int)tile_smem_);
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    last_enabled_ = en;
+    tiles_valid_ = true;
+}
+
+LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
+    LevelArgs a{};
+    a.n_features = F_;
+    a.max_leaves = tp.max_leaves;
+    a.sp = ScoreParams{tp.lambda, tp.gamma, tp.min_child_weight, tp.alpha, tp.max_delta_step, tp.eta, 1.0, 1.0};
+    a.scales = reinterpret_cast<const double*>(sums_.as<unsigned long long>() + 4);
+    a.hoff = d_hoff_.as<uint32_t>();
+    a.enabled = d_enabled_.as<uint8_t>();
+    a.mono = tp.monotone ? d_mono_.as<int8_t>() : nullptr;
+    a.is_cat = has_cat_ ? d_cat_.as<uint8_t>() : nullptr;
+    a.max_onehot = tp.max_cat_to_onehot;
+    a.max_cat_threshold = tp.max_cat_threshold;
+    a.floc = d_floc_.as<FeatLoc>();
+    a.st = state_.as<TreeState>();
+    a.hist_acc = hist_acc_.as<Pair>();
+    a.slot_pairs = std::max<uint64_t>(total_bins_, 1);
+    a.feat_best = feat_best_.as<SplitRec>();
+    a.feat_cats = feat_cats_.as<uint32_t>();
+    a.node_best = node_best_.as<SplitRec>();
+    a.node_cats = node_cats_.as<uint32_t>();
+    a.split = split_.as<SplitDesc>();
+    a.chunk_left = chunk_left_.as<uint32_t>();
+    a.chunk_off = chunk_off_.as<uint32_t>();
+    a.node_left = node_left_.as<uint32_t>();
+    a.node_left_global = node_left_.as<uint32_t>();
+    a.pred = pred_.as<float>();
+    a.trec = trec_.as<TreeRec>();
+    a.tcats = tcats_.as<uint32_t>();
+    return a;
+}
+
+void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out) {
+    ensure_features();
+    if (tp.max_depth > 14) throw InputError("max_depth must be in 0..=14");
+    if (tp.grow_policy != 0) throw InputError("grow_policy=lossguide is not available on the device path yet");
+    if (n_ == 0) throw InputError("training data must have at least one row");
+    ensure_tree_buffers(tp.max_depth, tp.max_leaves);
+    plan_tiles(enabled);
+    if (tp.monotone) {
+        std::vector<int8_t> m(tp.monotone, tp.monotone + F_);
+        if (m != last_mono_) {
+            FB_CUDA_CHECK(cudaMemcpyAsync(d_mono_.p, m.data(), F_, cudaMemcpyHostToDevice, s_));
+            last_mono_ = m;
+        }
+    }
+    LevelArgs a = level_args(tp);
+    const uint32_t maxd = tp.max_depth;
+    const uint32_t hist_grid = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(n_, 8192), 148 * 2));
+    FB_CUDA_CHECK(cudaEventRecord(ev0_, s_));
+    int cur = 0;
+    launch_iota(rows_[0].as<uint32_t>(), (uint32_t)n_, s_);
+    a.nodes = nodes_[0].as<NodeInfo>();
+    a.acc_list = acc_list_[0].as<uint32_t>();
+    a.acc_prefix = acc_prefix_[0].as<unsigned long long>();
+    a.chunk_prefix = chunk_prefix_[0].as<uint32_t>();
+    a.rows_cur = rows_[0].as<uint32_t>();
+    launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
+    for (uint32_t d = 0; d < maxd; d++) {
+        const uint32_t max_m = (uint32_t)std::min<uint64_t>(1ull << d, max_level_nodes_);
+        const uint32_t max_acc = d == 0 ? 1u : (uint32_t)std::min<uint64_t>(1ull << (d - 1), max_acc_);
+        a.depth = d;
+        a.last_level = d + 1 == maxd;
+        a.nodes = nodes_[cur].as<NodeInfo>();
+        a.next_nodes = nodes_[1 - cur].as<NodeInfo>();
+        a.acc_list = acc_list_[cur].as<uint32_t>();
+        a.acc_prefix = acc_prefix_[cur].as<unsigned long long>();
+        a.next_acc_list = acc_list_[1 - cur].as<uint32_t>();
+        a.next_acc_prefix = acc_prefix_[1 - cur].as<unsigned long long>();
+        a.chunk_prefix = chunk_prefix_[cur].as<uint32_t>();
+        a.next_chunk_prefix = chunk_prefix_[1 - cur].as<uint32_t>();
+        a.hist_cur = hist_[d & 1].as<Pair>();
+        a.hist_prev = hist_[(d + 1) & 1].as<Pair>();
+        a.rows_cur = rows_[cur].as<uint32_t>();
+        a.rows_next = rows_[1 - cur].as<uint32_t>();
+        FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, 16ull * a.slot_pairs * max_acc, s_));
+        if (stats_ && d < 15) {
+            // this level's accumulate rows and nodes (TreeState.acc_count, .acc_total)
+            FB_CUDA_CHECK(cudaMemcpyAsync(level_stats_.as<uint8_t>() + 16 * d,
+                                          reinterpret_cast<uint8_t*>(state_.p) + offsetof(TreeState, acc_count), 16,
+                                          cudaMemcpyDeviceToDevice, s_));
+            FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d], s_));
+        }
+        launch_hist(1, d_tiles_.as<TileDesc>(), n_tiles_w1_, d_tfeat_.as<TileFeat>(), a.rows_cur, fixed_.as<Pair>(),
+                    a.nodes, a.acc_list, a.acc_prefix, a.st, a.hist_acc, a.slot_pairs, hist_grid, tile_smem_, s_);
+        launch_hist(2, d_tiles_.as<TileDesc>() + n_tiles_w1_, n_tiles_w2_, d_tfeat_.as<TileFeat>(), a.rows_cur,
+                    fixed_.as<Pair>(), a.nodes, a.acc_list, a.acc_prefix, a.st, a.hist_acc, a.slot_pairs, hist_grid,
+                    tile_smem_, s_);
+        if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
+        launch_split(a, max_m, s_);
+        launch_decide(a, s_);
+        const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
+        launch_part_count(a, max_chunks, s_);
+        launch_part_scan(a, s_);
+        launch_part_scatter(a, max_chunks, s_);
+        launch_next_level(a, s_);
+        cur = 1 - cur;
+    }
+    a.nodes = nodes_[cur].as<NodeInfo>();
+    a.chunk_prefix = chunk_prefix_[cur].as<uint32_t>();
+    a.rows_cur = rows_[cur].as<uint32_t>();
+    const uint32_t last_m = (uint32_t)std::min<uint64_t>(1ull << maxd, max_level_nodes_);
+    launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
+    FB_CUDA_CHECK(cudaGetLastError());
+    FB_CUDA_CHECK(cudaEventRecord(ev1_, s_));
+    TreeRec* hrec = h_tree_.as<TreeRec>();
+    uint32_t* hcats = reinterpret_cast<uint32_t*>(hrec + max_tree_nodes_);
+    TreeState* hst = reinterpret_cast<TreeState*>(hcats + 8ull * max_tree_nodes_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(hst, state_.p, sizeof(TreeState), cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(hrec, trec_.p, sizeof(TreeRec) * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
+    if (has_cat_) FB_CUDA_CHECK(cudaMemcpyAsync(hcats, tcats_.p, 32ull * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
+    uint64_t lvl[32] = {0};
+    if (stats_) FB_CUDA_CHECK(cudaMemcpyAsync(lvl, level_stats_.p, 16 * 16, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    FB_CUDA_CHECK(cudaEventElapsedTime(&last_tree_ms_, ev0_, ev1_));
+    if (stats_) {
+        uint64_t row_bytes = 0, bins = 0;  // enabled features of this tree
+        for (uint32_t f = 0; f < F_; f++)
+            if (last_enabled_[f]) { row_bytes += width_[f]; bins += nbins_[f]; }
+        for (uint32_t d = 0; d < std::min<uint32_t>(maxd, 15); d++) {
+            float ms = 0.0f;
+            FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
+            const uint64_t acc_nodes = lvl[2 * d] & 0xffffffffull, rows = lvl[2 * d + 1];
+            hist_ms_ += ms;
+            hist_launches_ += (n_tiles_w1_ ? 1 : 0) + (n_tiles_w2_ ? 1 : 0);
+            hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
+        }
+    }
+    const uint32_t nn = hst->n_tree_nodes;
+    if (nn == 0 || nn > max_tree_nodes_) throw std::runtime_error("device tree has an invalid node count");
+    if (!out) return;
+    if (out->capacity < nn) throw InputError("fbgpu_tree_out capacity is smaller than the tree");
+    out->n_nodes = nn;
+    for (uint32_t i = 0; i < nn; i++) {
+        const TreeRec& r = hrec[i];
+        if (out->left) out->left[i] = r.left;
+        if (out->right) out->right[i] = r.right;
+        if (out->feat) out->feat[i] = r.feat;
+        if (out->bin) out->bin[i] = r.bin;
+        if (out->gain) out->gain[i] = r.gain;
+        if (out->leaf) out->leaf[i] = r.leaf;
+        if (out->hess) out->hess[i] = r.hess;
+        if (out->flags) out->flags[i] = r.flags;
+        if (out->cats) {
+            for (int w = 0; w < 8; w++) out->cats[i * 8 + w] = (r.flags & 4u) ? hcats[i * 8 + w] : 0u;
+        }
+    }
+}
+
+void TrainCtx::download_margins(float* out) {
+    FB_CUDA_CHECK(cudaMemcpyAsync(out, pred_.p, n_ * 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+// ---- component calls (kernel parity tests) --------------------------------
+void TrainCtx::histogram(const uint32_t* rows, uint64_t n_sel, const int64_t* fixed, int64_t* out) {
+    ensure_features();
+    if (fixed) FB_CUDA_CHECK(cudaMemcpyAsync(fixed_.p, fixed, n_ * 16, cudaMemcpyHostToDevice, s_));
+    ensure_tree_buffers(std::max<uint32_t>(buf_depth_ == 0xffffffffu ? 1 : buf_depth_, 1), buf_leaves_ == 0xffffffffu ? 0 : buf_leaves_);
+    plan_tiles(nullptr);
+    std::vector<uint32_t> all;
+    if (!rows) {
+        all.resize(n_);
+        for (uint64_t i = 0; i < n_; i++) all[i] = (uint32_t)i;
+        rows = all.data();
+        n_sel = n_;
+    }
+    DevMem drows;
+    drows.alloc(std::max<uint64_t>(n_sel, 1) * 4);
+    FB_CUDA_CHECK(cudaMemcpyAsync(drows.p, rows, n_sel * 4, cudaMemcpyHostToDevice, s_));
+    NodeInfo ni{};
+    ni.start = 0; ni.len = (uint32_t)n_sel; ni.tree_id = 0; ni.parent_slot = -1; ni.acc_slot = 0;
+    uint32_t acc_list = 0;
+    unsigned long long acc_prefix[2] = {0, n_sel};
+    TreeState st{};
+    st.m = 1; st.acc_count = 1; st.acc_total = n_sel;
+    FB_CUDA_CHECK(cudaMemcpyAsync(nodes_[0].p, &ni, sizeof ni, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(acc_list_[0].p, &acc_list, 4, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(acc_prefix_[0].p, acc_prefix, 16, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(state_.p, &st, sizeof st, cudaMemcpyHostToDevice, s_));
+    const unsigned long long slot = std::max<uint64_t>(total_bins_, 1);
+    FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, 16 * slot, s_));
+    const uint32_t grid = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(n_sel, 8192), 148 * 2));
+    launch_hist(1, d_tiles_.as<TileDesc>(), n_tiles_w1_, d_tfeat_.as<TileFeat>(), drows.as<uint32_t>(),
+                fixed_.as<Pair>(), nodes_[0].as<NodeInfo>(), acc_list_[0].as<uint32_t>(),
+                acc_prefix_[0].as<unsigned long long>(), state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid,
+                tile_smem_, s_);
+    launch_hist(2, d_tiles_.as<TileDesc>() + n_tiles_w1_, n_tiles_w2_, d_tfeat_.as<TileFeat>(), drows.as<uint32_t>(),
+                fixed_.as<Pair>(), nodes_[0].as<NodeInfo>(), acc_list_[0].as<uint32_t>(),
+                acc_prefix_[0].as<unsigned long long>(), state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid,
+                tile_smem_, s_);
+    FB_CUDA_CHECK(cudaGetLastError());
+    FB_CUDA_CHECK(cudaMemcpyAsync(out, hist_acc_.p, 16 * total_bins_, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const double* scales,
+                          const fbgpu_tree_params& tp, float lower, float upper, const uint8_t* enabled,
+                          fbgpu_split* out) {
+    ensure_features();
+    ensure_tree_buffers(std::max<uint32_t>(buf_depth_, 1), buf_leaves_);
+    std::vector<uint8_t> en(F_, 1);
+    if (enabled) for (uint32_t f = 0; f < F_; f++) en[f] = enabled[f] ? 1 : 0;
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_enabled_.p, en.data(), F_, cudaMemcpyHostToDevice, s_));
+    tiles_valid_ = false;
+    if (tp.monotone) FB_CUDA_CHECK(cudaMemcpyAsync(d_mono_.p, tp.monotone, F_, cudaMemcpyHostToDevice, s_));
+    last_mono_.clear();
+    FB_CUDA_CHECK(cudaMemcpyAsync(hist_acc_.p, hist, 16 * total_bins_, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, scales, 16, cudaMemcpyHostToDevice, s_));
+    NodeInfo ni{};
+    ni.start = 0; ni.len = 0; ni.tree_id = 0; ni.parent_slot = -1; ni.acc_slot = 0;
+    ni.lower = lower; ni.upper = upper; ni.sum = Pair{node_sum[0], node_sum[1]};
+    TreeState st{};
+    st.m = 1;
+    FB_CUDA_CHECK(cudaMemcpyAsync(nodes_[0].p, &ni, sizeof ni, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(state_.p, &st, sizeof st, cudaMemcpyHostToDevice, s_));
+    LevelArgs a = level_args(tp);
+    a.nodes = nodes_[0].as<NodeInfo>();
+    a.hist_cur = hist_[0].as<Pair>();
+    a.hist_prev = hist_[1].as<Pair>();
+    a.last_level = 1;
+    launch_split(a, 1, s_);
+    FB_CUDA_CHECK(cudaGetLastError());
+    SplitRec r;
+    uint32_t cats[8];
+    FB_CUDA_CHECK(cudaMemcpyAsync(&r, node_best_.p, sizeof r, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(cats, node_cats_.p, 32, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    std::memset(out, 0, sizeof *out);
+    out->found = r.flags & 1u;
+    if (!out->found) return;
+    out->feat = r.feat;
+    out->bin = r.bin;
+    out->missing_left = (r.flags >> 1) & 1u;
+    out->categorical = (r.flags >> 2) & 1u;
+    out->gain = r.gain;
+    out->left_grad = r.left.g; out->left_hess = r.left.h;
+    out->right_grad = r.right.g; out->right_hess = r.right.h;
+    if (out->categorical) std::memcpy(out->cats, cats, 32);
+}
+
+void TrainCtx::partition(const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin, int missing_left,
+                         const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left) {
+    ensure_features();
+    if (feat >= F_) throw InputError("feature id out of range");
+    if (n > n_) throw InputError("more rows than the context holds");
+    ensure_tree_buffers(std::max<uint32_t>(buf_depth_, 1), buf_leaves_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(rows_[0].p, rows, n * 4, cudaMemcpyHostToDevice, s_));
+    NodeInfo ni{};
+    ni.start = 0; ni.len = (uint32_t)n; ni.tree_id = 0; ni.parent_slot = -1;
+    SplitDesc sd{0, feat, bin, (missing_left ? 2u : 0u) | (cats ? 4u : 0u)};
+    uint32_t cw[8] = {0};
+    if (cats) std::memcpy(cw, cats, 32);
+    uint32_t cp[2] = {0, ceil_div(n, kChunkRows)};
+    TreeState st{};
+    st.m = 1; st.chunk_count = cp[1];
+    FB_CUDA_CHECK(cudaMemcpyAsync(nodes_[0].p, &ni, sizeof ni, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(split_.p, &sd, sizeof sd, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(node_cats_.p, cw, 32, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(chunk_prefix_[0].p, cp, 8, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(state_.p, &st, sizeof st, cudaMemcpyHostToDevice, s_));
+    fbgpu_tree_params tp{};
+    LevelArgs a = level_args(tp);
+    a.nodes = nodes_[0].as<NodeInfo>();
+    a.chunk_prefix = chunk_prefix_[0].as<uint32_t>();
+    a.rows_cur = rows_[0].as<uint32_t>();
+    a.rows_next = rows_[1].as<uint32_t>();
+    launch_part_count(a, std::max<uint32_t>(cp[1], 1), s_);
+    launch_part_scan(a, s_);
+    launch_part_scatter(a, std::max<uint32_t>(cp[1], 1), s_);
+    FB_CUDA_CHECK(cudaGetLastError());
+    uint32_t nl = 0;
+    FB_CUDA_CHECK(cudaMemcpyAsync(&nl, node_left_.p, 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(out_rows, rows_[1].p, n * 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    *n_left = nl;
+}
+
+// ======================================================================= explain
+void make_shap_rule(float* nodes, float* weights) {
+    const int n = kShapPoints;
+    auto legendre = [](int k, double x) {
+        if (k == 0) return 1.0;
+        double p0 = 1.0, p1 = x;
+        for (int j = 2; j <= k; j++) {
+            double jf = (double)j;
+            double pk = ((2.0 * jf - 1.0) * x * p1 - (jf - 1.0) * p0) / jf;
+            p0 = p1;
+            p1 = pk;
+        }
+        return p1;
+    };
+    const double pi = 3.14159265358979323846;
+    for (int i = 0; i < n; i++) {
+        double theta = pi * ((double)i + 0.75) / ((double)n + 0.5);
+        double x = std::cos(theta);
+        for (int it = 0; it < 64; it++) {
+            double pn = legendre(n, x);
+            double dpn = (double)n * (x * pn - legendre(n - 1, x)) / (x * x - 1.0);
+            double dx = pn / dpn;
+            x -= dx;
+            if (std::fabs(dx) < 1e-15) break;
+        }
+        double pn = legendre(n, x);
+        double dpn = (double)n * (x * pn - legendre(n - 1, x)) / (x * x - 1.0);
+        double wq = 2.0 / ((1.0 - x * x) * dpn * dpn);
+        double s = 0.5 * (x + 1.0);
+        double ws = 0.5 * wq;
+        nodes[n - 1 - i] = (float)(s * s);
+        weights[n - 1 - i] = (float)(2.0 * s * ws);
+    }
+}
+
+ExplainModel::ExplainModel(int device, uint32_t n_features, uint32_t n_trees, const uint32_t* tree_off,
+                           const int32_t* left, const int32_t* right, const uint32_t* feat, const float* value,
+                           const uint8_t* flags, const float* hess, const uint32_t* cat_off,
+                           const uint32_t* cat_len, const uint32_t* cat_words, uint64_t n_cat_words,
+                           float base_margin)
+    : device_(device), F_(n_features), T_(n_trees), base_margin_(base_margin) {
+    if (n_features == 0 || n_features > 0xffffff) throw InputError("model feature count out of range");
+    FB_CUDA_CHECK(cudaSetDevice(device));
+    FB_CUDA_CHECK(cudaStreamCreateWithFlags(&s_, cudaStreamNonBlocking));
+    const uint32_t nn = tree_off[n_trees];
+    std::vector<DevNode> nodes(std::max<uint32_t>(nn, 1));
+    std::vector<uint32_t> coff(std::max<uint32_t>(nn, 1), 0), clen(std::max<uint32_t>(nn, 1), 0);
+    double rm_sum = 0.0;
+    for (uint32_t t = 0; t < n_trees; t++) {
+        const uint32_t a = tree_off[t], b = tree_off[t + 1];
+        if (b <= a) throw InputError("every tree has at least one node");
+        for (uint32_t i = a; i < b; i++) {
+            DevNode d{};
+            d.val = value[i];
+            d.left = left[i];
+            d.right = right[i];
+            const uint32_t fl = flags[i] & 7u;
+            if (!(fl & 1u)) {
+                if (feat[i] >= n_features) throw InputError("split feature out of range");
+                if (left[i] <= (int32_t)(i - a) || right[i] <= (int32_t)(i - a) || left[i] >= (int32_t)(b - a) ||
+                    right[i] >= (int32_t)(b - a))
+                    throw InputError("child index out of range (children must follow their parent)");
+            }
+            d.meta = (feat[i] & 0xffffffu) | (fl << 24);
+            d.hess = hess ? hess[i] : 0.0f;
+            nodes[i] = d;
+            if (cat_off && (fl & 4u)) {
+                coff[i] = cat_off[i];
+                clen[i] = cat_len[i];
+                if ((uint64_t)cat_off[i] + cat_len[i] > n_cat_words) throw InputError("category set out of range");
+            }
+        }
+        // explain.rs:412-426 root_mean (f64, cover weighted); summed in tree order
+        std::vector<double> mean(b - a);
+        for (uint32_t i = b; i-- > a;) {
+            const DevNode& d = nodes[i];
+            if ((d.meta >> 24) & 1u) { mean[i - a] = (double)d.val; continue; }
+            double lm = mean[d.left], rmn = mean[d.right];
+            if (d.hess == 0.0f) mean[i - a] = 0.5 * (lm + rmn);
+            else mean[i - a] = (lm * (double)nodes[a + d.left].hess + rmn * (double)nodes[a + d.right].hess) / (double)d.hess;
+        }
+        rm_sum += mean[0];
+    }
+    root_mean_ = (float)rm_sum;
+    nodes_.alloc(sizeof(DevNode) * nodes.size());
+    tree_off_.alloc(4 * (n_trees + 1));
+    cat_off_.alloc(4 * coff.size());
+    cat_len_.alloc(4 * clen.size());
+    cat_words_.alloc(4 * std::max<uint64_t>(n_cat_words, 1));
+    FB_CUDA_CHECK(cudaMemcpyAsync(nodes_.p, nodes.data(), sizeof(DevNode) * nodes.size(), cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(tree_off_.p, tree_off, 4 * (n_trees + 1), cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(cat_off_.p, coff.data(), 4 * coff.size(), cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(cat_len_.p, clen.data(), 4 * clen.size(), cudaMemcpyHostToDevice, s_));
+    if (n_cat_words)
+        FB_CUDA_CHECK(cudaMemcpyAsync(cat_words_.p, cat_words, 4 * n_cat_words, cudaMemcpyHostToDevice, s_));
+    make_shap_rule(rule_nodes_, rule_weights_);
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    dm_.nodes = nodes_.as<DevNode>();
+    dm_.tree_off = tree_off_.as<uint32_t>();
+    dm_.cat_off = cat_off_.as<uint32_t>();
+    dm_.cat_len = cat_len_.as<uint32_t>();
+    dm_.cat_words = cat_words_.as<uint32_t>();
+    dm_.n_trees = n_trees;
+    dm_.n_features = n_features;
+}
+
+ExplainModel::~ExplainModel() {
+    if (s_) {
+        cudaStreamSynchronize(s_);
+        cudaStreamDestroy(s_);
+    }
+}
+
+void ExplainModel::predict_device(const float* X, uint64_t n, float* out, cudaStream_t s) {
+    FB_CUDA_CHECK(cudaSetDevice(device_));
+    launch_predict(dm_, X, n, base_margin_, out, s);
+    FB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ExplainModel::shap_device(const float* X, uint64_t n, float* out, cudaStream_t s) {
+    FB_CUDA_CHECK(cudaSetDevice(device_));
+    const uint64_t T = shap_threads(n);
+    if (T > scratch_threads_) {
+        path_.alloc(4 * T * F_);
+        tc_.alloc(4 * T * F_);
+        scratch_threads_ = T;
+    }
+    upload_shap_rule(rule_nodes_, rule_weights_, s);
+    launch_shap(dm_, X, n, base_margin_, root_mean_, out, path_.as<float>(), tc_.as<float>(), s);
+    FB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ExplainModel::predict_host(const float* X, uint64_t n, float* out) {
+    x_.alloc(std::max<uint64_t>(n * F_ * 4, 16));
+    out_.alloc(std::max<uint64_t>(n * 4, 16));
+    FB_CUDA_CHECK(cudaMemcpyAsync(x_.p, X, n * F_ * 4, cudaMemcpyHostToDevice, s_));
+    predict_device(x_.as<float>(), n, out_.as<float>(), s_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(out, out_.p, n * 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void ExplainModel::shap_host(const float* X, uint64_t n, float* out) {
+    x_.alloc(std::max<uint64_t>(n * F_ * 4, 16));
+    out_.alloc(std::max<uint64_t>(n * (F_ + 1) * 4, 16));
+    FB_CUDA_CHECK(cudaMemcpyAsync(x_.p, X, n * F_ * 4, cudaMemcpyHostToDevice, s_));
+    shap_device(x_.as<float>(), n, out_.as<float>(), s_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(out, out_.p, n * (F_ + 1) * 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+}  // namespace fbg
+
+// ======================================================================= C ABI
+using fbg::ExplainModel;
+using fbg::TrainCtx;
+
+struct fbgpu_ctx {
+    TrainCtx impl;
+    explicit fbgpu_ctx(const fbgpu_config& c) : impl(c) {}
+};
+struct fbgpu_model {
+    ExplainModel impl;
+    template <class... A> explicit fbgpu_model(A&&... a) : impl(std::forward<A>(a)...) {}
+};
+
+namespace {
+template <class F> fbgpu_status guard(fbgpu_ctx* ctx, F&& f) {
+    try {
+        f();
+        return FBGPU_OK;
+    } catch (const fbg::InputError& e) {
+        (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
+        return FBGPU_EINPUT;
+    } catch (const fbg::CudaError& e) {
+        (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
+        return FBGPU_ECUDA;
+    } catch (const std::exception& e) {
+        (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
+        return FBGPU_EINTERNAL;
+    }
+}
+}  // namespace
+
+extern "C" {
+
+const char* fbgpu_last_error(const fbgpu_ctx* ctx) { return ctx ? ctx->impl.err.c_str() : fbg::g_last_error.c_str(); }
+
+int32_t fbgpu_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+fbgpu_status fbgpu_ctx_create(const fbgpu_config* cfg, fbgpu_ctx** out) {
+    return guard(nullptr, [&] {
+        if (!cfg || !out) throw fbg::InputError("null argument");
+        *out = new fbgpu_ctx(*cfg);
+    });
+}
+void fbgpu_ctx_destroy(fbgpu_ctx* ctx) { delete ctx; }
+
+fbgpu_status fbgpu_set_features(fbgpu_ctx* ctx, const uint32_t* n_bins, const uint8_t* width,
+                                const uint8_t* categorical) {
+    return guard(ctx, [&] { ctx->impl.set_features(n_bins, width, categorical); });
+}
+fbgpu_status fbgpu_upload_block(fbgpu_ctx* ctx, const uint32_t* feat_ids, uint32_t n_feats, uint32_t width,
+                                const void* data) {
+    return guard(ctx, [&] { ctx->impl.upload_block(feat_ids, n_feats, width, data); });
+}
+fbgpu_status fbgpu_set_labels(fbgpu_ctx* ctx, const float* labels, const float* weights,
+                              const float* base_margin_rows, float base_margin) {
+    return guard(ctx, [&] { ctx->impl.set_labels(labels, weights, base_margin_rows, base_margin); });
+}
+fbgpu_status fbgpu_upload_and_quantize_gpair(fbgpu_ctx* ctx, const float* gpair, uint64_t sub_threshold, uint64_t seed,
+                                             uint64_t tree, double* scales_out, int64_t* root_sum_out) {
+    return guard(ctx, [&] {
+        ctx->impl.upload_and_quantize(gpair, sub_threshold, seed, tree, scales_out, root_sum_out);
+    });
+}
+fbgpu_status fbgpu_upload_gpair(fbgpu_ctx* ctx, const int64_t* fixed, const double* scales, const int64_t* root_sum) {
+    return guard(ctx, [&] { ctx->impl.upload_fixed(fixed, scales, root_sum); });
+}
+fbgpu_status fbgpu_round_from_exp(fbgpu_ctx* ctx, int32_t objective, const float* host_exp, uint64_t sub_threshold,
+                                  uint64_t seed, uint64_t tree, const double* scales) {
+    return guard(ctx, [&] { ctx->impl.round_from_exp(objective, host_exp, sub_threshold, seed, tree, scales); });
+}
+fbgpu_status fbgpu_round_device(fbgpu_ctx* ctx, int32_t objective, int32_t fast, uint64_t sub_threshold,
+                                uint64_t seed, uint64_t tree, double* scales_out, int64_t* root_sum_out) {
+    return guard(ctx, [&] {
+        ctx->impl.round_device(objective, fast, sub_threshold, seed, tree, scales_out, root_sum_out);
+    });
+}
+fbgpu_status fbgpu_build_tree(fbgpu_ctx* ctx, const fbgpu_tree_params* tp, const uint8_t* enabled,
+                              fbgpu_tree_out* out) {
+    return guard(ctx, [&] {
+        if (!tp) throw fbg::InputError("null tree parameters");
+        ctx->impl.build_tree(*tp, enabled, out);
+    });
+}
+fbgpu_status fbgpu_download_margins(fbgpu_ctx* ctx, float* out) {
+    return guard(ctx, [&] { ctx->impl.download_margins(out); });
+}
+fbgpu_status fbgpu_histogram(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n_sel, const int64_t* fixed,
+                             int64_t* out) {
+    return guard(ctx, [&] { ctx->impl.histogram(rows, n_sel, fixed, out); });
+}
+fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t* node_sum, const double* scales,
+                              const fbgpu_tree_params* tp, float lower, float upper, const uint8_t* enabled,
+                              fbgpu_split* out) {
+    return guard(ctx, [&] { ctx->impl.eval_split(hist, node_sum, scales, *tp, lower, upper, enabled, out); });
+}
+fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
+                             int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left) {
+    return guard(ctx, [&] { ctx->impl.partition(rows, n, feat, bin, missing_left, cats, out_rows, n_left); });
+}
+
+fbgpu_status fbgpu_model_create(int32_t device, uint32_t n_features, uint32_t n_trees, const uint32_t* tree_off,
+                                const int32_t* left, const int32_t* right, const uint32_t* feat, const float* value,
+                                const uint8_t* flags, const float* hess, const uint32_t* cat_off,
+                                const uint32_t* cat_len, const uint32_t* cat_words, uint64_t n_cat_words,
+                                float base_margin, fbgpu_model** out) {
+    return guard(nullptr, [&] {
+        if (!out || !tree_off) throw fbg::InputError("null argument");
+        *out = new fbgpu_model(device, n_features, n_trees, tree_off, left, right, feat, value, flags, hess, cat_off,
+                               cat_len, cat_words, n_cat_words, base_margin);
+    });
+}
+void fbgpu_model_destroy(fbgpu_model* m) { delete m; }
+fbgpu_status fbgpu_predict(fbgpu_model* m, const float* X, uint64_t n, float* out) {
+    return guard(nullptr, [&] { m->impl.predict_host(X, n, out); });
+}
+fbgpu_status fbgpu_predict_device(fbgpu_model* m, const float* X, uint64_t n, float* out, void* stream) {
+    return guard(nullptr, [&] { m->impl.predict_device(X, n, out, (cudaStream_t)stream); });
+}
+fbgpu_status fbgpu_shap(fbgpu_model* m, const float* X, uint64_t n, float* out) {
+    return guard(nullptr, [&] { m->impl.shap_host(X, n, out); });
+}
+fbgpu_status fbgpu_shap_device(fbgpu_model* m, const float* X, uint64_t n, float* out, void* stream) {
+    return guard(nullptr, [&] { m->impl.shap_device(X, n, out, (cudaStream_t)stream); });
+}
+
+}  // extern "C"

@@ -1,0 +1,201 @@
+// Host side of the training context and the explanation model (C++ classes
+// behind the C ABI in include/fbgpu.h).
+#pragma once
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/fbgpu.h"
+#include "explain_kernels.cuh"
+#include "train_kernels.cuh"
+
+namespace fbg {
+
+struct CudaError : std::runtime_error {
+    CudaError(cudaError_t e, const char* what, const char* file, int line)
+        : std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(e) + " in " + what + " (" + file + ":" +
+                             std::to_string(line) + ")") {}
+};
+struct InputError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+// Owning device allocation.
+struct DevMem {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevMem() = default;
+    DevMem(const DevMem&) = delete;
+    DevMem& operator=(const DevMem&) = delete;
+    ~DevMem() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    void alloc(size_t n) {
+        release();
+        if (n == 0) n = 16;
+        FB_CUDA_CHECK(cudaMalloc(&p, n));
+        bytes = n;
+    }
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct PinnedMem {
+    void* p = nullptr;
+    size_t bytes = 0;
+    PinnedMem() = default;
+    PinnedMem(const PinnedMem&) = delete;
+    PinnedMem& operator=(const PinnedMem&) = delete;
+    ~PinnedMem() { release(); }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    void reserve(size_t n) {
+        if (n <= bytes) return;
+        release();
+        FB_CUDA_CHECK(cudaMallocHost(&p, n));
+        bytes = n;
+    }
+    template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+class TrainCtx {
+   public:
+    explicit TrainCtx(const fbgpu_config& cfg);
+    ~TrainCtx();
+
+    void set_features(const uint32_t* n_bins, const uint8_t* width, const uint8_t* categorical);
+    void upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const void* data);
+    void set_labels(const float* labels, const float* weights, const float* base_rows, float base_margin);
+
+    // Round start variants; each leaves the fixed gradients, the root sum
+    // and the scales on the device.
+    void upload_and_quantize(const float* gpair, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
+                             int64_t* sum_out);
+    void upload_fixed(const int64_t* fixed, const double* scales, const int64_t* sum);
+    void round_from_exp(int objective, const float* host_exp, uint64_t th, uint64_t seed, uint64_t tree,
+                        const double* scales);
+    void round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
+                      int64_t* sum_out);
+
+    void build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
+    void download_margins(float* out);
+
+    void histogram(const uint32_t* rows, uint64_t n_sel, const int64_t* fixed, int64_t* out);
+    void eval_split(const int64_t* hist, const int64_t* node_sum, const double* scales, const fbgpu_tree_params& tp,
+                    float lower, float upper, const uint8_t* enabled, fbgpu_split* out);
+    void partition(const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin, int missing_left,
+                   const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left);
+
+    // Internal access for the engine (same library).
+    cudaStream_t stream() const { return s_; }
+    float* dev_margins() const { return pred_.as<float>(); }
+    uint64_t n_local() const { return n_; }
+    const fbgpu_config& config() const { return cfg_; }
+    float last_tree_ms() const { return last_tree_ms_; }
+    // Histogram-phase statistics of the trees grown since the last reset
+    // (enabled by set_stats): device time, launches and algorithmic bytes
+    // (rows x (bin bytes + 16 B gradient + 4 B row id) + bins x 16 B flushed).
+    void set_stats(bool on) { stats_ = on; }
+    void reset_stats() { hist_ms_ = 0; hist_launches_ = 0; hist_bytes_ = 0; }
+    double hist_ms() const { return hist_ms_; }
+    double hist_launches() const { return hist_launches_; }
+    double hist_bytes() const { return hist_bytes_; }
+
+    std::string err;
+
+   private:
+    struct Block {
+        std::vector<uint32_t> feats;  // global ids, ascending
+        uint32_t width = 2;
+        uint32_t stride = 0;
+        DevMem data;
+    };
+    void ensure_features() const;
+    void plan_tiles(const uint8_t* enabled);
+    void ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves);
+    LevelArgs level_args(const fbgpu_tree_params& tp) const;
+    GradArgs grad_args() const;
+
+    fbgpu_config cfg_;
+    cudaStream_t s_ = nullptr;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    uint64_t n_ = 0;
+    uint32_t F_ = 0;
+    std::vector<uint32_t> nbins_, hoff_;
+    std::vector<uint8_t> width_, cat_;
+    uint64_t total_bins_ = 0;
+    std::vector<std::unique_ptr<Block>> blocks_;
+    std::vector<int> feat_block_;
+    std::vector<uint32_t> feat_byte_;
+    bool has_cat_ = false;
+
+    // feature tables
+    DevMem d_hoff_, d_floc_, d_enabled_, d_mono_, d_cat_;
+    std::vector<uint8_t> last_enabled_;
+    std::vector<int8_t> last_mono_;
+    bool tiles_valid_ = false;
+    DevMem d_tiles_, d_tfeat_;
+    uint32_t n_tiles_w1_ = 0, n_tiles_w2_ = 0;
+    size_t tile_smem_ = 0;
+    int smem_budget_ = 0;
+
+    // rows / gradients
+    DevMem label_, weight_, pred_, gpair_f32_, host_exp_, fixed_;
+    DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double)
+    bool has_weight_ = false;
+    PinnedMem h_stage_;
+
+    // tree buffers
+    uint32_t buf_depth_ = 0xffffffffu, buf_leaves_ = 0xffffffffu;
+    uint32_t max_level_nodes_ = 0, max_split_nodes_ = 0, max_acc_ = 0, max_tree_nodes_ = 0, max_chunks_ = 0;
+    DevMem rows_[2], nodes_[2], acc_list_[2], acc_prefix_[2], chunk_prefix_[2];
+    DevMem hist_acc_, hist_[2], feat_best_, feat_cats_, node_best_, node_cats_, split_, chunk_left_, chunk_off_,
+        node_left_, trec_, tcats_, state_;
+    PinnedMem h_tree_;
+    float last_tree_ms_ = 0.0f;
+    bool stats_ = false;
+    cudaEvent_t hev_[32] = {};
+    DevMem level_stats_;
+    double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0;
+};
+
+class ExplainModel {
+   public:
+    ExplainModel(int device, uint32_t n_features, uint32_t n_trees, const uint32_t* tree_off, const int32_t* left,
+                 const int32_t* right, const uint32_t* feat, const float* value, const uint8_t* flags,
+                 const float* hess, const uint32_t* cat_off, const uint32_t* cat_len, const uint32_t* cat_words,
+                 uint64_t n_cat_words, float base_margin);
+    ~ExplainModel();
+    void predict_device(const float* X, uint64_t n, float* out, cudaStream_t s);
+    void shap_device(const float* X, uint64_t n, float* out, cudaStream_t s);
+    void predict_host(const float* X, uint64_t n, float* out);
+    void shap_host(const float* X, uint64_t n, float* out);
+    uint32_t n_features() const { return F_; }
+
+   private:
+    int device_;
+    uint32_t F_, T_;
+    float base_margin_, root_mean_;
+    DevMem nodes_, tree_off_, cat_off_, cat_len_, cat_words_, path_, tc_, x_, out_;
+    uint64_t scratch_threads_ = 0;
+    cudaStream_t s_ = nullptr;
+    DevModel dm_{};
+    float rule_nodes_[kShapPoints], rule_weights_[kShapPoints];
+};
+
+// explain.rs:141-169 endpoint-squared Gauss-Legendre rule (f64, stored as f32).
+void make_shap_rule(float* nodes, float* weights);
+
+// types.rs:366-385 pow2_scale with the host libm (exact mode).
+double pow2_scale_host(double max_abs, uint64_t n_rows);
+
+}  // namespace fbg

@@ -1,0 +1,903 @@
+// Host engine: dataset preparation, the boosting round loop and the model.
+//
+// Restates the reference's host control (mdai001/FerrisBoost, Rust): the
+// weighted quantile sketch and dense quantization (src/data/sketch.rs,
+// src/source/dense.rs, src/data/columns.rs), the round loop
+// (src/training/mod.rs:1895-2311), column sampling (src/data/colsample.rs),
+// row sampling (src/data/subsample.rs) and the XGBoost JSON writer
+// (src/model/tree.rs:600-1257).  Per-row and per-bin work runs on the device
+// through TrainCtx / ExplainModel (ctx.cu); this file only decides and
+// assembles.  Host float steps that must match the reference bit for bit
+// (sketch ranks, glibc expf in exact-mode logistic gradients, quantizer
+// scales) are compiled with -ffp-contract=off.
+#include <algorithm>
+#include <charconv>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <omp.h>
+
+#include "../../include/fb_engine.h"
+#include "ctx.h"
+
+namespace fbe {
+
+using fbg::InputError;
+thread_local std::string g_err;
+
+// ---------------------------------------------------------------- sketch
+// sketch.rs:28-435: log-structured merge of compressed weighted summaries.
+struct SEntry {
+    float v, w, rmin, rmax;
+    float rmid() const { return 0.5f * (rmin + rmax); }
+};
+using Summary = std::vector<SEntry>;
+
+Summary summarize(std::vector<std::pair<float, float>>& buf) {  // sketch.rs:305-329
+    std::sort(buf.begin(), buf.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+    Summary out;
+    out.reserve(buf.size());
+    float acc = 0.0f;
+    for (size_t i = 0; i < buf.size();) {
+        const float v = buf[i].first;
+        float w = 0.0f;
+        for (; i < buf.size() && buf[i].first == v; i++) w += buf[i].second;
+        out.push_back({v, w, acc, acc + w});
+        acc += w;
+    }
+    return out;
+}
+
+Summary merge(const Summary& a, const Summary& b) {  // sketch.rs:336-392
+    if (a.empty()) return b;
+    if (b.empty()) return a;
+    Summary m;
+    m.reserve(a.size() + b.size());
+    size_t i = 0, j = 0;
+    float pa = 0.0f, pb = 0.0f;
+    while (i < a.size() || j < b.size()) {
+        const bool ta = j >= b.size() || (i < a.size() && a[i].v <= b[j].v);
+        const SEntry e = ta ? a[i++] : b[j++];
+        const float shift = ta ? pb : pa;
+        SEntry x{e.v, e.w, e.rmin + shift, e.rmax + shift};
+        if (ta) pa = e.rmax; else pb = e.rmax;
+        if (!m.empty() && m.back().v == x.v) {
+            SEntry& l = m.back();
+            l.w += x.w;
+            l.rmin = std::min(l.rmin, x.rmin);
+            l.rmax = std::max(l.rmax, x.rmax);
+        } else {
+            m.push_back(x);
+        }
+    }
+    return m;
+}
+
+Summary prune(const Summary& e, size_t max_size) {  // sketch.rs:403-435 compress
+    const size_t n = e.size();
+    if (n <= max_size) return e;
+    const float total = e[n - 1].rmax;
+    const size_t slots = max_size - 1;
+    Summary out;
+    out.reserve(max_size);
+    out.push_back(e[0]);
+    size_t taken = 0;
+    for (size_t k = 1; k < slots; k++) {
+        const float target = total * (float)k / (float)slots;
+        size_t j = taken + 1;
+        while (j < n - 1 && e[j].rmid() < target) j++;
+        j = std::min(std::max(j, taken + 1), n - 1 - (slots - 1 - k));
+        if (j > taken) { out.push_back(e[j]); taken = j; }
+    }
+    if (taken < n - 1) out.push_back(e[n - 1]);
+    return out;
+}
+
+std::vector<float> feature_cuts(const float* X, uint64_t n, uint32_t F, uint32_t f, uint32_t max_bin,
+                                const float* w) {
+    const size_t limit = std::max<size_t>((size_t)max_bin * 16, 32);
+    std::vector<std::pair<float, float>> buf;
+    buf.reserve(limit);
+    std::vector<Summary> levels;
+    std::vector<char> used;
+    auto insert = [&](Summary cur) {  // sketch.rs:161-180
+        for (size_t l = 0;; l++) {
+            if (l == levels.size()) { levels.push_back(std::move(cur)); used.push_back(1); return; }
+            if (!used[l]) { levels[l] = std::move(cur); used[l] = 1; return; }
+            Summary ex = std::move(levels[l]);
+            levels[l].clear();
+            used[l] = 0;
+            cur = prune(merge(ex, cur), limit);
+        }
+    };
+    for (uint64_t r = 0; r < n; r++) {  // sketch.rs:128-147 push
+        const float v = X[r * F + f];
+        const float wt = w ? w[r] : 1.0f;
+        if (std::isnan(v) || wt <= 0.0f) continue;
+        buf.push_back({v, wt});
+        if (buf.size() >= limit) {
+            Summary s = prune(summarize(buf), limit);
+            buf.clear();
+            insert(std::move(s));
+        }
+    }
+    if (!buf.empty()) {
+        Summary s = prune(summarize(buf), limit);
+        buf.clear();
+        insert(std::move(s));
+    }
+    Summary acc;  // sketch.rs:183-201 collapse
+    for (size_t l = 0; l < levels.size(); l++)
+        if (used[l]) acc = acc.empty() ? levels[l] : merge(acc, levels[l]);
+    if (!acc.empty()) acc = prune(acc, limit);
+    std::vector<float> cuts;  // sketch.rs:236-275
+    const size_t n_cuts = max_bin >= 1 ? max_bin - 1 : 0;
+    if (n_cuts == 0 || acc.empty()) return cuts;
+    if (acc.size() <= n_cuts) {
+        for (size_t i = 0; i + 1 < acc.size(); i++) {  // sketch.rs:290-302 midpoint
+            const float a = acc[i].v, b = acc[i + 1].v;
+            const float d = b - a;
+            const float m = std::isfinite(d) ? a + d * 0.5f : a * 0.5f + b * 0.5f;
+            cuts.push_back(m <= a ? b : m);
+        }
+        return cuts;
+    }
+    const float total = acc.back().rmax;
+    for (size_t k = 1; k <= n_cuts; k++) {
+        const float target = total * (float)k / (float)max_bin;
+        size_t idx = std::partition_point(acc.begin(), acc.end(), [&](const SEntry& e) { return e.rmid() < target; }) -
+                     acc.begin();
+        idx = std::min(idx, acc.size() - 1);
+        const float v = acc[idx].v;
+        if (cuts.empty() || v > cuts.back()) cuts.push_back(v);
+    }
+    return cuts;
+}
+
+// ---------------------------------------------------------------- dataset
+struct Dataset {
+    uint64_t n = 0;
+    uint32_t F = 0;
+    std::vector<float> cuts;
+    std::vector<uint32_t> offsets;  // F+1
+    std::vector<uint8_t> cat;       // F
+    std::vector<uint8_t> width;     // F: bytes per bin
+    struct Block {
+        std::vector<uint32_t> feats;
+        uint32_t width;
+        std::vector<uint8_t> data;  // column-major
+    };
+    std::vector<Block> blocks;
+    std::vector<int> feat_block, feat_local;
+    uint32_t n_bins(uint32_t f) const { return offsets[f + 1] - offsets[f] + 1; }
+    uint32_t missing(uint32_t f) const { return width[f] == 2 ? 65535u : 255u; }
+    float threshold(uint32_t f, uint32_t bin) const {  // tree.rs:991-1000 split_threshold
+        const uint32_t nc = offsets[f + 1] - offsets[f];
+        if (bin == 0) return -std::numeric_limits<float>::max();
+        if (bin > nc) return std::numeric_limits<float>::max();
+        return cuts[offsets[f] + bin - 1];
+    }
+    uint32_t bin_of(uint32_t f, float v) const {  // columns.rs:335-341 find_bin
+        if (cat[f]) {  // categorical.rs:360-370 code_to_bin
+            const uint32_t nb = n_bins(f);
+            if (v >= 0.0f && v < (float)nb) return (uint32_t)v;
+            return missing(f) - 1;
+        }
+        const float* c = cuts.data() + offsets[f];
+        return (uint32_t)(std::upper_bound(c, c + (offsets[f + 1] - offsets[f]), v) - c);
+    }
+};
+
+// bins.rs:58-66 (8 bits unless more bins are needed) and columns.rs:446-461:
+// blocks of one width; the device stores every block row-major with a
+// 16-byte-padded record, so a block holds at most 64 16-bit or 128 8-bit
+// features (128-byte records).
+void build_blocks(Dataset& d, const float* X, int nth) {
+    d.width.resize(d.F);
+    for (uint32_t f = 0; f < d.F; f++) {
+        const uint32_t nb = d.n_bins(f);
+        const bool wide = d.cat[f] ? nb > 254u : nb > 255u;
+        d.width[f] = wide ? 2 : 1;
+    }
+    d.feat_block.assign(d.F, -1);
+    d.feat_local.assign(d.F, -1);
+    for (uint32_t w = 1; w <= 2; w++) {
+        const uint32_t per = w == 2 ? 64 : 128;
+        std::vector<uint32_t> feats;
+        for (uint32_t f = 0; f < d.F; f++) if (d.width[f] == w) feats.push_back(f);
+        for (size_t i = 0; i < feats.size(); i += per) {
+            Dataset::Block b;
+            b.width = w;
+            b.feats.assign(feats.begin() + i, feats.begin() + std::min(feats.size(), i + per));
+            d.blocks.push_back(std::move(b));
+        }
+    }
+    std::sort(d.blocks.begin(), d.blocks.end(), [](const Dataset::Block& a, const Dataset::Block& b) {
+        return a.feats[0] < b.feats[0];
+    });
+    for (size_t bi = 0; bi < d.blocks.size(); bi++) {
+        Dataset::Block& b = d.blocks[bi];
+        b.data.resize(b.feats.size() * d.n * b.width);
+        for (size_t i = 0; i < b.feats.size(); i++) {
+            d.feat_block[b.feats[i]] = (int)bi;
+            d.feat_local[b.feats[i]] = (int)i;
+        }
+    }
+    // dense.rs:288-308 quantize_dense (column-major, NaN -> missing)
+    int reserved = 0;
+    for (size_t bi = 0; bi < d.blocks.size(); bi++) {
+        Dataset::Block& b = d.blocks[bi];
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nth) reduction(| : reserved)
+        for (int64_t i = 0; i < (int64_t)b.feats.size(); i++) {
+            const uint32_t f = b.feats[i];
+            const uint32_t miss = d.missing(f);
+            for (uint64_t r = 0; r < d.n; r++) {
+                const float v = X[r * d.F + f];
+                if (v == std::numeric_limits<float>::max()) reserved = 1;
+                const uint32_t bin = std::isnan(v) ? miss : d.bin_of(f, v);
+                if (b.width == 2) reinterpret_cast<uint16_t*>(b.data.data())[(size_t)i * d.n + r] = (uint16_t)bin;
+                else b.data[(size_t)i * d.n + r] = (uint8_t)bin;
+            }
+        }
+    }
+    if (reserved)  // dense.rs:300
+        throw InputError("feature contains f32::MAX, reserved for missing-value split boundaries; rescale this feature");
+}
+
+int threads(int32_t nthread) { return nthread > 0 ? nthread : omp_get_max_threads(); }
+
+Dataset* dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                            const uint8_t* categorical, int32_t nthread) {
+    if (n == 0 || F == 0) throw InputError("training data must have at least one row and one feature");
+    if (max_bin == 0 || max_bin > 65535) throw InputError("max_bin must be in 1..=65535");
+    if (w)
+        for (uint64_t i = 0; i < n; i++)
+            if (!std::isfinite(w[i]) || w[i] < 0.0f) throw InputError("sample weights must be finite and non-negative");
+    auto d = std::make_unique<Dataset>();
+    d->n = n;
+    d->F = F;
+    d->cat.assign(F, 0);
+    if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
+    const int nth = threads(nthread);
+    std::vector<std::vector<float>> per(F);
+    std::string bad;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nth)
+    for (int64_t f = 0; f < (int64_t)F; f++) {
+        if (d->cat[f]) {  // sketch.rs:128-136 + categorical.rs:264-266
+            int32_t max_code = -1;
+            for (uint64_t r = 0; r < n; r++) {
+                const float v = X[r * F + f];
+                if (std::isnan(v)) continue;
+                if (v < 0.0f || v > 65533.0f || v != std::trunc(v)) {
+#pragma omp critical
+                    bad = "categorical feature #" + std::to_string(f) + " contains an invalid category code";
+                    break;
+                }
+                max_code = std::max(max_code, (int32_t)v);
+            }
+            for (int32_t k = 1; k <= std::max(max_code, 0); k++) per[f].push_back((float)k);
+        } else {
+            per[f] = feature_cuts(X, n, F, (uint32_t)f, max_bin, w);
+        }
+    }
+    if (!bad.empty()) throw InputError(bad);
+    d->offsets.push_back(0);
+    for (uint32_t f = 0; f < F; f++) {
+        d->cuts.insert(d->cuts.end(), per[f].begin(), per[f].end());
+        d->offsets.push_back((uint32_t)d->cuts.size());
+    }
+    build_blocks(*d, X, nth);
+    return d.release();
+}
+
+// ---------------------------------------------------------------- model
+struct Node {
+    int32_t left = -1, right = -1;
+    uint32_t feat = 0;
+    float cond = 0.0f;
+    bool default_left = false;
+    float leaf = 0.0f;
+    bool is_leaf = true;
+    bool is_cat = false;
+    float gain = 0.0f;
+    float hess = 0.0f;
+    std::vector<uint32_t> cats;
+};
+struct Tree {
+    std::vector<Node> nodes;
+};
+struct Model {
+    std::vector<Tree> trees;
+    float base_score = 0.5f;
+    int objective = 1;
+    uint32_t n_features = 0;
+    float scale_pos_weight = 1.0f;
+    std::vector<uint8_t> feature_types;
+    std::unique_ptr<fbg::ExplainModel> dev;
+    int dev_device = -1;
+    size_t dev_trees = 0;
+};
+
+float base_margin(int objective, float base_score) {  // objective.rs:368-399
+    if (objective == 1) {
+        const float x = std::min(std::max(base_score, 1e-6f), 1.0f - 1e-6f);
+        return -std::log(1.0f / x - 1.0f);
+    }
+    return base_score;
+}
+
+// Shortest round-trip digits of an f32 (the digit string serde_json's ryu and
+// Rust's Display both start from) and its decimal exponent.
+void shortest(float v, std::string& digits, int& kk) {
+    char buf[64];
+    auto r = std::to_chars(buf, buf + sizeof(buf), v, std::chars_format::scientific);
+    std::string s(buf, r.ptr);
+    const size_t e = s.find('e');
+    digits.clear();
+    for (size_t i = 0; i < e; i++) if (s[i] >= '0' && s[i] <= '9') digits.push_back(s[i]);
+    while (digits.size() > 1 && digits.back() == '0') digits.pop_back();
+    kk = std::atoi(s.c_str() + e + 1) + 1;
+}
+
+std::string json_f32(float v) {  // serde_json f32 (ryu layout)
+    if (!std::isfinite(v)) return "null";
+    std::string o;
+    if (std::signbit(v)) { o.push_back('-'); v = -v; }
+    if (v == 0.0f) return o + "0.0";
+    std::string d;
+    int kk;
+    shortest(v, d, kk);
+    const int len = (int)d.size(), k = kk - len;
+    if (0 <= k && kk <= 13) o += d + std::string((size_t)(kk - len), '0') + ".0";
+    else if (0 < kk && kk <= 13) o += d.substr(0, kk) + "." + d.substr(kk);
+    else if (-6 < kk && kk <= 0) o += "0." + std::string((size_t)(-kk), '0') + d;
+    else if (len == 1) o += d + "e" + std::to_string(kk - 1);
+    else o += d.substr(0, 1) + "." + d.substr(1) + "e" + std::to_string(kk - 1);
+    return o;
+}
+
+std::string display_f32(float v) {  // Rust Display for f32
+    if (std::isnan(v)) return "NaN";
+    std::string o;
+    if (std::signbit(v)) { o.push_back('-'); v = -v; }
+    if (std::isinf(v)) return o + "inf";
+    if (v == 0.0f) return o + "0";
+    std::string d;
+    int kk;
+    shortest(v, d, kk);
+    const int len = (int)d.size();
+    if (kk <= 0) o += "0." + std::string((size_t)(-kk), '0') + d;
+    else if (kk >= len) o += d + std::string((size_t)(kk - len), '0');
+    else o += d.substr(0, kk) + "." + d.substr(kk);
+    return o;
+}
+
+std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order of tree.rs:1167-1257
+    std::string o;
+    o.reserve(256 + m.trees.size() * 4096);
+    o += "{\"version\":[2,0,0],\"learner\":{\"attributes\":{},\"feature_names\":[],\"feature_types\":[";
+    bool any = std::any_of(m.feature_types.begin(), m.feature_types.end(), [](uint8_t c) { return c != 0; });
+    if (any)
+        for (uint32_t f = 0; f < m.n_features; f++) {
+            if (f) o.push_back(',');
+            o += m.feature_types[f] ? "\"c\"" : "\"q\"";
+        }
+    const size_t nt = m.trees.size();
+    o += "],\"gradient_booster\":{\"name\":\"gbtree\",\"model\":{\"gbtree_model_param\":{\"num_trees\":\"" +
+         std::to_string(nt) + "\",\"num_parallel_tree\":\"1\"},\"iteration_indptr\":[";
+    for (size_t i = 0; i <= nt; i++) { if (i) o.push_back(','); o += std::to_string(i); }
+    o += "],\"tree_info\":[";
+    for (size_t i = 0; i < nt; i++) { if (i) o.push_back(','); o.push_back('0'); }
+    o += "],\"trees\":[";
+    auto iarr = [&](const std::vector<int64_t>& v) {
+        o.push_back('[');
+        for (size_t i = 0; i < v.size(); i++) { if (i) o.push_back(','); o += std::to_string(v[i]); }
+        o.push_back(']');
+    };
+    auto farr = [&](const std::vector<float>& v) {
+        o.push_back('[');
+        for (size_t i = 0; i < v.size(); i++) { if (i) o.push_back(','); o += json_f32(v[i]); }
+        o.push_back(']');
+    };
+    for (size_t ti = 0; ti < nt; ti++) {
+        const std::vector<Node>& N = m.trees[ti].nodes;
+        const size_t nn = N.size();
+        std::vector<float> bw(nn), lc(nn), sc(nn), sh(nn);
+        std::vector<int64_t> dl(nn), lch(nn), rch(nn), par(nn, 2147483647), si(nn), st(nn, 0), cats, cnodes, cseg, csz;
+        for (size_t i = 0; i < nn; i++) {
+            const Node& nd = N[i];
+            lch[i] = nd.left; rch[i] = nd.right; dl[i] = nd.default_left; lc[i] = nd.gain; sh[i] = nd.hess;
+            if (nd.is_leaf) { sc[i] = nd.leaf; si[i] = 0; bw[i] = nd.leaf; continue; }
+            sc[i] = nd.cond; si[i] = nd.feat; bw[i] = 0.0f;
+            par[nd.left] = (int64_t)i; par[nd.right] = (int64_t)i;
+            if (nd.is_cat) {
+                st[i] = 1;
+                cnodes.push_back((int64_t)i);
+                cseg.push_back((int64_t)cats.size());
+                int64_t c = 0;
+                for (size_t w = 0; w < nd.cats.size(); w++)
+                    for (int b = 0; b < 32; b++)
+                        if ((nd.cats[w] >> b) & 1u) { cats.push_back((int64_t)(w * 32 + b)); c++; }
+                csz.push_back(c);
+            }
+        }
+        if (ti) o.push_back(',');
+        o += "{\"base_weights\":"; farr(bw);
+        o += ",\"categories\":"; iarr(cats);
+        o += ",\"categories_nodes\":"; iarr(cnodes);
+        o += ",\"categories_segments\":"; iarr(cseg);
+        o += ",\"categories_sizes\":"; iarr(csz);
+        o += ",\"default_left\":"; iarr(dl);
+        o += ",\"id\":" + std::to_string(ti);
+        o += ",\"left_children\":"; iarr(lch);
+        o += ",\"loss_changes\":"; farr(lc);
+        o += ",\"parents\":"; iarr(par);
+        o += ",\"right_children\":"; iarr(rch);
+        o += ",\"split_conditions\":"; farr(sc);
+        o += ",\"split_indices\":"; iarr(si);
+        o += ",\"split_type\":"; iarr(st);
+        o += ",\"sum_hessian\":"; farr(sh);
+        o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
+             "\",\"num_nodes\":\"" + std::to_string(nn) + "\",\"size_leaf_vector\":\"1\"}}";
+    }
+    o += "]}},\"learner_model_param\":{\"base_score\":\"" + display_f32(m.base_score) +
+         "\",\"boost_from_average\":\"1\",\"num_class\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
+         "\",\"num_target\":\"1\"},\"objective\":{\"name\":\"";
+    o += m.objective == 1 ? "binary:logistic" : "reg:squarederror";
+    o += "\",\"reg_loss_param\":{\"scale_pos_weight\":\"" + display_f32(m.scale_pos_weight) + "\"}}}}";
+    return o;
+}
+
+fbg::ExplainModel& device_model(Model& m, int device) {
+    if (m.dev && m.dev_device == device && m.dev_trees == m.trees.size()) return *m.dev;
+    std::vector<uint32_t> off{0}, feat, coff, clen, words;
+    std::vector<int32_t> left, right;
+    std::vector<float> val, hess;
+    std::vector<uint8_t> flags;
+    for (const Tree& t : m.trees) {
+        for (const Node& nd : t.nodes) {
+            left.push_back(nd.left); right.push_back(nd.right); feat.push_back(nd.feat);
+            val.push_back(nd.is_leaf ? nd.leaf : nd.cond); hess.push_back(nd.hess);
+            flags.push_back((uint8_t)((nd.is_leaf ? 1 : 0) | (nd.default_left ? 2 : 0) | (nd.is_cat ? 4 : 0)));
+            coff.push_back((uint32_t)words.size());
+            clen.push_back(nd.is_cat ? (uint32_t)nd.cats.size() : 0u);
+            if (nd.is_cat) words.insert(words.end(), nd.cats.begin(), nd.cats.end());
+        }
+        off.push_back((uint32_t)left.size());
+    }
+    m.dev.reset(new fbg::ExplainModel(device, m.n_features, (uint32_t)m.trees.size(), off.data(), left.data(),
+                                      right.data(), feat.data(), val.data(), flags.data(), hess.data(), coff.data(),
+                                      clen.data(), words.data(), words.size(), base_margin(m.objective, m.base_score)));
+    m.dev_device = device;
+    m.dev_trees = m.trees.size();
+    return *m.dev;
+}
+
+// ---------------------------------------------------------------- sampling
+inline uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+inline uint64_t rotl(uint64_t x, int r) { return (x << r) | (x >> (64 - r)); }
+uint64_t threshold_for(float rate) {  // subsample.rs:64-73
+    if (rate >= 1.0f || !(rate > 0.0f)) return UINT64_MAX;
+    return (uint64_t)((double)rate * (double)(1ull << 53));
+}
+inline bool row_selected(uint64_t row, uint64_t th, uint64_t seed, uint64_t tree) {  // subsample.rs:52-78
+    if (th == UINT64_MAX) return true;
+    return (mix64(seed ^ rotl(tree * 0x9E3779B97F4A7C15ull, 23) ^ (row * 0xD6E8FEB86659FD93ull)) >> 11) < th;
+}
+// colsample.rs:29-104: SplitMix64 Fisher-Yates over global feature ids.
+std::vector<uint8_t> sample_features(uint32_t nf, float rate, uint64_t seed, uint64_t round) {
+    std::vector<uint8_t> en(nf, 1);
+    if (rate >= 1.0f) return en;
+    double v = std::floor((double)rate * (double)nf);
+    uint64_t take = (std::isfinite(v) && v >= 1.0) ? (uint64_t)v : 1;
+    take = std::max<uint64_t>(1, std::min<uint64_t>(take, nf));
+    if (take >= nf) return en;
+    std::vector<uint32_t> ids(nf);
+    for (uint32_t i = 0; i < nf; i++) ids[i] = i;
+    uint64_t s = seed ^ rotl(round * 0x9E3779B97F4A7C15ull, 17);
+    for (uint32_t i = nf - 1; i >= 1; i--) {
+        const uint64_t n = (uint64_t)i + 1;
+        const uint64_t zone = UINT64_MAX - (UINT64_MAX % n) - 1;
+        uint64_t r;
+        do { s += 0x9E3779B97F4A7C15ull; r = mix64(s); } while (r > zone);
+        std::swap(ids[i], ids[r % n]);
+    }
+    std::fill(en.begin(), en.end(), 0);
+    for (uint64_t i = 0; i < take; i++) en[ids[i]] = 1;
+    return en;
+}
+
+// ---------------------------------------------------------------- booster
+struct Booster {
+    const Dataset* d = nullptr;
+    fb_params p{};
+    std::vector<int8_t> mono;
+    std::vector<float> labels, weights, grad_w;
+    std::unique_ptr<fbg::TrainCtx> ctx;
+    Model model;
+    uint32_t rounds_done = 0;
+    fbg::PinnedMem h_margin, h_exp;
+    double t_wall = 0, t_grad = 0, t_tree = 0, t_dev = 0;
+    std::vector<int32_t> o_left, o_right;
+    std::vector<uint32_t> o_feat, o_bin, o_flags, o_cats;
+    std::vector<float> o_gain, o_leaf, o_hess;
+};
+
+Booster* booster_create(const Dataset* d, const float* y, const float* w, const fb_params* pp) {
+    const fb_params& p = *pp;
+    if (p.objective != 0 && p.objective != 1) throw InputError("objective must be reg:squarederror or binary:logistic");
+    if (p.max_depth > 14) throw InputError("max_depth must be in 0..=14");
+    if (!(p.subsample > 0.0f && p.subsample <= 1.0f)) throw InputError("subsample must be in (0, 1]");
+    if (!(p.colsample_bytree > 0.0f && p.colsample_bytree <= 1.0f)) throw InputError("colsample_bytree must be in (0, 1]");
+    if (!(p.eta >= 0.0f) || !(p.lambda >= 0.0f) || !(p.gamma >= 0.0f) || !(p.min_child_weight >= 0.0f))
+        throw InputError("learning_rate, lambda, gamma and min_child_weight must be finite and non-negative");
+    for (uint64_t i = 0; i < d->n; i++)
+        if (!std::isfinite(y[i])) throw InputError("labels must all be finite");
+    if (p.objective == 1)
+        for (uint64_t i = 0; i < d->n; i++)
+            if (y[i] < 0.0f || y[i] > 1.0f) throw InputError("binary:logistic labels must be in [0, 1]");
+    auto b = std::make_unique<Booster>();
+    b->d = d;
+    b->p = p;
+    if (p.monotone) b->mono.assign(p.monotone, p.monotone + d->F);
+    b->labels.assign(y, y + d->n);
+    if (w) b->weights.assign(w, w + d->n);
+    // mod.rs:5470-5495 gradient weights (sample weight x scale_pos_weight on positives)
+    if (p.scale_pos_weight != 1.0f) {
+        b->grad_w.resize(d->n);
+        for (uint64_t i = 0; i < d->n; i++) {
+            const float wi = w ? w[i] : 1.0f;
+            b->grad_w[i] = y[i] == 1.0f ? wi * p.scale_pos_weight : wi;
+        }
+    } else if (w) {
+        b->grad_w = b->weights;
+    }
+    // objective.rs:41-61 label mean (FitInterceptGlmLike) when base_score is not given
+    float base = p.base_score;
+    if (std::isnan(base)) {
+        const uint64_t n = d->n;
+        if (!w) {
+            double acc = 0.0, nn = (double)n;
+            for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / nn;
+            base = (float)acc;
+        } else {
+            double sw = 0.0, acc = 0.0;
+            for (uint64_t i = 0; i < n; i++) sw = sw + (double)w[i];
+            if (sw <= 0.0) base = 0.5f;
+            else {
+                for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / sw * (double)w[i];
+                base = (float)acc;
+            }
+        }
+    }
+    if (p.objective == 1 && !(base >= 0.0f && base <= 1.0f))
+        throw InputError("logistic base_score is a probability and must be in [0, 1]");
+    b->model.base_score = base;
+    b->model.objective = p.objective;
+    b->model.n_features = d->F;
+    b->model.scale_pos_weight = p.scale_pos_weight;
+    if (std::any_of(d->cat.begin(), d->cat.end(), [](uint8_t c) { return c != 0; })) b->model.feature_types = d->cat;
+
+    fbgpu_config cfg{};
+    cfg.device = p.device;
+    cfg.n_features = d->F;
+    cfg.n_rows = d->n;
+    cfg.n_rows_global = d->n;
+    cfg.max_depth = p.max_depth;
+    cfg.max_leaves = p.max_leaves;
+    cfg.gpu_math = p.gpu_math;
+    if (const char* e = std::getenv("FBGPU_HIST_SMEM")) cfg.hist_smem_bytes = (uint32_t)std::atoi(e);
+    b->ctx.reset(new fbg::TrainCtx(cfg));
+    std::vector<uint32_t> nb(d->F);
+    for (uint32_t f = 0; f < d->F; f++) nb[f] = d->n_bins(f);
+    b->ctx->set_features(nb.data(), d->width.data(), d->cat.data());
+    for (const Dataset::Block& blk : d->blocks)
+        b->ctx->upload_block(blk.feats.data(), (uint32_t)blk.feats.size(), blk.width, blk.data.data());
+    b->ctx->set_labels(y, b->grad_w.empty() ? nullptr : b->grad_w.data(), nullptr, base_margin(p.objective, base));
+    const uint32_t cap = (2u << p.max_depth);
+    b->o_left.resize(cap); b->o_right.resize(cap); b->o_feat.resize(cap); b->o_bin.resize(cap);
+    b->o_flags.resize(cap); b->o_cats.resize(8ull * cap); b->o_gain.resize(cap); b->o_leaf.resize(cap);
+    b->o_hess.resize(cap);
+    return b.release();
+}
+
+// One boosting round (training/mod.rs:1895-2311).
+void booster_round(Booster& b) {
+    const fb_params& p = b.p;
+    const uint64_t n = b.d->n;
+    const uint32_t round = b.rounds_done;
+    const uint64_t th = threshold_for(p.subsample);
+    fbg::TrainCtx& ctx = *b.ctx;
+    auto t0 = std::chrono::steady_clock::now();
+    if (p.gpu_math == 1) {
+        ctx.round_device(p.objective, 1, th, p.seed, round, nullptr, nullptr);
+    } else if (p.objective == 0) {
+        ctx.round_device(0, 0, th, p.seed, round, nullptr, nullptr);
+    } else {
+        // exact logistic: glibc expf on the host, bounds of the f32 gradient,
+        // scales with the host libm; the device recomputes the same f32
+        // gradient from e and quantizes it (objective.rs:37-39, 519-526).
+        b.h_margin.reserve(n * 4);
+        b.h_exp.reserve(n * 4);
+        float* m = b.h_margin.as<float>();
+        float* e = b.h_exp.as<float>();
+        ctx.download_margins(m);
+        const float* y = b.labels.data();
+        const float* gw = b.grad_w.empty() ? nullptr : b.grad_w.data();
+        double mg = 0.0, mh = 0.0;
+        const int nth = threads(p.nthread);
+#pragma omp parallel for schedule(static) reduction(max : mg, mh) num_threads(nth)
+        for (int64_t i = 0; i < (int64_t)n; i++) {
+            const float ei = std::exp(-m[i]);
+            e[i] = ei;
+            const float s = 1.0f / (1.0f + ei);
+            const float hh = s * (1.0f - s);
+            float g = s - y[i];
+            float h = hh < 1e-16f ? 1e-16f : hh;
+            if (gw) { g = g * gw[i]; h = h * gw[i]; }
+            if (!row_selected((uint64_t)i, th, p.seed, round)) { g = 0.0f; h = 0.0f; }
+            mg = std::max(mg, std::isfinite(g) ? std::fabs((double)g) : HUGE_VAL);
+            mh = std::max(mh, std::isfinite(h) ? std::fabs((double)h) : HUGE_VAL);
+        }
+        if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
+        const double sc[2] = {fbg::pow2_scale_host(mg, n), fbg::pow2_scale_host(mh, n)};
+        ctx.round_from_exp(1, e, th, p.seed, round, sc);
+    }
+    auto t1 = std::chrono::steady_clock::now();
+    std::vector<uint8_t> en = sample_features(b.d->F, p.colsample_bytree, p.seed, round);
+    fbgpu_tree_params tp{};
+    tp.eta = p.eta; tp.lambda = p.lambda; tp.gamma = p.gamma; tp.min_child_weight = p.min_child_weight;
+    tp.alpha = p.alpha; tp.max_delta_step = p.max_delta_step; tp.max_depth = p.max_depth;
+    tp.max_leaves = p.max_leaves; tp.max_cat_to_onehot = p.max_cat_to_onehot;
+    tp.max_cat_threshold = p.max_cat_threshold; tp.grow_policy = p.grow_policy;
+    tp.monotone = b.mono.empty() ? nullptr : b.mono.data();
+    fbgpu_tree_out out{};
+    out.capacity = (uint32_t)b.o_left.size();
+    out.left = b.o_left.data(); out.right = b.o_right.data(); out.feat = b.o_feat.data(); out.bin = b.o_bin.data();
+    out.gain = b.o_gain.data(); out.leaf = b.o_leaf.data(); out.hess = b.o_hess.data(); out.flags = b.o_flags.data();
+    out.cats = b.o_cats.data();
+    ctx.build_tree(tp, p.colsample_bytree < 1.0f ? en.data() : nullptr, &out);
+    auto t2 = std::chrono::steady_clock::now();
+    Tree t;
+    t.nodes.resize(out.n_nodes);
+    for (uint32_t i = 0; i < out.n_nodes; i++) {
+        Node& nd = t.nodes[i];
+        const uint32_t fl = out.flags[i];
+        nd.is_leaf = fl & 1u;
+        nd.hess = out.hess[i];
+        if (nd.is_leaf) { nd.leaf = out.leaf[i]; continue; }
+        nd.left = out.left[i]; nd.right = out.right[i]; nd.feat = out.feat[i];
+        nd.default_left = (fl & 2u) != 0; nd.gain = out.gain[i]; nd.leaf = 0.0f;
+        nd.is_cat = (fl & 4u) != 0;
+        if (nd.is_cat) {
+            nd.cats.assign(out.cats + 8ull * i, out.cats + 8ull * i + 8);
+            while (!nd.cats.empty() && nd.cats.back() == 0) nd.cats.pop_back();
+            nd.cond = std::numeric_limits<float>::denorm_min();  // tree.rs:22 CATEGORICAL_SPLIT_COND
+        } else {
+            nd.cond = b.d->threshold(nd.feat, out.bin[i]);
+        }
+    }
+    b.model.trees.push_back(std::move(t));
+    b.rounds_done++;
+    b.t_grad += std::chrono::duration<double, std::milli>(t1 - t0).count();
+    b.t_tree += std::chrono::duration<double, std::milli>(t2 - t1).count();
+}
+
+template <class F> auto guarded(F&& f, decltype(f()) fail) -> decltype(f()) {
+    try {
+        return f();
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return fail;
+    }
+}
+
+}  // namespace fbe
+
+// ======================================================================= C ABI
+struct fb_dataset {
+    std::unique_ptr<fbe::Dataset> d;
+};
+struct fb_booster {
+    std::unique_ptr<fbe::Booster> b;
+};
+struct fb_model : fbe::Model {};
+
+extern "C" {
+
+void fb_default_params(fb_params* p) {  // types.rs:641-686
+    std::memset(p, 0, sizeof(*p));
+    p->objective = 1;
+    p->max_depth = 6;
+    p->max_bin = 255;
+    p->eta = 0.3f;
+    p->lambda = 1.0f;
+    p->min_child_weight = 1.0f;
+    p->scale_pos_weight = 1.0f;
+    p->subsample = 1.0f;
+    p->colsample_bytree = 1.0f;
+    p->base_score = std::numeric_limits<float>::quiet_NaN();
+    p->max_cat_to_onehot = 4;
+    p->max_cat_threshold = 64;
+}
+
+const char* fb_last_error(void) { return fbe::g_err.c_str(); }
+
+fb_dataset* fb_dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                                  const uint8_t* categorical, int32_t nthread) {
+    return fbe::guarded([&]() -> fb_dataset* {
+        auto* out = new fb_dataset();
+        out->d.reset(fbe::dataset_from_dense(X, n, F, max_bin, w, categorical, nthread));
+        return out;
+    }, nullptr);
+}
+
+fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const float* cuts, const uint32_t* offsets,
+                                 const uint8_t* categorical, int32_t nthread) {
+    return fbe::guarded([&]() -> fb_dataset* {
+        std::unique_ptr<fb_dataset> out(new fb_dataset());
+        out->d.reset(new fbe::Dataset());
+        fbe::Dataset* d = out->d.get();
+        d->n = n;
+        d->F = F;
+        d->offsets.assign(offsets, offsets + F + 1);
+        d->cuts.assign(cuts, cuts + offsets[F]);
+        d->cat.assign(F, 0);
+        if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
+        fbe::build_blocks(*d, X, fbe::threads(nthread));
+        return out.release();
+    }, nullptr);
+}
+
+void fb_dataset_free(fb_dataset* d) { delete d; }
+uint64_t fb_dataset_rows(const fb_dataset* h) { return h->d->n; }
+
+int64_t fb_dataset_cuts(const fb_dataset* h, float* cuts, uint32_t* offsets, uint64_t cap) {
+    const fbe::Dataset* d = h->d.get();
+    if (offsets) std::memcpy(offsets, d->offsets.data(), 4 * d->offsets.size());
+    if (cuts) std::memcpy(cuts, d->cuts.data(), 4 * std::min<uint64_t>(cap, d->cuts.size()));
+    return (int64_t)d->cuts.size();
+}
+
+int32_t fb_dataset_column(const fb_dataset* h, uint32_t f, uint16_t* out) {
+    const fbe::Dataset* d = h->d.get();
+    if (f >= d->F) return 1;
+    const fbe::Dataset::Block& b = d->blocks[d->feat_block[f]];
+    const size_t off = (size_t)d->feat_local[f] * d->n;
+    for (uint64_t r = 0; r < d->n; r++)
+        out[r] = b.width == 2 ? reinterpret_cast<const uint16_t*>(b.data.data())[off + r] : b.data[off + r];
+    return 0;
+}
+
+fb_booster* fb_booster_create(const fb_dataset* d, const float* labels, const float* weights, const fb_params* p) {
+    return fbe::guarded([&]() -> fb_booster* {
+        auto* out = new fb_booster();
+        out->b.reset(fbe::booster_create(d->d.get(), labels, weights, p));
+        return out;
+    }, nullptr);
+}
+
+void fb_booster_free(fb_booster* b) { delete b; }
+
+int32_t fb_booster_update(fb_booster* h, uint32_t n_rounds) {
+    fbe::Booster* b = h->b.get();
+    return fbe::guarded([&]() -> int32_t {
+        b->t_grad = b->t_tree = 0.0;
+        b->ctx->reset_stats();
+        cudaEvent_t e0, e1;
+        FB_CUDA_CHECK(cudaEventCreate(&e0));
+        FB_CUDA_CHECK(cudaEventCreate(&e1));
+        FB_CUDA_CHECK(cudaStreamSynchronize(b->ctx->stream()));
+        auto t0 = std::chrono::steady_clock::now();
+        FB_CUDA_CHECK(cudaEventRecord(e0, b->ctx->stream()));
+        for (uint32_t r = 0; r < n_rounds; r++) fbe::booster_round(*b);
+        FB_CUDA_CHECK(cudaEventRecord(e1, b->ctx->stream()));
+        FB_CUDA_CHECK(cudaEventSynchronize(e1));
+        b->t_wall = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        float ms = 0.0f;
+        FB_CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+        b->t_dev = ms;
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        return 0;
+    }, 1);
+}
+
+void fb_booster_timing(const fb_booster* h, double* out8) {
+    const fbe::Booster* b = h->b.get();
+    out8[0] = b->t_wall;
+    out8[1] = b->t_grad;
+    out8[2] = b->t_tree;
+    out8[3] = b->t_dev;
+    out8[4] = b->ctx->hist_ms();
+    out8[5] = b->ctx->hist_launches();
+    out8[6] = b->ctx->hist_bytes();
+    out8[7] = (double)b->rounds_done;
+}
+
+void fb_booster_set_stats(fb_booster* h, int32_t on) { h->b->ctx->set_stats(on != 0); }
+
+fb_model* fb_booster_model(fb_booster* h) {
+    fbe::Booster* b = h->b.get();
+    auto* m = new fb_model();
+    m->trees = b->model.trees;
+    m->base_score = b->model.base_score;
+    m->objective = b->model.objective;
+    m->n_features = b->model.n_features;
+    m->scale_pos_weight = b->model.scale_pos_weight;
+    m->feature_types = b->model.feature_types;
+    return m;
+}
+
+int32_t fb_booster_margins(fb_booster* h, float* out) {
+    return fbe::guarded([&]() -> int32_t { h->b->ctx->download_margins(out); return 0; }, 1);
+}
+
+fb_model* fb_train(const float* X, uint64_t n, uint32_t F, const float* y, const float* w, const uint8_t* categorical,
+                   const fb_params* p, uint32_t n_rounds) {
+    fb_dataset* d = fb_dataset_from_dense(X, n, F, p->max_bin, w, categorical, p->nthread);
+    if (!d) return nullptr;
+    fb_booster* b = fb_booster_create(d, y, w, p);
+    if (!b) { fb_dataset_free(d); return nullptr; }
+    fb_model* m = nullptr;
+    if (fb_booster_update(b, n_rounds) == 0) m = fb_booster_model(b);
+    fb_booster_free(b);
+    fb_dataset_free(d);
+    return m;
+}
+
+void fb_model_free(fb_model* m) { delete m; }
+uint32_t fb_model_num_trees(const fb_model* m) { return (uint32_t)m->trees.size(); }
+uint32_t fb_model_num_features(const fb_model* m) { return m->n_features; }
+float fb_model_base_margin(const fb_model* m) { return fbe::base_margin(m->objective, m->base_score); }
+
+int64_t fb_model_json(const fb_model* m, char* buf, int64_t cap) {
+    std::string s = fbe::model_json(*m);
+    if (buf && cap > 0) std::memcpy(buf, s.data(), (size_t)std::min<int64_t>(cap, (int64_t)s.size()));
+    return (int64_t)s.size();
+}
+
+int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* right, uint32_t* feat, float* cond,
+                      uint8_t* default_left, float* leaf, uint8_t* is_leaf, float* gain, float* hess, uint32_t* cats) {
+    if (t >= m->trees.size()) return -1;
+    const auto& N = m->trees[t].nodes;
+    for (size_t i = 0; i < N.size(); i++) {
+        const fbe::Node& nd = N[i];
+        if (left) left[i] = nd.left;
+        if (right) right[i] = nd.right;
+        if (feat) feat[i] = nd.feat;
+        if (cond) cond[i] = nd.cond;
+        if (default_left) default_left[i] = nd.default_left;
+        if (leaf) leaf[i] = nd.leaf;
+        if (is_leaf) is_leaf[i] = nd.is_leaf;
+        if (gain) gain[i] = nd.gain;
+        if (hess) hess[i] = nd.hess;
+        if (cats) for (int w = 0; w < 8; w++) cats[i * 8 + w] = w < (int)nd.cats.size() ? nd.cats[w] : 0u;
+    }
+    return (int64_t)N.size();
+}
+
+int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {
+    return fbe::guarded([&]() -> int32_t {
+        fbe::device_model(*m, device).predict_host(X, n, out);
+        return 0;
+    }, 1);
+}
+
+int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {
+    return fbe::guarded([&]() -> int32_t {
+        fbe::device_model(*m, device).shap_host(X, n, out);
+        return 0;
+    }, 1);
+}
+
+}  // extern "C"

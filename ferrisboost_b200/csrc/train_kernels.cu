@@ -1,0 +1,983 @@
+// Training kernels (sm_100a).  See train_kernels.cuh for the level pipeline.
+#include <cfloat>
+
+#include "train_kernels.cuh"
+
+namespace fbg {
+
+// ------------------------------------------------------------------ scans
+template <int NT>
+__device__ __forceinline__ Pair block_excl_scan_pair(Pair v, Pair* warp_tot, Pair& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    Pair incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        Pair t{__shfl_up_sync(0xffffffffu, incl.g, o), __shfl_up_sync(0xffffffffu, incl.h, o)};
+        if (lane >= o) incl = padd(incl, t);
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        Pair t = lane < NT / 32 ? warp_tot[lane] : Pair{0, 0};
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            Pair u{__shfl_up_sync(0xffffffffu, t.g, o), __shfl_up_sync(0xffffffffu, t.h, o)};
+            if (lane >= o) t = padd(t, u);
+        }
+        if (lane < NT / 32) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    Pair base = warp > 0 ? warp_tot[warp - 1] : Pair{0, 0};
+    total = warp_tot[NT / 32 - 1];
+    __syncthreads();
+    return psub(padd(base, incl), v);
+}
+
+template <int NT>
+__device__ __forceinline__ uint32_t block_excl_scan_u32(uint32_t v, uint32_t* warp_tot, uint32_t& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t t = lane < NT / 32 ? warp_tot[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t u = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += u;
+        }
+        if (lane < NT / 32) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    uint32_t base = warp > 0 ? warp_tot[warp - 1] : 0u;
+    total = warp_tot[NT / 32 - 1];
+    __syncthreads();
+    return base + incl - v;
+}
+
+template <int NT>
+__device__ __forceinline__ unsigned long long block_excl_scan_u64(unsigned long long v, unsigned long long* warp_tot,
+                                                                  unsigned long long& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned long long incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned long long t = lane < NT / 32 ? warp_tot[lane] : 0ull;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            unsigned long long u = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += u;
+        }
+        if (lane < NT / 32) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    unsigned long long base = warp > 0 ? warp_tot[warp - 1] : 0ull;
+    total = warp_tot[NT / 32 - 1];
+    __syncthreads();
+    return base + incl - v;
+}
+
+// Quantizer reciprocals of this round from the device scales (exact: the
+// scales are powers of two).
+__device__ __forceinline__ ScoreParams load_sp(const LevelArgs& a) {
+    ScoreParams sp = a.sp;
+    sp.inv_g = __ddiv_rn(1.0, a.scales[0]);
+    sp.inv_h = __ddiv_rn(1.0, a.scales[1]);
+    return sp;
+}
+
+// Largest j in [0, n) with prefix[j] <= x (prefix ascending, prefix[0] <= x).
+template <class T>
+__device__ __forceinline__ uint32_t find_segment(const T* prefix, uint32_t n, T x) {
+    uint32_t lo = 0, hi = n;  // invariant: prefix[lo] <= x, answer in [lo, hi)
+    while (hi - lo > 1) {
+        uint32_t mid = (lo + hi) >> 1;
+        if (prefix[mid] <= x) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// ------------------------------------------------------------------ gradients
+// data/subsample.rs:45-78 row hash (SplitMix64 finalizer of seed, tree, row).
+__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ bool row_selected(unsigned long long row, unsigned long long th,
+                                             unsigned long long seed, unsigned long long tree) {
+    if (th == ~0ull) return true;
+    unsigned long long t = tree * 0x9E3779B97F4A7C15ull;
+    unsigned long long h = mix64(seed ^ ((t << 23) | (t >> 41)) ^ (row * 0xD6E8FEB86659FD93ull));
+    return (h >> 11) < th;
+}
+
+
+
+__device__ __forceinline__ double bound_of(float v) {
+    return isfinite(v) ? fabs((double)v) : __longlong_as_double(0x7ff0000000000000ll);
+}
+
+// Block max of two non-negative doubles folded into global maxima.  Bit
+// patterns of non-negative doubles order like the values, so an integer max
+// is exact and order independent.
+__device__ __forceinline__ void fold_max(double mg, double mh, unsigned long long* maxbits) {
+    __shared__ unsigned long long smg[32], smh[32];
+    unsigned long long a = (unsigned long long)__double_as_longlong(mg);
+    unsigned long long b = (unsigned long long)__double_as_longlong(mh);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a = max(a, __shfl_down_sync(0xffffffffu, a, o));
+        b = max(b, __shfl_down_sync(0xffffffffu, b, o));
+    }
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { smg[warp] = a; smh[warp] = b; }
+    __syncthreads();
+    if (warp == 0) {
+        int nw = (blockDim.x + 31) >> 5;
+        a = lane < nw ? smg[lane] : 0ull;
+        b = lane < nw ? smh[lane] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            a = max(a, __shfl_down_sync(0xffffffffu, a, o));
+            b = max(b, __shfl_down_sync(0xffffffffu, b, o));
+        }
+        if (lane == 0) { atomicMax(&maxbits[0], a); atomicMax(&maxbits[1], b); }
+    }
+}
+
+__device__ __forceinline__ void fold_sum(Pair s, unsigned long long* sum) {
+    __shared__ long long sg[32], sh[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s.g = (long long)((unsigned long long)s.g + (unsigned long long)__shfl_down_sync(0xffffffffu, s.g, o));
+        s.h = (long long)((unsigned long long)s.h + (unsigned long long)__shfl_down_sync(0xffffffffu, s.h, o));
+    }
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { sg[warp] = s.g; sh[warp] = s.h; }
+    __syncthreads();
+    if (warp == 0) {
+        int nw = (blockDim.x + 31) >> 5;
+        Pair t{lane < nw ? sg[lane] : 0ll, lane < nw ? sh[lane] : 0ll};
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            t.g = (long long)((unsigned long long)t.g + (unsigned long long)__shfl_down_sync(0xffffffffu, t.g, o));
+            t.h = (long long)((unsigned long long)t.h + (unsigned long long)__shfl_down_sync(0xffffffffu, t.h, o));
+        }
+        if (lane == 0) {
+            atomicAdd(&sum[0], (unsigned long long)t.g);
+            atomicAdd(&sum[1], (unsigned long long)t.h);
+        }
+    }
+}
+
+// types.rs:334-337 quantize: round-half-away of v * 2^k (exact product).
+__device__ __forceinline__ Pair to_fixed(float g, float h, double gs, double hs) {
+    return {(long long)round(__dmul_rn((double)g, gs)), (long long)round(__dmul_rn((double)h, hs))};
+}
+
+// Reference exact path (backend upload_and_quantize_gpair_sampled): mask
+// unsampled rows of the host f32 pairs and fold the bounds.
+__global__ void k_mask_max(GradArgs a) {
+    double mg = 0.0, mh = 0.0;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
+        float g = a.gpair_in[2ull * i], h = a.gpair_in[2ull * i + 1];
+        if (!row_selected(a.row0 + i, a.sub_th, a.sub_seed, a.sub_tree)) { g = 0.0f; h = 0.0f; }
+        a.gpair_f32[2ull * i] = g;
+        a.gpair_f32[2ull * i + 1] = h;
+        mg = fmax(mg, bound_of(g));
+        mh = fmax(mh, bound_of(h));
+    }
+    fold_max(mg, mh, a.maxbits);
+}
+
+// objective.rs:37-39,513-526: the gradient of one row, in the reference's f32
+// operation order.  Logistic takes e = expf(-pred) (computed by the host's
+// glibc in exact mode, by CUDA's expf in fast mode).
+__device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, float e, float& g, float& h) {
+    float y = a.label[i];
+    if (a.objective == 1) {
+        float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+        float hh = __fmul_rn(s, __fsub_rn(1.0f, s));
+        g = __fsub_rn(s, y);
+        h = hh < 1e-16f ? 1e-16f : hh;
+    } else {
+        g = __fsub_rn(a.pred[i], y);
+        h = 1.0f;
+    }
+    if (a.weight) {  // training/mod.rs:5498-5505 weighted
+        float w = a.weight[i];
+        g = __fmul_rn(g, w);
+        h = __fmul_rn(h, w);
+    }
+    if (!row_selected(a.row0 + i, a.sub_th, a.sub_seed, a.sub_tree)) { g = 0.0f; h = 0.0f; }
+}
+
+// Gradient pass that only folds bounds and stores the f32 pairs (exact
+// squared error and fast mode).  mode 0: squared error / host exp; mode 1:
+// device expf (fast).
+__global__ void k_gradient_max(GradArgs a, int fast) {
+    double mg = 0.0, mh = 0.0;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
+        float e = 0.0f;
+        if (a.objective == 1) e = fast ? expf(-a.pred[i]) : a.host_exp[i];
+        float g, h;
+        row_gradient(a, i, e, g, h);
+        a.gpair_f32[2ull * i] = g;
+        a.gpair_f32[2ull * i + 1] = h;
+        mg = fmax(mg, bound_of(g));
+        mh = fmax(mh, bound_of(h));
+    }
+    fold_max(mg, mh, a.maxbits);
+}
+
+// Exact logistic with host exp: gradients recomputed on the device from e in
+// the same f32 order as the host, then quantized with the host's scales.
+__global__ void k_gradient_quantize_exp(GradArgs a) {
+    Pair s{0, 0};
+    double gs = a.scales[0], hs = a.scales[1];
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
+        float g, h;
+        row_gradient(a, i, a.host_exp[i], g, h);
+        Pair f = to_fixed(g, h, gs, hs);
+        a.fixed[i] = f;
+        s = padd(s, f);
+    }
+    fold_sum(s, a.sum);
+}
+
+__global__ void k_quantize(GradArgs a) {
+    Pair s{0, 0};
+    double gs = a.scales[0], hs = a.scales[1];
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
+        Pair f = to_fixed(a.gpair_f32[2ull * i], a.gpair_f32[2ull * i + 1], gs, hs);
+        a.fixed[i] = f;
+        s = padd(s, f);
+    }
+    fold_sum(s, a.sum);
+}
+
+// Fast mode: power-of-two scale on the device.  floor(log2(raw)) is taken as
+// the binary exponent (ilogb), as the reference device path does
+// (backend/cuda/histogram.cu:1179-1202); fast mode makes no byte-identity claim.
+__device__ double d_pow2_scale(double max_abs, unsigned long long n_rows) {
+    if (!(max_abs > 0.0) || !isfinite(max_abs)) return 1.0;
+    double budget = __ddiv_rn(4611686018427387904.0, (double)(n_rows > 0 ? n_rows : 1));
+    double raw = __ddiv_rn(budget, max_abs);
+    if (!isfinite(raw) || raw <= 0.0) return 1.0;
+    int k = ilogb(raw);
+    k = k < -1000 ? -1000 : (k > 1000 ? 1000 : k);
+    return ldexp(1.0, k);
+}
+__global__ void k_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales) {
+    scales[0] = d_pow2_scale(__longlong_as_double((long long)maxbits[0]), n_rows);
+    scales[1] = d_pow2_scale(__longlong_as_double((long long)maxbits[1]), n_rows);
+}
+
+// ------------------------------------------------------------------ histogram
+// Exact i64 histograms in shared memory as four 32-bit planes (g_lo, g_hi,
+// h_lo, h_hi).  A 64-bit add is a low-word atomic whose returned old value
+// gives the carry, then a high-word atomic of (hi + carry); the planes then
+// hold exactly the modulo-2^64 sums (hist.rs:94-274 semantics), whatever the
+// order of the additions.
+__device__ __forceinline__ void plane_add(uint32_t* lo, uint32_t* hi, uint32_t idx, long long v) {
+    uint32_t vl = (uint32_t)v;
+    uint32_t vh = (uint32_t)((unsigned long long)v >> 32);
+    uint32_t old = atomicAdd(&lo[idx], vl);
+    vh += (uint32_t)(old + vl < old);
+    if (vh) atomicAdd(&hi[idx], vh);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restrict__ tiles,
+                                                       const TileFeat* __restrict__ tfeat,
+                                                       const uint32_t* __restrict__ rows,
+                                                       const Pair* __restrict__ gpair,
+                                                       const NodeInfo* __restrict__ nodes,
+                                                       const uint32_t* __restrict__ acc_list,
+                                                       const unsigned long long* __restrict__ acc_prefix,
+                                                       const TreeState* __restrict__ st, Pair* __restrict__ hist_acc,
+                                                       unsigned long long slot_pairs) {
+    extern __shared__ uint32_t sm[];
+    const TileDesc td = tiles[blockIdx.y];
+    const uint32_t LB = td.local_bins;
+    uint32_t* glo = sm;
+    uint32_t* ghi = sm + LB;
+    uint32_t* hlo = sm + 2 * LB;
+    uint32_t* hhi = sm + 3 * LB;
+    TileFeat* tf = reinterpret_cast<TileFeat*>(sm + 4 * LB);
+    const unsigned long long R = st->acc_total;
+    const uint32_t n_acc = st->acc_count;
+    if (R == 0) return;
+    unsigned long long a = R * blockIdx.x / gridDim.x;
+    const unsigned long long b = R * (blockIdx.x + 1) / gridDim.x;
+    if (a >= b) return;
+    for (uint32_t t = threadIdx.x; t < td.n_feat; t += blockDim.x) tf[t] = tfeat[td.feat_begin + t];
+    for (uint32_t j = threadIdx.x; j < 4 * LB; j += blockDim.x) sm[j] = 0u;
+    __syncthreads();
+    const uint32_t nf = td.n_feat;
+    uint32_t k = find_segment(acc_prefix, n_acc, a);
+    while (a < b) {
+        const uint32_t node = acc_list[k];
+        const NodeInfo ni = nodes[node];
+        const unsigned long long seg_end = min(b, acc_prefix[k + 1]);
+        const uint32_t base = ni.start + (uint32_t)(a - acc_prefix[k]);
+        const uint32_t cnt = (uint32_t)(seg_end - a);
+        for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+            const uint32_t r = rows[base + i];
+            const Pair gp = gpair[r];
+            const uint8_t* rec = td.base + (size_t)r * td.stride;
+            for (uint32_t t = 0; t < nf; t++) {
+                const TileFeat f = tf[t];
+                uint32_t bin = W == 2 ? (uint32_t)(*reinterpret_cast<const uint16_t*>(rec + f.byte_off))
+                                      : (uint32_t)rec[f.byte_off];
+                if (bin == td.missing || bin >= f.nbins) continue;
+                const uint32_t idx = f.local_off + bin;
+                plane_add(glo, ghi, idx, gp.g);
+                plane_add(hlo, hhi, idx, gp.h);
+            }
+        }
+        __syncthreads();
+        // flush: one 64-bit global atomic per non-zero word, then clear
+        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
+        for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
+            unsigned long long g = ((unsigned long long)ghi[j] << 32) | glo[j];
+            unsigned long long h = ((unsigned long long)hhi[j] << 32) | hlo[j];
+            if (g | h) {
+                uint32_t lo = 0, hi = nf;
+                while (hi - lo > 1) {
+                    uint32_t mid = (lo + hi) >> 1;
+                    if (tf[mid].local_off <= j) lo = mid; else hi = mid;
+                }
+                const uint32_t gidx = tf[lo].global_off + (j - tf[lo].local_off);
+                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
+                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
+                glo[j] = 0u; ghi[j] = 0u; hlo[j] = 0u; hhi[j] = 0u;
+            }
+        }
+        __syncthreads();
+        a = seg_end;
+        k++;
+    }
+}
+
+// ------------------------------------------------------------------ split
+struct SplitSmem {
+    Pair warp_tot[32];
+    SplitRec best[kSplitThreads];
+    float w[kSplitThreads];
+    uint32_t idx[kSplitThreads];
+    uint32_t set_words[8];
+};
+
+__device__ __forceinline__ void consider(SplitRec& best, float gain, uint32_t ord, uint32_t bin, uint32_t flags,
+                                         Pair l, Pair r) {
+    if (!(gain > 1e-6f)) return;  // split.rs:260-270 update_best (NaN filtered too)
+    if (!(best.flags & 1u) || gain > best.gain || (gain == best.gain && ord < best.ord)) {
+        best.gain = gain; best.ord = ord; best.bin = bin; best.flags = flags | 1u;
+        best.left = l; best.right = r;
+    }
+}
+
+__device__ __forceinline__ void block_best(SplitSmem& s, SplitRec& mine) {
+    s.best[threadIdx.x] = mine;
+    __syncthreads();
+    for (int stride = kSplitThreads / 2; stride > 0; stride >>= 1) {
+        if ((int)threadIdx.x < stride && rec_better(s.best[threadIdx.x + stride], s.best[threadIdx.x]))
+            s.best[threadIdx.x] = s.best[threadIdx.x + stride];
+        __syncthreads();
+    }
+}
+
+// Per (node, feature) CTA: finish the node histogram (copy or parent minus
+// sibling), scan it, score every candidate and keep the first maximum in the
+// reference's enumeration order (split.rs:331-461; categorical :484-617).
+__global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
+    const uint32_t node = blockIdx.x, f = blockIdx.y, F = a.n_features;
+    if (node >= a.st->m) return;
+    SplitRec* out = a.feat_best + (size_t)node * F + f;
+    if (!a.enabled[f]) {
+        if (threadIdx.x == 0) out->flags = 0;
+        return;
+    }
+    __shared__ SplitSmem s;
+    const NodeInfo ni = a.nodes[node];
+    const uint32_t off = a.hoff[f], nb = a.hoff[f + 1] - off;
+    const Pair* acc = a.hist_acc + (unsigned long long)ni.acc_slot * a.slot_pairs + off;
+    const Pair* par = ni.parent_slot >= 0 ? a.hist_prev + (unsigned long long)ni.parent_slot * a.slot_pairs + off
+                                          : nullptr;
+    Pair* h = a.hist_cur + (unsigned long long)node * a.slot_pairs + off;
+    const bool keep_hist = !a.last_level;
+    const Pair sum = ni.sum;
+    const ScoreParams sp = load_sp(a);
+    const float parent_gain = node_gain(sum, sp, ni.lower, ni.upper);
+    const int cons = a.mono ? (int)a.mono[f] : 0;
+    SplitRec mine;
+    mine.flags = 0; mine.gain = 0.0f; mine.ord = 0xffffffffu; mine.bin = 0; mine.feat = f;
+    mine.left = Pair{0, 0}; mine.right = Pair{0, 0};
+
+    if (a.is_cat && a.is_cat[f]) {
+        // ---- categorical: one bin per category code, n <= 256 (one per thread)
+        const uint32_t n = nb, t = threadIdx.x;
+        Pair x{0, 0};
+        if (t < n) {
+            x = par ? psub(par[t], acc[t]) : acc[t];
+            if (keep_hist) h[t] = x;
+        }
+        if (n < a.max_onehot) {
+            Pair tot;
+            (void)block_excl_scan_pair<kSplitThreads>(x, s.warp_tot, tot);
+            const Pair missing = psub(sum, tot);
+            if (t < n) {
+                float gain;
+                Pair l = psub(sum, x);
+                if (split_gain(parent_gain, l, x, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, 2 * t, t, 2u | 4u, l, x);
+                Pair r = padd(x, missing);
+                l = psub(sum, r);
+                if (split_gain(parent_gain, l, r, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, 2 * t + 1, t, 4u, l, r);
+            }
+            block_best(s, mine);
+            if (threadIdx.x == 0) {
+                SplitRec b = s.best[0];
+                b.feat = f;
+                *out = b;
+                uint32_t* cw = a.feat_cats + ((size_t)node * F + f) * 8;
+                for (int w = 0; w < 8; w++) cw[w] = 0u;
+                if (b.flags & 1u) cw[b.bin >> 5] = 1u << (b.bin & 31);
+            }
+            return;
+        }
+        // partition mode: stable sort of categories by weight (CalcWeightCat)
+        float w = __int_as_float(0x7f800000);
+        if (t < n) w = xgb_weight(to_f64(x.g, sp.inv_g), to_f64(x.h, sp.inv_h), sp);
+        s.w[t] = w;
+        s.idx[t] = t;
+        __syncthreads();
+        for (uint32_t size = 2; size <= kSplitThreads; size <<= 1) {
+            for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+                uint32_t partner = t ^ stride;
+                if (partner > t) {
+                    bool up = (t & size) == 0;
+                    float wa = s.w[t], wb = s.w[partner];
+                    uint32_t ia = s.idx[t], ib = s.idx[partner];
+                    // (weight, index) order == std::stable_sort by `<` on weight
+                    bool a_gt_b = (wb < wa) || (!(wa < wb) && ib < ia);
+                    if (a_gt_b == up) {
+                        s.w[t] = wb; s.w[partner] = wa;
+                        s.idx[t] = ib; s.idx[partner] = ia;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        const uint32_t cat = s.idx[t];
+        Pair xs = t < n ? (par ? psub(par[cat], acc[cat]) : acc[cat]) : Pair{0, 0};
+        Pair tot;
+        Pair excl = block_excl_scan_pair<kSplitThreads>(xs, s.warp_tot, tot);
+        const uint32_t n_scan = min(a.max_cat_threshold, n);
+        if (n_scan >= 2 && t < n) {
+            float gain;
+            if (t + 1 < n_scan) {  // forward: first t+1 sorted categories go right, missing left
+                Pair r = padd(excl, xs);
+                Pair l = psub(sum, r);
+                if (split_gain(parent_gain, l, r, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, t, t + 1, 2u | 4u, l, r);
+            }
+            if (t >= n - (n_scan - 1)) {  // backward: sorted tail from t goes left, missing right
+                Pair l = psub(tot, excl);
+                Pair r = psub(sum, l);
+                if (split_gain(parent_gain, l, r, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, (n_scan - 1) + (n - 1 - t), t, 4u, l, r);
+            }
+        }
+        block_best(s, mine);
+        SplitRec b = s.best[0];
+        if (t < 8) s.set_words[t] = 0u;
+        __syncthreads();
+        if ((b.flags & 1u) && t < b.bin) atomicOr(&s.set_words[cat >> 5], 1u << (cat & 31));
+        __syncthreads();
+        if (t == 0) {
+            b.feat = f;
+            *out = b;
+            uint32_t* cw = a.feat_cats + ((size_t)node * F + f) * 8;
+            for (int wi = 0; wi < 8; wi++) cw[wi] = s.set_words[wi];
+        }
+        return;
+    }
+
+    // ---- numeric feature: forward (missing right) then reverse (missing left)
+    const uint32_t bpt = (nb + kSplitThreads - 1) / kSplitThreads;
+    const uint32_t b0 = threadIdx.x * bpt;
+    Pair v[kMaxBinsPerThread];
+    Pair loc{0, 0};
+#pragma unroll
+    for (int k = 0; k < kMaxBinsPerThread; k++) {
+        uint32_t bidx = b0 + k;
+        Pair x{0, 0};
+        if (k < (int)bpt && bidx < nb) {
+            x = par ? psub(par[bidx], acc[bidx]) : acc[bidx];
+            if (keep_hist) h[bidx] = x;
+        }
+        v[k] = x;
+        loc = padd(loc, x);
+    }
+    Pair total;
+    Pair run = block_excl_scan_pair<kSplitThreads>(loc, s.warp_tot, total);
+    const bool reverse = !peq(total, sum);
+#pragma unroll
+    for (int k = 0; k < kMaxBinsPerThread; k++) {
+        uint32_t bidx = b0 + k;
+        if (k < (int)bpt && bidx < nb) {
+            Pair excl = run;
+            run = padd(run, v[k]);
+            float gain;
+            Pair r = psub(sum, run);
+            if (split_gain(parent_gain, run, r, cons, ni.lower, ni.upper, sp, gain))
+                consider(mine, gain, bidx, bidx + 1, 0u, run, r);
+            if (reverse) {
+                Pair rr = psub(total, excl);
+                Pair ll = psub(sum, rr);
+                if (split_gain(parent_gain, ll, rr, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, nb + (nb - 1 - bidx), bidx, 2u, ll, rr);
+            }
+        }
+    }
+    block_best(s, mine);
+    if (threadIdx.x == 0) {
+        SplitRec b = s.best[0];
+        b.feat = f;
+        *out = b;
+    }
+}
+
+// Per node: the best feature (equal gains -> lower feature id, split.rs:631-642).
+__global__ void k_split_node(LevelArgs a) {
+    const uint32_t node = blockIdx.x;
+    if (node >= a.st->m) return;
+    const uint32_t F = a.n_features, lane = threadIdx.x;
+    float bg = 0.0f;
+    uint32_t bf = 0xffffffffu;
+    bool have = false;
+    for (uint32_t f = lane; f < F; f += 32) {
+        const SplitRec& r = a.feat_best[(size_t)node * F + f];
+        if (!(r.flags & 1u)) continue;
+        if (!have || r.gain > bg) { bg = r.gain; bf = f; have = true; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float og = __shfl_down_sync(0xffffffffu, bg, o);
+        uint32_t of = __shfl_down_sync(0xffffffffu, bf, o);
+        bool oh = __shfl_down_sync(0xffffffffu, (int)have, o);
+        if (oh && (!have || og > bg || (og == bg && of < bf))) { bg = og; bf = of; have = true; }
+    }
+    have = __shfl_sync(0xffffffffu, (int)have, 0) != 0;
+    bf = __shfl_sync(0xffffffffu, bf, 0);
+    if (lane == 0) {
+        SplitRec r;
+        if (have) {
+            r = a.feat_best[(size_t)node * F + bf];
+            r.feat = bf;
+        } else {
+            r.flags = 0;
+        }
+        a.node_best[node] = r;
+    }
+    if (have && lane < 8 && a.is_cat && a.is_cat[bf])
+        a.node_cats[node * 8 + lane] = a.feat_cats[((size_t)node * F + bf) * 8 + lane];
+}
+
+// Depthwise decisions of one level (one CTA): the max_leaves budget in node
+// order (training/mod.rs:4140-4151), tree arrays of the split nodes and their
+// children (tree.rs:140-170 split_leaf; mod.rs:5069-5103 leaf values), and
+// the children's sums / bounds.
+__global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    TreeState* st = a.st;
+    const uint32_t m = st->m;
+    const uint32_t leaf_count = st->leaf_count;
+    const uint32_t base_nodes = st->n_tree_nodes;
+    const uint32_t remaining = a.max_leaves == 0 ? 0xffffffffu
+                                                 : (a.max_leaves > leaf_count ? a.max_leaves - leaf_count : 0u);
+    const ScoreParams sp = load_sp(a);
+    uint32_t found_before = 0;
+    for (uint32_t c = 0; c < m; c += 1024) {
+        const uint32_t i = c + threadIdx.x;
+        const bool found = i < m && (a.node_best[i].flags & 1u);
+        uint32_t tot;
+        const uint32_t rank = found_before + block_excl_scan_u32<1024>(found ? 1u : 0u, wt, tot);
+        found_before += tot;
+        if (i < m) {
+            SplitDesc sd{-1, 0, 0, 0};
+            if (found && rank < remaining) {
+                const SplitRec b = a.node_best[i];
+                const NodeInfo ni = a.nodes[i];
+                const uint32_t k = rank;
+                const int32_t L = (int32_t)(base_nodes + 2 * k), Rt = L + 1;
+                const double lg = to_f64(b.left.g, sp.inv_g), lh = to_f64(b.left.h, sp.inv_h);
+                const double rg = to_f64(b.right.g, sp.inv_g), rh = to_f64(b.right.h, sp.inv_h);
+                const float wl = apply_bounds(xgb_weight(lg, lh, sp), ni.lower, ni.upper);
+                const float wr = apply_bounds(xgb_weight(rg, rh, sp), ni.lower, ni.upper);
+                const int cons = a.mono ? (int)a.mono[b.feat] : 0;
+                const float mid = __fdiv_rn(__fadd_rn(wl, wr), 2.0f);
+                float llo = ni.lower, lhi = ni.upper, rlo = ni.lower, rhi = ni.upper;
+                if (cons < 0) { llo = mid; rhi = mid; } else if (cons > 0) { lhi = mid; rlo = mid; }
+                const bool is_cat = (b.flags & 4u) != 0;
+                TreeRec p;
+                p.left = L; p.right = Rt; p.feat = b.feat; p.bin = b.bin; p.gain = b.gain; p.leaf = 0.0f;
+                p.hess = a.trec[ni.tree_id].hess;
+                p.flags = ((b.flags & 2u) ? 2u : 0u) | (is_cat ? 4u : 0u);
+                a.trec[ni.tree_id] = p;
+                if (is_cat)
+                    for (int w = 0; w < 8; w++) a.tcats[(size_t)ni.tree_id * 8 + w] = a.node_cats[i * 8 + w];
+                TreeRec cl{-1, -1, 0, 0, 0.0f, __fmul_rn(wl, sp.eta), __double2float_rn(lh), 1u};
+                TreeRec cr{-1, -1, 0, 0, 0.0f, __fmul_rn(wr, sp.eta), __double2float_rn(rh), 1u};
+                a.trec[L] = cl;
+                a.trec[Rt] = cr;
+                NodeInfo nl, nr;
+                nl.tree_id = L; nl.sum = b.left; nl.lower = llo; nl.upper = lhi;
+                nr.tree_id = Rt; nr.sum = b.right; nr.lower = rlo; nr.upper = rhi;
+                nl.start = nr.start = 0; nl.len = nr.len = 0; nl.parent_slot = nr.parent_slot = -1;
+                nl.acc_slot = nr.acc_slot = 0; nl.len_global = nr.len_global = 0;
+                a.next_nodes[2 * k] = nl;
+                a.next_nodes[2 * k + 1] = nr;
+                sd.child_slot = (int32_t)(2 * k);
+                sd.feat = b.feat;
+                sd.bin = b.bin;
+                sd.flags = b.flags & 6u;
+            }
+            a.split[i] = sd;
+        }
+    }
+    if (threadIdx.x == 0) {
+        const uint32_t kept = min(found_before, remaining);
+        st->kept = kept;
+        st->n_tree_nodes = base_nodes + 2 * kept;
+        st->leaf_count = leaf_count + kept;
+    }
+}
+
+// ------------------------------------------------------------------ partition
+__device__ __forceinline__ bool goes_left(const LevelArgs& a, const SplitDesc& sd, const uint32_t* cats,
+                                          uint32_t row) {
+    const FeatLoc fl = a.floc[sd.feat];
+    const uint8_t* p = fl.base + (size_t)row * fl.stride + fl.byte_off;
+    uint32_t bin = fl.width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+    if (bin == fl.missing) return (sd.flags & 2u) != 0;
+    if (sd.flags & 4u) return bin >= 256u || ((cats[bin >> 5] >> (bin & 31)) & 1u) == 0u;
+    return bin < sd.bin;
+}
+
+// Count the left rows of every chunk of a split node; add the leaf value to
+// the predictions of every row of a node that stops growing here
+// (training/mod.rs:4409-4425; delta[row] = leaf, then pred += delta, is the
+// same single f32 addition).
+__global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    __shared__ uint32_t cats[8];
+    const uint32_t c = blockIdx.x;
+    const TreeState* st = a.st;
+    if (c >= st->chunk_count) return;
+    const uint32_t m = st->m;
+    const uint32_t j = find_segment(a.chunk_prefix, m, c);
+    const NodeInfo ni = a.nodes[j];
+    const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
+    const uint32_t cnt = min(kChunkRows, ni.len - r0);
+    const uint32_t* rows = a.rows_cur + ni.start + r0;
+    const SplitDesc sd = a.split[j];
+    if (sd.child_slot < 0) {
+        const float leaf = a.trec[ni.tree_id].leaf;
+        for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+            const uint32_t r = rows[i];
+            a.pred[r] = __fadd_rn(a.pred[r], leaf);
+        }
+        if (threadIdx.x == 0) a.chunk_left[c] = 0u;
+        return;
+    }
+    if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
+    __syncthreads();
+    uint32_t nleft = 0;
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) nleft += goes_left(a, sd, cats, rows[i]) ? 1u : 0u;
+    uint32_t tot;
+    (void)block_excl_scan_u32<kPartThreads>(nleft, wt, tot);
+    if (threadIdx.x == 0) a.chunk_left[c] = tot;
+}
+
+// Exclusive scan of the chunk left counts (one CTA) and per-node left totals.
+__global__ void __launch_bounds__(1024) k_part_scan(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    const TreeState* st = a.st;
+    const uint32_t nc = st->chunk_count, m = st->m;
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < nc; base += 1024) {
+        const uint32_t c = base + threadIdx.x;
+        const uint32_t v = c < nc ? a.chunk_left[c] : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan_u32<1024>(v, wt, tot);
+        if (c < nc) a.chunk_off[c] = carry + ex;
+        carry += tot;
+    }
+    __syncthreads();
+    for (uint32_t j = threadIdx.x; j < m; j += blockDim.x) {
+        const uint32_t c0 = a.chunk_prefix[j], c1 = a.chunk_prefix[j + 1];
+        const uint32_t first = c0 < nc ? a.chunk_off[c0] : carry;
+        const uint32_t last = c1 < nc ? a.chunk_off[c1] : carry;
+        a.node_left[j] = last - first;
+    }
+}
+
+// Stable scatter of every chunk of a split node into [left | right] of the
+// node's span in the next arena.
+__global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    __shared__ uint32_t cats[8];
+    __shared__ uint32_t stage[kChunkRows];
+    const uint32_t c = blockIdx.x;
+    const TreeState* st = a.st;
+    if (c >= st->chunk_count) return;
+    const uint32_t m = st->m;
+    const uint32_t j = find_segment(a.chunk_prefix, m, c);
+    const SplitDesc sd = a.split[j];
+    if (sd.child_slot < 0) return;
+    const NodeInfo ni = a.nodes[j];
+    const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
+    const uint32_t cnt = min(kChunkRows, ni.len - r0);
+    const uint32_t* rows = a.rows_cur + ni.start + r0;
+    if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
+    __syncthreads();
+    uint32_t r[kPartItems];
+    uint32_t flags = 0, nl = 0;
+    const uint32_t i0 = threadIdx.x * kPartItems;
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        const uint32_t i = i0 + k;
+        r[k] = i < cnt ? rows[i] : 0u;
+        if (i < cnt && goes_left(a, sd, cats, r[k])) { flags |= 1u << k; nl++; }
+    }
+    uint32_t L;
+    const uint32_t lpos = block_excl_scan_u32<kPartThreads>(nl, wt, L);
+    uint32_t li = lpos, ri = L + (min(i0, cnt) - lpos);
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        const uint32_t i = i0 + k;
+        if (i < cnt) {
+            if (flags & (1u << k)) stage[li++] = r[k];
+            else stage[ri++] = r[k];
+        }
+    }
+    __syncthreads();
+    const uint32_t node_first = a.chunk_off[a.chunk_prefix[j]];
+    const uint32_t left_before = a.chunk_off[c] - node_first;
+    const uint32_t right_before = r0 - left_before;
+    const uint32_t node_nl = a.node_left[j];
+    uint32_t* dst_l = a.rows_next + ni.start + left_before;
+    uint32_t* dst_r = a.rows_next + ni.start + node_nl + right_before;
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+        if (i < L) dst_l[i] = stage[i];
+        else dst_r[i - L] = stage[i];
+    }
+}
+
+// Next level's node table, accumulate list and chunk table (one CTA).  The
+// smaller child (by rows over all ranks; training/mod.rs:4478-4482) is
+// accumulated, the larger one is its parent minus the smaller one.
+__global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
+    __shared__ unsigned long long wt64[32];
+    __shared__ uint32_t wt[32];
+    TreeState* st = a.st;
+    const uint32_t m = st->m, kept = st->kept;
+    for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
+        const SplitDesc sd = a.split[i];
+        if (sd.child_slot < 0) continue;
+        const uint32_t k = (uint32_t)sd.child_slot >> 1;
+        const NodeInfo ni = a.nodes[i];
+        const uint32_t nl = a.node_left[i], nr = ni.len - nl;
+        const uint32_t nlg = a.node_left_global[i], nrg = ni.len_global - nlg;
+        NodeInfo& L = a.next_nodes[2 * k];
+        NodeInfo& R = a.next_nodes[2 * k + 1];
+        L.start = ni.start; L.len = nl; L.len_global = nlg;
+        R.start = ni.start + nl; R.len = nr; R.len_global = nrg;
+        const uint32_t small = nlg <= nrg ? 0u : 1u;
+        L.acc_slot = (int32_t)k; R.acc_slot = (int32_t)k;
+        L.parent_slot = small == 0 ? -1 : (int32_t)i;
+        R.parent_slot = small == 1 ? -1 : (int32_t)i;
+        a.next_acc_list[k] = 2 * k + small;
+    }
+    __syncthreads();
+    unsigned long long carry = 0;
+    for (uint32_t base = 0; base < kept; base += 1024) {
+        const uint32_t k = base + threadIdx.x;
+        unsigned long long v = k < kept ? a.next_nodes[a.next_acc_list[k]].len : 0ull;
+        unsigned long long tot;
+        unsigned long long ex = block_excl_scan_u64<1024>(v, wt64, tot);
+        if (k < kept) a.next_acc_prefix[k] = carry + ex;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) a.next_acc_prefix[kept] = carry;
+    uint32_t ccarry = 0;
+    const uint32_t m2 = 2 * kept;
+    for (uint32_t base = 0; base < m2; base += 1024) {
+        const uint32_t s = base + threadIdx.x;
+        const uint32_t v = s < m2 ? (a.next_nodes[s].len + kChunkRows - 1) / kChunkRows : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan_u32<1024>(v, wt, tot);
+        if (s < m2) a.next_chunk_prefix[s] = ccarry + ex;
+        ccarry += tot;
+    }
+    if (threadIdx.x == 0) {
+        a.next_chunk_prefix[m2] = ccarry;
+        st->m = m2;
+        st->acc_count = kept;
+        st->acc_total = carry;
+        st->chunk_count = ccarry;
+    }
+}
+
+// Final level: every remaining node is a leaf (training/mod.rs:4524-4550).
+__global__ void __launch_bounds__(kPartThreads) k_leaf_final(LevelArgs a) {
+    const uint32_t c = blockIdx.x;
+    const TreeState* st = a.st;
+    if (c >= st->chunk_count) return;
+    const uint32_t j = find_segment(a.chunk_prefix, st->m, c);
+    const NodeInfo ni = a.nodes[j];
+    const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
+    const uint32_t cnt = min(kChunkRows, ni.len - r0);
+    const uint32_t* rows = a.rows_cur + ni.start + r0;
+    const float leaf = a.trec[ni.tree_id].leaf;
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+        const uint32_t r = rows[i];
+        a.pred[r] = __fadd_rn(a.pred[r], leaf);
+    }
+}
+
+// Root of a new tree (training/mod.rs:3466-3469, 3499-3501).
+__global__ void k_tree_init(LevelArgs a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum) {
+    if (threadIdx.x != 0) return;
+    const Pair sum{(long long)root_sum[0], (long long)root_sum[1]};
+    NodeInfo r;
+    r.start = 0; r.len = n_local; r.tree_id = 0; r.parent_slot = -1; r.acc_slot = 0;
+    r.lower = -FLT_MAX; r.upper = FLT_MAX; r.len_global = n_global; r.sum = sum;
+    a.nodes[0] = r;
+    const ScoreParams sp = load_sp(a);
+    const double g = to_f64(sum.g, sp.inv_g), h = to_f64(sum.h, sp.inv_h);
+    TreeRec t{-1, -1, 0, 0, 0.0f, __fmul_rn(xgb_weight(g, h, sp), sp.eta), __double2float_rn(h), 1u};
+    a.trec[0] = t;
+    const_cast<uint32_t*>(a.acc_list)[0] = 0;
+    const_cast<unsigned long long*>(a.acc_prefix)[0] = 0;
+    const_cast<unsigned long long*>(a.acc_prefix)[1] = n_local;
+    const_cast<uint32_t*>(a.chunk_prefix)[0] = 0;
+    const_cast<uint32_t*>(a.chunk_prefix)[1] = (n_local + kChunkRows - 1) / kChunkRows;
+    TreeState* st = a.st;
+    st->m = 1; st->n_tree_nodes = 1; st->leaf_count = 1; st->acc_count = 1; st->acc_total = n_local;
+    st->chunk_count = (n_local + kChunkRows - 1) / kChunkRows; st->kept = 0; st->error = 0;
+}
+
+__global__ void k_iota(uint32_t* rows, uint32_t n) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += blockDim.x * gridDim.x) rows[i] = i;
+}
+
+// Column-major block (reference BinData, columns.rs:9-25) to the device's
+// row-major record layout: dst[row * stride + local * width].
+template <int W>
+__global__ void k_transpose_block(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint32_t n_rows,
+                                  uint32_t n_feats, uint32_t stride, uint64_t row0) {
+    for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < (uint64_t)n_rows * n_feats;
+         idx += (uint64_t)blockDim.x * gridDim.x) {
+        const uint32_t f = (uint32_t)(idx / n_rows);
+        const uint32_t r = (uint32_t)(idx % n_rows);
+        if (W == 2) {
+            const uint16_t v = reinterpret_cast<const uint16_t*>(src)[(size_t)f * n_rows + r];
+            *reinterpret_cast<uint16_t*>(dst + (size_t)(row0 + r) * stride + (size_t)f * 2) = v;
+        } else {
+            dst[(size_t)(row0 + r) * stride + f] = src[(size_t)f * n_rows + r];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ launchers
+static unsigned grad_grid(uint32_t n) {
+    unsigned b = (n + 255) / 256;
+    return b < 148u * 8u ? (b ? b : 1u) : 148u * 8u;
+}
+void launch_mask_max(const GradArgs& a, cudaStream_t s) { k_mask_max<<<grad_grid(a.n), 256, 0, s>>>(a); }
+void launch_gradient_max(const GradArgs& a, int fast, cudaStream_t s) {
+    k_gradient_max<<<grad_grid(a.n), 256, 0, s>>>(a, fast);
+}
+void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s) {
+    k_gradient_quantize_exp<<<grad_grid(a.n), 256, 0, s>>>(a);
+}
+void launch_quantize(const GradArgs& a, cudaStream_t s) { k_quantize<<<grad_grid(a.n), 256, 0, s>>>(a); }
+void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
+                          cudaStream_t s) {
+    k_device_scales<<<1, 1, 0, s>>>(maxbits, n_rows, scales);
+}
+void set_hist_smem_limit(int bytes) {
+    cudaFuncSetAttribute(k_hist<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+void launch_hist(int width, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat, const uint32_t* rows,
+                 const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                 const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                 unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s) {
+    if (n_tiles == 0) return;
+    dim3 grid(grid_x, n_tiles);
+    if (width == 2)
+        k_hist<2><<<grid, kHistThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix, st,
+                                                   hist_acc, slot_pairs);
+    else
+        k_hist<1><<<grid, kHistThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix, st,
+                                                   hist_acc, slot_pairs);
+}
+void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
+    dim3 grid(max_m, a.n_features);
+    k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    k_split_node<<<max_m, 32, 0, s>>>(a);
+}
+void launch_decide(const LevelArgs& a, cudaStream_t s) { k_decide<<<1, 1024, 0, s>>>(a); }
+void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    k_part_count<<<max_chunks, kPartThreads, 0, s>>>(a);
+}
+void launch_part_scan(const LevelArgs& a, cudaStream_t s) { k_part_scan<<<1, 1024, 0, s>>>(a); }
+void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    k_part_scatter<<<max_chunks, kPartThreads, 0, s>>>(a);
+}
+void launch_next_level(const LevelArgs& a, cudaStream_t s) { k_next_level<<<1, 1024, 0, s>>>(a); }
+void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    k_leaf_final<<<max_chunks, kPartThreads, 0, s>>>(a);
+}
+void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
+                      cudaStream_t s) {
+    k_tree_init<<<1, 32, 0, s>>>(a, n_local, n_global, root_sum);
+}
+void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s) {
+    k_iota<<<grad_grid(n), 256, 0, s>>>(rows, n);
+}
+void launch_transpose(int width, const uint8_t* src, uint8_t* dst, uint32_t n_rows, uint32_t n_feats,
+                      uint32_t stride, uint64_t row0, cudaStream_t s) {
+    if (width == 2) k_transpose_block<2><<<148 * 16, 256, 0, s>>>(src, dst, n_rows, n_feats, stride, row0);
+    else k_transpose_block<1><<<148 * 16, 256, 0, s>>>(src, dst, n_rows, n_feats, stride, row0);
+}
+
+// Explicit instantiations used by the host code.
+template __global__ void k_hist<1>(const TileDesc*, const TileFeat*, const uint32_t*, const Pair*, const NodeInfo*,
+                                   const uint32_t*, const unsigned long long*, const TreeState*, Pair*,
+                                   unsigned long long);
+template __global__ void k_hist<2>(const TileDesc*, const TileFeat*, const uint32_t*, const Pair*, const NodeInfo*,
+                                   const uint32_t*, const unsigned long long*, const TreeState*, Pair*,
+                                   unsigned long long);
+template __global__ void k_transpose_block<1>(const uint8_t*, uint8_t*, uint32_t, uint32_t, uint32_t, uint64_t);
+template __global__ void k_transpose_block<2>(const uint8_t*, uint8_t*, uint32_t, uint32_t, uint32_t, uint64_t);
+
+}  // namespace fbg

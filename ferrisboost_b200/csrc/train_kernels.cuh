@@ -1,0 +1,148 @@
+// Device-side tree growth for sm_100a.
+//
+// One tree is grown level by level entirely on the device: the histogram,
+// split, decision, partition and next-level kernels of every level are
+// enqueued back to back on one stream and read their node counts from device
+// memory (TreeState), so growing a tree needs no host round trip.  The host
+// reads the finished tree arrays once.  Kernels launched with an upper-bound
+// grid return early for the nodes / chunks that do not exist in a level.
+//
+// The arithmetic restates the reference CPU engine (mdai001/FerrisBoost):
+// histograms are i64 fixed-point sums modulo 2^64 (src/training/hist.rs),
+// split scoring follows src/training/split.rs:182-461 in the given-weight
+// form, partitions are stable (src/training/mod.rs:5169-5429) and leaf values
+// follow src/training/mod.rs:5069-5103.
+#pragma once
+#include "common.cuh"
+
+namespace fbg {
+
+constexpr int kSplitThreads = 256;
+constexpr int kMaxBinsPerThread = 4;  // features up to 1024 bins per CTA scan
+constexpr uint32_t kChunkRows = 4096; // partition / leaf chunk
+constexpr int kPartThreads = 512;
+constexpr int kPartItems = kChunkRows / kPartThreads;
+constexpr int kHistThreads = 512;
+
+// A histogram tile: a set of features of one storage block whose bins fit in
+// shared memory.  Features are listed in TileFeat[feat_begin, feat_begin+n).
+struct TileDesc {
+    const uint8_t* base;  // row-major bins of the storage block
+    uint32_t stride;      // bytes per row (multiple of 16)
+    uint32_t width;       // bytes per bin (1 or 2)
+    uint32_t feat_begin;
+    uint32_t n_feat;
+    uint32_t local_bins;  // shared-memory bins of this tile
+    uint32_t missing;     // missing-value sentinel of this width
+};
+struct TileFeat {
+    uint32_t byte_off;    // byte offset of the feature inside a row record
+    uint32_t local_off;   // first bin in the tile's shared histogram
+    uint32_t nbins;
+    uint32_t global_off;  // first bin in the node histogram
+};
+
+// Per-feature bin locator for partitions.
+struct FeatLoc {
+    const uint8_t* base;
+    uint32_t stride;
+    uint32_t byte_off;
+    uint32_t width;
+    uint32_t missing;
+};
+
+// Per-node split decision of the current level.
+struct SplitDesc {
+    int32_t child_slot;  // -1: terminal; else slot of the left child in the next level
+    uint32_t feat;
+    uint32_t bin;
+    uint32_t flags;      // bit1 missing left, bit2 categorical
+};
+
+struct LevelArgs {
+    // tree-wide
+    uint32_t n_features;
+    uint32_t max_leaves;
+    uint32_t depth;
+    uint32_t last_level;         // 1 when depth + 1 == max_depth (children are final leaves)
+    ScoreParams sp;              // inv_g / inv_h are taken from `scales` on the device
+    const double* scales;        // [2] quantizer scales of this round (device)
+    const uint32_t* hoff;        // F+1 node-histogram offsets
+    const uint8_t* enabled;      // per feature (colsample)
+    const int8_t* mono;          // per feature monotone direction (may be null)
+    const uint8_t* is_cat;       // per feature categorical flag (may be null)
+    uint32_t max_onehot, max_cat_threshold;
+    const FeatLoc* floc;
+    // level buffers
+    TreeState* st;
+    NodeInfo* nodes;             // current level
+    NodeInfo* next_nodes;        // next level
+    const uint32_t* acc_list;    // current level: node index of each accumulate node
+    const unsigned long long* acc_prefix;  // acc_count+1 row prefix
+    uint32_t* next_acc_list;
+    unsigned long long* next_acc_prefix;
+    const uint32_t* chunk_prefix; // m+1 chunk prefix of the current level
+    uint32_t* next_chunk_prefix;
+    Pair* hist_acc;              // accumulate-node histograms (acc index slots)
+    Pair* hist_cur;              // full histograms of this level (node slots)
+    const Pair* hist_prev;       // full histograms of the previous level
+    unsigned long long slot_pairs; // pairs per histogram slot (total bins)
+    SplitRec* feat_best;         // [node * F + f]
+    uint32_t* feat_cats;         // [node * F + f][8]
+    SplitRec* node_best;         // [node]
+    uint32_t* node_cats;         // [node][8]
+    SplitDesc* split;            // [node]
+    uint32_t* chunk_left;        // per chunk left count
+    uint32_t* chunk_off;         // per chunk left offset within its node
+    uint32_t* node_left;         // per node left count (this rank)
+    const uint32_t* node_left_global; // per node left count over all ranks
+    const uint32_t* rows_cur;
+    uint32_t* rows_next;
+    float* pred;
+    TreeRec* trec;
+    uint32_t* tcats;             // [tree node][8]
+};
+
+struct GradArgs {
+    uint32_t n;               // rows on this rank
+    unsigned long long row0;  // global index of this rank's first row (sampling hash)
+    unsigned long long sub_th, sub_seed, sub_tree;
+    const float* label;
+    const float* weight;      // may be null
+    const float* pred;
+    const float* host_exp;    // exact logistic: expf(-pred) computed by glibc on the host
+    const float* gpair_in;    // exact reference path: f32 pairs from the host
+    float* gpair_f32;         // scratch f32 pairs
+    Pair* fixed;
+    unsigned long long* sum;  // [2] root sum (mod 2^64)
+    unsigned long long* maxbits; // [2] max |g|, |h| as double bit patterns
+    const double* scales;     // [2]
+    int objective;            // 0 squared error, 1 logistic
+};
+
+// Host-side launchers (train_kernels.cu).
+void launch_mask_max(const GradArgs& a, cudaStream_t s);
+void launch_gradient_max(const GradArgs& a, int fast, cudaStream_t s);
+void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s);
+void launch_quantize(const GradArgs& a, cudaStream_t s);
+void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
+                          cudaStream_t s);
+void set_hist_smem_limit(int bytes);
+void launch_hist(int width, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat, const uint32_t* rows,
+                 const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                 const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                 unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
+void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
+void launch_decide(const LevelArgs& a, cudaStream_t s);
+void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
+void launch_part_scan(const LevelArgs& a, cudaStream_t s);
+void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
+void launch_next_level(const LevelArgs& a, cudaStream_t s);
+void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
+void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
+                      cudaStream_t s);
+void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s);
+void launch_transpose(int width, const uint8_t* src, uint8_t* dst, uint32_t n_rows, uint32_t n_feats,
+                      uint32_t stride, uint64_t row0, cudaStream_t s);
+
+}  // namespace fbg

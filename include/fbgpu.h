@@ -1,0 +1,236 @@
+/*
+ * fbgpu.h — C ABI of the FerrisBoost B200 engine (libfbgpu.so).
+ *
+ * Plain pointers, sizes and status codes; no C++ types cross the boundary and
+ * no exception leaves it.  Every entry point returns an fbgpu_status; the
+ * message of the last failure is available from fbgpu_last_error(ctx) or,
+ * for failures without a context, fbgpu_last_error(NULL) (thread local).
+ *
+ * Entry points are grouped as the reference's CUDA backend boundary
+ * (mdai001/FerrisBoost src/backend/mod.rs, the cfg-swapped stub whose
+ * signatures the Rust training engine calls) plus the explanation models
+ * (src/backend/cuda/explain.rs, src/backend/cuda/inference.rs) and the
+ * engine-level calls the Python package uses.  Each declaration cites the
+ * reference interface it replaces.
+ *
+ * Layout contracts:
+ *   - gradient pairs are interleaved [grad, hess] per row (types.rs:101-107
+ *     GradPair as f32, types.rs:151-175 GradPairFixed as int64);
+ *   - a column block is column-major, data[local_feat * n_rows + row]
+ *     (data/columns.rs:9-25), 1 or 2 bytes per bin, missing = 255 / 65535;
+ *   - histograms are total_bins int64 pairs, features in ascending global
+ *     order, feature f at offsets[f] (data/columns.rs:270-279).
+ */
+#ifndef FBGPU_H
+#define FBGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  INPUT maps to Python ValueError and the others to
+ * RuntimeError, as the reference's InputError split does (src/error.rs:1-70). */
+typedef enum fbgpu_status {
+    FBGPU_OK = 0,
+    FBGPU_EINPUT = 1,
+    FBGPU_ECUDA = 2,
+    FBGPU_ENCCL = 3,
+    FBGPU_ETIMEOUT = 4,
+    FBGPU_EINTERNAL = 5
+} fbgpu_status;
+
+typedef struct fbgpu_ctx fbgpu_ctx;
+typedef struct fbgpu_model fbgpu_model;
+
+/* Context shape.  Replaces GpuTrainCtx::new_with_shape
+ * (src/backend/mod.rs:245-255): every device buffer of a training run is
+ * allocated here, none during training (src/training/mod.rs:1708-1714). */
+typedef struct fbgpu_config {
+    int32_t device;
+    uint32_t n_features;
+    uint64_t n_rows;          /* rows held by this context (its shard) */
+    uint64_t n_rows_global;   /* rows over all ranks (quantizer budget) */
+    uint64_t row_offset;      /* global index of this shard's first row */
+    uint32_t max_depth;       /* 0..=14 (types.rs:424 MAX_DEPTH_LIMIT) */
+    uint32_t max_leaves;      /* 0 = unlimited */
+    uint32_t hist_smem_bytes; /* shared-memory budget of a histogram tile; 0 = default */
+    int32_t gpu_math;         /* 0 exact, 1 fast (types.rs:80-87 GpuMath) */
+} fbgpu_config;
+
+/* Per-tree split parameters (TrainParams, types.rs:433-686). */
+typedef struct fbgpu_tree_params {
+    float eta;
+    float lambda;
+    float gamma;
+    float min_child_weight;
+    float alpha;
+    float max_delta_step;
+    uint32_t max_depth;
+    uint32_t max_leaves;
+    uint32_t max_cat_to_onehot;
+    uint32_t max_cat_threshold;
+    int32_t grow_policy;        /* 0 depthwise, 1 lossguide */
+    const int8_t* monotone;     /* n_features entries or NULL */
+} fbgpu_tree_params;
+
+/* A grown tree (model/tree.rs:52-79 Node, arrays by node id).  The caller
+ * provides arrays of `capacity` entries (2^(max_depth+1) - 1 suffices);
+ * `bin` is the right-boundary bin of a numeric split (split.rs:17-52) and
+ * cats holds 8 words (the right-going category set) per node. */
+typedef struct fbgpu_tree_out {
+    uint32_t capacity;
+    uint32_t n_nodes;
+    int32_t* left;
+    int32_t* right;
+    uint32_t* feat;
+    uint32_t* bin;
+    float* gain;
+    float* leaf;
+    float* hess;
+    uint32_t* flags;            /* bit0 leaf, bit1 default_left, bit2 categorical */
+    uint32_t* cats;             /* 8 words per node, may be NULL */
+} fbgpu_tree_out;
+
+/* Result of one node's split search (split.rs:17-52 SplitCandidate;
+ * backend/cuda/histogram.cu:6-11 SplitPacket). */
+typedef struct fbgpu_split {
+    uint32_t found;
+    uint32_t feat;
+    uint32_t bin;
+    uint32_t missing_left;
+    float gain;
+    uint32_t categorical;
+    int64_t left_grad, left_hess, right_grad, right_hess;
+    uint32_t cats[8];
+} fbgpu_split;
+
+const char* fbgpu_last_error(const fbgpu_ctx* ctx);
+int32_t fbgpu_device_count(void);
+
+/* ---------------------------------------------------------- training context */
+
+/* Replaces GpuTrainCtx::new_with_shape (src/backend/mod.rs:245-255). */
+fbgpu_status fbgpu_ctx_create(const fbgpu_config* cfg, fbgpu_ctx** out);
+void fbgpu_ctx_destroy(fbgpu_ctx* ctx);
+
+/* Feature metadata: bins per feature (cuts + 1), storage width in bytes
+ * (bins.rs:58-66 BinWidth::for_feature) and categorical flags (may be NULL).
+ * Replaces the cuts half of GpuTrainCtx::block_session_bins
+ * (src/backend/mod.rs:352-362). */
+fbgpu_status fbgpu_set_features(fbgpu_ctx* ctx, const uint32_t* n_bins, const uint8_t* width,
+                                const uint8_t* categorical);
+
+/* Upload one column block (reference ColumnBlock BinData, column-major) into
+ * the resident device layout.  Replaces block_session_bins /
+ * block_session_resident_width (src/backend/mod.rs:352-383). */
+fbgpu_status fbgpu_upload_block(fbgpu_ctx* ctx, const uint32_t* feat_ids, uint32_t n_feats, uint32_t width,
+                                const void* data);
+
+/* Labels, optional sample weights (NULL) and starting margins (per-row
+ * base_margin rows, or NULL for the scalar base_margin).  Replaces
+ * GpuTrainCtx::init_fast_math (src/training/mod.rs:1837-1860); in exact mode
+ * the device copy of the margins is kept as well. */
+fbgpu_status fbgpu_set_labels(fbgpu_ctx* ctx, const float* labels, const float* weights,
+                              const float* base_margin_rows, float base_margin);
+
+/* Exact-mode round start from host f32 gradient pairs: row-sampling mask,
+ * bound scan, power-of-two scales (types.rs:366-385), fixed-point conversion
+ * and root sum on the device.  Replaces upload_and_quantize_gpair_sampled
+ * (src/backend/mod.rs:298-306).  sub_threshold = UINT64_MAX keeps all rows. */
+fbgpu_status fbgpu_upload_and_quantize_gpair(fbgpu_ctx* ctx, const float* gpair, uint64_t sub_threshold,
+                                             uint64_t seed, uint64_t tree, double* scales_out,
+                                             int64_t* root_sum_out);
+
+/* Exact-mode round start from host-quantized pairs.  Replaces upload_gpair
+ * (src/backend/mod.rs:286). */
+fbgpu_status fbgpu_upload_gpair(fbgpu_ctx* ctx, const int64_t* fixed, const double* scales,
+                                const int64_t* root_sum);
+
+/* Exact logistic round start: `host_exp` holds glibc expf(-margin) per row
+ * (the only non-IEEE-basic step of the gradient, computed on the host like the
+ * reference's exact mode, objective.rs:37-39); the device recomputes the
+ * gradient from it in the host's f32 operation order and quantizes with the
+ * host's scales.  No counterpart with this exact signature in the reference:
+ * it is the exact-mode boundary of upload_and_quantize_gpair_sampled with
+ * 4 bytes per row instead of 8. */
+fbgpu_status fbgpu_round_from_exp(fbgpu_ctx* ctx, int32_t objective, const float* host_exp,
+                                  uint64_t sub_threshold, uint64_t seed, uint64_t tree, const double* scales);
+
+/* Round start with the gradient computed on the device from the resident
+ * margins.  fast = 1 is gpu_math="fast" (CUDA expf; replaces
+ * fast_gradient_and_quantize, src/backend/mod.rs:220-228); fast = 0 is exact
+ * squared error (pure f32 arithmetic) with the scales taken by the host.
+ * scales_out / root_sum_out may be NULL (no host synchronisation then). */
+fbgpu_status fbgpu_round_device(fbgpu_ctx* ctx, int32_t objective, int32_t fast, uint64_t sub_threshold,
+                                uint64_t seed, uint64_t tree, double* scales_out, int64_t* root_sum_out);
+
+/* Grow one tree on the device and add its leaf values to the resident
+ * margins.  `enabled` marks the features of this tree (colsample_bytree,
+ * colsample.rs:74-95), NULL = all.  Replaces the per-level loop of
+ * build_tree over GpuBlockSession / GpuPartitionSession
+ * (src/training/mod.rs:3569-4564): histogram_device_batch, split_cached_batch,
+ * partition_resident_batch, resolve_partitions, assign_leaf_values. */
+fbgpu_status fbgpu_build_tree(fbgpu_ctx* ctx, const fbgpu_tree_params* tp, const uint8_t* enabled,
+                              fbgpu_tree_out* out);
+
+/* Copy the resident margins to the host.  Replaces download_prediction_delta
+ * / with_prediction_delta (src/backend/mod.rs:331-340): the device adds each
+ * tree's leaf values itself, so the host receives margins instead of deltas. */
+fbgpu_status fbgpu_download_margins(fbgpu_ctx* ctx, float* out);
+
+/* ---------------------------------------------------------- component calls */
+
+/* Histogram of `rows` (host array, ascending or not; NULL = every row) over
+ * all features, with the context's current fixed-point gradients or `fixed`
+ * (host, 2 x n_rows int64) when given.  out: total_bins x 2 int64.  The C
+ * form of hist::build (src/training/hist.rs:35-62) and of
+ * GpuBlockSession::histogram_device_batch (src/backend/mod.rs:433-439). */
+fbgpu_status fbgpu_histogram(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n_sel, const int64_t* fixed,
+                             int64_t* out);
+
+/* Best split of one node from a host histogram.  The C form of
+ * split::best_split_in_block_typed (src/training/split.rs:331-461) as the
+ * device split kernels compute it. */
+fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t* node_sum, const double* scales,
+                              const fbgpu_tree_params* tp, float lower, float upper, const uint8_t* enabled,
+                              fbgpu_split* out);
+
+/* Stable partition of `rows` by one split: left rows first, then right.
+ * Replaces GpuPartitionSession::partition / partition_categorical
+ * (src/backend/mod.rs:468-483). cats: 8 words or NULL. */
+fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
+                             int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left);
+
+/* ---------------------------------------------------------- explanation models */
+
+/* A model for device prediction and SHAP.  Node arrays of all trees back to
+ * back; tree t owns nodes [tree_off[t], tree_off[t+1]) with tree-local child
+ * indices; value = leaf value (leaf) or split condition (numeric split);
+ * flags: bit0 leaf, bit1 default_left, bit2 categorical; categorical node i
+ * tests cat_words[cat_off[i] .. cat_off[i] + cat_len[i]).  Replaces
+ * GpuExplainModel::new and GpuInferenceModel construction
+ * (src/backend/cuda/explain.rs:355, src/backend/cuda/inference.rs:67). */
+fbgpu_status fbgpu_model_create(int32_t device, uint32_t n_features, uint32_t n_trees, const uint32_t* tree_off,
+                                const int32_t* left, const int32_t* right, const uint32_t* feat, const float* value,
+                                const uint8_t* flags, const float* hess, const uint32_t* cat_off,
+                                const uint32_t* cat_len, const uint32_t* cat_words, uint64_t n_cat_words,
+                                float base_margin, fbgpu_model** out);
+void fbgpu_model_destroy(fbgpu_model* m);
+
+/* Raw margins of host rows (row-major n x n_features).  Replaces
+ * GpuInferenceModel::predict_margins (src/backend/cuda/inference.rs:300-339). */
+fbgpu_status fbgpu_predict(fbgpu_model* m, const float* X, uint64_t n, float* out);
+/* The same on device buffers, enqueued on `stream` (a cudaStream_t). */
+fbgpu_status fbgpu_predict_device(fbgpu_model* m, const float* X, uint64_t n, float* out, void* stream);
+
+/* QuadratureTreeSHAP contributions, n x (n_features + 1), bias last.
+ * Replaces GpuExplainModel::compute (src/backend/cuda/explain.rs:491). */
+fbgpu_status fbgpu_shap(fbgpu_model* m, const float* X, uint64_t n, float* out);
+fbgpu_status fbgpu_shap_device(fbgpu_model* m, const float* X, uint64_t n, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <charconv>
 #include <cmath>
 #include <cstdint>
@@ -35,6 +36,8 @@
 namespace {
 
 thread_local std::string g_err;
+thread_local double g_setup_s = 0.0;
+thread_local std::vector<double> g_round_s;
 
 constexpr float kMinGainEps = 1e-6f;  // split.rs:15 MIN_GAIN_EPS
 constexpr float kRtEps = 1e-6f;       // objective.rs:18 K_RT_EPS
@@ -945,6 +948,8 @@ Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const 
         if (any) P.cat.assign(rp->categorical, rp->categorical + F);
     }
     const rc_params& p = P.p;
+    auto t_setup = std::chrono::steady_clock::now();
+    g_round_s.clear();
     if (n == 0 || F == 0) { g_err = "training data must have at least one row and one feature"; return nullptr; }
     if (p.max_depth > 14) { g_err = "max_depth must be in 0..=14"; return nullptr; }
     int nth = n_threads(p.nthread);
@@ -978,7 +983,9 @@ Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const 
     std::vector<GP> gp(n);
     std::vector<FX> fixed(n);
     uint64_t sub_th = threshold_for(p.subsample);
+    g_setup_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_setup).count();
     for (uint32_t round = 0; round < p.n_rounds; round++) {
+        auto t_round = std::chrono::steady_clock::now();
         // gradient (mod.rs:5624-5634) + row sampling mask + bounds (mod.rs:4811-4842)
         double mg = 0.0, mh = 0.0;
 #pragma omp parallel for reduction(max : mg, mh) num_threads(nth)
@@ -1010,6 +1017,7 @@ Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const 
         Tree t = p.grow_policy == 1 ? build_tree_lossguide(C, fixed, root_sum, q, preds, en)
                                     : build_tree_depthwise(C, fixed, root_sum, q, preds, en);
         m->trees.push_back(std::move(t));
+        g_round_s.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t_round).count());
     }
     return m;
 }
@@ -1316,6 +1324,13 @@ void rc_default_params(rc_params* p) {  // types.rs:641-686 Default for TrainPar
 }
 
 const char* rc_last_error(void) { return g_err.c_str(); }
+
+int32_t rc_last_timing(double* setup_s, double* round_s, int32_t cap) {
+    if (setup_s) *setup_s = g_setup_s;
+    const int32_t n = (int32_t)g_round_s.size();
+    for (int32_t i = 0; i < n && i < cap; i++) round_s[i] = g_round_s[i];
+    return n;
+}
 
 void* rc_train(const float* X, uint64_t n, uint32_t F, const float* y, const float* w, const rc_params* p) {
     try {

@@ -53,6 +53,9 @@ void rc_default_params(rc_params* p);
 void* rc_train(const float* X, uint64_t n, uint32_t F, const float* y,
                const float* w, const rc_params* p);
 const char* rc_last_error(void);
+/* Wall seconds of the last rc_train on this thread: setup (sketch, bins) and
+ * each round.  Returns the number of rounds. */
+int32_t rc_last_timing(double* setup_s, double* round_s, int32_t cap);
 void rc_model_free(void* model);
 uint32_t rc_model_num_trees(void* model);
 /* XGBoost-compatible JSON; returns the length (writes at most cap bytes). */

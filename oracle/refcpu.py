@@ -56,6 +56,8 @@ class RefCPU:
         lib.rc_train.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.c_uint32, C.POINTER(C.c_float),
                                  C.POINTER(C.c_float), C.POINTER(rc_params)]
         lib.rc_last_error.restype = C.c_char_p
+        lib.rc_last_timing.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_int32]
+        lib.rc_last_timing.restype = C.c_int32
         lib.rc_model_free.argtypes = [_P]
         lib.rc_model_num_trees.argtypes = [_P]
         lib.rc_model_num_trees.restype = C.c_uint32
@@ -126,6 +128,12 @@ class RefCPU:
         if not h:
             raise RuntimeError(self.lib.rc_last_error().decode())
         return RefModel(self, h, X.shape[1])
+
+    def last_timing(self):
+        setup = C.c_double()
+        rounds = (C.c_double * 100000)()
+        k = self.lib.rc_last_timing(C.byref(setup), rounds, 100000)
+        return setup.value, list(rounds[:k])
 
     # ---------------------------------------------------------------- components
     def sketch(self, X, max_bin, w=None, categorical=None, nthread=0):

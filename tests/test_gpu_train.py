@@ -1,0 +1,136 @@
+"""End-to-end training on the device against the oracle and the reference's
+XGBoost 3.4.1 golden margins.  Exact mode must be byte-identical: same JSON
+bytes as the oracle, margins bit for bit."""
+import json
+
+import numpy as np
+import pytest
+
+import ferrisboost_b200 as fb
+from conftest import golden_cases
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = golden_cases("index.json") + golden_cases("weighted_index.json") + golden_cases("monotone_index.json")
+
+
+def _fb_params(params):
+    p = dict(params)
+    p.pop("num_boost_round", None)
+    return p
+
+
+@pytest.mark.parametrize("case", GOLDEN, ids=[c[0] for c in GOLDEN])
+def test_golden_margins_bit_exact(oracle, case):
+    name, X, y, w, want, params = case
+    m = fb.train(_fb_params(params), X, label=y, num_boost_round=params["num_boost_round"], weight=w)
+    got = m.predict(X, output_margin=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), name
+    ref = oracle.train(X, y, w, **params)
+    assert m.to_json() == ref.json(), name
+
+
+def _synthetic(n, F, seed, missing=0.0):
+    # configs[0] generator shape: N(0,1) features, logistic labels
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, F), dtype=np.float32)
+    w = rng.standard_normal(F)
+    z = X @ w + 0.5 * X[:, 0] * X[:, 1] - 0.3 * X[:, 2] ** 2
+    y = (rng.random(n) < 1.0 / (1.0 + np.exp(-z))).astype(np.float32)
+    if missing:
+        X[rng.random(X.shape) < missing] = np.nan
+    return X, y
+
+
+CONFIGS = [
+    dict(objective="binary:logistic", max_depth=6, eta=0.1, max_bin=256),
+    dict(objective="reg:squarederror", max_depth=8, eta=0.3, max_bin=256),
+    dict(objective="binary:logistic", max_depth=5, eta=0.3, max_bin=64, subsample=0.7, colsample_bytree=0.5,
+         seed=3),
+    dict(objective="binary:logistic", max_depth=7, eta=0.2, max_bin=1024, max_leaves=40, min_child_weight=5.0,
+         gamma=0.2, reg_lambda=2.0),
+    dict(objective="reg:squarederror", max_depth=4, eta=0.5, max_bin=255, alpha=0.5, max_delta_step=0.3),
+]
+
+
+@pytest.mark.parametrize("k", range(len(CONFIGS)))
+def test_synthetic_models_byte_identical(oracle, k):
+    p = CONFIGS[k]
+    X, y = _synthetic(30000, 28, seed=k, missing=0.03 if k % 2 else 0.0)
+    if p["objective"] == "reg:squarederror":
+        y = (X[:, 0] * 2 + np.nan_to_num(X[:, 3]) ** 2).astype(np.float32)
+    w = np.random.default_rng(k).uniform(0.2, 2.0, len(y)).astype(np.float32) if k == 3 else None
+    m = fb.train(p, X, label=y, num_boost_round=12, weight=w)
+    ref = oracle.train(X, y, w, n_rounds=12, **p)
+    a, b = m.to_json(), ref.json()
+    assert a == b
+    got = m.predict(X, output_margin=True)
+    assert np.array_equal(got.view(np.uint32), ref.predict_margin(X).view(np.uint32))
+
+
+def test_root_only_and_depth_one(oracle):
+    X, y = _synthetic(5000, 5, seed=9)
+    for depth in (0, 1):
+        p = dict(objective="binary:logistic", max_depth=depth)
+        m = fb.train(p, X, label=y, num_boost_round=3)
+        assert m.to_json() == oracle.train(X, y, n_rounds=3, **p).json()
+
+
+def test_categorical_depthwise_byte_identical(oracle):
+    rng = np.random.default_rng(4)
+    n = 20000
+    Xn = rng.standard_normal((n, 6)).astype(np.float32)
+    Xn[rng.random(Xn.shape) < 0.05] = np.nan
+    Xc = rng.integers(0, 64, (n, 3)).astype(np.float32)
+    Xc[:, 2] = rng.integers(0, 3, n)  # few categories: one-hot
+    X = np.concatenate([Xn, Xc], axis=1)
+    eff = rng.standard_normal(64)
+    y = (eff[Xc[:, 0].astype(int)] + np.nan_to_num(Xn[:, 0]) + rng.normal(0, 0.5, n)).astype(np.float32)
+    ft = ["q"] * 6 + ["c"] * 3
+    cat = np.array([0] * 6 + [1] * 3, np.uint8)
+    p = dict(objective="reg:squarederror", max_depth=6, eta=0.3, max_bin=256)
+    m = fb.train(p, X, label=y, num_boost_round=8, feature_types=ft)
+    ref = oracle.train(X, y, n_rounds=8, categorical=cat, **p)
+    assert m.to_json() == ref.json()
+    assert np.array_equal(m.predict(X, output_margin=True).view(np.uint32), ref.predict_margin(X).view(np.uint32))
+
+
+def test_fast_mode_within_tolerance(oracle):
+    X, y = _synthetic(40000, 28, seed=21)
+    p = dict(objective="binary:logistic", max_depth=6, eta=0.1, max_bin=256)
+    fast = fb.train(dict(p, gpu_math="fast"), X, label=y, num_boost_round=20)
+    exact = oracle.train(X, y, n_rounds=20, **p)
+    a = fast.predict(X, output_margin=True).astype(np.float64)
+    b = exact.predict_margin(X).astype(np.float64)
+
+    def logloss(m):
+        pr = np.clip(1 / (1 + np.exp(-m)), 1e-15, 1 - 1e-15)
+        return -np.mean(y * np.log(pr) + (1 - y) * np.log(1 - pr))
+
+    assert abs(logloss(a) - logloss(b)) < 1e-4
+    pa, pb = 1 / (1 + np.exp(-a)), 1 / (1 + np.exp(-b))
+    assert np.median(np.abs(pa - pb) / np.abs(pb)) < 1e-5
+
+
+def test_predict_and_shap_match_oracle(oracle):
+    X, y = _synthetic(20000, 28, seed=5, missing=0.02)
+    p = dict(objective="binary:logistic", max_depth=8, eta=0.1, max_bin=256)
+    m = fb.train(p, X, label=y, num_boost_round=15)
+    ref = oracle.train(X, y, n_rounds=15, **p)
+    Xt, _ = _synthetic(3000, 28, seed=77, missing=0.02)
+    assert np.array_equal(m.predict(Xt, output_margin=True).view(np.uint32),
+                          ref.predict_margin(Xt).view(np.uint32))
+    phi = m.predict(Xt, pred_contribs=True)
+    want = ref.shap(Xt)
+    assert np.max(np.abs(phi - want)) <= 1e-5
+    np.testing.assert_allclose(phi.sum(axis=1), ref.predict_margin(Xt), atol=2e-4)
+
+
+def test_json_is_valid_xgboost_schema():
+    X, y = _synthetic(3000, 4, seed=1)
+    m = fb.train({"max_depth": 3}, X, label=y, num_boost_round=2)
+    doc = json.loads(m.to_json())
+    t = doc["learner"]["gradient_booster"]["model"]["trees"][0]
+    n = int(t["tree_param"]["num_nodes"])
+    assert len(t["left_children"]) == n == len(t["split_conditions"])
+    assert doc["learner"]["objective"]["name"] == "binary:logistic"
