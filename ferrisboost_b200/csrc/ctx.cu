@@ -433,10 +433,12 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         a.rows_next = rows_[1 - cur].as<uint32_t>();
         FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, 16ull * a.slot_pairs * max_acc, s_));
         if (stats_ && d < 15) {
-            // this level's accumulate rows and nodes (TreeState.acc_count, .acc_total)
+            // this level's accumulate nodes and rows: TreeState bytes [8, 24) hold
+            // leaf_count, acc_count (u32 each) and acc_total (u64)
+            static_assert(offsetof(TreeState, acc_count) == 12 && offsetof(TreeState, acc_total) == 16,
+                          "TreeState layout");
             FB_CUDA_CHECK(cudaMemcpyAsync(level_stats_.as<uint8_t>() + 16 * d,
-                                          reinterpret_cast<uint8_t*>(state_.p) + offsetof(TreeState, acc_count), 16,
-                                          cudaMemcpyDeviceToDevice, s_));
+                                          reinterpret_cast<uint8_t*>(state_.p) + 8, 16, cudaMemcpyDeviceToDevice, s_));
             FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d], s_));
         }
         launch_hist(1, d_tiles_.as<TileDesc>(), n_tiles_w1_, d_tfeat_.as<TileFeat>(), a.rows_cur, fixed_.as<Pair>(),
@@ -478,7 +480,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         for (uint32_t d = 0; d < std::min<uint32_t>(maxd, 15); d++) {
             float ms = 0.0f;
             FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
-            const uint64_t acc_nodes = lvl[2 * d] & 0xffffffffull, rows = lvl[2 * d + 1];
+            const uint64_t acc_nodes = lvl[2 * d] >> 32, rows = lvl[2 * d + 1];
             hist_ms_ += ms;
             hist_launches_ += (n_tiles_w1_ ? 1 : 0) + (n_tiles_w2_ ? 1 : 0);
             hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
@@ -588,9 +590,9 @@ void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const do
     out->found = r.flags & 1u;
     if (!out->found) return;
     out->feat = r.feat;
-    out->bin = r.bin;
     out->missing_left = (r.flags >> 1) & 1u;
     out->categorical = (r.flags >> 2) & 1u;
+    out->bin = out->categorical ? 0u : r.bin;  // split.rs:41-51: a categorical split carries its set, bin 0
     out->gain = r.gain;
     out->left_grad = r.left.g; out->left_hess = r.left.h;
     out->right_grad = r.right.g; out->right_hess = r.right.h;

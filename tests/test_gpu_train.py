@@ -58,7 +58,7 @@ def test_synthetic_models_byte_identical(oracle, k):
     p = CONFIGS[k]
     X, y = _synthetic(30000, 28, seed=k, missing=0.03 if k % 2 else 0.0)
     if p["objective"] == "reg:squarederror":
-        y = (X[:, 0] * 2 + np.nan_to_num(X[:, 3]) ** 2).astype(np.float32)
+        y = (np.nan_to_num(X[:, 0]) * 2 + np.nan_to_num(X[:, 3]) ** 2).astype(np.float32)
     w = np.random.default_rng(k).uniform(0.2, 2.0, len(y)).astype(np.float32) if k == 3 else None
     m = fb.train(p, X, label=y, num_boost_round=12, weight=w)
     ref = oracle.train(X, y, w, n_rounds=12, **p)
