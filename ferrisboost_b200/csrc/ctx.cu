@@ -14,6 +14,8 @@ thread_local std::string g_last_error;
 uint32_t ceil_div(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
 }  // namespace
 
+void noalloc_set_error(const char* msg) { g_last_error = msg; }
+
 double pow2_scale_host(double max_abs, uint64_t n_rows) {
     if (!(max_abs > 0.0) || !std::isfinite(max_abs)) return 1.0;
     double budget = (double)(1ull << 62) / (double)(n_rows > 0 ? n_rows : 1);

@@ -192,6 +192,9 @@ class ExplainModel {
     float rule_nodes_[kShapPoints], rule_weights_[kShapPoints];
 };
 
+// Sets the message fbgpu_last_error(NULL) returns on this thread.
+void noalloc_set_error(const char* msg);
+
 // explain.rs:141-169 endpoint-squared Gauss-Legendre rule (f64, stored as f32).
 void make_shap_rule(float* nodes, float* weights);
 

@@ -203,6 +203,26 @@ fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t
 fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
                              int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left);
 
+/* Stable partition of device row ids by one numeric or categorical split,
+ * allocating no device memory.  No counterpart in the reference: it exists for
+ * callers that own every device allocation themselves and cannot call
+ * cudaMalloc (the reference's Rust host keeps all allocation on its side,
+ * src/backend/mod.rs:7-10).  All pointers are device pointers except `cats`
+ * (8 host words, the right-going categories, or NULL for a numeric split
+ * `bin < split bin goes left`).  `bins` is a row-major record matrix: the
+ * feature's bin of row r is the `width`-byte value at bins + r*stride +
+ * byte_off (missing = 255 / 65535).  Writes the left rows then the right rows
+ * of `rows` to `out_rows` in input order, and the left count to *n_left.
+ * Work is enqueued on `stream` (a cudaStream_t, NULL = default stream).
+ * The kernels' scratch is one fixed 512 KiB static device array per device,
+ * so at most 268435456 rows per call (larger requests fail with
+ * FBGPU_EINPUT).  The first call on a device looks the array up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every call shares the array: calls that overlap on the GPU race. */
+fbgpu_status fbgpu_partition_noalloc(const void* bins, uint32_t stride, uint32_t width, uint32_t byte_off,
+                                     const uint32_t* rows, uint64_t n, uint32_t bin, int32_t missing_left,
+                                     const uint32_t* cats, uint32_t* out_rows, uint32_t* n_left, void* stream);
+
 /* ---------------------------------------------------------- explanation models */
 
 /* A model for device prediction and SHAP.  Node arrays of all trees back to
