@@ -307,44 +307,69 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
     buf_leaves_ = max_leaves;
 }
 
-// Histogram tiles: the enabled features of every block, greedily grouped so
-// that a tile's four 32-bit planes fit the shared-memory budget.
+// Histogram tiles: the enabled features of every block, grouped per kernel.
+// Lane-per-feature tiles take up to 32 features whose [bin][32] planes fit in
+// shared memory (features of at most kLpfMaxBins bins); the remaining features
+// go to row-per-thread tiles sized by the shared-memory budget.
 void TrainCtx::plan_tiles(const uint8_t* enabled) {
     std::vector<uint8_t> en(F_, 1);
     if (enabled) for (uint32_t f = 0; f < F_; f++) en[f] = enabled[f] ? 1 : 0;
     if (tiles_valid_ && en == last_enabled_) return;
-    std::vector<TileDesc> tiles[2];
+    const uint32_t kLpfMaxBins = 440;  // 440 x 32 lanes x 16 B = 220 KiB
+    static const bool force_tpr = [] {
+        const char* e = std::getenv("FBGPU_HIST");
+        return e && std::string(e) == "tpr";
+    }();
+    std::vector<TileDesc> gen[2], lpf[2];
     std::vector<TileFeat> tf;
-    size_t smem = 0;
+    size_t smem_gen = 16, smem_lpf = 16;
     const uint32_t max_local = (uint32_t)((smem_budget_ - 64 * sizeof(TileFeat)) / 16);
-    for (int wpass = 1; wpass <= 2; wpass++) {
-        for (const auto& bp : blocks_) {
-            const Block& b = *bp;
-            if ((int)b.width != wpass) continue;
-            TileDesc cur{b.data.as<uint8_t>(), b.stride, b.width, (uint32_t)tf.size(), 0, 0, b.width == 2 ? 65535u : 255u};
-            auto flush = [&]() {
-                if (cur.n_feat == 0) return;
-                tiles[wpass - 1].push_back(cur);
-                smem = std::max(smem, (size_t)cur.local_bins * 16 + (size_t)cur.n_feat * sizeof(TileFeat));
-                cur.feat_begin = (uint32_t)tf.size();
-                cur.n_feat = 0;
-                cur.local_bins = 0;
-            };
-            for (uint32_t i = 0; i < b.feats.size(); i++) {
-                uint32_t f = b.feats[i];
-                if (!en[f]) continue;
-                if (cur.n_feat == 64 || cur.local_bins + nbins_[f] > max_local) flush();
-                tf.push_back(TileFeat{feat_byte_[f], cur.local_bins, nbins_[f], hoff_[f]});
-                cur.local_bins += nbins_[f];
-                cur.n_feat++;
-            }
-            flush();
+    for (const auto& bp : blocks_) {
+        const Block& b = *bp;
+        const int wi = (int)b.width - 1;
+        const uint32_t miss = b.width == 2 ? 65535u : 255u;
+        // lane-per-feature tiles
+        TileDesc cur{b.data.as<uint8_t>(), b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
+        uint32_t maxb = 0;
+        auto flush_lpf = [&]() {
+            if (cur.n_feat == 0) return;
+            cur.local_bins = maxb * 32;
+            lpf[wi].push_back(cur);
+            smem_lpf = std::max(smem_lpf, (size_t)cur.local_bins * 16);
+            cur.feat_begin = (uint32_t)tf.size();
+            cur.n_feat = 0;
+            maxb = 0;
+        };
+        for (uint32_t f : b.feats) {
+            if (!en[f] || force_tpr || nbins_[f] > kLpfMaxBins) continue;
+            if (cur.n_feat == 32) flush_lpf();
+            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
+            maxb = std::max(maxb, nbins_[f]);
+            cur.n_feat++;
         }
+        flush_lpf();
+        // row-per-thread tiles for the rest
+        TileDesc g{b.data.as<uint8_t>(), b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
+        auto flush_gen = [&]() {
+            if (g.n_feat == 0) return;
+            gen[wi].push_back(g);
+            smem_gen = std::max(smem_gen, (size_t)g.local_bins * 16 + (size_t)g.n_feat * sizeof(TileFeat));
+            g.feat_begin = (uint32_t)tf.size();
+            g.n_feat = 0;
+            g.local_bins = 0;
+        };
+        for (uint32_t f : b.feats) {
+            if (!en[f] || !(force_tpr || nbins_[f] > kLpfMaxBins)) continue;
+            if (g.n_feat == 64 || g.local_bins + nbins_[f] > max_local) flush_gen();
+            tf.push_back(TileFeat{feat_byte_[f], g.local_bins, nbins_[f], hoff_[f]});
+            g.local_bins += nbins_[f];
+            g.n_feat++;
+        }
+        flush_gen();
     }
-    n_tiles_w1_ = (uint32_t)tiles[0].size();
-    n_tiles_w2_ = (uint32_t)tiles[1].size();
-    std::vector<TileDesc> all = tiles[0];
-    all.insert(all.end(), tiles[1].begin(), tiles[1].end());
+    std::vector<TileDesc> all;
+    for (int w = 0; w < 2; w++) { tile_off_gen_[w] = (uint32_t)all.size(); n_gen_[w] = (uint32_t)gen[w].size(); all.insert(all.end(), gen[w].begin(), gen[w].end()); }
+    for (int w = 0; w < 2; w++) { tile_off_lpf_[w] = (uint32_t)all.size(); n_lpf_[w] = (uint32_t)lpf[w].size(); all.insert(all.end(), lpf[w].begin(), lpf[w].end()); }
     d_tiles_.alloc(sizeof(TileDesc) * std::max<size_t>(all.size(), 1));
     d_tfeat_.alloc(sizeof(TileFeat) * std::max<size_t>(tf.size(), 1));
     if (!all.empty())
@@ -352,11 +377,30 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     if (!tf.empty())
         FB_CUDA_CHECK(cudaMemcpyAsync(d_tfeat_.p, tf.data(), sizeof(TileFeat) * tf.size(), cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(d_enabled_.p, en.data(), F_, cudaMemcpyHostToDevice, s_));
-    tile_smem_ = std::max<size_t>(smem, 16);
+    tile_smem_ = smem_gen;
+    tile_smem_lpf_ = smem_lpf;
     set_hist_smem_limit((int)tile_smem_);
+    set_hist_lpf_smem_limit((int)tile_smem_lpf_);
     FB_CUDA_CHECK(cudaStreamSynchronize(s_));
     last_enabled_ = en;
     tiles_valid_ = true;
+}
+
+// One histogram pass over the accumulate rows of the current level (all tiles).
+void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, const uint32_t* acc_list,
+                                 const unsigned long long* acc_prefix, uint64_t rows_upper) {
+    const TileDesc* T = d_tiles_.as<TileDesc>();
+    const TileFeat* TF = d_tfeat_.as<TileFeat>();
+    const unsigned long long slot = std::max<uint64_t>(total_bins_, 1);
+    const uint32_t grid_gen = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 8192), 148 * 2));
+    const int per_sm = tile_smem_lpf_ + 1024 <= 113 * 1024 ? 2 : 1;
+    const uint32_t grid_lpf = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 4096), 148u * per_sm));
+    for (int w = 0; w < 2; w++) {
+        launch_hist(w + 1, T + tile_off_gen_[w], n_gen_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list, acc_prefix,
+                    state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_gen, tile_smem_, s_);
+        launch_hist_lpf(w + 1, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
+                        acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf, tile_smem_lpf_, s_);
+    }
 }
 
 LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
@@ -406,7 +450,6 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     }
     LevelArgs a = level_args(tp);
     const uint32_t maxd = tp.max_depth;
-    const uint32_t hist_grid = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(n_, 8192), 148 * 2));
     FB_CUDA_CHECK(cudaEventRecord(ev0_, s_));
     int cur = 0;
     launch_iota(rows_[0].as<uint32_t>(), (uint32_t)n_, s_);
@@ -443,11 +486,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
                                           reinterpret_cast<uint8_t*>(state_.p) + 8, 16, cudaMemcpyDeviceToDevice, s_));
             FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d], s_));
         }
-        launch_hist(1, d_tiles_.as<TileDesc>(), n_tiles_w1_, d_tfeat_.as<TileFeat>(), a.rows_cur, fixed_.as<Pair>(),
-                    a.nodes, a.acc_list, a.acc_prefix, a.st, a.hist_acc, a.slot_pairs, hist_grid, tile_smem_, s_);
-        launch_hist(2, d_tiles_.as<TileDesc>() + n_tiles_w1_, n_tiles_w2_, d_tfeat_.as<TileFeat>(), a.rows_cur,
-                    fixed_.as<Pair>(), a.nodes, a.acc_list, a.acc_prefix, a.st, a.hist_acc, a.slot_pairs, hist_grid,
-                    tile_smem_, s_);
+        launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
         launch_split(a, max_m, s_);
         launch_decide(a, s_);
@@ -484,7 +523,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
             const uint64_t acc_nodes = lvl[2 * d] >> 32, rows = lvl[2 * d + 1];
             hist_ms_ += ms;
-            hist_launches_ += (n_tiles_w1_ ? 1 : 0) + (n_tiles_w2_ ? 1 : 0);
+            hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0);
             hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
         }
     }
@@ -542,15 +581,8 @@ void TrainCtx::histogram(const uint32_t* rows, uint64_t n_sel, const int64_t* fi
     FB_CUDA_CHECK(cudaMemcpyAsync(state_.p, &st, sizeof st, cudaMemcpyHostToDevice, s_));
     const unsigned long long slot = std::max<uint64_t>(total_bins_, 1);
     FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, 16 * slot, s_));
-    const uint32_t grid = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(n_sel, 8192), 148 * 2));
-    launch_hist(1, d_tiles_.as<TileDesc>(), n_tiles_w1_, d_tfeat_.as<TileFeat>(), drows.as<uint32_t>(),
-                fixed_.as<Pair>(), nodes_[0].as<NodeInfo>(), acc_list_[0].as<uint32_t>(),
-                acc_prefix_[0].as<unsigned long long>(), state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid,
-                tile_smem_, s_);
-    launch_hist(2, d_tiles_.as<TileDesc>() + n_tiles_w1_, n_tiles_w2_, d_tfeat_.as<TileFeat>(), drows.as<uint32_t>(),
-                fixed_.as<Pair>(), nodes_[0].as<NodeInfo>(), acc_list_[0].as<uint32_t>(),
-                acc_prefix_[0].as<unsigned long long>(), state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid,
-                tile_smem_, s_);
+    launch_histograms(drows.as<uint32_t>(), nodes_[0].as<NodeInfo>(), acc_list_[0].as<uint32_t>(),
+                      acc_prefix_[0].as<unsigned long long>(), n_sel);
     FB_CUDA_CHECK(cudaGetLastError());
     FB_CUDA_CHECK(cudaMemcpyAsync(out, hist_acc_.p, 16 * total_bins_, cudaMemcpyDeviceToHost, s_));
     FB_CUDA_CHECK(cudaStreamSynchronize(s_));

@@ -121,6 +121,8 @@ class TrainCtx {
     };
     void ensure_features() const;
     void plan_tiles(const uint8_t* enabled);
+    void launch_histograms(const uint32_t* rows, const NodeInfo* nodes, const uint32_t* acc_list,
+                           const unsigned long long* acc_prefix, uint64_t rows_upper);
     void ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves);
     LevelArgs level_args(const fbgpu_tree_params& tp) const;
     GradArgs grad_args() const;
@@ -144,8 +146,8 @@ class TrainCtx {
     std::vector<int8_t> last_mono_;
     bool tiles_valid_ = false;
     DevMem d_tiles_, d_tfeat_;
-    uint32_t n_tiles_w1_ = 0, n_tiles_w2_ = 0;
-    size_t tile_smem_ = 0;
+    uint32_t tile_off_gen_[2] = {0, 0}, n_gen_[2] = {0, 0}, tile_off_lpf_[2] = {0, 0}, n_lpf_[2] = {0, 0};
+    size_t tile_smem_ = 0, tile_smem_lpf_ = 0;
     int smem_budget_ = 0;
 
     // rows / gradients

@@ -372,6 +372,98 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
     }
 }
 
+// Lane-per-feature histogram.  A warp takes kLpfRows consecutive arena rows at
+// a time; lane t owns tile feature t (at most 32 per tile), so one row's bins
+// arrive with a single coalesced record load.  The shared histogram is laid
+// out [bin][32 lanes] per plane, so the 32 lanes of an atomic instruction
+// always fall in 32 distinct banks: no bank conflicts whatever the bins.
+constexpr int kLpfRows = 8;
+
+template <int W>
+__global__ void __launch_bounds__(kHistLpfThreads) k_hist_lpf(const TileDesc* __restrict__ tiles,
+                                                               const TileFeat* __restrict__ tfeat,
+                                                               const uint32_t* __restrict__ rows,
+                                                               const Pair* __restrict__ gpair,
+                                                               const NodeInfo* __restrict__ nodes,
+                                                               const uint32_t* __restrict__ acc_list,
+                                                               const unsigned long long* __restrict__ acc_prefix,
+                                                               const TreeState* __restrict__ st,
+                                                               Pair* __restrict__ hist_acc,
+                                                               unsigned long long slot_pairs) {
+    extern __shared__ uint32_t sm[];
+    const TileDesc td = tiles[blockIdx.y];
+    const uint32_t LB = td.local_bins;  // max bins of the tile x 32
+    uint32_t* glo = sm;
+    uint32_t* ghi = sm + LB;
+    uint32_t* hlo = sm + 2 * LB;
+    uint32_t* hhi = sm + 3 * LB;
+    const unsigned long long R = st->acc_total;
+    const uint32_t n_acc = st->acc_count;
+    if (R == 0) return;
+    unsigned long long a = R * blockIdx.x / gridDim.x;
+    const unsigned long long b = R * (blockIdx.x + 1) / gridDim.x;
+    if (a >= b) return;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t nf = td.n_feat;
+    TileFeat f{0, 0, 0, 0};
+    if (lane < nf) f = tfeat[td.feat_begin + lane];
+    const bool active = lane < nf;
+    for (uint32_t j = threadIdx.x; j < 4 * LB; j += blockDim.x) sm[j] = 0u;
+    __syncthreads();
+    uint32_t k = find_segment(acc_prefix, n_acc, a);
+    while (a < b) {
+        const uint32_t node = acc_list[k];
+        const NodeInfo ni = nodes[node];
+        const unsigned long long seg_end = min(b, acc_prefix[k + 1]);
+        const uint32_t* seg_rows = rows + ni.start + (uint32_t)(a - acc_prefix[k]);
+        const uint32_t cnt = (uint32_t)(seg_end - a);
+        for (uint32_t base = warp * kLpfRows; base < cnt; base += nwarps * kLpfRows) {
+            const uint32_t kk = min((uint32_t)kLpfRows, cnt - base);
+            const uint32_t rid = lane < kk ? seg_rows[base + lane] : 0u;
+            uint32_t bin[kLpfRows];
+            Pair gp[kLpfRows];
+#pragma unroll
+            for (int q = 0; q < kLpfRows; q++) {
+                const uint32_t r = __shfl_sync(0xffffffffu, rid, q);
+                bin[q] = td.missing;
+                gp[q] = Pair{0, 0};
+                if ((uint32_t)q < kk) {
+                    gp[q] = gpair[r];
+                    if (active) {
+                        const uint8_t* p = td.base + (size_t)r * td.stride + f.byte_off;
+                        bin[q] = W == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kLpfRows; q++) {
+                if (bin[q] != td.missing && bin[q] < f.nbins) {
+                    const uint32_t idx = bin[q] * 32u + lane;
+                    plane_add(glo, ghi, idx, gp[q].g);
+                    plane_add(hlo, hhi, idx, gp[q].h);
+                }
+            }
+        }
+        __syncthreads();
+        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
+        for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
+            const unsigned long long g = ((unsigned long long)ghi[j] << 32) | glo[j];
+            const unsigned long long h = ((unsigned long long)hhi[j] << 32) | hlo[j];
+            if (g | h) {
+                const uint32_t t = j & 31u, bb = j >> 5;
+                const TileFeat ft = tfeat[td.feat_begin + t];
+                const uint32_t gidx = ft.global_off + bb;
+                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
+                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
+                glo[j] = 0u; ghi[j] = 0u; hlo[j] = 0u; hhi[j] = 0u;
+            }
+        }
+        __syncthreads();
+        a = seg_end;
+        k++;
+    }
+}
+
 // ------------------------------------------------------------------ split
 struct SplitSmem {
     Pair warp_tot[32];
@@ -940,6 +1032,23 @@ void launch_hist(int width, const TileDesc* tiles, uint32_t n_tiles, const TileF
         k_hist<1><<<grid, kHistThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix, st,
                                                    hist_acc, slot_pairs);
 }
+void set_hist_lpf_smem_limit(int bytes) {
+    cudaFuncSetAttribute(k_hist_lpf<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_lpf<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat,
+                     const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                     const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                     unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s) {
+    if (n_tiles == 0) return;
+    dim3 grid(grid_x, n_tiles);
+    if (width == 2)
+        k_hist_lpf<2><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix,
+                                                          st, hist_acc, slot_pairs);
+    else
+        k_hist_lpf<1><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix,
+                                                          st, hist_acc, slot_pairs);
+}
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
     dim3 grid(max_m, a.n_features);
     k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
@@ -977,6 +1086,12 @@ template __global__ void k_hist<1>(const TileDesc*, const TileFeat*, const uint3
 template __global__ void k_hist<2>(const TileDesc*, const TileFeat*, const uint32_t*, const Pair*, const NodeInfo*,
                                    const uint32_t*, const unsigned long long*, const TreeState*, Pair*,
                                    unsigned long long);
+template __global__ void k_hist_lpf<1>(const TileDesc*, const TileFeat*, const uint32_t*, const Pair*,
+                                       const NodeInfo*, const uint32_t*, const unsigned long long*, const TreeState*,
+                                       Pair*, unsigned long long);
+template __global__ void k_hist_lpf<2>(const TileDesc*, const TileFeat*, const uint32_t*, const Pair*,
+                                       const NodeInfo*, const uint32_t*, const unsigned long long*, const TreeState*,
+                                       Pair*, unsigned long long);
 template __global__ void k_transpose_block<1>(const uint8_t*, uint8_t*, uint32_t, uint32_t, uint32_t, uint64_t);
 template __global__ void k_transpose_block<2>(const uint8_t*, uint8_t*, uint32_t, uint32_t, uint32_t, uint64_t);
 

@@ -23,6 +23,7 @@ constexpr uint32_t kChunkRows = 4096; // partition / leaf chunk
 constexpr int kPartThreads = 512;
 constexpr int kPartItems = kChunkRows / kPartThreads;
 constexpr int kHistThreads = 512;
+constexpr int kHistLpfThreads = 1024;
 
 // A histogram tile: a set of features of one storage block whose bins fit in
 // shared memory.  Features are listed in TileFeat[feat_begin, feat_begin+n).
@@ -132,6 +133,11 @@ void launch_hist(int width, const TileDesc* tiles, uint32_t n_tiles, const TileF
                  const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
                  const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
                  unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
+void set_hist_lpf_smem_limit(int bytes);
+void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat,
+                     const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                     const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                     unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
 void launch_decide(const LevelArgs& a, cudaStream_t s);
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
