@@ -82,6 +82,8 @@ SIGNATURES = {
     "fbgpu_round_device": (C.c_int, [P, C.c_int32, C.c_int32, C.c_uint64, C.c_uint64, C.c_uint64, f64p, i64p]),
     "fbgpu_build_tree": (C.c_int, [P, C.POINTER(FbgpuTreeParams), u8p, C.POINTER(FbgpuTreeOut)]),
     "fbgpu_download_margins": (C.c_int, [P, f32p]),
+"fbgpu_exact_exp_available": (C.c_int32, [C.POINTER(C.c_char_p)]),
+    "fbgpu_expf_check": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, u64p, u32p]),
     "fbgpu_histogram": (C.c_int, [P, u32p, C.c_uint64, i64p, i64p]),
     "fbgpu_eval_split": (C.c_int, [P, i64p, i64p, f64p, C.POINTER(FbgpuTreeParams), C.c_float, C.c_float, u8p,
                                    C.POINTER(FbgpuSplit)]),

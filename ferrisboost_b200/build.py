@@ -37,7 +37,30 @@ def _stale() -> bool:
     return any(p.stat().st_mtime > t for p in deps)
 
 
+EXP_TABLE = HERE / "expf_exceptions.bin"
+
+
+def build_exp_table(force: bool = False) -> pathlib.Path:
+    """Generate expf_exceptions.bin: every f32 input on which the host libm's
+    expf differs from the library's f64 exp (csrc/fexp.h), by evaluating both
+    on all 2^32 inputs (csrc/gen_expf_table.cpp; a few seconds on 8 cores)."""
+    gen_src = CSRC / "gen_expf_table.cpp"
+    if not force and EXP_TABLE.exists() and EXP_TABLE.stat().st_mtime >= max(
+            gen_src.stat().st_mtime, (CSRC / "fexp.h").stat().st_mtime):
+        return EXP_TABLE
+    obj_dir = HERE / "_build"
+    obj_dir.mkdir(exist_ok=True)
+    exe = obj_dir / "gen_expf_table"
+    subprocess.run(["/usr/bin/g++", "-O2", "-std=c++17", "-fopenmp", "-ffp-contract=off", "-march=x86-64-v2",
+                    "-I", str(CSRC), str(gen_src), "-o", str(exe)], check=True)
+    tmp = EXP_TABLE.with_suffix(".bin.tmp")
+    subprocess.run([str(exe), str(tmp)], check=True, stdout=subprocess.DEVNULL)
+    os.replace(tmp, EXP_TABLE)
+    return EXP_TABLE
+
+
 def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
+    build_exp_table()
     if not force and not _stale():
         return LIB
     objs = []

@@ -1,10 +1,17 @@
 // Training context, explanation model and the C ABI of include/fbgpu.h.
 #include "ctx.h"
 
+#include <dlfcn.h>
+#include <omp.h>
+
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <mutex>
+
+#include "fexp.h"
 
 namespace fbg {
 
@@ -15,6 +22,101 @@ uint32_t ceil_div(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); 
 }  // namespace
 
 void noalloc_set_error(const char* msg) { g_last_error = msg; }
+
+// ---------------------------------------------------------------- host expf table
+namespace {
+struct ExpTable {
+    bool ok = false;
+    std::string why;
+    std::vector<std::pair<uint32_t, uint32_t>> entries;  // sorted (input bits, host expf bits)
+    std::vector<uint2> slots;
+    uint32_t probes = 0;
+};
+
+uint32_t host_expf_bits(float x) {
+    const float g = expf(x);
+    uint32_t b;
+    std::memcpy(&b, &g, 4);
+    return b;
+}
+
+// Loads expf_exceptions.bin (next to this library, or $FBGPU_EXPF_TABLE) and
+// checks it against the running host's expf: every listed input, plus 2^21
+// pseudo-random inputs, must equal fexp_core corrected by the table.
+ExpTable load_exp_table() {
+    ExpTable t;
+    std::string path;
+    if (const char* e = std::getenv("FBGPU_EXPF_TABLE")) {
+        path = e;
+    } else {
+        Dl_info info;
+        if (dladdr(reinterpret_cast<void*>(&host_expf_bits), &info) && info.dli_fname) {
+            path = info.dli_fname;
+            path = path.substr(0, path.find_last_of('/') + 1) + "expf_exceptions.bin";
+        }
+    }
+    FILE* f = path.empty() ? nullptr : std::fopen(path.c_str(), "rb");
+    if (!f) { t.why = "exception table not found at " + path; return t; }
+    char magic[8];
+    uint64_t n = 0;
+    bool good = std::fread(magic, 1, 8, f) == 8 && std::memcmp(magic, "FBEXPT01", 8) == 0 &&
+                std::fread(&n, 8, 1, f) == 1 && n < (fbx::kExpTableSlots / 2);
+    if (good) {
+        t.entries.resize(n);
+        for (uint64_t i = 0; i < n && good; i++)
+            good = std::fread(&t.entries[i].first, 4, 1, f) == 1 && std::fread(&t.entries[i].second, 4, 1, f) == 1;
+    }
+    std::fclose(f);
+    if (!good) { t.why = "malformed exception table " + path; t.entries.clear(); return t; }
+    long bad = 0;
+#pragma omp parallel for reduction(+ : bad) schedule(static)
+    for (int64_t i = 0; i < (int64_t)t.entries.size(); i++) {
+        float x;
+        std::memcpy(&x, &t.entries[i].first, 4);
+        if (host_expf_bits(x) != t.entries[i].second) bad++;
+    }
+#pragma omp parallel for reduction(+ : bad) schedule(static)
+    for (int64_t i = 0; i < (1 << 21); i++) {
+        uint64_t z = (uint64_t)i * 0x9E3779B97F4A7C15ull + 12345;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z ^= z >> 31;
+        uint32_t key = (uint32_t)z;
+        if (i & 1) {  // half the sample inside the non-trivial range [-104, 89]
+            float x = -104.0f + (float)((z >> 32) % 193000000ull) * 1e-6f;
+            std::memcpy(&key, &x, 4);
+        }
+        float x;
+        std::memcpy(&x, &key, 4);
+        auto it = std::lower_bound(t.entries.begin(), t.entries.end(), std::make_pair(key, 0u));
+        uint32_t want;
+        if (it != t.entries.end() && it->first == key) {
+            want = it->second;
+        } else {
+            const float m = fbx::fexp_core(x);
+            std::memcpy(&want, &m, 4);
+        }
+        const uint32_t got = host_expf_bits(x);
+        const bool both_nan = std::isnan(x) || (std::isnan(expf(x)));
+        if (got != want && !both_nan) bad++;
+    }
+    if (bad) { t.why = "the exception table does not match this host's expf (" + std::to_string(bad) + " inputs)"; return t; }
+    t.slots.assign(fbx::kExpTableSlots, make_uint2(fbx::kEmptyKey, 0u));
+    for (const auto& e : t.entries) {
+        uint32_t slot = fbx::exp_slot(e.first), len = 1;
+        while (t.slots[slot].x != fbx::kEmptyKey) { slot = (slot + 1) & (fbx::kExpTableSlots - 1); len++; }
+        t.slots[slot] = make_uint2(e.first, e.second);
+        t.probes = std::max(t.probes, len);
+    }
+    t.probes += 1;  // one more probe sees the empty slot that ends a sequence
+    t.ok = true;
+    return t;
+}
+
+const ExpTable& exp_table() {
+    static ExpTable t = load_exp_table();
+    return t;
+}
+}  // namespace
 
 double pow2_scale_host(double max_abs, uint64_t n_rows) {
     if (!(max_abs > 0.0) || !std::isfinite(max_abs)) return 1.0;
@@ -54,6 +156,15 @@ TrainCtx::TrainCtx(const fbgpu_config& cfg) : cfg_(cfg) {
     FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 64, s_));
     FB_CUDA_CHECK(cudaMemsetAsync(pred_.p, 0, n_ * 4, s_));
     ensure_tree_buffers(cfg.max_depth, cfg.max_leaves);
+    const ExpTable& et = exp_table();
+    const char* force = std::getenv("FBGPU_EXACT_EXP");
+    if (et.ok && !(force && std::string(force) == "host")) {
+        exptab_.alloc(sizeof(uint2) * et.slots.size());
+        FB_CUDA_CHECK(cudaMemcpyAsync(exptab_.p, et.slots.data(), sizeof(uint2) * et.slots.size(),
+                                      cudaMemcpyHostToDevice, s_));
+        exp_probes_ = et.probes;
+        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    }
 }
 
 TrainCtx::~TrainCtx() {
@@ -186,6 +297,8 @@ GradArgs TrainCtx::grad_args() const {
     a.sum = sums_.as<unsigned long long>();
     a.maxbits = sums_.as<unsigned long long>() + 2;
     a.scales = reinterpret_cast<const double*>(sums_.as<unsigned long long>() + 4);
+    a.exptab = exptab_.p ? exptab_.as<uint2>() : nullptr;
+    a.exp_probes = exp_probes_;
     return a;
 }
 
@@ -239,9 +352,10 @@ void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed,
     GradArgs a = grad_args();
     a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
     a.objective = objective;
-    if (!fast && objective == 1)
-        throw InputError("exact logistic gradients need the host exp (fbgpu_round_from_exp)");
-    launch_gradient_max(a, fast, s_);
+    if (!fast && objective == 1 && !a.exptab)
+        throw InputError("exact logistic gradients on the device need the verified host-expf table; "
+                         "use fbgpu_round_from_exp with host exp values");
+    launch_gradient_max(a, fast ? 1 : (objective == 1 ? 2 : 0), s_);
     double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
     if (fast) {
         launch_device_scales(a.maxbits, cfg_.n_rows_global, dscales, s_);
@@ -924,6 +1038,62 @@ fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t
 fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
                              int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left) {
     return guard(ctx, [&] { ctx->impl.partition(rows, n, feat, bin, missing_left, cats, out_rows, n_left); });
+}
+
+int32_t fbgpu_exact_exp_available(const char** why) {
+    const auto& t = fbg::exp_table();
+    if (why) *why = t.ok ? "" : t.why.c_str();
+    return t.ok ? 1 : 0;
+}
+
+fbgpu_status fbgpu_expf_check(int32_t device, uint32_t begin, uint32_t count, uint64_t* mismatches,
+                              uint32_t* report) {
+    return guard(nullptr, [&] {
+        const auto& t = fbg::exp_table();
+        if (!t.ok) throw fbg::InputError(t.why);
+        FB_CUDA_CHECK(cudaSetDevice(device));
+        fbg::DevMem tab, out;
+        tab.alloc(sizeof(uint2) * t.slots.size());
+        out.alloc(4ull * std::max<uint32_t>(count, 1));
+        FB_CUDA_CHECK(cudaMemcpy(tab.p, t.slots.data(), sizeof(uint2) * t.slots.size(), cudaMemcpyHostToDevice));
+        fbg::launch_expf_emulate(tab.as<uint2>(), t.probes, begin, count, out.as<uint32_t>(), nullptr);
+        std::vector<uint32_t> dev(count);
+        FB_CUDA_CHECK(cudaMemcpy(dev.data(), out.p, 4ull * count, cudaMemcpyDeviceToHost));
+        uint64_t bad = 0;
+#pragma omp parallel for reduction(+ : bad) schedule(static)
+        for (int64_t i = 0; i < (int64_t)count; i++) {
+            const uint32_t key = begin + (uint32_t)i;
+            float x;
+            std::memcpy(&x, &key, 4);
+            const float g = expf(x);
+            uint32_t gb;
+            std::memcpy(&gb, &g, 4);
+            float d;
+            std::memcpy(&d, &dev[i], 4);
+            if (gb != dev[i] && !(std::isnan(g) && std::isnan(d))) bad++;
+        }
+        *mismatches = bad;
+        if (report && bad) {  // first mismatches: (input, host expf, device, host fexp_core) x 4
+            int k = 0;
+            for (uint32_t i = 0; i < count && k < 4; i++) {
+                const uint32_t key = begin + i;
+                float x;
+                std::memcpy(&x, &key, 4);
+                const float g = expf(x);
+                uint32_t gb;
+                std::memcpy(&gb, &g, 4);
+                float d;
+                std::memcpy(&d, &dev[i], 4);
+                if (gb != dev[i] && !(std::isnan(g) && std::isnan(d))) {
+                    const float m = fbx::fexp_core(x);
+                    uint32_t mb;
+                    std::memcpy(&mb, &m, 4);
+                    report[4 * k] = key; report[4 * k + 1] = gb; report[4 * k + 2] = dev[i]; report[4 * k + 3] = mb;
+                    k++;
+                }
+            }
+        }
+    });
 }
 
 fbgpu_status fbgpu_model_create(int32_t device, uint32_t n_features, uint32_t n_trees, const uint32_t* tree_off,

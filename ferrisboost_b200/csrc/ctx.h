@@ -101,6 +101,8 @@ class TrainCtx {
     uint64_t n_local() const { return n_; }
     const fbgpu_config& config() const { return cfg_; }
     float last_tree_ms() const { return last_tree_ms_; }
+    // Exact logistic gradients can run on the device (verified host-expf table).
+    bool has_exact_exp() const { return exptab_.p != nullptr; }
     // Histogram-phase statistics of the trees grown since the last reset
     // (enabled by set_stats): device time, launches and algorithmic bytes
     // (rows x (bin bytes + 16 B gradient + 4 B row id) + bins x 16 B flushed).
@@ -153,6 +155,8 @@ class TrainCtx {
     // rows / gradients
     DevMem label_, weight_, pred_, gpair_f32_, host_exp_, fixed_;
     DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double)
+    DevMem exptab_;  // host-expf exception table (fexp.h), empty when unverified
+    uint32_t exp_probes_ = 0;
     bool has_weight_ = false;
     PinnedMem h_stage_;
 

@@ -620,8 +620,10 @@ void booster_round(Booster& b) {
     auto t0 = std::chrono::steady_clock::now();
     if (p.gpu_math == 1) {
         ctx.round_device(p.objective, 1, th, p.seed, round, nullptr, nullptr);
-    } else if (p.objective == 0) {
-        ctx.round_device(0, 0, th, p.seed, round, nullptr, nullptr);
+    } else if (p.objective == 0 || ctx.has_exact_exp()) {
+        // exact squared error, or exact logistic with the device reproduction
+        // of the host expf: gradients on the device, scales from the host libm
+        ctx.round_device(p.objective, 0, th, p.seed, round, nullptr, nullptr);
     } else {
         // exact logistic: glibc expf on the host, bounds of the f32 gradient,
         // scales with the host libm; the device recomputes the same f32

@@ -224,14 +224,36 @@ __device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, floa
     if (!row_selected(a.row0 + i, a.sub_th, a.sub_seed, a.sub_tree)) { g = 0.0f; h = 0.0f; }
 }
 
+// The host C library's expf on the device: fexp_core, except on the inputs the
+// exception table lists (fexp.h).  The probe loop is bounded by the table's
+// longest probe sequence.
+__device__ __forceinline__ float host_expf(float x, const uint2* tab, uint32_t probes) {
+    const uint32_t key = __float_as_uint(x);
+    uint32_t slot = fbx::exp_slot(key);
+    for (uint32_t i = 0; i < probes; i++) {
+        const uint2 e = tab[slot];
+        if (e.x == fbx::kEmptyKey) break;  // before the key test: kEmptyKey is also a NaN input
+        if (e.x == key) return __uint_as_float(e.y);
+        slot = (slot + 1) & (fbx::kExpTableSlots - 1);
+    }
+    return fbx::fexp_core(x);
+}
+
+__global__ void k_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint32_t count, uint32_t* out) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x)
+        out[i] = __float_as_uint(host_expf(__uint_as_float(begin + i), tab, probes));
+}
+
 // Gradient pass that only folds bounds and stores the f32 pairs (exact
-// squared error and fast mode).  mode 0: squared error / host exp; mode 1:
-// device expf (fast).
-__global__ void k_gradient_max(GradArgs a, int fast) {
+// squared error, exact logistic with the emulated host expf, fast mode).
+__global__ void k_gradient_max(GradArgs a, int mode) {
     double mg = 0.0, mh = 0.0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
         float e = 0.0f;
-        if (a.objective == 1) e = fast ? expf(-a.pred[i]) : a.host_exp[i];
+        if (a.objective == 1) {
+            const float x = -a.pred[i];
+            e = mode == 1 ? expf(x) : (mode == 2 ? host_expf(x, a.exptab, a.exp_probes) : a.host_exp[i]);
+        }
         float g, h;
         row_gradient(a, i, e, g, h);
         a.gpair_f32[2ull * i] = g;
@@ -1004,8 +1026,12 @@ static unsigned grad_grid(uint32_t n) {
     return b < 148u * 8u ? (b ? b : 1u) : 148u * 8u;
 }
 void launch_mask_max(const GradArgs& a, cudaStream_t s) { k_mask_max<<<grad_grid(a.n), 256, 0, s>>>(a); }
-void launch_gradient_max(const GradArgs& a, int fast, cudaStream_t s) {
-    k_gradient_max<<<grad_grid(a.n), 256, 0, s>>>(a, fast);
+void launch_gradient_max(const GradArgs& a, int mode, cudaStream_t s) {
+    k_gradient_max<<<grad_grid(a.n), 256, 0, s>>>(a, mode);
+}
+void launch_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint32_t count, uint32_t* out,
+                         cudaStream_t s) {
+    k_expf_emulate<<<148 * 8, 256, 0, s>>>(tab, probes, begin, count, out);
 }
 void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s) {
     k_gradient_quantize_exp<<<grad_grid(a.n), 256, 0, s>>>(a);

@@ -14,6 +14,7 @@
 // follow src/training/mod.rs:5069-5103.
 #pragma once
 #include "common.cuh"
+#include "fexp.h"
 
 namespace fbg {
 
@@ -119,11 +120,17 @@ struct GradArgs {
     unsigned long long* maxbits; // [2] max |g|, |h| as double bit patterns
     const double* scales;     // [2]
     int objective;            // 0 squared error, 1 logistic
+    const uint2* exptab;      // host-expf exception table (fexp.h), or null
+    uint32_t exp_probes;      // longest probe sequence in exptab
 };
 
 // Host-side launchers (train_kernels.cu).
 void launch_mask_max(const GradArgs& a, cudaStream_t s);
-void launch_gradient_max(const GradArgs& a, int fast, cudaStream_t s);
+// mode 0: e from host_exp (or squared error), 1: CUDA expf (fast mode),
+// 2: the host C library's expf reproduced on the device (fexp_core + exptab).
+void launch_gradient_max(const GradArgs& a, int mode, cudaStream_t s);
+void launch_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint32_t count, uint32_t* out,
+                         cudaStream_t s);
 void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s);
 void launch_quantize(const GradArgs& a, cudaStream_t s);
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,

@@ -161,7 +161,9 @@ fbgpu_status fbgpu_round_from_exp(fbgpu_ctx* ctx, int32_t objective, const float
 /* Round start with the gradient computed on the device from the resident
  * margins.  fast = 1 is gpu_math="fast" (CUDA expf; replaces
  * fast_gradient_and_quantize, src/backend/mod.rs:220-228); fast = 0 is exact
- * squared error (pure f32 arithmetic) with the scales taken by the host.
+ * mode with the scales taken by the host's libm: squared error is pure f32
+ * arithmetic, logistic uses the device reproduction of the host expf
+ * (fbgpu_exact_exp_available must be 1).
  * scales_out / root_sum_out may be NULL (no host synchronisation then). */
 fbgpu_status fbgpu_round_device(fbgpu_ctx* ctx, int32_t objective, int32_t fast, uint64_t sub_threshold,
                                 uint64_t seed, uint64_t tree, double* scales_out, int64_t* root_sum_out);
@@ -179,6 +181,23 @@ fbgpu_status fbgpu_build_tree(fbgpu_ctx* ctx, const fbgpu_tree_params* tp, const
  * / with_prediction_delta (src/backend/mod.rs:331-340): the device adds each
  * tree's leaf values itself, so the host receives margins instead of deltas. */
 fbgpu_status fbgpu_download_margins(fbgpu_ctx* ctx, float* out);
+
+/* Whether exact-mode logistic gradients can be computed on the device: the
+ * host C library's expf (which Rust's f32::exp calls in the reference,
+ * objective.rs:37-39) is reproduced on the device by an f64 exp plus a table
+ * of the inputs where the two differ, and the table has been checked against
+ * this host's expf.  Returns 1 or 0; *why gets the reason when 0.  No
+ * counterpart in the reference, whose exact mode always computes gradients on
+ * the host. */
+int32_t fbgpu_exact_exp_available(const char** why);
+
+/* Compares the device's reproduction of the host expf with the host's own
+ * expf on the inputs with bit patterns [begin, begin + count) and stores the
+ * number of differing results; `report` (16 words or NULL) receives up to four
+ * (input, host expf, device result, host fexp_core) bit quadruples (test entry
+ * point; allocates device memory). */
+fbgpu_status fbgpu_expf_check(int32_t device, uint32_t begin, uint32_t count, uint64_t* mismatches,
+                              uint32_t* report);
 
 /* ---------------------------------------------------------- component calls */
 

@@ -97,3 +97,10 @@ def test_invalid_category_is_rejected():
     X = np.array([[0.0], [1.5]], dtype=np.float32)
     with pytest.raises(ValueError, match="invalid category"):
         fb.Dataset(X, feature_types=["c"])
+
+
+def test_host_expf_table_is_verified_on_this_host():
+    import ctypes as C
+    from ferrisboost_b200 import _lib
+    why = C.c_char_p()
+    assert _lib.load().fbgpu_exact_exp_available(C.byref(why)) == 1, why.value
