@@ -411,6 +411,7 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
     FB_CUDA_CHECK(cudaMemsetAsync(node_cats_.p, 0, node_cats_.bytes, s_));
     split_.alloc(sizeof(SplitDesc) * lvl);
     chunk_left_.alloc(4 * (uint64_t)max_chunks_);
+    dirflags_.alloc((uint64_t)max_chunks_ * kPartThreads);
     chunk_off_.alloc(4 * (uint64_t)max_chunks_);
     node_left_.alloc(4 * lvl);
     trec_.alloc(sizeof(TreeRec) * tree_nodes);
@@ -540,6 +541,7 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.split = split_.as<SplitDesc>();
     a.chunk_left = chunk_left_.as<uint32_t>();
     a.chunk_off = chunk_off_.as<uint32_t>();
+    a.dirflags = dirflags_.as<uint8_t>();
     a.node_left = node_left_.as<uint32_t>();
     a.node_left_global = node_left_.as<uint32_t>();
     a.pred = pred_.as<float>();

@@ -164,7 +164,7 @@ class TrainCtx {
     uint32_t buf_depth_ = 0xffffffffu, buf_leaves_ = 0xffffffffu;
     uint32_t max_level_nodes_ = 0, max_split_nodes_ = 0, max_acc_ = 0, max_tree_nodes_ = 0, max_chunks_ = 0;
     DevMem rows_[2], nodes_[2], acc_list_[2], acc_prefix_[2], chunk_prefix_[2];
-    DevMem hist_acc_, hist_[2], feat_best_, feat_cats_, node_best_, node_cats_, split_, chunk_left_, chunk_off_,
+    DevMem dirflags_, hist_acc_, hist_[2], feat_best_, feat_cats_, node_best_, node_cats_, split_, chunk_left_, chunk_off_,
         node_left_, trec_, tcats_, state_;
     PinnedMem h_tree_;
     float last_tree_ms_ = 0.0f;

@@ -797,7 +797,9 @@ __device__ __forceinline__ bool goes_left(const LevelArgs& a, const SplitDesc& s
 // Count the left rows of every chunk of a split node; add the leaf value to
 // the predictions of every row of a node that stops growing here
 // (training/mod.rs:4409-4425; delta[row] = leaf, then pred += delta, is the
-// same single f32 addition).
+// same single f32 addition).  Thread t owns rows [8t, 8t + 8) of its chunk;
+// with a.dirflags set it stores their directions as one byte (bit k = row
+// 8t + k goes left) so the scatter pass does not gather the bins again.
 __global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
     __shared__ uint32_t wt[32];
     __shared__ uint32_t cats[8];
@@ -811,21 +813,42 @@ __global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
     const uint32_t cnt = min(kChunkRows, ni.len - r0);
     const uint32_t* rows = a.rows_cur + ni.start + r0;
     const SplitDesc sd = a.split[j];
+    const uint32_t i0 = threadIdx.x * kPartItems;
+    uint32_t r[kPartItems];
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) r[k] = i0 + k < cnt ? rows[i0 + k] : 0u;
     if (sd.child_slot < 0) {
         const float leaf = a.trec[ni.tree_id].leaf;
-        for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-            const uint32_t r = rows[i];
-            a.pred[r] = __fadd_rn(a.pred[r], leaf);
-        }
+#pragma unroll
+        for (int k = 0; k < kPartItems; k++)
+            if (i0 + k < cnt) a.pred[r[k]] = __fadd_rn(a.pred[r[k]], leaf);
         if (threadIdx.x == 0) a.chunk_left[c] = 0u;
         return;
     }
     if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
+    const FeatLoc fl = a.floc[sd.feat];
     __syncthreads();
-    uint32_t nleft = 0;
-    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) nleft += goes_left(a, sd, cats, rows[i]) ? 1u : 0u;
+    uint32_t bin[kPartItems];
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        bin[k] = fl.missing;
+        if (i0 + k < cnt) {
+            const uint8_t* p = fl.base + (size_t)r[k] * fl.stride + fl.byte_off;
+            bin[k] = fl.width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+        }
+    }
+    uint32_t flags = 0;
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        bool left;
+        if (bin[k] == fl.missing) left = (sd.flags & 2u) != 0;
+        else if (sd.flags & 4u) left = bin[k] >= 256u || ((cats[bin[k] >> 5] >> (bin[k] & 31)) & 1u) == 0u;
+        else left = bin[k] < sd.bin;
+        if (i0 + k < cnt && left) flags |= 1u << k;
+    }
+    if (a.dirflags) a.dirflags[(size_t)c * kPartThreads + threadIdx.x] = (uint8_t)flags;
     uint32_t tot;
-    (void)block_excl_scan_u32<kPartThreads>(nleft, wt, tot);
+    (void)block_excl_scan_u32<kPartThreads>((uint32_t)__popc(flags), wt, tot);
     if (threadIdx.x == 0) a.chunk_left[c] = tot;
 }
 
@@ -853,7 +876,8 @@ __global__ void __launch_bounds__(1024) k_part_scan(LevelArgs a) {
 }
 
 // Stable scatter of every chunk of a split node into [left | right] of the
-// node's span in the next arena.
+// node's span in the next arena (directions from k_part_count's bytes, or
+// recomputed when a.dirflags is null).
 __global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
     __shared__ uint32_t wt[32];
     __shared__ uint32_t cats[8];
@@ -869,17 +893,21 @@ __global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
     const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
     const uint32_t cnt = min(kChunkRows, ni.len - r0);
     const uint32_t* rows = a.rows_cur + ni.start + r0;
-    if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
-    __syncthreads();
-    uint32_t r[kPartItems];
-    uint32_t flags = 0, nl = 0;
     const uint32_t i0 = threadIdx.x * kPartItems;
+    uint32_t r[kPartItems];
 #pragma unroll
-    for (int k = 0; k < kPartItems; k++) {
-        const uint32_t i = i0 + k;
-        r[k] = i < cnt ? rows[i] : 0u;
-        if (i < cnt && goes_left(a, sd, cats, r[k])) { flags |= 1u << k; nl++; }
+    for (int k = 0; k < kPartItems; k++) r[k] = i0 + k < cnt ? rows[i0 + k] : 0u;
+    uint32_t flags = 0;
+    if (a.dirflags) {
+        flags = a.dirflags[(size_t)c * kPartThreads + threadIdx.x];
+    } else {
+        if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kPartItems; k++)
+            if (i0 + k < cnt && goes_left(a, sd, cats, r[k])) flags |= 1u << k;
     }
+    const uint32_t nl = (uint32_t)__popc(flags);
     uint32_t L;
     const uint32_t lpos = block_excl_scan_u32<kPartThreads>(nl, wt, L);
     uint32_t li = lpos, ri = L + (min(i0, cnt) - lpos);

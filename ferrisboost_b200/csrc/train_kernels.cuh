@@ -96,6 +96,7 @@ struct LevelArgs {
     SplitDesc* split;            // [node]
     uint32_t* chunk_left;        // per chunk left count
     uint32_t* chunk_off;         // per chunk left offset within its node
+    uint8_t* dirflags;           // per 8 rows of a chunk: direction bits (null: recompute)
     uint32_t* node_left;         // per node left count (this rank)
     const uint32_t* node_left_global; // per node left count over all ranks
     const uint32_t* rows_cur;
