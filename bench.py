@@ -9,13 +9,17 @@ config's shape stands in for HIGGS (not in this container).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--rows R]
 
-value: exact-mode s/100 rounds from CUDA events on the training stream (bins
-resident in HBM; the per-round exact-mode host step — margins D2H, glibc
-expf, exp values H2D — is inside the interval).  e2e: the same metric through
-the public train() call from host arrays (sketch, quantization, H2D of the
-bins and labels, K rounds, model download), normalised per 100 rounds.
-cpu_baseline / --impl reference: the C++ restatement of the reference CPU
-engine (oracle/), all host threads, bounded sample of the same workload.
+value: exact-mode s/100 rounds from CUDA events on the training stream, bins
+resident in HBM (gradients, glibc-exact expf reproduced on the device,
+quantization, the tree's levels and the margin update are all inside the
+interval).  e2e: the same metric through the public train() call from host
+arrays (sketch, binning, H2D of the bins and labels, K rounds, model JSON),
+normalised per 100 rounds.  N > 1 (torchrun, one process per GPU): rows are
+sharded over the ranks, the library's NCCL communicator all-reduces the
+per-level histograms; the total work is fixed (strong scaling) and times are
+the max over ranks.  cpu_baseline / --impl reference: the C++ restatement of
+the reference CPU engine (oracle/), all host threads, bounded sample of the
+same workload.
 """
 import argparse
 import json
@@ -125,42 +129,92 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def _dist(world):
+    """gloo process group for the barrier and the max over ranks (the training
+    collectives are the library's own NCCL communicator)."""
+    if world == 1:
+        return None
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def _fence(dist):
+    """Barrier + device synchronize, on both sides of a timed region."""
+    import torch
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(dist, v):
+    if not dist:
+        return float(v)
+    import torch
+    t = torch.tensor([float(v)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_ours(args, rank, world):
+    import torch
     import ferrisboost_b200 as fb
-    if world > 1:
-        raise SystemExit("multi-GPU row sharding is not wired into bench.py yet")
+    from ferrisboost_b200 import distributed as fbd
+    from ferrisboost_b200 import _lib
+    dist = _dist(world)
     device = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(device)
+    lib = _lib.load()
     t0 = time.perf_counter()
     X, y = make_data(args.rows)
     gen_s = time.perf_counter() - t0
     p = dict(PARAMS, device=f"cuda:{device}")
+    n = args.rows
+    lo, hi = fbd.shard_range(n, world, rank)
 
-    # e2e: the public train() from host arrays, K rounds
+    def train_public(params, rounds, booster=False):
+        if world == 1:
+            if booster:
+                ds = fb.Dataset(X, max_bin=params["max_bin"])
+                b = fb.Booster(params, ds, y)
+                b.update(rounds)
+                return b
+            return fb.train(params, X, label=y, num_boost_round=rounds)
+        return fbd.train(params, X, label=y, num_boost_round=rounds, timeout_s=300, return_booster=booster)
+
+    # e2e: the public train() from host arrays, K rounds (sketch, binning,
+    # uploads, K rounds, model); wall clock, max over ranks
+    _fence(dist)
     t0 = time.perf_counter()
-    m = fb.train(p, X, label=y, num_boost_round=args.steps)
-    e2e_s = time.perf_counter() - t0
+    m = train_public(p, args.steps)
     json_bytes = len(m.to_json())
+    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
     del m
 
-    # device-resident steps
+    # device-resident steps: W warm-up rounds, then K rounds timed with CUDA
+    # events on the training stream, bracketed by barrier + synchronize
     t0 = time.perf_counter()
-    ds = fb.Dataset(X, max_bin=p["max_bin"])
-    sketch_s = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    b = fb.Booster(p, ds, y)
-    upload_s = time.perf_counter() - t0
-    b.update(args.warmup)
+    b = train_public(p, args.warmup, booster=True)
+    setup_s = time.perf_counter() - t0
     b.set_stats(True)
+    _fence(dist)
+    l0 = lib.fbgpu_launch_count()
     with ClockSampler(device) as clk:
         b.update(args.steps)
+    launches = lib.fbgpu_launch_count() - l0
+    _fence(dist)
     t = b.timing()
-    ms_step = t["device_ms"] / args.steps
+    dev_ms = _max_over_ranks(dist, t["device_ms"])
+    ms_step = dev_ms / args.steps
     s100 = ms_step * 100.0 / 1000.0
 
-    fast = fb.Booster(dict(p, gpu_math="fast"), ds, y)
-    fast.update(args.warmup)
+    fast = train_public(dict(p, gpu_math="fast"), args.warmup, booster=True)
+    _fence(dist)
     fast.update(args.steps)
-    tf = fast.timing()
+    _fence(dist)
+    fast_ms = _max_over_ranks(dist, fast.timing()["device_ms"])
+    del fast
 
     peaks = {}
     try:
@@ -170,42 +224,49 @@ def run_ours(args, rank, world):
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    launches = max(t["hist_launches"], 1.0)
+    hist_launches = max(t["hist_launches"], 1.0)
     hist_gbs = t["hist_bytes"] / (t["hist_ms"] / 1000.0) / 1e9 if t["hist_ms"] > 0 else None
 
-    n = args.rows
-    bins_bytes = n * 64
+    rows_local = hi - lo
+    bins_bytes = rows_local * 56  # 28 16-bit bins per row (max_bin 256 needs 257 bins + missing)
+    depth = PARAMS["max_depth"]
+    tree_readback = 32 * (2 ** (depth + 1)) + 64
     line = {
         "metric": "train s/100 rounds", "value": round(s100, 4), "unit": "s/100 rounds", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
         "config": {"workload": "configs[1] binary:logistic 11M x 28, depth 8, max_bin 256, eta 0.1, gpu_math exact",
-                   "rows": n, "features": N_FEATURES, "l2": "inputs larger than L2 (bins 704 MB, gradients 176 MB)"},
+                   "rows": n, "features": N_FEATURES, "parallelism": f"row shards x{world}",
+                   "l2": "inputs larger than L2 (bins 704 MB, gradients 176 MB)"},
         "e2e": {"value": round(e2e_s / args.steps * 100.0, 4), "unit": "s/100 rounds",
-                "h2d_bytes_per_step": int((bins_bytes + 4 * n) / args.steps + 4 * n),
-                "d2h_bytes_per_step": int(4 * n + json_bytes / args.steps),
-                "includes": "sketch + quantize + upload + K rounds + model JSON, public train()"},
-        "gpu_launches": int(t["trees"] and (9 + 8 * 9) * args.steps),
+                "h2d_bytes_per_step": int((bins_bytes + 4 * rows_local) / args.steps),
+                "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / args.steps),
+                "includes": "sketch + binning + upload + K rounds + model JSON through the public train(); "
+                            "per-rank bytes; wall clock, max over ranks"},
+        "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(hist_gbs / hbm_peak, 4) if hist_gbs else None,
-                     "traffic": None, "kernel": "k_hist (histogram)",
-                     "per_launch_ms": round(t["hist_ms"] / launches, 4),
-                     "alg_bytes_per_launch": int(t["hist_bytes"] / launches), "peak_source": peak_src},
+                     "traffic": None, "kernel": "k_hist_lpf (histogram), rank 0",
+                     "per_launch_ms": round(t["hist_ms"] / hist_launches, 4),
+                     "alg_bytes_per_launch": int(t["hist_bytes"] / hist_launches), "peak_source": peak_src},
         "clocks": clk.summary(),
         "breakdown": {"hist_share_of_device": round(t["hist_ms"] / t["device_ms"], 4) if t["device_ms"] else None,
-                      "host_gradient_ms_per_step": round(t["gradient_ms"] / args.steps, 3),
-                      "fast_mode_s_per_100_rounds": round(tf["device_ms"] / args.steps * 100 / 1000, 4),
-                      "setup_s": {"datagen": round(gen_s, 2), "sketch_quantize": round(sketch_s, 2),
-                                  "upload": round(upload_s, 2)}},
+                      "fast_mode_s_per_100_rounds": round(fast_ms / args.steps * 100 / 1000, 4),
+                      "setup_s": {"datagen": round(gen_s, 2), "sketch_bin_upload_warmup": round(setup_s, 2)}},
     }
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         csteps = 2
         setup, rs = reference_rounds(X, y, csteps, 1)
         line["cpu_baseline"] = {"value": round(float(np.mean(rs)) * 100, 4), "unit": "s/100 rounds",
                                 "cores": cpu_threads(), "kind": "port",
                                 "sample": f"{csteps} rounds after 1 warm-up round on the full {n}-row workload "
                                           f"(oracle C++ restatement, all host threads)"}
-    print(json.dumps(line), flush=True)
+    del b
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def main():
@@ -219,6 +280,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
+        # one process per GPU: relaunch under torchrun on this node
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={args.gpus}",
+               "--master-addr", "127.0.0.1", "--master-port", os.environ.get("MASTER_PORT", "29517"),
+               os.path.abspath(__file__)] + sys.argv[1:]
+        raise SystemExit(subprocess.call(cmd))
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

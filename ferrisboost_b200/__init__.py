@@ -16,7 +16,7 @@ import ctypes as C
 import json
 import math
 import os
-from typing import Any, Mapping, Sequence
+from typing import Any, Mapping, NamedTuple, Sequence
 
 import numpy as np
 
@@ -203,19 +203,42 @@ def _feature_flags(feature_types: Sequence[str] | None, n: int) -> np.ndarray | 
     return flags if flags.any() else None
 
 
+class Shard(NamedTuple):
+    """One rank's part of a row-sharded run (see ``ferrisboost_b200.distributed``)."""
+    row_offset: int       # global index of this rank's first row
+    n_rows_global: int    # rows over all ranks
+    nccl_id: bytes        # fbgpu_nccl_unique_id of rank 0, 128 bytes
+    nranks: int
+    rank: int
+    base_score: float     # label mean over all rows (fb_label_mean) or the given base_score
+    timeout_ms: int = 120000
+
+
 class Dataset:
     """Quantized training data: cuts from the weighted quantile sketch and
     column blocks of u8/u16 bins (the reference's DenseSource)."""
 
     def __init__(self, data: Any, max_bin: int = 255, weight: Any = None, feature_types=None, nthread: int = 0,
-                 missing: float = float("nan")):
+                 missing: float = float("nan"), cuts: tuple[np.ndarray, np.ndarray] | None = None):
+        """``cuts`` = (cut values, F+1 offsets) bins the rows with given cuts
+        (validation data, or one row shard of a multi-GPU run) instead of
+        sketching them."""
         X = _as_matrix(data, missing)
         self.n_rows, self.n_features = X.shape
         w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
         cat = _feature_flags(feature_types, self.n_features)
         self.categorical = cat
-        self._h = lib().fb_dataset_from_dense(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
-                                              _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), nthread)
+        if cuts is None:
+            self._h = lib().fb_dataset_from_dense(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
+                                                  _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), nthread)
+        else:
+            cv = np.ascontiguousarray(cuts[0], dtype=np.float32)
+            off = np.ascontiguousarray(cuts[1], dtype=np.uint32)
+            if off.shape != (self.n_features + 1,) or int(off[-1]) != cv.size or np.any(np.diff(off.astype(np.int64)) < 0):
+                raise ValueError("cuts must be (values, offsets) with F+1 non-decreasing offsets ending at len(values)")
+            self._h = lib().fb_dataset_with_cuts(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1],
+                                                 _lib.ptr(cv if cv.size else np.zeros(1, np.float32), C.c_float),
+                                                 _lib.ptr(off, C.c_uint32), _lib.ptr(cat, C.c_uint8), nthread)
         if not self._h:
             raise ValueError(_err())
 
@@ -242,7 +265,11 @@ class Dataset:
 class Booster:
     """A training run on one CUDA device; ``update(k)`` adds k trees."""
 
-    def __init__(self, params: Mapping[str, Any], dataset: Dataset, label: Any, weight: Any = None):
+    def __init__(self, params: Mapping[str, Any], dataset: Dataset, label: Any, weight: Any = None,
+                 shard: "Shard | None" = None):
+        """``shard`` makes this booster one rank of a row-sharded multi-GPU run
+        (``ferrisboost_b200.distributed``); ``dataset``, ``label`` and
+        ``weight`` then hold that rank's rows only."""
         p = _normalize_params(params, 1)
         y = np.ascontiguousarray(label, dtype=np.float32)
         if y.shape != (dataset.n_rows,):
@@ -260,7 +287,15 @@ class Booster:
             mono[:len(mc)] = mc
             fp.monotone = _lib.ptr(mono, C.c_int8)
         self._keep = (y, w, mono, dataset)
-        self._h = lib().fb_booster_create(dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), C.byref(fp))
+        if shard is None:
+            self._h = lib().fb_booster_create(dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float),
+                                              C.byref(fp))
+        else:
+            fp.base_score = shard.base_score
+            nid = np.frombuffer(shard.nccl_id, dtype=np.uint8).copy()
+            self._h = lib().fb_booster_create_sharded(
+                dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), C.byref(fp), shard.row_offset,
+                shard.n_rows_global, _lib.ptr(nid, C.c_uint8), shard.nranks, shard.rank, shard.timeout_ms)
         if not self._h:
             raise ValueError(_err())
 

@@ -71,6 +71,7 @@ SIGNATURES = {
     # include/fbgpu.h
     "fbgpu_last_error": (C.c_char_p, [P]),
     "fbgpu_device_count": (C.c_int32, []),
+    "fbgpu_launch_count": (C.c_uint64, []),
     "fbgpu_ctx_create": (C.c_int, [C.POINTER(FbgpuConfig), C.POINTER(P)]),
     "fbgpu_ctx_destroy": (None, [P]),
     "fbgpu_set_features": (C.c_int, [P, u32p, u8p, u8p]),
@@ -82,13 +83,15 @@ SIGNATURES = {
     "fbgpu_round_device": (C.c_int, [P, C.c_int32, C.c_int32, C.c_uint64, C.c_uint64, C.c_uint64, f64p, i64p]),
     "fbgpu_build_tree": (C.c_int, [P, C.POINTER(FbgpuTreeParams), u8p, C.POINTER(FbgpuTreeOut)]),
     "fbgpu_download_margins": (C.c_int, [P, f32p]),
-"fbgpu_exact_exp_available": (C.c_int32, [C.POINTER(C.c_char_p)]),
+    "fbgpu_nccl_unique_id": (C.c_int, [u8p]),
+    "fbgpu_ctx_set_comm": (C.c_int, [P, u8p, C.c_int32, C.c_int32, C.c_uint32]),
+    "fbgpu_exact_exp_available": (C.c_int32, [C.POINTER(C.c_char_p)]),
     "fbgpu_expf_check": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, u64p, u32p]),
     "fbgpu_histogram": (C.c_int, [P, u32p, C.c_uint64, i64p, i64p]),
     "fbgpu_eval_split": (C.c_int, [P, i64p, i64p, f64p, C.POINTER(FbgpuTreeParams), C.c_float, C.c_float, u8p,
                                    C.POINTER(FbgpuSplit)]),
     "fbgpu_partition": (C.c_int, [P, u32p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_int32, u32p, u32p, u64p]),
-"fbgpu_partition_noalloc": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint64, C.c_uint32,
+    "fbgpu_partition_noalloc": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint64, C.c_uint32,
                                          C.c_int32, u32p, P, P, P]),
     "fbgpu_model_create": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, u32p, i32p, i32p, u32p, f32p, u8p, f32p,
                                      u32p, u32p, u32p, C.c_uint64, C.c_float, C.POINTER(P)]),
@@ -102,11 +105,16 @@ SIGNATURES = {
     "fb_last_error": (C.c_char_p, []),
     "fb_dataset_from_dense": (P, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, C.c_int32]),
     "fb_dataset_with_cuts": (P, [f32p, C.c_uint64, C.c_uint32, f32p, u32p, u8p, C.c_int32]),
+    "fb_sketch_features": (C.c_int64, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, u32p, C.c_uint32,
+                                       C.c_int32, f32p, u32p, C.c_uint64]),
+    "fb_label_mean": (C.c_float, [f32p, f32p, C.c_uint64]),
     "fb_dataset_free": (None, [P]),
     "fb_dataset_rows": (C.c_uint64, [P]),
     "fb_dataset_cuts": (C.c_int64, [P, f32p, u32p, C.c_uint64]),
     "fb_dataset_column": (C.c_int32, [P, C.c_uint32, u16p]),
     "fb_booster_create": (P, [P, f32p, f32p, C.POINTER(FbParams)]),
+    "fb_booster_create_sharded": (P, [P, f32p, f32p, C.POINTER(FbParams), C.c_uint64, C.c_uint64, u8p, C.c_int32,
+                                      C.c_int32, C.c_uint32]),
     "fb_booster_free": (None, [P]),
     "fb_booster_update": (C.c_int32, [P, C.c_uint32]),
     "fb_booster_timing": (None, [P, f64p]),

@@ -17,7 +17,7 @@ import sys
 HERE = pathlib.Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libfbgpu.so"
-SOURCES = ["train_kernels.cu", "explain_kernels.cu", "ctx.cu", "engine.cu", "noalloc.cu"]
+SOURCES = ["train_kernels.cu", "explain_kernels.cu", "ctx.cu", "engine.cu", "noalloc.cu", "nccl_loader.cu"]
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 
 
@@ -27,6 +27,26 @@ def _nvcc() -> str:
         if c and (pathlib.Path(c).exists() or c == "nvcc"):
             return c
     return "nvcc"
+
+
+def _nccl_include() -> str:
+    """Directory of nccl.h: the one of the NCCL wheel PyTorch loads at run time
+    (the library binds NCCL with dlopen, so only the header is needed here),
+    else the system's."""
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+        if spec and spec.submodule_search_locations:
+            for loc in spec.submodule_search_locations:
+                inc = pathlib.Path(loc) / "include"
+                if (inc / "nccl.h").exists():
+                    return str(inc)
+    except (ImportError, ValueError):
+        pass
+    for inc in (os.environ.get("NCCL_INCLUDE"), "/usr/include", "/usr/local/include"):
+        if inc and (pathlib.Path(inc) / "nccl.h").exists():
+            return inc
+    raise RuntimeError("nccl.h not found (set NCCL_INCLUDE)")
 
 
 def _stale() -> bool:
@@ -67,7 +87,8 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     obj_dir = HERE / "_build"
     obj_dir.mkdir(exist_ok=True)
     common = [_nvcc(), ARCH, "-lineinfo", "-O3", "-std=c++17", "-fmad=false", "-ccbin", "/usr/bin/g++",
-              "-Xcompiler", "-fPIC,-fopenmp,-ffp-contract=off,-O3", "-I", str(HERE.parent / "include")]
+              "-Xcompiler", "-fPIC,-fopenmp,-ffp-contract=off,-O3", "-I", str(HERE.parent / "include"),
+              "-I", _nccl_include()]
     procs = []
     for src in SOURCES:
         obj = obj_dir / (pathlib.Path(src).stem + ".o")
@@ -86,7 +107,7 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     if failed:
         raise RuntimeError("nvcc failed:\n" + "\n".join(failed))
     tmp = LIB.with_suffix(".so.tmp")
-    link = [_nvcc(), ARCH, "-shared", "-ccbin", "/usr/bin/g++", "-o", str(tmp)] + objs + ["-lgomp"]
+    link = [_nvcc(), ARCH, "-shared", "-ccbin", "/usr/bin/g++", "-o", str(tmp)] + objs + ["-lgomp", "-ldl"]
     subprocess.run(link, check=True)
     os.replace(tmp, LIB)
     return LIB

@@ -9,6 +9,9 @@
 
 namespace fbg {
 
+// Counts this library's kernel launches (fbgpu_launch_count).
+void count_launch();
+
 // Fixed-point gradient pair, modulo-2^64 arithmetic (types.rs:151-227).
 struct Pair {
     long long g, h;

@@ -5,6 +5,7 @@
 #include <omp.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
@@ -22,6 +23,11 @@ uint32_t ceil_div(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); 
 }  // namespace
 
 void noalloc_set_error(const char* msg) { g_last_error = msg; }
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 // ---------------------------------------------------------------- host expf table
 namespace {
@@ -130,12 +136,53 @@ double pow2_scale_host(double max_abs, uint64_t n_rows) {
 }
 
 // ======================================================================= TrainCtx
+void TrainCtx::set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t timeout_ms) {
+    if (!unique_id) throw InputError("unique_id is null");
+    if (nranks < 1 || rank < 0 || rank >= nranks) throw InputError("invalid rank / world size");
+    if (comm_) throw InputError("the context already has a communicator");
+    if (nranks == 1) return;
+    comm_.reset(new NcclComm(unique_id, nranks, rank, cfg_.device, timeout_ms));
+    nranks_ = nranks;
+    rank_ = rank;
+}
+
+void TrainCtx::allreduce_max_host(double* v, int count) {
+    if (!comm_ || count <= 0) return;
+    if (count > 8) throw InputError("allreduce_max_host takes at most 8 values");
+    for (int i = 0; i < count; i++)
+        if (!(v[i] >= 0.0)) throw InputError("allreduce_max_host needs non-negative values");
+    if (!comm_scratch_.p) comm_scratch_.alloc(64);
+    double* h = h_small_.as<double>();
+    std::memcpy(h, v, 8ull * count);
+    FB_CUDA_CHECK(cudaMemcpyAsync(comm_scratch_.p, h, 8ull * count, cudaMemcpyHostToDevice, s_));
+    allreduce_u64(comm_scratch_.p, count, true);
+    FB_CUDA_CHECK(cudaMemcpyAsync(h, comm_scratch_.p, 8ull * count, cudaMemcpyDeviceToHost, s_));
+    sync();
+    std::memcpy(v, h, 8ull * count);
+}
+
+void TrainCtx::sync() {
+    if (comm_) comm_->sync(s_);
+    else FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+}
+
+void TrainCtx::allreduce_u64(void* buf, size_t count, bool max_op) {
+    if (!comm_ || count == 0) return;
+    comm_->allreduce(buf, buf, count, /*u64=*/true, max_op, s_);
+}
+
+void TrainCtx::allreduce_u32(const void* src, void* dst, size_t count) {
+    if (!comm_ || count == 0) return;
+    comm_->allreduce(src, dst, count, /*u64=*/false, false, s_);
+}
+
 TrainCtx::TrainCtx(const fbgpu_config& cfg) : cfg_(cfg) {
     if (cfg.n_features == 0) throw InputError("training data must have at least one feature");
     if (cfg.n_rows > 0xffffffffull) throw InputError("a shard holds at most 2^32 - 1 rows (u32 row ids)");
     if (cfg.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     FB_CUDA_CHECK(cudaSetDevice(cfg.device));
     FB_CUDA_CHECK(cudaStreamCreateWithFlags(&s_, cudaStreamNonBlocking));
+    h_small_.reserve(512);
     FB_CUDA_CHECK(cudaEventCreate(&ev0_));
     FB_CUDA_CHECK(cudaEventCreate(&ev1_));
     for (auto& e : hev_) FB_CUDA_CHECK(cudaEventCreate(&e));
@@ -168,6 +215,13 @@ TrainCtx::TrainCtx(const fbgpu_config& cfg) : cfg_(cfg) {
 }
 
 TrainCtx::~TrainCtx() {
+    if (comm_ && s_) {
+        try {
+            comm_->sync(s_);
+        } catch (const std::exception&) {
+        }
+    }
+    comm_.reset();
     if (s_) cudaStreamSynchronize(s_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
@@ -206,7 +260,7 @@ void TrainCtx::set_features(const uint32_t* n_bins, const uint8_t* width, const 
     tiles_valid_ = false;
     buf_depth_ = 0xffffffffu;  // histogram slots depend on total_bins
     ensure_tree_buffers(cfg_.max_depth, cfg_.max_leaves);
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
 }
 
 void TrainCtx::ensure_features() const {
@@ -246,7 +300,7 @@ void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t
         FB_CUDA_CHECK(cudaMemcpyAsync(stage.p, host.data(), rows * n_feats * width, cudaMemcpyHostToDevice, s_));
         launch_transpose((int)width, stage.as<uint8_t>(), b->data.as<uint8_t>(), (uint32_t)rows, n_feats, b->stride,
                          r0, s_);
-        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+        sync();
     }
     std::vector<FeatLoc> floc(F_);
     const int bi = (int)blocks_.size();
@@ -261,7 +315,7 @@ void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t
         floc[f] = FeatLoc{blk.data.as<uint8_t>(), blk.stride, feat_byte_[f], blk.width, blk.width == 2 ? 65535u : 255u};
     }
     FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_.p, floc.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
     tiles_valid_ = false;
 }
 
@@ -277,9 +331,9 @@ void TrainCtx::set_labels(const float* labels, const float* weights, const float
     } else {
         std::vector<float> v(n_, base_margin);
         FB_CUDA_CHECK(cudaMemcpyAsync(pred_.p, v.data(), n_ * 4, cudaMemcpyHostToDevice, s_));
-        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+        sync();
     }
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
 }
 
 GradArgs TrainCtx::grad_args() const {
@@ -309,41 +363,49 @@ void TrainCtx::upload_and_quantize(const float* gpair, uint64_t th, uint64_t see
     GradArgs a = grad_args();
     a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
     launch_mask_max(a, s_);
-    unsigned long long mb[2];
+    allreduce_u64(a.maxbits, 2, true);
+    unsigned long long* mb = h_small_.as<unsigned long long>();
     FB_CUDA_CHECK(cudaMemcpyAsync(mb, sums_.as<unsigned long long>() + 2, 16, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
     double mg, mh;
     std::memcpy(&mg, &mb[0], 8);
     std::memcpy(&mh, &mb[1], 8);
     if (!std::isfinite(mg) || !std::isfinite(mh))
         throw InputError("non-finite gradient or Hessian (or invalid bounds); reduce extreme labels, weights, "
                          "base_score or objective parameters");
-    double sc[2] = {pow2_scale_host(mg, cfg_.n_rows_global), pow2_scale_host(mh, cfg_.n_rows_global)};
+    double* sc = h_small_.as<double>() + 2;
+    sc[0] = pow2_scale_host(mg, cfg_.n_rows_global);
+    sc[1] = pow2_scale_host(mh, cfg_.n_rows_global);
     FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, sc, 16, cudaMemcpyHostToDevice, s_));
     launch_quantize(a, s_);
+    allreduce_u64(sums_.p, 2, false);
     if (scales_out) { scales_out[0] = sc[0]; scales_out[1] = sc[1]; }
-    if (sum_out) {
-        FB_CUDA_CHECK(cudaMemcpyAsync(sum_out, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
-    }
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    int64_t* hs = h_small_.as<int64_t>() + 4;
+    FB_CUDA_CHECK(cudaMemcpyAsync(hs, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
+    sync();
+    if (sum_out) { sum_out[0] = hs[0]; sum_out[1] = hs[1]; }
 }
 
 void TrainCtx::upload_fixed(const int64_t* fixed, const double* scales, const int64_t* sum) {
     FB_CUDA_CHECK(cudaMemcpyAsync(fixed_.p, fixed, n_ * 16, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, sum, 16, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, scales, 16, cudaMemcpyHostToDevice, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
 }
 
 void TrainCtx::round_from_exp(int objective, const float* host_exp, uint64_t th, uint64_t seed, uint64_t tree,
                               const double* scales) {
     if (host_exp) FB_CUDA_CHECK(cudaMemcpyAsync(host_exp_.p, host_exp, n_ * 4, cudaMemcpyHostToDevice, s_));
-    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, scales, 16, cudaMemcpyHostToDevice, s_));
+    double* hsc = h_small_.as<double>() + 8;
+    hsc[0] = scales[0];
+    hsc[1] = scales[1];
+    FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, hsc, 16, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 16, s_));
     GradArgs a = grad_args();
     a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
     a.objective = objective;
     launch_gradient_quantize_exp(a, s_);
+    allreduce_u64(sums_.p, 2, false);
 }
 
 void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
@@ -356,25 +418,33 @@ void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed,
         throw InputError("exact logistic gradients on the device need the verified host-expf table; "
                          "use fbgpu_round_from_exp with host exp values");
     launch_gradient_max(a, fast ? 1 : (objective == 1 ? 2 : 0), s_);
+    allreduce_u64(a.maxbits, 2, true);
     double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
     if (fast) {
         launch_device_scales(a.maxbits, cfg_.n_rows_global, dscales, s_);
     } else {
-        unsigned long long mb[2];
+        unsigned long long* mb = h_small_.as<unsigned long long>();
         FB_CUDA_CHECK(cudaMemcpyAsync(mb, a.maxbits, 16, cudaMemcpyDeviceToHost, s_));
-        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+        sync();
         double mg, mh;
         std::memcpy(&mg, &mb[0], 8);
         std::memcpy(&mh, &mb[1], 8);
         if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
-        double sc[2] = {pow2_scale_host(mg, cfg_.n_rows_global), pow2_scale_host(mh, cfg_.n_rows_global)};
+        double* sc = h_small_.as<double>() + 2;
+        sc[0] = pow2_scale_host(mg, cfg_.n_rows_global);
+        sc[1] = pow2_scale_host(mh, cfg_.n_rows_global);
         FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
-        FB_CUDA_CHECK(cudaStreamSynchronize(s_));
     }
     launch_quantize(a, s_);
-    if (scales_out) FB_CUDA_CHECK(cudaMemcpyAsync(scales_out, dscales, 16, cudaMemcpyDeviceToHost, s_));
-    if (sum_out) FB_CUDA_CHECK(cudaMemcpyAsync(sum_out, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
-    if (scales_out || sum_out) FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    allreduce_u64(sums_.p, 2, false);
+    if (scales_out || sum_out) {
+        unsigned long long* hs = h_small_.as<unsigned long long>() + 4;
+        FB_CUDA_CHECK(cudaMemcpyAsync(hs, dscales, 16, cudaMemcpyDeviceToHost, s_));
+        FB_CUDA_CHECK(cudaMemcpyAsync(hs + 2, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
+        sync();
+        if (scales_out) std::memcpy(scales_out, hs, 16);
+        if (sum_out) std::memcpy(sum_out, hs + 2, 16);
+    }
 }
 
 void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
@@ -414,6 +484,7 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
     dirflags_.alloc((uint64_t)max_chunks_ * kPartThreads);
     chunk_off_.alloc(4 * (uint64_t)max_chunks_);
     node_left_.alloc(4 * lvl);
+    node_left_global_.alloc(4 * lvl);
     trec_.alloc(sizeof(TreeRec) * tree_nodes);
     tcats_.alloc(32 * tree_nodes);
     state_.alloc(sizeof(TreeState));
@@ -496,7 +567,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     tile_smem_lpf_ = smem_lpf;
     set_hist_smem_limit((int)tile_smem_);
     set_hist_lpf_smem_limit((int)tile_smem_lpf_);
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
     last_enabled_ = en;
     tiles_valid_ = true;
 }
@@ -543,7 +614,7 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.chunk_off = chunk_off_.as<uint32_t>();
     a.dirflags = dirflags_.as<uint8_t>();
     a.node_left = node_left_.as<uint32_t>();
-    a.node_left_global = node_left_.as<uint32_t>();
+    a.node_left_global = comm_ ? node_left_global_.as<uint32_t>() : node_left_.as<uint32_t>();
     a.pred = pred_.as<float>();
     a.trec = trec_.as<TreeRec>();
     a.tcats = tcats_.as<uint32_t>();
@@ -603,12 +674,14 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d], s_));
         }
         launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
+        allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc, false);
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
         launch_split(a, max_m, s_);
         launch_decide(a, s_);
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
         launch_part_count(a, max_chunks, s_);
         launch_part_scan(a, s_);
+        allreduce_u32(node_left_.p, node_left_global_.p, max_m);
         launch_part_scatter(a, max_chunks, s_);
         launch_next_level(a, s_);
         cur = 1 - cur;
@@ -626,9 +699,9 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     FB_CUDA_CHECK(cudaMemcpyAsync(hst, state_.p, sizeof(TreeState), cudaMemcpyDeviceToHost, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(hrec, trec_.p, sizeof(TreeRec) * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
     if (has_cat_) FB_CUDA_CHECK(cudaMemcpyAsync(hcats, tcats_.p, 32ull * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
-    uint64_t lvl[32] = {0};
+    uint64_t* lvl = h_small_.as<uint64_t>() + 32;  // 16 levels x 16 bytes
     if (stats_) FB_CUDA_CHECK(cudaMemcpyAsync(lvl, level_stats_.p, 16 * 16, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
     FB_CUDA_CHECK(cudaEventElapsedTime(&last_tree_ms_, ev0_, ev1_));
     if (stats_) {
         uint64_t row_bytes = 0, bins = 0;  // enabled features of this tree
@@ -666,7 +739,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
 
 void TrainCtx::download_margins(float* out) {
     FB_CUDA_CHECK(cudaMemcpyAsync(out, pred_.p, n_ * 4, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
 }
 
 // ---- component calls (kernel parity tests) --------------------------------
@@ -701,7 +774,7 @@ void TrainCtx::histogram(const uint32_t* rows, uint64_t n_sel, const int64_t* fi
                       acc_prefix_[0].as<unsigned long long>(), n_sel);
     FB_CUDA_CHECK(cudaGetLastError());
     FB_CUDA_CHECK(cudaMemcpyAsync(out, hist_acc_.p, 16 * total_bins_, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
 }
 
 void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const double* scales,
@@ -735,7 +808,7 @@ void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const do
     uint32_t cats[8];
     FB_CUDA_CHECK(cudaMemcpyAsync(&r, node_best_.p, sizeof r, cudaMemcpyDeviceToHost, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(cats, node_cats_.p, 32, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
     std::memset(out, 0, sizeof *out);
     out->found = r.flags & 1u;
     if (!out->found) return;
@@ -782,7 +855,7 @@ void TrainCtx::partition(const uint32_t* rows, uint64_t n, uint32_t feat, uint32
     uint32_t nl = 0;
     FB_CUDA_CHECK(cudaMemcpyAsync(&nl, node_left_.p, 4, cudaMemcpyDeviceToHost, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(out_rows, rows_[1].p, n * 4, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    sync();
     *n_left = nl;
 }
 
@@ -962,6 +1035,12 @@ template <class F> fbgpu_status guard(fbgpu_ctx* ctx, F&& f) {
     } catch (const fbg::CudaError& e) {
         (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
         return FBGPU_ECUDA;
+    } catch (const fbg::TimeoutError& e) {
+        (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
+        return FBGPU_ETIMEOUT;
+    } catch (const fbg::NcclError& e) {
+        (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
+        return FBGPU_ENCCL;
     } catch (const std::exception& e) {
         (ctx ? ctx->impl.err : fbg::g_last_error) = e.what();
         return FBGPU_EINTERNAL;
@@ -1040,6 +1119,17 @@ fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t
 fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
                              int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left) {
     return guard(ctx, [&] { ctx->impl.partition(rows, n, feat, bin, missing_left, cats, out_rows, n_left); });
+}
+
+uint64_t fbgpu_launch_count(void) { return fbg::g_launches.load(std::memory_order_relaxed); }
+
+fbgpu_status fbgpu_nccl_unique_id(uint8_t* out) {
+    return guard(nullptr, [&] { fbg::nccl_unique_id(out); });
+}
+
+fbgpu_status fbgpu_ctx_set_comm(fbgpu_ctx* ctx, const uint8_t* unique_id, int32_t nranks, int32_t rank,
+                                uint32_t timeout_ms) {
+    return guard(ctx, [&] { ctx->impl.set_comm(unique_id, nranks, rank, timeout_ms); });
 }
 
 int32_t fbgpu_exact_exp_available(const char** why) {

@@ -9,6 +9,8 @@
 
 #include <cuda_runtime.h>
 
+#include "nccl_loader.h"
+
 #include "../../include/fbgpu.h"
 #include "explain_kernels.cuh"
 #include "train_kernels.cuh"
@@ -87,6 +89,16 @@ class TrainCtx {
                       int64_t* sum_out);
 
     void build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
+
+    // Row sharding over several GPUs: one context per GPU, one NCCL
+    // communicator per context (ranks in the same order on every GPU).
+    void set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t timeout_ms);
+    int nranks() const { return nranks_; }
+    // Waits for the training stream; when sharded, a bounded poll that aborts
+    // the communicator if a peer stops answering.
+    void sync();
+    // Max over ranks of non-negative host doubles (bit patterns order like the values).
+    void allreduce_max_host(double* v, int count);
     void download_margins(float* out);
 
     void histogram(const uint32_t* rows, uint64_t n_sel, const int64_t* fixed, int64_t* out);
@@ -156,6 +168,11 @@ class TrainCtx {
     DevMem label_, weight_, pred_, gpair_f32_, host_exp_, fixed_;
     DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double)
     DevMem exptab_;  // host-expf exception table (fexp.h), empty when unverified
+    std::unique_ptr<NcclComm> comm_;
+    int nranks_ = 1, rank_ = 0;
+    DevMem node_left_global_, comm_scratch_;
+    void allreduce_u64(void* buf, size_t count, bool max_op);
+    void allreduce_u32(const void* src, void* dst, size_t count);
     uint32_t exp_probes_ = 0;
     bool has_weight_ = false;
     PinnedMem h_stage_;
@@ -167,6 +184,7 @@ class TrainCtx {
     DevMem dirflags_, hist_acc_, hist_[2], feat_best_, feat_cats_, node_best_, node_cats_, split_, chunk_left_, chunk_off_,
         node_left_, trec_, tcats_, state_;
     PinnedMem h_tree_;
+    PinnedMem h_small_;  // 512 B of pinned readback: no pageable copy waits behind a collective
     float last_tree_ms_ = 0.0f;
     bool stats_ = false;
     cudaEvent_t hev_[32] = {};

@@ -251,6 +251,38 @@ void build_blocks(Dataset& d, const float* X, int nth) {
 
 int threads(int32_t nthread) { return nthread > 0 ? nthread : omp_get_max_threads(); }
 
+// Cuts of the listed features (numeric: weighted quantile sketch; categorical:
+// 1..max code, sketch.rs:128-136 + categorical.rs:264-266).  Features are
+// independent, so row shards on several ranks may each sketch some features.
+std::vector<std::vector<float>> sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_bin,
+                                                const float* w, const uint8_t* cat,
+                                                const std::vector<uint32_t>& feats, int nth) {
+    std::vector<std::vector<float>> per(feats.size());
+    std::string bad;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nth)
+    for (int64_t i = 0; i < (int64_t)feats.size(); i++) {
+        const uint32_t f = feats[i];
+        if (cat && cat[f]) {
+            int32_t max_code = -1;
+            for (uint64_t r = 0; r < n; r++) {
+                const float v = X[r * F + f];
+                if (std::isnan(v)) continue;
+                if (v < 0.0f || v > 65533.0f || v != std::trunc(v)) {
+#pragma omp critical
+                    bad = "categorical feature #" + std::to_string(f) + " contains an invalid category code";
+                    break;
+                }
+                max_code = std::max(max_code, (int32_t)v);
+            }
+            for (int32_t k = 1; k <= std::max(max_code, 0); k++) per[i].push_back((float)k);
+        } else {
+            per[i] = feature_cuts(X, n, F, f, max_bin, w);
+        }
+    }
+    if (!bad.empty()) throw InputError(bad);
+    return per;
+}
+
 Dataset* dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
                             const uint8_t* categorical, int32_t nthread) {
     if (n == 0 || F == 0) throw InputError("training data must have at least one row and one feature");
@@ -264,28 +296,9 @@ Dataset* dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32_t max
     d->cat.assign(F, 0);
     if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
     const int nth = threads(nthread);
-    std::vector<std::vector<float>> per(F);
-    std::string bad;
-#pragma omp parallel for schedule(dynamic, 1) num_threads(nth)
-    for (int64_t f = 0; f < (int64_t)F; f++) {
-        if (d->cat[f]) {  // sketch.rs:128-136 + categorical.rs:264-266
-            int32_t max_code = -1;
-            for (uint64_t r = 0; r < n; r++) {
-                const float v = X[r * F + f];
-                if (std::isnan(v)) continue;
-                if (v < 0.0f || v > 65533.0f || v != std::trunc(v)) {
-#pragma omp critical
-                    bad = "categorical feature #" + std::to_string(f) + " contains an invalid category code";
-                    break;
-                }
-                max_code = std::max(max_code, (int32_t)v);
-            }
-            for (int32_t k = 1; k <= std::max(max_code, 0); k++) per[f].push_back((float)k);
-        } else {
-            per[f] = feature_cuts(X, n, F, (uint32_t)f, max_bin, w);
-        }
-    }
-    if (!bad.empty()) throw InputError(bad);
+    std::vector<uint32_t> all(F);
+    for (uint32_t f = 0; f < F; f++) all[f] = f;
+    std::vector<std::vector<float>> per = sketch_features(X, n, F, max_bin, w, d->cat.data(), all, nth);
     d->offsets.push_back(0);
     for (uint32_t f = 0; f < F; f++) {
         d->cuts.insert(d->cuts.end(), per[f].begin(), per[f].end());
@@ -517,8 +530,32 @@ std::vector<uint8_t> sample_features(uint32_t nf, float rate, uint64_t seed, uin
 }
 
 // ---------------------------------------------------------------- booster
+// objective.rs:41-61 label mean (FitInterceptGlmLike), the base_score when
+// none is given: a sequential f64 sum in row order.
+float label_mean(const float* y, const float* w, uint64_t n) {
+    if (!w) {
+        double acc = 0.0, nn = (double)n;
+        for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / nn;
+        return (float)acc;
+    }
+    double sw = 0.0, acc = 0.0;
+    for (uint64_t i = 0; i < n; i++) sw = sw + (double)w[i];
+    if (sw <= 0.0) return 0.5f;
+    for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / sw * (double)w[i];
+    return (float)acc;
+}
+
+// Row shard of a booster trained on several GPUs (one process per GPU).
+struct ShardInfo {
+    uint64_t row_offset = 0, n_global = 0;
+    const uint8_t* nccl_id = nullptr;
+    int nranks = 1, rank = 0;
+    uint32_t timeout_ms = 0;
+};
+
 struct Booster {
     const Dataset* d = nullptr;
+    uint64_t row0 = 0, n_global = 0;  // global index of row 0, rows over all ranks
     fb_params p{};
     std::vector<int8_t> mono;
     std::vector<float> labels, weights, grad_w;
@@ -532,8 +569,15 @@ struct Booster {
     std::vector<float> o_gain, o_leaf, o_hess;
 };
 
-Booster* booster_create(const Dataset* d, const float* y, const float* w, const fb_params* pp) {
+Booster* booster_create(const Dataset* d, const float* y, const float* w, const fb_params* pp,
+                        const ShardInfo& sh = ShardInfo{}) {
     const fb_params& p = *pp;
+    if (sh.nranks > 1) {
+        if (std::isnan(p.base_score))
+            throw InputError("a row-sharded booster needs base_score (the label mean over all rows)");
+        if (!sh.nccl_id) throw InputError("a row-sharded booster needs an NCCL unique id");
+        if (sh.row_offset + d->n > sh.n_global) throw InputError("row_offset + rows exceeds n_rows_global");
+    }
     if (p.objective != 0 && p.objective != 1) throw InputError("objective must be reg:squarederror or binary:logistic");
     if (p.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     if (!(p.subsample > 0.0f && p.subsample <= 1.0f)) throw InputError("subsample must be in (0, 1]");
@@ -548,6 +592,8 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     auto b = std::make_unique<Booster>();
     b->d = d;
     b->p = p;
+    b->row0 = sh.nranks > 1 ? sh.row_offset : 0;
+    b->n_global = sh.nranks > 1 ? sh.n_global : d->n;
     if (p.monotone) b->mono.assign(p.monotone, p.monotone + d->F);
     b->labels.assign(y, y + d->n);
     if (w) b->weights.assign(w, w + d->n);
@@ -563,22 +609,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     }
     // objective.rs:41-61 label mean (FitInterceptGlmLike) when base_score is not given
     float base = p.base_score;
-    if (std::isnan(base)) {
-        const uint64_t n = d->n;
-        if (!w) {
-            double acc = 0.0, nn = (double)n;
-            for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / nn;
-            base = (float)acc;
-        } else {
-            double sw = 0.0, acc = 0.0;
-            for (uint64_t i = 0; i < n; i++) sw = sw + (double)w[i];
-            if (sw <= 0.0) base = 0.5f;
-            else {
-                for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / sw * (double)w[i];
-                base = (float)acc;
-            }
-        }
-    }
+    if (std::isnan(base)) base = label_mean(y, w, d->n);
     if (p.objective == 1 && !(base >= 0.0f && base <= 1.0f))
         throw InputError("logistic base_score is a probability and must be in [0, 1]");
     b->model.base_score = base;
@@ -591,12 +622,14 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     cfg.device = p.device;
     cfg.n_features = d->F;
     cfg.n_rows = d->n;
-    cfg.n_rows_global = d->n;
+    cfg.n_rows_global = b->n_global;
+    cfg.row_offset = b->row0;
     cfg.max_depth = p.max_depth;
     cfg.max_leaves = p.max_leaves;
     cfg.gpu_math = p.gpu_math;
     if (const char* e = std::getenv("FBGPU_HIST_SMEM")) cfg.hist_smem_bytes = (uint32_t)std::atoi(e);
     b->ctx.reset(new fbg::TrainCtx(cfg));
+    if (sh.nranks > 1) b->ctx->set_comm(sh.nccl_id, sh.nranks, sh.rank, sh.timeout_ms);
     std::vector<uint32_t> nb(d->F);
     for (uint32_t f = 0; f < d->F; f++) nb[f] = d->n_bins(f);
     b->ctx->set_features(nb.data(), d->width.data(), d->cat.data());
@@ -646,12 +679,16 @@ void booster_round(Booster& b) {
             float g = s - y[i];
             float h = hh < 1e-16f ? 1e-16f : hh;
             if (gw) { g = g * gw[i]; h = h * gw[i]; }
-            if (!row_selected((uint64_t)i, th, p.seed, round)) { g = 0.0f; h = 0.0f; }
+            if (!row_selected(b.row0 + (uint64_t)i, th, p.seed, round)) { g = 0.0f; h = 0.0f; }
             mg = std::max(mg, std::isfinite(g) ? std::fabs((double)g) : HUGE_VAL);
             mh = std::max(mh, std::isfinite(h) ? std::fabs((double)h) : HUGE_VAL);
         }
+        double m2[2] = {mg, mh};
+        ctx.allreduce_max_host(m2, 2);  // global bounds when row-sharded
+        mg = m2[0];
+        mh = m2[1];
         if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
-        const double sc[2] = {fbg::pow2_scale_host(mg, n), fbg::pow2_scale_host(mh, n)};
+        const double sc[2] = {fbg::pow2_scale_host(mg, b.n_global), fbg::pow2_scale_host(mh, b.n_global)};
         ctx.round_from_exp(1, e, th, p.seed, round, sc);
     }
     auto t1 = std::chrono::steady_clock::now();
@@ -760,6 +797,37 @@ fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const f
     }, nullptr);
 }
 
+int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                           const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
+                           float* cuts, uint32_t* counts, uint64_t cap) {
+    return fbe::guarded([&]() -> int64_t {
+        if (n == 0 || F == 0) throw fbe::InputError("training data must have at least one row and one feature");
+        if (max_bin == 0 || max_bin > 65535) throw fbe::InputError("max_bin must be in 1..=65535");
+        if (w)
+            for (uint64_t i = 0; i < n; i++)
+                if (!std::isfinite(w[i]) || w[i] < 0.0f)
+                    throw fbe::InputError("sample weights must be finite and non-negative");
+        std::vector<uint32_t> fs(feats, feats + n_feats);
+        for (uint32_t f : fs)
+            if (f >= F) throw fbe::InputError("feature index out of range");
+        auto per = fbe::sketch_features(X, n, F, max_bin, w, categorical, fs, fbe::threads(nthread));
+        uint64_t total = 0;
+        for (size_t i = 0; i < per.size(); i++) total += per[i].size();
+        if (total > cap) throw fbe::InputError("cuts capacity is too small: need " + std::to_string(total));
+        uint64_t at = 0;
+        for (size_t i = 0; i < per.size(); i++) {
+            counts[i] = (uint32_t)per[i].size();
+            std::memcpy(cuts + at, per[i].data(), 4 * per[i].size());
+            at += per[i].size();
+        }
+        return (int64_t)total;
+    }, (int64_t)-1);
+}
+
+float fb_label_mean(const float* labels, const float* weights, uint64_t n) {
+    return fbe::label_mean(labels, weights, n);
+}
+
 void fb_dataset_free(fb_dataset* d) { delete d; }
 uint64_t fb_dataset_rows(const fb_dataset* h) { return h->d->n; }
 
@@ -788,6 +856,25 @@ fb_booster* fb_booster_create(const fb_dataset* d, const float* labels, const fl
     }, nullptr);
 }
 
+fb_booster* fb_booster_create_sharded(const fb_dataset* shard, const float* labels, const float* weights,
+                                      const fb_params* p, uint64_t row_offset, uint64_t n_rows_global,
+                                      const uint8_t* nccl_id, int32_t nranks, int32_t rank, uint32_t timeout_ms) {
+    return fbe::guarded([&]() -> fb_booster* {
+        fbe::ShardInfo sh;
+        sh.row_offset = row_offset;
+        sh.n_global = n_rows_global;
+        sh.nccl_id = nccl_id;
+        sh.nranks = nranks;
+        sh.rank = rank;
+        sh.timeout_ms = timeout_ms;
+        if (nranks < 1 || rank < 0 || rank >= nranks) throw fbe::InputError("invalid rank / world size");
+        auto* out = new fb_booster();
+        std::unique_ptr<fb_booster> guard_out(out);
+        out->b.reset(fbe::booster_create(shard->d.get(), labels, weights, p, sh));
+        return guard_out.release();
+    }, nullptr);
+}
+
 void fb_booster_free(fb_booster* b) { delete b; }
 
 int32_t fb_booster_update(fb_booster* h, uint32_t n_rounds) {
@@ -798,12 +885,12 @@ int32_t fb_booster_update(fb_booster* h, uint32_t n_rounds) {
         cudaEvent_t e0, e1;
         FB_CUDA_CHECK(cudaEventCreate(&e0));
         FB_CUDA_CHECK(cudaEventCreate(&e1));
-        FB_CUDA_CHECK(cudaStreamSynchronize(b->ctx->stream()));
+        b->ctx->sync();
         auto t0 = std::chrono::steady_clock::now();
         FB_CUDA_CHECK(cudaEventRecord(e0, b->ctx->stream()));
         for (uint32_t r = 0; r < n_rounds; r++) fbe::booster_round(*b);
         FB_CUDA_CHECK(cudaEventRecord(e1, b->ctx->stream()));
-        FB_CUDA_CHECK(cudaEventSynchronize(e1));
+        b->ctx->sync();
         b->t_wall = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
         float ms = 0.0f;
         FB_CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));

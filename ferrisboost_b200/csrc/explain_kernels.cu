@@ -193,6 +193,7 @@ void launch_predict(const DevModel& m, const float* X, uint64_t n, float base_ma
     if (n == 0) return;
     uint64_t blocks = (n + 255) / 256;
     if (blocks > 148ull * 64) blocks = 148ull * 64;
+    count_launch();
     k_predict<<<(unsigned)blocks, 256, 0, s>>>(m, X, n, base_margin, out);
 }
 
@@ -206,6 +207,7 @@ void launch_shap(const DevModel& m, const float* X, uint64_t n, float bias, floa
                  float* path, float* tc, cudaStream_t s) {
     if (n == 0) return;
     const uint64_t T = shap_threads(n);
+    count_launch();
     k_shap<<<(unsigned)(T / 128), 128, 0, s>>>(m, X, n, bias, root_mean, out, path, tc);
 }
 

@@ -5,6 +5,9 @@
 
 namespace fbg {
 
+// Counts this library's kernel launches (fbgpu_launch_count).
+void count_launch();
+
 constexpr int kShapPoints = 8;     // explain.rs:32 POINTS
 constexpr int kMaxShapDepth = 14;  // types.rs:424 MAX_DEPTH_LIMIT
 

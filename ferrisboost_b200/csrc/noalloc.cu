@@ -115,6 +115,7 @@ extern "C" fbgpu_status fbgpu_partition_noalloc(const void* bins, uint32_t strid
         if (cats)
             for (int w = 0; w < 8; w++) ia.cats[w] = cats[w];
         ia.floc = FeatLoc{static_cast<const uint8_t*>(bins), stride, byte_off, width, width == 2 ? 65535u : 255u};
+        count_launch();
         k_noalloc_init<<<1, 32, 0, s>>>(scr, ia);
         LevelArgs a{};
         a.st = &scr->st;

@@ -1053,20 +1053,24 @@ static unsigned grad_grid(uint32_t n) {
     unsigned b = (n + 255) / 256;
     return b < 148u * 8u ? (b ? b : 1u) : 148u * 8u;
 }
-void launch_mask_max(const GradArgs& a, cudaStream_t s) { k_mask_max<<<grad_grid(a.n), 256, 0, s>>>(a); }
+void launch_mask_max(const GradArgs& a, cudaStream_t s) { count_launch(); k_mask_max<<<grad_grid(a.n), 256, 0, s>>>(a); }
 void launch_gradient_max(const GradArgs& a, int mode, cudaStream_t s) {
+    count_launch();
     k_gradient_max<<<grad_grid(a.n), 256, 0, s>>>(a, mode);
 }
 void launch_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint32_t count, uint32_t* out,
                          cudaStream_t s) {
+    count_launch();
     k_expf_emulate<<<148 * 8, 256, 0, s>>>(tab, probes, begin, count, out);
 }
 void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s) {
+    count_launch();
     k_gradient_quantize_exp<<<grad_grid(a.n), 256, 0, s>>>(a);
 }
-void launch_quantize(const GradArgs& a, cudaStream_t s) { k_quantize<<<grad_grid(a.n), 256, 0, s>>>(a); }
+void launch_quantize(const GradArgs& a, cudaStream_t s) { count_launch(); k_quantize<<<grad_grid(a.n), 256, 0, s>>>(a); }
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
                           cudaStream_t s) {
+    count_launch();
     k_device_scales<<<1, 1, 0, s>>>(maxbits, n_rows, scales);
 }
 void set_hist_smem_limit(int bytes) {
@@ -1079,6 +1083,7 @@ void launch_hist(int width, const TileDesc* tiles, uint32_t n_tiles, const TileF
                  unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s) {
     if (n_tiles == 0) return;
     dim3 grid(grid_x, n_tiles);
+    count_launch();
     if (width == 2)
         k_hist<2><<<grid, kHistThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix, st,
                                                    hist_acc, slot_pairs);
@@ -1096,6 +1101,7 @@ void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const T
                      unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s) {
     if (n_tiles == 0) return;
     dim3 grid(grid_x, n_tiles);
+    count_launch();
     if (width == 2)
         k_hist_lpf<2><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix,
                                                           st, hist_acc, slot_pairs);
@@ -1105,30 +1111,38 @@ void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const T
 }
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
     dim3 grid(max_m, a.n_features);
+    count_launch();
     k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    count_launch();
     k_split_node<<<max_m, 32, 0, s>>>(a);
 }
-void launch_decide(const LevelArgs& a, cudaStream_t s) { k_decide<<<1, 1024, 0, s>>>(a); }
+void launch_decide(const LevelArgs& a, cudaStream_t s) { count_launch(); k_decide<<<1, 1024, 0, s>>>(a); }
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    count_launch();
     k_part_count<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
-void launch_part_scan(const LevelArgs& a, cudaStream_t s) { k_part_scan<<<1, 1024, 0, s>>>(a); }
+void launch_part_scan(const LevelArgs& a, cudaStream_t s) { count_launch(); k_part_scan<<<1, 1024, 0, s>>>(a); }
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    count_launch();
     k_part_scatter<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
-void launch_next_level(const LevelArgs& a, cudaStream_t s) { k_next_level<<<1, 1024, 0, s>>>(a); }
+void launch_next_level(const LevelArgs& a, cudaStream_t s) { count_launch(); k_next_level<<<1, 1024, 0, s>>>(a); }
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    count_launch();
     k_leaf_final<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
 void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
                       cudaStream_t s) {
+    count_launch();
     k_tree_init<<<1, 32, 0, s>>>(a, n_local, n_global, root_sum);
 }
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s) {
+    count_launch();
     k_iota<<<grad_grid(n), 256, 0, s>>>(rows, n);
 }
 void launch_transpose(int width, const uint8_t* src, uint8_t* dst, uint32_t n_rows, uint32_t n_feats,
                       uint32_t stride, uint64_t row0, cudaStream_t s) {
+    count_launch();
     if (width == 2) k_transpose_block<2><<<148 * 16, 256, 0, s>>>(src, dst, n_rows, n_feats, stride, row0);
     else k_transpose_block<1><<<148 * 16, 256, 0, s>>>(src, dst, n_rows, n_feats, stride, row0);
 }

@@ -1,0 +1,171 @@
+"""Row-sharded training on the GPUs of one node, one process per GPU.
+
+Each rank holds a contiguous range of the rows (``shard_range``).  The ranks
+split the per-feature quantile sketch between them and exchange the cuts, bin
+only their own rows, and grow every tree together: the library runs NCCL
+collectives on its training stream for the gradient bounds and root sum of
+each round and for the accumulated node histograms and per-node row counts of
+each level.  The histograms are sums of integers modulo 2^64, so in exact mode
+every rank ends with the model a single GPU trains on all the rows, byte for
+byte.
+
+The reference trains on one GPU only; its communication trait has a
+single-process ``Local`` implementation (src/training/comm.rs:10-41).  This
+module is the multi-GPU replacement for that trait.
+
+    torchrun --nproc-per-node 8 my_train.py   # in my_train.py:
+    torch.distributed.init_process_group("gloo")
+    model = ferrisboost_b200.distributed.train(params, X, label=y, num_boost_round=100)
+
+``torch.distributed`` (any backend; gloo is enough) only carries the NCCL id,
+the cuts and the label mean between the ranks before training.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Any, Mapping, Sequence
+
+import numpy as np
+
+from . import (Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params, lib)
+
+__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train"]
+
+
+def shard_range(n_rows: int, world_size: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) of ``rank``: contiguous, sizes differing by at most one."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError(f"invalid rank {rank} of world size {world_size}")
+    base, extra = divmod(int(n_rows), world_size)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (made on rank 0, sent to the others)."""
+    buf = np.zeros(128, dtype=np.uint8)
+    st = lib().fbgpu_nccl_unique_id(_lib.ptr(buf, C.c_uint8))
+    if st:
+        raise RuntimeError(lib().fbgpu_last_error(None).decode())
+    return buf.tobytes()
+
+
+def sketch_features(X: np.ndarray, feats: Sequence[int], max_bin: int, weight=None, categorical=None,
+                    nthread: int = 0) -> list[np.ndarray]:
+    """Cuts of the listed features (the sketch of ``Dataset``, feature by feature)."""
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    fs = np.ascontiguousarray(feats, dtype=np.uint32)
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    cat = None if categorical is None else np.ascontiguousarray(categorical, dtype=np.uint8)
+    cap = sum(65534 if cat is not None and cat[f] else max(max_bin, 1) for f in fs) + 1
+    cuts = np.zeros(cap, dtype=np.float32)
+    counts = np.zeros(max(len(fs), 1), dtype=np.uint32)
+    n = lib().fb_sketch_features(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin, _lib.ptr(w, C.c_float),
+                                 _lib.ptr(cat, C.c_uint8), _lib.ptr(fs, C.c_uint32), len(fs), nthread,
+                                 _lib.ptr(cuts, C.c_float), _lib.ptr(counts, C.c_uint32), cap)
+    if n < 0:
+        raise ValueError(_err())
+    out, at = [], 0
+    for i in range(len(fs)):
+        out.append(cuts[at:at + counts[i]].copy())
+        at += int(counts[i])
+    return out
+
+
+def sketch_cuts(X: np.ndarray, max_bin: int, weight=None, categorical=None, nthread: int = 0, group=None):
+    """(cut values, F+1 offsets) of all rows of X, the features sketched
+    round-robin by the ranks of ``group`` and all-gathered.  Equal to the
+    cuts one process sketches alone."""
+    import torch.distributed as dist
+    F = X.shape[1]
+    rank, world = _rank_world(group)
+    mine = list(range(rank, F, world))
+    local = sketch_features(X, mine, max_bin, weight, categorical, nthread)
+    gathered: list = [None] * world
+    if world > 1:
+        dist.all_gather_object(gathered, (mine, [c.tobytes() for c in local]), group=group)
+    else:
+        gathered = [(mine, [c.tobytes() for c in local])]
+    per = [None] * F
+    for feats, cuts in gathered:
+        for f, c in zip(feats, cuts):
+            per[f] = np.frombuffer(c, dtype=np.float32)
+    off = np.zeros(F + 1, dtype=np.uint32)
+    off[1:] = np.cumsum([len(c) for c in per])
+    vals = np.concatenate(per) if off[-1] else np.zeros(0, np.float32)
+    return vals.astype(np.float32), off
+
+
+def _rank_world(group=None) -> tuple[int, int]:
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+
+
+def _broadcast(obj, group=None):
+    import torch.distributed as dist
+    box = [obj]
+    dist.broadcast_object_list(box, src=0, group=group)
+    return box[0]
+
+
+def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
+          feature_types: Sequence[str] | None = None, group=None, timeout_s: float = 120.0,
+          return_booster: bool = False):
+    """``ferrisboost_b200.train`` over all ranks of ``group`` (an initialised
+    ``torch.distributed`` process group; one process per GPU).
+
+    Every rank passes the whole data set (as each reads the same file); rank
+    r bins and trains rows ``shard_range(n, world, r)`` on ``cuda:LOCAL_RANK``
+    (unless ``params["device"]`` names one).  Returns the model, identical on
+    every rank (or the booster with ``return_booster``).  Collective waits
+    give up after ``timeout_s`` with a RuntimeError on the ranks still waiting.
+    """
+    rank, world = _rank_world(group)
+    params = dict(params)
+    if params.get("device") in (None, "cuda", "gpu"):
+        params["device"] = f"cuda:{int(os.environ.get('LOCAL_RANK', rank))}"
+    if not params.get("nthread"):
+        local = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+        params["nthread"] = max(1, len(os.sched_getaffinity(0)) // max(local, 1))
+    p = _normalize_params(params, num_boost_round)
+    if label is None:
+        raise ValueError("label is required for array input")
+    X = _as_matrix(data, p["missing"])
+    n, F = X.shape
+    y = np.ascontiguousarray(label, dtype=np.float32)
+    if y.shape != (n,):
+        raise ValueError(f"label has shape {y.shape}, expected ({n},)")
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    if world == 1:
+        from . import train as train_one
+        return train_one(params, X, label=y, num_boost_round=num_boost_round, weight=w, feature_types=feature_types)
+    if n < world:  # the same on every rank: all raise before any collective
+        raise ValueError(f"{n} rows cannot be sharded over {world} ranks")
+    cat = _feature_flags(feature_types, F)
+    cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group)
+    lo, hi = shard_range(n, world, rank)
+    base = p["base_score"]
+    if base is None:
+        base = float(lib().fb_label_mean(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), n))
+    nid = None
+    if rank == 0:  # a failure on rank 0 is sent to every rank, which all raise
+        try:
+            nid = nccl_unique_id()
+        except RuntimeError as e:
+            nid = "error: " + str(e)
+    nid = _broadcast(nid, group)
+    if isinstance(nid, str):
+        raise RuntimeError(f"rank 0 could not create an NCCL id ({nid})")
+    ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts)
+    shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
+                  timeout_ms=int(max(1.0, timeout_s) * 1000))
+    b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)
+    b.update(num_boost_round)
+    if return_booster:
+        return b
+    m = b.model()
+    m.params = p
+    return m

@@ -61,6 +61,20 @@ fb_dataset* fb_dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32
  * DenseSource::with_cuts, src/source/dense.rs:215-235). */
 fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const float* cuts, const uint32_t* offsets,
                                  const uint8_t* categorical, int32_t nthread);
+/* Cuts of the listed features only, with the sketch of fb_dataset_from_dense
+ * (features are sketched independently, so the ranks of a row-sharded run
+ * can split the features between them and exchange the cuts).  The cuts of
+ * feats[i] are written back to back into `cuts`, their count into counts[i].
+ * Returns the total, or -1 (fb_last_error) when it exceeds `cap` or an input
+ * is invalid.  Replaces the per-feature part of DenseSource::new_weighted
+ * (src/source/dense.rs:136-209, sketch.rs:128-302). */
+int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* weights,
+                           const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
+                           float* cuts, uint32_t* counts, uint64_t cap);
+/* The base_score estimated from the labels when none is given: the label mean
+ * (weighted when weights != NULL), summed in f64 in row order
+ * (src/objective.rs:41-61). */
+float fb_label_mean(const float* labels, const float* weights, uint64_t n);
 void fb_dataset_free(fb_dataset* d);
 uint64_t fb_dataset_rows(const fb_dataset* d);
 /* Cuts: copies up to cap values; returns the total.  offsets: F+1 entries. */
@@ -71,6 +85,18 @@ int32_t fb_dataset_column(const fb_dataset* d, uint32_t f, uint16_t* out);
 /* A booster trains every row of the dataset on one device (p->device).  It
  * allocates all device memory at creation and none during training. */
 fb_booster* fb_booster_create(const fb_dataset* d, const float* labels, const float* weights, const fb_params* p);
+/* A booster over one row shard of a run on `nranks` GPUs, one process per
+ * GPU: the dataset holds rows [row_offset, row_offset + rows) of
+ * n_rows_global, binned with the cuts of the whole data; labels and weights
+ * are those rows'.  p->base_score must be set (fb_label_mean of all labels).
+ * Every rank passes the same parameters and the same NCCL unique id
+ * (fbgpu_nccl_unique_id on rank 0) and calls update with the same counts; each
+ * then holds the same model, byte for byte the single-GPU model in exact
+ * mode.  Collective waits give up after timeout_ms (0 = 120000).  No
+ * counterpart in the reference (single GPU only). */
+fb_booster* fb_booster_create_sharded(const fb_dataset* shard, const float* labels, const float* weights,
+                                      const fb_params* p, uint64_t row_offset, uint64_t n_rows_global,
+                                      const uint8_t* nccl_id, int32_t nranks, int32_t rank, uint32_t timeout_ms);
 void fb_booster_free(fb_booster* b);
 /* Train n_rounds more trees. */
 int32_t fb_booster_update(fb_booster* b, uint32_t n_rounds);

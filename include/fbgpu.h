@@ -109,11 +109,40 @@ typedef struct fbgpu_split {
 const char* fbgpu_last_error(const fbgpu_ctx* ctx);
 int32_t fbgpu_device_count(void);
 
+/* Number of kernels this library has launched in this process (all devices
+ * and threads; library kernels such as NCCL's are not counted).  A
+ * diagnostic with no counterpart in the reference. */
+uint64_t fbgpu_launch_count(void);
+
 /* ---------------------------------------------------------- training context */
 
 /* Replaces GpuTrainCtx::new_with_shape (src/backend/mod.rs:245-255). */
 fbgpu_status fbgpu_ctx_create(const fbgpu_config* cfg, fbgpu_ctx** out);
 void fbgpu_ctx_destroy(fbgpu_ctx* ctx);
+
+/* ------------------------------------------------------------ row sharding */
+
+/* Size of an NCCL unique id (NCCL_UNIQUE_ID_BYTES). */
+#define FBGPU_NCCL_ID_BYTES 128
+
+/* Creates an NCCL unique id on the calling rank (rank 0 makes one and sends
+ * its bytes to the other ranks by the caller's own means).  No counterpart in
+ * the reference, whose communication trait has only the single-process
+ * `Local` implementation (src/training/comm.rs:10-41); this replaces that
+ * trait for row sharding. */
+fbgpu_status fbgpu_nccl_unique_id(uint8_t* out_id);
+
+/* Joins `ctx` to a communicator of `nranks` contexts, one per GPU and
+ * process, each holding a contiguous row range (fbgpu_config.row_offset,
+ * n_rows_global).  Collectives then run on the context's stream: the max of
+ * the gradient bounds and the sum of the root gradient per round, the sum of
+ * the accumulated node histograms and of the per-node left counts per level.
+ * Every rank must make the same calls in the same order.  Waits on the
+ * communicator poll for at most `timeout_ms` (0 = 120000); past that the
+ * communicator is aborted and calls return FBGPU_ETIMEOUT, later ones
+ * FBGPU_ENCCL.  nranks == 1 is a no-op. */
+fbgpu_status fbgpu_ctx_set_comm(fbgpu_ctx* ctx, const uint8_t* unique_id, int32_t nranks, int32_t rank,
+                                uint32_t timeout_ms);
 
 /* Feature metadata: bins per feature (cuts + 1), storage width in bytes
  * (bins.rs:58-66 BinWidth::for_feature) and categorical flags (may be NULL).
