@@ -18,8 +18,6 @@ namespace fbg {
 
 namespace {
 thread_local std::string g_last_error;
-
-uint32_t ceil_div(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
 }  // namespace
 
 void noalloc_set_error(const char* msg) { g_last_error = msg; }
@@ -447,8 +445,8 @@ void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed,
     }
 }
 
-void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
-    if (max_depth == buf_depth_ && max_leaves == buf_leaves_) return;
+void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide) {
+    if (max_depth == buf_depth_ && max_leaves == buf_leaves_ && lossguide == buf_lossguide_) return;
     uint64_t lvl = 1ull << max_depth;                 // nodes of the deepest level
     uint64_t split_nodes = max_depth ? (1ull << (max_depth - 1)) : 1;  // deepest split level
     uint64_t acc = max_depth >= 2 ? (1ull << (max_depth - 2)) : 1;
@@ -459,6 +457,14 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
     }
     uint64_t tree_nodes = (2ull << max_depth) - 1;
     if (max_leaves) tree_nodes = std::min<uint64_t>(tree_nodes, 2ull * max_leaves + 1);
+    if (lossguide) {
+        // best-first waves (lossguide.cu): up to max_leaves expansions per wave,
+        // two evaluated children each; hist_[0] is the histogram pool
+        lvl = 2ull * max_leaves + 2;
+        split_nodes = 2ull * max_leaves + 4;
+        acc = (uint64_t)max_leaves + 1;
+        tree_nodes = 2ull * max_leaves + 1;
+    }
     max_level_nodes_ = (uint32_t)lvl;
     max_split_nodes_ = (uint32_t)split_nodes;
     max_acc_ = (uint32_t)acc;
@@ -471,7 +477,7 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
         acc_list_[i].alloc(4 * (lvl + 1));
         acc_prefix_[i].alloc(8 * (lvl + 2));
         chunk_prefix_[i].alloc(4 * (lvl + 2));
-        hist_[i].alloc(16 * tb * split_nodes);
+        hist_[i].alloc(lossguide && i == 1 ? 16 : 16 * tb * split_nodes);
     }
     hist_acc_.alloc(16 * tb * acc);
     feat_best_.alloc(sizeof(SplitRec) * split_nodes * F_);
@@ -491,6 +497,7 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves) {
     h_tree_.reserve(sizeof(TreeRec) * tree_nodes + 32 * tree_nodes + sizeof(TreeState));
     buf_depth_ = max_depth;
     buf_leaves_ = max_leaves;
+    buf_lossguide_ = lossguide;
 }
 
 // Histogram tiles: the enabled features of every block, grouped per kernel.
@@ -621,12 +628,61 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     return a;
 }
 
+// Lossguide grows the same tree as depthwise growth when max_leaves cannot
+// bind (0, or at least 2^max_depth leaves): every leaf with a split is popped
+// before the budget runs out (lossguide.rs:555-700), so only the node order
+// differs.
+bool lossguide_is_levelwise(const fbgpu_tree_params& tp) {
+    return tp.max_leaves == 0 || tp.max_depth >= 31 || tp.max_leaves >= (1u << tp.max_depth);
+}
+
+// Best-first pop order over a grown tree (lossguide.rs:46-53 ordering: larger
+// gain by f32 total order first, then the lower node id; children get ids
+// in pop order, left then right).
+void lossguide_order(const TreeRec* rec, uint32_t nn, std::vector<uint32_t>& old_of_new,
+                     std::vector<uint32_t>& new_of_old) {
+    struct E {
+        int32_t key;   // f32 gain as a total-order integer
+        uint32_t id;   // new id
+        uint32_t old;  // depthwise id
+    };
+    auto total_key = [](float g) {
+        int32_t i;
+        std::memcpy(&i, &g, 4);
+        return i ^ (int32_t)(((uint32_t)(i >> 31)) >> 1);
+    };
+    auto less = [](const E& a, const E& b) { return a.key != b.key ? a.key < b.key : a.id > b.id; };
+    old_of_new.assign(nn, 0);
+    new_of_old.assign(nn, 0);
+    uint32_t next = 1;
+    std::vector<E> heap;
+    if (!(rec[0].flags & 1u)) heap.push_back({total_key(rec[0].gain), 0, 0});
+    while (!heap.empty()) {
+        std::pop_heap(heap.begin(), heap.end(), less);
+        const E e = heap.back();
+        heap.pop_back();
+        const int32_t kids[2] = {rec[e.old].left, rec[e.old].right};
+        for (int32_t c : kids) {
+            if (c < 0 || (uint32_t)c >= nn || next >= nn) throw std::runtime_error("device tree is malformed");
+            new_of_old[c] = next;
+            old_of_new[next] = (uint32_t)c;
+            if (!(rec[c].flags & 1u)) {
+                heap.push_back({total_key(rec[c].gain), next, (uint32_t)c});
+                std::push_heap(heap.begin(), heap.end(), less);
+            }
+            next++;
+        }
+    }
+    if (next != nn) throw std::runtime_error("device tree is malformed");
+}
+
 void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out) {
     ensure_features();
     if (tp.max_depth > 14) throw InputError("max_depth must be in 0..=14");
-    if (tp.grow_policy != 0) throw InputError("grow_policy=lossguide is not available on the device path yet");
+    const bool lossguide = tp.grow_policy != 0;
     if (n_ == 0) throw InputError("training data must have at least one row");
-    ensure_tree_buffers(tp.max_depth, tp.max_leaves);
+    const bool best_first = lossguide && !lossguide_is_levelwise(tp);
+    ensure_tree_buffers(tp.max_depth, tp.max_leaves, best_first);
     plan_tiles(enabled);
     if (tp.monotone) {
         std::vector<int8_t> m(tp.monotone, tp.monotone + F_);
@@ -634,6 +690,11 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             FB_CUDA_CHECK(cudaMemcpyAsync(d_mono_.p, m.data(), F_, cudaMemcpyHostToDevice, s_));
             last_mono_ = m;
         }
+    }
+    if (best_first) {
+        ensure_lossguide_buffers(tp.max_leaves);
+        build_tree_lossguide(tp, enabled, out);
+        return;
     }
     LevelArgs a = level_args(tp);
     const uint32_t maxd = tp.max_depth;
@@ -721,10 +782,15 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     if (!out) return;
     if (out->capacity < nn) throw InputError("fbgpu_tree_out capacity is smaller than the tree");
     out->n_nodes = nn;
+    // lossguide: the same splits, numbered in best-first pop order
+    std::vector<uint32_t> old_of_new, new_of_old;
+    if (lossguide) lossguide_order(hrec, nn, old_of_new, new_of_old);
     for (uint32_t i = 0; i < nn; i++) {
-        const TreeRec& r = hrec[i];
-        if (out->left) out->left[i] = r.left;
-        if (out->right) out->right[i] = r.right;
+        const uint32_t o = lossguide ? old_of_new[i] : i;
+        const TreeRec& r = hrec[o];
+        const uint32_t ci = o;  // categories stay with their node
+        if (out->left) out->left[i] = r.left < 0 || !lossguide ? r.left : (int32_t)new_of_old[r.left];
+        if (out->right) out->right[i] = r.right < 0 || !lossguide ? r.right : (int32_t)new_of_old[r.right];
         if (out->feat) out->feat[i] = r.feat;
         if (out->bin) out->bin[i] = r.bin;
         if (out->gain) out->gain[i] = r.gain;
@@ -732,7 +798,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         if (out->hess) out->hess[i] = r.hess;
         if (out->flags) out->flags[i] = r.flags;
         if (out->cats) {
-            for (int w = 0; w < 8; w++) out->cats[i * 8 + w] = (r.flags & 4u) ? hcats[i * 8 + w] : 0u;
+            for (int w = 0; w < 8; w++) out->cats[i * 8 + w] = (r.flags & 4u) ? hcats[ci * 8 + w] : 0u;
         }
     }
 }

@@ -17,6 +17,8 @@
 
 namespace fbg {
 
+inline uint32_t ceil_div(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
+
 struct CudaError : std::runtime_error {
     CudaError(cudaError_t e, const char* what, const char* file, int line)
         : std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(e) + " in " + what + " (" + file + ":" +
@@ -137,7 +139,9 @@ class TrainCtx {
     void plan_tiles(const uint8_t* enabled);
     void launch_histograms(const uint32_t* rows, const NodeInfo* nodes, const uint32_t* acc_list,
                            const unsigned long long* acc_prefix, uint64_t rows_upper);
-    void ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves);
+    void ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide = false);
+    void ensure_lossguide_buffers(uint32_t max_leaves);
+    void build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
     LevelArgs level_args(const fbgpu_tree_params& tp) const;
     GradArgs grad_args() const;
 
@@ -179,6 +183,12 @@ class TrainCtx {
 
     // tree buffers
     uint32_t buf_depth_ = 0xffffffffu, buf_leaves_ = 0xffffffffu;
+    bool buf_lossguide_ = false;
+    // best-first growth (lossguide.cu): slot table, wave descriptors, final leaves
+    DevMem lg_slots_, lg_slot_hist_, lg_slot_best_, lg_slot_cats_, lg_wave_, lg_wave_out_, lg_eval_slot_,
+        lg_node_hist_, lg_final_slot_, lg_final_value_;
+    PinnedMem h_lg_;
+    uint32_t lg_leaves_ = 0xffffffffu, lg_kmax_ = 0, lg_slot_cap_ = 0, lg_hist_cap_ = 0;
     uint32_t max_level_nodes_ = 0, max_split_nodes_ = 0, max_acc_ = 0, max_tree_nodes_ = 0, max_chunks_ = 0;
     DevMem rows_[2], nodes_[2], acc_list_[2], acc_prefix_[2], chunk_prefix_[2];
     DevMem dirflags_, hist_acc_, hist_[2], feat_best_, feat_cats_, node_best_, node_cats_, split_, chunk_left_, chunk_off_,

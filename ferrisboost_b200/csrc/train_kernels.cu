@@ -88,15 +88,6 @@ __device__ __forceinline__ unsigned long long block_excl_scan_u64(unsigned long 
     return base + incl - v;
 }
 
-// Quantizer reciprocals of this round from the device scales (exact: the
-// scales are powers of two).
-__device__ __forceinline__ ScoreParams load_sp(const LevelArgs& a) {
-    ScoreParams sp = a.sp;
-    sp.inv_g = __ddiv_rn(1.0, a.scales[0]);
-    sp.inv_h = __ddiv_rn(1.0, a.scales[1]);
-    return sp;
-}
-
 // Largest j in [0, n) with prefix[j] <= x (prefix ascending, prefix[0] <= x).
 template <class T>
 __device__ __forceinline__ uint32_t find_segment(const T* prefix, uint32_t n, T x) {
@@ -492,6 +483,7 @@ struct SplitSmem {
     SplitRec best[kSplitThreads];
     float w[kSplitThreads];
     uint32_t idx[kSplitThreads];
+    Pair x[kSplitThreads];       // categorical: the finished histogram (parent and child may share memory)
     uint32_t set_words[8];
 };
 
@@ -531,7 +523,9 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
     const Pair* acc = a.hist_acc + (unsigned long long)ni.acc_slot * a.slot_pairs + off;
     const Pair* par = ni.parent_slot >= 0 ? a.hist_prev + (unsigned long long)ni.parent_slot * a.slot_pairs + off
                                           : nullptr;
-    Pair* h = a.hist_cur + (unsigned long long)node * a.slot_pairs + off;
+    // the subtracted child may be written over its parent's histogram (lossguide pool):
+    // every bin is read once, by the thread that writes it
+    Pair* h = a.hist_cur + (unsigned long long)(a.node_hist ? a.node_hist[node] : node) * a.slot_pairs + off;
     const bool keep_hist = !a.last_level;
     const Pair sum = ni.sum;
     const ScoreParams sp = load_sp(a);
@@ -579,6 +573,7 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
         if (t < n) w = xgb_weight(to_f64(x.g, sp.inv_g), to_f64(x.h, sp.inv_h), sp);
         s.w[t] = w;
         s.idx[t] = t;
+        s.x[t] = x;
         __syncthreads();
         for (uint32_t size = 2; size <= kSplitThreads; size <<= 1) {
             for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
@@ -598,7 +593,7 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
             }
         }
         const uint32_t cat = s.idx[t];
-        Pair xs = t < n ? (par ? psub(par[cat], acc[cat]) : acc[cat]) : Pair{0, 0};
+        Pair xs = t < n ? s.x[cat] : Pair{0, 0};
         Pair tot;
         Pair excl = block_excl_scan_pair<kSplitThreads>(xs, s.warp_tot, tot);
         const uint32_t n_scan = min(a.max_cat_threshold, n);

@@ -104,7 +104,19 @@ struct LevelArgs {
     float* pred;
     TreeRec* trec;
     uint32_t* tcats;             // [tree node][8]
+    const uint32_t* node_hist;   // lossguide: histogram-pool slot of each node (null: level slots)
 };
+
+#ifdef __CUDACC__
+// Quantizer reciprocals of this round from the device scales (exact: the
+// scales are powers of two).
+__device__ __forceinline__ ScoreParams load_sp(const LevelArgs& a) {
+    ScoreParams sp = a.sp;
+    sp.inv_g = __ddiv_rn(1.0, a.scales[0]);
+    sp.inv_h = __ddiv_rn(1.0, a.scales[1]);
+    return sp;
+}
+#endif
 
 struct GradArgs {
     uint32_t n;               // rows on this rank

@@ -134,3 +134,78 @@ def test_json_is_valid_xgboost_schema():
     n = int(t["tree_param"]["num_nodes"])
     assert len(t["left_children"]) == n == len(t["split_conditions"])
     assert doc["learner"]["objective"]["name"] == "binary:logistic"
+
+
+def test_lossguide_known_answers_on_device(oracle):
+    from test_lossguide_oracle import BASE, known_answers
+
+    def train(x, y, **kw):
+        p = dict(BASE, **kw)
+        rounds = p.pop("n_rounds")
+        got = fb.train(p, x, label=y, num_boost_round=rounds).to_json()
+        assert got == oracle.train(x, y, **dict(BASE, **kw)).json()
+        return got
+
+    known_answers(train)
+
+
+LOSSGUIDE = [
+    # max_leaves cannot bind: the depthwise tree renumbered in pop order
+    dict(objective="reg:squarederror", grow_policy="lossguide", max_depth=6, max_leaves=255, eta=0.3, max_bin=256),
+    dict(objective="binary:logistic", grow_policy="lossguide", max_depth=5, max_leaves=0, eta=0.3, max_bin=64),
+    # binding leaf caps: best-first waves
+    dict(objective="binary:logistic", grow_policy="lossguide", max_depth=8, max_leaves=20, eta=0.2, max_bin=128),
+    dict(objective="reg:squarederror", grow_policy="lossguide", max_depth=14, max_leaves=63, eta=0.1, max_bin=1024,
+         min_child_weight=3.0, subsample=0.8, colsample_bytree=0.6, seed=5),
+    dict(objective="reg:squarederror", grow_policy="lossguide", max_depth=10, max_leaves=7, eta=0.5, max_bin=256,
+         gamma=0.5, reg_lambda=3.0),
+]
+
+
+@pytest.mark.parametrize("k", range(len(LOSSGUIDE)))
+def test_lossguide_models_byte_identical(oracle, k):
+    p = LOSSGUIDE[k]
+    X, y = _synthetic(30000, 20, seed=40 + k, missing=0.05)
+    if p["objective"] == "reg:squarederror":
+        y = (np.nan_to_num(X[:, 0]) * 2 + np.nan_to_num(X[:, 3]) ** 2 + np.nan_to_num(X[:, 5])).astype(np.float32)
+    m = fb.train(p, X, label=y, num_boost_round=10)
+    ref = oracle.train(X, y, n_rounds=10, **p)
+    assert m.to_json() == ref.json()
+    assert np.array_equal(m.predict(X, output_margin=True).view(np.uint32), ref.predict_margin(X).view(np.uint32))
+
+
+def test_lossguide_categorical_and_monotone_byte_identical(oracle):
+    # configs[3] shape at a small size: numeric features with NaN, 64-code
+    # categorical features (partition splits), a leaf cap that binds
+    rng = np.random.default_rng(8)
+    n = 40000
+    Xn = rng.standard_normal((n, 8)).astype(np.float32)
+    Xn[rng.random(Xn.shape) < 0.05] = np.nan
+    Xc = rng.integers(0, 64, (n, 4)).astype(np.float32)
+    X = np.concatenate([Xn, Xc], axis=1)
+    eff = rng.standard_normal((4, 64))
+    y = (sum(eff[j][Xc[:, j].astype(int)] for j in range(4)) + np.nan_to_num(Xn) @ rng.standard_normal(8)
+         + rng.normal(0, 0.5, n)).astype(np.float32)
+    ft = ["q"] * 8 + ["c"] * 4
+    cat = np.array([0] * 8 + [1] * 4, np.uint8)
+    p = dict(objective="reg:squarederror", grow_policy="lossguide", max_depth=12, max_leaves=31, eta=0.05,
+             max_bin=1024, monotone_constraints=[1, 0, -1, 0, 0, 0, 0, 0, 0, 0, 0, 0])
+    m = fb.train(p, X, label=y, num_boost_round=6, feature_types=ft)
+    ref = oracle.train(X, y, n_rounds=6, categorical=cat, **p)
+    assert m.to_json() == ref.json()
+    assert np.array_equal(m.predict(X, output_margin=True).view(np.uint32), ref.predict_margin(X).view(np.uint32))
+
+
+def test_lossguide_fast_mode_within_tolerance(oracle):
+    X, y = _synthetic(40000, 28, seed=23)
+    p = dict(objective="binary:logistic", grow_policy="lossguide", max_depth=10, max_leaves=40, eta=0.1)
+    fast = fb.train(dict(p, gpu_math="fast"), X, label=y, num_boost_round=15)
+    exact = oracle.train(X, y, n_rounds=15, **p)
+    a = fast.predict(X, output_margin=True).astype(np.float64)
+    b = exact.predict_margin(X).astype(np.float64)
+
+    def logloss(m):
+        pr = np.clip(1 / (1 + np.exp(-m)), 1e-15, 1 - 1e-15)
+        return -np.mean(y * np.log(pr) + (1 - y) * np.log(1 - pr))
+
+    assert abs(logloss(a) - logloss(b)) < 1e-4
