@@ -1,25 +1,30 @@
 """Benchmark: FerrisBoost training on B200, seconds per 100 boosting rounds.
 
-Workload (the config the metric is quoted on):
-11,000,000 rows x 28 f32 features ~ N(0,1) from seed 0, labels
+Default workload (the config the metric is quoted
+on): 11,000,000 rows x 28 f32 features ~ N(0,1) from seed 0, labels
 ~ Bernoulli(sigmoid(w.x + 0.5 x0 x1 - 0.3 x2^2)); binary:logistic,
 max_bin=256, depthwise max_depth=8, eta=0.1, gpu_math="exact".  A step is one
 boosting round over the resident quantized data.  Synthetic data of the
 config's shape stands in for HIGGS (not in this container).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--rows R]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config c0|c1|c2|c3|c3d14|c4] [--rows R] [--no-cpu]
 
 value: exact-mode s/100 rounds from CUDA events on the training stream, bins
 resident in HBM (gradients, glibc-exact expf reproduced on the device,
 quantization, the tree's levels and the margin update are all inside the
-interval).  e2e: the same metric through the public train() call from host
-arrays (sketch, binning, H2D of the bins and labels, K rounds, model JSON),
-normalised per 100 rounds.  N > 1 (torchrun, one process per GPU): rows are
-sharded over the ranks, the library's NCCL communicator all-reduces the
-per-level histograms; the total work is fixed (strong scaling) and times are
-the max over ranks.  cpu_baseline / --impl reference: the C++ restatement of
-the reference CPU engine (oracle/), all host threads, bounded sample of the
-same workload.
+interval).  e2e: 100 rounds through the public train() from host arrays
+(sketch, binning, H2D of the bins and labels, the rounds, model JSON), wall
+seconds.  N > 1 (torchrun, one process per GPU): rows are sharded over the
+ranks and the library's NCCL communicator all-reduces the per-level
+histograms; the total work is fixed (strong scaling) and times are the max
+over ranks.  cpu_baseline / --impl reference: the C++ restatement of the
+reference CPU engine (oracle/), all host threads, a bounded sample of the same
+workload.
+
+--config selects the other BASELINE configs (configs[0], [2], [3] and the
+max_depth 14 variant of [3], and [4]: TreeSHAP rows/s); they print the same
+JSON line for their own workload.
 """
 import argparse
 import json
@@ -36,6 +41,7 @@ sys.path.insert(0, ROOT)
 
 N_FEATURES = 28
 PARAMS = {"objective": "binary:logistic", "max_depth": 8, "eta": 0.1, "lambda": 1.0, "max_bin": 256}
+E2E_ROUNDS = 100
 
 
 def make_data(n, seed=0):
@@ -45,7 +51,59 @@ def make_data(n, seed=0):
     w = rng.standard_normal(N_FEATURES)
     z = X @ w + 0.5 * X[:, 0].astype(np.float64) * X[:, 1] - 0.3 * X[:, 2].astype(np.float64) ** 2
     y = (rng.random(n) < 1.0 / (1.0 + np.exp(-z))).astype(np.float32)
-    return X, y
+    return X, y, None
+
+
+def make_wide(n, seed=0, F=2000):
+    """Uniform(-1, 1) features, labels from 50 random features."""
+    rng = np.random.default_rng(seed)
+    X = rng.uniform(-1.0, 1.0, (n, F)).astype(np.float32)
+    idx = rng.choice(F, 50, replace=False)
+    beta = rng.standard_normal(50)
+    y = ((X[:, idx] @ beta + rng.normal(0.0, 0.1, n)) > 0).astype(np.float32)
+    return X, y, None
+
+
+def make_mixed(n, seed=0):
+    """80 N(0,1) features with 5 % NaN, 20 categorical features
+    with 64 codes; target = per-code effects + linear term (NaN as 0) + noise."""
+    rng = np.random.default_rng(seed)
+    X = np.empty((n, 100), dtype=np.float32)
+    X[:, :80] = rng.standard_normal((n, 80), dtype=np.float32)
+    codes = rng.integers(0, 64, (n, 20), dtype=np.int32)
+    eff = rng.standard_normal((20, 64))
+    w = rng.standard_normal(80).astype(np.float32)
+    y = (X[:, :80] @ w).astype(np.float64)
+    X[:, :80][rng.random((n, 80), dtype=np.float32) < 0.05] = np.nan
+    for j in range(20):
+        y += eff[j][codes[:, j]]
+    X[:, 80:] = codes
+    y += rng.normal(0.0, 0.5, n)
+    return X, y.astype(np.float32), ["q"] * 80 + ["c"] * 20
+
+
+CONFIGS = {
+    "c0": dict(make=make_data, rows=1_000_000,
+               params=dict(PARAMS, max_depth=6),
+               workload="configs[0] binary:logistic 1M x 28, depth 6, max_bin 256, eta 0.1, gpu_math exact"),
+    "c1": dict(make=make_data, rows=11_000_000, params=PARAMS,
+               workload="configs[1] binary:logistic 11M x 28, depth 8, max_bin 256, eta 0.1, gpu_math exact"),
+    "c2": dict(make=make_wide, rows=400_000,
+               params=dict(PARAMS, colsample_bytree=0.5),
+               workload="configs[2] binary:logistic 400k x 2000 Uniform(-1,1), depth 8, max_bin 256, "
+                        "colsample_bytree 0.5, eta 0.1, gpu_math exact"),
+    "c3": dict(make=make_mixed, rows=10_000_000,
+               params={"objective": "reg:squarederror", "grow_policy": "lossguide", "max_leaves": 255,
+                       "max_bin": 1024, "eta": 0.05, "max_depth": 6},
+               workload="configs[3] reg:squarederror 10M x (80 numeric, 5% NaN + 20 categorical x 64), "
+                        "lossguide max_leaves 255, max_depth 6 (default; the cap does not bind), max_bin 1024, "
+                        "eta 0.05, gpu_math exact"),
+    "c3d14": dict(make=make_mixed, rows=10_000_000,
+                  params={"objective": "reg:squarederror", "grow_policy": "lossguide", "max_leaves": 255,
+                          "max_bin": 1024, "eta": 0.05, "max_depth": 14},
+                  workload="configs[3] with max_depth 14: lossguide max_leaves 255 binds (best-first waves), "
+                           "10M x 100, max_bin 1024, eta 0.05, gpu_math exact"),
+}
 
 
 class ClockSampler:
@@ -64,9 +122,10 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            time.sleep(0.3)  # the first sample lands before the timed work starts
         except OSError:
             self.proc = None
         return self
@@ -98,33 +157,46 @@ def cpu_threads():
     return len(os.sched_getaffinity(0))
 
 
-def reference_rounds(X, y, rounds, warmup):
+def reference_rounds(X, y, params, rounds, warmup, feature_types=None):
     """Oracle (C++ restatement of the reference CPU engine) on the workload:
-    per-round wall seconds of rounds after `warmup`, all host threads."""
+    set-up seconds and per-round wall seconds of the rounds after `warmup`,
+    all host threads."""
     from oracle import RefCPU
     rc = RefCPU()
-    rc.train(X, y, n_rounds=warmup + rounds, nthread=0, **PARAMS)
+    kw = dict(params)
+    if feature_types is not None:
+        kw["categorical"] = np.array([t == "c" for t in feature_types], np.uint8)
+    rc.train(X, y, n_rounds=warmup + rounds, nthread=0, **kw)
     setup, per_round = rc.last_timing()
     return setup, per_round[warmup:]
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU engine (the oracle restatement) on the same
+    workload: rank 0 alone; `value` = mean round x 100, `e2e` = set-up +
+    100 rounds."""
     if rank != 0:
         return
-    X, y = make_data(args.rows)
-    setup, rs = reference_rounds(X, y, args.steps, args.warmup)
-    s100 = float(np.mean(rs)) * 100.0
+    cfg = CONFIGS[args.config]
+    n = args.rows or cfg["rows"]
+    X, y, ft = cfg["make"](n)
+    steps = min(args.steps, 10)  # bounded sample: at most 10 timed rounds
+    warm = min(args.warmup, 1)
+    setup, rs = reference_rounds(X, y, cfg["params"], steps, warm, ft)
+    mean = float(np.mean(rs))
     line = {
-        "metric": "train s/100 rounds", "value": round(s100, 4), "unit": "s/100 rounds", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * float(np.mean(rs)), 3),
+        "metric": "train s/100 rounds", "value": round(mean * 100.0, 4), "unit": "s/100 rounds", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * mean, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "configs[1] binary:logistic 11M x 28, depth 8, max_bin 256, eta 0.1",
-                   "rows": args.rows, "features": N_FEATURES},
-        "cpu_baseline": {"value": round(s100, 4), "unit": "s/100 rounds", "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{args.steps} timed rounds after {args.warmup} warm-up rounds on the full "
-                                   f"{args.rows}-row workload; setup {setup:.2f} s not included"},
-        "e2e": {"value": round(s100, 4), "unit": "s/100 rounds", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": cfg["workload"].replace(", gpu_math exact", ""), "rows": n,
+                   "features": int(X.shape[1])},
+        "cpu_baseline": {"value": round(mean * 100.0, 4), "unit": "s/100 rounds", "cores": cpu_threads(),
+                         "kind": "port",
+                         "sample": f"{steps} timed rounds after {warm} warm-up round(s) on the full {n}-row "
+                                   f"workload; sketch + quantize set-up {setup:.2f} s"},
+        "e2e": {"value": round(setup + mean * E2E_ROUNDS, 4), "unit": "s/100 rounds", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0, "includes": "set-up + 100 x the mean timed round"},
     }
     print(json.dumps(line), flush=True)
 
@@ -157,6 +229,15 @@ def _max_over_ranks(dist, v):
     return float(t.item())
 
 
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        peaks = {}
+    return float(peaks.get("hbm_gbs", 6650.0)), "measured" if "hbm_gbs" in peaks else "fallback"
+
+
 def run_ours(args, rank, world):
     import torch
     import ferrisboost_b200 as fb
@@ -166,28 +247,31 @@ def run_ours(args, rank, world):
     device = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(device)
     lib = _lib.load()
+    cfg = CONFIGS[args.config]
+    n = args.rows or cfg["rows"]
     t0 = time.perf_counter()
-    X, y = make_data(args.rows)
+    X, y, ft = cfg["make"](n)
     gen_s = time.perf_counter() - t0
-    p = dict(PARAMS, device=f"cuda:{device}")
-    n = args.rows
+    p = dict(cfg["params"], device=f"cuda:{device}")
+    F = int(X.shape[1])
     lo, hi = fbd.shard_range(n, world, rank)
 
     def train_public(params, rounds, booster=False):
         if world == 1:
             if booster:
-                ds = fb.Dataset(X, max_bin=params["max_bin"])
+                ds = fb.Dataset(X, max_bin=params["max_bin"], feature_types=ft)
                 b = fb.Booster(params, ds, y)
                 b.update(rounds)
                 return b
-            return fb.train(params, X, label=y, num_boost_round=rounds)
-        return fbd.train(params, X, label=y, num_boost_round=rounds, timeout_s=300, return_booster=booster)
+            return fb.train(params, X, label=y, num_boost_round=rounds, feature_types=ft)
+        return fbd.train(params, X, label=y, num_boost_round=rounds, feature_types=ft, timeout_s=300,
+                         return_booster=booster)
 
-    # e2e: the public train() from host arrays, K rounds (sketch, binning,
-    # uploads, K rounds, model); wall clock, max over ranks
+    # e2e: 100 rounds through the public train() from host arrays (sketch,
+    # binning, uploads, rounds, model JSON); wall clock, max over ranks
     _fence(dist)
     t0 = time.perf_counter()
-    m = train_public(p, args.steps)
+    m = train_public(p, E2E_ROUNDS)
     json_bytes = len(m.to_json())
     e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
     del m
@@ -198,50 +282,41 @@ def run_ours(args, rank, world):
     b = train_public(p, args.warmup, booster=True)
     setup_s = time.perf_counter() - t0
     b.set_stats(True)
-    _fence(dist)
-    l0 = lib.fbgpu_launch_count()
+    fast = train_public(dict(p, gpu_math="fast"), args.warmup, booster=True)
     with ClockSampler(device) as clk:
+        _fence(dist)
+        l0 = lib.fbgpu_launch_count()
         b.update(args.steps)
-    launches = lib.fbgpu_launch_count() - l0
-    _fence(dist)
+        launches = lib.fbgpu_launch_count() - l0
+        _fence(dist)
+        fast.update(args.steps)
+        _fence(dist)
     t = b.timing()
     dev_ms = _max_over_ranks(dist, t["device_ms"])
+    fast_ms = _max_over_ranks(dist, fast.timing()["device_ms"])
+    del fast
     ms_step = dev_ms / args.steps
     s100 = ms_step * 100.0 / 1000.0
 
-    fast = train_public(dict(p, gpu_math="fast"), args.warmup, booster=True)
-    _fence(dist)
-    fast.update(args.steps)
-    _fence(dist)
-    fast_ms = _max_over_ranks(dist, fast.timing()["device_ms"])
-    del fast
-
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
-    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    hbm_peak, peak_src = _peaks()
     hist_launches = max(t["hist_launches"], 1.0)
     hist_gbs = t["hist_bytes"] / (t["hist_ms"] / 1000.0) / 1e9 if t["hist_ms"] > 0 else None
-
     rows_local = hi - lo
-    bins_bytes = rows_local * 56  # 28 16-bit bins per row (max_bin 256 needs 257 bins + missing)
-    depth = PARAMS["max_depth"]
-    tree_readback = 32 * (2 ** (depth + 1)) + 64
+    depth = p.get("max_depth", 6)
+    leaves = p.get("max_leaves", 0) or 2 ** depth
+    tree_readback = 32 * min(2 ** (depth + 1), 2 * leaves + 1) + 64
+    bin_bytes = F * (2 if p["max_bin"] > 255 else 1)
     line = {
         "metric": "train s/100 rounds", "value": round(s100, 4), "unit": "s/100 rounds", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": "configs[1] binary:logistic 11M x 28, depth 8, max_bin 256, eta 0.1, gpu_math exact",
-                   "rows": n, "features": N_FEATURES, "parallelism": f"row shards x{world}",
-                   "l2": "inputs larger than L2 (bins 704 MB, gradients 176 MB)"},
-        "e2e": {"value": round(e2e_s / args.steps * 100.0, 4), "unit": "s/100 rounds",
-                "h2d_bytes_per_step": int((bins_bytes + 4 * rows_local) / args.steps),
-                "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / args.steps),
-                "includes": "sketch + binning + upload + K rounds + model JSON through the public train(); "
+        "config": {"workload": cfg["workload"], "rows": n, "features": F, "parallelism": f"row shards x{world}",
+                   "l2": "inputs larger than L2 (bin records and fixed-point gradients exceed 126 MB)"
+                   if n * 16 > 126e6 else "inputs smaller than L2"},
+        "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds",
+                "h2d_bytes_per_step": int((rows_local * (bin_bytes + 4)) / E2E_ROUNDS),
+                "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / E2E_ROUNDS),
+                "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "
                             "per-rank bytes; wall clock, max over ranks"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
@@ -256,12 +331,107 @@ def run_ours(args, rank, world):
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         csteps = 2
-        setup, rs = reference_rounds(X, y, csteps, 1)
+        setup, rs = reference_rounds(X, y, cfg["params"], csteps, 1, ft)
         line["cpu_baseline"] = {"value": round(float(np.mean(rs)) * 100, 4), "unit": "s/100 rounds",
                                 "cores": cpu_threads(), "kind": "port",
                                 "sample": f"{csteps} rounds after 1 warm-up round on the full {n}-row workload "
                                           f"(oracle C++ restatement, all host threads)"}
     del b
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_shap(args, rank, world):
+    """TreeSHAP and prediction of the 500-tree depth-8 configs[1]
+    model on 1M fresh N(0,1) rows (seed 1), rows sharded over the ranks."""
+    import torch
+    import ferrisboost_b200 as fb
+    from ferrisboost_b200 import distributed as fbd
+    from ferrisboost_b200 import _lib
+    dist = _dist(world)
+    device = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(device)
+    lib = _lib.load()
+    trees = 50 if args.rows else 500
+    Xtr, ytr, _ = make_data(args.rows or 11_000_000)
+    t0 = time.perf_counter()
+    model = fb.train(dict(PARAMS, device=f"cuda:{device}"), Xtr, label=ytr, num_boost_round=trees)
+    train_s = time.perf_counter() - t0
+    del Xtr, ytr
+    n = 1_000_000
+    Xe = np.random.default_rng(1).standard_normal((n, N_FEATURES), dtype=np.float32)
+    lo, hi = fbd.shard_range(n, world, rank)
+    Xs = np.ascontiguousarray(Xe[lo:hi])
+    # e2e: public predict(pred_contribs=True) from host rows, results on the host
+    model.predict(Xs[:1000], pred_contribs=True)
+    _fence(dist)
+    t0 = time.perf_counter()
+    phi = model.predict(Xs, pred_contribs=True)
+    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    t0 = time.perf_counter()
+    margin = model.predict(Xs, output_margin=True)
+    pred_e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    err = float(np.max(np.abs(phi.astype(np.float64).sum(axis=1) - margin.astype(np.float64))))
+    # device-resident: rows and outputs in HBM, CUDA events on the launching stream
+    xd = torch.from_numpy(Xs).cuda()
+    od = torch.empty((hi - lo, N_FEATURES + 1), dtype=torch.float32, device="cuda")
+    pd = torch.empty(hi - lo, dtype=torch.float32, device="cuda")
+    h = model.device_handle(device)
+    s = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        if lib.fbgpu_shap_device(h, xd.data_ptr(), hi - lo, od.data_ptr(), s.cuda_stream):
+            raise RuntimeError(lib.fbgpu_last_error(None).decode())
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    l0 = lib.fbgpu_launch_count()
+    with ClockSampler(device) as clk:
+        _fence(dist)
+        ev[0].record(s)
+        for _ in range(args.steps):
+            lib.fbgpu_shap_device(h, xd.data_ptr(), hi - lo, od.data_ptr(), s.cuda_stream)
+        ev[1].record(s)
+        ev[2].record(s)
+        for _ in range(args.steps):
+            lib.fbgpu_predict_device(h, xd.data_ptr(), hi - lo, pd.data_ptr(), s.cuda_stream)
+        ev[3].record(s)
+        _fence(dist)
+    launches = lib.fbgpu_launch_count() - l0
+    shap_ms = _max_over_ranks(dist, ev[0].elapsed_time(ev[1]) / args.steps)
+    pred_ms = _max_over_ranks(dist, ev[2].elapsed_time(ev[3]) / args.steps)
+    same = bool(np.array_equal(od.cpu().numpy(), phi))
+    line = {
+        "metric": "TreeSHAP rows/s", "value": round(n / (shap_ms / 1000.0), 1), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(shap_ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"configs[4] TreeSHAP of the {trees}-tree depth-8 configs[1] model on 1M N(0,1) "
+                               "rows (seed 1)", "rows": n, "trees": trees, "parallelism": f"row shards x{world}"},
+        "e2e": {"value": round(n / e2e_s, 1), "unit": "rows/s",
+                "h2d_bytes_per_step": int((hi - lo) * 4 * N_FEATURES),
+                "d2h_bytes_per_step": int((hi - lo) * 4 * (N_FEATURES + 1)),
+                "includes": "public Model.predict(pred_contribs=True) from host rows"},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "breakdown": {"predict_rows_per_s": round(n / (pred_ms / 1000.0), 1),
+                      "predict_e2e_rows_per_s": round(n / pred_e2e_s, 1),
+                      "max_abs_rowsum_minus_margin": err, "device_equals_public": same,
+                      "train_s_for_model": round(train_s, 2)},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import RefCPU
+        rc = RefCPU()
+        Xs_tr, ys_tr, _ = make_data(200_000)
+        ref = rc.train(Xs_tr, ys_tr, n_rounds=20, nthread=0, **PARAMS)
+        rows = Xe[:2000]
+        ref.shap(rows[:100])
+        t0 = time.perf_counter()
+        ref.shap(rows)
+        cpu_s = time.perf_counter() - t0
+        rps = len(rows) / cpu_s * 20.0 / trees
+        line["cpu_baseline"] = {"value": round(rps, 1), "unit": "rows/s", "cores": cpu_threads(), "kind": "port",
+                                "sample": f"oracle TreeSHAP of 2000 rows with a 20-tree depth-8 model (200k "
+                                          f"training rows), scaled linearly to {trees} trees"}
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -275,7 +445,8 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--rows", type=int, default=11_000_000)
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["c4"])
+    ap.add_argument("--rows", type=int, default=0, help="override the config's row count (smaller runs)")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -289,7 +460,14 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
+        if args.config == "c4":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference arm times training configs; "
+                                  "configs[4] TreeSHAP is timed as cpu_baseline of --config c4"}))
+            return
         run_reference(args, rank, world)
+    elif args.config == "c4":
+        run_shap(args, rank, world)
     else:
         run_ours(args, rank, world)
 

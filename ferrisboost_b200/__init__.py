@@ -361,6 +361,14 @@ class Model:
             return d
         return int(str(d).split(":", 1)[1])
 
+    def device_handle(self, device=None):
+        """The model's device copy (an include/fbgpu.h ``fbgpu_model*``) for
+        fbgpu_predict_device / fbgpu_shap_device on rows already in HBM."""
+        h = lib().fb_model_device(self._h, self._device(device))
+        if not h:
+            raise RuntimeError(_err())
+        return h
+
     def to_json(self) -> bytes:
         n = lib().fb_model_json(self._h, None, 0)
         buf = C.create_string_buffer(n)

@@ -130,6 +130,7 @@ SIGNATURES = {
     "fb_model_tree": (C.c_int64, [P, C.c_uint32, i32p, i32p, u32p, f32p, u8p, f32p, u8p, f32p, f32p, u32p]),
     "fb_model_predict": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
     "fb_model_shap": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
+    "fb_model_device": (P, [P, C.c_int32]),
 }
 
 _lib = None

@@ -159,6 +159,19 @@ void TrainCtx::allreduce_max_host(double* v, int count) {
     std::memcpy(v, h, 8ull * count);
 }
 
+// The root gradient sum of a round, over all ranks.  Unless a caller wants it
+// now, it rides along with the root's histogram allreduce (one collective
+// fewer per round): build_tree appends it to that buffer.
+void TrainCtx::reduce_root_sum(bool now) {
+    if (!comm_) return;
+    if (now) {
+        allreduce_u64(sums_.p, 2, false);
+        root_pending_ = false;
+    } else {
+        root_pending_ = true;
+    }
+}
+
 void TrainCtx::sync() {
     if (comm_) comm_->sync(s_);
     else FB_CUDA_CHECK(cudaStreamSynchronize(s_));
@@ -376,7 +389,7 @@ void TrainCtx::upload_and_quantize(const float* gpair, uint64_t th, uint64_t see
     sc[1] = pow2_scale_host(mh, cfg_.n_rows_global);
     FB_CUDA_CHECK(cudaMemcpyAsync(sums_.as<unsigned long long>() + 4, sc, 16, cudaMemcpyHostToDevice, s_));
     launch_quantize(a, s_);
-    allreduce_u64(sums_.p, 2, false);
+    reduce_root_sum(sum_out != nullptr);
     if (scales_out) { scales_out[0] = sc[0]; scales_out[1] = sc[1]; }
     int64_t* hs = h_small_.as<int64_t>() + 4;
     FB_CUDA_CHECK(cudaMemcpyAsync(hs, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
@@ -403,7 +416,7 @@ void TrainCtx::round_from_exp(int objective, const float* host_exp, uint64_t th,
     a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
     a.objective = objective;
     launch_gradient_quantize_exp(a, s_);
-    allreduce_u64(sums_.p, 2, false);
+    reduce_root_sum(false);
 }
 
 void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
@@ -434,7 +447,7 @@ void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed,
         FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
     }
     launch_quantize(a, s_);
-    allreduce_u64(sums_.p, 2, false);
+    reduce_root_sum(sum_out != nullptr);
     if (scales_out || sum_out) {
         unsigned long long* hs = h_small_.as<unsigned long long>() + 4;
         FB_CUDA_CHECK(cudaMemcpyAsync(hs, dscales, 16, cudaMemcpyDeviceToHost, s_));
@@ -479,7 +492,7 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
         chunk_prefix_[i].alloc(4 * (lvl + 2));
         hist_[i].alloc(lossguide && i == 1 ? 16 : 16 * tb * split_nodes);
     }
-    hist_acc_.alloc(16 * tb * acc);
+    hist_acc_.alloc(16 * tb * acc + 16);  // + the root sum riding on the root's allreduce
     feat_best_.alloc(sizeof(SplitRec) * split_nodes * F_);
     feat_cats_.alloc(32 * split_nodes * F_);
     node_best_.alloc(sizeof(SplitRec) * split_nodes);
@@ -621,7 +634,9 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.chunk_off = chunk_off_.as<uint32_t>();
     a.dirflags = dirflags_.as<uint8_t>();
     a.node_left = node_left_.as<uint32_t>();
-    a.node_left_global = comm_ ? node_left_global_.as<uint32_t>() : node_left_.as<uint32_t>();
+    // sharded: the accumulated child is chosen by global hessian sums, so no
+    // per-level count allreduce is needed (the choice never changes the model)
+    a.node_left_global = comm_ ? nullptr : node_left_.as<uint32_t>();
     a.pred = pred_.as<float>();
     a.trec = trec_.as<TreeRec>();
     a.tcats = tcats_.as<uint32_t>();
@@ -706,6 +721,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     a.acc_prefix = acc_prefix_[0].as<unsigned long long>();
     a.chunk_prefix = chunk_prefix_[0].as<uint32_t>();
     a.rows_cur = rows_[0].as<uint32_t>();
+    if (root_pending_ && maxd == 0) reduce_root_sum(true);
     launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
     for (uint32_t d = 0; d < maxd; d++) {
         const uint32_t max_m = (uint32_t)std::min<uint64_t>(1ull << d, max_level_nodes_);
@@ -734,15 +750,25 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
                                           reinterpret_cast<uint8_t*>(state_.p) + 8, 16, cudaMemcpyDeviceToDevice, s_));
             FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d], s_));
         }
+        const bool root_rides = d == 0 && root_pending_;
+        if (root_rides)
+            FB_CUDA_CHECK(cudaMemcpyAsync(hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, sums_.p, 16,
+                                          cudaMemcpyDeviceToDevice, s_));
         launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
-        allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc, false);
+        allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc + (root_rides ? 2 : 0), false);
+        if (root_rides) {
+            FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, 16,
+                                          cudaMemcpyDeviceToDevice, s_));
+            // the root again, now with the global sum (same spans and state)
+            launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
+            root_pending_ = false;
+        }
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
         launch_split(a, max_m, s_);
         launch_decide(a, s_);
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
         launch_part_count(a, max_chunks, s_);
         launch_part_scan(a, s_);
-        allreduce_u32(node_left_.p, node_left_global_.p, max_m);
         launch_part_scatter(a, max_chunks, s_);
         launch_next_level(a, s_);
         cur = 1 - cur;
@@ -1084,10 +1110,6 @@ using fbg::TrainCtx;
 struct fbgpu_ctx {
     TrainCtx impl;
     explicit fbgpu_ctx(const fbgpu_config& c) : impl(c) {}
-};
-struct fbgpu_model {
-    ExplainModel impl;
-    template <class... A> explicit fbgpu_model(A&&... a) : impl(std::forward<A>(a)...) {}
 };
 
 namespace {

@@ -5,6 +5,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -177,6 +178,8 @@ class TrainCtx {
     DevMem node_left_global_, comm_scratch_;
     void allreduce_u64(void* buf, size_t count, bool max_op);
     void allreduce_u32(const void* src, void* dst, size_t count);
+    void reduce_root_sum(bool now);
+    bool root_pending_ = false;  // sharded: this round's root sum is still rank-local
     uint32_t exp_probes_ = 0;
     bool has_weight_ = false;
     PinnedMem h_stage_;
@@ -236,3 +239,9 @@ void make_shap_rule(float* nodes, float* weights);
 double pow2_scale_host(double max_abs, uint64_t n_rows);
 
 }  // namespace fbg
+
+// The C ABI's explanation-model handle (include/fbgpu.h fbgpu_model).
+struct fbgpu_model {
+    fbg::ExplainModel impl;
+    template <class... A> explicit fbgpu_model(A&&... a) : impl(std::forward<A>(a)...) {}
+};

@@ -331,7 +331,7 @@ struct Model {
     uint32_t n_features = 0;
     float scale_pos_weight = 1.0f;
     std::vector<uint8_t> feature_types;
-    std::unique_ptr<fbg::ExplainModel> dev;
+    std::unique_ptr<fbgpu_model> dev;  // device copy for prediction / SHAP
     int dev_device = -1;
     size_t dev_trees = 0;
 };
@@ -467,7 +467,7 @@ std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order 
 }
 
 fbg::ExplainModel& device_model(Model& m, int device) {
-    if (m.dev && m.dev_device == device && m.dev_trees == m.trees.size()) return *m.dev;
+    if (m.dev && m.dev_device == device && m.dev_trees == m.trees.size()) return m.dev->impl;
     std::vector<uint32_t> off{0}, feat, coff, clen, words;
     std::vector<int32_t> left, right;
     std::vector<float> val, hess;
@@ -483,12 +483,12 @@ fbg::ExplainModel& device_model(Model& m, int device) {
         }
         off.push_back((uint32_t)left.size());
     }
-    m.dev.reset(new fbg::ExplainModel(device, m.n_features, (uint32_t)m.trees.size(), off.data(), left.data(),
-                                      right.data(), feat.data(), val.data(), flags.data(), hess.data(), coff.data(),
-                                      clen.data(), words.data(), words.size(), base_margin(m.objective, m.base_score)));
+    m.dev.reset(new fbgpu_model(device, m.n_features, (uint32_t)m.trees.size(), off.data(), left.data(),
+                                right.data(), feat.data(), val.data(), flags.data(), hess.data(), coff.data(),
+                                clen.data(), words.data(), words.size(), base_margin(m.objective, m.base_score)));
     m.dev_device = device;
     m.dev_trees = m.trees.size();
-    return *m.dev;
+    return m.dev->impl;
 }
 
 // ---------------------------------------------------------------- sampling
@@ -980,6 +980,13 @@ int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, in
         fbe::device_model(*m, device).predict_host(X, n, out);
         return 0;
     }, 1);
+}
+
+fbgpu_model* fb_model_device(fb_model* m, int32_t device) {
+    return fbe::guarded([&]() -> fbgpu_model* {
+        fbe::device_model(*m, device);
+        return m->dev.get();
+    }, nullptr);
 }
 
 int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {

@@ -191,7 +191,8 @@ __global__ void __launch_bounds__(1024) k_wave_children(LevelArgs a, LgArgs g) {
         const NodeInfo ni = a.nodes[k];
         const SplitRec b = g.slot_best[we.slot];
         const uint32_t nl = a.node_left[k], nr = ni.len - nl;
-        const uint32_t nlg = a.node_left_global[k], nrg = ni.len_global - nlg;
+        const uint32_t nlg = a.node_left_global ? a.node_left_global[k] : 0u;
+        const uint32_t nrg = a.node_left_global ? ni.len_global - nlg : 0u;
         const double lg = to_f64(b.left.g, sp.inv_g), lh = to_f64(b.left.h, sp.inv_h);
         const double rg = to_f64(b.right.g, sp.inv_g), rh = to_f64(b.right.h, sp.inv_h);
         const float wl = apply_bounds(xgb_weight(lg, lh, sp), ni.lower, ni.upper);
@@ -204,7 +205,8 @@ __global__ void __launch_bounds__(1024) k_wave_children(LevelArgs a, LgArgs g) {
         L.start = ni.start; L.len = nl; L.len_global = nlg; L.sum = b.left; L.lower = llo; L.upper = lhi;
         R.start = ni.start + nl; R.len = nr; R.len_global = nrg; R.sum = b.right; R.lower = rlo; R.upper = rhi;
         L.tree_id = R.tree_id = -1;
-        const uint32_t small = nlg <= nrg ? 0u : 1u;
+        // by rows; row-sharded: by the children's global hessian sums
+        const uint32_t small = a.node_left_global ? (nlg <= nrg ? 0u : 1u) : (b.left.h <= b.right.h ? 0u : 1u);
         WaveOut o;
         o.lv = __fmul_rn(wl, sp.eta);
         o.rv = __fmul_rn(wr, sp.eta);
@@ -371,8 +373,20 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
     auto evaluate = [&](uint32_t n_acc, uint32_t m) {
         FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, 16ull * a.slot_pairs * n_acc, s_));
         a.nodes = eval_nodes;
+        const bool root_rides = root_pending_;  // only at the root: the round's sum rides along
+        if (root_rides)
+            FB_CUDA_CHECK(cudaMemcpyAsync(hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, sums_.p, 16,
+                                          cudaMemcpyDeviceToDevice, s_));
         launch_histograms(a.rows_cur, eval_nodes, a.acc_list, a.acc_prefix, n_);
-        allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * n_acc, false);
+        allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * n_acc + (root_rides ? 2 : 0), false);
+        if (root_rides) {
+            FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, 16,
+                                          cudaMemcpyDeviceToDevice, s_));
+            launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
+            count_launch();
+            k_lg_root<<<1, 32, 0, s_>>>(a, g);
+            root_pending_ = false;
+        }
         launch_split(a, m, s_);
         count_launch();
         k_wave_store<<<ceil_div(m, 256), 256, 0, s_>>>(a, g);
@@ -400,6 +414,10 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
     count_launch();
     k_lg_root<<<1, 32, 0, s_>>>(a, g);
     const bool root_only = max_depth == 0 || max_leaves == 1;
+    if (root_only && root_pending_) {
+        reduce_root_sum(true);
+        launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
+    }
     if (!root_only) evaluate(1, 1);
     FB_CUDA_CHECK(cudaMemcpyAsync(h_root, trec_.p, sizeof(TreeRec), cudaMemcpyDeviceToHost, s_));
     sync();
@@ -474,7 +492,6 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
             const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + k;
             launch_part_count(a, max_chunks, s_);
             launch_part_scan(a, s_);
-            allreduce_u32(node_left_.p, node_left_global_.p, k);
             launch_part_scatter(a, max_chunks, s_);
             count_launch();
             k_wave_copy_back<<<max_chunks, kPartThreads, 0, s_>>>(a);

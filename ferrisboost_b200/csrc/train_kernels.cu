@@ -928,8 +928,9 @@ __global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
 }
 
 // Next level's node table, accumulate list and chunk table (one CTA).  The
-// smaller child (by rows over all ranks; training/mod.rs:4478-4482) is
-// accumulated, the larger one is its parent minus the smaller one.
+// smaller child (by rows, training/mod.rs:4478-4482; by hessian sum over all
+// ranks when row-sharded) is accumulated, the larger one is its parent minus
+// the smaller one.  Which one is accumulated never changes the histograms.
 __global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
     __shared__ unsigned long long wt64[32];
     __shared__ uint32_t wt[32];
@@ -941,12 +942,19 @@ __global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
         const uint32_t k = (uint32_t)sd.child_slot >> 1;
         const NodeInfo ni = a.nodes[i];
         const uint32_t nl = a.node_left[i], nr = ni.len - nl;
-        const uint32_t nlg = a.node_left_global[i], nrg = ni.len_global - nlg;
         NodeInfo& L = a.next_nodes[2 * k];
         NodeInfo& R = a.next_nodes[2 * k + 1];
-        L.start = ni.start; L.len = nl; L.len_global = nlg;
-        R.start = ni.start + nl; R.len = nr; R.len_global = nrg;
-        const uint32_t small = nlg <= nrg ? 0u : 1u;
+        L.start = ni.start; L.len = nl;
+        R.start = ni.start + nl; R.len = nr;
+        uint32_t small;
+        if (a.node_left_global) {
+            const uint32_t nlg = a.node_left_global[i], nrg = ni.len_global - nlg;
+            L.len_global = nlg; R.len_global = nrg;
+            small = nlg <= nrg ? 0u : 1u;
+        } else {  // row-sharded: by the children's global hessian sums
+            L.len_global = R.len_global = 0;
+            small = L.sum.h <= R.sum.h ? 0u : 1u;
+        }
         L.acc_slot = (int32_t)k; R.acc_slot = (int32_t)k;
         L.parent_slot = small == 0 ? -1 : (int32_t)i;
         R.parent_slot = small == 1 ? -1 : (int32_t)i;

@@ -127,6 +127,10 @@ int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* rig
                       uint8_t* default_left, float* leaf, uint8_t* is_leaf, float* gain, float* hess, uint32_t* cats);
 /* Raw margins of host rows, computed on the device. */
 int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, int32_t device);
+/* The model's device copy on `device` as an include/fbgpu.h handle (owned by
+ * the model, valid until the model is freed or gains trees), for
+ * fbgpu_predict_device / fbgpu_shap_device on device-resident rows. */
+struct fbgpu_model* fb_model_device(fb_model* m, int32_t device);
 /* SHAP contributions n x (F+1) on the device. */
 int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device);
 
