@@ -126,6 +126,38 @@ def test_predict_and_shap_match_oracle(oracle):
     np.testing.assert_allclose(phi.sum(axis=1), ref.predict_margin(Xt), atol=2e-4)
 
 
+def test_shap_kernels_against_oracle(oracle, monkeypatch):
+    # default kernel: the CPU engine's f32 order, bit for bit; FBGPU_SHAP=lanes:
+    # one lane per quadrature point with precomputed reciprocals, within 1e-5
+    X, y = _synthetic(8000, 12, seed=6, missing=0.03)
+    p = dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=64)
+    ref = oracle.train(X, y, n_rounds=8, **p)
+    Xt, _ = _synthetic(1000, 12, seed=78, missing=0.03)
+    m = fb.train(p, X, label=y, num_boost_round=8)
+    assert np.array_equal(m.predict(Xt, pred_contribs=True).view(np.uint32), ref.shap(Xt).view(np.uint32))
+    monkeypatch.setenv("FBGPU_SHAP", "lanes")
+    lanes = fb.train(p, X, label=y, num_boost_round=8).predict(Xt, pred_contribs=True)
+    assert np.max(np.abs(lanes - ref.shap(Xt))) <= 1e-5
+
+
+def test_shap_deep_trees_and_categorical(oracle):
+    # depth-14 lossguide trees (deepest DFS stacks) and categorical splits
+    rng = np.random.default_rng(12)
+    n = 20000
+    Xn = rng.standard_normal((n, 5)).astype(np.float32)
+    Xc = rng.integers(0, 20, (n, 2)).astype(np.float32)
+    X = np.concatenate([Xn, Xc], axis=1)
+    y = (Xn[:, 0] + np.sin(3 * Xn[:, 1]) + (Xc[:, 0] % 3) - 0.5 * Xc[:, 1] / 10).astype(np.float32)
+    p = dict(objective="reg:squarederror", grow_policy="lossguide", max_depth=14, max_leaves=200, eta=0.3)
+    cat = np.array([0] * 5 + [1] * 2, np.uint8)
+    m = fb.train(p, X, label=y, num_boost_round=6, feature_types=["q"] * 5 + ["c"] * 2)
+    ref = oracle.train(X, y, n_rounds=6, categorical=cat, **p)
+    Xt = X[:2000]
+    phi = m.predict(Xt, pred_contribs=True)
+    assert np.max(np.abs(phi - ref.shap(Xt))) <= 1e-5
+    np.testing.assert_allclose(phi.sum(axis=1), ref.predict_margin(Xt), atol=2e-4)
+
+
 def test_json_is_valid_xgboost_schema():
     X, y = _synthetic(3000, 4, seed=1)
     m = fb.train({"max_depth": 3}, X, label=y, num_boost_round=2)
