@@ -245,7 +245,10 @@ class Dataset:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            lib().fb_dataset_free(h)
+            try:
+                lib().fb_dataset_free(h)
+            except TypeError:  # interpreter shutdown: module globals already cleared
+                pass
             self._h = None
 
     def cuts(self):
@@ -302,7 +305,10 @@ class Booster:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            lib().fb_booster_free(h)
+            try:
+                lib().fb_booster_free(h)
+            except TypeError:  # interpreter shutdown: module globals already cleared
+                pass
             self._h = None
 
     def update(self, n_rounds: int = 1) -> None:
@@ -342,7 +348,10 @@ class Model:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            lib().fb_model_free(h)
+            try:
+                lib().fb_model_free(h)
+            except TypeError:  # interpreter shutdown: module globals already cleared
+                pass
             self._h = None
 
     @property

@@ -1035,47 +1035,6 @@ ExplainModel::ExplainModel(int device, uint32_t n_features, uint32_t n_trees, co
         rm_sum += mean[0];
     }
     root_mean_ = (float)rm_sum;
-    make_shap_rule(rule_nodes_, rule_weights_);
-    // per-edge QuadratureTreeSHAP factors (k_shap_q) and the deepest leaf
-    std::vector<float2> ew(nodes.size(), float2{0.0f, 0.0f});
-    std::vector<float> ef(nodes.size() * kShapPoints, 0.0f), er(nodes.size() * kShapPoints, 0.0f);
-    uint32_t max_depth = 0;
-    for (uint32_t t = 0; t < n_trees; t++) {
-        const uint32_t a = tree_off[t], b = tree_off[t + 1];
-        std::vector<uint32_t> depth(b - a, 0);
-        for (uint32_t i = a; i < b; i++) {
-            const DevNode& d = nodes[i];
-            max_depth = std::max(max_depth, depth[i - a]);
-            if ((d.meta >> 24) & 1u) continue;
-            for (int32_t c : {d.left, d.right}) {
-                depth[c] = depth[i - a] + 1;
-                const uint32_t cg = a + (uint32_t)c;
-                // explain.rs:182-192 branch_weight, then p_e = 1 / cw on a first visit
-                const float parent = d.hess, cover = nodes[cg].hess;
-                float cw = 0.5f;
-                if (parent > 0.0f) {
-                    cw = cover / parent;
-                    if (cw < 1e-12f) cw = 1e-12f;
-                }
-                const float pe = 1.0f / cw;
-                ew[cg] = float2{cw, pe};
-                for (int k = 0; k < kShapPoints; k++) {
-                    const float fk = 1.0f + (pe - 1.0f) * rule_nodes_[k];
-                    ef[(size_t)cg * kShapPoints + k] = fk;
-                    er[(size_t)cg * kShapPoints + k] = 1.0f / fk;
-                }
-            }
-        }
-    }
-    edge_w_.alloc(sizeof(float2) * ew.size());
-    edge_f_.alloc(4 * ef.size());
-    edge_r_.alloc(4 * er.size());
-    FB_CUDA_CHECK(cudaMemcpyAsync(edge_w_.p, ew.data(), sizeof(float2) * ew.size(), cudaMemcpyHostToDevice, s_));
-    FB_CUDA_CHECK(cudaMemcpyAsync(edge_f_.p, ef.data(), 4 * ef.size(), cudaMemcpyHostToDevice, s_));
-    FB_CUDA_CHECK(cudaMemcpyAsync(edge_r_.p, er.data(), 4 * er.size(), cudaMemcpyHostToDevice, s_));
-    se_.w = edge_w_.as<float2>();
-    se_.f = edge_f_.as<float>();
-    se_.r = edge_r_.as<float>();
     nodes_.alloc(sizeof(DevNode) * nodes.size());
     tree_off_.alloc(4 * (n_trees + 1));
     cat_off_.alloc(4 * coff.size());
@@ -1087,13 +1046,8 @@ ExplainModel::ExplainModel(int device, uint32_t n_features, uint32_t n_trees, co
     FB_CUDA_CHECK(cudaMemcpyAsync(cat_len_.p, clen.data(), 4 * clen.size(), cudaMemcpyHostToDevice, s_));
     if (n_cat_words)
         FB_CUDA_CHECK(cudaMemcpyAsync(cat_words_.p, cat_words, 4 * n_cat_words, cudaMemcpyHostToDevice, s_));
+    make_shap_rule(rule_nodes_, rule_weights_);
     FB_CUDA_CHECK(cudaStreamSynchronize(s_));
-    // FBGPU_SHAP=lanes selects the lane-per-quadrature-point kernel (k_shap_q);
-    // the default is the one-thread-per-row kernel, bit-equal to the CPU
-    // engine's f32 order and faster on B200 (read when the model is built)
-    const char* sv = std::getenv("FBGPU_SHAP");
-    shap_exact_ = !(sv && std::string(sv) == "lanes");
-    dm_.max_depth = max_depth;
     dm_.nodes = nodes_.as<DevNode>();
     dm_.tree_off = tree_off_.as<uint32_t>();
     dm_.cat_off = cat_off_.as<uint32_t>();
@@ -1125,11 +1079,7 @@ void ExplainModel::shap_device(const float* X, uint64_t n, float* out, cudaStrea
         scratch_threads_ = T;
     }
     upload_shap_rule(rule_nodes_, rule_weights_, s);
-    if (!shap_exact_ && shap_q_supported(dm_)) {
-        launch_shap_q(dm_, se_, X, n, base_margin_, root_mean_, out, s);
-    } else {
-        launch_shap(dm_, X, n, base_margin_, root_mean_, out, path_.as<float>(), tc_.as<float>(), s);
-    }
+    launch_shap(dm_, X, n, base_margin_, root_mean_, out, path_.as<float>(), tc_.as<float>(), s);
     FB_CUDA_CHECK(cudaGetLastError());
 }
 

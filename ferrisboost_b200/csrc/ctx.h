@@ -222,9 +222,7 @@ class ExplainModel {
     int device_;
     uint32_t F_, T_;
     float base_margin_, root_mean_;
-    DevMem nodes_, tree_off_, cat_off_, cat_len_, cat_words_, path_, tc_, x_, out_, edge_w_, edge_f_, edge_r_;
-    ShapEdges se_{};
-    bool shap_exact_ = false;
+    DevMem nodes_, tree_off_, cat_off_, cat_len_, cat_words_, path_, tc_, x_, out_;
     uint64_t scratch_threads_ = 0;
     cudaStream_t s_ = nullptr;
     DevModel dm_{};

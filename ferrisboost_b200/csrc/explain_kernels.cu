@@ -10,7 +10,6 @@
 // threads of a warp walk the same nodes in the same order and only their
 // feature values differ (no divergence on the traversal itself).
 #include <cstdint>
-#include <cstdlib>
 
 #include "explain_kernels.cuh"
 
@@ -185,160 +184,9 @@ __global__ void __launch_bounds__(128) k_shap(DevModel m, const float* __restric
     }
 }
 
-// ---------------------------------------------------------------------------
-// QuadratureTreeSHAP with one lane per quadrature point.  A warp explains four
-// rows at a time: lane 8g + i holds point i of row g.  The traversal is the
-// same DFS as k_shap, identical for every row, so all 32 lanes stay in step.
-// The per-edge factors that do not depend on the row are precomputed per
-// tree (ShapEdges: the branch weight cw, 1/cw, and for each point the factor
-// 1 + (1/cw - 1) x_i and its reciprocal; the not-satisfied factor 1 - x_i is a
-// constant), so a visit is a few multiplies per lane instead of up to 25 f32
-// divisions per row.  Dividing by a factor becomes multiplying by its
-// reciprocal and the 8-point sums are reduced by butterfly shuffles, so the
-// results differ from the reference in the last bits (the contract's bar is
-// 1e-5 absolute; explain.rs:198-216, 312-358 give the recurrence).  The path
-// probability of a feature is read from the DFS frames themselves: the
-// deepest ancestor frame that splits on the same feature.
-__constant__ float c_f0[kShapPoints];  // 1 - x_i (not satisfied: p_e = 0)
-__constant__ float c_r0[kShapPoints];  // 1 / (1 - x_i)
-
-constexpr int kShapQWarps = 4;
-constexpr int kShapQFrames = kMaxShapDepth + 1;
-
-__global__ void __launch_bounds__(32 * kShapQWarps) k_shap_q(DevModel m, ShapEdges e, const float* __restrict__ X,
-                                                            uint64_t n, float bias, float root_mean,
-                                                            float* __restrict__ out, uint32_t phi_in_smem) {
-    extern __shared__ float sphi[];                       // [warp][4 rows][F + 1] when phi_in_smem
-    __shared__ uint32_t s_feat[kShapQWarps][kShapQFrames];  // split feature of each frame (uniform)
-    const uint32_t F = m.n_features;
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t g = lane >> 3, pt = lane & 7;
-    const float xi = c_rule_nodes[pt], wi = c_rule_weights[pt];
-    const float f0 = c_f0[pt], r0 = c_r0[pt];
-    float fc[kShapQFrames], fhl[kShapQFrames], fwp[kShapQFrames], fpe[kShapQFrames], fre[kShapQFrames];
-    uint32_t fidx[kShapQFrames], fstage[kShapQFrames];
-    const uint64_t step = (uint64_t)gridDim.x * kShapQWarps * 4;
-    for (uint64_t base = ((uint64_t)blockIdx.x * kShapQWarps + warp) * 4; base < n; base += step) {
-        const uint64_t r = base + g;
-        const bool valid = r < n;
-        const uint64_t rr = valid ? r : n - 1;
-        const float* x = X + rr * F;
-        float* phi = phi_in_smem ? sphi + (size_t)(warp * 4 + g) * (F + 1) : out + rr * (F + 1);
-        if (valid || phi_in_smem)
-            for (uint32_t f = pt; f <= F; f += 8) phi[f] = 0.0f;
-        __syncwarp();
-        for (uint32_t t = 0; t < m.n_trees; t++) {
-            const uint32_t gb = m.tree_off[t];
-            const DevNode* nodes = m.nodes + gb;
-            if ((nodes[0].meta >> 24) & kNodeLeaf) continue;
-            int sp = 0;
-            fc[0] = 1.0f;
-            fwp[0] = 1.0f;
-            fidx[0] = 0;
-            fstage[0] = 0;
-            float h = 0.0f;
-            bool have_ret = false;
-            while (sp >= 0) {
-                const uint32_t idx = fidx[sp];
-                const DevNode nd = nodes[idx];
-                const uint32_t feat = nd.meta & 0xffffffu;
-                // the path probability before this node's edge: deepest ancestor on the same feature
-                int anc = -1;
-                for (int k = sp - 1; k >= 0; k--)
-                    if (s_feat[warp][k] == feat) { anc = k; break; }
-                const bool seen = anc >= 0;
-                const float p_old = seen ? fpe[anc] : 1.0f;
-                const float r_old = seen ? fre[anc] : 1.0f;
-                if (have_ret) {
-                    // return from the edge taken in fstage[sp]: explain.rs:345-349 + extract_delta
-                    const float pe = fpe[sp];
-                    float acc = 0.0f;
-                    if (pe != 1.0f) acc = __fmul_rn(__fmul_rn(__fsub_rn(pe, 1.0f), h), fre[sp]);
-                    if (seen && p_old != 1.0f)
-                        acc = __fsub_rn(acc, __fmul_rn(__fmul_rn(__fsub_rn(p_old, 1.0f), h), r_old));
-                    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-                    acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-                    if (pt == 0 && (valid || phi_in_smem)) phi[feat] += acc;
-                    if (fstage[sp] == 0) {
-                        fhl[sp] = h;
-                        fstage[sp] = 1;
-                        have_ret = false;
-                    } else {
-                        h = __fadd_rn(fhl[sp], h);
-                        sp--;
-                        continue;  // have_ret stays true for the parent frame
-                    }
-                }
-                // take the edge of fstage[sp]: explain.rs:312-350 visit_child
-                const bool left_side = fstage[sp] == 0;
-                const int32_t child = left_side ? nd.left : nd.right;
-                const uint32_t cg = gb + (uint32_t)child;
-                const float2 ew = e.w[cg];  // (cw, 1 / cw)
-                const bool gl = node_goes_left(nd, m, gb + idx, x[feat]);
-                const bool sat = left_side ? gl : !gl;
-                float pe, fe, re;
-                if (!sat) {
-                    pe = 0.0f; fe = f0; re = r0;
-                } else if (!seen) {
-                    pe = ew.y; fe = e.f[cg * kShapPoints + pt]; re = e.r[cg * kShapPoints + pt];
-                } else {
-                    pe = __fdiv_rn(p_old, ew.x);
-                    fe = __fadd_rn(1.0f, __fmul_rn(__fsub_rn(pe, 1.0f), xi));
-                    re = __fdividef(1.0f, fe);
-                }
-                float cc = __fmul_rn(fc[sp], fe);
-                if (seen && p_old != 1.0f) cc = __fmul_rn(cc, r_old);
-                fpe[sp] = pe;
-                fre[sp] = re;
-                if (lane == 0) s_feat[warp][sp] = feat;
-                __syncwarp();
-                const float wpc = __fmul_rn(fwp[sp], ew.x);
-                const DevNode ch = nodes[child];
-                if ((ch.meta >> 24) & kNodeLeaf) {
-                    h = __fmul_rn(__fmul_rn(cc, __fmul_rn(wpc, ch.val)), wi);
-                    have_ret = true;
-                } else {
-                    sp++;
-                    fc[sp] = cc;
-                    fwp[sp] = wpc;
-                    fidx[sp] = (uint32_t)child;
-                    fstage[sp] = 0;
-                }
-            }
-        }
-        if (pt == 0 && (valid || phi_in_smem)) phi[F] = __fadd_rn(__fadd_rn(phi[F], root_mean), bias);
-        __syncwarp();
-        if (phi_in_smem && valid)
-            for (uint32_t f = pt; f <= F; f += 8) out[rr * (F + 1) + f] = phi[f];
-        __syncwarp();
-    }
-}
-
 void upload_shap_rule(const float* nodes, const float* weights, cudaStream_t s) {
     cudaMemcpyToSymbolAsync(c_rule_nodes, nodes, sizeof(float) * kShapPoints, 0, cudaMemcpyHostToDevice, s);
     cudaMemcpyToSymbolAsync(c_rule_weights, weights, sizeof(float) * kShapPoints, 0, cudaMemcpyHostToDevice, s);
-    float f0[kShapPoints], r0[kShapPoints];
-    for (int i = 0; i < kShapPoints; i++) {
-        f0[i] = 1.0f + (-1.0f) * nodes[i];  // alpha = p_e - 1 = -1
-        r0[i] = 1.0f / f0[i];
-    }
-    cudaMemcpyToSymbolAsync(c_f0, f0, sizeof(f0), 0, cudaMemcpyHostToDevice, s);
-    cudaMemcpyToSymbolAsync(c_r0, r0, sizeof(r0), 0, cudaMemcpyHostToDevice, s);
-}
-
-bool shap_q_supported(const DevModel& m) { return m.max_depth <= kMaxShapDepth; }
-
-void launch_shap_q(const DevModel& m, const ShapEdges& e, const float* X, uint64_t n, float bias, float root_mean,
-                   float* out, cudaStream_t s) {
-    if (n == 0) return;
-    const uint32_t F = m.n_features;
-    const size_t smem = (size_t)kShapQWarps * 4 * (F + 1) * sizeof(float);
-    const uint32_t in_smem = smem <= 48 * 1024 ? 1u : 0u;
-    uint64_t blocks = (n + 4 * kShapQWarps - 1) / (4 * kShapQWarps);
-    if (blocks > 148ull * 32) blocks = 148ull * 32;
-    count_launch();
-    k_shap_q<<<(unsigned)blocks, 32 * kShapQWarps, in_smem ? smem : 0, s>>>(m, e, X, n, bias, root_mean, out, in_smem);
 }
 
 void launch_predict(const DevModel& m, const float* X, uint64_t n, float base_margin, float* out, cudaStream_t s) {
@@ -349,17 +197,11 @@ void launch_predict(const DevModel& m, const float* X, uint64_t n, float base_ma
     k_predict<<<(unsigned)blocks, 256, 0, s>>>(m, X, n, base_margin, out);
 }
 
-// Rows in flight: each thread's DFS frames (up to 15 x 84 B) live in local
-// memory, so the resident threads are capped to keep that working set in L1
-// (FBGPU_SHAP_CTAS_PER_SM overrides the cap of 128-thread CTAs per SM).
+// At most one wave of 128-thread CTAs: the kernel's 54 registers per thread
+// allow 9 per SM, and a second partial wave would leave a tail.
 uint64_t shap_threads(uint64_t n) {
-    static const uint64_t per_sm = [] {
-        const char* v = std::getenv("FBGPU_SHAP_CTAS_PER_SM");
-        const long k = v ? std::atol(v) : 0;
-        return (uint64_t)(k > 0 && k <= 64 ? k : 16);
-    }();
     uint64_t t = ((n + 127) / 128) * 128;
-    const uint64_t cap = 148ull * per_sm * 128;
+    const uint64_t cap = 148ull * 9 * 128;
     return t < cap ? t : cap;
 }
 

@@ -36,15 +36,6 @@ struct DevModel {
     const uint32_t* cat_words;
     uint32_t n_trees;
     uint32_t n_features;
-    uint32_t max_depth;         // deepest leaf over all trees
-};
-
-// Row-independent QuadratureTreeSHAP factors of every node's parent edge
-// (index = global node id; unused for roots).
-struct ShapEdges {
-    const float2* w;            // (cw, 1 / cw): explain.rs:182-192 branch_weight and p_e of a first visit
-    const float* f;             // [node][8]: 1 + (1/cw - 1) x_i
-    const float* r;             // [node][8]: 1 / f
 };
 
 void upload_shap_rule(const float* nodes, const float* weights, cudaStream_t s);
@@ -52,8 +43,5 @@ void launch_predict(const DevModel& m, const float* X, uint64_t n, float base_ma
 uint64_t shap_threads(uint64_t n);
 void launch_shap(const DevModel& m, const float* X, uint64_t n, float bias, float root_mean, float* out,
                  float* path, float* tc, cudaStream_t s);
-bool shap_q_supported(const DevModel& m);
-void launch_shap_q(const DevModel& m, const ShapEdges& e, const float* X, uint64_t n, float bias, float root_mean,
-                   float* out, cudaStream_t s);
 
 }  // namespace fbg

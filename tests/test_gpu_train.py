@@ -126,18 +126,14 @@ def test_predict_and_shap_match_oracle(oracle):
     np.testing.assert_allclose(phi.sum(axis=1), ref.predict_margin(Xt), atol=2e-4)
 
 
-def test_shap_kernels_against_oracle(oracle, monkeypatch):
-    # default kernel: the CPU engine's f32 order, bit for bit; FBGPU_SHAP=lanes:
-    # one lane per quadrature point with precomputed reciprocals, within 1e-5
+def test_shap_bit_equal_to_oracle(oracle):
+    # the kernel keeps the CPU engine's f32 operation order
     X, y = _synthetic(8000, 12, seed=6, missing=0.03)
     p = dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=64)
     ref = oracle.train(X, y, n_rounds=8, **p)
     Xt, _ = _synthetic(1000, 12, seed=78, missing=0.03)
     m = fb.train(p, X, label=y, num_boost_round=8)
     assert np.array_equal(m.predict(Xt, pred_contribs=True).view(np.uint32), ref.shap(Xt).view(np.uint32))
-    monkeypatch.setenv("FBGPU_SHAP", "lanes")
-    lanes = fb.train(p, X, label=y, num_boost_round=8).predict(Xt, pred_contribs=True)
-    assert np.max(np.abs(lanes - ref.shap(Xt))) <= 1e-5
 
 
 def test_shap_deep_trees_and_categorical(oracle):
