@@ -598,9 +598,11 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
     const TileDesc* T = d_tiles_.as<TileDesc>();
     const TileFeat* TF = d_tfeat_.as<TileFeat>();
     const unsigned long long slot = std::max<uint64_t>(total_bins_, 1);
-    const uint32_t grid_gen = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 8192), 148 * 2));
+    const uint32_t grid_gen = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 1024), 148 * 2));
     const int per_sm = tile_smem_lpf_ + 1024 <= 113 * 1024 ? 2 : 1;
-    const uint32_t grid_lpf = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 4096), 148u * per_sm));
+    // every SM gets a CTA once there are ~512 rows per CTA: the kernel is
+    // issue-bound, so idle SMs cost more than the extra flushes
+    const uint32_t grid_lpf = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u * per_sm));
     for (int w = 0; w < 2; w++) {
         launch_hist(w + 1, T + tile_off_gen_[w], n_gen_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list, acc_prefix,
                     state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_gen, tile_smem_, s_);

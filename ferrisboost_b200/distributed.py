@@ -30,7 +30,57 @@ import numpy as np
 
 from . import (Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params, lib)
 
-__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train"]
+__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost"]
+
+
+class PeerLost(RuntimeError):
+    """A rank of the run left or stopped answering; raised on the host before
+    any collective is launched, so no GPU waits on the missing rank."""
+
+
+class Liveness:
+    """Host-side liveness of the ranks through the process group's key-value
+    store.  Every rank stamps a heartbeat before each round; a rank that ends
+    early marks itself as left.  ``check()`` raises PeerLost when a peer has
+    left or its heartbeat is older than ``stale_s``, so the surviving ranks stop
+    between rounds instead of entering a collective that cannot complete.  The
+    library's bounded NCCL waits (``timeout_s`` of ``train``) remain the last
+    resort for a rank that dies inside a round."""
+
+    def __init__(self, store, rank: int, world: int, stale_s: float = 60.0, prefix: str = "fbgpu"):
+        import datetime
+        self.store, self.rank, self.world, self.stale_s, self.prefix = store, rank, world, stale_s, prefix
+        self.beat()
+        # every rank's first heartbeat, within stale_s
+        for r in range(world):
+            try:
+                store.wait([self._key("beat", r)], datetime.timedelta(seconds=stale_s))
+            except Exception as e:  # the store's timeout error
+                raise PeerLost(f"rank {r} never joined the run") from e
+
+    def _key(self, kind: str, r: int) -> str:
+        return f"{self.prefix}/{kind}/{r}"
+
+    def beat(self) -> None:
+        import time
+        self.store.set(self._key("beat", self.rank), repr(time.time()))
+
+    def leave(self) -> None:
+        self.store.set(self._key("left", self.rank), "1")
+
+    def check(self) -> None:
+        import time
+        now = time.time()
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            if self.store.check([self._key("left", r)]):
+                raise PeerLost(f"rank {r} left the run")
+            if not self.store.check([self._key("beat", r)]):
+                raise PeerLost(f"rank {r} never joined the run")
+            age = now - float(self.store.get(self._key("beat", r)).decode())
+            if age > self.stale_s:
+                raise PeerLost(f"rank {r} has not answered for {age:.1f} s")
 
 
 def shard_range(n_rows: int, world_size: int, rank: int) -> tuple[int, int]:
@@ -113,7 +163,7 @@ def _broadcast(obj, group=None):
 
 def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
           feature_types: Sequence[str] | None = None, group=None, timeout_s: float = 120.0,
-          return_booster: bool = False):
+          return_booster: bool = False, liveness: Liveness | None = None):
     """``ferrisboost_b200.train`` over all ranks of ``group`` (an initialised
     ``torch.distributed`` process group; one process per GPU).
 
@@ -122,6 +172,8 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     (unless ``params["device"]`` names one).  Returns the model, identical on
     every rank (or the booster with ``return_booster``).  Collective waits
     give up after ``timeout_s`` with a RuntimeError on the ranks still waiting.
+    With ``liveness``, the rounds run one at a time and every rank checks its
+    peers before each round (PeerLost).
     """
     rank, world = _rank_world(group)
     params = dict(params)
@@ -163,7 +215,13 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
                   timeout_ms=int(max(1.0, timeout_s) * 1000))
     b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)
-    b.update(num_boost_round)
+    if liveness is None:
+        b.update(num_boost_round)
+    else:
+        for _ in range(num_boost_round):
+            liveness.beat()
+            liveness.check()
+            b.update(1)
     if return_booster:
         return b
     m = b.model()

@@ -117,3 +117,44 @@ def test_gloo_two_ranks_share_cuts_and_id(tmp_path):
         assert np.array_equal(z["cuts"], want_cuts) and np.array_equal(z["off"], want_off)
         assert bool(z["same_id"])
         assert "base_score" in (tmp_path / f"err{r}.txt").read_text()
+
+
+def _liveness_worker(rank, world, port, out_dir, scenario):
+    import datetime
+    import time
+    import torch.distributed as dist
+    from ferrisboost_b200.distributed import Liveness, PeerLost
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=30))
+    live = Liveness(store, rank, world, stale_s=2.0, prefix=scenario)
+    outcome = "ok"
+    try:
+        for step in range(6):
+            if rank == 1 and step == 3:
+                if scenario == "leave":
+                    live.leave()  # a graceful early exit between rounds
+                break             # "stall": stop beating without a word
+            live.beat()
+            if step == 4:
+                time.sleep(2.5)   # past stale_s: a stalled peer is now stale
+            live.check()
+            time.sleep(0.2)
+    except PeerLost as e:
+        outcome = f"lost: {e}"
+    with open(os.path.join(out_dir, f"{scenario}{rank}.txt"), "w") as f:
+        f.write(outcome)
+    if rank == 0:
+        time.sleep(0.5)  # keep the store's server up until rank 1 is done with it
+
+
+@pytest.mark.parametrize("scenario", ["leave", "stall"])
+def test_liveness_detects_a_lost_peer_before_the_next_round(tmp_path, scenario):
+    import torch.multiprocessing as mp
+    port = _free_port()
+    mp.start_processes(_liveness_worker, args=(2, port, str(tmp_path), scenario), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = (tmp_path / f"{scenario}0.txt").read_text()
+    assert r0.startswith("lost: rank 1"), r0
+    if scenario == "leave":
+        assert "left" in r0
+    else:
+        assert "has not answered" in r0
