@@ -42,6 +42,10 @@ sys.path.insert(0, ROOT)
 N_FEATURES = 28
 PARAMS = {"objective": "binary:logistic", "max_depth": 8, "eta": 0.1, "lambda": 1.0, "max_bin": 256}
 E2E_ROUNDS = 100
+# DRAM bytes / algorithmic bytes of k_hist_lpf over one tree, from an ncu capture
+# (profiles/k_hist_lpf_c1_4Mrows_traffic.md); roofline.traffic = this x the
+# algorithmic bytes per launch measured live
+HIST_TRAFFIC_RATIO = 2225.7 / 8 / 133.8
 
 
 def make_data(n, seed=0):
@@ -321,7 +325,10 @@ def run_ours(args, rank, world):
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(hist_gbs / hbm_peak, 4) if hist_gbs else None,
-                     "traffic": None, "kernel": "k_hist_lpf (histogram), rank 0",
+                     "traffic": int(HIST_TRAFFIC_RATIO * t["hist_bytes"] / hist_launches) if hist_gbs else None,
+                     "traffic_source": "ncu dram bytes / algorithmic bytes of one tree at 4M rows (ratio 2.08), "
+                                       "scaled to this launch",
+                     "kernel": "k_hist_lpf (histogram), rank 0",
                      "per_launch_ms": round(t["hist_ms"] / hist_launches, 4),
                      "alg_bytes_per_launch": int(t["hist_bytes"] / hist_launches), "peak_source": peak_src},
         "clocks": clk.summary(),
