@@ -219,28 +219,45 @@ class Dataset:
     column blocks of u8/u16 bins (the reference's DenseSource)."""
 
     def __init__(self, data: Any, max_bin: int = 255, weight: Any = None, feature_types=None, nthread: int = 0,
-                 missing: float = float("nan"), cuts: tuple[np.ndarray, np.ndarray] | None = None):
+                 missing: float = float("nan"), cuts: tuple[np.ndarray, np.ndarray] | None = None,
+                 device: int | None = None):
         """``cuts`` = (cut values, F+1 offsets) bins the rows with given cuts
         (validation data, or one row shard of a multi-GPU run) instead of
-        sketching them."""
+        sketching them.  ``device`` = N sketches and quantizes on CUDA device
+        N and keeps the bins there (the same cuts and bins as the host
+        preparation; a booster on that device trains from them in place)."""
         X = _as_matrix(data, missing)
         self.n_rows, self.n_features = X.shape
         w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
         cat = _feature_flags(feature_types, self.n_features)
         self.categorical = cat
-        if cuts is None:
+        self.device = device
+        if device is not None:
+            cv = off = None
+            if cuts is not None:
+                cv, off = self._check_cuts(cuts)
+                cv = cv if cv.size else np.zeros(1, np.float32)
+            self._h = lib().fb_dataset_on_device(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
+                                                 _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8),
+                                                 _lib.ptr(cv, C.c_float), _lib.ptr(off, C.c_uint32), nthread,
+                                                 int(device))
+        elif cuts is None:
             self._h = lib().fb_dataset_from_dense(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
                                                   _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), nthread)
         else:
-            cv = np.ascontiguousarray(cuts[0], dtype=np.float32)
-            off = np.ascontiguousarray(cuts[1], dtype=np.uint32)
-            if off.shape != (self.n_features + 1,) or int(off[-1]) != cv.size or np.any(np.diff(off.astype(np.int64)) < 0):
-                raise ValueError("cuts must be (values, offsets) with F+1 non-decreasing offsets ending at len(values)")
+            cv, off = self._check_cuts(cuts)
             self._h = lib().fb_dataset_with_cuts(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1],
                                                  _lib.ptr(cv if cv.size else np.zeros(1, np.float32), C.c_float),
                                                  _lib.ptr(off, C.c_uint32), _lib.ptr(cat, C.c_uint8), nthread)
         if not self._h:
             raise ValueError(_err())
+
+    def _check_cuts(self, cuts):
+        cv = np.ascontiguousarray(cuts[0], dtype=np.float32)
+        off = np.ascontiguousarray(cuts[1], dtype=np.uint32)
+        if off.shape != (self.n_features + 1,) or int(off[-1]) != cv.size or np.any(np.diff(off.astype(np.int64)) < 0):
+            raise ValueError("cuts must be (values, offsets) with F+1 non-decreasing offsets ending at len(values)")
+        return cv, off
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -432,7 +449,7 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     if label is None:
         raise ValueError("label is required for array input")
     ds = Dataset(data, max_bin=p["max_bin"], weight=weight, feature_types=feature_types, nthread=p["nthread"],
-                 missing=p["missing"])
+                 missing=p["missing"], device=p["device_index"])
     b = Booster(params, ds, label, weight)
     b.update(num_boost_round)
     m = b.model()

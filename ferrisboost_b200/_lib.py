@@ -105,8 +105,13 @@ SIGNATURES = {
     "fb_last_error": (C.c_char_p, []),
     "fb_dataset_from_dense": (P, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, C.c_int32]),
     "fb_dataset_with_cuts": (P, [f32p, C.c_uint64, C.c_uint32, f32p, u32p, u8p, C.c_int32]),
+    "fb_dataset_on_device": (P, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, f32p, u32p, C.c_int32,
+                                 C.c_int32]),
+    "fb_dataset_device": (C.c_int32, [P]),
     "fb_sketch_features": (C.c_int64, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, u32p, C.c_uint32,
                                        C.c_int32, f32p, u32p, C.c_uint64]),
+    "fb_sketch_features_device": (C.c_int64, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, u32p, C.c_uint32,
+                                              C.c_int32, f32p, u32p, C.c_uint64]),
     "fb_label_mean": (C.c_float, [f32p, f32p, C.c_uint64]),
     "fb_dataset_free": (None, [P]),
     "fb_dataset_rows": (C.c_uint64, [P]),

@@ -280,7 +280,7 @@ void TrainCtx::ensure_features() const {
         if (feat_block_[f] < 0) throw InputError("feature " + std::to_string(f) + " has no uploaded column block");
 }
 
-void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const void* data) {
+std::unique_ptr<TrainCtx::Block> TrainCtx::new_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width) {
     if (nbins_.empty()) throw InputError("fbgpu_set_features must be called before fbgpu_upload_block");
     if (width != 1 && width != 2) throw InputError("bin width must be 1 or 2 bytes");
     if (n_feats == 0) throw InputError("a column block holds at least one feature");
@@ -295,7 +295,40 @@ void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t
     }
     b->width = width;
     b->stride = ((n_feats * width + 15) / 16) * 16;
+    return b;
+}
+
+void TrainCtx::register_block(std::unique_ptr<Block> b) {
+    std::vector<FeatLoc> floc(F_);
+    const int bi = (int)blocks_.size();
+    for (uint32_t i = 0; i < (uint32_t)b->feats.size(); i++) {
+        feat_block_[b->feats[i]] = bi;
+        feat_byte_[b->feats[i]] = i * b->width;
+    }
+    blocks_.push_back(std::move(b));
+    for (uint32_t f = 0; f < F_; f++) {
+        if (feat_block_[f] < 0) { floc[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
+        const Block& blk = *blocks_[feat_block_[f]];
+        floc[f] = FeatLoc{blk.base, blk.stride, feat_byte_[f], blk.width, blk.width == 2 ? 65535u : 255u};
+    }
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_.p, floc.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
+    sync();
+    tiles_valid_ = false;
+}
+
+void TrainCtx::adopt_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const uint8_t* records,
+                           uint32_t stride) {
+    auto b = new_block(feat_ids, n_feats, width);
+    if (stride != b->stride) throw InputError("row records must be padded to a multiple of 16 bytes");
+    if (!records) throw InputError("null row records");
+    b->base = records;
+    register_block(std::move(b));
+}
+
+void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const void* data) {
+    auto b = new_block(feat_ids, n_feats, width);
     b->data.alloc((size_t)n_ * b->stride + 16);
+    b->base = b->data.as<uint8_t>();
     FB_CUDA_CHECK(cudaMemsetAsync(b->data.p, 0, (size_t)n_ * b->stride + 16, s_));
     // column-major host block -> staging -> row-major records, in row slabs
     const uint64_t slab = std::max<uint64_t>(1, std::min<uint64_t>(n_, (256ull << 20) / ((uint64_t)n_feats * width)));
@@ -313,21 +346,7 @@ void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t
                          r0, s_);
         sync();
     }
-    std::vector<FeatLoc> floc(F_);
-    const int bi = (int)blocks_.size();
-    for (uint32_t i = 0; i < n_feats; i++) {
-        feat_block_[feat_ids[i]] = bi;
-        feat_byte_[feat_ids[i]] = i * width;
-    }
-    blocks_.push_back(std::move(b));
-    for (uint32_t f = 0; f < F_; f++) {
-        if (feat_block_[f] < 0) { floc[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
-        const Block& blk = *blocks_[feat_block_[f]];
-        floc[f] = FeatLoc{blk.data.as<uint8_t>(), blk.stride, feat_byte_[f], blk.width, blk.width == 2 ? 65535u : 255u};
-    }
-    FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_.p, floc.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
-    sync();
-    tiles_valid_ = false;
+    register_block(std::move(b));
 }
 
 void TrainCtx::set_labels(const float* labels, const float* weights, const float* base_rows, float base_margin) {
@@ -535,7 +554,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
         const int wi = (int)b.width - 1;
         const uint32_t miss = b.width == 2 ? 65535u : 255u;
         // lane-per-feature tiles
-        TileDesc cur{b.data.as<uint8_t>(), b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
+        TileDesc cur{b.base, b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
         uint32_t maxb = 0;
         auto flush_lpf = [&]() {
             if (cur.n_feat == 0) return;
@@ -555,7 +574,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
         }
         flush_lpf();
         // row-per-thread tiles for the rest
-        TileDesc g{b.data.as<uint8_t>(), b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
+        TileDesc g{b.base, b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
         auto flush_gen = [&]() {
             if (g.n_feat == 0) return;
             gen[wi].push_back(g);

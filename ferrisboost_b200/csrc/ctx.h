@@ -79,6 +79,11 @@ class TrainCtx {
 
     void set_features(const uint32_t* n_bins, const uint8_t* width, const uint8_t* categorical);
     void upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const void* data);
+    // A block already quantized on this device as row records (`stride`
+    // bytes, zero padded, n_rows + 16 B); the caller keeps it alive for the
+    // context's lifetime.
+    void adopt_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width, const uint8_t* records,
+                     uint32_t stride);
     void set_labels(const float* labels, const float* weights, const float* base_rows, float base_margin);
 
     // Round start variants; each leaves the fixed gradients, the root sum
@@ -134,8 +139,11 @@ class TrainCtx {
         std::vector<uint32_t> feats;  // global ids, ascending
         uint32_t width = 2;
         uint32_t stride = 0;
-        DevMem data;
+        DevMem data;                   // owned records (upload_block)
+        const uint8_t* base = nullptr; // records read by the kernels (owned or adopted)
     };
+    std::unique_ptr<Block> new_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width);
+    void register_block(std::unique_ptr<Block> b);
     void ensure_features() const;
     void plan_tiles(const uint8_t* enabled);
     void launch_histograms(const uint32_t* rows, const NodeInfo* nodes, const uint32_t* acc_list,

@@ -24,6 +24,7 @@
 
 #include "../../include/fb_engine.h"
 #include "ctx.h"
+#include "sketch.cuh"
 
 namespace fbe {
 
@@ -170,10 +171,13 @@ struct Dataset {
     struct Block {
         std::vector<uint32_t> feats;
         uint32_t width;
-        std::vector<uint8_t> data;  // column-major
+        std::vector<uint8_t> data;  // column-major (host datasets)
+        std::unique_ptr<fbg::DevMem> dev;  // row records of `stride` bytes (device datasets)
+        uint32_t stride = 0;
     };
     std::vector<Block> blocks;
     std::vector<int> feat_block, feat_local;
+    int device = -1;  // >= 0: the bins were quantized on this device and live there
     uint32_t n_bins(uint32_t f) const { return offsets[f + 1] - offsets[f] + 1; }
     uint32_t missing(uint32_t f) const { return width[f] == 2 ? 65535u : 255u; }
     float threshold(uint32_t f, uint32_t bin) const {  // tree.rs:991-1000 split_threshold
@@ -197,7 +201,7 @@ struct Dataset {
 // blocks of one width; the device stores every block row-major with a
 // 16-byte-padded record, so a block holds at most 64 16-bit or 128 8-bit
 // features (128-byte records).
-void build_blocks(Dataset& d, const float* X, int nth) {
+void plan_blocks(Dataset& d) {
     d.width.resize(d.F);
     for (uint32_t f = 0; f < d.F; f++) {
         const uint32_t nb = d.n_bins(f);
@@ -222,12 +226,17 @@ void build_blocks(Dataset& d, const float* X, int nth) {
     });
     for (size_t bi = 0; bi < d.blocks.size(); bi++) {
         Dataset::Block& b = d.blocks[bi];
-        b.data.resize(b.feats.size() * d.n * b.width);
+        b.stride = ((uint32_t)b.feats.size() * b.width + 15u) / 16u * 16u;
         for (size_t i = 0; i < b.feats.size(); i++) {
             d.feat_block[b.feats[i]] = (int)bi;
             d.feat_local[b.feats[i]] = (int)i;
         }
     }
+}
+
+void build_blocks(Dataset& d, const float* X, int nth) {
+    plan_blocks(d);
+    for (Dataset::Block& b : d.blocks) b.data.resize(b.feats.size() * d.n * b.width);
     // dense.rs:288-308 quantize_dense (column-major, NaN -> missing)
     int reserved = 0;
     for (size_t bi = 0; bi < d.blocks.size(); bi++) {
@@ -305,6 +314,117 @@ Dataset* dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32_t max
         d->offsets.push_back((uint32_t)d->cuts.size());
     }
     build_blocks(*d, X, nth);
+    return d.release();
+}
+
+// Cuts of the listed features from the device copy of the rows: the device
+// sketch for numeric features (unit weights), the device max-code scan for
+// categorical ones (sketch.rs:128-136, categorical.rs:264-266).
+std::vector<std::vector<float>> device_sketch(fbg::DeviceMatrix& M, uint32_t max_bin, const uint8_t* cat,
+                                              const std::vector<uint32_t>& feats) {
+    std::vector<std::vector<float>> per(feats.size());
+    std::vector<uint32_t> num, cf, num_i, cf_i;
+    for (size_t i = 0; i < feats.size(); i++) {
+        const bool c = cat && cat[feats[i]];
+        (c ? cf : num).push_back(feats[i]);
+        (c ? cf_i : num_i).push_back((uint32_t)i);
+    }
+    std::vector<std::vector<float>> pn;
+    M.numeric_cuts(max_bin, num, pn);
+    for (size_t i = 0; i < num.size(); i++) per[num_i[i]] = std::move(pn[i]);
+    std::vector<int32_t> mc;
+    int64_t bad = -1;
+    M.categorical_scan(cf, mc, bad);
+    if (bad >= 0)
+        throw InputError("categorical feature #" + std::to_string(cf[bad]) + " contains an invalid category code");
+    for (size_t i = 0; i < cf.size(); i++)
+        for (int32_t k = 1; k <= std::max(mc[i], 0); k++) per[cf_i[i]].push_back((float)k);
+    return per;
+}
+
+// A stream on `device` for dataset preparation, synchronized and destroyed
+// at scope exit.
+struct PrepStream {
+    cudaStream_t s = nullptr;
+    explicit PrepStream(int32_t device) {
+        int n_dev = 0;
+        if (cudaGetDeviceCount(&n_dev) != cudaSuccess || device < 0 || device >= n_dev)
+            throw InputError("device " + std::to_string(device) + " is not a visible CUDA device");
+        FB_CUDA_CHECK(cudaSetDevice(device));
+        FB_CUDA_CHECK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    }
+    ~PrepStream() {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+    }
+};
+
+// Checks of given cuts (DenseSource::with_cuts): F+1 non-decreasing offsets.
+void check_cuts(const uint32_t* offsets, uint32_t F) {
+    if (!offsets) throw InputError("cuts need F+1 offsets");
+    if (offsets[0] != 0) throw InputError("cut offsets must start at 0");
+    for (uint32_t f = 0; f < F; f++)
+        if (offsets[f + 1] < offsets[f]) throw InputError("cut offsets must be non-decreasing");
+}
+
+// The same dataset as dataset_from_dense / fb_dataset_with_cuts, prepared on
+// `device`: the rows are copied to the device once, numeric cuts come from
+// the device sketch (unit weights; the host sketch when weights are given,
+// since only the order of equal values' weights would differ), categorical
+// cuts from a device max-code scan, and the bins are written straight into
+// the row records the training context reads, which stay on the device.
+Dataset* dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                           const uint8_t* categorical, const float* cuts, const uint32_t* offsets, int32_t nthread,
+                           int32_t device) {
+    if (n == 0 || F == 0) throw InputError("training data must have at least one row and one feature");
+    if (!cuts && (max_bin == 0 || max_bin > 65535)) throw InputError("max_bin must be in 1..=65535");
+    if (w)
+        for (uint64_t i = 0; i < n; i++)
+            if (!std::isfinite(w[i]) || w[i] < 0.0f) throw InputError("sample weights must be finite and non-negative");
+    PrepStream ps(device);
+    const cudaStream_t s = ps.s;
+    auto d = std::make_unique<Dataset>();
+    d->n = n;
+    d->F = F;
+    d->device = device;
+    d->cat.assign(F, 0);
+    if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
+    fbg::DeviceMatrix M(X, n, F, s);
+    if (cuts) {
+        check_cuts(offsets, F);
+        d->offsets.assign(offsets, offsets + F + 1);
+        d->cuts.assign(cuts, cuts + offsets[F]);
+    } else {
+        std::vector<uint32_t> all(F);
+        for (uint32_t f = 0; f < F; f++) all[f] = f;
+        std::vector<std::vector<float>> per =
+            (w || max_bin * 16ull > fbg::kSketchMaxLimit)
+                ? sketch_features(X, n, F, max_bin, w, d->cat.data(), all, threads(nthread))
+                : device_sketch(M, max_bin, d->cat.data(), all);
+        d->offsets.push_back(0);
+        for (uint32_t f = 0; f < F; f++) {
+            d->cuts.insert(d->cuts.end(), per[f].begin(), per[f].end());
+            d->offsets.push_back((uint32_t)d->cuts.size());
+        }
+    }
+    plan_blocks(*d);
+    fbg::DevMem d_cuts, d_off, d_cat;
+    d_cuts.alloc(std::max<size_t>(d->cuts.size(), 1) * 4);
+    d_off.alloc(d->offsets.size() * 4);
+    d_cat.alloc(F);
+    if (!d->cuts.empty())
+        FB_CUDA_CHECK(cudaMemcpyAsync(d_cuts.p, d->cuts.data(), d->cuts.size() * 4, cudaMemcpyHostToDevice, s));
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_off.p, d->offsets.data(), d->offsets.size() * 4, cudaMemcpyHostToDevice, s));
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_cat.p, d->cat.data(), F, cudaMemcpyHostToDevice, s));
+    bool reserved = false;
+    for (Dataset::Block& b : d->blocks) {
+        b.dev = std::make_unique<fbg::DevMem>();
+        b.dev->alloc((size_t)n * b.stride + 16);
+        reserved |= M.bin_block(b.feats.data(), (uint32_t)b.feats.size(), b.width, d_cuts.as<float>(),
+                                d_off.as<uint32_t>(), d_cat.as<uint8_t>(), b.dev->as<uint8_t>(), b.stride);
+    }
+    if (reserved)  // dense.rs:300
+        throw InputError("feature contains f32::MAX, reserved for missing-value split boundaries; rescale this feature");
     return d.release();
 }
 
@@ -633,8 +753,16 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     std::vector<uint32_t> nb(d->F);
     for (uint32_t f = 0; f < d->F; f++) nb[f] = d->n_bins(f);
     b->ctx->set_features(nb.data(), d->width.data(), d->cat.data());
-    for (const Dataset::Block& blk : d->blocks)
-        b->ctx->upload_block(blk.feats.data(), (uint32_t)blk.feats.size(), blk.width, blk.data.data());
+    if (d->device >= 0 && d->device != p.device)
+        throw InputError("the dataset was quantized on device " + std::to_string(d->device) +
+                         ", the booster runs on device " + std::to_string(p.device));
+    for (const Dataset::Block& blk : d->blocks) {
+        if (blk.dev)  // device dataset: the context reads its records in place
+            b->ctx->adopt_block(blk.feats.data(), (uint32_t)blk.feats.size(), blk.width, blk.dev->as<uint8_t>(),
+                                blk.stride);
+        else
+            b->ctx->upload_block(blk.feats.data(), (uint32_t)blk.feats.size(), blk.width, blk.data.data());
+    }
     b->ctx->set_labels(y, b->grad_w.empty() ? nullptr : b->grad_w.data(), nullptr, base_margin(p.objective, base));
     const uint32_t cap = (2u << p.max_depth);
     b->o_left.resize(cap); b->o_right.resize(cap); b->o_feat.resize(cap); b->o_bin.resize(cap);
@@ -797,6 +925,48 @@ fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const f
     }, nullptr);
 }
 
+fb_dataset* fb_dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                                 const uint8_t* categorical, const float* cuts, const uint32_t* offsets,
+                                 int32_t nthread, int32_t device) {
+    return fbe::guarded([&]() -> fb_dataset* {
+        std::unique_ptr<fb_dataset> out(new fb_dataset());
+        out->d.reset(fbe::dataset_on_device(X, n, F, max_bin, w, categorical, cuts, offsets, nthread, device));
+        return out.release();
+    }, nullptr);
+}
+
+int32_t fb_dataset_device(const fb_dataset* h) { return h->d->device; }
+
+int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                                  const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t device,
+                                  float* cuts, uint32_t* counts, uint64_t cap) {
+    if (w || max_bin * 16ull > fbg::kSketchMaxLimit)
+        return fb_sketch_features(X, n, F, max_bin, w, categorical, feats, n_feats, 0, cuts, counts, cap);
+    return fbe::guarded([&]() -> int64_t {
+        if (n == 0 || F == 0) throw fbe::InputError("training data must have at least one row and one feature");
+        if (max_bin == 0) throw fbe::InputError("max_bin must be in 1..=65535");
+        std::vector<uint32_t> fs(feats, feats + n_feats);
+        for (uint32_t f : fs)
+            if (f >= F) throw fbe::InputError("feature index out of range");
+        std::vector<std::vector<float>> per;
+        {
+            fbe::PrepStream ps(device);
+            fbg::DeviceMatrix M(X, n, F, ps.s);
+            per = fbe::device_sketch(M, max_bin, categorical, fs);
+        }
+        uint64_t total = 0;
+        for (size_t i = 0; i < per.size(); i++) total += per[i].size();
+        if (total > cap) throw fbe::InputError("cuts capacity is too small: need " + std::to_string(total));
+        uint64_t at = 0;
+        for (size_t i = 0; i < per.size(); i++) {
+            counts[i] = (uint32_t)per[i].size();
+            std::memcpy(cuts + at, per[i].data(), 4 * per[i].size());
+            at += per[i].size();
+        }
+        return (int64_t)total;
+    }, (int64_t)-1);
+}
+
 int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
                            const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
                            float* cuts, uint32_t* counts, uint64_t cap) {
@@ -842,6 +1012,18 @@ int32_t fb_dataset_column(const fb_dataset* h, uint32_t f, uint16_t* out) {
     const fbe::Dataset* d = h->d.get();
     if (f >= d->F) return 1;
     const fbe::Dataset::Block& b = d->blocks[d->feat_block[f]];
+    if (b.dev) {  // row records on the device: a strided copy of the feature's bytes
+        return fbe::guarded([&]() -> int32_t {
+            const size_t lo = (size_t)d->feat_local[f] * b.width;
+            std::vector<uint8_t> col((size_t)d->n * b.width);
+            FB_CUDA_CHECK(cudaSetDevice(d->device));
+            FB_CUDA_CHECK(cudaMemcpy2D(col.data(), b.width, b.dev->as<uint8_t>() + lo, b.stride, b.width, d->n,
+                                       cudaMemcpyDeviceToHost));
+            for (uint64_t r = 0; r < d->n; r++)
+                out[r] = b.width == 2 ? reinterpret_cast<const uint16_t*>(col.data())[r] : col[r];
+            return 0;
+        }, 2);
+    }
     const size_t off = (size_t)d->feat_local[f] * d->n;
     for (uint64_t r = 0; r < d->n; r++)
         out[r] = b.width == 2 ? reinterpret_cast<const uint16_t*>(b.data.data())[off + r] : b.data[off + r];

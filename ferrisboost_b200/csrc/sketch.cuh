@@ -1,0 +1,55 @@
+// Dataset preparation on the device: the weighted quantile sketch of
+// src/data/sketch.rs (unit weights) and dense quantization into the row
+// records the training context reads (src/source/dense.rs:288-308).
+//
+// The sketch is a restatement, not an approximation of it: every chunk
+// summary, merge, compression and cut selection performs the same f32
+// operations as the sequential reference, so the cuts are bit-identical to
+// the host engine's (and the CPU oracle's) for the same input.
+#pragma once
+#include <cstdint>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+namespace fbg {
+
+// Largest sketch summary the device path supports: max_bin <= 1024
+// (limit = max_bin x 16 entries, sketch.rs:73), which also bounds the bins
+// the device split search accepts.
+constexpr uint32_t kSketchMaxLimit = 16384;
+
+// A row-major f32 matrix (n x F) resident on one device, with the sketch and
+// binning passes over it.  All work runs on `stream` of the current device.
+class DeviceMatrix {
+   public:
+    DeviceMatrix(const float* X_host, uint64_t n, uint32_t F, cudaStream_t stream);
+    ~DeviceMatrix();
+    DeviceMatrix(const DeviceMatrix&) = delete;
+    DeviceMatrix& operator=(const DeviceMatrix&) = delete;
+
+    // sketch.rs:128-302 cuts of the listed numeric features with unit
+    // weights (FeatureSketch::push of every non-NaN value in row order, then
+    // cuts(max_bin)).  per[i] receives the cuts of feats[i].
+    void numeric_cuts(uint32_t max_bin, const std::vector<uint32_t>& feats, std::vector<std::vector<float>>& per);
+    // categorical.rs scan of the listed features: the largest valid code
+    // (-1 when none), and the first feature (in list order) holding a value
+    // that is not a category code (-1 when none).
+    void categorical_scan(const std::vector<uint32_t>& feats, std::vector<int32_t>& max_code, int64_t& bad_feat);
+    // dense.rs:288-308 quantize_dense into one row-record block: record r of
+    // `dst` (stride bytes, zero padded) holds the bins of feats[0..n_feats)
+    // at byte i x width.  Cuts are the dataset's flat cuts and F+1 offsets
+    // (device copies); NaN -> the missing sentinel (255 / 65535), categorical
+    // codes -> their bin.  Returns true if any value of these features equals
+    // f32::MAX (reserved, dense.rs:300).
+    bool bin_block(const uint32_t* feats, uint32_t n_feats, uint32_t width, const float* d_cuts,
+                   const uint32_t* d_offsets, const uint8_t* d_cat, uint8_t* dst, uint32_t stride);
+
+   private:
+    uint64_t n_;
+    uint32_t F_;
+    cudaStream_t s_;
+    float* x_ = nullptr;
+};
+
+}  // namespace fbg

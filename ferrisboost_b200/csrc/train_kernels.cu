@@ -477,6 +477,146 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_lpf(const TileDesc* __
     }
 }
 
+// Staged lane-per-feature histogram.  As in k_hist_lpf, lane t of a warp
+// owns tile feature t and the shared histogram is laid out [bin][32 lanes].
+// The difference is how rows reach the lanes: each warp keeps S batches of
+// kStageRows rows in flight through cp.async (16-byte copies into shared
+// memory, cached in L2 only): for every row the 16-byte chunks of its record
+// that hold the tile's bins, and its 16-byte gradient pair.  A batch is
+// consumed from shared memory while the next S-1 are still arriving, so a
+// warp never stalls on one row's gather, and no registers hold loads in
+// flight.  Row ids come in coalesced 32-row loads, one super-batch (4
+// batches) ahead.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <int W, int S>
+__global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* __restrict__ tiles,
+                                                                 const TileFeat* __restrict__ tfeat,
+                                                                 const uint32_t* __restrict__ rows,
+                                                                 const Pair* __restrict__ gpair,
+                                                                 const NodeInfo* __restrict__ nodes,
+                                                                 const uint32_t* __restrict__ acc_list,
+                                                                 const unsigned long long* __restrict__ acc_prefix,
+                                                                 const TreeState* __restrict__ st,
+                                                                 Pair* __restrict__ hist_acc,
+                                                                 unsigned long long slot_pairs) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const TileDesc td = tiles[blockIdx.y];
+    const uint32_t LB = td.local_bins;  // max bins of the tile x 32
+    uint32_t* glo = sm;
+    uint32_t* ghi = sm + LB;
+    uint32_t* hlo = sm + 2 * LB;
+    uint32_t* hhi = sm + 3 * LB;
+    const unsigned long long R = st->acc_total;
+    const uint32_t n_acc = st->acc_count;
+    if (R == 0) return;
+    unsigned long long a = R * blockIdx.x / gridDim.x;
+    const unsigned long long b = R * (blockIdx.x + 1) / gridDim.x;
+    if (a >= b) return;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t nf = td.n_feat, nch = td.n_chunks;
+    const uint32_t rec_bytes = nch * 16u;
+    const uint32_t stage_bytes = kStageRows * (rec_bytes + 16u);
+    uint8_t* wbuf = reinterpret_cast<uint8_t*>(sm + 4 * LB) + (size_t)warp * S * stage_bytes;
+    TileFeat f{0, 0, 0, 0};
+    if (lane < nf) f = tfeat[td.feat_begin + lane];
+    const bool active = lane < nf;
+    const uint32_t foff = active ? f.byte_off - td.chunk0 * 16u : 0u;
+    const uint8_t* rec_base = td.base + td.chunk0 * 16u;
+    // copy assignment: lane = (item group g, row q); items of a row are its
+    // record chunks 0..nch-1 and its gradient pair (item nch)
+    const uint32_t cq = lane & 7u, cg = lane >> 3;
+    for (uint32_t j = threadIdx.x; j < 4 * LB; j += blockDim.x) sm[j] = 0u;
+    __syncthreads();
+    uint32_t k = find_segment(acc_prefix, n_acc, a);
+    while (a < b) {
+        const uint32_t node = acc_list[k];
+        const NodeInfo ni = nodes[node];
+        const unsigned long long seg_end = min(b, acc_prefix[k + 1]);
+        const uint32_t* seg_rows = rows + ni.start + (uint32_t)(a - acc_prefix[k]);
+        const uint32_t cnt = (uint32_t)(seg_end - a);
+        // this warp's super-batches: 32 rows each, sb = warp, warp + nwarps, ...
+        const uint32_t n_sb = (cnt + 31) / 32;
+        const uint32_t my_sb = warp < n_sb ? (n_sb - warp + nwarps - 1) / nwarps : 0u;
+        const uint32_t nb = my_sb * 4;
+        auto load_ids = [&](uint32_t kk) -> uint32_t {
+            const uint32_t r = (warp + kk * nwarps) * 32u + lane;
+            return (kk < my_sb && r < cnt) ? seg_rows[r] : 0u;
+        };
+        uint32_t ids_cur = load_ids(0), ids_nxt = load_ids(1), k_cur = 0;
+        auto issue = [&](uint32_t bb) {
+            if (bb < nb) {
+                const uint32_t kk = bb >> 2, sub = bb & 3u;
+                const uint32_t ids = kk == k_cur ? ids_cur : ids_nxt;
+                const uint32_t first = (warp + kk * nwarps) * 32u + sub * kStageRows;
+                const uint32_t kq = first < cnt ? min(kStageRows, cnt - first) : 0u;
+                const uint32_t rid = __shfl_sync(0xffffffffu, ids, sub * kStageRows + cq);
+                uint8_t* stg = wbuf + (bb % S) * stage_bytes;
+                if (cq < kq) {
+                    for (uint32_t it = cg; it <= nch; it += 4) {
+                        if (it < nch)
+                            cp_async16(stg + cq * rec_bytes + it * 16u, rec_base + (size_t)rid * td.stride + it * 16u);
+                        else
+                            cp_async16(stg + kStageRows * rec_bytes + cq * 16u, gpair + rid);
+                    }
+                }
+            }
+            cp_async_commit();
+        };
+#pragma unroll
+        for (int s0 = 0; s0 < S; s0++) issue((uint32_t)s0);
+        for (uint32_t bb = 0; bb < nb; bb++) {
+            if (bb > 0 && (bb & 3u) == 0) {  // next super-batch: rotate the prefetched ids
+                k_cur++;
+                ids_cur = ids_nxt;
+                ids_nxt = load_ids(k_cur + 1);
+            }
+            cp_async_wait<S - 1>();
+            __syncwarp();
+            const uint32_t first = (warp + (bb >> 2) * nwarps) * 32u + (bb & 3u) * kStageRows;
+            const uint32_t kq = first < cnt ? min(kStageRows, cnt - first) : 0u;
+            const uint8_t* stg = wbuf + (bb % S) * stage_bytes;
+            const Pair* gps = reinterpret_cast<const Pair*>(stg + kStageRows * rec_bytes);
+            for (uint32_t q = 0; q < kq; q++) {
+                const uint8_t* p = stg + q * rec_bytes + foff;
+                const uint32_t bin = W == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+                const Pair gp = gps[q];
+                if (active && bin != td.missing && bin < f.nbins) {
+                    const uint32_t idx = bin * 32u + lane;
+                    plane_add(glo, ghi, idx, gp.g);
+                    plane_add(hlo, hhi, idx, gp.h);
+                }
+            }
+            __syncwarp();
+            issue(bb + S);
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
+        for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
+            const unsigned long long g = ((unsigned long long)ghi[j] << 32) | glo[j];
+            const unsigned long long h = ((unsigned long long)hhi[j] << 32) | hlo[j];
+            if (g | h) {
+                const uint32_t t = j & 31u, bb = j >> 5;
+                const TileFeat ft = tfeat[td.feat_begin + t];
+                const uint32_t gidx = ft.global_off + bb;
+                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
+                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
+                glo[j] = 0u; ghi[j] = 0u; hlo[j] = 0u; hhi[j] = 0u;
+            }
+        }
+        __syncthreads();
+        a = seg_end;
+        k++;
+    }
+}
+
 // ------------------------------------------------------------------ split
 struct SplitSmem {
     Pair warp_tot[32];
@@ -1111,6 +1251,29 @@ void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const T
     else
         k_hist_lpf<1><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix,
                                                           st, hist_acc, slot_pairs);
+}
+void set_hist_stage_smem_limit(int bytes) {
+    cudaFuncSetAttribute(k_hist_stage<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat,
+                       const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                       const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                       unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s) {
+    if (n_tiles == 0) return;
+    dim3 grid(grid_x, n_tiles);
+    count_launch();
+#define FB_HS(W, S)                                                                                                \
+    k_hist_stage<W, S><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix, \
+                                                          st, hist_acc, slot_pairs)
+    if (width == 2) {
+        if (stages == 4) FB_HS(2, 4); else FB_HS(2, 2);
+    } else {
+        if (stages == 4) FB_HS(1, 4); else FB_HS(1, 2);
+    }
+#undef FB_HS
 }
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
     dim3 grid(max_m, a.n_features);

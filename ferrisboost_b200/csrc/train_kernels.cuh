@@ -36,6 +36,8 @@ struct TileDesc {
     uint32_t n_feat;
     uint32_t local_bins;  // shared-memory bins of this tile
     uint32_t missing;     // missing-value sentinel of this width
+    uint32_t chunk0;      // staged histogram: first 16-byte chunk of the record the tile reads
+    uint32_t n_chunks;    // and the number of chunks (the features' bytes lie inside them)
 };
 struct TileFeat {
     uint32_t byte_off;    // byte offset of the feature inside a row record
@@ -158,6 +160,20 @@ void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const T
                      const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
                      const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
                      unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
+// Lane-per-feature histogram with the rows' record chunks and gradient pairs
+// staged in shared memory by a per-warp cp.async pipeline of `stages` (2 or
+// 4) batches of kStageRows rows.  Shared memory: the tile's histogram planes
+// plus hist_stage_bytes(n_chunks, stages).
+constexpr uint32_t kStageRows = 8;
+constexpr uint32_t kStageWarps = kHistLpfThreads / 32;
+inline size_t hist_stage_bytes(uint32_t n_chunks, int stages) {
+    return (size_t)kStageWarps * stages * kStageRows * (n_chunks * 16 + 16);
+}
+void set_hist_stage_smem_limit(int bytes);
+void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat,
+                       const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                       const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                       unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
 void launch_decide(const LevelArgs& a, cudaStream_t s);
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);

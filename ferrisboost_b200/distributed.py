@@ -102,8 +102,9 @@ def nccl_unique_id() -> bytes:
 
 
 def sketch_features(X: np.ndarray, feats: Sequence[int], max_bin: int, weight=None, categorical=None,
-                    nthread: int = 0) -> list[np.ndarray]:
-    """Cuts of the listed features (the sketch of ``Dataset``, feature by feature)."""
+                    nthread: int = 0, device: int | None = None) -> list[np.ndarray]:
+    """Cuts of the listed features (the sketch of ``Dataset``, feature by
+    feature); on CUDA device ``device`` when given (the same cuts)."""
     X = np.ascontiguousarray(X, dtype=np.float32)
     fs = np.ascontiguousarray(feats, dtype=np.uint32)
     w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
@@ -111,9 +112,15 @@ def sketch_features(X: np.ndarray, feats: Sequence[int], max_bin: int, weight=No
     cap = sum(65534 if cat is not None and cat[f] else max(max_bin, 1) for f in fs) + 1
     cuts = np.zeros(cap, dtype=np.float32)
     counts = np.zeros(max(len(fs), 1), dtype=np.uint32)
-    n = lib().fb_sketch_features(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin, _lib.ptr(w, C.c_float),
-                                 _lib.ptr(cat, C.c_uint8), _lib.ptr(fs, C.c_uint32), len(fs), nthread,
-                                 _lib.ptr(cuts, C.c_float), _lib.ptr(counts, C.c_uint32), cap)
+    if device is None:
+        n = lib().fb_sketch_features(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin, _lib.ptr(w, C.c_float),
+                                     _lib.ptr(cat, C.c_uint8), _lib.ptr(fs, C.c_uint32), len(fs), nthread,
+                                     _lib.ptr(cuts, C.c_float), _lib.ptr(counts, C.c_uint32), cap)
+    else:
+        n = lib().fb_sketch_features_device(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
+                                            _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), _lib.ptr(fs, C.c_uint32),
+                                            len(fs), int(device), _lib.ptr(cuts, C.c_float),
+                                            _lib.ptr(counts, C.c_uint32), cap)
     if n < 0:
         raise ValueError(_err())
     out, at = [], 0
@@ -123,15 +130,17 @@ def sketch_features(X: np.ndarray, feats: Sequence[int], max_bin: int, weight=No
     return out
 
 
-def sketch_cuts(X: np.ndarray, max_bin: int, weight=None, categorical=None, nthread: int = 0, group=None):
+def sketch_cuts(X: np.ndarray, max_bin: int, weight=None, categorical=None, nthread: int = 0, group=None,
+                device: int | None = None):
     """(cut values, F+1 offsets) of all rows of X, the features sketched
-    round-robin by the ranks of ``group`` and all-gathered.  Equal to the
-    cuts one process sketches alone."""
+    round-robin by the ranks of ``group`` (each on its CUDA device when
+    ``device`` is given) and all-gathered.  Equal to the cuts one process
+    sketches alone."""
     import torch.distributed as dist
     F = X.shape[1]
     rank, world = _rank_world(group)
     mine = list(range(rank, F, world))
-    local = sketch_features(X, mine, max_bin, weight, categorical, nthread)
+    local = sketch_features(X, mine, max_bin, weight, categorical, nthread, device)
     gathered: list = [None] * world
     if world > 1:
         dist.all_gather_object(gathered, (mine, [c.tobytes() for c in local]), group=group)
@@ -197,7 +206,7 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     if n < world:  # the same on every rank: all raise before any collective
         raise ValueError(f"{n} rows cannot be sharded over {world} ranks")
     cat = _feature_flags(feature_types, F)
-    cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group)
+    cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group, device=p["device_index"])
     lo, hi = shard_range(n, world, rank)
     base = p["base_score"]
     if base is None:
@@ -211,7 +220,8 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     nid = _broadcast(nid, group)
     if isinstance(nid, str):
         raise RuntimeError(f"rank 0 could not create an NCCL id ({nid})")
-    ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts)
+    ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts,
+                 device=p["device_index"])
     shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
                   timeout_ms=int(max(1.0, timeout_s) * 1000))
     b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)

@@ -61,6 +61,21 @@ fb_dataset* fb_dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32
  * DenseSource::with_cuts, src/source/dense.rs:215-235). */
 fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const float* cuts, const uint32_t* offsets,
                                  const uint8_t* categorical, int32_t nthread);
+/* The dataset of fb_dataset_from_dense (cuts == NULL) or fb_dataset_with_cuts
+ * (cuts and F+1 offsets given), quantized on CUDA device `device`: the rows
+ * are copied to the device once, the weighted quantile sketch runs there
+ * (cuts bit-identical to fb_dataset_from_dense; with weights, or max_bin >
+ * 1024, the host sketch supplies them), and the bins are written straight
+ * into the row records a booster on that device trains from, which stay
+ * resident (no host copy of the bins exists).  A booster built from it must
+ * use the same device.  Replaces the sketch + quantize_row_major passes of
+ * DenseSource::new_weighted_with_nthread (src/source/dense.rs:99-209,
+ * src/data/sketch.rs:128-302) for device training. */
+fb_dataset* fb_dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* weights,
+                                 const uint8_t* categorical, const float* cuts, const uint32_t* offsets,
+                                 int32_t nthread, int32_t device);
+/* Device holding the dataset's bins, or -1 for a host dataset. */
+int32_t fb_dataset_device(const fb_dataset* d);
 /* Cuts of the listed features only, with the sketch of fb_dataset_from_dense
  * (features are sketched independently, so the ranks of a row-sharded run
  * can split the features between them and exchange the cuts).  The cuts of
@@ -71,6 +86,12 @@ fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const f
 int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* weights,
                            const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
                            float* cuts, uint32_t* counts, uint64_t cap);
+/* fb_sketch_features computed on CUDA device `device` (the rows are copied
+ * there once); the same cuts, bit for bit.  With weights, or max_bin > 1024,
+ * the host sketch runs instead. */
+int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* weights,
+                                  const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t device,
+                                  float* cuts, uint32_t* counts, uint64_t cap);
 /* The base_score estimated from the labels when none is given: the label mean
  * (weighted when weights != NULL), summed in f64 in row order
  * (src/objective.rs:41-61). */
