@@ -263,7 +263,7 @@ def run_ours(args, rank, world):
     def train_public(params, rounds, booster=False):
         if world == 1:
             if booster:
-                ds = fb.Dataset(X, max_bin=params["max_bin"], feature_types=ft)
+                ds = fb.Dataset(X, max_bin=params["max_bin"], feature_types=ft, device=device)
                 b = fb.Booster(params, ds, y)
                 b.update(rounds)
                 return b

@@ -548,6 +548,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     std::vector<TileDesc> gen[2], lpf[2];
     std::vector<TileFeat> tf;
     size_t smem_gen = 16, smem_lpf = 16;
+    uint32_t max_chunks = 0;
     const uint32_t max_local = (uint32_t)((smem_budget_ - 64 * sizeof(TileFeat)) / 16);
     for (const auto& bp : blocks_) {
         const Block& b = *bp;
@@ -559,6 +560,15 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
         auto flush_lpf = [&]() {
             if (cur.n_feat == 0) return;
             cur.local_bins = maxb * 32;
+            // 16-byte chunks of the record holding the tile's bins (staged kernel)
+            uint32_t lo = ~0u, hi = 0;
+            for (uint32_t i = cur.feat_begin; i < cur.feat_begin + cur.n_feat; i++) {
+                lo = std::min(lo, tf[i].byte_off);
+                hi = std::max(hi, tf[i].byte_off + b.width);
+            }
+            cur.chunk0 = lo / 16;
+            cur.n_chunks = (hi + 15) / 16 - cur.chunk0;
+            max_chunks = std::max(max_chunks, cur.n_chunks);
             lpf[wi].push_back(cur);
             smem_lpf = std::max(smem_lpf, (size_t)cur.local_bins * 16);
             cur.feat_begin = (uint32_t)tf.size();
@@ -606,6 +616,26 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     tile_smem_lpf_ = smem_lpf;
     set_hist_smem_limit((int)tile_smem_);
     set_hist_lpf_smem_limit((int)tile_smem_lpf_);
+    // staged lane-per-feature kernel: 4 stages when the histogram leaves room
+    // for them in the 227 KiB a CTA may use, else 2, else the unstaged kernel
+    static const bool no_stage = [] {
+        const char* e = std::getenv("FBGPU_HIST");
+        return e && std::string(e) == "lpf";
+    }();
+    const size_t kMaxSmem = 227 * 1024;
+    hist_stages_ = 0;
+    tile_smem_stage_ = 0;
+    if (!no_stage && max_chunks > 0) {
+        for (int st : {4, 2}) {
+            const size_t need = smem_lpf + hist_stage_bytes(max_chunks, st);
+            if (need <= kMaxSmem) {
+                hist_stages_ = st;
+                tile_smem_stage_ = need;
+                break;
+            }
+        }
+        if (hist_stages_) set_hist_stage_smem_limit((int)tile_smem_stage_);
+    }
     sync();
     last_enabled_ = en;
     tiles_valid_ = true;
@@ -618,15 +648,22 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
     const TileFeat* TF = d_tfeat_.as<TileFeat>();
     const unsigned long long slot = std::max<uint64_t>(total_bins_, 1);
     const uint32_t grid_gen = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 1024), 148 * 2));
-    const int per_sm = tile_smem_lpf_ + 1024 <= 113 * 1024 ? 2 : 1;
+    const size_t lpf_smem = hist_stages_ ? tile_smem_stage_ : tile_smem_lpf_;
+    const int per_sm = lpf_smem + 1024 <= 113 * 1024 ? 2 : 1;
     // every SM gets a CTA once there are ~512 rows per CTA: the kernel is
     // issue-bound, so idle SMs cost more than the extra flushes
     const uint32_t grid_lpf = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u * per_sm));
     for (int w = 0; w < 2; w++) {
         launch_hist(w + 1, T + tile_off_gen_[w], n_gen_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list, acc_prefix,
                     state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_gen, tile_smem_, s_);
-        launch_hist_lpf(w + 1, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
-                        acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf, tile_smem_lpf_, s_);
+        if (hist_stages_)
+            launch_hist_stage(w + 1, hist_stages_, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes,
+                              acc_list, acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf,
+                              lpf_smem, s_);
+        else
+            launch_hist_lpf(w + 1, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
+                            acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf, tile_smem_lpf_,
+                            s_);
     }
 }
 

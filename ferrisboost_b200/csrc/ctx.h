@@ -174,7 +174,8 @@ class TrainCtx {
     bool tiles_valid_ = false;
     DevMem d_tiles_, d_tfeat_;
     uint32_t tile_off_gen_[2] = {0, 0}, n_gen_[2] = {0, 0}, tile_off_lpf_[2] = {0, 0}, n_lpf_[2] = {0, 0};
-    size_t tile_smem_ = 0, tile_smem_lpf_ = 0;
+    size_t tile_smem_ = 0, tile_smem_lpf_ = 0, tile_smem_stage_ = 0;
+    int hist_stages_ = 0;  // staged lane-per-feature histogram: cp.async stages, 0 = unstaged kernel
     int smem_budget_ = 0;
 
     // rows / gradients
