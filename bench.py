@@ -316,7 +316,8 @@ def run_ours(args, rank, world):
         "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
         "config": {"workload": cfg["workload"], "rows": n, "features": F, "parallelism": f"row shards x{world}",
                    "l2": "inputs larger than L2 (bin records and fixed-point gradients exceed 126 MB)"
-                   if n * 16 > 126e6 else "inputs smaller than L2"},
+                   if n * ((F * (2 if p["max_bin"] > 255 else 1) + 15) // 16 * 16 + 16) > 126e6
+                   else "inputs smaller than L2"},
         "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds",
                 "h2d_bytes_per_step": int((rows_local * (bin_bytes + 4)) / E2E_ROUNDS),
                 "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / E2E_ROUNDS),

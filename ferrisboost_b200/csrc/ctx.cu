@@ -299,6 +299,17 @@ std::unique_ptr<TrainCtx::Block> TrainCtx::new_block(const uint32_t* feat_ids, u
 }
 
 void TrainCtx::register_block(std::unique_ptr<Block> b) {
+    // column-major copy for the partition passes (FBGPU_PART=rec keeps them on the records)
+    static const bool part_rec = [] {
+        const char* e = std::getenv("FBGPU_PART");
+        return e && std::string(e) == "rec";
+    }();
+    if (!part_rec && n_ > 0) {
+        b->cols.alloc((size_t)n_ * b->feats.size() * b->width);
+        launch_records_to_columns((int)b->width, b->base, b->stride, n_, (uint32_t)b->feats.size(), b->cols.as<uint8_t>(),
+                                  s_);
+        FB_CUDA_CHECK(cudaGetLastError());
+    }
     std::vector<FeatLoc> floc(F_);
     const int bi = (int)blocks_.size();
     for (uint32_t i = 0; i < (uint32_t)b->feats.size(); i++) {
@@ -309,7 +320,12 @@ void TrainCtx::register_block(std::unique_ptr<Block> b) {
     for (uint32_t f = 0; f < F_; f++) {
         if (feat_block_[f] < 0) { floc[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
         const Block& blk = *blocks_[feat_block_[f]];
-        floc[f] = FeatLoc{blk.base, blk.stride, feat_byte_[f], blk.width, blk.width == 2 ? 65535u : 255u};
+        const uint32_t miss = blk.width == 2 ? 65535u : 255u;
+        if (blk.cols.p)
+            floc[f] = FeatLoc{blk.cols.as<uint8_t>() + (size_t)(feat_byte_[f] / blk.width) * n_ * blk.width, blk.width,
+                              0, blk.width, miss};
+        else
+            floc[f] = FeatLoc{blk.base, blk.stride, feat_byte_[f], blk.width, miss};
     }
     FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_.p, floc.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
     sync();
@@ -627,7 +643,8 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     tile_smem_stage_ = 0;
     if (!no_stage && max_chunks > 0) {
         for (int st : {4, 2}) {
-            const size_t need = smem_lpf + hist_stage_bytes(max_chunks, st);
+            // + one discard row of 4 planes x 32 lanes
+            const size_t need = smem_lpf + 512 + hist_stage_bytes(max_chunks, st);
             if (need <= kMaxSmem) {
                 hist_stages_ = st;
                 tile_smem_stage_ = need;

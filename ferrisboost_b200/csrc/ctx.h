@@ -141,6 +141,7 @@ class TrainCtx {
         uint32_t stride = 0;
         DevMem data;                   // owned records (upload_block)
         const uint8_t* base = nullptr; // records read by the kernels (owned or adopted)
+        DevMem cols;                   // column-major copy read by the partition passes
     };
     std::unique_ptr<Block> new_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width);
     void register_block(std::unique_ptr<Block> b);

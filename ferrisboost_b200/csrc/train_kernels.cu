@@ -495,6 +495,17 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// 64-bit modular add into a (low, high) pair of 32-bit shared words: the low
+// atomic returns the old word, whose sum with the addend's low word gives the
+// carry; the high atomic always runs, so no branch depends on the value.
+__device__ __forceinline__ void add64_planes(uint32_t* lo, uint32_t* hi, long long v) {
+    const uint32_t vl = (uint32_t)v, vh = (uint32_t)((unsigned long long)v >> 32);
+    const uint32_t old = atomicAdd(lo, vl);
+    uint32_t sum, hi_add;
+    asm("add.cc.u32 %0, %2, %3;\n\taddc.u32 %1, %4, 0;" : "=r"(sum), "=r"(hi_add) : "r"(old), "r"(vl), "r"(vh));
+    atomicAdd(hi, hi_add);
+}
+
 template <int W, int S>
 __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* __restrict__ tiles,
                                                                  const TileFeat* __restrict__ tfeat,
@@ -509,10 +520,9 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
     extern __shared__ __align__(16) uint32_t sm[];
     const TileDesc td = tiles[blockIdx.y];
     const uint32_t LB = td.local_bins;  // max bins of the tile x 32
-    uint32_t* glo = sm;
-    uint32_t* ghi = sm + LB;
-    uint32_t* hlo = sm + 2 * LB;
-    uint32_t* hhi = sm + 3 * LB;
+    // histogram words laid out [bin][plane g_lo, g_hi, h_lo, h_hi][32 lanes]:
+    // one address per (bin, lane) reaches all four planes by fixed offsets,
+    // and the 32 lanes of an atomic still fall in 32 distinct banks
     const unsigned long long R = st->acc_total;
     const uint32_t n_acc = st->acc_count;
     if (R == 0) return;
@@ -521,13 +531,19 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
     if (a >= b) return;
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const uint32_t nf = td.n_feat, nch = td.n_chunks;
+    uint32_t* hlane = sm + lane;
     const uint32_t rec_bytes = nch * 16u;
     const uint32_t stage_bytes = kStageRows * (rec_bytes + 16u);
-    uint8_t* wbuf = reinterpret_cast<uint8_t*>(sm + 4 * LB) + (size_t)warp * S * stage_bytes;
+    // bins 0 .. LB/32 - 1, then one discard row that missing bins and idle
+    // lanes add to, so the row loop has no branch on the bin
+    const uint32_t discard = LB >> 5;
+    uint8_t* wbuf = reinterpret_cast<uint8_t*>(sm + 4 * (LB + 32)) + (size_t)warp * S * stage_bytes;
     TileFeat f{0, 0, 0, 0};
     if (lane < nf) f = tfeat[td.feat_begin + lane];
     const bool active = lane < nf;
     const uint32_t foff = active ? f.byte_off - td.chunk0 * 16u : 0u;
+    // the missing sentinel (255 / 65535) is never below a feature's bin count
+    const uint32_t nbins = active ? f.nbins : 0u;
     const uint8_t* rec_base = td.base + td.chunk0 * 16u;
     // copy assignment: lane = (item group g, row q); items of a row are its
     // record chunks 0..nch-1 and its gradient pair (item nch)
@@ -583,15 +599,21 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
             const uint32_t kq = first < cnt ? min(kStageRows, cnt - first) : 0u;
             const uint8_t* stg = wbuf + (bb % S) * stage_bytes;
             const Pair* gps = reinterpret_cast<const Pair*>(stg + kStageRows * rec_bytes);
-            for (uint32_t q = 0; q < kq; q++) {
-                const uint8_t* p = stg + q * rec_bytes + foff;
-                const uint32_t bin = W == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+            const uint8_t* pr = stg + foff;
+            auto row = [&](uint32_t q) {
+                const uint8_t* p = pr + q * rec_bytes;
+                uint32_t bin = W == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+                bin = bin < nbins ? bin : discard;
                 const Pair gp = gps[q];
-                if (active && bin != td.missing && bin < f.nbins) {
-                    const uint32_t idx = bin * 32u + lane;
-                    plane_add(glo, ghi, idx, gp.g);
-                    plane_add(hlo, hhi, idx, gp.h);
-                }
+                uint32_t* w = hlane + bin * 128u;
+                add64_planes(w, w + 32, gp.g);
+                add64_planes(w + 64, w + 96, gp.h);
+            };
+            if (kq == kStageRows) {
+#pragma unroll
+                for (uint32_t q = 0; q < kStageRows; q++) row(q);
+            } else {
+                for (uint32_t q = 0; q < kq; q++) row(q);
             }
             __syncwarp();
             issue(bb + S);
@@ -600,15 +622,16 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
         __syncthreads();
         Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
         for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
-            const unsigned long long g = ((unsigned long long)ghi[j] << 32) | glo[j];
-            const unsigned long long h = ((unsigned long long)hhi[j] << 32) | hlo[j];
+            const uint32_t t = j & 31u, bb = j >> 5;
+            uint32_t* w = sm + bb * 128u + t;
+            const unsigned long long g = ((unsigned long long)w[32] << 32) | w[0];
+            const unsigned long long h = ((unsigned long long)w[96] << 32) | w[64];
             if (g | h) {
-                const uint32_t t = j & 31u, bb = j >> 5;
                 const TileFeat ft = tfeat[td.feat_begin + t];
                 const uint32_t gidx = ft.global_off + bb;
                 if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
                 if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
-                glo[j] = 0u; ghi[j] = 0u; hlo[j] = 0u; hhi[j] = 0u;
+                w[0] = 0u; w[32] = 0u; w[64] = 0u; w[96] = 0u;
             }
         }
         __syncthreads();
@@ -1191,6 +1214,40 @@ __global__ void k_transpose_block(const uint8_t* __restrict__ src, uint8_t* __re
     }
 }
 
+// Column-major copy of a block's row records (feature i of the block at
+// cols + i * n_rows * W): the partition passes gather one bin per row, and
+// the rows of a node are ascending ids, so at the shallow levels neighbouring
+// rows of a node share the 32-byte sectors of a column but never a record's.
+// Tiled transpose: a CTA stages kTrRows records in shared memory with
+// coalesced word loads (row pitch stride + 4 bytes, so the column reads hit
+// distinct banks), then writes each feature's kTrRows bins contiguously.
+constexpr uint32_t kTrRows = 256;
+template <int W>
+__global__ void __launch_bounds__(256) k_records_to_columns(const uint8_t* __restrict__ rec, uint32_t stride,
+                                                            uint64_t n_rows, uint32_t n_feats,
+                                                            uint8_t* __restrict__ cols) {
+    extern __shared__ uint32_t tile[];
+    const uint32_t wpr = stride / 4, pitch = wpr + 1;  // words per record, padded pitch
+    for (uint64_t r0 = (uint64_t)blockIdx.x * kTrRows; r0 < n_rows; r0 += (uint64_t)gridDim.x * kTrRows) {
+        const uint32_t rows = (uint32_t)min((uint64_t)kTrRows, n_rows - r0);
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(rec + r0 * stride);
+        for (uint32_t i = threadIdx.x; i < rows * wpr; i += blockDim.x) {
+            const uint32_t r = i / wpr, w = i - r * wpr;
+            tile[r * pitch + w] = src[i];
+        }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < rows * n_feats; i += blockDim.x) {
+            const uint32_t f = i / rows, r = i - f * rows;
+            const uint8_t* row = reinterpret_cast<const uint8_t*>(tile + r * pitch);
+            if (W == 2)
+                reinterpret_cast<uint16_t*>(cols)[f * n_rows + r0 + r] = *reinterpret_cast<const uint16_t*>(row + f * 2);
+            else
+                cols[f * n_rows + r0 + r] = row[f];
+        }
+        __syncthreads();
+    }
+}
+
 // ------------------------------------------------------------------ launchers
 static unsigned grad_grid(uint32_t n) {
     unsigned b = (n + 255) / 256;
@@ -1305,6 +1362,18 @@ void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, c
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s) {
     count_launch();
     k_iota<<<grad_grid(n), 256, 0, s>>>(rows, n);
+}
+void launch_records_to_columns(int width, const uint8_t* rec, uint32_t stride, uint64_t n_rows, uint32_t n_feats,
+                               uint8_t* cols, cudaStream_t s) {
+    const size_t smem = (size_t)kTrRows * (stride + 4);
+    if (smem > 48 * 1024) {
+        cudaFuncSetAttribute(k_records_to_columns<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_records_to_columns<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
+    const uint32_t grid = (uint32_t)std::min<uint64_t>((n_rows + kTrRows - 1) / kTrRows, 148ull * 8);
+    count_launch();
+    if (width == 2) k_records_to_columns<2><<<grid, 256, smem, s>>>(rec, stride, n_rows, n_feats, cols);
+    else k_records_to_columns<1><<<grid, 256, smem, s>>>(rec, stride, n_rows, n_feats, cols);
 }
 void launch_transpose(int width, const uint8_t* src, uint8_t* dst, uint32_t n_rows, uint32_t n_feats,
                       uint32_t stride, uint64_t row0, cudaStream_t s) {

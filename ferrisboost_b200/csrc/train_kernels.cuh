@@ -46,7 +46,9 @@ struct TileFeat {
     uint32_t global_off;  // first bin in the node histogram
 };
 
-// Per-feature bin locator for partitions.
+// Per-feature bin locator for partitions: the bin of row r is at
+// base + r * stride + byte_off (row records, or a column-major copy with
+// stride = width and byte_off = 0).
 struct FeatLoc {
     const uint8_t* base;
     uint32_t stride;
@@ -184,6 +186,8 @@ void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
                       cudaStream_t s);
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s);
+void launch_records_to_columns(int width, const uint8_t* rec, uint32_t stride, uint64_t n_rows, uint32_t n_feats,
+                               uint8_t* cols, cudaStream_t s);
 void launch_transpose(int width, const uint8_t* src, uint8_t* dst, uint32_t n_rows, uint32_t n_feats,
                       uint32_t stride, uint64_t row0, cudaStream_t s);
 
