@@ -1123,6 +1123,11 @@ ExplainModel::ExplainModel(int device, uint32_t n_features, uint32_t n_trees, co
         FB_CUDA_CHECK(cudaMemcpyAsync(cat_words_.p, cat_words, 4 * n_cat_words, cudaMemcpyHostToDevice, s_));
     make_shap_rule(rule_nodes_, rule_weights_);
     FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    h_nodes_ = std::move(nodes);
+    h_tree_off_.assign(tree_off, tree_off + n_trees + 1);
+    h_coff_ = std::move(coff);
+    h_clen_ = std::move(clen);
+    if (n_cat_words) h_cat_words_.assign(cat_words, cat_words + n_cat_words);
     dm_.nodes = nodes_.as<DevNode>();
     dm_.tree_off = tree_off_.as<uint32_t>();
     dm_.cat_off = cat_off_.as<uint32_t>();
@@ -1147,6 +1152,24 @@ void ExplainModel::predict_device(const float* X, uint64_t n, float* out, cudaSt
 
 void ExplainModel::shap_device(const float* X, uint64_t n, float* out, cudaStream_t s) {
     FB_CUDA_CHECK(cudaSetDevice(device_));
+    // path TreeSHAP unless a model shape needs the node-by-node kernel, or
+    // FBGPU_SHAP=dfs asks for it (the reference's exact f32 operation order)
+    const char* sel = std::getenv("FBGPU_SHAP");
+    const bool dfs = sel && std::string(sel) == "dfs";
+    if (!dfs && ShapPaths::smem_bytes(F_) <= 227 * 1024) {
+        if (!paths_built_) {
+            paths_.build(h_nodes_, h_tree_off_.data(), T_, F_, h_coff_, h_clen_, h_cat_words_.data(), rule_nodes_,
+                         rule_weights_);
+            if (paths_.supported) paths_.upload(s_);
+            FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+            paths_built_ = true;
+        }
+        if (paths_.supported) {
+            paths_.launch(X, n, F_, base_margin_, root_mean_, out, s);
+            FB_CUDA_CHECK(cudaGetLastError());
+            return;
+        }
+    }
     const uint64_t T = shap_threads(n);
     if (T > scratch_threads_) {
         path_.alloc(4 * T * F_);

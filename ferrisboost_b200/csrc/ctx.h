@@ -215,6 +215,23 @@ class TrainCtx {
     double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0;
 };
 
+// Root-to-leaf path form of a model's trees for the path TreeSHAP kernel
+// (shap_paths.cu): per path element the feature's condition and the
+// row-independent quadrature factors.
+struct ShapPaths {
+    int M = 4, KMAX = 8;              // quadrature points, features per path (kernel template)
+    bool supported = false;           // false: a path the kernel cannot represent (use the DFS kernel)
+    uint32_t n_elems = 0;
+    std::vector<uint32_t> words, chunk_off, masks;
+    DevMem d_words, d_chunks, d_masks;
+    void build(const std::vector<DevNode>& nodes, const uint32_t* tree_off, uint32_t n_trees, uint32_t F,
+               const std::vector<uint32_t>& cat_off, const std::vector<uint32_t>& cat_len, const uint32_t* cat_words,
+               const float* rule_nodes, const float* rule_weights);
+    void upload(cudaStream_t s);
+    static size_t smem_bytes(uint32_t F);
+    void launch(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out, cudaStream_t s) const;
+};
+
 class ExplainModel {
    public:
     ExplainModel(int device, uint32_t n_features, uint32_t n_trees, const uint32_t* tree_off, const int32_t* left,
@@ -237,6 +254,11 @@ class ExplainModel {
     cudaStream_t s_ = nullptr;
     DevModel dm_{};
     float rule_nodes_[kShapPoints], rule_weights_[kShapPoints];
+    // host copy of the trees for the path form, built at the first SHAP call
+    std::vector<DevNode> h_nodes_;
+    std::vector<uint32_t> h_tree_off_, h_coff_, h_clen_, h_cat_words_;
+    ShapPaths paths_;
+    bool paths_built_ = false;
 };
 
 // Sets the message fbgpu_last_error(NULL) returns on this thread.

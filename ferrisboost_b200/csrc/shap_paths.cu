@@ -1,0 +1,427 @@
+// TreeSHAP over root-to-leaf paths (sm_100a).
+//
+// The reference's QuadratureTreeSHAP (model/explain.rs:198-400) walks every
+// node of a tree per row and divides at every edge.  Its result is, for each
+// leaf L with value v and each feature f on the path to L (repeated splits
+// on f merged into one element):
+//
+//     phi_f += v (o_f - z_f) sum_i w_i prod_{g != f} (z_g + (o_g - z_g) y_i)
+//
+// where z_g is the product of the cover ratios (branch_weight) of g's edges
+// on the path, o_g is 1 when the row satisfies every one of g's conditions on
+// the path and 0 otherwise, and (y_i, w_i) is the quadrature rule on [0, 1].
+// The integrand is a polynomial of degree < k (k = features on the path), so
+// any rule exact to that degree gives the reference's value; the reference's
+// 8-point endpoint-squared rule is exact for k <= 8.  Models whose paths all
+// have k <= 8 use a 4-point Gauss-Legendre rule (also exact); others use the
+// reference's own rule, so both compute the same quadrature sum.  The result
+// differs from the reference only by f32 rounding (the parity bar is 1e-5).
+//
+// Everything except o_g is independent of the row, so the host precomputes
+// per path element and rule point a_o = z + (o - z) y (o = 0, 1), b_o = w / a_o
+// and c_o = v (o - z).  Per row and path the device only tests the row
+// against each element's condition (an interval [lo, hi), the NaN default
+// direction, or a category mask), multiplies P_i = prod_g a_{o_g,i}, and adds
+// c_{o_f} sum_i b_{o_f,i} P_i to phi_f: no division, no recursion, no
+// per-thread stack.
+//
+// Layout: one thread per row; the CTA's rows keep x and phi in shared memory
+// ([feature][thread], conflict-free), and the path elements stream through
+// shared memory in chunks of whole paths, read by every thread at the same
+// address (broadcast).
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "ctx.h"
+
+namespace fbg {
+
+namespace {
+
+constexpr int kPathThreads = 128;
+constexpr uint32_t kChunkBytes = 24 * 1024;
+
+// Element record, in 32-bit words: [0] feature | flags << 24, [1] lo (f32) or
+// category-mask index, [2] hi (f32), [3] elements in the path (first element
+// of a path only), then a0[M], a1[M], b0[M], b1[M], c0, c1 and two pad words.
+constexpr uint32_t kElemNanOk = 1u, kElemCat = 2u, kElemOutOk = 4u;
+template <int M> __host__ __device__ constexpr uint32_t elem_words() { return 4 + 4 * M + 4; }
+
+// Row test of one path element: every edge x < c (left) or x >= c (right),
+// merged into lo <= x < hi (hi = NaN when no edge bounds it above); NaN rows
+// follow the default directions; categorical rows test the intersection of
+// the edges' category sets (data/categorical.rs:330-345).
+__device__ __forceinline__ bool elem_test(uint4 h, float x, const uint32_t* __restrict__ cat_masks) {
+    const uint32_t fl = h.x >> 24;
+    if (x != x) return (fl & kElemNanOk) != 0;
+    if (fl & kElemCat) {
+        if (x < 0.0f || x >= 16777216.0f) return (fl & kElemOutOk) != 0;
+        const uint32_t code = (uint32_t)x;
+        return code < 256u ? ((cat_masks[h.y * 8u + (code >> 5)] >> (code & 31u)) & 1u) != 0 : (fl & kElemOutOk) != 0;
+    }
+    return !(x < __uint_as_float(h.y)) && !(x >= __uint_as_float(h.z));
+}
+
+template <int M>
+__device__ __forceinline__ void load_vec(const uint32_t* p, float (&v)[M]) {
+#pragma unroll
+    for (int q = 0; q < M / 4; q++) {
+        const float4 f = reinterpret_cast<const float4*>(p)[q];
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+    }
+}
+
+// R rows per thread (rows t and t + kPathThreads of a CTA tile): the path
+// data each element loads serves R independent product chains.
+template <int M, int KMAX, int R>
+__global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __restrict__ X, uint64_t n, uint32_t F,
+                                                             const uint4* __restrict__ elems,
+                                                             const uint32_t* __restrict__ chunk_off,
+                                                             uint32_t n_chunks, const uint32_t* __restrict__ cat_masks,
+                                                             float bias, float root_mean, float* __restrict__ out) {
+    constexpr uint32_t EW = elem_words<M>();
+    constexpr uint32_t TR = kPathThreads * R;  // rows per CTA tile
+    extern __shared__ __align__(16) uint32_t smem[];
+    // phi accumulates in f64: a value receives one term per path that tests
+    // its feature (tens of thousands per row), where the reference adds one
+    // per-tree sum per tree; f32 accumulation would drift past the 1e-5 bar
+    double* ph = reinterpret_cast<double*>(smem);                       // [F][TR]
+    float* xs = reinterpret_cast<float*>(ph + (size_t)F * TR);          // [F][TR]
+    uint32_t* ch = reinterpret_cast<uint32_t*>(xs + (size_t)F * TR);    // chunk of elements
+    const uint32_t t = threadIdx.x;
+    for (uint64_t r0 = (uint64_t)blockIdx.x * TR; r0 < n; r0 += (uint64_t)gridDim.x * TR) {
+        const uint32_t rows = (uint32_t)min((uint64_t)TR, n - r0);
+        __syncthreads();
+        for (uint32_t i = t; i < rows * F; i += kPathThreads) {
+            const uint32_t rr = i / F, f = i - rr * F;
+            xs[f * TR + rr] = X[r0 * F + i];
+        }
+        for (uint32_t i = t; i < F * TR; i += kPathThreads) ph[i] = 0.0;
+        for (uint32_t c = 0; c < n_chunks; c++) {
+            const uint32_t e0 = chunk_off[c], e1 = chunk_off[c + 1];
+            __syncthreads();
+            const uint4* src = elems + (size_t)e0 * (EW / 4);
+            uint4* dst = reinterpret_cast<uint4*>(ch);
+            for (uint32_t i = t; i < (e1 - e0) * (EW / 4); i += kPathThreads) dst[i] = src[i];
+            __syncthreads();
+            if (t >= rows) continue;
+            uint32_t e = 0;
+            while (e < e1 - e0) {
+                const uint32_t k = ch[e * EW + 3];
+                float P[R][M];
+#pragma unroll
+                for (int r = 0; r < R; r++)
+#pragma unroll
+                    for (int i = 0; i < M; i++) P[r][i] = 1.0f;
+                uint32_t obits[R], feats[KMAX];
+#pragma unroll
+                for (int r = 0; r < R; r++) obits[r] = 0;
+#pragma unroll
+                for (int j = 0; j < KMAX; j++) {
+                    if ((uint32_t)j < k) {
+                        const uint32_t* E = ch + (e + j) * EW;
+                        const uint4 h = *reinterpret_cast<const uint4*>(E);
+                        const uint32_t f = h.x & 0xffffffu;
+                        feats[j] = f;
+                        float a0[M], a1[M];
+                        load_vec<M>(E + 4, a0);
+                        load_vec<M>(E + 4 + M, a1);
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            const bool o = elem_test(h, xs[f * TR + t + r * kPathThreads], cat_masks);
+                            obits[r] |= (o ? 1u : 0u) << j;
+#pragma unroll
+                            for (int i = 0; i < M; i++) P[r][i] = __fmul_rn(P[r][i], o ? a1[i] : a0[i]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < KMAX; j++) {
+                    if ((uint32_t)j < k) {
+                        const uint32_t* E = ch + (e + j) * EW;
+                        float b0[M], b1[M];
+                        load_vec<M>(E + 4 + 2 * M, b0);
+                        load_vec<M>(E + 4 + 3 * M, b1);
+                        const float2 cc = *reinterpret_cast<const float2*>(E + 4 + 4 * M);
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            const bool o = (obits[r] >> j) & 1u;
+                            float sacc = 0.0f;
+#pragma unroll
+                            for (int i = 0; i < M; i++) sacc = __fmaf_rn(o ? b1[i] : b0[i], P[r][i], sacc);
+                            double* p = ph + feats[j] * TR + t + r * kPathThreads;
+                            *p = __dadd_rn(*p, (double)__fmul_rn(o ? cc.y : cc.x, sacc));
+                        }
+                    }
+                }
+                e += k;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const uint32_t rr = t + r * kPathThreads;
+            if (rr < rows) {
+                float* o = out + (r0 + rr) * (uint64_t)(F + 1);
+                for (uint32_t f = 0; f < F; f++) o[f] = __double2float_rn(ph[f * TR + rr]);
+                o[F] = __fadd_rn(__fadd_rn(0.0f, root_mean), bias);  // explain.rs:725-726
+            }
+        }
+    }
+}
+
+}  // namespace
+
+// Gauss-Legendre rule with m points on [0, 1] (Golub-Welsch-free Newton on
+// the Legendre recurrence, f64).
+static void gauss_legendre01(int m, double* y, double* w) {
+    for (int i = 0; i < m; i++) {
+        double x = std::cos(3.14159265358979323846 * (i + 0.75) / (m + 0.5));
+        double dp = 1.0;
+        for (int it = 0; it < 100; it++) {
+            double p0 = 1.0, p1 = x;
+            for (int k = 2; k <= m; k++) {
+                const double pk = ((2.0 * k - 1.0) * x * p1 - (k - 1.0) * p0) / k;
+                p0 = p1;
+                p1 = pk;
+            }
+            dp = m * (x * p1 - p0) / (x * x - 1.0);
+            const double dx = p1 / dp;
+            x -= dx;
+            if (std::fabs(dx) < 1e-16) break;
+        }
+        y[i] = 0.5 * (x + 1.0);
+        w[i] = 1.0 / ((1.0 - x * x) * dp * dp);  // (2 / ((1 - x^2) P'^2)) / 2
+    }
+}
+
+void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_off, uint32_t n_trees, uint32_t F,
+                      const std::vector<uint32_t>& cat_off, const std::vector<uint32_t>& cat_len,
+                      const uint32_t* cat_words, const float* rule_nodes, const float* rule_weights) {
+    struct El {
+        uint32_t feat;
+        double z;
+        float lo, hi;
+        bool nan_ok, cat, out_ok;
+        uint32_t mask[8];
+    };
+    struct Path {
+        float v;
+        std::vector<El> els;
+    };
+    supported = true;
+    std::vector<Path> paths;
+    std::vector<int> pos(F, -1);
+    std::vector<El> st;
+    uint32_t kmax = 0;
+    for (uint32_t t = 0; t < n_trees; t++) {
+        const uint32_t a = tree_off[t];
+        const DevNode* nd = nodes.data() + a;
+        if ((nd[0].meta >> 24) & kNodeLeaf) continue;  // explain.rs:393-400: a leaf root adds nothing
+        // explicit DFS: (node, next child to visit, undo record)
+        struct Fr {
+            uint32_t i;
+            int stage;
+            int slot;
+            El saved;
+            bool fresh;
+        };
+        std::vector<Fr> stack;
+        stack.push_back(Fr{0, 0, -1, El{}, false});
+        while (!stack.empty()) {
+            Fr& fr = stack.back();
+            const DevNode& d = nd[fr.i];
+            if ((d.meta >> 24) & kNodeLeaf) {
+                paths.push_back(Path{d.val, st});
+                kmax = std::max<uint32_t>(kmax, (uint32_t)st.size());
+                stack.pop_back();
+                continue;
+            }
+            // undo the previous child's edge
+            if (fr.stage > 0 && fr.slot >= 0) {
+                if (fr.fresh) {
+                    pos[st.back().feat] = -1;
+                    st.pop_back();
+                } else {
+                    st[fr.slot] = fr.saved;
+                }
+            }
+            if (fr.stage == 2) {
+                stack.pop_back();
+                continue;
+            }
+            const bool left = fr.stage == 0;
+            const uint32_t child = (uint32_t)(left ? d.left : d.right);
+            fr.stage++;
+            const uint32_t f = d.meta & 0xffffffu;
+            const uint32_t flags = d.meta >> 24;
+            // explain.rs:182-192 branch_weight in f32
+            float cw;
+            const float pc = d.hess, cc = nd[child].hess;
+            if (pc <= 0.0f) {
+                cw = 0.5f;
+            } else {
+                cw = cc / pc;
+                if (cw < 1e-12f) cw = 1e-12f;
+            }
+            int slot = pos[f];
+            fr.fresh = slot < 0;
+            if (fr.fresh) {
+                El e{};
+                e.feat = f;
+                e.z = 1.0;
+                e.lo = -INFINITY;
+                e.hi = INFINITY;
+                e.nan_ok = true;
+                e.cat = (flags & kNodeCategorical) != 0;
+                e.out_ok = true;
+                for (auto& w : e.mask) w = 0xffffffffu;
+                st.push_back(e);
+                slot = (int)st.size() - 1;
+                pos[f] = slot;
+            } else {
+                fr.saved = st[slot];
+            }
+            fr.slot = slot;
+            El& e = st[slot];
+            e.z *= (double)cw;
+            e.nan_ok = e.nan_ok && (((flags & kNodeDefaultLeft) != 0) == left);
+            if (flags & kNodeCategorical) {
+                const uint32_t co = cat_off[a + fr.i], cl = cat_len[a + fr.i];
+                if (cl > 8) {  // codes >= 256 in a set: the 8-word masks cannot hold it
+                    supported = false;
+                    return;
+                }
+                for (uint32_t wi = 0; wi < 8; wi++) {
+                    const uint32_t s = wi < cl ? cat_words[co + wi] : 0u;
+                    e.mask[wi] &= left ? ~s : s;
+                }
+                e.out_ok = e.out_ok && left;
+            } else if (left) {
+                e.hi = std::min(e.hi, d.val);
+            } else {
+                e.lo = std::max(e.lo, d.val);
+            }
+            stack.push_back(Fr{child, 0, -1, El{}, false});
+        }
+    }
+    // rule: 4-point Gauss-Legendre when every path has at most 8 features,
+    // else the reference's 8-point endpoint-squared rule
+    M = kmax <= 8 ? 4 : 8;
+    KMAX = M == 4 ? 8 : 14;
+    if (kmax > 14) {
+        supported = false;
+        return;
+    }
+    double y[8], w[8];
+    if (M == 4) {
+        gauss_legendre01(4, y, w);
+    } else {
+        for (int i = 0; i < 8; i++) { y[i] = rule_nodes[i]; w[i] = rule_weights[i]; }
+    }
+    const uint32_t EW = 4 + 4 * M + 4;
+    const uint32_t chunk_elems = kChunkBytes / (EW * 4);
+    words.clear();
+    masks.clear();
+    chunk_off.assign(1, 0);
+    uint32_t in_chunk = 0, total = 0;
+    auto clamp = [](double x) {
+        if (!(x == x)) return 0.0f;
+        if (x > FLT_MAX) return FLT_MAX;
+        if (x < -FLT_MAX) return -FLT_MAX;
+        return (float)x;
+    };
+    for (const Path& p : paths) {
+        const uint32_t k = (uint32_t)p.els.size();
+        if (in_chunk + k > chunk_elems) {
+            chunk_off.push_back(total);
+            in_chunk = 0;
+        }
+        for (uint32_t j = 0; j < k; j++) {
+            const El& e = p.els[j];
+            uint32_t rec[4 + 4 * 8 + 4] = {};
+            const uint32_t fl = (e.nan_ok ? kElemNanOk : 0u) | (e.cat ? kElemCat : 0u) | (e.out_ok ? kElemOutOk : 0u);
+            rec[0] = (e.feat & 0xffffffu) | (fl << 24);
+            if (e.cat) {
+                rec[1] = (uint32_t)(masks.size() / 8);
+                masks.insert(masks.end(), e.mask, e.mask + 8);
+                rec[2] = 0;
+            } else {
+                // no upper bound: hi = NaN, so the test !(x >= hi) always passes (x = +inf included)
+                const float hi = e.hi == INFINITY ? NAN : e.hi;
+                std::memcpy(&rec[1], &e.lo, 4);
+                std::memcpy(&rec[2], &hi, 4);
+            }
+            rec[3] = j == 0 ? k : 0u;
+            float* tab = reinterpret_cast<float*>(rec + 4);
+            for (int i = 0; i < M; i++) {
+                const double a0 = e.z * (1.0 - y[i]), a1 = e.z + (1.0 - e.z) * y[i];
+                tab[i] = clamp(a0);
+                tab[M + i] = clamp(a1);
+                tab[2 * M + i] = clamp(w[i] / a0);
+                tab[3 * M + i] = clamp(w[i] / a1);
+            }
+            tab[4 * M] = clamp((double)p.v * (0.0 - e.z));
+            tab[4 * M + 1] = clamp((double)p.v * (1.0 - e.z));
+            words.insert(words.end(), rec, rec + EW);
+        }
+        in_chunk += k;
+        total += k;
+    }
+    chunk_off.push_back(total);
+    if (chunk_off.size() >= 2 && chunk_off[chunk_off.size() - 2] == total) chunk_off.pop_back();
+    n_elems = total;
+}
+
+void ShapPaths::upload(cudaStream_t s) {
+    d_words.alloc(std::max<size_t>(words.size(), 4) * 4);
+    d_chunks.alloc(chunk_off.size() * 4);
+    d_masks.alloc(std::max<size_t>(masks.size(), 8) * 4);
+    if (!words.empty())
+        FB_CUDA_CHECK(cudaMemcpyAsync(d_words.p, words.data(), words.size() * 4, cudaMemcpyHostToDevice, s));
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_chunks.p, chunk_off.data(), chunk_off.size() * 4, cudaMemcpyHostToDevice, s));
+    if (!masks.empty())
+        FB_CUDA_CHECK(cudaMemcpyAsync(d_masks.p, masks.data(), masks.size() * 4, cudaMemcpyHostToDevice, s));
+}
+
+// rows per thread of the launch (FBGPU_SHAP_ROWS=1 or 2)
+static int path_rows() {
+    const char* e = std::getenv("FBGPU_SHAP_ROWS");
+    return e && std::atoi(e) == 1 ? 1 : 2;
+}
+
+size_t ShapPaths::smem_bytes(uint32_t F) { return (size_t)F * kPathThreads * path_rows() * (8 + 4) + kChunkBytes; }
+
+void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out,
+                       cudaStream_t s) const {
+    if (n == 0) return;
+    const uint32_t n_chunks = (uint32_t)chunk_off.size() - 1;
+    const size_t smem = smem_bytes(F);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int R = path_rows();
+    const uint64_t tiles = (n + (uint64_t)kPathThreads * R - 1) / ((uint64_t)kPathThreads * R);
+#define FB_SP(MM, KK, RR)                                                                                            \
+    do {                                                                                                             \
+        cudaFuncSetAttribute(k_shap_paths<MM, KK, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
+        int per_sm = 1;                                                                                              \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_shap_paths<MM, KK, RR>, kPathThreads, smem);        \
+        const uint64_t grid = std::min<uint64_t>(tiles, (uint64_t)sms * std::max(per_sm, 1));                        \
+        count_launch();                                                                                              \
+        k_shap_paths<MM, KK, RR><<<(unsigned)grid, kPathThreads, smem, s>>>(                                        \
+            X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(), bias, root_mean, \
+            out);                                                                                                    \
+    } while (0)
+    if (M == 4) {
+        if (R == 2) FB_SP(4, 8, 2); else FB_SP(4, 8, 1);
+    } else {
+        if (R == 2) FB_SP(8, 14, 2); else FB_SP(8, 14, 1);
+    }
+#undef FB_SP
+}
+
+}  // namespace fbg

@@ -126,14 +126,49 @@ def test_predict_and_shap_match_oracle(oracle):
     np.testing.assert_allclose(phi.sum(axis=1), ref.predict_margin(Xt), atol=2e-4)
 
 
-def test_shap_bit_equal_to_oracle(oracle):
-    # the kernel keeps the CPU engine's f32 operation order
+def test_shap_bit_equal_to_oracle(oracle, monkeypatch):
+    # the node-by-node kernel keeps the CPU engine's f32 operation order
     X, y = _synthetic(8000, 12, seed=6, missing=0.03)
     p = dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=64)
     ref = oracle.train(X, y, n_rounds=8, **p)
     Xt, _ = _synthetic(1000, 12, seed=78, missing=0.03)
     m = fb.train(p, X, label=y, num_boost_round=8)
+    monkeypatch.setenv("FBGPU_SHAP", "dfs")
     assert np.array_equal(m.predict(Xt, pred_contribs=True).view(np.uint32), ref.shap(Xt).view(np.uint32))
+
+
+def test_path_shap_matches_node_kernel_and_oracle(oracle, monkeypatch):
+    # the path kernel (default) against the node-by-node kernel on a
+    # 200-tree depth-8 model, and against the oracle; rows sum to margins
+    X, y = _synthetic(40000, 28, seed=15, missing=0.02)
+    p = dict(objective="binary:logistic", max_depth=8, eta=0.1, max_bin=256)
+    m = fb.train(p, X, label=y, num_boost_round=200)
+    Xt, _ = _synthetic(5000, 28, seed=79, missing=0.02)
+    Xt[::37, 3] = np.inf
+    Xt[::41, 5] = -np.inf
+    phi = m.predict(Xt, pred_contribs=True)
+    monkeypatch.setenv("FBGPU_SHAP", "dfs")
+    dfs = m.predict(Xt, pred_contribs=True)
+    assert np.max(np.abs(phi - dfs)) <= 1e-5
+    np.testing.assert_allclose(phi.sum(axis=1), m.predict(Xt, output_margin=True), atol=2e-4)
+    ref = oracle.train(X, y, n_rounds=20, **p)
+    m20 = fb.train(p, X, label=y, num_boost_round=20)
+    monkeypatch.delenv("FBGPU_SHAP")
+    assert np.max(np.abs(m20.predict(Xt[:1000], pred_contribs=True) - ref.shap(Xt[:1000]))) <= 1e-5
+
+
+def test_path_shap_deep_paths_use_the_reference_rule(oracle):
+    # depth-14 trees over 40 features: paths with more than 8 features, where
+    # the reference's 8-point rule is not exact and the path kernel uses it too
+    rng = np.random.default_rng(33)
+    X = rng.standard_normal((6000, 40)).astype(np.float32)
+    z = X[:, :12].sum(1) + X[:, 12] * X[:, 13]
+    y = (rng.random(6000) < 1 / (1 + np.exp(-z))).astype(np.float32)
+    p = dict(objective="binary:logistic", max_depth=14, eta=0.3, max_bin=64, min_child_weight=0.0)
+    m = fb.train(p, X, label=y, num_boost_round=4)
+    ref = oracle.train(X, y, n_rounds=4, **p)
+    Xt = rng.standard_normal((800, 40)).astype(np.float32)
+    assert np.max(np.abs(m.predict(Xt, pred_contribs=True) - ref.shap(Xt))) <= 1e-5
 
 
 def test_shap_deep_trees_and_categorical(oracle):
@@ -152,6 +187,17 @@ def test_shap_deep_trees_and_categorical(oracle):
     phi = m.predict(Xt, pred_contribs=True)
     assert np.max(np.abs(phi - ref.shap(Xt))) <= 1e-5
     np.testing.assert_allclose(phi.sum(axis=1), ref.predict_margin(Xt), atol=2e-4)
+    # unseen, negative, fractional, very large and missing category codes,
+    # and missing numeric values (every branch of the category test)
+    Xo = X[2000:2600].copy()
+    Xo[0::7, 5] = np.nan
+    Xo[1::7, 5] = -1.0
+    Xo[2::7, 6] = 25.0
+    Xo[3::7, 6] = 300.0
+    Xo[4::7, 5] = 2.5
+    Xo[5::7, 6] = 3.0e7
+    Xo[6::7, 0] = np.nan
+    assert np.max(np.abs(m.predict(Xo, pred_contribs=True) - ref.shap(Xo))) <= 1e-5
 
 
 def test_json_is_valid_xgboost_schema():
