@@ -14,6 +14,7 @@
 #include <charconv>
 #include <chrono>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <limits>
 #include <memory>
@@ -389,7 +390,18 @@ Dataset* dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_
     d->device = device;
     d->cat.assign(F, 0);
     if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
+    // FBGPU_TRACE=1: wall time of each preparation phase on stderr
+    static const bool trace = std::getenv("FBGPU_TRACE") != nullptr;
+    auto tp = std::chrono::steady_clock::now();
+    auto phase = [&](const char* what) {
+        if (!trace) return;
+        const auto now = std::chrono::steady_clock::now();
+        std::fprintf(stderr, "[fbgpu] dataset %-14s %8.3f ms\n", what,
+                     std::chrono::duration<double, std::milli>(now - tp).count());
+        tp = now;
+    };
     fbg::DeviceMatrix M(X, n, F, s);
+    phase("rows to device");
     if (cuts) {
         check_cuts(offsets, F);
         d->offsets.assign(offsets, offsets + F + 1);
@@ -407,6 +419,7 @@ Dataset* dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_
             d->offsets.push_back((uint32_t)d->cuts.size());
         }
     }
+    phase("sketch");
     plan_blocks(*d);
     fbg::DevMem d_cuts, d_off, d_cat;
     d_cuts.alloc(std::max<size_t>(d->cuts.size(), 1) * 4);
@@ -423,6 +436,7 @@ Dataset* dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_
         reserved |= M.bin_block(b.feats.data(), (uint32_t)b.feats.size(), b.width, d_cuts.as<float>(),
                                 d_off.as<uint32_t>(), d_cat.as<uint8_t>(), b.dev->as<uint8_t>(), b.stride);
     }
+    phase("binning");
     if (reserved)  // dense.rs:300
         throw InputError("feature contains f32::MAX, reserved for missing-value split boundaries; rescale this feature");
     return d.release();
