@@ -422,13 +422,33 @@ class Model:
         lib().fb_model_tree(self._h, t, *[_lib.ptr(v, c) for v, c in zip(a.values(), ct)])
         return a
 
-    def predict(self, data: Any, output_margin: bool = False, pred_contribs: bool = False, device=None):
+    def predict(self, data: Any, output_margin: bool = False, pred_contribs: bool = False, device=None, *,
+                approx_contribs: bool = False, pred_interactions: bool = False, pred_leaf: bool = False):
         """Predictions (probabilities for binary:logistic unless output_margin),
-        or SHAP contributions n x (F+1) with the bias last (pred_contribs)."""
+        or (the reference's _core.Model.predict options): SHAP contributions
+        n x (F+1) with the bias last (pred_contribs; Saabas values with
+        approx_contribs), SHAP interaction values n x (F+1) x (F+1)
+        (pred_interactions), or the leaf node index of every tree, n x n_trees
+        as float32 (pred_leaf)."""
         X = _as_matrix(data, self.params.get("missing", float("nan")))
         if X.shape[1] != self.n_features:
             raise ValueError(f"data has {X.shape[1]} features, the model has {self.n_features}")
+        if sum(bool(v) for v in (pred_contribs, pred_interactions, pred_leaf)) > 1:
+            raise ValueError("pred_contribs, pred_interactions and pred_leaf are mutually exclusive")
         dev = self._device(device)
+        kind = None
+        if pred_leaf:
+            kind, shape = 0, (X.shape[0], self.num_trees)
+        elif pred_contribs and approx_contribs:
+            kind, shape = 1, (X.shape[0], X.shape[1] + 1)
+        elif pred_interactions:
+            kind, shape = 2, (X.shape[0], X.shape[1] + 1, X.shape[1] + 1)
+        if kind is not None:
+            out = np.zeros(shape, dtype=np.float32)
+            if lib().fb_model_explain(self._h, kind, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float),
+                                      dev):
+                raise RuntimeError(_err())
+            return out
         if pred_contribs:
             out = np.zeros((X.shape[0], X.shape[1] + 1), dtype=np.float32)
             if lib().fb_model_shap(self._h, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float), dev):

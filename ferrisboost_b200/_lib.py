@@ -100,6 +100,8 @@ SIGNATURES = {
     "fbgpu_predict_device": (C.c_int, [P, P, C.c_uint64, P, P]),
     "fbgpu_shap": (C.c_int, [P, f32p, C.c_uint64, f32p]),
     "fbgpu_shap_device": (C.c_int, [P, P, C.c_uint64, P, P]),
+    "fbgpu_explain": (C.c_int, [P, C.c_int32, f32p, C.c_uint64, f32p]),
+    "fbgpu_explain_device": (C.c_int, [P, C.c_int32, P, C.c_uint64, P, P]),
     # include/fb_engine.h
     "fb_default_params": (None, [C.POINTER(FbParams)]),
     "fb_last_error": (C.c_char_p, []),
@@ -135,6 +137,7 @@ SIGNATURES = {
     "fb_model_tree": (C.c_int64, [P, C.c_uint32, i32p, i32p, u32p, f32p, u8p, f32p, u8p, f32p, f32p, u32p]),
     "fb_model_predict": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
     "fb_model_shap": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
+    "fb_model_explain": (C.c_int32, [P, C.c_int32, f32p, C.c_uint64, f32p, C.c_int32]),
     "fb_model_device": (P, [P, C.c_int32]),
 }
 

@@ -1157,13 +1157,7 @@ void ExplainModel::shap_device(const float* X, uint64_t n, float* out, cudaStrea
     const char* sel = std::getenv("FBGPU_SHAP");
     const bool dfs = sel && std::string(sel) == "dfs";
     if (!dfs && ShapPaths::smem_bytes(F_) <= 227 * 1024) {
-        if (!paths_built_) {
-            paths_.build(h_nodes_, h_tree_off_.data(), T_, F_, h_coff_, h_clen_, h_cat_words_.data(), rule_nodes_,
-                         rule_weights_);
-            if (paths_.supported) paths_.upload(s_);
-            FB_CUDA_CHECK(cudaStreamSynchronize(s_));
-            paths_built_ = true;
-        }
+        ensure_paths();
         if (paths_.supported) {
             paths_.launch(X, n, F_, base_margin_, root_mean_, out, s);
             FB_CUDA_CHECK(cudaGetLastError());
@@ -1179,6 +1173,73 @@ void ExplainModel::shap_device(const float* X, uint64_t n, float* out, cudaStrea
     upload_shap_rule(rule_nodes_, rule_weights_, s);
     launch_shap(dm_, X, n, base_margin_, root_mean_, out, path_.as<float>(), tc_.as<float>(), s);
     FB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ExplainModel::ensure_paths() {
+    if (paths_built_) return;
+    paths_.build(h_nodes_, h_tree_off_.data(), T_, F_, h_coff_, h_clen_, h_cat_words_.data(), rule_nodes_,
+                 rule_weights_);
+    if (paths_.supported) paths_.upload(s_);
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    paths_built_ = true;
+}
+
+uint64_t ExplainModel::explain_width(int kind) const {
+    if (kind == 0) return T_;
+    if (kind == 1) return (uint64_t)F_ + 1;
+    if (kind == 2) return ((uint64_t)F_ + 1) * (F_ + 1);
+    throw InputError("explain kind must be 0 (leaf), 1 (approx contributions) or 2 (interactions)");
+}
+
+// explain.rs:409-421 fill_node_means: float32, children first, then
+// (left mean x left cover + right mean x right cover) / cover.
+static float node_means(const std::vector<DevNode>& nodes, uint32_t base, uint32_t i, std::vector<float>& means) {
+    const DevNode& d = nodes[base + i];
+    float v;
+    if ((d.meta >> 24) & kNodeLeaf) {
+        v = d.val;
+    } else {
+        float res = node_means(nodes, base, (uint32_t)d.left, means) * nodes[base + d.left].hess;
+        res += node_means(nodes, base, (uint32_t)d.right, means) * nodes[base + d.right].hess;
+        v = res / d.hess;
+    }
+    means[base + i] = v;
+    return v;
+}
+
+void ExplainModel::explain_device(int kind, const float* X, uint64_t n, float* out, cudaStream_t s) {
+    FB_CUDA_CHECK(cudaSetDevice(device_));
+    (void)explain_width(kind);
+    if (kind == 0) {
+        launch_pred_leaf(dm_, X, n, out, s);
+    } else if (kind == 1) {
+        if (approx_smem_bytes(F_) > 227 * 1024) throw InputError("approx_contribs on the device supports at most 221 features");
+        if (!means_.p) {
+            std::vector<float> means(std::max<size_t>(h_nodes_.size(), 1), 0.0f);
+            for (uint32_t t = 0; t < T_; t++) node_means(h_nodes_, h_tree_off_[t], 0, means);
+            means_.alloc(4 * means.size());
+            FB_CUDA_CHECK(cudaMemcpyAsync(means_.p, means.data(), 4 * means.size(), cudaMemcpyHostToDevice, s_));
+            FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+        }
+        launch_pred_approx(dm_, means_.as<float>(), X, n, base_margin_, out, s);
+    } else {
+        ensure_paths();
+        if (!paths_.supported)
+            throw InputError("pred_interactions on the device supports category sets below 256 codes and at most 14 "
+                             "features on a path");
+        paths_.launch_inter(X, n, F_, base_margin_, root_mean_, out, s);
+    }
+    FB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ExplainModel::explain_host(int kind, const float* X, uint64_t n, float* out) {
+    const uint64_t w = explain_width(kind);
+    x_.alloc(std::max<uint64_t>(n * F_ * 4, 16));
+    out_.alloc(std::max<uint64_t>(n * w * 4, 16));
+    FB_CUDA_CHECK(cudaMemcpyAsync(x_.p, X, n * F_ * 4, cudaMemcpyHostToDevice, s_));
+    explain_device(kind, x_.as<float>(), n, out_.as<float>(), s_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(out, out_.p, n * w * 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
 }
 
 void ExplainModel::predict_host(const float* X, uint64_t n, float* out) {
@@ -1397,6 +1458,13 @@ fbgpu_status fbgpu_shap(fbgpu_model* m, const float* X, uint64_t n, float* out) 
 }
 fbgpu_status fbgpu_shap_device(fbgpu_model* m, const float* X, uint64_t n, float* out, void* stream) {
     return guard(nullptr, [&] { m->impl.shap_device(X, n, out, (cudaStream_t)stream); });
+}
+fbgpu_status fbgpu_explain(fbgpu_model* m, int32_t kind, const float* X, uint64_t n, float* out) {
+    return guard(nullptr, [&] { m->impl.explain_host(kind, X, n, out); });
+}
+fbgpu_status fbgpu_explain_device(fbgpu_model* m, int32_t kind, const float* X, uint64_t n, float* out,
+                                  void* stream) {
+    return guard(nullptr, [&] { m->impl.explain_device(kind, X, n, out, (cudaStream_t)stream); });
 }
 
 }  // extern "C"

@@ -230,6 +230,12 @@ struct ShapPaths {
     void upload(cudaStream_t s);
     static size_t smem_bytes(uint32_t F);
     void launch(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out, cudaStream_t s) const;
+    // SHAP interaction values over the same paths (warp per row)
+    float rule_w8[8] = {};
+    DevMem d_rule_w;
+    static size_t inter_smem_bytes(uint32_t F, uint32_t warps);
+    static uint32_t inter_warps(uint32_t F);
+    void launch_inter(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out, cudaStream_t s);
 };
 
 class ExplainModel {
@@ -243,6 +249,10 @@ class ExplainModel {
     void shap_device(const float* X, uint64_t n, float* out, cudaStream_t s);
     void predict_host(const float* X, uint64_t n, float* out);
     void shap_host(const float* X, uint64_t n, float* out);
+    // explain.rs Kind::Leaf (0), Contribs { approx: true } (1), Interactions (2)
+    void explain_device(int kind, const float* X, uint64_t n, float* out, cudaStream_t s);
+    void explain_host(int kind, const float* X, uint64_t n, float* out);
+    uint64_t explain_width(int kind) const;
     uint32_t n_features() const { return F_; }
 
    private:
@@ -259,6 +269,8 @@ class ExplainModel {
     std::vector<uint32_t> h_tree_off_, h_coff_, h_clen_, h_cat_words_;
     ShapPaths paths_;
     bool paths_built_ = false;
+    void ensure_paths();
+    DevMem means_;  // Saabas per-node means (explain.rs:409-421), built at the first approx call
 };
 
 // Sets the message fbgpu_last_error(NULL) returns on this thread.

@@ -1192,4 +1192,11 @@ int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32
     }, 1);
 }
 
+int32_t fb_model_explain(fb_model* m, int32_t kind, const float* X, uint64_t n, float* out, int32_t device) {
+    return fbe::guarded([&]() -> int32_t {
+        fbe::device_model(*m, device).explain_host(kind, X, n, out);
+        return 0;
+    }, 1);
+}
+
 }  // extern "C"

@@ -184,6 +184,105 @@ __global__ void __launch_bounds__(128) k_shap(DevModel m, const float* __restric
     }
 }
 
+// explain.rs:690-701 leaf_row: the node index each tree's traversal ends
+// at, as f32, n x n_trees.
+__global__ void k_pred_leaf(DevModel m, const float* __restrict__ X, uint64_t n, float* __restrict__ out) {
+    for (uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; r < n; r += (uint64_t)blockDim.x * gridDim.x) {
+        const float* x = X + r * m.n_features;
+        for (uint32_t t = 0; t < m.n_trees; t++) {
+            const uint32_t base = m.tree_off[t];
+            uint32_t i = 0;
+            for (;;) {
+                const DevNode nd = m.nodes[base + i];
+                if ((nd.meta >> 24) & kNodeLeaf) break;
+                const uint32_t f = nd.meta & 0xffffffu;
+                i = (uint32_t)(node_goes_left(nd, m, base + i, x[f]) ? nd.left : nd.right);
+            }
+            out[r * m.n_trees + t] = (float)i;
+        }
+    }
+}
+
+// explain.rs:729-760 saabas_row (approx_contribs): along each tree's path,
+// the change of the cover-weighted node mean goes to the split feature.
+// `means` are the per-node f32 means of explain.rs:409-421, in node order.
+// Per tree the deltas gather in tc (one feature may split several times on
+// a path), then add to the row's totals, as the reference does; shared
+// memory holds tc and the totals as [feature][thread].
+constexpr int kApproxThreads = 128;
+__global__ void __launch_bounds__(kApproxThreads) k_pred_approx(DevModel m, const float* __restrict__ means,
+                                                                const float* __restrict__ X, uint64_t n, float bias,
+                                                                float* __restrict__ out) {
+    extern __shared__ float sm_approx[];
+    const uint32_t F = m.n_features, nc = F + 1, t = threadIdx.x;
+    float* p = sm_approx;                       // [nc][kApproxThreads]
+    float* tc = sm_approx + nc * kApproxThreads;  // [nc][kApproxThreads]
+    for (uint64_t r0 = (uint64_t)blockIdx.x * kApproxThreads; r0 < n; r0 += (uint64_t)gridDim.x * kApproxThreads) {
+        const uint64_t r = r0 + t;
+        if (r < n) {
+            const float* x = X + r * F;
+            for (uint32_t c = 0; c < nc; c++) { p[c * kApproxThreads + t] = 0.0f; tc[c * kApproxThreads + t] = 0.0f; }
+            for (uint32_t tr = 0; tr < m.n_trees; tr++) {
+                const uint32_t base = m.tree_off[tr];
+                float node_value = means[base];
+                float& tb = tc[F * kApproxThreads + t];
+                tb = __fadd_rn(tb, node_value);
+                uint32_t touched[kMaxShapDepth + 1];
+                uint32_t nt = 0;
+                DevNode nd = m.nodes[base];
+                if (!((nd.meta >> 24) & kNodeLeaf)) {
+                    uint32_t i = 0, split = 0;
+                    while (!((nd.meta >> 24) & kNodeLeaf)) {
+                        split = nd.meta & 0xffffffu;
+                        i = (uint32_t)(node_goes_left(nd, m, base + i, x[split]) ? nd.left : nd.right);
+                        const float nv = means[base + i];
+                        float& ts = tc[split * kApproxThreads + t];
+                        ts = __fadd_rn(ts, __fsub_rn(nv, node_value));
+                        if (nt <= (uint32_t)kMaxShapDepth) touched[nt++] = split;
+                        node_value = nv;
+                        nd = m.nodes[base + i];
+                    }
+                    float& ts = tc[split * kApproxThreads + t];
+                    ts = __fadd_rn(ts, __fsub_rn(nd.val, node_value));
+                }
+                // p[c] += tc[c] for every column; untouched columns hold 0
+                for (uint32_t k = 0; k < nt; k++) {
+                    const uint32_t f = touched[k];
+                    float& tf = tc[f * kApproxThreads + t];
+                    p[f * kApproxThreads + t] = __fadd_rn(p[f * kApproxThreads + t], tf);
+                    tf = 0.0f;
+                }
+                p[F * kApproxThreads + t] = __fadd_rn(p[F * kApproxThreads + t], tb);
+                tb = 0.0f;
+            }
+            float* o = out + r * nc;
+            for (uint32_t c = 0; c < F; c++) o[c] = p[c * kApproxThreads + t];
+            o[F] = __fadd_rn(p[F * kApproxThreads + t], bias);
+        }
+    }
+}
+
+void launch_pred_leaf(const DevModel& m, const float* X, uint64_t n, float* out, cudaStream_t s) {
+    if (n == 0) return;
+    uint64_t blocks = (n + 255) / 256;
+    if (blocks > 148ull * 64) blocks = 148ull * 64;
+    count_launch();
+    k_pred_leaf<<<(unsigned)blocks, 256, 0, s>>>(m, X, n, out);
+}
+
+void launch_pred_approx(const DevModel& m, const float* means, const float* X, uint64_t n, float bias, float* out,
+                        cudaStream_t s) {
+    if (n == 0) return;
+    const size_t smem = 2ull * (m.n_features + 1) * kApproxThreads * sizeof(float);
+    cudaFuncSetAttribute(k_pred_approx, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    uint64_t blocks = (n + kApproxThreads - 1) / kApproxThreads;
+    if (blocks > 148ull * 16) blocks = 148ull * 16;
+    count_launch();
+    k_pred_approx<<<(unsigned)blocks, kApproxThreads, smem, s>>>(m, means, X, n, bias, out);
+}
+
+size_t approx_smem_bytes(uint32_t n_features) { return 2ull * (n_features + 1) * kApproxThreads * sizeof(float); }
+
 void upload_shap_rule(const float* nodes, const float* weights, cudaStream_t s) {
     cudaMemcpyToSymbolAsync(c_rule_nodes, nodes, sizeof(float) * kShapPoints, 0, cudaMemcpyHostToDevice, s);
     cudaMemcpyToSymbolAsync(c_rule_weights, weights, sizeof(float) * kShapPoints, 0, cudaMemcpyHostToDevice, s);

@@ -39,6 +39,10 @@ struct DevModel {
 };
 
 void upload_shap_rule(const float* nodes, const float* weights, cudaStream_t s);
+void launch_pred_leaf(const DevModel& m, const float* X, uint64_t n, float* out, cudaStream_t s);
+void launch_pred_approx(const DevModel& m, const float* means, const float* X, uint64_t n, float bias, float* out,
+                        cudaStream_t s);
+size_t approx_smem_bytes(uint32_t n_features);
 void launch_predict(const DevModel& m, const float* X, uint64_t n, float base_margin, float* out, cudaStream_t s);
 uint64_t shap_threads(uint64_t n);
 void launch_shap(const DevModel& m, const float* X, uint64_t n, float bias, float root_mean, float* out,

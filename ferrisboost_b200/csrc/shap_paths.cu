@@ -46,7 +46,7 @@ constexpr uint32_t kChunkBytes = 24 * 1024;
 
 // Element record, in 32-bit words: [0] feature | flags << 24, [1] lo (f32) or
 // category-mask index, [2] hi (f32), [3] elements in the path (first element
-// of a path only), then a0[M], a1[M], b0[M], b1[M], c0, c1 and two pad words.
+// of a path only), then a0[M], a1[M], b0[M], b1[M], c0, c1, z and a pad word.
 constexpr uint32_t kElemNanOk = 1u, kElemCat = 2u, kElemOutOk = 4u;
 template <int M> __host__ __device__ constexpr uint32_t elem_words() { return 4 + 4 * M + 4; }
 
@@ -169,6 +169,121 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
                 for (uint32_t f = 0; f < F; f++) o[f] = __double2float_rn(ph[f * TR + rr]);
                 o[F] = __fadd_rn(__fadd_rn(0.0f, root_mean), bias);  // explain.rs:725-726
             }
+        }
+    }
+}
+
+// SHAP interaction values (explain.rs:267-301, 762-805) over the same paths.
+// For features i != j on a path the reference accumulates, at the deeper of
+// the two edges, v (o_i - z_i)(o_j - z_j) sum_k w_k prod_{g != i,j} a_{g,k},
+// and halves it when it symmetrises the matrix; the diagonal is the SHAP
+// value minus the row's off-diagonal sum.  Here every pair of a path adds
+// half that product to both (i, j) and (j, i), with
+// w prod_{g != i,j} a_g = P b_i b_j / w (b = w / a).  One warp per row: lane j
+// holds the path's element j, the warp multiplies P across lanes, and lane j
+// adds its feature's SHAP term and its pairs with later elements.  The matrix
+// accumulates in f64 in shared memory.
+constexpr int kInterWarps = 4;
+__host__ __device__ constexpr size_t inter_off(size_t bytes) { return (bytes + 15) & ~(size_t)15; }
+
+template <int M>
+__global__ void __launch_bounds__(kInterWarps * 32) k_shap_inter(const float* __restrict__ X, uint64_t n, uint32_t F,
+                                                                 const uint4* __restrict__ elems,
+                                                                 const uint32_t* __restrict__ chunk_off,
+                                                                 uint32_t n_chunks,
+                                                                 const uint32_t* __restrict__ cat_masks,
+                                                                 const float* __restrict__ rule_w, uint32_t warps,
+                                                                 float bias, float root_mean, float* __restrict__ out) {
+    constexpr uint32_t EW = elem_words<M>();
+    extern __shared__ __align__(16) uint32_t smem[];
+    const uint32_t nc = F + 1;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const size_t mat = (size_t)nc * nc;
+    // regions rounded to 16 bytes: matrices, diagonals, rows, path chunk
+    uint8_t* base = reinterpret_cast<uint8_t*>(smem);
+    double* mats = reinterpret_cast<double*>(base);                                  // [warps][nc][nc]
+    double* diags = reinterpret_cast<double*>(base + inter_off(warps * mat * 8));    // [warps][nc]
+    float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(diags) + inter_off(warps * nc * 8));  // [warps][F]
+    uint32_t* ch = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(xs) + inter_off((size_t)warps * F * 4));
+    double* m = mats + warp * mat;
+    double* dg = diags + warp * nc;
+    float* x = xs + warp * F;
+    float inv_w[M];
+#pragma unroll
+    for (int i = 0; i < M; i++) inv_w[i] = 1.0f / rule_w[i];
+    for (uint64_t g0 = (uint64_t)blockIdx.x * warps; g0 < n; g0 += (uint64_t)gridDim.x * warps) {
+        const uint64_t r = g0 + warp;
+        const bool live = warp < warps && r < n;
+        __syncthreads();
+        if (live) {
+            for (uint32_t i = lane; i < mat; i += 32) m[i] = 0.0;
+            for (uint32_t i = lane; i < nc; i += 32) dg[i] = 0.0;
+            for (uint32_t i = lane; i < F; i += 32) x[i] = X[r * F + i];
+        }
+        for (uint32_t c = 0; c < n_chunks; c++) {
+            const uint32_t e0 = chunk_off[c], e1 = chunk_off[c + 1];
+            __syncthreads();
+            const uint4* src = elems + (size_t)e0 * (EW / 4);
+            uint4* dst = reinterpret_cast<uint4*>(ch);
+            for (uint32_t i = threadIdx.x; i < (e1 - e0) * (EW / 4); i += blockDim.x) dst[i] = src[i];
+            __syncthreads();
+            if (!live) continue;
+            uint32_t e = 0;
+            while (e < e1 - e0) {
+                const uint32_t k = ch[e * EW + 3];
+                const bool mine = lane < k;
+                const uint32_t* E = ch + (e + (mine ? lane : 0)) * EW;
+                const uint4 h = *reinterpret_cast<const uint4*>(E);
+                const uint32_t f = h.x & 0xffffffu;
+                const bool o = mine && elem_test(h, x[f], cat_masks);
+                float a[M], b[M], P[M];
+                load_vec<M>(E + 4 + (o ? M : 0), a);
+                load_vec<M>(E + 4 + 2 * M + (o ? M : 0), b);
+                const float cj = __uint_as_float(E[4 + 4 * M + (o ? 1 : 0)]);
+                const float dj = __fsub_rn(o ? 1.0f : 0.0f, __uint_as_float(E[4 + 4 * M + 2]));
+#pragma unroll
+                for (int i = 0; i < M; i++) P[i] = mine ? a[i] : 1.0f;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                    for (int i = 0; i < M; i++) P[i] = __fmul_rn(P[i], __shfl_xor_sync(0xffffffffu, P[i], off));
+                if (mine) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < M; i++) s = __fmaf_rn(b[i], P[i], s);
+                    dg[f] = __dadd_rn(dg[f], (double)__fmul_rn(cj, s));
+                }
+                for (uint32_t l = 1; l < k; l++) {
+                    float bl[M];
+#pragma unroll
+                    for (int i = 0; i < M; i++) bl[i] = __shfl_sync(0xffffffffu, b[i], l);
+                    const float dl = __shfl_sync(0xffffffffu, dj, l);
+                    const uint32_t fl = __shfl_sync(0xffffffffu, f, l);
+                    if (lane < l) {
+                        float s = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < M; i++) s = __fmaf_rn(__fmul_rn(b[i], bl[i]), __fmul_rn(P[i], inv_w[i]), s);
+                        const double t = 0.5 * (double)cj * (double)dl * (double)s;
+                        m[(size_t)f * nc + fl] = __dadd_rn(m[(size_t)f * nc + fl], t);
+                        m[(size_t)fl * nc + f] = __dadd_rn(m[(size_t)fl * nc + f], t);
+                    }
+                }
+                __syncwarp();  // the next path's lanes may update the same entries
+                e += k;
+            }
+        }
+        __syncwarp();
+        if (live) {
+            // diagonal: the additive value minus the row's interactions
+            for (uint32_t i = lane; i < nc; i += 32) {
+                double v = i == F ? (double)__fadd_rn(__fadd_rn(0.0f, root_mean), bias) : dg[i];
+                for (uint32_t j = 0; j < nc; j++)
+                    if (j != i) v -= m[(size_t)i * nc + j];
+                m[(size_t)i * nc + i] = v;
+            }
+            __syncwarp();
+            float* o = out + r * mat;
+            for (uint32_t i = lane; i < mat; i += 32) o[i] = __double2float_rn(m[i]);
         }
     }
 }
@@ -322,6 +437,7 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
     } else {
         for (int i = 0; i < 8; i++) { y[i] = rule_nodes[i]; w[i] = rule_weights[i]; }
     }
+    for (int i = 0; i < 8; i++) rule_w8[i] = rule_weights[i];
     const uint32_t EW = 4 + 4 * M + 4;
     const uint32_t chunk_elems = kChunkBytes / (EW * 4);
     words.clear();
@@ -366,6 +482,7 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
             }
             tab[4 * M] = clamp((double)p.v * (0.0 - e.z));
             tab[4 * M + 1] = clamp((double)p.v * (1.0 - e.z));
+            tab[4 * M + 2] = (float)e.z;  // interactions: o - z of a partner
             words.insert(words.end(), rec, rec + EW);
         }
         in_chunk += k;
@@ -391,6 +508,52 @@ void ShapPaths::upload(cudaStream_t s) {
 static int path_rows() {
     const char* e = std::getenv("FBGPU_SHAP_ROWS");
     return e && std::atoi(e) == 1 ? 1 : 2;
+}
+
+size_t ShapPaths::inter_smem_bytes(uint32_t F, uint32_t warps) {
+    const size_t nc = F + 1;
+    return inter_off(warps * nc * nc * 8) + inter_off(warps * nc * 8) + inter_off((size_t)warps * F * 4) + kChunkBytes;
+}
+
+uint32_t ShapPaths::inter_warps(uint32_t F) {
+    for (uint32_t w = kInterWarps; w >= 1; w--)
+        if (inter_smem_bytes(F, w) <= 200 * 1024) return w;
+    return 0;
+}
+
+void ShapPaths::launch_inter(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out,
+                             cudaStream_t s) {
+    if (n == 0) return;
+    const uint32_t warps = inter_warps(F);
+    if (warps == 0) throw InputError("pred_interactions on the device supports at most 160 features");
+    if (!d_rule_w.p) {
+        double y[8], w[8];
+        float wf[8];
+        if (M == 4) gauss_legendre01(4, y, w);
+        for (int i = 0; i < M; i++) wf[i] = M == 4 ? (float)w[i] : rule_w8[i];
+        d_rule_w.alloc(sizeof(float) * 8);
+        FB_CUDA_CHECK(cudaMemcpyAsync(d_rule_w.p, wf, sizeof(float) * M, cudaMemcpyHostToDevice, s));
+    }
+    const uint32_t n_chunks = (uint32_t)chunk_off.size() - 1;
+    const size_t smem = inter_smem_bytes(F, warps);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint64_t groups = (n + warps - 1) / warps;
+#define FB_SI(MM)                                                                                                  \
+    do {                                                                                                           \
+        cudaFuncSetAttribute(k_shap_inter<MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);            \
+        int per_sm = 1;                                                                                            \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_shap_inter<MM>, kInterWarps * 32, smem);          \
+        const uint64_t grid = std::min<uint64_t>(groups, (uint64_t)sms * std::max(per_sm, 1));                     \
+        count_launch();                                                                                            \
+        k_shap_inter<MM><<<(unsigned)grid, kInterWarps * 32, smem, s>>>(                                          \
+            X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(),               \
+            d_rule_w.as<float>(), warps, bias, root_mean, out);                                                    \
+    } while (0)
+    if (M == 4) FB_SI(4);
+    else FB_SI(8);
+#undef FB_SI
 }
 
 size_t ShapPaths::smem_bytes(uint32_t F) { return (size_t)F * kPathThreads * path_rows() * (8 + 4) + kChunkBytes; }

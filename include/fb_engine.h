@@ -154,6 +154,11 @@ int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, in
 struct fbgpu_model* fb_model_device(fb_model* m, int32_t device);
 /* SHAP contributions n x (F+1) on the device. */
 int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device);
+/* Leaf indices (kind 0, n x n_trees), Saabas contributions (kind 1,
+ * n x (F+1)) or SHAP interaction values (kind 2, n x (F+1)^2) on the device
+ * (the reference's predict(pred_leaf / approx_contribs / pred_interactions),
+ * src/model/explain.rs Kind). */
+int32_t fb_model_explain(fb_model* m, int32_t kind, const float* X, uint64_t n, float* out, int32_t device);
 
 #ifdef __cplusplus
 }

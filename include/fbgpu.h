@@ -298,6 +298,18 @@ fbgpu_status fbgpu_predict_device(fbgpu_model* m, const float* X, uint64_t n, fl
 fbgpu_status fbgpu_shap(fbgpu_model* m, const float* X, uint64_t n, float* out);
 fbgpu_status fbgpu_shap_device(fbgpu_model* m, const float* X, uint64_t n, float* out, void* stream);
 
+/* The other explanation kinds of GpuExplainModel::compute
+ * (src/backend/cuda/explain.rs:491; src/model/explain.rs Kind):
+ *   FBGPU_EXPLAIN_LEAF          n x n_trees: the node index each tree's traversal ends at (as float);
+ *   FBGPU_EXPLAIN_APPROX        n x (n_features + 1): Saabas contributions (approx_contribs), bias last;
+ *   FBGPU_EXPLAIN_INTERACTIONS  n x (n_features + 1)^2: SHAP interaction values, bias row/column last. */
+#define FBGPU_EXPLAIN_LEAF 0
+#define FBGPU_EXPLAIN_APPROX 1
+#define FBGPU_EXPLAIN_INTERACTIONS 2
+fbgpu_status fbgpu_explain(fbgpu_model* m, int32_t kind, const float* X, uint64_t n, float* out);
+fbgpu_status fbgpu_explain_device(fbgpu_model* m, int32_t kind, const float* X, uint64_t n, float* out,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1291,6 +1291,105 @@ struct ShapRunner {  // explain.rs:302-400 Runner with the additive formulation
     }
 };
 
+// explain.rs:218-246 extract_interaction_delta
+inline float extract_interaction_delta(const Rule& R, const float* h, float pe, float px, float q) {
+    if (q == 1.0f) return 0.0f;
+    const float ap = q - 1.0f, ae = pe - 1.0f;
+    float acc = 0.0f;
+    if (px == 1.0f) {
+        for (int i = 0; i < kPts; i++) {
+            float edge = ae / (1.0f + ae * R.nodes[i]);
+            acc += ap * h[i] * edge / (1.0f + ap * R.nodes[i]);
+        }
+    } else {
+        const float ax = px - 1.0f;
+        for (int i = 0; i < kPts; i++) {
+            float edge = ae / (1.0f + ae * R.nodes[i]) - ax / (1.0f + ax * R.nodes[i]);
+            acc += ap * h[i] * edge / (1.0f + ap * R.nodes[i]);
+        }
+    }
+    return acc;
+}
+
+// explain.rs:267-301 Interaction formulation over the Runner of explain.rs:302-400
+struct InteractionRunner {
+    const std::vector<Node>& nodes;
+    const float* x;
+    const Rule& R;
+    float* path_prob;
+    std::vector<std::pair<uint32_t, float>>& path;
+    float* diag;
+    float* matrix;
+    uint32_t ncols;
+    void on_return(uint32_t feat, const float* h, float pe, float px) {
+        diag[feat] += extract_delta(R, h, pe, px);
+        // partners: the newest occurrence of every other feature on the live
+        // path, newest to oldest; the current split (the newest entry) is skipped
+        const size_t len = path.size();
+        bool skipped_current = false;
+        for (size_t i = len; i-- > 0;) {
+            const uint32_t split = path[i].first;
+            const float p_child = path[i].second;
+            bool shadowed = false;
+            for (size_t j = i + 1; j < len; j++)
+                if (path[j].first == split) { shadowed = true; break; }
+            if (shadowed) continue;
+            if (!skipped_current && split == feat) { skipped_current = true; continue; }
+            matrix[(size_t)feat * ncols + split] += extract_interaction_delta(R, h, pe, px, p_child);
+        }
+    }
+    void visit_child(int split, int child, float cw, bool sat, const float* c, float wp, float* out_h) {
+        uint32_t feat = nodes[split].feat;
+        float p_old = path_prob[feat];
+        float pe = sat ? (p_old == kUnseen ? 1.0f / cw : p_old / cw) : 0.0f;
+        float cc[kPts];
+        float ae = pe - 1.0f;
+        for (int i = 0; i < kPts; i++) cc[i] = c[i] * (1.0f + ae * R.nodes[i]);
+        if (p_old != kUnseen) {
+            float ao = p_old - 1.0f;
+            if (ao != 0.0f)
+                for (int i = 0; i < kPts; i++) cc[i] /= 1.0f + ao * R.nodes[i];
+        }
+        path_prob[feat] = pe;
+        path.push_back({feat, pe});
+        run_node(child, cc, wp * cw, out_h);
+        float px = p_old == kUnseen ? 1.0f : p_old;
+        on_return(feat, out_h, pe, px);
+        path.pop_back();
+        path_prob[feat] = p_old;
+    }
+    void run_node(int idx, const float* c, float wp, float* out_h) {
+        const Node& nd = nodes[idx];
+        if (nd.is_leaf) {
+            float ls = wp * nd.leaf;
+            for (int i = 0; i < kPts; i++) out_h[i] = c[i] * ls * R.weights[i];
+            return;
+        }
+        float lw = branch_weight(nodes[nd.left].hess, nd.hess);
+        float rw = branch_weight(nodes[nd.right].hess, nd.hess);
+        bool gl = node_goes_left(nd, x[nd.feat]);
+        float rh[kPts] = {0};
+        visit_child(idx, nd.left, lw, gl, c, wp, out_h);
+        visit_child(idx, nd.right, rw, !gl, c, wp, rh);
+        for (int i = 0; i < kPts; i++) out_h[i] += rh[i];
+    }
+};
+
+// explain.rs:409-421 fill_node_means (float32, FillNodeMeanValues)
+float fill_node_means(const std::vector<Node>& nodes, int idx, std::vector<float>& means) {
+    const Node& nd = nodes[idx];
+    float value;
+    if (nd.is_leaf) {
+        value = nd.leaf;
+    } else {
+        float result = fill_node_means(nodes, nd.left, means) * nodes[nd.left].hess;
+        result += fill_node_means(nodes, nd.right, means) * nodes[nd.right].hess;
+        value = result / nd.hess;
+    }
+    means[idx] = value;
+    return value;
+}
+
 double root_mean(const std::vector<Node>& nodes, int idx) {  // explain.rs:412-426
     const Node& nd = nodes[idx];
     if (nd.is_leaf) return (double)nd.leaf;
@@ -1412,6 +1511,111 @@ void rc_shap(void* mp, const float* X, uint64_t n, float* out, int32_t nthread) 
             }
             p[nc - 1] += root_mean_f;
             p[nc - 1] += bias;
+        }
+    }
+}
+
+void rc_pred_leaf(void* mp, const float* X, uint64_t n, float* out, int32_t nthread) {  // explain.rs:690-701
+    const Model& m = *(Model*)mp;
+    const uint32_t F = m.n_features, T = (uint32_t)m.trees.size();
+    int nth = n_threads(nthread);
+#pragma omp parallel for schedule(static) num_threads(nth)
+    for (int64_t r = 0; r < (int64_t)n; r++) {
+        const float* x = X + (size_t)r * F;
+        for (uint32_t t = 0; t < T; t++) {
+            const std::vector<Node>& nodes = m.trees[t].nodes;
+            size_t i = 0;
+            while (!nodes[i].is_leaf) i = node_goes_left(nodes[i], x[nodes[i].feat]) ? (size_t)nodes[i].left : (size_t)nodes[i].right;
+            out[(size_t)r * T + t] = (float)i;
+        }
+    }
+}
+
+void rc_pred_approx(void* mp, const float* X, uint64_t n, float* out, int32_t nthread) {  // explain.rs:729-760 saabas_row
+    const Model& m = *(Model*)mp;
+    const uint32_t F = m.n_features, nc = F + 1;
+    std::vector<std::vector<float>> means(m.trees.size());
+    for (size_t t = 0; t < m.trees.size(); t++) {  // explain.rs:515-525
+        means[t].assign(m.trees[t].nodes.size(), 0.0f);
+        fill_node_means(m.trees[t].nodes, 0, means[t]);
+    }
+    const float bias = base_margin(m.objective, m.base_score);
+    int nth = n_threads(nthread);
+#pragma omp parallel num_threads(nth)
+    {
+        std::vector<float> tc(nc);
+#pragma omp for schedule(static)
+        for (int64_t r = 0; r < (int64_t)n; r++) {
+            const float* x = X + (size_t)r * F;
+            float* p = out + (size_t)r * nc;
+            for (uint32_t c = 0; c < nc; c++) p[c] = 0.0f;
+            for (size_t t = 0; t < m.trees.size(); t++) {
+                std::fill(tc.begin(), tc.end(), 0.0f);
+                const std::vector<Node>& nodes = m.trees[t].nodes;
+                const std::vector<float>& mv = means[t];
+                float node_value = mv[0];
+                tc[nc - 1] += node_value;
+                if (!nodes[0].is_leaf) {
+                    size_t idx = 0;
+                    uint32_t split = 0;
+                    while (!nodes[idx].is_leaf) {
+                        const Node& nd = nodes[idx];
+                        split = nd.feat;
+                        idx = node_goes_left(nd, x[split]) ? (size_t)nd.left : (size_t)nd.right;
+                        const float nv = mv[idx];
+                        tc[split] += nv - node_value;
+                        node_value = nv;
+                    }
+                    tc[split] += nodes[idx].leaf - node_value;
+                }
+                for (uint32_t c = 0; c < nc; c++) p[c] += tc[c];
+            }
+            p[nc - 1] += bias;
+        }
+    }
+}
+
+void rc_pred_interactions(void* mp, const float* X, uint64_t n, float* out, int32_t nthread) {  // explain.rs:762-805
+    const Model& m = *(Model*)mp;
+    const uint32_t F = m.n_features, nc = F + 1;
+    double sum = 0.0;
+    for (const Tree& t : m.trees) sum += root_mean(t.nodes, 0);
+    const float root_mean_f = (float)sum;
+    const float bias = base_margin(m.objective, m.base_score);
+    const Rule& R = rule();
+    int nth = n_threads(nthread);
+#pragma omp parallel num_threads(nth)
+    {
+        std::vector<float> path_prob(F, kUnseen), diag(nc);
+        std::vector<std::pair<uint32_t, float>> path;
+#pragma omp for schedule(dynamic, 4)
+        for (int64_t r = 0; r < (int64_t)n; r++) {
+            const float* x = X + (size_t)r * F;
+            float* matrix = out + (size_t)r * nc * nc;
+            for (size_t c = 0; c < (size_t)nc * nc; c++) matrix[c] = 0.0f;
+            std::fill(diag.begin(), diag.end(), 0.0f);
+            for (const Tree& t : m.trees) {
+                path.clear();
+                if (t.nodes[0].is_leaf) continue;
+                InteractionRunner run{t.nodes, x, R, path_prob.data(), path, diag.data(), matrix, nc};
+                float ones[kPts], h[kPts];
+                for (int i = 0; i < kPts; i++) { ones[i] = 1.0f; h[i] = 0.0f; }
+                run.run_node(0, ones, 1.0f, h);
+            }
+            diag[nc - 1] += root_mean_f;
+            diag[nc - 1] += bias;
+            for (uint32_t a = 0; a < nc; a++)  // symmetric: the mean of the two directions
+                for (uint32_t b = a + 1; b < nc; b++) {
+                    const float sym = 0.5f * (matrix[a * nc + b] + matrix[b * nc + a]);
+                    matrix[a * nc + b] = sym;
+                    matrix[b * nc + a] = sym;
+                }
+            for (uint32_t a = 0; a < nc; a++) {  // diagonal: the additive value minus the row's interactions
+                float value = diag[a];
+                for (uint32_t b = 0; b < nc; b++)
+                    if (b != a) value -= matrix[a * nc + b];
+                matrix[a * nc + a] = value;
+            }
         }
     }
 }

@@ -71,6 +71,13 @@ void rc_predict_margin(void* model, const float* X, uint64_t n, float* out,
 void rc_shap(void* model, const float* X, uint64_t n, float* out,
              int32_t nthread);
 
+/* Leaf node index of every tree, n x T (as float, explain.rs:690-701). */
+void rc_pred_leaf(void* model, const float* X, uint64_t n, float* out, int32_t nthread);
+/* Saabas contributions (approx_contribs), n x (F+1), bias last. */
+void rc_pred_approx(void* model, const float* X, uint64_t n, float* out, int32_t nthread);
+/* SHAP interaction values, n x (F+1) x (F+1). */
+void rc_pred_interactions(void* model, const float* X, uint64_t n, float* out, int32_t nthread);
+
 /* ---- component entry points used by the kernel parity tests ---- */
 
 /* Weighted quantile sketch cuts.  offsets has F+1 entries; returns the total

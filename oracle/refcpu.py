@@ -67,6 +67,8 @@ class RefCPU:
         lib.rc_model_base_margin.restype = C.c_float
         lib.rc_predict_margin.argtypes = [_P, C.POINTER(C.c_float), C.c_uint64, C.POINTER(C.c_float), C.c_int32]
         lib.rc_shap.argtypes = [_P, C.POINTER(C.c_float), C.c_uint64, C.POINTER(C.c_float), C.c_int32]
+        for name in ("rc_pred_leaf", "rc_pred_approx", "rc_pred_interactions"):
+            getattr(lib, name).argtypes = [_P, C.POINTER(C.c_float), C.c_uint64, C.POINTER(C.c_float), C.c_int32]
         lib.rc_sketch.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.c_uint32, C.c_uint32, C.POINTER(C.c_float),
                                   C.POINTER(C.c_uint8), C.POINTER(C.c_float), C.POINTER(C.c_uint32), C.c_uint64,
                                   C.c_int32]
@@ -231,4 +233,23 @@ class RefModel:
         X = np.ascontiguousarray(X, dtype=np.float32)
         out = np.zeros((X.shape[0], X.shape[1] + 1), dtype=np.float32)
         self.rc.lib.rc_shap(self.h, _ptr(X, C.c_float), X.shape[0], _ptr(out, C.c_float), nthread)
+        return out
+
+    def pred_leaf(self, X, nthread=0):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        out = np.zeros((X.shape[0], self.num_trees), dtype=np.float32)
+        self.rc.lib.rc_pred_leaf(self.h, _ptr(X, C.c_float), X.shape[0], _ptr(out, C.c_float), nthread)
+        return out
+
+    def approx_contribs(self, X, nthread=0):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        out = np.zeros((X.shape[0], X.shape[1] + 1), dtype=np.float32)
+        self.rc.lib.rc_pred_approx(self.h, _ptr(X, C.c_float), X.shape[0], _ptr(out, C.c_float), nthread)
+        return out
+
+    def interactions(self, X, nthread=0):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        nc = X.shape[1] + 1
+        out = np.zeros((X.shape[0], nc, nc), dtype=np.float32)
+        self.rc.lib.rc_pred_interactions(self.h, _ptr(X, C.c_float), X.shape[0], _ptr(out, C.c_float), nthread)
         return out
