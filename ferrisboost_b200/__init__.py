@@ -212,6 +212,7 @@ class Shard(NamedTuple):
     rank: int
     base_score: float     # label mean over all rows (fb_label_mean) or the given base_score
     timeout_ms: int = 120000
+    comm: Any = None      # a distributed.Communicator started ahead (its initialization overlaps data preparation)
 
 
 class Dataset:
@@ -310,6 +311,12 @@ class Booster:
         if shard is None:
             self._h = lib().fb_booster_create(dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float),
                                               C.byref(fp))
+        elif shard.comm is not None:
+            fp.base_score = shard.base_score
+            self._keep = self._keep + (shard.comm,)
+            self._h = lib().fb_booster_create_sharded_comm(
+                dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), C.byref(fp), shard.row_offset,
+                shard.n_rows_global, shard.comm.handle, shard.nranks, shard.rank)
         else:
             fp.base_score = shard.base_score
             nid = np.frombuffer(shard.nccl_id, dtype=np.uint8).copy()

@@ -122,6 +122,11 @@ SIGNATURES = {
     "fb_booster_create": (P, [P, f32p, f32p, C.POINTER(FbParams)]),
     "fb_booster_create_sharded": (P, [P, f32p, f32p, C.POINTER(FbParams), C.c_uint64, C.c_uint64, u8p, C.c_int32,
                                       C.c_int32, C.c_uint32]),
+    "fb_booster_create_sharded_comm": (P, [P, f32p, f32p, C.POINTER(FbParams), C.c_uint64, C.c_uint64, P,
+                                           C.c_int32, C.c_int32]),
+    "fbgpu_comm_begin": (C.c_int, [u8p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32, C.POINTER(P)]),
+    "fbgpu_comm_free": (None, [P]),
+    "fbgpu_ctx_adopt_comm": (C.c_int, [P, P]),
     "fb_booster_free": (None, [P]),
     "fb_booster_update": (C.c_int32, [P, C.c_uint32]),
     "fb_booster_timing": (None, [P, f64p]),

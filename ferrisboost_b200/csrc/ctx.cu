@@ -144,6 +144,15 @@ void TrainCtx::set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t
     rank_ = rank;
 }
 
+void TrainCtx::adopt_comm(std::unique_ptr<NcclComm> comm, int nranks, int rank) {
+    if (nranks < 1 || rank < 0 || rank >= nranks) throw InputError("invalid rank / world size");
+    if (comm_) throw InputError("the context already has a communicator");
+    if (nranks == 1) return;
+    comm_ = std::move(comm);
+    nranks_ = nranks;
+    rank_ = rank;
+}
+
 void TrainCtx::allreduce_max_host(double* v, int count) {
     if (!comm_ || count <= 0) return;
     if (count > 8) throw InputError("allreduce_max_host takes at most 8 values");
@@ -1271,6 +1280,7 @@ struct fbgpu_ctx {
     explicit fbgpu_ctx(const fbgpu_config& c) : impl(c) {}
 };
 
+
 namespace {
 template <class F> fbgpu_status guard(fbgpu_ctx* ctx, F&& f) {
     try {
@@ -1372,6 +1382,51 @@ uint64_t fbgpu_launch_count(void) { return fbg::g_launches.load(std::memory_orde
 
 fbgpu_status fbgpu_nccl_unique_id(uint8_t* out) {
     return guard(nullptr, [&] { fbg::nccl_unique_id(out); });
+}
+
+fbgpu_status fbgpu_comm_begin(const uint8_t* unique_id, int32_t nranks, int32_t rank, int32_t device,
+                              uint32_t timeout_ms, fbgpu_comm** out) {
+    return guard(nullptr, [&] {
+        if (!unique_id || !out) throw fbg::InputError("unique_id and out must not be null");
+        if (nranks < 2 || rank < 0 || rank >= nranks) throw fbg::InputError("invalid rank / world size");
+        auto pc = std::make_unique<fbgpu_comm>();
+        pc->impl.nranks = nranks;
+        pc->impl.rank = rank;
+        pc->impl.comm.reset(new fbg::NcclComm(unique_id, nranks, rank, device, timeout_ms, false));
+        fbg::PendingComm* p = &pc->impl;
+        p->worker = std::thread([p, device] {
+            try {
+                FB_CUDA_CHECK(cudaSetDevice(device));
+                p->comm->wait_init();
+                // the first collectives of each size set up NCCL's connections;
+                // run a small and a histogram-sized one now, on every rank
+                cudaStream_t st = nullptr;
+                FB_CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+                struct Owner {
+                    cudaStream_t s;
+                    ~Owner() { cudaStreamDestroy(s); }
+                } owner{st};
+                fbg::DevMem buf;
+                buf.alloc(8u << 20);
+                FB_CUDA_CHECK(cudaMemsetAsync(buf.p, 0, 8u << 20, st));
+                p->comm->allreduce(buf.p, buf.p, 2, true, false, st);
+                p->comm->allreduce(buf.p, buf.p, (8u << 20) / 8, true, false, st);
+                p->comm->sync(st);
+            } catch (...) {
+                p->error = std::current_exception();
+            }
+        });
+        *out = pc.release();
+    });
+}
+
+void fbgpu_comm_free(fbgpu_comm* c) { delete c; }
+
+fbgpu_status fbgpu_ctx_adopt_comm(fbgpu_ctx* ctx, fbgpu_comm* c) {
+    return guard(ctx, [&] {
+        if (!c) throw fbg::InputError("null communicator");
+        ctx->impl.adopt_comm(c->impl.take(), c->impl.nranks, c->impl.rank);
+    });
 }
 
 fbgpu_status fbgpu_ctx_set_comm(fbgpu_ctx* ctx, const uint8_t* unique_id, int32_t nranks, int32_t rank,

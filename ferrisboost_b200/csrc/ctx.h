@@ -5,6 +5,8 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <thread>
+#include <exception>
 #include <utility>
 #include <vector>
 
@@ -101,6 +103,8 @@ class TrainCtx {
     // Row sharding over several GPUs: one context per GPU, one NCCL
     // communicator per context (ranks in the same order on every GPU).
     void set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t timeout_ms);
+    // A communicator initialized ahead of time (fbgpu_comm_begin).
+    void adopt_comm(std::unique_ptr<NcclComm> comm, int nranks, int rank);
     int nranks() const { return nranks_; }
     // Waits for the training stream; when sharded, a bounded poll that aborts
     // the communicator if a peer stops answering.
@@ -273,6 +277,25 @@ class ExplainModel {
     DevMem means_;  // Saabas per-node means (explain.rs:409-421), built at the first approx call
 };
 
+// A communicator whose initialization, and a warm-up of the collectives the
+// training will use, run on a background host thread while the caller
+// prepares its data (fbgpu_comm_begin).  take() waits for it.
+struct PendingComm {
+    std::unique_ptr<NcclComm> comm;
+    std::thread worker;
+    std::exception_ptr error;
+    int nranks = 1, rank = 0;
+    ~PendingComm() {
+        if (worker.joinable()) worker.join();
+    }
+    std::unique_ptr<NcclComm> take() {
+        if (worker.joinable()) worker.join();
+        if (error) std::rethrow_exception(error);
+        if (!comm) throw InputError("the communicator was already taken by a context");
+        return std::move(comm);
+    }
+};
+
 // Sets the message fbgpu_last_error(NULL) returns on this thread.
 void noalloc_set_error(const char* msg);
 
@@ -283,6 +306,11 @@ void make_shap_rule(float* nodes, float* weights);
 double pow2_scale_host(double max_abs, uint64_t n_rows);
 
 }  // namespace fbg
+
+// The C ABI's early communicator handle (include/fbgpu.h fbgpu_comm).
+struct fbgpu_comm {
+    fbg::PendingComm impl;
+};
 
 // The C ABI's explanation-model handle (include/fbgpu.h fbgpu_model).
 struct fbgpu_model {

@@ -683,6 +683,7 @@ float label_mean(const float* y, const float* w, uint64_t n) {
 struct ShardInfo {
     uint64_t row_offset = 0, n_global = 0;
     const uint8_t* nccl_id = nullptr;
+    fbgpu_comm* comm = nullptr;  // a communicator started ahead (fbgpu_comm_begin), else made from nccl_id
     int nranks = 1, rank = 0;
     uint32_t timeout_ms = 0;
 };
@@ -709,7 +710,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     if (sh.nranks > 1) {
         if (std::isnan(p.base_score))
             throw InputError("a row-sharded booster needs base_score (the label mean over all rows)");
-        if (!sh.nccl_id) throw InputError("a row-sharded booster needs an NCCL unique id");
+        if (!sh.nccl_id && !sh.comm) throw InputError("a row-sharded booster needs an NCCL unique id or communicator");
         if (sh.row_offset + d->n > sh.n_global) throw InputError("row_offset + rows exceeds n_rows_global");
     }
     if (p.objective != 0 && p.objective != 1) throw InputError("objective must be reg:squarederror or binary:logistic");
@@ -763,7 +764,15 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     cfg.gpu_math = p.gpu_math;
     if (const char* e = std::getenv("FBGPU_HIST_SMEM")) cfg.hist_smem_bytes = (uint32_t)std::atoi(e);
     b->ctx.reset(new fbg::TrainCtx(cfg));
-    if (sh.nranks > 1) b->ctx->set_comm(sh.nccl_id, sh.nranks, sh.rank, sh.timeout_ms);
+    if (sh.nranks > 1) {
+        if (sh.comm) {
+            if (sh.comm->impl.nranks != sh.nranks || sh.comm->impl.rank != sh.rank)
+                throw InputError("the communicator was started for another rank / world size");
+            b->ctx->adopt_comm(sh.comm->impl.take(), sh.nranks, sh.rank);
+        } else {
+            b->ctx->set_comm(sh.nccl_id, sh.nranks, sh.rank, sh.timeout_ms);
+        }
+    }
     std::vector<uint32_t> nb(d->F);
     for (uint32_t f = 0; f < d->F; f++) nb[f] = d->n_bins(f);
     b->ctx->set_features(nb.data(), d->width.data(), d->cat.data());
@@ -1064,6 +1073,25 @@ fb_booster* fb_booster_create_sharded(const fb_dataset* shard, const float* labe
         sh.rank = rank;
         sh.timeout_ms = timeout_ms;
         if (nranks < 1 || rank < 0 || rank >= nranks) throw fbe::InputError("invalid rank / world size");
+        auto* out = new fb_booster();
+        std::unique_ptr<fb_booster> guard_out(out);
+        out->b.reset(fbe::booster_create(shard->d.get(), labels, weights, p, sh));
+        return guard_out.release();
+    }, nullptr);
+}
+
+fb_booster* fb_booster_create_sharded_comm(const fb_dataset* shard, const float* labels, const float* weights,
+                                           const fb_params* p, uint64_t row_offset, uint64_t n_rows_global,
+                                           fbgpu_comm* comm, int32_t nranks, int32_t rank) {
+    return fbe::guarded([&]() -> fb_booster* {
+        fbe::ShardInfo sh;
+        sh.row_offset = row_offset;
+        sh.n_global = n_rows_global;
+        sh.comm = comm;
+        sh.nranks = nranks;
+        sh.rank = rank;
+        if (nranks < 1 || rank < 0 || rank >= nranks) throw fbe::InputError("invalid rank / world size");
+        if (nranks > 1 && !comm) throw fbe::InputError("a row-sharded booster needs a communicator");
         auto* out = new fb_booster();
         std::unique_ptr<fb_booster> guard_out(out);
         out->b.reset(fbe::booster_create(shard->d.get(), labels, weights, p, sh));

@@ -76,7 +76,7 @@ void nccl_unique_id(uint8_t* out) {
     std::memcpy(out, id.internal, kNcclUniqueIdBytes);
 }
 
-NcclComm::NcclComm(const uint8_t* unique_id, int nranks, int rank, int device, uint32_t timeout_ms)
+NcclComm::NcclComm(const uint8_t* unique_id, int nranks, int rank, int device, uint32_t timeout_ms, bool wait)
     : timeout_ms_(timeout_ms ? timeout_ms : 120000u) {
     static_assert(sizeof(ncclUniqueId) == kNcclUniqueIdBytes, "ncclUniqueId size");
     const Api& a = api();
@@ -93,7 +93,7 @@ NcclComm::NcclComm(const uint8_t* unique_id, int nranks, int rank, int device, u
         comm_ = nullptr;
         throw NcclError(nccl_msg("ncclCommInitRankConfig", rc));
     }
-    wait_ready("ncclCommInitRankConfig");
+    if (wait) wait_ready("ncclCommInitRankConfig");
 }
 
 NcclComm::~NcclComm() {

@@ -27,7 +27,10 @@ void nccl_unique_id(uint8_t* out);
 
 class NcclComm {
 public:
-    NcclComm(const uint8_t* unique_id, int nranks, int rank, int device, uint32_t timeout_ms);
+    // wait == false returns as soon as the non-blocking initialization has
+    // started; wait_init() then completes it.
+    NcclComm(const uint8_t* unique_id, int nranks, int rank, int device, uint32_t timeout_ms, bool wait = true);
+    void wait_init() { wait_ready("ncclCommInitRankConfig"); }
     ~NcclComm();
     NcclComm(const NcclComm&) = delete;
     NcclComm& operator=(const NcclComm&) = delete;

@@ -30,7 +30,32 @@ import numpy as np
 
 from . import (Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params, lib)
 
-__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost"]
+__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost", "Communicator"]
+
+
+class Communicator:
+    """An NCCL communicator started before the data is prepared
+    (fbgpu_comm_begin): its initialization and a warm-up of the collectives
+    run on a background thread of the library while this rank sketches and
+    bins its rows.  Every rank creates one with the same unique id; a
+    Booster built with ``Shard(comm=...)`` takes it over."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int, timeout_ms: int = 120000):
+        nid = np.frombuffer(unique_id, dtype=np.uint8).copy()
+        h = C.c_void_p()
+        st = lib().fbgpu_comm_begin(_lib.ptr(nid, C.c_uint8), nranks, rank, device, timeout_ms, C.byref(h))
+        if st:
+            raise RuntimeError(lib().fbgpu_last_error(None).decode())
+        self.handle = h
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                lib().fbgpu_comm_free(h)
+            except TypeError:  # interpreter shutdown: module globals already cleared
+                pass
+            self.handle = None
 
 
 class PeerLost(RuntimeError):
@@ -206,11 +231,6 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     if n < world:  # the same on every rank: all raise before any collective
         raise ValueError(f"{n} rows cannot be sharded over {world} ranks")
     cat = _feature_flags(feature_types, F)
-    cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group, device=p["device_index"])
-    lo, hi = shard_range(n, world, rank)
-    base = p["base_score"]
-    if base is None:
-        base = float(lib().fb_label_mean(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), n))
     nid = None
     if rank == 0:  # a failure on rank 0 is sent to every rank, which all raise
         try:
@@ -220,10 +240,18 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     nid = _broadcast(nid, group)
     if isinstance(nid, str):
         raise RuntimeError(f"rank 0 could not create an NCCL id ({nid})")
+    timeout_ms = int(max(1.0, timeout_s) * 1000)
+    # the communicator initializes while the cuts are sketched and the rows binned
+    comm = Communicator(nid, world, rank, p["device_index"], timeout_ms)
+    cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group, device=p["device_index"])
+    lo, hi = shard_range(n, world, rank)
+    base = p["base_score"]
+    if base is None:
+        base = float(lib().fb_label_mean(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), n))
     ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts,
                  device=p["device_index"])
     shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
-                  timeout_ms=int(max(1.0, timeout_s) * 1000))
+                  timeout_ms=timeout_ms, comm=comm)
     b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)
     if liveness is None:
         b.update(num_boost_round)

@@ -118,6 +118,14 @@ fb_booster* fb_booster_create(const fb_dataset* d, const float* labels, const fl
 fb_booster* fb_booster_create_sharded(const fb_dataset* shard, const float* labels, const float* weights,
                                       const fb_params* p, uint64_t row_offset, uint64_t n_rows_global,
                                       const uint8_t* nccl_id, int32_t nranks, int32_t rank, uint32_t timeout_ms);
+/* fb_booster_create_sharded with a communicator already started by
+ * fbgpu_comm_begin (include/fbgpu.h), so its initialization overlapped the
+ * data preparation; the booster takes the communicator over (the handle is
+ * still freed with fbgpu_comm_free). */
+struct fbgpu_comm;
+fb_booster* fb_booster_create_sharded_comm(const fb_dataset* shard, const float* labels, const float* weights,
+                                           const fb_params* p, uint64_t row_offset, uint64_t n_rows_global,
+                                           struct fbgpu_comm* comm, int32_t nranks, int32_t rank);
 void fb_booster_free(fb_booster* b);
 /* Train n_rounds more trees. */
 int32_t fb_booster_update(fb_booster* b, uint32_t n_rounds);

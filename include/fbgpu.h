@@ -144,6 +144,19 @@ fbgpu_status fbgpu_nccl_unique_id(uint8_t* out_id);
 fbgpu_status fbgpu_ctx_set_comm(fbgpu_ctx* ctx, const uint8_t* unique_id, int32_t nranks, int32_t rank,
                                 uint32_t timeout_ms);
 
+/* The same communicator, started ahead of the context: the non-blocking
+ * NCCL initialization and a warm-up of two all-reduces (16 B and 8 MiB, which
+ * set up NCCL's connections) run on a background host thread while the
+ * caller sketches and bins its data; fbgpu_ctx_adopt_comm joins it to a
+ * context (waiting for it if needed) and fbgpu_comm_free releases the
+ * handle.  Every rank calls fbgpu_comm_begin, with the same unique id.  No
+ * counterpart in the reference. */
+typedef struct fbgpu_comm fbgpu_comm;
+fbgpu_status fbgpu_comm_begin(const uint8_t* unique_id, int32_t nranks, int32_t rank, int32_t device,
+                              uint32_t timeout_ms, fbgpu_comm** out);
+fbgpu_status fbgpu_ctx_adopt_comm(fbgpu_ctx* ctx, fbgpu_comm* comm);
+void fbgpu_comm_free(fbgpu_comm* comm);
+
 /* Feature metadata: bins per feature (cuts + 1), storage width in bytes
  * (bins.rs:58-66 BinWidth::for_feature) and categorical flags (may be NULL).
  * Replaces the cuts half of GpuTrainCtx::block_session_bins
