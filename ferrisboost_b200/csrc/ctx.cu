@@ -796,6 +796,17 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         return;
     }
     LevelArgs a = level_args(tp);
+    static const bool no_fuse = [] {
+        const char* e = std::getenv("FBGPU_FUSE");
+        return e && std::string(e) == "0";
+    }();
+    if (!no_fuse) {
+        if (!fuse_.p) {
+            fuse_.alloc(16);
+            FB_CUDA_CHECK(cudaMemsetAsync(fuse_.p, 0, 16, s_));
+        }
+        a.fuse = fuse_.as<unsigned int>();
+    }
     const uint32_t maxd = tp.max_depth;
     FB_CUDA_CHECK(cudaEventRecord(ev0_, s_));
     int cur = 0;
@@ -848,13 +859,19 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             root_pending_ = false;
         }
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
-        launch_split(a, max_m, s_);
-        launch_decide(a, s_);
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
-        launch_part_count(a, max_chunks, s_);
-        launch_part_scan(a, s_);
-        launch_part_scatter(a, max_chunks, s_);
-        launch_next_level(a, s_);
+        if (a.fuse) {  // the one-CTA steps ride in the last CTA of the kernel before them
+            launch_split_decide(a, max_m, s_);
+            launch_part_count(a, max_chunks, s_);
+            launch_part_scatter(a, max_chunks, s_);
+        } else {
+            launch_split(a, max_m, s_);
+            launch_decide(a, s_);
+            launch_part_count(a, max_chunks, s_);
+            launch_part_scan(a, s_);
+            launch_part_scatter(a, max_chunks, s_);
+            launch_next_level(a, s_);
+        }
         cur = 1 - cur;
     }
     a.nodes = nodes_[cur].as<NodeInfo>();

@@ -216,6 +216,7 @@ class TrainCtx {
     bool stats_ = false;
     cudaEvent_t hev_[32] = {};
     DevMem level_stats_;
+    DevMem fuse_;  // last-CTA counters of the fused level kernels (depthwise)
     double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0;
 };
 

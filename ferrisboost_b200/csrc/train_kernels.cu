@@ -836,6 +836,24 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
 }
 
 // Per node: the best feature (equal gains -> lower feature id, split.rs:631-642).
+// Last-block pattern for fusing a one-CTA step into the kernel before it:
+// every CTA publishes its results, fences, and takes a ticket; the CTA that
+// takes the last one (all others have finished) runs the step and resets
+// the counter for the next launch.  No CTA waits on another.
+__device__ __forceinline__ bool last_block_done(unsigned int* counter) {
+    __shared__ bool last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int ticket = atomicAdd(counter, 1u);
+        last = ticket == gridDim.x - 1;
+        if (last) *counter = 0u;
+    }
+    __syncthreads();
+    if (last) __threadfence();
+    return last;
+}
+
 __global__ void k_split_node(LevelArgs a) {
     const uint32_t node = blockIdx.x;
     if (node >= a.st->m) return;
@@ -875,8 +893,8 @@ __global__ void k_split_node(LevelArgs a) {
 // order (training/mod.rs:4140-4151), tree arrays of the split nodes and their
 // children (tree.rs:140-170 split_leaf; mod.rs:5069-5103 leaf values), and
 // the children's sums / bounds.
-__global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
-    __shared__ uint32_t wt[32];
+template <int NT>
+__device__ void decide_body(const LevelArgs& a, uint32_t* wt) {
     TreeState* st = a.st;
     const uint32_t m = st->m;
     const uint32_t leaf_count = st->leaf_count;
@@ -885,16 +903,22 @@ __global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
                                                  : (a.max_leaves > leaf_count ? a.max_leaves - leaf_count : 0u);
     const ScoreParams sp = load_sp(a);
     uint32_t found_before = 0;
-    for (uint32_t c = 0; c < m; c += 1024) {
+    for (uint32_t c = 0; c < m; c += NT) {
         const uint32_t i = c + threadIdx.x;
-        const bool found = i < m && (a.node_best[i].flags & 1u);
+        const bool found = i < m && (__ldcg(&a.node_best[i].flags) & 1u);
         uint32_t tot;
-        const uint32_t rank = found_before + block_excl_scan_u32<1024>(found ? 1u : 0u, wt, tot);
+        const uint32_t rank = found_before + block_excl_scan_u32<NT>(found ? 1u : 0u, wt, tot);
         found_before += tot;
         if (i < m) {
             SplitDesc sd{-1, 0, 0, 0};
             if (found && rank < remaining) {
-                const SplitRec b = a.node_best[i];
+                SplitRec b;
+                {
+                    const uint4* src = reinterpret_cast<const uint4*>(&a.node_best[i]);
+                    uint4* dst = reinterpret_cast<uint4*>(&b);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) dst[q] = __ldcg(src + q);
+                }
                 const NodeInfo ni = a.nodes[i];
                 const uint32_t k = rank;
                 const int32_t L = (int32_t)(base_nodes + 2 * k), Rt = L + 1;
@@ -913,7 +937,7 @@ __global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
                 p.flags = ((b.flags & 2u) ? 2u : 0u) | (is_cat ? 4u : 0u);
                 a.trec[ni.tree_id] = p;
                 if (is_cat)
-                    for (int w = 0; w < 8; w++) a.tcats[(size_t)ni.tree_id * 8 + w] = a.node_cats[i * 8 + w];
+                    for (int w = 0; w < 8; w++) a.tcats[(size_t)ni.tree_id * 8 + w] = __ldcg(&a.node_cats[i * 8 + w]);
                 TreeRec cl{-1, -1, 0, 0, 0.0f, __fmul_rn(wl, sp.eta), __double2float_rn(lh), 1u};
                 TreeRec cr{-1, -1, 0, 0, 0.0f, __fmul_rn(wr, sp.eta), __double2float_rn(rh), 1u};
                 a.trec[L] = cl;
@@ -941,6 +965,52 @@ __global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
     }
 }
 
+__global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    decide_body<1024>(a, wt);
+}
+
+// k_split_node for 8 nodes per CTA (one warp each) with the level's decisions
+// (k_decide) run by the last CTA.
+__global__ void __launch_bounds__(256) k_split_node_decide(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t node = blockIdx.x * 8 + warp;
+    if (node < a.st->m) {
+        const uint32_t F = a.n_features;
+        float bg = 0.0f;
+        uint32_t bf = 0xffffffffu;
+        bool have = false;
+        for (uint32_t f = lane; f < F; f += 32) {
+            const SplitRec& r = a.feat_best[(size_t)node * F + f];
+            if (!(r.flags & 1u)) continue;
+            if (!have || r.gain > bg) { bg = r.gain; bf = f; have = true; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float og = __shfl_down_sync(0xffffffffu, bg, o);
+            uint32_t of = __shfl_down_sync(0xffffffffu, bf, o);
+            bool oh = __shfl_down_sync(0xffffffffu, (int)have, o);
+            if (oh && (!have || og > bg || (og == bg && of < bf))) { bg = og; bf = of; have = true; }
+        }
+        have = __shfl_sync(0xffffffffu, (int)have, 0) != 0;
+        bf = __shfl_sync(0xffffffffu, bf, 0);
+        if (lane == 0) {
+            SplitRec r;
+            if (have) {
+                r = a.feat_best[(size_t)node * F + bf];
+                r.feat = bf;
+            } else {
+                r.flags = 0;
+            }
+            a.node_best[node] = r;
+        }
+        if (have && lane < 8 && a.is_cat && a.is_cat[bf])
+            a.node_cats[node * 8 + lane] = a.feat_cats[((size_t)node * F + bf) * 8 + lane];
+    }
+    if (last_block_done(a.fuse + 0)) decide_body<256>(a, wt);
+}
+
 // ------------------------------------------------------------------ partition
 __device__ __forceinline__ bool goes_left(const LevelArgs& a, const SplitDesc& sd, const uint32_t* cats,
                                           uint32_t row) {
@@ -958,7 +1028,7 @@ __device__ __forceinline__ bool goes_left(const LevelArgs& a, const SplitDesc& s
 // same single f32 addition).  Thread t owns rows [8t, 8t + 8) of its chunk;
 // with a.dirflags set it stores their directions as one byte (bit k = row
 // 8t + k goes left) so the scatter pass does not gather the bins again.
-__global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
+__device__ __forceinline__ void part_count_work(const LevelArgs& a) {
     __shared__ uint32_t wt[32];
     __shared__ uint32_t cats[8];
     const uint32_t c = blockIdx.x;
@@ -1011,16 +1081,16 @@ __global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
 }
 
 // Exclusive scan of the chunk left counts (one CTA) and per-node left totals.
-__global__ void __launch_bounds__(1024) k_part_scan(LevelArgs a) {
-    __shared__ uint32_t wt[32];
+template <int NT>
+__device__ void part_scan_body(const LevelArgs& a, uint32_t* wt) {
     const TreeState* st = a.st;
     const uint32_t nc = st->chunk_count, m = st->m;
     uint32_t carry = 0;
-    for (uint32_t base = 0; base < nc; base += 1024) {
+    for (uint32_t base = 0; base < nc; base += NT) {
         const uint32_t c = base + threadIdx.x;
-        const uint32_t v = c < nc ? a.chunk_left[c] : 0u;
+        const uint32_t v = c < nc ? __ldcg(&a.chunk_left[c]) : 0u;
         uint32_t tot;
-        const uint32_t ex = block_excl_scan_u32<1024>(v, wt, tot);
+        const uint32_t ex = block_excl_scan_u32<NT>(v, wt, tot);
         if (c < nc) a.chunk_off[c] = carry + ex;
         carry += tot;
     }
@@ -1033,10 +1103,15 @@ __global__ void __launch_bounds__(1024) k_part_scan(LevelArgs a) {
     }
 }
 
+__global__ void __launch_bounds__(1024) k_part_scan(LevelArgs a) {
+    __shared__ uint32_t wt[32];
+    part_scan_body<1024>(a, wt);
+}
+
 // Stable scatter of every chunk of a split node into [left | right] of the
 // node's span in the next arena (directions from k_part_count's bytes, or
 // recomputed when a.dirflags is null).
-__global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
+__device__ __forceinline__ void part_scatter_work(const LevelArgs& a) {
     __shared__ uint32_t wt[32];
     __shared__ uint32_t cats[8];
     __shared__ uint32_t stage[kChunkRows];
@@ -1094,9 +1169,8 @@ __global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
 // smaller child (by rows, training/mod.rs:4478-4482; by hessian sum over all
 // ranks when row-sharded) is accumulated, the larger one is its parent minus
 // the smaller one.  Which one is accumulated never changes the histograms.
-__global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
-    __shared__ unsigned long long wt64[32];
-    __shared__ uint32_t wt[32];
+template <int NT>
+__device__ void next_level_body(const LevelArgs& a, unsigned long long* wt64, uint32_t* wt) {
     TreeState* st = a.st;
     const uint32_t m = st->m, kept = st->kept;
     for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
@@ -1125,22 +1199,22 @@ __global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
     }
     __syncthreads();
     unsigned long long carry = 0;
-    for (uint32_t base = 0; base < kept; base += 1024) {
+    for (uint32_t base = 0; base < kept; base += NT) {
         const uint32_t k = base + threadIdx.x;
         unsigned long long v = k < kept ? a.next_nodes[a.next_acc_list[k]].len : 0ull;
         unsigned long long tot;
-        unsigned long long ex = block_excl_scan_u64<1024>(v, wt64, tot);
+        unsigned long long ex = block_excl_scan_u64<NT>(v, wt64, tot);
         if (k < kept) a.next_acc_prefix[k] = carry + ex;
         carry += tot;
     }
     if (threadIdx.x == 0) a.next_acc_prefix[kept] = carry;
     uint32_t ccarry = 0;
     const uint32_t m2 = 2 * kept;
-    for (uint32_t base = 0; base < m2; base += 1024) {
+    for (uint32_t base = 0; base < m2; base += NT) {
         const uint32_t s = base + threadIdx.x;
         const uint32_t v = s < m2 ? (a.next_nodes[s].len + kChunkRows - 1) / kChunkRows : 0u;
         uint32_t tot;
-        const uint32_t ex = block_excl_scan_u32<1024>(v, wt, tot);
+        const uint32_t ex = block_excl_scan_u32<NT>(v, wt, tot);
         if (s < m2) a.next_chunk_prefix[s] = ccarry + ex;
         ccarry += tot;
     }
@@ -1150,6 +1224,32 @@ __global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
         st->acc_count = kept;
         st->acc_total = carry;
         st->chunk_count = ccarry;
+    }
+}
+
+__global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
+    __shared__ unsigned long long wt64[32];
+    __shared__ uint32_t wt[32];
+    next_level_body<1024>(a, wt64, wt);
+}
+
+// Partition passes; with a.fuse set (depthwise growth) the last CTA of the
+// count pass also scans the chunk counts (k_part_scan) and the last CTA of
+// the scatter pass builds the next level (k_next_level).
+__global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
+    part_count_work(a);
+    if (a.fuse && last_block_done(a.fuse + 1)) {
+        __shared__ uint32_t wt_scan[32];
+        part_scan_body<kPartThreads>(a, wt_scan);
+    }
+}
+
+__global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
+    part_scatter_work(a);
+    if (a.fuse && last_block_done(a.fuse + 2)) {
+        __shared__ unsigned long long wt64_next[32];
+        __shared__ uint32_t wt_next[32];
+        next_level_body<kPartThreads>(a, wt64_next, wt_next);
     }
 }
 
@@ -1340,6 +1440,13 @@ void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
     k_split_node<<<max_m, 32, 0, s>>>(a);
 }
 void launch_decide(const LevelArgs& a, cudaStream_t s) { count_launch(); k_decide<<<1, 1024, 0, s>>>(a); }
+void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
+    dim3 grid(max_m, a.n_features);
+    count_launch();
+    k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    count_launch();
+    k_split_node_decide<<<(max_m + 7) / 8, 256, 0, s>>>(a);
+}
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
     count_launch();
     k_part_count<<<max_chunks, kPartThreads, 0, s>>>(a);

@@ -109,6 +109,8 @@ struct LevelArgs {
     TreeRec* trec;
     uint32_t* tcats;             // [tree node][8]
     const uint32_t* node_hist;   // lossguide: histogram-pool slot of each node (null: level slots)
+    unsigned int* fuse;          // depthwise: 3 zeroed counters; the one-CTA steps run in the last CTA
+                                 // of the kernel before them (null: separate launches)
 };
 
 #ifdef __CUDACC__
@@ -178,6 +180,8 @@ void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_
                        unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
 void launch_decide(const LevelArgs& a, cudaStream_t s);
+// k_split_feat, then per-node reduction and decisions in one launch (a.fuse set)
+void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_part_scan(const LevelArgs& a, cudaStream_t s);
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
