@@ -327,9 +327,10 @@ def run_ours(args, rank, world):
         "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(hist_gbs / hbm_peak, 4) if hist_gbs else None,
                      "traffic": int(HIST_TRAFFIC_RATIO * t["hist_bytes"] / hist_launches) if hist_gbs else None,
-                     "traffic_source": "ncu dram bytes / algorithmic bytes of one tree at 4M rows (ratio 2.08), "
-                                       "scaled to this launch",
-                     "kernel": "k_hist_lpf (histogram), rank 0",
+                     "traffic_source": f"ncu dram bytes / algorithmic bytes of one tree at 4M rows (ratio "
+                                       f"{HIST_TRAFFIC_RATIO:.2f}), scaled to this launch",
+                     "kernel": "k_hist_stage (the histogram kernels of one level), rank 0",
+                     "note": None if hist_gbs else "histogram timing is collected on level-wise trees only",
                      "per_launch_ms": round(t["hist_ms"] / hist_launches, 4),
                      "alg_bytes_per_launch": int(t["hist_bytes"] / hist_launches), "peak_source": peak_src},
         "clocks": clk.summary(),

@@ -559,21 +559,38 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
 
 // Histogram tiles: the enabled features of every block, grouped per kernel.
 // Lane-per-feature tiles take up to 32 features whose [bin][32] planes fit in
-// shared memory (features of at most kLpfMaxBins bins); the remaining features
-// go to row-per-thread tiles sized by the shared-memory budget.
+// shared memory (features of at most kLpfMaxBins bins); wide tiles take up to
+// 8 two-byte features of at most kWideMaxBins bins whose bins lie within 4
+// record chunks (the staged kernel with 8 lanes per row); the remaining
+// features go to row-per-thread tiles sized by the shared-memory budget.
 void TrainCtx::plan_tiles(const uint8_t* enabled) {
     std::vector<uint8_t> en(F_, 1);
     if (enabled) for (uint32_t f = 0; f < F_; f++) en[f] = enabled[f] ? 1 : 0;
     if (tiles_valid_ && en == last_enabled_) return;
-    const uint32_t kLpfMaxBins = 440;  // 440 x 32 lanes x 16 B = 220 KiB
+    const uint32_t kLpfMaxBins = 440;    // 440 x 32 lanes x 16 B = 220 KiB
+    const uint32_t kWideMaxBins = 1024;  // 1028 x 8 lanes x 16 B = 128.5 KiB
+    const uint32_t kWideMaxChunks = 4;
     static const bool force_tpr = [] {
         const char* e = std::getenv("FBGPU_HIST");
         return e && std::string(e) == "tpr";
     }();
-    std::vector<TileDesc> gen[2], lpf[2];
+    // FBGPU_HIST=lpf selects the unstaged lane-per-feature kernel (and no wide tiles)
+    static const bool no_stage = [] {
+        const char* e = std::getenv("FBGPU_HIST");
+        return e && std::string(e) == "lpf";
+    }();
+    static const bool no_wide = [] {
+        const char* e = std::getenv("FBGPU_WIDE");
+        return e && std::string(e) == "0";
+    }();
+    auto is_wide = [&](uint32_t f, uint32_t width) {
+        return !force_tpr && !no_stage && !no_wide && width == 2 && nbins_[f] > kLpfMaxBins &&
+               nbins_[f] <= kWideMaxBins;
+    };
+    std::vector<TileDesc> gen[2], lpf[2], wide;
     std::vector<TileFeat> tf;
-    size_t smem_gen = 16, smem_lpf = 16;
-    uint32_t max_chunks = 0;
+    size_t smem_gen = 16, smem_lpf = 16, smem_wide = 16;
+    uint32_t max_chunks = 0, max_chunks_wide = 0;
     const uint32_t max_local = (uint32_t)((smem_budget_ - 64 * sizeof(TileFeat)) / 16);
     for (const auto& bp : blocks_) {
         const Block& b = *bp;
@@ -608,6 +625,35 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
             cur.n_feat++;
         }
         flush_lpf();
+        // wide tiles
+        TileDesc wd{b.base, b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
+        uint32_t wlo = ~0u, whi = 0;
+        maxb = 0;
+        auto flush_wide = [&]() {
+            if (wd.n_feat == 0) return;
+            wd.local_bins = maxb * kWideLanes;
+            wd.chunk0 = wlo / 16;
+            wd.n_chunks = (whi + 15) / 16 - wd.chunk0;
+            max_chunks_wide = std::max(max_chunks_wide, wd.n_chunks);
+            wide.push_back(wd);
+            smem_wide = std::max(smem_wide, hist_wide_bytes(maxb));
+            wd.feat_begin = (uint32_t)tf.size();
+            wd.n_feat = 0;
+            maxb = 0;
+            wlo = ~0u;
+            whi = 0;
+        };
+        for (uint32_t f : b.feats) {
+            if (!en[f] || !is_wide(f, b.width)) continue;
+            const uint32_t lo = std::min(wlo, feat_byte_[f]), hi = std::max(whi, feat_byte_[f] + 2);
+            if (wd.n_feat == kWideLanes || (hi + 15) / 16 - lo / 16 > kWideMaxChunks) flush_wide();
+            wlo = std::min(wlo, feat_byte_[f]);
+            whi = std::max(whi, feat_byte_[f] + 2);
+            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
+            maxb = std::max(maxb, nbins_[f]);
+            wd.n_feat++;
+        }
+        flush_wide();
         // row-per-thread tiles for the rest
         TileDesc g{b.base, b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
         auto flush_gen = [&]() {
@@ -619,7 +665,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
             g.local_bins = 0;
         };
         for (uint32_t f : b.feats) {
-            if (!en[f] || !(force_tpr || nbins_[f] > kLpfMaxBins)) continue;
+            if (!en[f] || !(force_tpr || nbins_[f] > kLpfMaxBins) || is_wide(f, b.width)) continue;
             if (g.n_feat == 64 || g.local_bins + nbins_[f] > max_local) flush_gen();
             tf.push_back(TileFeat{feat_byte_[f], g.local_bins, nbins_[f], hoff_[f]});
             g.local_bins += nbins_[f];
@@ -630,6 +676,9 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     std::vector<TileDesc> all;
     for (int w = 0; w < 2; w++) { tile_off_gen_[w] = (uint32_t)all.size(); n_gen_[w] = (uint32_t)gen[w].size(); all.insert(all.end(), gen[w].begin(), gen[w].end()); }
     for (int w = 0; w < 2; w++) { tile_off_lpf_[w] = (uint32_t)all.size(); n_lpf_[w] = (uint32_t)lpf[w].size(); all.insert(all.end(), lpf[w].begin(), lpf[w].end()); }
+    tile_off_wide_ = (uint32_t)all.size();
+    n_wide_ = (uint32_t)wide.size();
+    all.insert(all.end(), wide.begin(), wide.end());
     d_tiles_.alloc(sizeof(TileDesc) * std::max<size_t>(all.size(), 1));
     d_tfeat_.alloc(sizeof(TileFeat) * std::max<size_t>(tf.size(), 1));
     if (!all.empty())
@@ -643,10 +692,6 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     set_hist_lpf_smem_limit((int)tile_smem_lpf_);
     // staged lane-per-feature kernel: 4 stages when the histogram leaves room
     // for them in the 227 KiB a CTA may use, else 2, else the unstaged kernel
-    static const bool no_stage = [] {
-        const char* e = std::getenv("FBGPU_HIST");
-        return e && std::string(e) == "lpf";
-    }();
     const size_t kMaxSmem = 227 * 1024;
     hist_stages_ = 0;
     tile_smem_stage_ = 0;
@@ -662,6 +707,11 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
         }
         if (hist_stages_) set_hist_stage_smem_limit((int)tile_smem_stage_);
     }
+    // wide tiles: at most 4 chunks a record, so 4 stages always fit
+    // (128.5 KiB + 32 warps x 4 x 8 rows x 80 B)
+    wide_stages_ = 4;
+    tile_smem_wide_ = smem_wide + hist_stage_bytes(std::max(max_chunks_wide, 1u), wide_stages_);
+    if (n_wide_) set_hist_wide_smem_limit((int)tile_smem_wide_);
     sync();
     last_enabled_ = en;
     tiles_valid_ = true;
@@ -690,6 +740,12 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
             launch_hist_lpf(w + 1, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
                             acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf, tile_smem_lpf_,
                             s_);
+    }
+    if (n_wide_) {
+        const uint32_t grid_wide = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u));
+        launch_hist_wide(wide_stages_, T + tile_off_wide_, n_wide_, TF, rows, fixed_.as<Pair>(), nodes, acc_list,
+                         acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_wide, tile_smem_wide_,
+                         s_);
     }
 }
 
@@ -900,7 +956,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
             const uint64_t acc_nodes = lvl[2 * d] >> 32, rows = lvl[2 * d + 1];
             hist_ms_ += ms;
-            hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0);
+            hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) + (n_wide_ ? 1 : 0);
             hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
         }
     }

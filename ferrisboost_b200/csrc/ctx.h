@@ -181,6 +181,9 @@ class TrainCtx {
     uint32_t tile_off_gen_[2] = {0, 0}, n_gen_[2] = {0, 0}, tile_off_lpf_[2] = {0, 0}, n_lpf_[2] = {0, 0};
     size_t tile_smem_ = 0, tile_smem_lpf_ = 0, tile_smem_stage_ = 0;
     int hist_stages_ = 0;  // staged lane-per-feature histogram: cp.async stages, 0 = unstaged kernel
+    uint32_t tile_off_wide_ = 0, n_wide_ = 0;  // wide tiles (8 lanes per row)
+    size_t tile_smem_wide_ = 0;
+    int wide_stages_ = 4;
     int smem_budget_ = 0;
 
     // rows / gradients

@@ -506,7 +506,7 @@ __device__ __forceinline__ void add64_planes(uint32_t* lo, uint32_t* hi, long lo
     atomicAdd(hi, hi_add);
 }
 
-template <int W, int S>
+template <int W, int S, int LPR>
 __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* __restrict__ tiles,
                                                                  const TileFeat* __restrict__ tfeat,
                                                                  const uint32_t* __restrict__ rows,
@@ -519,28 +519,39 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
                                                                  unsigned long long slot_pairs) {
     extern __shared__ __align__(16) uint32_t sm[];
     const TileDesc td = tiles[blockIdx.y];
-    const uint32_t LB = td.local_bins;  // max bins of the tile x 32
-    // histogram words laid out [bin][plane g_lo, g_hi, h_lo, h_hi][32 lanes]:
-    // one address per (bin, lane) reaches all four planes by fixed offsets,
-    // and the 32 lanes of an atomic still fall in 32 distinct banks
+    const uint32_t LB = td.local_bins;  // max bins of the tile x LPR
+    // LPR = 32 (features up to 440 bins): lane t of a warp owns tile feature
+    // t; words laid out [bin][plane g_lo, g_hi, h_lo, h_hi][32 lanes], so one
+    // address per (bin, lane) reaches all four planes by fixed offsets and the
+    // 32 lanes of an atomic fall in 32 distinct banks.
+    // LPR = 8 (wide features, up to 1024 bins): a warp takes 4 rows at a time,
+    // lanes 8g..8g+7 the 8 tile features of row g; words laid out
+    // [plane][bin][8 lanes] (bins padded to a multiple of 4), so a lane's bank
+    // is 8 (bin mod 4) + feature and the four rows spread over the banks by
+    // their bins.
     const unsigned long long R = st->acc_total;
     const uint32_t n_acc = st->acc_count;
     if (R == 0) return;
     unsigned long long a = R * blockIdx.x / gridDim.x;
     const unsigned long long b = R * (blockIdx.x + 1) / gridDim.x;
     if (a >= b) return;
+    constexpr uint32_t G = 32 / LPR;  // rows per step
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t tl = lane % LPR, grp = lane / LPR;
     const uint32_t nf = td.n_feat, nch = td.n_chunks;
-    uint32_t* hlane = sm + lane;
+    const uint32_t MB = LB / LPR;                       // bins per feature slot (discard row = MB)
+    const uint32_t PS = ((MB + 1 + 3) & ~3u) * LPR;     // words per plane (LPR = 8)
+    const uint32_t hist_words = LPR == 32 ? 4 * (LB + 32) : 4 * PS;
+    uint32_t* hlane = sm + tl;
     const uint32_t rec_bytes = nch * 16u;
     const uint32_t stage_bytes = kStageRows * (rec_bytes + 16u);
-    // bins 0 .. LB/32 - 1, then one discard row that missing bins and idle
+    // bins 0 .. MB - 1, then one discard row that missing bins and idle
     // lanes add to, so the row loop has no branch on the bin
-    const uint32_t discard = LB >> 5;
-    uint8_t* wbuf = reinterpret_cast<uint8_t*>(sm + 4 * (LB + 32)) + (size_t)warp * S * stage_bytes;
+    const uint32_t discard = MB;
+    uint8_t* wbuf = reinterpret_cast<uint8_t*>(sm + hist_words) + (size_t)warp * S * stage_bytes;
     TileFeat f{0, 0, 0, 0};
-    if (lane < nf) f = tfeat[td.feat_begin + lane];
-    const bool active = lane < nf;
+    if (tl < nf) f = tfeat[td.feat_begin + tl];
+    const bool active = tl < nf;
     const uint32_t foff = active ? f.byte_off - td.chunk0 * 16u : 0u;
     // the missing sentinel (255 / 65535) is never below a feature's bin count
     const uint32_t nbins = active ? f.nbins : 0u;
@@ -548,7 +559,7 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
     // copy assignment: lane = (item group g, row q); items of a row are its
     // record chunks 0..nch-1 and its gradient pair (item nch)
     const uint32_t cq = lane & 7u, cg = lane >> 3;
-    for (uint32_t j = threadIdx.x; j < 4 * LB; j += blockDim.x) sm[j] = 0u;
+    for (uint32_t j = threadIdx.x; j < (LPR == 32 ? 4 * LB : hist_words); j += blockDim.x) sm[j] = 0u;
     __syncthreads();
     uint32_t k = find_segment(acc_prefix, n_acc, a);
     while (a < b) {
@@ -605,15 +616,29 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
                 uint32_t bin = W == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
                 bin = bin < nbins ? bin : discard;
                 const Pair gp = gps[q];
-                uint32_t* w = hlane + bin * 128u;
-                add64_planes(w, w + 32, gp.g);
-                add64_planes(w + 64, w + 96, gp.h);
+                if (LPR == 32) {
+                    uint32_t* w = hlane + bin * 128u;
+                    add64_planes(w, w + 32, gp.g);
+                    add64_planes(w + 64, w + 96, gp.h);
+                } else {
+                    uint32_t* w = hlane + bin * LPR;
+                    add64_planes(w, w + PS, gp.g);
+                    add64_planes(w + 2 * PS, w + 3 * PS, gp.h);
+                }
             };
-            if (kq == kStageRows) {
+            if (LPR == 32) {
+                if (kq == kStageRows) {
 #pragma unroll
-                for (uint32_t q = 0; q < kStageRows; q++) row(q);
+                    for (uint32_t q = 0; q < kStageRows; q++) row(q);
+                } else {
+                    for (uint32_t q = 0; q < kq; q++) row(q);
+                }
             } else {
-                for (uint32_t q = 0; q < kq; q++) row(q);
+#pragma unroll
+                for (uint32_t s2 = 0; s2 < kStageRows / G; s2++) {
+                    const uint32_t q = s2 * G + grp;
+                    if (q < kq) row(q);
+                }
             }
             __syncwarp();
             issue(bb + S);
@@ -622,16 +647,17 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
         __syncthreads();
         Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
         for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
-            const uint32_t t = j & 31u, bb = j >> 5;
-            uint32_t* w = sm + bb * 128u + t;
-            const unsigned long long g = ((unsigned long long)w[32] << 32) | w[0];
-            const unsigned long long h = ((unsigned long long)w[96] << 32) | w[64];
+            const uint32_t t = j % LPR, bb = j / LPR;
+            uint32_t* w = LPR == 32 ? sm + bb * 128u + t : sm + bb * LPR + t;
+            const uint32_t o1 = LPR == 32 ? 32u : PS, o2 = LPR == 32 ? 64u : 2 * PS, o3 = LPR == 32 ? 96u : 3 * PS;
+            const unsigned long long g = ((unsigned long long)w[o1] << 32) | w[0];
+            const unsigned long long h = ((unsigned long long)w[o3] << 32) | w[o2];
             if (g | h) {
                 const TileFeat ft = tfeat[td.feat_begin + t];
                 const uint32_t gidx = ft.global_off + bb;
                 if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
                 if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
-                w[0] = 0u; w[32] = 0u; w[64] = 0u; w[96] = 0u;
+                w[0] = 0u; w[o1] = 0u; w[o2] = 0u; w[o3] = 0u;
             }
         }
         __syncthreads();
@@ -1410,10 +1436,28 @@ void launch_hist_lpf(int width, const TileDesc* tiles, uint32_t n_tiles, const T
                                                           st, hist_acc, slot_pairs);
 }
 void set_hist_stage_smem_limit(int bytes) {
-    cudaFuncSetAttribute(k_hist_stage<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    cudaFuncSetAttribute(k_hist_stage<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    cudaFuncSetAttribute(k_hist_stage<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    cudaFuncSetAttribute(k_hist_stage<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<1, 2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<2, 2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<1, 4, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<2, 4, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+void set_hist_wide_smem_limit(int bytes) {
+    cudaFuncSetAttribute(k_hist_stage<2, 2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(k_hist_stage<2, 4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+void launch_hist_wide(int stages, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat, const uint32_t* rows,
+                      const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                      const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                      unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s) {
+    if (n_tiles == 0) return;
+    dim3 grid(grid_x, n_tiles);
+    count_launch();
+    if (stages == 4)
+        k_hist_stage<2, 4, 8><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list,
+                                                                  acc_prefix, st, hist_acc, slot_pairs);
+    else
+        k_hist_stage<2, 2, 8><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list,
+                                                                  acc_prefix, st, hist_acc, slot_pairs);
 }
 void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat,
                        const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
@@ -1423,8 +1467,8 @@ void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_
     dim3 grid(grid_x, n_tiles);
     count_launch();
 #define FB_HS(W, S)                                                                                                \
-    k_hist_stage<W, S><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list, acc_prefix, \
-                                                          st, hist_acc, slot_pairs)
+    k_hist_stage<W, S, 32><<<grid, kHistLpfThreads, smem, s>>>(tiles, tfeat, rows, gpair, nodes, acc_list,         \
+                                                              acc_prefix, st, hist_acc, slot_pairs)
     if (width == 2) {
         if (stages == 4) FB_HS(2, 4); else FB_HS(2, 2);
     } else {

@@ -174,6 +174,17 @@ inline size_t hist_stage_bytes(uint32_t n_chunks, int stages) {
     return (size_t)kStageWarps * stages * kStageRows * (n_chunks * 16 + 16);
 }
 void set_hist_stage_smem_limit(int bytes);
+// Wide features (441..1024 bins, 2-byte bins): the staged kernel with 8 lanes per
+// row (4 rows per warp step), 8 features per tile.
+constexpr uint32_t kWideLanes = 8;
+inline size_t hist_wide_bytes(uint32_t max_bins) {  // four planes, bins + discard padded to 4
+    return 4ull * (((max_bins + 1 + 3) / 4) * 4) * kWideLanes * 4;
+}
+void set_hist_wide_smem_limit(int bytes);
+void launch_hist_wide(int stages, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat, const uint32_t* rows,
+                      const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
+                      const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
+                      unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
 void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat,
                        const uint32_t* rows, const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,
                        const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,

@@ -68,6 +68,25 @@ def test_synthetic_models_byte_identical(oracle, k):
     assert np.array_equal(got.view(np.uint32), ref.predict_margin(X).view(np.uint32))
 
 
+def test_mixed_bin_counts_byte_identical(oracle):
+    # two-byte bins of every histogram tile kind in one block: features up to
+    # 440 bins (lane per feature), 441..1024 bins (8 lanes per row, tiles cut
+    # at 8 features or 4 record chunks) and beyond max_bin's 1024 when a
+    # feature has fewer distinct values than bins; colsample leaves holes
+    rng = np.random.default_rng(31)
+    n = 30000
+    levels = [300, 2000, 700, 50, 1024, 441, 5000, 440, 900, 3000, 600, 128, 1500, 800, 999, 2500, 460]
+    X = np.stack([rng.integers(0, k, n).astype(np.float32) / k for k in levels], axis=1)
+    X[rng.random(X.shape) < 0.03] = np.nan
+    y = (np.nan_to_num(X[:, 1]) + np.nan_to_num(X[:, 4]) ** 2 - np.nan_to_num(X[:, 9]) + rng.normal(0, 0.1, n)).astype(
+        np.float32)
+    for p in (dict(objective="reg:squarederror", max_depth=7, eta=0.3, max_bin=1024),
+              dict(objective="reg:squarederror", max_depth=6, eta=0.3, max_bin=1024, colsample_bytree=0.6, seed=2),
+              dict(objective="reg:squarederror", max_depth=6, eta=0.3, max_bin=512)):
+        m = fb.train(p, X, label=y, num_boost_round=6)
+        assert m.to_json() == oracle.train(X, y, n_rounds=6, **p).json(), p
+
+
 def test_root_only_and_depth_one(oracle):
     X, y = _synthetic(5000, 5, seed=9)
     for depth in (0, 1):
