@@ -8,7 +8,7 @@ boosting round over the resident quantized data.  Synthetic data of the
 config's shape stands in for HIGGS (not in this container).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config c0|c1|c2|c3|c3d14|c4] [--rows R] [--no-cpu]
+                  [--config c0|c1|c2|c3|c3d14|c4] [--rows R] [--no-cpu] [--parquet]
 
 value: exact-mode s/100 rounds from CUDA events on the training stream, bins
 resident in HBM (gradients, glibc-exact expf reproduced on the device,
@@ -278,7 +278,33 @@ def run_ours(args, rank, world):
     m = train_public(p, E2E_ROUNDS)
     json_bytes = len(m.to_json())
     e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    ref_json = m.to_json() if args.parquet else None
     del m
+    e2e_parquet = None
+    if args.parquet and world == 1:
+        # the same 100 rounds from a Parquet file of the workload (written
+        # untimed): column decode, column-major upload, sketch, binning, rounds
+        import tempfile
+        import pyarrow as pa
+        import pyarrow.parquet as pq
+        tmp = tempfile.mkdtemp(prefix="fb_bench_")
+        path = os.path.join(tmp, "train.parquet")
+        names = [f"f{i}" for i in range(F)]
+        pq.write_table(pa.table({**{nm: X[:, i] for i, nm in enumerate(names)}, "label": y}), path,
+                       row_group_size=1 << 20)
+        file_bytes = os.path.getsize(path)
+        t0 = time.perf_counter()
+        m = fb.train(p, path, label="label", num_boost_round=E2E_ROUNDS, feature_types=ft)
+        pq_s = time.perf_counter() - t0
+        same = m.to_json() == ref_json.replace(b'"feature_names":[]', b'"feature_names":' + json.dumps(
+            names, separators=(",", ":")).encode(), 1)
+        del m
+        os.remove(path)
+        os.rmdir(tmp)
+        e2e_parquet = {"value": round(pq_s, 4), "unit": "s/100 rounds", "file_bytes": file_bytes,
+                       "model_equals_array_input": same,
+                       "includes": "pyarrow decode of the Parquet file + column-major upload + device sketch and "
+                                   "binning + 100 rounds + model JSON through the public train(path); wall clock"}
 
     # device-resident steps: W warm-up rounds, then K rounds timed with CUDA
     # events on the training stream, bracketed by barrier + synchronize
@@ -323,6 +349,7 @@ def run_ours(args, rank, world):
                 "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / E2E_ROUNDS),
                 "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "
                             "per-rank bytes; wall clock, max over ranks"},
+        **({"e2e_parquet": e2e_parquet} if e2e_parquet else {}),
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(hist_gbs / hbm_peak, 4) if hist_gbs else None,
@@ -457,6 +484,8 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["c4"])
     ap.add_argument("--rows", type=int, default=0, help="override the config's row count (smaller runs)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--parquet", action="store_true",
+                    help="also time the e2e leg from a Parquet file of the workload (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -20,7 +20,7 @@ from typing import Any, Mapping, NamedTuple, Sequence
 
 import numpy as np
 
-from . import _lib
+from . import _lib, columnar
 
 __all__ = ["train", "Model", "Booster", "Dataset", "build", "lib"]
 
@@ -226,9 +226,20 @@ class Dataset:
         (validation data, or one row shard of a multi-GPU run) instead of
         sketching them.  ``device`` = N sketches and quantizes on CUDA device
         N and keeps the bins there (the same cuts and bins as the host
-        preparation; a booster on that device trains from them in place)."""
-        X = _as_matrix(data, missing)
-        self.n_rows, self.n_features = X.shape
+        preparation; a booster on that device trains from them in place).
+        ``data`` may also be a ``columnar.Columns`` (decoded Parquet / Arrow
+        feature columns, column-major), which the device path ingests as is."""
+        cols = data if isinstance(data, columnar.Columns) else None
+        if cols is not None:
+            X = cols.X
+            self.n_features, self.n_rows = X.shape
+            self.feature_names = list(cols.names)
+            if feature_types is None and cols.categorical is not None:
+                feature_types = ["c" if c else "q" for c in cols.categorical]
+        else:
+            X = _as_matrix(data, missing)
+            self.n_rows, self.n_features = X.shape
+            self.feature_names = None
         w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
         cat = _feature_flags(feature_types, self.n_features)
         self.categorical = cat
@@ -238,11 +249,16 @@ class Dataset:
             if cuts is not None:
                 cv, off = self._check_cuts(cuts)
                 cv = cv if cv.size else np.zeros(1, np.float32)
-            self._h = lib().fb_dataset_on_device(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
-                                                 _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8),
-                                                 _lib.ptr(cv, C.c_float), _lib.ptr(off, C.c_uint32), nthread,
-                                                 int(device))
-        elif cuts is None:
+            make = lib().fb_dataset_on_device_columns if cols is not None else lib().fb_dataset_on_device
+            self._h = make(_lib.ptr(X, C.c_float), self.n_rows, self.n_features, max_bin, _lib.ptr(w, C.c_float),
+                           _lib.ptr(cat, C.c_uint8), _lib.ptr(cv, C.c_float), _lib.ptr(off, C.c_uint32), nthread,
+                           int(device))
+            if not self._h:
+                raise ValueError(_err())
+            return
+        if cols is not None:  # host preparation reads rows
+            X = np.ascontiguousarray(X.T)
+        if cuts is None:
             self._h = lib().fb_dataset_from_dense(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
                                                   _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), nthread)
         else:
@@ -368,6 +384,9 @@ class Model:
             raise RuntimeError(_err())
         self._h = handle
         self.params = dict(params or {})
+        # column names of a Parquet / Arrow training set (src/model/tree.rs:244):
+        # written to the JSON and used to bind prediction columns by name
+        self.feature_names: list[str] | None = None
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -406,7 +425,11 @@ class Model:
         n = lib().fb_model_json(self._h, None, 0)
         buf = C.create_string_buffer(n)
         lib().fb_model_json(self._h, buf, n)
-        return buf.raw[:n]
+        out = buf.raw[:n]
+        if self.feature_names:
+            names = json.dumps(list(self.feature_names), ensure_ascii=False, separators=(",", ":"))
+            out = out.replace(b'"feature_names":[]', b'"feature_names":' + names.encode("utf-8"), 1)
+        return out
 
     def save_model(self, path: str | os.PathLike) -> None:
         """XGBoost-compatible JSON (reference src/model/model_io.rs: atomic write)."""
@@ -429,6 +452,21 @@ class Model:
         lib().fb_model_tree(self._h, t, *[_lib.ptr(v, c) for v, c in zip(a.values(), ct)])
         return a
 
+    def _rows(self, data: Any) -> np.ndarray:
+        """Row-major f32 rows for the prediction entry points."""
+        missing = self.params.get("missing", float("nan"))
+        specs = columnar.path_specs(data)
+        table = None if specs is not None else columnar.arrow_table(data)
+        if specs is None and table is None:
+            return _as_matrix(data, missing)
+        if not self.feature_names:
+            raise ValueError("this model has no feature names to bind Parquet / Arrow columns to; pass an array")
+        if specs is not None:
+            X = columnar.read_file_features(specs, self.feature_names, missing)
+        else:
+            X = columnar.read_table(table, False, None, missing, order=list(self.feature_names), scoring=True).X
+        return np.ascontiguousarray(X.T)
+
     def predict(self, data: Any, output_margin: bool = False, pred_contribs: bool = False, device=None, *,
                 approx_contribs: bool = False, pred_interactions: bool = False, pred_leaf: bool = False):
         """Predictions (probabilities for binary:logistic unless output_margin),
@@ -436,8 +474,10 @@ class Model:
         n x (F+1) with the bias last (pred_contribs; Saabas values with
         approx_contribs), SHAP interaction values n x (F+1) x (F+1)
         (pred_interactions), or the leaf node index of every tree, n x n_trees
-        as float32 (pred_leaf)."""
-        X = _as_matrix(data, self.params.get("missing", float("nan")))
+        as float32 (pred_leaf).  Parquet paths and pyarrow tables bind their
+        columns to the model's feature names (any column order; other columns
+        of a file, such as the label, are not read)."""
+        X = self._rows(data)
         if X.shape[1] != self.n_features:
             raise ValueError(f"data has {X.shape[1]} features, the model has {self.n_features}")
         if sum(bool(v) for v in (pred_contribs, pred_interactions, pred_leaf)) > 1:
@@ -471,8 +511,27 @@ class Model:
 
 def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
           feature_types: Sequence[str] | None = None, quiet: bool = True) -> Model:
-    """Train a model (reference python/ferrisboost/__init__.py:1090 ``train``)."""
+    """Train a model (reference python/ferrisboost/__init__.py:1090 ``train``).
+
+    ``data`` is a 2-D array with ``label`` (and ``weight``) arrays; a
+    ``.parquet`` path, a list of paths, a directory or a glob pattern with
+    ``label`` (and ``weight``) naming columns of the files; or a pyarrow
+    Table / RecordBatch / RecordBatchReader with ``label`` an array
+    (``columnar`` has the decode rules).  Columnar inputs record their column
+    names as the model's feature names."""
     p = _normalize_params(params, num_boost_round)
+    specs = columnar.path_specs(data)
+    table = None if specs is not None else columnar.arrow_table(data)
+    if specs is not None:
+        if not isinstance(label, str):
+            raise ValueError("for file input, label must be the name of a column of the file")
+        if weight is not None and not isinstance(weight, str):
+            raise ValueError("for file input, weight must be the name of a column of the file")
+        data = columnar.read_files(specs, label, weight, feature_types, p["missing"])
+        label, weight, feature_types = data.label, data.weight, None
+    elif table is not None:
+        data = columnar.read_table(table, p["enable_categorical"], feature_types, p["missing"])
+        feature_types = None
     if label is None:
         raise ValueError("label is required for array input")
     ds = Dataset(data, max_bin=p["max_bin"], weight=weight, feature_types=feature_types, nthread=p["nthread"],
@@ -481,4 +540,5 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     b.update(num_boost_round)
     m = b.model()
     m.params = p
+    m.feature_names = ds.feature_names
     return m

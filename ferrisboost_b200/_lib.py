@@ -109,6 +109,8 @@ SIGNATURES = {
     "fb_dataset_with_cuts": (P, [f32p, C.c_uint64, C.c_uint32, f32p, u32p, u8p, C.c_int32]),
     "fb_dataset_on_device": (P, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, f32p, u32p, C.c_int32,
                                  C.c_int32]),
+    "fb_dataset_on_device_columns": (P, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, f32p, u32p,
+                                         C.c_int32, C.c_int32]),
     "fb_dataset_device": (C.c_int32, [P]),
     "fb_sketch_features": (C.c_int64, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, u32p, C.c_uint32,
                                        C.c_int32, f32p, u32p, C.c_uint64]),

@@ -100,7 +100,7 @@ Summary prune(const Summary& e, size_t max_size) {  // sketch.rs:403-435 compres
     return out;
 }
 
-std::vector<float> feature_cuts(const float* X, uint64_t n, uint32_t F, uint32_t f, uint32_t max_bin,
+std::vector<float> feature_cuts(const fbg::HostMatrix& X, uint64_t n, uint32_t f, uint32_t max_bin,
                                 const float* w) {
     const size_t limit = std::max<size_t>((size_t)max_bin * 16, 32);
     std::vector<std::pair<float, float>> buf;
@@ -118,7 +118,7 @@ std::vector<float> feature_cuts(const float* X, uint64_t n, uint32_t F, uint32_t
         }
     };
     for (uint64_t r = 0; r < n; r++) {  // sketch.rs:128-147 push
-        const float v = X[r * F + f];
+        const float v = X.at(r, f);
         const float wt = w ? w[r] : 1.0f;
         if (std::isnan(v) || wt <= 0.0f) continue;
         buf.push_back({v, wt});
@@ -235,7 +235,7 @@ void plan_blocks(Dataset& d) {
     }
 }
 
-void build_blocks(Dataset& d, const float* X, int nth) {
+void build_blocks(Dataset& d, const fbg::HostMatrix& X, int nth) {
     plan_blocks(d);
     for (Dataset::Block& b : d.blocks) b.data.resize(b.feats.size() * d.n * b.width);
     // dense.rs:288-308 quantize_dense (column-major, NaN -> missing)
@@ -247,7 +247,7 @@ void build_blocks(Dataset& d, const float* X, int nth) {
             const uint32_t f = b.feats[i];
             const uint32_t miss = d.missing(f);
             for (uint64_t r = 0; r < d.n; r++) {
-                const float v = X[r * d.F + f];
+                const float v = X.at(r, f);
                 if (v == std::numeric_limits<float>::max()) reserved = 1;
                 const uint32_t bin = std::isnan(v) ? miss : d.bin_of(f, v);
                 if (b.width == 2) reinterpret_cast<uint16_t*>(b.data.data())[(size_t)i * d.n + r] = (uint16_t)bin;
@@ -264,7 +264,7 @@ int threads(int32_t nthread) { return nthread > 0 ? nthread : omp_get_max_thread
 // Cuts of the listed features (numeric: weighted quantile sketch; categorical:
 // 1..max code, sketch.rs:128-136 + categorical.rs:264-266).  Features are
 // independent, so row shards on several ranks may each sketch some features.
-std::vector<std::vector<float>> sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_bin,
+std::vector<std::vector<float>> sketch_features(const fbg::HostMatrix& X, uint64_t n, uint32_t max_bin,
                                                 const float* w, const uint8_t* cat,
                                                 const std::vector<uint32_t>& feats, int nth) {
     std::vector<std::vector<float>> per(feats.size());
@@ -275,7 +275,7 @@ std::vector<std::vector<float>> sketch_features(const float* X, uint64_t n, uint
         if (cat && cat[f]) {
             int32_t max_code = -1;
             for (uint64_t r = 0; r < n; r++) {
-                const float v = X[r * F + f];
+                const float v = X.at(r, f);
                 if (std::isnan(v)) continue;
                 if (v < 0.0f || v > 65533.0f || v != std::trunc(v)) {
 #pragma omp critical
@@ -286,7 +286,7 @@ std::vector<std::vector<float>> sketch_features(const float* X, uint64_t n, uint
             }
             for (int32_t k = 1; k <= std::max(max_code, 0); k++) per[i].push_back((float)k);
         } else {
-            per[i] = feature_cuts(X, n, F, f, max_bin, w);
+            per[i] = feature_cuts(X, n, f, max_bin, w);
         }
     }
     if (!bad.empty()) throw InputError(bad);
@@ -308,13 +308,14 @@ Dataset* dataset_from_dense(const float* X, uint64_t n, uint32_t F, uint32_t max
     const int nth = threads(nthread);
     std::vector<uint32_t> all(F);
     for (uint32_t f = 0; f < F; f++) all[f] = f;
-    std::vector<std::vector<float>> per = sketch_features(X, n, F, max_bin, w, d->cat.data(), all, nth);
+    const fbg::HostMatrix hm{X, F, 1};
+    std::vector<std::vector<float>> per = sketch_features(hm, n, max_bin, w, d->cat.data(), all, nth);
     d->offsets.push_back(0);
     for (uint32_t f = 0; f < F; f++) {
         d->cuts.insert(d->cuts.end(), per[f].begin(), per[f].end());
         d->offsets.push_back((uint32_t)d->cuts.size());
     }
-    build_blocks(*d, X, nth);
+    build_blocks(*d, hm, nth);
     return d.release();
 }
 
@@ -374,7 +375,7 @@ void check_cuts(const uint32_t* offsets, uint32_t F) {
 // since only the order of equal values' weights would differ), categorical
 // cuts from a device max-code scan, and the bins are written straight into
 // the row records the training context reads, which stay on the device.
-Dataset* dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+Dataset* dataset_on_device(const fbg::HostMatrix& X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
                            const uint8_t* categorical, const float* cuts, const uint32_t* offsets, int32_t nthread,
                            int32_t device) {
     if (n == 0 || F == 0) throw InputError("training data must have at least one row and one feature");
@@ -411,7 +412,7 @@ Dataset* dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_
         for (uint32_t f = 0; f < F; f++) all[f] = f;
         std::vector<std::vector<float>> per =
             (w || max_bin * 16ull > fbg::kSketchMaxLimit)
-                ? sketch_features(X, n, F, max_bin, w, d->cat.data(), all, threads(nthread))
+                ? sketch_features(X, n, max_bin, w, d->cat.data(), all, threads(nthread))
                 : device_sketch(M, max_bin, d->cat.data(), all);
         d->offsets.push_back(0);
         for (uint32_t f = 0; f < F; f++) {
@@ -943,7 +944,7 @@ fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const f
         d->cuts.assign(cuts, cuts + offsets[F]);
         d->cat.assign(F, 0);
         if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
-        fbe::build_blocks(*d, X, fbe::threads(nthread));
+        fbe::build_blocks(*d, fbg::HostMatrix{X, F, 1}, fbe::threads(nthread));
         return out.release();
     }, nullptr);
 }
@@ -953,7 +954,19 @@ fb_dataset* fb_dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_
                                  int32_t nthread, int32_t device) {
     return fbe::guarded([&]() -> fb_dataset* {
         std::unique_ptr<fb_dataset> out(new fb_dataset());
-        out->d.reset(fbe::dataset_on_device(X, n, F, max_bin, w, categorical, cuts, offsets, nthread, device));
+        out->d.reset(fbe::dataset_on_device(fbg::HostMatrix{X, F, 1}, n, F, max_bin, w, categorical, cuts, offsets,
+                                            nthread, device));
+        return out.release();
+    }, nullptr);
+}
+
+fb_dataset* fb_dataset_on_device_columns(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
+                                         const uint8_t* categorical, const float* cuts, const uint32_t* offsets,
+                                         int32_t nthread, int32_t device) {
+    return fbe::guarded([&]() -> fb_dataset* {
+        std::unique_ptr<fb_dataset> out(new fb_dataset());
+        out->d.reset(fbe::dataset_on_device(fbg::HostMatrix{X, 1, n}, n, F, max_bin, w, categorical, cuts, offsets,
+                                            nthread, device));
         return out.release();
     }, nullptr);
 }
@@ -974,7 +987,7 @@ int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32
         std::vector<std::vector<float>> per;
         {
             fbe::PrepStream ps(device);
-            fbg::DeviceMatrix M(X, n, F, ps.s);
+            fbg::DeviceMatrix M(fbg::HostMatrix{X, F, 1}, n, F, ps.s);
             per = fbe::device_sketch(M, max_bin, categorical, fs);
         }
         uint64_t total = 0;
@@ -1003,7 +1016,7 @@ int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_
         std::vector<uint32_t> fs(feats, feats + n_feats);
         for (uint32_t f : fs)
             if (f >= F) throw fbe::InputError("feature index out of range");
-        auto per = fbe::sketch_features(X, n, F, max_bin, w, categorical, fs, fbe::threads(nthread));
+        auto per = fbe::sketch_features(fbg::HostMatrix{X, F, 1}, n, max_bin, w, categorical, fs, fbe::threads(nthread));
         uint64_t total = 0;
         for (size_t i = 0; i < per.size(); i++) total += per[i].size();
         if (total > cap) throw fbe::InputError("cuts capacity is too small: need " + std::to_string(total));

@@ -304,7 +304,7 @@ __device__ __forceinline__ float midpoint(float a, float b) {
 // --------------------------------------------------------------- kernels
 // Non-NaN values per (feature, row tile).  Warp j of the CTA counts feature
 // g0 + j of the batch over the tile's rows.
-__global__ void __launch_bounds__(256) k_valid_count(const float* __restrict__ X, uint64_t n, uint32_t F,
+__global__ void __launch_bounds__(256) k_valid_count(const float* __restrict__ X, uint64_t n, uint64_t rs, uint64_t cs,
                                                      const uint32_t* __restrict__ feats, uint32_t nbf,
                                                      uint32_t n_tiles, uint32_t* __restrict__ cnt) {
     const uint32_t tile = blockIdx.x, lane = threadIdx.x & 31u, j = blockIdx.y * kTileFeats + (threadIdx.x >> 5);
@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(256) k_valid_count(const float* __restrict__ X
     const uint32_t rows = (uint32_t)min((uint64_t)kTileRows, n - r0);
     const uint32_t f = feats[j];
     uint32_t c = 0;
-    for (uint32_t r = lane; r < rows; r += 32) c += isnan(X[(r0 + r) * F + f]) ? 0u : 1u;
+    for (uint32_t r = lane; r < rows; r += 32) c += isnan(X[(r0 + r) * rs + f * cs]) ? 0u : 1u;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
     if (lane == 0) cnt[(size_t)j * n_tiles + tile] = c;
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(256) k_valid_count(const float* __restrict__ X
 
 // Stable compaction: the non-NaN values of batch feature j, in row order, to
 // vals[vbase[j] + ...]; tile_off[j * n_tiles + t] = values before tile t.
-__global__ void __launch_bounds__(256) k_compact(const float* __restrict__ X, uint64_t n, uint32_t F,
+__global__ void __launch_bounds__(256) k_compact(const float* __restrict__ X, uint64_t n, uint64_t rs, uint64_t cs,
                                                  const uint32_t* __restrict__ feats, uint32_t nbf, uint32_t n_tiles,
                                                  const unsigned long long* __restrict__ vbase,
                                                  const uint32_t* __restrict__ tile_off, float* __restrict__ vals) {
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(256) k_compact(const float* __restrict__ X, ui
     uint32_t pos = 0;
     for (uint32_t r = 0; r < rows; r += 32) {
         const uint32_t rr = r + lane;
-        const float x = rr < rows ? X[(r0 + rr) * F + f] : __int_as_float(0x7fc00000);
+        const float x = rr < rows ? X[(r0 + rr) * rs + f * cs] : __int_as_float(0x7fc00000);
         const bool ok = !isnan(x);
         const uint32_t bal = __ballot_sync(0xffffffffu, ok);
         if (ok) out[pos + __popc(bal & ((1u << lane) - 1u))] = x;
@@ -492,7 +492,7 @@ __global__ void __launch_bounds__(kSkThreads) k_collapse_cuts(SlotArrays S, cons
 // categorical.rs:264-266 scan: largest valid code of batch feature
 // blockIdx.y; invalid codes (negative, > 65533 or fractional) flag the
 // feature.
-__global__ void __launch_bounds__(256) k_cat_scan(const float* __restrict__ X, uint64_t n, uint32_t F,
+__global__ void __launch_bounds__(256) k_cat_scan(const float* __restrict__ X, uint64_t n, uint64_t rs, uint64_t cs,
                                                   const uint32_t* __restrict__ feats, int* max_code,
                                                   unsigned int* bad) {
     __shared__ int smax[8];
@@ -500,7 +500,7 @@ __global__ void __launch_bounds__(256) k_cat_scan(const float* __restrict__ X, u
     const uint32_t j = blockIdx.y, f = feats[j];
     int mx = -1, b = 0;
     for (uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; r < n; r += (uint64_t)gridDim.x * blockDim.x) {
-        const float x = X[r * F + f];
+        const float x = X[r * rs + f * cs];
         if (isnan(x)) continue;
         if (x < 0.0f || x > 65533.0f || x != truncf(x)) b = 1;
         else mx = max(mx, (int)x);
@@ -520,10 +520,11 @@ __global__ void __launch_bounds__(256) k_cat_scan(const float* __restrict__ X, u
 }
 
 // dense.rs:288-308 quantize_dense into row records, one warp per row: lane i
-// bins block feature i (+32, +64, +96), so reads of X and writes of the
-// record are both contiguous.
+// bins block feature i (+32, +64, +96), so writes of the record are
+// contiguous, and so are reads of a row-major X (a column-major X is read a
+// 32-byte sector per column, shared by the 8 consecutive rows of a CTA).
 template <int W>
-__global__ void __launch_bounds__(256) k_bin_block(const float* __restrict__ X, uint64_t n, uint32_t F,
+__global__ void __launch_bounds__(256) k_bin_block(const float* __restrict__ X, uint64_t n, uint64_t rs, uint64_t cs,
                                                    const uint32_t* __restrict__ bfeats, uint32_t nf,
                                                    const float* __restrict__ cuts, const uint32_t* __restrict__ off,
                                                    const uint8_t* __restrict__ cat, uint8_t* __restrict__ dst,
@@ -548,7 +549,7 @@ __global__ void __launch_bounds__(256) k_bin_block(const float* __restrict__ X, 
         for (int q = 0; q < 4; q++) {
             const uint32_t i = lane + 32u * q;
             if (i >= nf) break;
-            const float x = X[r * F + fid[q]];
+            const float x = X[r * rs + fid[q] * cs];
             if (x == FLT_MAX) res = 1;
             uint32_t bin;
             if (isnan(x)) bin = miss;
@@ -568,8 +569,10 @@ template <class T> void upload(DevMem& d, const std::vector<T>& h, cudaStream_t 
 
 }  // namespace
 
-DeviceMatrix::DeviceMatrix(const float* X_host, uint64_t n, uint32_t F, cudaStream_t stream)
-    : n_(n), F_(F), s_(stream) {
+DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cudaStream_t stream)
+    : n_(n), F_(F), rs_(X_host.rs), cs_(X_host.cs), s_(stream) {
+    if (!((rs_ == F && cs_ == 1) || (rs_ == 1 && cs_ == n)))
+        throw std::invalid_argument("DeviceMatrix: the host matrix must be contiguous row-major or column-major");
     const size_t bytes = (size_t)n * F * sizeof(float);
     FB_CUDA_CHECK(cudaMalloc(&x_, std::max<size_t>(bytes, 16)));
     // pageable source: pinned staging in slabs, two buffers so the host copy
@@ -582,7 +585,7 @@ DeviceMatrix::DeviceMatrix(const float* X_host, uint64_t n, uint32_t F, cudaStre
             stage[i].reserve(slab);
             FB_CUDA_CHECK(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
         }
-        const char* src = reinterpret_cast<const char*>(X_host);
+        const char* src = reinterpret_cast<const char*>(X_host.p);
         int k = 0;
         bool used[2] = {false, false};
         try {
@@ -644,7 +647,7 @@ void DeviceMatrix::numeric_cuts(uint32_t max_bin, const std::vector<uint32_t>& f
         d_cnt.alloc((size_t)nbf * n_tiles * 4);
         dim3 tg(n_tiles, ceil_div(nbf, kTileFeats));
         count_launch();
-        k_valid_count<<<tg, 256, 0, s_>>>(x_, n_, F_, d_feats.as<uint32_t>(), nbf, n_tiles, d_cnt.as<uint32_t>());
+        k_valid_count<<<tg, 256, 0, s_>>>(x_, n_, rs_, cs_, d_feats.as<uint32_t>(), nbf, n_tiles, d_cnt.as<uint32_t>());
         FB_CUDA_CHECK(cudaGetLastError());
         std::vector<uint32_t> cnt((size_t)nbf * n_tiles);
         FB_CUDA_CHECK(cudaMemcpyAsync(cnt.data(), d_cnt.p, cnt.size() * 4, cudaMemcpyDeviceToHost, s_));
@@ -670,7 +673,7 @@ void DeviceMatrix::numeric_cuts(uint32_t max_bin, const std::vector<uint32_t>& f
         upload(d_sbase, sbase, s_);
         d_vals.alloc(std::max<size_t>(vbase[nbf], 1) * 4);
         count_launch();
-        k_compact<<<tg, 256, 0, s_>>>(x_, n_, F_, d_feats.as<uint32_t>(), nbf, n_tiles,
+        k_compact<<<tg, 256, 0, s_>>>(x_, n_, rs_, cs_, d_feats.as<uint32_t>(), nbf, n_tiles,
                                       d_vbase.as<unsigned long long>(), d_toff.as<uint32_t>(), d_vals.as<float>());
         FB_CUDA_CHECK(cudaGetLastError());
         if (n_slots == 0) {  // every batch feature is all-NaN: no cuts
@@ -781,7 +784,7 @@ void DeviceMatrix::categorical_scan(const std::vector<uint32_t>& feats, std::vec
     const uint32_t gx = std::min<uint32_t>(ceil_div(n_, 256), 148u * 4u);
     dim3 grid(gx, (uint32_t)feats.size());
     count_launch();
-    k_cat_scan<<<grid, 256, 0, s_>>>(x_, n_, F_, d_feats.as<uint32_t>(), d_max.as<int>(), d_bad.as<unsigned int>());
+    k_cat_scan<<<grid, 256, 0, s_>>>(x_, n_, rs_, cs_, d_feats.as<uint32_t>(), d_max.as<int>(), d_bad.as<unsigned int>());
     FB_CUDA_CHECK(cudaGetLastError());
     std::vector<uint32_t> bad(feats.size());
     FB_CUDA_CHECK(cudaMemcpyAsync(max_code.data(), d_max.p, feats.size() * 4, cudaMemcpyDeviceToHost, s_));
@@ -803,10 +806,10 @@ bool DeviceMatrix::bin_block(const uint32_t* feats, uint32_t n_feats, uint32_t w
         const uint32_t grid = std::min<uint32_t>(ceil_div(n_, 8), 148u * 16u);
         count_launch();
         if (width == 2)
-            k_bin_block<2><<<grid, 256, 0, s_>>>(x_, n_, F_, d_feats.as<uint32_t>(), n_feats, d_cuts, d_offsets, d_cat,
+            k_bin_block<2><<<grid, 256, 0, s_>>>(x_, n_, rs_, cs_, d_feats.as<uint32_t>(), n_feats, d_cuts, d_offsets, d_cat,
                                                  dst, stride, d_res.as<unsigned int>());
         else
-            k_bin_block<1><<<grid, 256, 0, s_>>>(x_, n_, F_, d_feats.as<uint32_t>(), n_feats, d_cuts, d_offsets, d_cat,
+            k_bin_block<1><<<grid, 256, 0, s_>>>(x_, n_, rs_, cs_, d_feats.as<uint32_t>(), n_feats, d_cuts, d_offsets, d_cat,
                                                  dst, stride, d_res.as<unsigned int>());
         FB_CUDA_CHECK(cudaGetLastError());
     }

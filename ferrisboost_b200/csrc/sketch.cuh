@@ -19,11 +19,21 @@ namespace fbg {
 // the device split search accepts.
 constexpr uint32_t kSketchMaxLimit = 16384;
 
-// A row-major f32 matrix (n x F) resident on one device, with the sketch and
-// binning passes over it.  All work runs on `stream` of the current device.
+// A dense f32 matrix in one contiguous buffer: element (r, f) at
+// p[r * rs + f * cs] (row-major: rs = F, cs = 1; column-major, one column
+// per feature back to back: rs = 1, cs = n).
+struct HostMatrix {
+    const float* p;
+    uint64_t rs, cs;
+    float at(uint64_t r, uint32_t f) const { return p[r * rs + (uint64_t)f * cs]; }
+};
+
+// An f32 matrix (n x F) resident on one device in the layout of its host
+// source, with the sketch and binning passes over it.  All work runs on
+// `stream` of the current device.
 class DeviceMatrix {
    public:
-    DeviceMatrix(const float* X_host, uint64_t n, uint32_t F, cudaStream_t stream);
+    DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cudaStream_t stream);
     ~DeviceMatrix();
     DeviceMatrix(const DeviceMatrix&) = delete;
     DeviceMatrix& operator=(const DeviceMatrix&) = delete;
@@ -48,6 +58,7 @@ class DeviceMatrix {
    private:
     uint64_t n_;
     uint32_t F_;
+    uint64_t rs_, cs_;  // element (r, f) at x_[r * rs_ + f * cs_]
     cudaStream_t s_;
     float* x_ = nullptr;
 };

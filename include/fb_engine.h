@@ -74,6 +74,14 @@ fb_dataset* fb_dataset_with_cuts(const float* X, uint64_t n, uint32_t F, const f
 fb_dataset* fb_dataset_on_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* weights,
                                  const uint8_t* categorical, const float* cuts, const uint32_t* offsets,
                                  int32_t nthread, int32_t device);
+/* fb_dataset_on_device with the features given column-major: X holds F
+ * columns of n values back to back (feature f at X + f * n), the layout a
+ * columnar file (Parquet / Arrow) decodes into; same sketch, bins and errors.
+ * Replaces the column-chunk ingest of src/source/parquet_source.rs:541-620
+ * (open / open_with_cuts) after the reader has decoded the feature columns. */
+fb_dataset* fb_dataset_on_device_columns(const float* X, uint64_t n, uint32_t F, uint32_t max_bin,
+                                         const float* weights, const uint8_t* categorical, const float* cuts,
+                                         const uint32_t* offsets, int32_t nthread, int32_t device);
 /* Device holding the dataset's bins, or -1 for a host dataset. */
 int32_t fb_dataset_device(const fb_dataset* d);
 /* Cuts of the listed features only, with the sketch of fb_dataset_from_dense
