@@ -27,6 +27,7 @@ import base64
 import glob
 import math
 import os
+from concurrent.futures import ThreadPoolExecutor
 from typing import Any, NamedTuple, Sequence
 
 import numpy as np
@@ -143,10 +144,18 @@ def _file_column_f32(col, name: str, missing: float, out: np.ndarray, allow_inf:
                     if col.num_chunks else pa.chunked_array([], dict_values)
             out[:] = np.asarray(col.cast(pa.float64()).to_numpy(zero_copy_only=False), np.float64).astype(np.float32)
         elif t in (pa.float32(), pa.float64()):
-            out[:] = np.asarray(col.to_numpy(zero_copy_only=False)).astype(np.float32)
+            # chunk by chunk into place: a float chunk without nulls is read in
+            # place, and the assignment is the one f64 -> f32 rounding
+            pos = 0
+            for ch in col.chunks:
+                out[pos:pos + len(ch)] = ch.to_numpy(zero_copy_only=False)
+                pos += len(ch)
         elif t in (pa.int32(), pa.int64()):
-            vals = np.asarray(pc.fill_null(col, 0).to_numpy(zero_copy_only=False), np.int64)
-            out[:] = vals.astype(np.float32)
+            pos = 0
+            for ch in col.chunks:
+                vals = (pc.fill_null(ch, 0) if ch.null_count else ch).to_numpy(zero_copy_only=False)
+                out[pos:pos + len(ch)] = vals.astype(np.int64, copy=False)
+                pos += len(ch)
         else:
             raise ValueError(f"column {name!r} is {t}; only numeric columns (float32, float64, int32, int64 or a "
                              "numeric dictionary) are supported")
@@ -198,9 +207,11 @@ def read_files(specs: Sequence[str], label: str | None, weight: str | None, feat
             raise ValueError(f"{f_path} lacks the columns {miss} of {files[0]}")
         table = pq.read_table(f_path, columns=want, use_threads=True)
         for i, name in enumerate(feats):
-            ft = sch.field(name).type
-            dict_cols[i] |= pa.types.is_dictionary(ft)
-            _file_column_f32(table.column(name), name, missing, X[i, r0:r0 + cnt], file_type=ft)
+            dict_cols[i] |= pa.types.is_dictionary(sch.field(name).type)
+        # columns convert in parallel (the numpy copies release the GIL)
+        with ThreadPoolExecutor(max(1, min(F, os.cpu_count() or 1))) as ex:
+            list(ex.map(lambda i: _file_column_f32(table.column(feats[i]), feats[i], missing, X[i, r0:r0 + cnt],
+                                                   file_type=sch.field(feats[i]).type), range(F)))
         for name, out in ((label, y), (weight, w)):
             if name is None:
                 continue
@@ -232,9 +243,10 @@ def read_file_features(specs: Sequence[str], names: Sequence[str], missing: floa
         if miss:
             raise ValueError(f"{f_path} lacks the model's feature columns {miss}")
         table = pq.read_table(f_path, columns=list(names), use_threads=True)
-        for i, name in enumerate(names):
-            _file_column_f32(table.column(name), name, missing, X[i, r0:r0 + cnt], allow_inf=True,
-                             file_type=sch.field(name).type)
+        with ThreadPoolExecutor(max(1, min(len(names), os.cpu_count() or 1))) as ex:
+            list(ex.map(lambda i: _file_column_f32(table.column(names[i]), names[i], missing, X[i, r0:r0 + cnt],
+                                                   allow_inf=True, file_type=sch.field(names[i]).type),
+                        range(len(names))))
         r0 += cnt
     return X
 
