@@ -58,6 +58,7 @@ _DEFAULTS: dict[str, Any] = {  # python/ferrisboost/__init__.py:47-157 (the subs
     "missing": float("nan"),
     "max_cat_to_onehot": 4,
     "max_cat_threshold": 64,
+    "num_class": 0,
 }
 _ALIASES = {  # python/ferrisboost/__init__.py:160-167
     "learning_rate": "eta",
@@ -70,7 +71,7 @@ _ALIASES = {  # python/ferrisboost/__init__.py:160-167
 # (every configuration is resident in HBM), so their values do not change the model.
 _PLANNER_OWNED = ("cols_per_block", "hist_streams", "resident_blocks", "hist_nodes_per_batch", "gpu_memory_budget",
                   "device_quantize")
-_OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1}
+_OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 2, "multi:softmax": 3}
 
 
 def lib():
@@ -103,8 +104,11 @@ def _normalize_params(params: Mapping[str, Any], num_boost_round: int) -> dict[s
         raise ValueError(f"max_bin must be in 1..=65535, got {out['max_bin']}")
     if num_boost_round < 1:
         raise ValueError(f"num_boost_round must be >= 1, got {num_boost_round}")
-    for key in ("max_depth", "max_leaves", "max_bin", "nthread", "seed", "max_cat_to_onehot", "max_cat_threshold"):
+    for key in ("max_depth", "max_leaves", "max_bin", "nthread", "seed", "max_cat_to_onehot", "max_cat_threshold",
+                "num_class"):
         out[key] = int(out[key])
+    if out["objective"].startswith("multi:") and out["num_class"] < 2:  # objective.rs:331-337
+        raise ValueError(f"{out['objective']} requires num_class >= 2, got {out['num_class']}")
     if out["max_leaves"] < 0:
         raise ValueError(f"max_leaves must be >= 0, got {out['max_leaves']}")
     if not 0 <= out["max_depth"] <= 14:
@@ -178,6 +182,7 @@ def _fb_params(p: Mapping[str, Any]) -> _lib.FbParams:
     fp.nthread = p["nthread"]
     fp.gpu_math = 1 if p["gpu_math"] == "fast" else 0
     fp.device = p["device_index"]
+    fp.num_class = p["num_class"] if p["objective"].startswith("multi:") else 0
     return fp
 
 
@@ -365,8 +370,10 @@ class Booster:
         return {k: float(v) for k, v in zip(keys, t)}
 
     def margins(self) -> np.ndarray:
+        """Training margins: n values, or K x n (class-major) for multiclass."""
         n = self._keep[3].n_rows
-        out = np.zeros(n, dtype=np.float32)
+        K = self.params["num_class"] if self.params["objective"].startswith("multi:") else 1
+        out = np.zeros(n if K == 1 else (K, n), dtype=np.float32)
         if lib().fb_booster_margins(self._h, _lib.ptr(out, C.c_float)):
             raise RuntimeError(_err())
         return out
@@ -404,6 +411,11 @@ class Model:
     @property
     def n_features(self) -> int:
         return lib().fb_model_num_features(self._h)
+
+    @property
+    def num_outputs(self) -> int:
+        """num_class for multi:softprob / multi:softmax models, else 1."""
+        return lib().fb_model_num_outputs(self._h)
 
     def _device(self, device=None) -> int:
         d = device if device is not None else self.params.get("device")
@@ -483,13 +495,16 @@ class Model:
         if sum(bool(v) for v in (pred_contribs, pred_interactions, pred_leaf)) > 1:
             raise ValueError("pred_contribs, pred_interactions and pred_leaf are mutually exclusive")
         dev = self._device(device)
+        K = self.num_outputs
+        groups = (K,) if K > 1 else ()  # multiclass: a class axis after the row (explain.rs:704-727)
         kind = None
+        nc = X.shape[1] + 1
         if pred_leaf:
             kind, shape = 0, (X.shape[0], self.num_trees)
         elif pred_contribs and approx_contribs:
-            kind, shape = 1, (X.shape[0], X.shape[1] + 1)
+            kind, shape = 1, (X.shape[0], *groups, nc)
         elif pred_interactions:
-            kind, shape = 2, (X.shape[0], X.shape[1] + 1, X.shape[1] + 1)
+            kind, shape = 2, (X.shape[0], *groups, nc, nc)
         if kind is not None:
             out = np.zeros(shape, dtype=np.float32)
             if lib().fb_model_explain(self._h, kind, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float),
@@ -497,15 +512,21 @@ class Model:
                 raise RuntimeError(_err())
             return out
         if pred_contribs:
-            out = np.zeros((X.shape[0], X.shape[1] + 1), dtype=np.float32)
+            out = np.zeros((X.shape[0], *groups, nc), dtype=np.float32)
             if lib().fb_model_shap(self._h, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float), dev):
                 raise RuntimeError(_err())
             return out
-        out = np.zeros(X.shape[0], dtype=np.float32)
+        out = np.zeros((X.shape[0], *groups), dtype=np.float32)
         if lib().fb_model_predict(self._h, _lib.ptr(X, C.c_float), X.shape[0], _lib.ptr(out, C.c_float), dev):
             raise RuntimeError(_err())
-        if output_margin or self.params.get("objective", "binary:logistic") != "binary:logistic":
+        objective = self.params.get("objective", "binary:logistic")
+        if output_margin or objective == "reg:squarederror":
             return out
+        if K > 1:  # objective.rs:1260-1333: softprob -> probabilities, softmax -> class index
+            classes = np.zeros(X.shape[0], dtype=np.float32)
+            if lib().fb_model_transform(self._h, _lib.ptr(out, C.c_float), X.shape[0], _lib.ptr(classes, C.c_float)):
+                raise RuntimeError(_err())
+            return classes if objective == "multi:softmax" else out
         return (1.0 / (1.0 + np.exp(-out.astype(np.float64)))).astype(np.float32)
 
 

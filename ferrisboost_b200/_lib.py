@@ -30,7 +30,7 @@ class FbParams(C.Structure):
         ("max_delta_step", C.c_float), ("scale_pos_weight", C.c_float), ("subsample", C.c_float),
         ("colsample_bytree", C.c_float), ("base_score", C.c_float), ("seed", C.c_uint64),
         ("max_cat_to_onehot", C.c_uint32), ("max_cat_threshold", C.c_uint32), ("nthread", C.c_int32),
-        ("gpu_math", C.c_int32), ("device", C.c_int32), ("monotone", i8p),
+        ("gpu_math", C.c_int32), ("device", C.c_int32), ("monotone", i8p), ("num_class", C.c_uint32),
     ]
 
 
@@ -143,6 +143,8 @@ SIGNATURES = {
     "fb_model_json": (C.c_int64, [P, C.c_char_p, C.c_int64]),
     "fb_model_tree": (C.c_int64, [P, C.c_uint32, i32p, i32p, u32p, f32p, u8p, f32p, u8p, f32p, f32p, u32p]),
     "fb_model_predict": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
+    "fb_model_num_outputs": (C.c_uint32, [P]),
+    "fb_model_transform": (C.c_int32, [P, f32p, C.c_uint64, f32p]),
     "fb_model_shap": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
     "fb_model_explain": (C.c_int32, [P, C.c_int32, f32p, C.c_uint64, f32p, C.c_int32]),
     "fb_model_device": (P, [P, C.c_int32]),

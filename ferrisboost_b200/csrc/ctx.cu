@@ -398,7 +398,7 @@ GradArgs TrainCtx::grad_args() const {
     a.sub_th = ~0ull;
     a.label = label_.as<float>();
     a.weight = has_weight_ ? weight_.as<float>() : nullptr;
-    a.pred = pred_.as<float>();
+    a.pred = pred_.as<float>() + (size_t)pred_col_ * n_;
     a.host_exp = host_exp_.as<float>();
     a.gpair_in = gpair_f32_.as<float>();
     a.gpair_f32 = gpair_f32_.as<float>();
@@ -500,6 +500,54 @@ void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed,
         if (scales_out) std::memcpy(scales_out, hs, 16);
         if (sum_out) std::memcpy(sum_out, hs + 2, 16);
     }
+}
+
+void TrainCtx::set_outputs(uint32_t K, const float* class_margins) {
+    if (K < 2) throw InputError("a multiclass context needs at least 2 classes");
+    K_ = K;
+    pred_col_ = 0;
+    pred_.alloc((size_t)K * n_ * 4);
+    gp_multi_.alloc((size_t)K * n_ * 8);
+    std::vector<float> v((size_t)K * n_);
+    for (uint32_t k = 0; k < K; k++) std::fill(v.begin() + (size_t)k * n_, v.begin() + (size_t)(k + 1) * n_, class_margins[k]);
+    FB_CUDA_CHECK(cudaMemcpyAsync(pred_.p, v.data(), v.size() * 4, cudaMemcpyHostToDevice, s_));
+    sync();
+}
+
+void TrainCtx::softmax_gradients(int fast) {
+    if (K_ < 2) throw InputError("softmax gradients need a multiclass context");
+    if (!fast && !exptab_.p)
+        throw InputError("exact multiclass gradients on the device need the verified host-expf table");
+    GradArgs a = grad_args();
+    a.pred = pred_.as<float>();
+    launch_softmax_gradients(a, K_, gp_multi_.as<float>(), fast, s_);
+}
+
+void TrainCtx::quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast) {
+    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 32, s_));
+    GradArgs a = grad_args();
+    a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
+    a.gpair_in = gp_multi_.as<float>() + 2ull * k * n_;
+    launch_mask_max(a, s_);  // mod.rs:4811-4842 mask_and_bounds
+    allreduce_u64(a.maxbits, 2, true);
+    double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
+    if (fast) {
+        launch_device_scales(a.maxbits, cfg_.n_rows_global, dscales, s_);
+    } else {
+        unsigned long long* mb = h_small_.as<unsigned long long>();
+        FB_CUDA_CHECK(cudaMemcpyAsync(mb, a.maxbits, 16, cudaMemcpyDeviceToHost, s_));
+        sync();
+        double mg, mh;
+        std::memcpy(&mg, &mb[0], 8);
+        std::memcpy(&mh, &mb[1], 8);
+        if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
+        double* sc = h_small_.as<double>() + 2;
+        sc[0] = pow2_scale_host(mg, cfg_.n_rows_global);
+        sc[1] = pow2_scale_host(mh, cfg_.n_rows_global);
+        FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
+    }
+    launch_quantize(a, s_);
+    reduce_root_sum(false);
 }
 
 void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide) {
@@ -777,7 +825,7 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     // sharded: the accumulated child is chosen by global hessian sums, so no
     // per-level count allreduce is needed (the choice never changes the model)
     a.node_left_global = comm_ ? nullptr : node_left_.as<uint32_t>();
-    a.pred = pred_.as<float>();
+    a.pred = pred_.as<float>() + (size_t)pred_col_ * n_;
     a.trec = trec_.as<TreeRec>();
     a.tcats = tcats_.as<uint32_t>();
     return a;
@@ -987,7 +1035,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
 }
 
 void TrainCtx::download_margins(float* out) {
-    FB_CUDA_CHECK(cudaMemcpyAsync(out, pred_.p, n_ * 4, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(out, pred_.p, (size_t)K_ * n_ * 4, cudaMemcpyDeviceToHost, s_));
     sync();
 }
 

@@ -100,6 +100,19 @@ class TrainCtx {
 
     void build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
 
+    // Multiclass (multi:softprob / multi:softmax, training/mod.rs:2564-2800):
+    // K margin columns, class-major, each starting at its class's base margin.
+    void set_outputs(uint32_t K, const float* class_margins);
+    uint32_t outputs() const { return K_; }
+    // objective.rs:1175-1219 softmax gradients of all K classes from the
+    // current margins (the host expf reproduced on the device unless fast).
+    void softmax_gradients(int fast);
+    // Class k's column: sampling mask keyed by `tree`, bounds, scales (host
+    // libm, or the device in fast mode), fixed point and root sum.
+    void quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast);
+    // The margin column the next build_tree adds its leaf values to.
+    void set_pred_column(uint32_t k) { pred_col_ = k; }
+
     // Row sharding over several GPUs: one context per GPU, one NCCL
     // communicator per context (ranks in the same order on every GPU).
     void set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t timeout_ms);
@@ -188,6 +201,8 @@ class TrainCtx {
 
     // rows / gradients
     DevMem label_, weight_, pred_, gpair_f32_, host_exp_, fixed_;
+    uint32_t K_ = 1, pred_col_ = 0;  // margin columns (classes) and the one the tree updates
+    DevMem gp_multi_;                 // multiclass: K x n f32 gradient pairs of the round
     DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double)
     DevMem exptab_;  // host-expf exception table (fexp.h), empty when unverified
     std::unique_ptr<NcclComm> comm_;

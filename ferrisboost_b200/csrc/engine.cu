@@ -462,13 +462,16 @@ struct Tree {
 struct Model {
     std::vector<Tree> trees;
     float base_score = 0.5f;
-    int objective = 1;
+    int objective = 1;                 // 0 reg:squarederror, 1 binary:logistic, 2 multi:softprob, 3 multi:softmax
     uint32_t n_features = 0;
     float scale_pos_weight = 1.0f;
     std::vector<uint8_t> feature_types;
-    std::unique_ptr<fbgpu_model> dev;  // device copy for prediction / SHAP
+    std::vector<float> class_margins;  // multiclass: one base margin per class (tree.rs:260); tree t is class t % K
+    std::unique_ptr<fbgpu_model> dev;  // device copy of all trees (prediction / SHAP / leaf indices)
+    std::vector<std::unique_ptr<fbgpu_model>> dev_class;  // multiclass: class k's trees, its base margin
     int dev_device = -1;
     size_t dev_trees = 0;
+    uint32_t outputs() const { return class_margins.empty() ? 1u : (uint32_t)class_margins.size(); }
 };
 
 float base_margin(int objective, float base_score) {  // objective.rs:368-399
@@ -535,12 +538,14 @@ std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order 
             if (f) o.push_back(',');
             o += m.feature_types[f] ? "\"c\"" : "\"q\"";
         }
-    const size_t nt = m.trees.size();
+    const size_t nt = m.trees.size(), K = m.outputs();
     o += "],\"gradient_booster\":{\"name\":\"gbtree\",\"model\":{\"gbtree_model_param\":{\"num_trees\":\"" +
          std::to_string(nt) + "\",\"num_parallel_tree\":\"1\"},\"iteration_indptr\":[";
-    for (size_t i = 0; i <= nt; i++) { if (i) o.push_back(','); o += std::to_string(i); }
+    // tree.rs:688-697: K trees per round, tree t belongs to output t % K
+    for (size_t i = 0; i < nt; i += K) { o += std::to_string(i); o.push_back(','); }
+    o += std::to_string(nt);
     o += "],\"tree_info\":[";
-    for (size_t i = 0; i < nt; i++) { if (i) o.push_back(','); o.push_back('0'); }
+    for (size_t i = 0; i < nt; i++) { if (i) o.push_back(','); o += std::to_string(i % K); }
     o += "],\"trees\":[";
     auto iarr = [&](const std::vector<int64_t>& v) {
         o.push_back('[');
@@ -593,21 +598,34 @@ std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order 
         o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
              "\",\"num_nodes\":\"" + std::to_string(nn) + "\",\"size_leaf_vector\":\"1\"}}";
     }
-    o += "]}},\"learner_model_param\":{\"base_score\":\"" + display_f32(m.base_score) +
-         "\",\"boost_from_average\":\"1\",\"num_class\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
-         "\",\"num_target\":\"1\"},\"objective\":{\"name\":\"";
-    o += m.objective == 1 ? "binary:logistic" : "reg:squarederror";
-    o += "\",\"reg_loss_param\":{\"scale_pos_weight\":\"" + display_f32(m.scale_pos_weight) + "\"}}}}";
+    std::string base = display_f32(m.base_score);
+    if (!m.class_margins.empty()) {  // tree.rs:704-720: the vector form "[a,b,c]", margin space
+        base = "[";
+        for (size_t k = 0; k < K; k++) { if (k) base.push_back(','); base += display_f32(m.class_margins[k]); }
+        base.push_back(']');
+    }
+    o += "]}},\"learner_model_param\":{\"base_score\":\"" + base +
+         "\",\"boost_from_average\":\"1\",\"num_class\":\"" + std::to_string(m.class_margins.empty() ? 0 : K) +
+         "\",\"num_feature\":\"" + std::to_string(m.n_features) + "\",\"num_target\":\"1\"},\"objective\":{\"name\":\"";
+    if (m.objective >= 2) {  // objective.rs:816-820 softmax_multiclass_param
+        o += m.objective == 2 ? "multi:softprob" : "multi:softmax";
+        o += "\",\"softmax_multiclass_param\":{\"num_class\":\"" + std::to_string(K) + "\"}}}}";
+    } else {
+        o += m.objective == 1 ? "binary:logistic" : "reg:squarederror";
+        o += "\",\"reg_loss_param\":{\"scale_pos_weight\":\"" + display_f32(m.scale_pos_weight) + "\"}}}}";
+    }
     return o;
 }
 
-fbg::ExplainModel& device_model(Model& m, int device) {
-    if (m.dev && m.dev_device == device && m.dev_trees == m.trees.size()) return m.dev->impl;
+// The device copy of trees cls, cls + step, cls + 2 step, ... (all trees:
+// cls = 0, step = 1) with the given base margin.
+std::unique_ptr<fbgpu_model> upload_trees(const Model& m, int device, size_t cls, size_t step, float bias) {
     std::vector<uint32_t> off{0}, feat, coff, clen, words;
     std::vector<int32_t> left, right;
     std::vector<float> val, hess;
     std::vector<uint8_t> flags;
-    for (const Tree& t : m.trees) {
+    for (size_t ti = cls; ti < m.trees.size(); ti += step) {
+        const Tree& t = m.trees[ti];
         for (const Node& nd : t.nodes) {
             left.push_back(nd.left); right.push_back(nd.right); feat.push_back(nd.feat);
             val.push_back(nd.is_leaf ? nd.leaf : nd.cond); hess.push_back(nd.hess);
@@ -618,12 +636,40 @@ fbg::ExplainModel& device_model(Model& m, int device) {
         }
         off.push_back((uint32_t)left.size());
     }
-    m.dev.reset(new fbgpu_model(device, m.n_features, (uint32_t)m.trees.size(), off.data(), left.data(),
-                                right.data(), feat.data(), val.data(), flags.data(), hess.data(), coff.data(),
-                                clen.data(), words.data(), words.size(), base_margin(m.objective, m.base_score)));
+    return std::unique_ptr<fbgpu_model>(new fbgpu_model(device, m.n_features, (uint32_t)(off.size() - 1), off.data(),
+                                                        left.data(), right.data(), feat.data(), val.data(),
+                                                        flags.data(), hess.data(), coff.data(), clen.data(),
+                                                        words.data(), words.size(), bias));
+}
+
+void ensure_device(Model& m, int device) {
+    if (m.dev && m.dev_device == device && m.dev_trees == m.trees.size()) return;
+    m.dev = upload_trees(m, device, 0, 1, m.class_margins.empty() ? base_margin(m.objective, m.base_score) : 0.0f);
+    m.dev_class.clear();
+    for (size_t k = 0; k < m.class_margins.size(); k++)
+        m.dev_class.push_back(upload_trees(m, device, k, m.class_margins.size(), m.class_margins[k]));
     m.dev_device = device;
     m.dev_trees = m.trees.size();
+}
+
+fbg::ExplainModel& device_model(Model& m, int device) {
+    ensure_device(m, device);
     return m.dev->impl;
+}
+
+// Per-class outputs of a multiclass model (tree.rs:468-480 predict_margins_upto,
+// explain.rs:704-727 one group per class): class k's device model writes
+// `width` values per row into a scratch block, interleaved into out[row][k][..].
+template <class Fn>
+void per_class(Model& m, int device, uint64_t n, size_t width, float* out, Fn&& run) {
+    ensure_device(m, device);
+    const size_t K = m.class_margins.size();
+    std::vector<float> tmp(n * width);
+    for (size_t k = 0; k < K; k++) {
+        run(m.dev_class[k]->impl, tmp.data());
+        for (uint64_t r = 0; r < n; r++)
+            std::memcpy(out + (r * K + k) * width, tmp.data() + r * width, width * sizeof(float));
+    }
 }
 
 // ---------------------------------------------------------------- sampling
@@ -705,6 +751,29 @@ struct Booster {
     std::vector<float> o_gain, o_leaf, o_hess;
 };
 
+// objective.rs:1225-1247 initial_class_margins (XGBoost SoftmaxMultiClassObj
+// InitEstimation): weighted class counts summed in f32 in row order,
+// log((f32)(count / sum_w) + 1e-6) per class, minus their mean taken as
+// 0 + v0/K + v1/K + ... in f32.
+std::vector<float> initial_class_margins(const float* y, const float* w, uint64_t n, uint32_t K) {
+    std::vector<float> bins(K, 0.0f);
+    for (uint64_t i = 0; i < n; i++) bins[(size_t)y[i]] += w ? w[i] : 1.0f;
+    double sum_w = (double)n;
+    if (w) {
+        sum_w = 0.0;
+        for (uint64_t i = 0; i < n; i++) sum_w += (double)w[i];
+    }
+    if (sum_w < 1e-6) return std::vector<float>(K, 0.0f);
+    const double inv = 1.0 / sum_w;
+    std::vector<float> v(K);
+    for (uint32_t k = 0; k < K; k++) v[k] = std::log((float)((double)bins[k] * inv) + 1e-6f);
+    const float kf = (float)K;
+    float mean = 0.0f;
+    for (uint32_t k = 0; k < K; k++) mean = mean + v[k] / kf;
+    for (uint32_t k = 0; k < K; k++) v[k] = v[k] - mean;
+    return v;
+}
+
 Booster* booster_create(const Dataset* d, const float* y, const float* w, const fb_params* pp,
                         const ShardInfo& sh = ShardInfo{}) {
     const fb_params& p = *pp;
@@ -714,7 +783,11 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
         if (!sh.nccl_id && !sh.comm) throw InputError("a row-sharded booster needs an NCCL unique id or communicator");
         if (sh.row_offset + d->n > sh.n_global) throw InputError("row_offset + rows exceeds n_rows_global");
     }
-    if (p.objective != 0 && p.objective != 1) throw InputError("objective must be reg:squarederror or binary:logistic");
+    if (p.objective < 0 || p.objective > 3)
+        throw InputError("objective must be reg:squarederror, binary:logistic, multi:softprob or multi:softmax");
+    const bool multi = p.objective >= 2;
+    if (multi && p.num_class < 2) throw InputError("multi:softprob / multi:softmax need num_class >= 2");
+    if (multi && sh.nranks > 1) throw InputError("multiclass training runs on one GPU in this version");
     if (p.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     if (!(p.subsample > 0.0f && p.subsample <= 1.0f)) throw InputError("subsample must be in (0, 1]");
     if (!(p.colsample_bytree > 0.0f && p.colsample_bytree <= 1.0f)) throw InputError("colsample_bytree must be in (0, 1]");
@@ -725,6 +798,11 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     if (p.objective == 1)
         for (uint64_t i = 0; i < d->n; i++)
             if (y[i] < 0.0f || y[i] > 1.0f) throw InputError("binary:logistic labels must be in [0, 1]");
+    if (multi)  // objective.rs:681-688
+        for (uint64_t i = 0; i < d->n; i++)
+            if (!(y[i] >= 0.0f && y[i] < (float)p.num_class && y[i] == std::trunc(y[i])))
+                throw InputError("multiclass labels must be integers in [0, num_class=" + std::to_string(p.num_class) +
+                                 ")");
     auto b = std::make_unique<Booster>();
     b->d = d;
     b->p = p;
@@ -733,8 +811,9 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     if (p.monotone) b->mono.assign(p.monotone, p.monotone + d->F);
     b->labels.assign(y, y + d->n);
     if (w) b->weights.assign(w, w + d->n);
-    // mod.rs:5470-5495 gradient weights (sample weight x scale_pos_weight on positives)
-    if (p.scale_pos_weight != 1.0f) {
+    // mod.rs:5470-5495 gradient weights (sample weight x scale_pos_weight on
+    // positives; objective.rs uses_scale_pos_weight: not for multiclass)
+    if (p.scale_pos_weight != 1.0f && !multi) {
         b->grad_w.resize(d->n);
         for (uint64_t i = 0; i < d->n; i++) {
             const float wi = w ? w[i] : 1.0f;
@@ -745,6 +824,11 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     }
     // objective.rs:41-61 label mean (FitInterceptGlmLike) when base_score is not given
     float base = p.base_score;
+    if (multi) {  // mod.rs:1430-1450: per-class margins, the given base_score K times
+        b->model.class_margins = std::isnan(base) ? initial_class_margins(y, w, d->n, p.num_class)
+                                                  : std::vector<float>(p.num_class, base);
+        base = b->model.class_margins[0];
+    }
     if (std::isnan(base)) base = label_mean(y, w, d->n);
     if (p.objective == 1 && !(base >= 0.0f && base <= 1.0f))
         throw InputError("logistic base_score is a probability and must be in [0, 1]");
@@ -788,6 +872,11 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
             b->ctx->upload_block(blk.feats.data(), (uint32_t)blk.feats.size(), blk.width, blk.data.data());
     }
     b->ctx->set_labels(y, b->grad_w.empty() ? nullptr : b->grad_w.data(), nullptr, base_margin(p.objective, base));
+    if (multi) {
+        if (p.gpu_math != 1 && !b->ctx->has_exact_exp())
+            throw InputError("exact multiclass training needs the verified host-expf table on the device");
+        b->ctx->set_outputs(p.num_class, b->model.class_margins.data());
+    }
     const uint32_t cap = (2u << p.max_depth);
     b->o_left.resize(cap); b->o_right.resize(cap); b->o_feat.resize(cap); b->o_bin.resize(cap);
     b->o_flags.resize(cap); b->o_cats.resize(8ull * cap); b->o_gain.resize(cap); b->o_leaf.resize(cap);
@@ -796,8 +885,50 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
 }
 
 // One boosting round (training/mod.rs:1895-2311).
+// A finished device tree (fbgpu_tree_out arrays) as a model tree.
+Tree assemble_tree(const Booster& b, const fbgpu_tree_out& out);
+fbgpu_tree_params tree_params(const Booster& b);
+fbgpu_tree_out tree_out(Booster& b);
+
+// One multiclass round (training/mod.rs:2578-2800): the softmax gradients of
+// all K classes from the round's starting margins, then for k = 0..K-1 the
+// tree with index round*K + k (which keys row sampling and colsample_bytree)
+// on class k's gradient column, adding its leaf values to class k's margins.
+void booster_round_multi(Booster& b) {
+    const fb_params& p = b.p;
+    const uint32_t K = p.num_class;
+    const uint64_t th = threshold_for(p.subsample);
+    fbg::TrainCtx& ctx = *b.ctx;
+    const int fast = p.gpu_math == 1 ? 1 : 0;
+    auto t0 = std::chrono::steady_clock::now();
+    ctx.softmax_gradients(fast);
+    double t_grad = 0, t_tree = 0;
+    for (uint32_t k = 0; k < K; k++) {
+        const uint64_t tree = (uint64_t)b.rounds_done * K + k;
+        auto ta = std::chrono::steady_clock::now();
+        ctx.quantize_class(k, th, p.seed, tree, fast);
+        std::vector<uint8_t> en = sample_features(b.d->F, p.colsample_bytree, p.seed, tree);
+        fbgpu_tree_params tp = tree_params(b);
+        fbgpu_tree_out out = tree_out(b);
+        ctx.set_pred_column(k);
+        auto tb = std::chrono::steady_clock::now();
+        ctx.build_tree(tp, p.colsample_bytree < 1.0f ? en.data() : nullptr, &out);
+        auto tc = std::chrono::steady_clock::now();
+        b.model.trees.push_back(assemble_tree(b, out));
+        t_grad += std::chrono::duration<double, std::milli>(tb - ta).count();
+        t_tree += std::chrono::duration<double, std::milli>(tc - tb).count();
+    }
+    ctx.set_pred_column(0);
+    b.rounds_done++;
+    b.t_grad += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count() - t_tree;
+    b.t_tree += t_tree;
+    (void)t_grad;
+}
+
+// One boosting round (training/mod.rs:1895-2311).
 void booster_round(Booster& b) {
     const fb_params& p = b.p;
+    if (p.objective >= 2) return booster_round_multi(b);
     const uint64_t n = b.d->n;
     const uint32_t round = b.rounds_done;
     const uint64_t th = threshold_for(p.subsample);
@@ -845,19 +976,37 @@ void booster_round(Booster& b) {
     }
     auto t1 = std::chrono::steady_clock::now();
     std::vector<uint8_t> en = sample_features(b.d->F, p.colsample_bytree, p.seed, round);
+    fbgpu_tree_params tp = tree_params(b);
+    fbgpu_tree_out out = tree_out(b);
+    ctx.build_tree(tp, p.colsample_bytree < 1.0f ? en.data() : nullptr, &out);
+    auto t2 = std::chrono::steady_clock::now();
+    b.model.trees.push_back(assemble_tree(b, out));
+    b.rounds_done++;
+    b.t_grad += std::chrono::duration<double, std::milli>(t1 - t0).count();
+    b.t_tree += std::chrono::duration<double, std::milli>(t2 - t1).count();
+}
+
+fbgpu_tree_params tree_params(const Booster& b) {
+    const fb_params& p = b.p;
     fbgpu_tree_params tp{};
     tp.eta = p.eta; tp.lambda = p.lambda; tp.gamma = p.gamma; tp.min_child_weight = p.min_child_weight;
     tp.alpha = p.alpha; tp.max_delta_step = p.max_delta_step; tp.max_depth = p.max_depth;
     tp.max_leaves = p.max_leaves; tp.max_cat_to_onehot = p.max_cat_to_onehot;
     tp.max_cat_threshold = p.max_cat_threshold; tp.grow_policy = p.grow_policy;
     tp.monotone = b.mono.empty() ? nullptr : b.mono.data();
+    return tp;
+}
+
+fbgpu_tree_out tree_out(Booster& b) {
     fbgpu_tree_out out{};
     out.capacity = (uint32_t)b.o_left.size();
     out.left = b.o_left.data(); out.right = b.o_right.data(); out.feat = b.o_feat.data(); out.bin = b.o_bin.data();
     out.gain = b.o_gain.data(); out.leaf = b.o_leaf.data(); out.hess = b.o_hess.data(); out.flags = b.o_flags.data();
     out.cats = b.o_cats.data();
-    ctx.build_tree(tp, p.colsample_bytree < 1.0f ? en.data() : nullptr, &out);
-    auto t2 = std::chrono::steady_clock::now();
+    return out;
+}
+
+Tree assemble_tree(const Booster& b, const fbgpu_tree_out& out) {
     Tree t;
     t.nodes.resize(out.n_nodes);
     for (uint32_t i = 0; i < out.n_nodes; i++) {
@@ -877,10 +1026,7 @@ void booster_round(Booster& b) {
             nd.cond = b.d->threshold(nd.feat, out.bin[i]);
         }
     }
-    b.model.trees.push_back(std::move(t));
-    b.rounds_done++;
-    b.t_grad += std::chrono::duration<double, std::milli>(t1 - t0).count();
-    b.t_tree += std::chrono::duration<double, std::milli>(t2 - t1).count();
+    return t;
 }
 
 template <class F> auto guarded(F&& f, decltype(f()) fail) -> decltype(f()) {
@@ -1161,6 +1307,7 @@ fb_model* fb_booster_model(fb_booster* h) {
     m->n_features = b->model.n_features;
     m->scale_pos_weight = b->model.scale_pos_weight;
     m->feature_types = b->model.feature_types;
+    m->class_margins = b->model.class_margins;
     return m;
 }
 
@@ -1214,7 +1361,39 @@ int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* rig
 
 int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {
     return fbe::guarded([&]() -> int32_t {
-        fbe::device_model(*m, device).predict_host(X, n, out);
+        if (m->outputs() > 1)
+            fbe::per_class(*m, device, n, 1, out, [&](fbg::ExplainModel& e, float* o) { e.predict_host(X, n, o); });
+        else
+            fbe::device_model(*m, device).predict_host(X, n, out);
+        return 0;
+    }, 1);
+}
+
+uint32_t fb_model_num_outputs(const fb_model* m) { return m->outputs(); }
+
+int32_t fb_model_transform(const fb_model* m, float* margins, uint64_t n, float* classes) {
+    return fbe::guarded([&]() -> int32_t {
+        const uint32_t K = m->outputs();
+        if (m->objective < 2 || K < 2) throw fbe::InputError("fb_model_transform is for multiclass models");
+        for (uint64_t r = 0; r < n; r++) {
+            float* row = margins + r * K;
+            if (m->objective == 3) {  // objective.rs:1324-1333 argmax, first maximum
+                uint32_t best = 0;
+                for (uint32_t k = 1; k < K; k++)
+                    if (row[k] > row[best]) best = k;
+                if (classes) classes[r] = (float)best;
+            } else {  // objective.rs:1308-1322 softmax_in_place
+                float wmax = row[0];
+                for (uint32_t k = 1; k < K; k++) wmax = std::fmax(row[k], wmax);
+                double wsum = 0.0;
+                for (uint32_t k = 0; k < K; k++) {
+                    row[k] = std::exp(row[k] - wmax);
+                    wsum += (double)row[k];
+                }
+                const float d = (float)wsum;
+                for (uint32_t k = 0; k < K; k++) row[k] /= d;
+            }
+        }
         return 0;
     }, 1);
 }
@@ -1228,14 +1407,24 @@ fbgpu_model* fb_model_device(fb_model* m, int32_t device) {
 
 int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {
     return fbe::guarded([&]() -> int32_t {
-        fbe::device_model(*m, device).shap_host(X, n, out);
+        if (m->outputs() > 1)
+            fbe::per_class(*m, device, n, (size_t)m->n_features + 1, out,
+                           [&](fbg::ExplainModel& e, float* o) { e.shap_host(X, n, o); });
+        else
+            fbe::device_model(*m, device).shap_host(X, n, out);
         return 0;
     }, 1);
 }
 
 int32_t fb_model_explain(fb_model* m, int32_t kind, const float* X, uint64_t n, float* out, int32_t device) {
     return fbe::guarded([&]() -> int32_t {
-        fbe::device_model(*m, device).explain_host(kind, X, n, out);
+        if (m->outputs() > 1 && (kind == 1 || kind == 2)) {  // per class: n x K x (F+1) [x (F+1)]
+            const size_t nc = (size_t)m->n_features + 1;
+            fbe::per_class(*m, device, n, kind == 1 ? nc : nc * nc, out,
+                           [&](fbg::ExplainModel& e, float* o) { e.explain_host(kind, X, n, o); });
+        } else {
+            fbe::device_model(*m, device).explain_host(kind, X, n, out);  // leaf indices: all trees in order
+        }
         return 0;
     }, 1);
 }

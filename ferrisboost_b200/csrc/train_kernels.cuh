@@ -152,6 +152,10 @@ void launch_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint
                          cudaStream_t s);
 void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s);
 void launch_quantize(const GradArgs& a, cudaStream_t s);
+// objective.rs:1175-1219 softmax gradients of K classes: margins a.pred
+// (K x a.n, class-major), labels, optional weights -> out (K x a.n f32 pairs,
+// class-major).  fast: CUDA expf; else the host expf (a.exptab).
+void launch_softmax_gradients(const GradArgs& a, uint32_t K, float* out, int fast, cudaStream_t s);
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
                           cudaStream_t s);
 void set_hist_smem_limit(int bytes);

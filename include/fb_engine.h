@@ -26,7 +26,7 @@ typedef struct fb_model fb_model;
 /* Training parameters (TrainParams, src/types.rs:433-686, and the objective /
  * base_score of TrainConfig, src/training/mod.rs:627-675). */
 typedef struct fb_params {
-    int32_t objective;          /* 0 reg:squarederror, 1 binary:logistic */
+    int32_t objective;          /* 0 reg:squarederror, 1 binary:logistic, 2 multi:softprob, 3 multi:softmax */
     int32_t grow_policy;        /* 0 depthwise, 1 lossguide */
     uint32_t max_depth;
     uint32_t max_leaves;
@@ -48,6 +48,7 @@ typedef struct fb_params {
     int32_t gpu_math;           /* 0 exact, 1 fast */
     int32_t device;
     const int8_t* monotone;     /* n_features or NULL */
+    uint32_t num_class;         /* multi:softprob / multi:softmax: classes, >= 2 (K trees per round) */
 } fb_params;
 
 void fb_default_params(fb_params* p);
@@ -162,16 +163,27 @@ int64_t fb_model_json(const fb_model* m, char* buf, int64_t cap);
  * receives 8 words per node (the right-going category set). */
 int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* right, uint32_t* feat, float* cond,
                       uint8_t* default_left, float* leaf, uint8_t* is_leaf, float* gain, float* hess, uint32_t* cats);
-/* Raw margins of host rows, computed on the device. */
+/* Raw margins of host rows, computed on the device: n values, or n x K
+ * (row-major) for a multiclass model of K outputs (src/model/tree.rs:468-480
+ * predict_margins_upto). */
 int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, int32_t device);
+/* Outputs per row: num_class for multi:softprob / multi:softmax, else 1. */
+uint32_t fb_model_num_outputs(const fb_model* m);
+/* Multiclass prediction transform of n x K margins (objective.rs:1260-1333
+ * transform_rows): multi:softprob turns each row into probabilities in
+ * place; multi:softmax writes each row's class index (first maximum) to
+ * classes[r]. */
+int32_t fb_model_transform(const fb_model* m, float* margins, uint64_t n, float* classes);
 /* The model's device copy on `device` as an include/fbgpu.h handle (owned by
  * the model, valid until the model is freed or gains trees), for
  * fbgpu_predict_device / fbgpu_shap_device on device-resident rows. */
 struct fbgpu_model* fb_model_device(fb_model* m, int32_t device);
-/* SHAP contributions n x (F+1) on the device. */
+/* SHAP contributions n x (F+1) on the device; n x K x (F+1) for a
+ * multiclass model (one group per class, src/model/explain.rs:704-727). */
 int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device);
 /* Leaf indices (kind 0, n x n_trees), Saabas contributions (kind 1,
- * n x (F+1)) or SHAP interaction values (kind 2, n x (F+1)^2) on the device
+ * n x (F+1)) or SHAP interaction values (kind 2, n x (F+1)^2) on the device;
+ * kinds 1 and 2 of a multiclass model carry a class axis after the row
  * (the reference's predict(pred_leaf / approx_contribs / pred_interactions),
  * src/model/explain.rs Kind). */
 int32_t fb_model_explain(fb_model* m, int32_t kind, const float* X, uint64_t n, float* out, int32_t device);

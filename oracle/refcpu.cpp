@@ -571,6 +571,7 @@ struct Model {
     std::vector<Tree> trees;
     float base_score = 0.5f;
     int objective = 1;
+    std::vector<float> class_margins;  // multiclass: one base margin per class (tree.rs:260)
     uint32_t n_features = 0;
     float scale_pos_weight = 1.0f;
     std::vector<uint8_t> feature_types;
@@ -593,6 +594,45 @@ inline GP gradient_of(float pred, float label, int objective) {
         return {s - label, h < 1e-16f ? 1e-16f : h};
     }
     return {pred - label, 1.0f};
+}
+
+// objective.rs:1175-1219 softmax_gradients of one row: wmax starts at the
+// smallest positive normal f32 (XGBoost's numeric_limits<float>::min()),
+// the exps are summed in f64, p = exp / (f32)sum, h = max(2 p (1 - p) w, 1e-16)
+// and the label's class takes p - 1; g = p w.
+inline void softmax_row(const float* m, uint32_t K, float label, float wt, GP* out) {
+    float wmax = std::numeric_limits<float>::min();
+    for (uint32_t k = 0; k < K; k++) wmax = std::fmax(m[k], wmax);
+    double wsum = 0.0;
+    for (uint32_t k = 0; k < K; k++) wsum += (double)std::exp(m[k] - wmax);
+    for (uint32_t k = 0; k < K; k++) {
+        float p = std::exp(m[k] - wmax) / (float)wsum;
+        const float h = std::fmax(2.0f * p * (1.0f - p) * wt, 1e-16f);
+        if (label == (float)k) p -= 1.0f;
+        out[k] = {p * wt, h};
+    }
+}
+
+// objective.rs:1225-1247 initial_class_margins (XGBoost SoftmaxMultiClassObj
+// InitEstimation): weighted class frequencies counted in f32 in row order,
+// log(freq + kRtEps), minus their mean (0 + v0/K + v1/K + ... in f32).
+std::vector<float> initial_class_margins(const float* y, uint64_t n, const float* w, uint32_t K) {
+    std::vector<float> bins(K, 0.0f);
+    for (uint64_t i = 0; i < n; i++) bins[(size_t)y[i]] += w ? w[i] : 1.0f;
+    double sum_w = (double)n;
+    if (w) {
+        sum_w = 0.0;
+        for (uint64_t i = 0; i < n; i++) sum_w += (double)w[i];
+    }
+    if (sum_w < (double)kRtEps) return std::vector<float>(K, 0.0f);
+    const double inv = 1.0 / sum_w;
+    std::vector<float> logs(K);
+    for (uint32_t k = 0; k < K; k++) logs[k] = std::log((float)((double)bins[k] * inv) + kRtEps);
+    const float nk = (float)K;
+    float mean = 0.0f;
+    for (uint32_t k = 0; k < K; k++) mean = mean + logs[k] / nk;
+    for (uint32_t k = 0; k < K; k++) logs[k] = logs[k] - mean;
+    return logs;
 }
 
 // objective.rs:41-61 label_mean; objective.rs:403-474 initial_base_score
@@ -938,6 +978,73 @@ Tree build_tree_lossguide(Ctx& C, const std::vector<FX>& gpair, FX root_sum, con
     return t;
 }
 
+// training/mod.rs:2564-2800 train_multiclass_rounds (exact, host gradients):
+// per round one softmax gradient of all K classes from the round's starting
+// margins; then for class k = 0..K-1 the tree with index round*K + k keys the
+// row sampling and colsample_bytree, its gradient column is masked, bounded
+// and quantized, and the tree (the single-output builder) updates the class's
+// margins before the next class's tree.
+void train_multiclass(Ctx& C, Model* m, const float* y, const float* w, uint64_t n, uint32_t F) {
+    const rc_params& p = C.P.p;
+    const uint32_t K = p.num_class;
+    m->class_margins = std::isnan(p.base_score) ? initial_class_margins(y, n, w, K)
+                                                : std::vector<float>(K, p.base_score);
+    m->base_score = m->class_margins[0];
+    std::vector<std::vector<float>> preds(K);
+    for (uint32_t k = 0; k < K; k++) preds[k].assign(n, m->class_margins[k]);
+    std::vector<GP> gp((size_t)K * n);
+    std::vector<GP> col(n);
+    std::vector<FX> fixed(n);
+    const uint64_t sub_th = threshold_for(p.subsample);
+    const int nth = C.nth;
+    for (uint32_t round = 0; round < p.n_rounds; round++) {
+        auto t_round = std::chrono::steady_clock::now();
+#pragma omp parallel num_threads(nth)
+        {
+            std::vector<float> mr(K);
+            std::vector<GP> out(K);
+#pragma omp for schedule(static)
+            for (int64_t i = 0; i < (int64_t)n; i++) {
+                for (uint32_t k = 0; k < K; k++) mr[k] = preds[k][i];
+                softmax_row(mr.data(), K, y[i], w ? w[i] : 1.0f, out.data());
+                for (uint32_t k = 0; k < K; k++) gp[(size_t)k * n + i] = out[k];
+            }
+        }
+        for (uint32_t k = 0; k < K; k++) {
+            const uint64_t tree = (uint64_t)round * K + k;
+            double mg = 0.0, mh = 0.0;
+#pragma omp parallel for reduction(max : mg, mh) num_threads(nth)
+            for (int64_t i = 0; i < (int64_t)n; i++) {  // mod.rs:4811-4842 mask_and_bounds
+                GP g = gp[(size_t)k * n + i];
+                if (sub_th != UINT64_MAX && (row_hash((uint64_t)i, p.seed, tree) >> 11) >= sub_th) g = {0.0f, 0.0f};
+                col[i] = g;
+                mg = std::max(mg, finite_abs(g.g));
+                mh = std::max(mh, finite_abs(g.h));
+            }
+            if (!std::isfinite(mg) || !std::isfinite(mh)) throw std::runtime_error("non-finite gradient or Hessian");
+            Quantizer q = Quantizer::from_scales(pow2_scale(mg, n), pow2_scale(mh, n));
+            int64_t sg = 0, sh = 0;
+#pragma omp parallel for reduction(+ : sg, sh) num_threads(nth)
+            for (int64_t i = 0; i < (int64_t)n; i++) {
+                FX f = q.to_fixed(col[i]);
+                fixed[i] = f;
+                sg = (int64_t)((uint64_t)sg + (uint64_t)f.g);
+                sh = (int64_t)((uint64_t)sh + (uint64_t)f.h);
+            }
+            std::vector<uint8_t> enabled;
+            if (p.colsample_bytree < 1.0f) {
+                enabled.assign(F, 0);
+                for (uint32_t f : sample_features(F, p.colsample_bytree, p.seed, tree)) enabled[f] = 1;
+            }
+            const uint8_t* en = enabled.empty() ? nullptr : enabled.data();
+            Tree t = p.grow_policy == 1 ? build_tree_lossguide(C, fixed, FX{sg, sh}, q, preds[k], en)
+                                        : build_tree_depthwise(C, fixed, FX{sg, sh}, q, preds[k], en);
+            m->trees.push_back(std::move(t));
+        }
+        g_round_s.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t_round).count());
+    }
+}
+
 Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const float* w, const rc_params* rp) {
     Params P;
     P.p = *rp;
@@ -976,6 +1083,18 @@ Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const 
             gw[i] = y[i] == 1.0f ? wi * p.scale_pos_weight : wi;
         }
         gwp = gw.data();
+    }
+    if (p.objective >= 2) {  // objective.rs:642-690 validate_labels
+        if (p.num_class < 2) { g_err = "multi:softprob / multi:softmax need num_class >= 2"; delete m; return nullptr; }
+        for (uint64_t i = 0; i < n; i++)
+            if (!(y[i] >= 0.0f && y[i] < (float)p.num_class && y[i] == std::trunc(y[i]))) {
+                g_err = "multiclass labels must be integers in [0, num_class)";
+                delete m;
+                return nullptr;
+            }
+        g_setup_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_setup).count();
+        train_multiclass(C, m, y, w, n, F);
+        return m;
     }
     m->base_score = std::isnan(p.base_score) ? estimate_base_score(y, n, w) : p.base_score;
     float margin = base_margin(p.objective, m->base_score);
@@ -1121,11 +1240,14 @@ std::string model_json(const Model& m) {
         o += "[]";
     }
     size_t nt = m.trees.size();
+    const size_t K = m.class_margins.empty() ? 1 : m.class_margins.size();
     o += ",\"gradient_booster\":{\"name\":\"gbtree\",\"model\":{\"gbtree_model_param\":{\"num_trees\":\"" +
          std::to_string(nt) + "\",\"num_parallel_tree\":\"1\"},\"iteration_indptr\":[";
-    for (size_t i = 0; i <= nt; i++) { if (i) o.push_back(','); o += std::to_string(i); }
+    for (size_t i = 0; i < nt; i += K) { if (i) o.push_back(','); o += std::to_string(i); }  // tree.rs:690-697
+    if (nt) o.push_back(',');
+    o += std::to_string(nt);
     o += "],\"tree_info\":[";
-    for (size_t i = 0; i < nt; i++) { if (i) o.push_back(','); o.push_back('0'); }
+    for (size_t i = 0; i < nt; i++) { if (i) o.push_back(','); o += std::to_string(i % K); }
     o += "],\"trees\":[";
     auto fj = [](float v) { return fmt_f32_json(v); };
     auto ij = [](int64_t v) { return std::to_string(v); };
@@ -1182,11 +1304,22 @@ std::string model_json(const Model& m) {
         o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
              "\",\"num_nodes\":\"" + std::to_string(nn) + "\",\"size_leaf_vector\":\"1\"}}";
     }
-    o += "]}},\"learner_model_param\":{\"base_score\":\"" + fmt_f32_display(m.base_score) +
-         "\",\"boost_from_average\":\"1\",\"num_class\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
-         "\",\"num_target\":\"1\"},\"objective\":{\"name\":\"";
-    o += m.objective == 1 ? "binary:logistic" : "reg:squarederror";
-    o += "\",\"reg_loss_param\":{\"scale_pos_weight\":\"" + fmt_f32_display(m.scale_pos_weight) + "\"}}}}";
+    std::string base = fmt_f32_display(m.base_score);
+    if (!m.class_margins.empty()) {  // tree.rs:704-720: the vector form "[a,b,c]"
+        base = "[";
+        for (size_t k = 0; k < K; k++) { if (k) base.push_back(','); base += fmt_f32_display(m.class_margins[k]); }
+        base.push_back(']');
+    }
+    o += "]}},\"learner_model_param\":{\"base_score\":\"" + base +
+         "\",\"boost_from_average\":\"1\",\"num_class\":\"" + std::to_string(m.class_margins.empty() ? 0 : K) +
+         "\",\"num_feature\":\"" + std::to_string(m.n_features) + "\",\"num_target\":\"1\"},\"objective\":{\"name\":\"";
+    if (m.objective >= 2) {  // objective.rs:816-820 softmax_multiclass_param
+        o += m.objective == 2 ? "multi:softprob" : "multi:softmax";
+        o += "\",\"softmax_multiclass_param\":{\"num_class\":\"" + std::to_string(K) + "\"}}}}";
+    } else {
+        o += m.objective == 1 ? "binary:logistic" : "reg:squarederror";
+        o += "\",\"reg_loss_param\":{\"scale_pos_weight\":\"" + fmt_f32_display(m.scale_pos_weight) + "\"}}}}";
+    }
     return o;
 }
 
@@ -1442,6 +1575,28 @@ void* rc_train(const float* X, uint64_t n, uint32_t F, const float* y, const flo
 
 void rc_model_free(void* m) { delete (Model*)m; }
 uint32_t rc_model_num_trees(void* m) { return (uint32_t)((Model*)m)->trees.size(); }
+void rc_softmax_gradients(const float* margins, const float* y, const float* w, uint64_t n, uint32_t K, float* out) {
+    std::vector<float> mr(K);
+    std::vector<GP> g(K);
+    for (uint64_t i = 0; i < n; i++) {
+        for (uint32_t k = 0; k < K; k++) mr[k] = margins[(size_t)k * n + i];
+        softmax_row(mr.data(), K, y[i], w ? w[i] : 1.0f, g.data());
+        for (uint32_t k = 0; k < K; k++) {
+            out[2 * ((size_t)k * n + i)] = g[k].g;
+            out[2 * ((size_t)k * n + i) + 1] = g[k].h;
+        }
+    }
+}
+
+void rc_class_margins(const float* y, const float* w, uint64_t n, uint32_t K, float* out) {
+    std::vector<float> v = initial_class_margins(y, n, w, K);
+    for (uint32_t k = 0; k < K; k++) out[k] = v[k];
+}
+
+uint32_t rc_model_num_outputs(void* m) {
+    const Model* M = (Model*)m;
+    return M->class_margins.empty() ? 1u : (uint32_t)M->class_margins.size();
+}
 float rc_model_base_margin(void* m) { Model* M = (Model*)m; return base_margin(M->objective, M->base_score); }
 
 int64_t rc_model_json(void* m, char* buf, int64_t cap) {
@@ -1472,6 +1627,17 @@ void rc_predict_margin(void* mp, const float* X, uint64_t n, float* out, int32_t
     const Model& m = *(Model*)mp;
     float bm = base_margin(m.objective, m.base_score);
     int nth = n_threads(nthread);
+    if (!m.class_margins.empty()) {  // tree.rs:468-480 predict_margins_upto: n x K, row-major
+        const size_t K = m.class_margins.size();
+#pragma omp parallel for schedule(static) num_threads(nth)
+        for (int64_t r = 0; r < (int64_t)n; r++) {
+            const float* x = X + (size_t)r * m.n_features;
+            float* o = out + (size_t)r * K;
+            for (size_t k = 0; k < K; k++) o[k] = m.class_margins[k];
+            for (size_t t = 0; t < m.trees.size(); t++) o[t % K] += tree_leaf_value(m.trees[t], x);
+        }
+        return;
+    }
 #pragma omp parallel for schedule(static) num_threads(nth)
     for (int64_t r = 0; r < (int64_t)n; r++) {  // tree.rs:498-510 predict_margin_upto
         const float* x = X + (size_t)r * m.n_features;
@@ -1485,32 +1651,39 @@ void rc_shap(void* mp, const float* X, uint64_t n, float* out, int32_t nthread) 
     const Model& m = *(Model*)mp;
     const uint32_t F = m.n_features;
     const uint32_t nc = F + 1;
-    double sum = 0.0;  // explain.rs:527-539 group_root_mean
-    for (const Tree& t : m.trees) sum += root_mean(t.nodes, 0);
-    float root_mean_f = (float)sum;
-    float bias = base_margin(m.objective, m.base_score);
+    const size_t K = m.class_margins.empty() ? 1 : m.class_margins.size();
+    std::vector<double> sums(K, 0.0);  // explain.rs:527-539 group_root_mean, one group per output
+    for (size_t t = 0; t < m.trees.size(); t++) sums[t % K] += root_mean(m.trees[t].nodes, 0);
+    std::vector<float> group_mean(K), bias(K);
+    for (size_t g = 0; g < K; g++) {
+        group_mean[g] = (float)sums[g];
+        bias[g] = m.class_margins.empty() ? base_margin(m.objective, m.base_score) : m.class_margins[g];
+    }
     const Rule& R = rule();
     int nth = n_threads(nthread);
 #pragma omp parallel num_threads(nth)
     {
         std::vector<float> path(F, kUnseen), tc(nc, 0.0f);
 #pragma omp for schedule(dynamic, 16)
-        for (int64_t r = 0; r < (int64_t)n; r++) {  // explain.rs:704-728 shap_row
+        for (int64_t r = 0; r < (int64_t)n; r++) {  // explain.rs:704-728 shap_row: groups g, trees g, g + K, ...
             const float* x = X + (size_t)r * F;
-            float* p = out + (size_t)r * nc;
-            for (uint32_t c = 0; c < nc; c++) p[c] = 0.0f;
-            for (const Tree& t : m.trees) {
-                std::fill(tc.begin(), tc.end(), 0.0f);
-                if (!t.nodes[0].is_leaf) {
-                    ShapRunner run{t.nodes, x, R, path.data(), tc.data()};
-                    float ones[kPts], h[kPts];
-                    for (int i = 0; i < kPts; i++) { ones[i] = 1.0f; h[i] = 0.0f; }
-                    run.run_node(0, ones, 1.0f, h);
+            for (size_t g = 0; g < K; g++) {
+                float* p = out + ((size_t)r * K + g) * nc;
+                for (uint32_t c = 0; c < nc; c++) p[c] = 0.0f;
+                for (size_t ti = g; ti < m.trees.size(); ti += K) {
+                    const Tree& t = m.trees[ti];
+                    std::fill(tc.begin(), tc.end(), 0.0f);
+                    if (!t.nodes[0].is_leaf) {
+                        ShapRunner run{t.nodes, x, R, path.data(), tc.data()};
+                        float ones[kPts], h[kPts];
+                        for (int i = 0; i < kPts; i++) { ones[i] = 1.0f; h[i] = 0.0f; }
+                        run.run_node(0, ones, 1.0f, h);
+                    }
+                    for (uint32_t c = 0; c + 1 < nc; c++) p[c] += tc[c];
                 }
-                for (uint32_t c = 0; c + 1 < nc; c++) p[c] += tc[c];
+                p[nc - 1] += group_mean[g];
+                p[nc - 1] += bias[g];
             }
-            p[nc - 1] += root_mean_f;
-            p[nc - 1] += bias;
         }
     }
 }

@@ -22,7 +22,7 @@ extern "C" {
 
 /* Training parameters; field meanings follow TrainParams (src/types.rs:433-686). */
 typedef struct rc_params {
-    int32_t objective;          /* 0 reg:squarederror, 1 binary:logistic */
+    int32_t objective;          /* 0 reg:squarederror, 1 binary:logistic, 2 multi:softprob, 3 multi:softmax */
     int32_t grow_policy;        /* 0 depthwise, 1 lossguide */
     uint32_t n_rounds;
     uint32_t max_depth;
@@ -44,6 +44,7 @@ typedef struct rc_params {
     int32_t nthread;            /* 0 = all cores */
     const int8_t* monotone;     /* n_features entries or NULL */
     const uint8_t* categorical; /* n_features entries or NULL */
+    uint32_t num_class;         /* multi:softprob / multi:softmax: classes (>= 2) */
 } rc_params;
 
 void rc_default_params(rc_params* p);
@@ -60,6 +61,13 @@ void rc_model_free(void* model);
 uint32_t rc_model_num_trees(void* model);
 /* XGBoost-compatible JSON; returns the length (writes at most cap bytes). */
 int64_t rc_model_json(void* model, char* buf, int64_t cap);
+/* objective.rs:1175-1219 softmax gradients: margins K x n (class-major) ->
+ * out K x n (g, h) pairs; w may be NULL. */
+void rc_softmax_gradients(const float* margins, const float* y, const float* w, uint64_t n, uint32_t K, float* out);
+/* objective.rs:1225-1247 initial_class_margins. */
+void rc_class_margins(const float* y, const float* w, uint64_t n, uint32_t K, float* out);
+/* Outputs per row: num_class for a multiclass model, else 1. */
+uint32_t rc_model_num_outputs(void* model);
 /* Flat tree arrays of tree t (node count returned; arrays may be NULL). */
 int64_t rc_model_tree(void* model, uint32_t t, uint32_t* feat, float* cond,
                       int32_t* left, int32_t* right, uint8_t* default_left,

@@ -25,7 +25,7 @@ class rc_params(C.Structure):
         ("scale_pos_weight", C.c_float), ("subsample", C.c_float), ("colsample_bytree", C.c_float),
         ("base_score", C.c_float), ("seed", C.c_uint64), ("max_cat_to_onehot", C.c_uint32),
         ("max_cat_threshold", C.c_uint32), ("nthread", C.c_int32),
-        ("monotone", C.POINTER(C.c_int8)), ("categorical", C.POINTER(C.c_uint8)),
+        ("monotone", C.POINTER(C.c_int8)), ("categorical", C.POINTER(C.c_uint8)), ("num_class", C.c_uint32),
     ]
 
 
@@ -38,7 +38,7 @@ class rc_split(C.Structure):
 
 
 _P = C.c_void_p
-OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1}
+OBJECTIVES = {"reg:squarederror": 0, "binary:logistic": 1, "multi:softprob": 2, "multi:softmax": 3}
 
 
 def _ptr(a, ctype):
@@ -61,6 +61,12 @@ class RefCPU:
         lib.rc_model_free.argtypes = [_P]
         lib.rc_model_num_trees.argtypes = [_P]
         lib.rc_model_num_trees.restype = C.c_uint32
+        lib.rc_model_num_outputs.argtypes = [_P]
+        lib.rc_model_num_outputs.restype = C.c_uint32
+        lib.rc_softmax_gradients.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                             C.c_uint64, C.c_uint32, C.POINTER(C.c_float)]
+        lib.rc_class_margins.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_float), C.c_uint64, C.c_uint32,
+                                         C.POINTER(C.c_float)]
         lib.rc_model_json.argtypes = [_P, C.c_char_p, C.c_int64]
         lib.rc_model_json.restype = C.c_int64
         lib.rc_model_base_margin.argtypes = [_P]
@@ -130,6 +136,24 @@ class RefCPU:
         if not h:
             raise RuntimeError(self.lib.rc_last_error().decode())
         return RefModel(self, h, X.shape[1])
+
+    def softmax_gradients(self, margins, y, w=None):
+        """margins K x n (class-major) -> K x n x 2 (g, h)."""
+        m = np.ascontiguousarray(margins, dtype=np.float32)
+        K, n = m.shape
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        w = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+        out = np.zeros((K, n, 2), dtype=np.float32)
+        self.lib.rc_softmax_gradients(_ptr(m, C.c_float), _ptr(y, C.c_float), _ptr(w, C.c_float), n, K,
+                                      _ptr(out, C.c_float))
+        return out
+
+    def class_margins(self, y, K, w=None):
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        w = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+        out = np.zeros(K, dtype=np.float32)
+        self.lib.rc_class_margins(_ptr(y, C.c_float), _ptr(w, C.c_float), y.shape[0], K, _ptr(out, C.c_float))
+        return out
 
     def last_timing(self):
         setup = C.c_double()
@@ -223,15 +247,24 @@ class RefModel:
         self.rc.lib.rc_model_json(self.h, buf, n)
         return buf.raw[:n]
 
+    @property
+    def num_outputs(self):
+        return self.rc.lib.rc_model_num_outputs(self.h)
+
     def predict_margin(self, X, nthread=0):
+        """Raw margins: n values, or n x num_class for a multiclass model."""
         X = np.ascontiguousarray(X, dtype=np.float32)
-        out = np.zeros(X.shape[0], dtype=np.float32)
+        k = self.num_outputs
+        out = np.zeros(X.shape[0] if k == 1 else (X.shape[0], k), dtype=np.float32)
         self.rc.lib.rc_predict_margin(self.h, _ptr(X, C.c_float), X.shape[0], _ptr(out, C.c_float), nthread)
         return out
 
     def shap(self, X, nthread=0):
+        """n x (F+1), or n x K x (F+1) for a multiclass model."""
         X = np.ascontiguousarray(X, dtype=np.float32)
-        out = np.zeros((X.shape[0], X.shape[1] + 1), dtype=np.float32)
+        k = self.num_outputs
+        out = np.zeros((X.shape[0], X.shape[1] + 1) if k == 1 else (X.shape[0], k, X.shape[1] + 1),
+                       dtype=np.float32)
         self.rc.lib.rc_shap(self.h, _ptr(X, C.c_float), X.shape[0], _ptr(out, C.c_float), nthread)
         return out
 
