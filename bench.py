@@ -8,7 +8,7 @@ boosting round over the resident quantized data.  Synthetic data of the
 config's shape stands in for HIGGS (not in this container).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config c0|c1|c2|c3|c3d14|c4] [--rows R] [--no-cpu] [--parquet]
+                  [--config c0|c1|c1mc|c2|c3|c3d14|c4] [--rows R] [--no-cpu] [--parquet]
 
 value: exact-mode s/100 rounds from CUDA events on the training stream, bins
 resident in HBM (gradients, glibc-exact expf reproduced on the device,
@@ -86,6 +86,17 @@ def make_mixed(n, seed=0):
     return X, y.astype(np.float32), ["q"] * 80 + ["c"] * 20
 
 
+def make_multiclass(n, seed=0, K=5):
+    """Multiclass workload (no BASELINE config names one): configs[1]'s 28
+    N(0,1) features; the label is the argmax of K random linear scores plus
+    Gumbel noise (a softmax model's draw)."""
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, N_FEATURES), dtype=np.float32)
+    W = rng.standard_normal((N_FEATURES, K)).astype(np.float32) * 0.5
+    z = X @ W + rng.gumbel(size=(n, K)).astype(np.float32)
+    return X, np.argmax(z, axis=1).astype(np.float32), None
+
+
 CONFIGS = {
     "c0": dict(make=make_data, rows=1_000_000,
                params=dict(PARAMS, max_depth=6),
@@ -102,6 +113,10 @@ CONFIGS = {
                workload="configs[3] reg:squarederror 10M x (80 numeric, 5% NaN + 20 categorical x 64), "
                         "lossguide max_leaves 255, max_depth 6 (default; the cap does not bind), max_bin 1024, "
                         "eta 0.05, gpu_math exact"),
+    "c1mc": dict(make=make_multiclass, rows=11_000_000,
+                 params=dict(PARAMS, objective="multi:softprob", num_class=5),
+                 workload="multiclass multi:softprob, 5 classes, 11M x 28 (configs[1] shape), depth 8, max_bin 256, "
+                          "eta 0.1, gpu_math exact: 5 trees per round"),
     "c3d14": dict(make=make_mixed, rows=10_000_000,
                   params={"objective": "reg:squarederror", "grow_policy": "lossguide", "max_leaves": 255,
                           "max_bin": 1024, "eta": 0.05, "max_depth": 14},

@@ -263,6 +263,7 @@ void TrainCtx::set_features(const uint32_t* n_bins, const uint8_t* width, const 
     hoff_.assign(F_ + 1, 0);
     for (uint32_t f = 0; f < F_; f++) {
         if (width_[f] != 1 && width_[f] != 2) throw InputError("bin width must be 1 or 2 bytes");
+        if (width_[f] == 1 && nbins_[f] > 256) throw InputError("one-byte bins hold at most 256 bins");
         if (nbins_[f] == 0) throw InputError("a feature has at least one bin");
         if (nbins_[f] > 1024) throw InputError("device split search supports at most 1024 bins per feature");
         if (cat_[f] && nbins_[f] > 256) throw InputError("device categorical splits support at most 256 categories");
@@ -329,7 +330,9 @@ void TrainCtx::register_block(std::unique_ptr<Block> b) {
     for (uint32_t f = 0; f < F_; f++) {
         if (feat_block_[f] < 0) { floc[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
         const Block& blk = *blocks_[feat_block_[f]];
-        const uint32_t miss = blk.width == 2 ? 65535u : 255u;
+        // the missing sentinel: 65535 / 255, none for a full-range one-byte
+        // feature (256 bins: it holds no missing value)
+        const uint32_t miss = blk.width == 2 ? 65535u : (nbins_[f] <= 255u ? 255u : 0xffffffffu);
         if (blk.cols.p)
             floc[f] = FeatLoc{blk.cols.as<uint8_t>() + (size_t)(feat_byte_[f] / blk.width) * n_ * blk.width, blk.width,
                               0, blk.width, miss};

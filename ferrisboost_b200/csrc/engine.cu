@@ -169,6 +169,7 @@ struct Dataset {
     std::vector<uint32_t> offsets;  // F+1
     std::vector<uint8_t> cat;       // F
     std::vector<uint8_t> width;     // F: bytes per bin
+    std::vector<uint8_t> has_nan;   // F: the feature holds a NaN (empty: unknown)
     struct Block {
         std::vector<uint32_t> feats;
         uint32_t width;
@@ -202,11 +203,17 @@ struct Dataset {
 // blocks of one width; the device stores every block row-major with a
 // 16-byte-padded record, so a block holds at most 64 16-bit or 128 8-bit
 // features (128-byte records).
+// Bin width per feature (the reference's bins.rs:58-66 picks u8 up to 255
+// bins, keeping 255 for missing): one byte up to 255 bins, and also at
+// exactly 256 bins when the feature holds no missing value (every byte value
+// is then a bin; d.has_nan decides, unknown counts as missing); categorical
+// features keep two byte values for missing and invalid codes.
 void plan_blocks(Dataset& d) {
     d.width.resize(d.F);
     for (uint32_t f = 0; f < d.F; f++) {
         const uint32_t nb = d.n_bins(f);
-        const bool wide = d.cat[f] ? nb > 254u : nb > 255u;
+        const bool nan = d.has_nan.empty() || d.has_nan[f] != 0;
+        const bool wide = d.cat[f] ? nb > 254u : (nb > 256u || (nb == 256u && nan));
         d.width[f] = wide ? 2 : 1;
     }
     d.feat_block.assign(d.F, -1);
@@ -236,6 +243,15 @@ void plan_blocks(Dataset& d) {
 }
 
 void build_blocks(Dataset& d, const fbg::HostMatrix& X, int nth) {
+    // NaN flags of the 256-bin numeric features (the only ones whose width they decide)
+    d.has_nan.assign(d.F, 1);
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nth)
+    for (int64_t f = 0; f < (int64_t)d.F; f++) {
+        if (d.cat[f] || d.n_bins((uint32_t)f) != 256u) continue;
+        uint8_t any = 0;
+        for (uint64_t r = 0; r < d.n && !any; r++) any = std::isnan(X.at(r, (uint32_t)f)) ? 1 : 0;
+        d.has_nan[f] = any;
+    }
     plan_blocks(d);
     for (Dataset::Block& b : d.blocks) b.data.resize(b.feats.size() * d.n * b.width);
     // dense.rs:288-308 quantize_dense (column-major, NaN -> missing)
@@ -421,6 +437,7 @@ Dataset* dataset_on_device(const fbg::HostMatrix& X, uint64_t n, uint32_t F, uin
         }
     }
     phase("sketch");
+    d->has_nan = M.nan_features();
     plan_blocks(*d);
     fbg::DevMem d_cuts, d_off, d_cat;
     d_cuts.alloc(std::max<size_t>(d->cuts.size(), 1) * 4);

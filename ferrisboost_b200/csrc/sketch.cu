@@ -519,6 +519,16 @@ __global__ void __launch_bounds__(256) k_cat_scan(const float* __restrict__ X, u
     }
 }
 
+// Which features hold a NaN: one coalesced pass over the matrix; a NaN sets
+// its feature's flag with a plain store (every writer stores 1).
+__global__ void __launch_bounds__(256) k_nan_scan(const float* __restrict__ X, uint64_t n, uint32_t F, uint64_t cs,
+                                                  uint8_t* __restrict__ flags) {
+    const uint64_t total = n * F;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x)
+        if (isnan(X[e])) flags[cs == 1 ? (uint32_t)(e % F) : (uint32_t)(e / n)] = 1;
+}
+
 // dense.rs:288-308 quantize_dense into row records, one warp per row: lane i
 // bins block feature i (+32, +64, +96), so writes of the record are
 // contiguous, and so are reads of a row-major X (a column-major X is read a
@@ -610,6 +620,22 @@ DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cud
         }
         for (auto& e : done) cudaEventDestroy(e);
     }
+}
+
+std::vector<uint8_t> DeviceMatrix::nan_features() {
+    DevMem d_flags;
+    d_flags.alloc(std::max<uint32_t>(F_, 1));
+    FB_CUDA_CHECK(cudaMemsetAsync(d_flags.p, 0, std::max<uint32_t>(F_, 1), s_));
+    if (n_ && F_) {
+        const uint64_t blocks = std::min<uint64_t>(ceil_div((uint64_t)n_ * F_, 256), 148ull * 16);
+        count_launch();
+        k_nan_scan<<<(unsigned)blocks, 256, 0, s_>>>(x_, n_, F_, cs_, d_flags.as<uint8_t>());
+        FB_CUDA_CHECK(cudaGetLastError());
+    }
+    std::vector<uint8_t> out(F_);
+    if (F_) FB_CUDA_CHECK(cudaMemcpyAsync(out.data(), d_flags.p, F_, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s_));
+    return out;
 }
 
 DeviceMatrix::~DeviceMatrix() {

@@ -54,6 +54,8 @@ class DeviceMatrix {
     // f32::MAX (reserved, dense.rs:300).
     bool bin_block(const uint32_t* feats, uint32_t n_feats, uint32_t width, const float* d_cuts,
                    const uint32_t* d_offsets, const uint8_t* d_cat, uint8_t* dst, uint32_t stride);
+    // Features holding at least one NaN (1) or none (0), F entries.
+    std::vector<uint8_t> nan_features();
 
    private:
     uint64_t n_;

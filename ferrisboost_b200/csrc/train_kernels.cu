@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
                 const TileFeat f = tf[t];
                 uint32_t bin = W == 2 ? (uint32_t)(*reinterpret_cast<const uint16_t*>(rec + f.byte_off))
                                       : (uint32_t)rec[f.byte_off];
-                if (bin == td.missing || bin >= f.nbins) continue;
+                if (bin >= f.nbins) continue;  // missing sentinels lie at or above every feature's bin count
                 const uint32_t idx = f.local_off + bin;
                 plane_add(glo, ghi, idx, gp.g);
                 plane_add(hlo, hhi, idx, gp.h);
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_lpf(const TileDesc* __
 #pragma unroll
             for (int q = 0; q < kLpfRows; q++) {
                 const uint32_t r = __shfl_sync(0xffffffffu, rid, q);
-                bin[q] = td.missing;
+                bin[q] = 0xffffffffu;
                 gp[q] = Pair{0, 0};
                 if ((uint32_t)q < kk) {
                     gp[q] = gpair[r];
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_lpf(const TileDesc* __
             }
 #pragma unroll
             for (int q = 0; q < kLpfRows; q++) {
-                if (bin[q] != td.missing && bin[q] < f.nbins) {
+                if (bin[q] < f.nbins) {  // missing sentinels lie at or above every feature's bin count
                     const uint32_t idx = bin[q] * 32u + lane;
                     plane_add(glo, ghi, idx, gp[q].g);
                     plane_add(hlo, hhi, idx, gp[q].h);

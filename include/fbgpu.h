@@ -159,6 +159,9 @@ void fbgpu_comm_free(fbgpu_comm* comm);
 
 /* Feature metadata: bins per feature (cuts + 1), storage width in bytes
  * (bins.rs:58-66 BinWidth::for_feature) and categorical flags (may be NULL).
+ * One-byte bins hold up to 255 bins with 255 as the missing value, or
+ * exactly 256 bins for a feature that holds no missing value (every byte
+ * value is a bin; the reference would store such a feature in two bytes).
  * Replaces the cuts half of GpuTrainCtx::block_session_bins
  * (src/backend/mod.rs:352-362). */
 fbgpu_status fbgpu_set_features(fbgpu_ctx* ctx, const uint32_t* n_bins, const uint8_t* width,
