@@ -278,6 +278,7 @@ void TrainCtx::set_features(const uint32_t* n_bins, const uint8_t* width, const 
     d_mono_.alloc(F_);
     FB_CUDA_CHECK(cudaMemsetAsync(d_mono_.p, 0, F_, s_));
     d_floc_.alloc(sizeof(FeatLoc) * F_);
+    d_floc_rec_.alloc(sizeof(FeatLoc) * F_);
     tiles_valid_ = false;
     buf_depth_ = 0xffffffffu;  // histogram slots depend on total_bins
     ensure_tree_buffers(cfg_.max_depth, cfg_.max_leaves);
@@ -320,7 +321,7 @@ void TrainCtx::register_block(std::unique_ptr<Block> b) {
                                   s_);
         FB_CUDA_CHECK(cudaGetLastError());
     }
-    std::vector<FeatLoc> floc(F_);
+    std::vector<FeatLoc> floc(F_), floc_rec(F_);
     const int bi = (int)blocks_.size();
     for (uint32_t i = 0; i < (uint32_t)b->feats.size(); i++) {
         feat_block_[b->feats[i]] = bi;
@@ -328,7 +329,7 @@ void TrainCtx::register_block(std::unique_ptr<Block> b) {
     }
     blocks_.push_back(std::move(b));
     for (uint32_t f = 0; f < F_; f++) {
-        if (feat_block_[f] < 0) { floc[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
+        if (feat_block_[f] < 0) { floc[f] = floc_rec[f] = FeatLoc{nullptr, 0, 0, 1, 255}; continue; }
         const Block& blk = *blocks_[feat_block_[f]];
         // the missing sentinel: 65535 / 255, none for a full-range one-byte
         // feature (256 bins: it holds no missing value)
@@ -338,8 +339,10 @@ void TrainCtx::register_block(std::unique_ptr<Block> b) {
                               0, blk.width, miss};
         else
             floc[f] = FeatLoc{blk.base, blk.stride, feat_byte_[f], blk.width, miss};
+        floc_rec[f] = FeatLoc{blk.base, blk.stride, feat_byte_[f], blk.width, miss};
     }
     FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_.p, floc.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_floc_rec_.p, floc_rec.data(), sizeof(FeatLoc) * F_, cudaMemcpyHostToDevice, s_));
     sync();
     tiles_valid_ = false;
 }
@@ -813,6 +816,7 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.max_onehot = tp.max_cat_to_onehot;
     a.max_cat_threshold = tp.max_cat_threshold;
     a.floc = d_floc_.as<FeatLoc>();
+    a.floc_rec = d_floc_rec_.as<FeatLoc>();
     a.st = state_.as<TreeState>();
     a.hist_acc = hist_acc_.as<Pair>();
     a.slot_pairs = std::max<uint64_t>(total_bins_, 1);
@@ -914,6 +918,20 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         }
         a.fuse = fuse_.as<unsigned int>();
     }
+    // Leaf values reach the margins either by one walk of the finished tree
+    // per row (k_tree_walk; the last level then needs no partition) or per
+    // partition chunk and k_leaf_final.  Measured on B200: the walk is faster
+    // up to a few million local rows (C0, 1M rows: -3 %), the partition path
+    // beyond (C1, 11M rows: the walk is +2 %).  FBGPU_WALK=0 / 1 forces one.
+    static const int walk_env = [] {
+        const char* e = std::getenv("FBGPU_WALK");
+        return e ? std::atoi(e) : -1;
+    }();
+    a.walk = walk_env >= 0 ? (walk_env ? 1u : 0u) : (n_ <= (4ull << 20) ? 1u : 0u);
+    if (blocks_.size() == 1 && blocks_[0]->stride <= 64 && blocks_[0]->stride % 4 == 0) {
+        a.walk_rec = blocks_[0]->base;
+        a.walk_stride = blocks_[0]->stride;
+    }
     const uint32_t maxd = tp.max_depth;
     FB_CUDA_CHECK(cudaEventRecord(ev0_, s_));
     int cur = 0;
@@ -967,7 +985,14 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         }
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
-        if (a.fuse) {  // the one-CTA steps ride in the last CTA of the kernel before them
+        if (a.walk && a.last_level) {  // the last level's children are leaves: no partition
+            if (a.fuse) {
+                launch_split_decide(a, max_m, s_);
+            } else {
+                launch_split(a, max_m, s_);
+                launch_decide(a, s_);
+            }
+        } else if (a.fuse) {  // the one-CTA steps ride in the last CTA of the kernel before them
             launch_split_decide(a, max_m, s_);
             launch_part_count(a, max_chunks, s_);
             launch_part_scatter(a, max_chunks, s_);
@@ -985,7 +1010,10 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     a.chunk_prefix = chunk_prefix_[cur].as<uint32_t>();
     a.rows_cur = rows_[cur].as<uint32_t>();
     const uint32_t last_m = (uint32_t)std::min<uint64_t>(1ull << maxd, max_level_nodes_);
-    launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
+    if (a.walk)
+        launch_tree_walk(a, (uint32_t)n_, s_);
+    else
+        launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
     FB_CUDA_CHECK(cudaGetLastError());
     FB_CUDA_CHECK(cudaEventRecord(ev1_, s_));
     TreeRec* hrec = h_tree_.as<TreeRec>();

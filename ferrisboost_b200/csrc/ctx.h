@@ -186,7 +186,7 @@ class TrainCtx {
     bool has_cat_ = false;
 
     // feature tables
-    DevMem d_hoff_, d_floc_, d_enabled_, d_mono_, d_cat_;
+    DevMem d_hoff_, d_floc_, d_floc_rec_, d_enabled_, d_mono_, d_cat_;
     std::vector<uint8_t> last_enabled_;
     std::vector<int8_t> last_mono_;
     bool tiles_valid_ = false;

@@ -1101,10 +1101,12 @@ __device__ __forceinline__ void part_count_work(const LevelArgs& a) {
 #pragma unroll
     for (int k = 0; k < kPartItems; k++) r[k] = i0 + k < cnt ? rows[i0 + k] : 0u;
     if (sd.child_slot < 0) {
-        const float leaf = a.trec[ni.tree_id].leaf;
+        if (!a.walk) {  // with k_tree_walk the leaf reaches these rows after the tree is finished
+            const float leaf = a.trec[ni.tree_id].leaf;
 #pragma unroll
-        for (int k = 0; k < kPartItems; k++)
-            if (i0 + k < cnt) a.pred[r[k]] = __fadd_rn(a.pred[r[k]], leaf);
+            for (int k = 0; k < kPartItems; k++)
+                if (i0 + k < cnt) a.pred[r[k]] = __fadd_rn(a.pred[r[k]], leaf);
+        }
         if (threadIdx.x == 0) a.chunk_left[c] = 0u;
         return;
     }
@@ -1325,6 +1327,146 @@ __global__ void __launch_bounds__(kPartThreads) k_leaf_final(LevelArgs a) {
     }
 }
 
+// One thread per row, rows in order so the margin update is coalesced: from
+// the root, each split reads the row's bin of its feature and goes the way
+// the partition would (missing -> default direction, categorical set ->
+// right, else bin < split bin -> left); the leaf's value is added to the
+// row's margin.  Trees of up to kWalkNodes nodes are first laid out in shared
+// memory, one 32-byte entry per node holding everything a step needs.  When
+// all features sit in one record block of at most kWalkStageBytes per row
+// (a.walk_rec), each CTA first copies its 256 rows' records into shared
+// memory with coalesced word loads (pitch + 4 bytes, so the 32 lanes' rows
+// fall in different banks) and the steps read bins from there; otherwise each
+// step reads its byte from the records in global memory.
+constexpr uint32_t kWalkNodes = 512;
+constexpr uint32_t kWalkThreads = 256;
+constexpr uint32_t kWalkStageBytes = 64;
+struct WalkNode {
+    const uint8_t* p;  // split: record base + the feature's byte offset
+    uint32_t stride;   // split: record stride
+    uint32_t lr;       // split: left | right << 16 (tree-local ids)
+    uint32_t bin_fl;   // split bin | node flags << 16 | bin width << 24
+    uint32_t val;      // split: missing sentinel; leaf: the leaf value's bits
+    uint32_t off;      // split: the feature's byte offset in the record
+    uint32_t pad;
+};
+static_assert(sizeof(WalkNode) == 32, "WalkNode layout");
+
+__global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_t n_rows) {
+    __shared__ WalkNode wn[kWalkNodes];
+    __shared__ uint32_t stage[kWalkThreads * (kWalkStageBytes / 4 + 1)];
+    const uint32_t nn = a.st->n_tree_nodes;
+    const bool table = nn <= kWalkNodes;
+    if (table) {
+        for (uint32_t i = threadIdx.x; i < nn; i += blockDim.x) {
+            const TreeRec t = a.trec[i];
+            WalkNode w{};
+            if (t.flags & 1u) {
+                w.bin_fl = 1u << 16;
+                w.val = __float_as_uint(t.leaf);
+            } else {
+                const FeatLoc fl = a.floc_rec[t.feat];
+                w.p = fl.base + fl.byte_off;
+                w.stride = fl.stride;
+                w.lr = (uint32_t)t.left | ((uint32_t)t.right << 16);
+                w.bin_fl = (t.bin & 0xffffu) | ((t.flags & 0xffu) << 16) | (fl.width << 24);
+                w.val = fl.missing;
+                w.off = fl.byte_off;
+            }
+            wn[i] = w;
+        }
+    }
+    const bool staged = table && a.walk_rec != nullptr;
+    const uint32_t words = a.walk_stride / 4, pitch = words + 1;
+    const uint8_t* srow = reinterpret_cast<const uint8_t*>(stage + threadIdx.x * pitch);
+    // staged: the next step's records are loaded into registers (word i of
+    // the step's contiguous block at i = threadIdx.x + k * blockDim.x) while
+    // the current step walks, then stored to shared memory
+    constexpr uint32_t kWalkWords = kWalkStageBytes / 4;
+    uint32_t nxt[kWalkWords];
+    const uint32_t step = blockDim.x * gridDim.x;
+    auto load_next = [&](uint32_t base) {
+        const uint32_t rows = base < n_rows ? min((uint32_t)blockDim.x, n_rows - base) : 0u;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.walk_rec + (size_t)base * a.walk_stride);
+#pragma unroll
+        for (uint32_t k = 0; k < kWalkWords; k++) {
+            const uint32_t i = threadIdx.x + k * blockDim.x;
+            nxt[k] = (k < words && i < rows * words) ? src[i] : 0u;
+        }
+    };
+    auto store_next = [&]() {
+#pragma unroll
+        for (uint32_t k = 0; k < kWalkWords; k++) {
+            const uint32_t i = threadIdx.x + k * blockDim.x;
+            if (k < words) {
+                const uint32_t rr = i / words, ww = i - rr * words;
+                stage[rr * pitch + ww] = nxt[k];
+            }
+        }
+    };
+    if (staged) load_next(blockIdx.x * blockDim.x);
+    __syncthreads();
+    for (uint32_t base = blockIdx.x * blockDim.x; base < n_rows; base += step) {
+        const uint32_t r = base + threadIdx.x;
+        if (staged) {
+            store_next();
+            __syncthreads();
+            load_next(base + step);
+        }
+        const float pv = r < n_rows ? a.pred[r] : 0.0f;  // in flight during the walk
+        if (r < n_rows) {
+            uint32_t node = 0;
+            for (uint32_t depth = 0; depth < 64; depth++) {  // trees are at most 15 levels deep
+                uint32_t flags, sbin, missing, width, left_id, right_id, bin;
+                float leaf = 0.0f;
+                if (table) {
+                    const WalkNode w = wn[node];
+                    flags = (w.bin_fl >> 16) & 0xffu;
+                    if (flags & 1u) leaf = __uint_as_float(w.val);
+                    sbin = w.bin_fl & 0xffffu;
+                    width = w.bin_fl >> 24;
+                    missing = w.val;
+                    left_id = w.lr & 0xffffu;
+                    right_id = w.lr >> 16;
+                    if (!(flags & 1u)) {
+                        if (staged)
+                            bin = width == 2 ? (uint32_t)srow[w.off] | ((uint32_t)srow[w.off + 1] << 8)
+                                             : (uint32_t)srow[w.off];
+                        else {
+                            const uint8_t* p = w.p + (size_t)r * w.stride;
+                            bin = width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+                        }
+                    }
+                } else {
+                    const TreeRec t = a.trec[node];
+                    flags = t.flags;
+                    leaf = t.leaf;
+                    sbin = t.bin;
+                    left_id = (uint32_t)t.left;
+                    right_id = (uint32_t)t.right;
+                    if (!(flags & 1u)) {
+                        const FeatLoc fl = a.floc_rec[t.feat];
+                        width = fl.width;
+                        missing = fl.missing;
+                        const uint8_t* p = fl.base + (size_t)r * fl.stride + fl.byte_off;
+                        bin = width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+                    }
+                }
+                if (flags & 1u) {
+                    a.pred[r] = __fadd_rn(pv, leaf);
+                    break;
+                }
+                bool left;
+                if (bin == missing) left = (flags & 2u) != 0;
+                else if (flags & 4u) left = bin >= 256u || ((a.tcats[(size_t)node * 8 + (bin >> 5)] >> (bin & 31)) & 1u) == 0u;
+                else left = bin < sbin;
+                node = left ? left_id : right_id;
+            }
+        }
+        if (staged) __syncthreads();
+    }
+}
+
 // Root of a new tree (training/mod.rs:3466-3469, 3499-3501).
 __global__ void k_tree_init(LevelArgs a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum) {
     if (threadIdx.x != 0) return;
@@ -1537,6 +1679,13 @@ void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s
     k_part_scatter<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
 void launch_next_level(const LevelArgs& a, cudaStream_t s) { count_launch(); k_next_level<<<1, 1024, 0, s>>>(a); }
+void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s) {
+    if (n_rows == 0) return;
+    count_launch();
+    // one resident wave (shared memory allows 6 CTAs per SM)
+    const uint32_t blocks = std::min<uint32_t>((n_rows + kWalkThreads - 1) / kWalkThreads, 148u * 6u);
+    k_tree_walk<<<blocks, kWalkThreads, 0, s>>>(a, n_rows);
+}
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
     count_launch();
     k_leaf_final<<<max_chunks, kPartThreads, 0, s>>>(a);

@@ -79,6 +79,10 @@ struct LevelArgs {
     const uint8_t* is_cat;       // per feature categorical flag (may be null)
     uint32_t max_onehot, max_cat_threshold;
     const FeatLoc* floc;
+    const FeatLoc* floc_rec;     // the same features in the row records (k_tree_walk)
+    uint32_t walk;               // depthwise: leaf values reach the margins by k_tree_walk, not per partition
+    const uint8_t* walk_rec;     // k_tree_walk: the one record block holding every feature (stride <= 64), or null
+    uint32_t walk_stride;
     // level buffers
     TreeState* st;
     NodeInfo* nodes;             // current level
@@ -202,6 +206,10 @@ void launch_part_scan(const LevelArgs& a, cudaStream_t s);
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_next_level(const LevelArgs& a, cudaStream_t s);
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
+// Every local row walks the finished tree (a.trec / a.tcats) on its record's
+// bins and adds its leaf's value to its margin (training/mod.rs:5020-5063,
+// one addition per row per tree as in the partition path).
+void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s);
 void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
                       cudaStream_t s);
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s);
