@@ -42,10 +42,10 @@ sys.path.insert(0, ROOT)
 N_FEATURES = 28
 PARAMS = {"objective": "binary:logistic", "max_depth": 8, "eta": 0.1, "lambda": 1.0, "max_bin": 256}
 E2E_ROUNDS = 100
-# DRAM bytes / algorithmic bytes of k_hist_lpf over one tree, from an ncu capture
-# (profiles/k_hist_lpf_c1_4Mrows_traffic.md); roofline.traffic = this x the
-# algorithmic bytes per launch measured live
-HIST_TRAFFIC_RATIO = 2225.7 / 8 / 133.8
+# DRAM bytes / algorithmic bytes of k_hist_stage over one tree, from an ncu
+# capture (profiles/k_hist_stage_c1_4Mrows_traffic.md); roofline.traffic =
+# this x the algorithmic bytes per launch measured live
+HIST_TRAFFIC_RATIO = 1800.9 / 8 / 84.44
 
 
 def make_data(n, seed=0):

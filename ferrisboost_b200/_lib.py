@@ -81,6 +81,10 @@ SIGNATURES = {
     "fbgpu_upload_gpair": (C.c_int, [P, i64p, f64p, i64p]),
     "fbgpu_round_from_exp": (C.c_int, [P, C.c_int32, f32p, C.c_uint64, C.c_uint64, C.c_uint64, f64p]),
     "fbgpu_round_device": (C.c_int, [P, C.c_int32, C.c_int32, C.c_uint64, C.c_uint64, C.c_uint64, f64p, i64p]),
+    "fbgpu_set_outputs": (C.c_int, [P, C.c_uint32, f32p]),
+    "fbgpu_multiclass_gradients": (C.c_int, [P, C.c_int32]),
+    "fbgpu_quantize_class": (C.c_int, [P, C.c_uint32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_int32, f64p, i64p]),
+    "fbgpu_set_output_column": (C.c_int, [P, C.c_uint32]),
     "fbgpu_build_tree": (C.c_int, [P, C.POINTER(FbgpuTreeParams), u8p, C.POINTER(FbgpuTreeOut)]),
     "fbgpu_download_margins": (C.c_int, [P, f32p]),
     "fbgpu_nccl_unique_id": (C.c_int, [u8p]),

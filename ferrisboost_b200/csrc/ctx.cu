@@ -529,7 +529,8 @@ void TrainCtx::softmax_gradients(int fast) {
     launch_softmax_gradients(a, K_, gp_multi_.as<float>(), fast, s_);
 }
 
-void TrainCtx::quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast) {
+void TrainCtx::quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast, double* scales_out,
+                              int64_t* sum_out) {
     FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 32, s_));
     GradArgs a = grad_args();
     a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
@@ -553,7 +554,15 @@ void TrainCtx::quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t t
         FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
     }
     launch_quantize(a, s_);
-    reduce_root_sum(false);
+    reduce_root_sum(sum_out != nullptr);
+    if (scales_out || sum_out) {
+        unsigned long long* hs = h_small_.as<unsigned long long>() + 4;
+        FB_CUDA_CHECK(cudaMemcpyAsync(hs, dscales, 16, cudaMemcpyDeviceToHost, s_));
+        FB_CUDA_CHECK(cudaMemcpyAsync(hs + 2, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
+        sync();
+        if (scales_out) std::memcpy(scales_out, hs, 16);
+        if (sum_out) std::memcpy(sum_out, hs + 2, 16);
+    }
 }
 
 void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide) {
@@ -1504,6 +1513,25 @@ fbgpu_status fbgpu_round_device(fbgpu_ctx* ctx, int32_t objective, int32_t fast,
                                 uint64_t seed, uint64_t tree, double* scales_out, int64_t* root_sum_out) {
     return guard(ctx, [&] {
         ctx->impl.round_device(objective, fast, sub_threshold, seed, tree, scales_out, root_sum_out);
+    });
+}
+fbgpu_status fbgpu_set_outputs(fbgpu_ctx* ctx, uint32_t n_classes, const float* class_margins) {
+    return guard(ctx, [&] { ctx->impl.set_outputs(n_classes, class_margins); });
+}
+fbgpu_status fbgpu_multiclass_gradients(fbgpu_ctx* ctx, int32_t fast) {
+    return guard(ctx, [&] { ctx->impl.softmax_gradients(fast); });
+}
+fbgpu_status fbgpu_quantize_class(fbgpu_ctx* ctx, uint32_t cls, uint64_t sub_threshold, uint64_t seed, uint64_t tree,
+                                  int32_t fast, double* scales_out, int64_t* root_sum_out) {
+    return guard(ctx, [&] {
+        if (cls >= ctx->impl.outputs()) throw fbg::InputError("class index out of range");
+        ctx->impl.quantize_class(cls, sub_threshold, seed, tree, fast, scales_out, root_sum_out);
+    });
+}
+fbgpu_status fbgpu_set_output_column(fbgpu_ctx* ctx, uint32_t cls) {
+    return guard(ctx, [&] {
+        if (cls >= ctx->impl.outputs()) throw fbg::InputError("class index out of range");
+        ctx->impl.set_pred_column(cls);
     });
 }
 fbgpu_status fbgpu_build_tree(fbgpu_ctx* ctx, const fbgpu_tree_params* tp, const uint8_t* enabled,

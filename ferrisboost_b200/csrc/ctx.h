@@ -109,7 +109,8 @@ class TrainCtx {
     void softmax_gradients(int fast);
     // Class k's column: sampling mask keyed by `tree`, bounds, scales (host
     // libm, or the device in fast mode), fixed point and root sum.
-    void quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast);
+    void quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast, double* scales_out = nullptr,
+                        int64_t* sum_out = nullptr);
     // The margin column the next build_tree adds its leaf values to.
     void set_pred_column(uint32_t k) { pred_col_ = k; }
 

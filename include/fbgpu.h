@@ -213,6 +213,27 @@ fbgpu_status fbgpu_round_from_exp(fbgpu_ctx* ctx, int32_t objective, const float
 fbgpu_status fbgpu_round_device(fbgpu_ctx* ctx, int32_t objective, int32_t fast, uint64_t sub_threshold,
                                 uint64_t seed, uint64_t tree, double* scales_out, int64_t* root_sum_out);
 
+/* Multiclass (multi:softprob / multi:softmax, src/training/mod.rs:2564-2800).
+ * fbgpu_set_outputs makes the margins K columns (class-major), column k
+ * starting at class_margins[k]; replaces init_fast_math with K margins
+ * (src/backend/mod.rs:161-168).  fbgpu_multiclass_gradients computes the
+ * softmax gradients of all K classes from the current margins
+ * (objective.rs:1175-1219; fast = 0: the host expf reproduced on the device,
+ * fbgpu_exact_exp_available must be 1); replaces fast_multiclass_begin_round
+ * (mod.rs:192-194).  fbgpu_quantize_class masks, bounds and quantizes class
+ * k's column for the tree with index `tree` (round * K + k) and leaves the
+ * fixed gradients, root sum and scales on the device (scales by the host
+ * libm, or on the device when fast; scales_out / root_sum_out may be NULL);
+ * replaces fast_multiclass_gradient_and_quantize (mod.rs:195-203).
+ * fbgpu_set_output_column selects the column the next fbgpu_build_tree adds
+ * its leaf values to; with it, fast_multiclass_apply_delta (mod.rs:204-206)
+ * has no separate step.  fbgpu_download_margins then returns K x n. */
+fbgpu_status fbgpu_set_outputs(fbgpu_ctx* ctx, uint32_t n_classes, const float* class_margins);
+fbgpu_status fbgpu_multiclass_gradients(fbgpu_ctx* ctx, int32_t fast);
+fbgpu_status fbgpu_quantize_class(fbgpu_ctx* ctx, uint32_t cls, uint64_t sub_threshold, uint64_t seed, uint64_t tree,
+                                  int32_t fast, double* scales_out, int64_t* root_sum_out);
+fbgpu_status fbgpu_set_output_column(fbgpu_ctx* ctx, uint32_t cls);
+
 /* Grow one tree on the device and add its leaf values to the resident
  * margins.  `enabled` marks the features of this tree (colsample_bytree,
  * colsample.rs:74-95), NULL = all.  Replaces the per-level loop of

@@ -150,3 +150,50 @@ def test_categorical_partition_sends_the_set_right():
     inset = np.isin(v, [1, 5, 33, 63])
     left = np.where(v == 255, True, ~inset)
     assert nl == left.sum() and np.array_equal(out, np.concatenate([rows[left], rows[~left]]))
+
+
+def test_multiclass_gradients_and_quantize_match_oracle(oracle):
+    # tests/gpu_histogram.rs:2666-2720: class-major K base margins, softmax
+    # gradients of all classes, then per class the sampled bounds, scales and
+    # root sum (the tree index keys the row sampling)
+    import ctypes as C
+    from gpu_util import check, lib
+    from ferrisboost_b200 import _lib
+    from test_multiclass_oracle import fixture
+    K, n = 5, 3000
+    _, y, w = fixture(n, 4, K)
+    rng = np.random.default_rng(4)
+    bins, widths = random_bins(rng, n, [8, 8])
+    margins = np.array([0.3 * c - 0.7 for c in range(K)], np.float32)
+    ctx = Ctx(bins, [8, 8], widths)
+    yy = np.ascontiguousarray(y, np.float32)
+    ww = np.ascontiguousarray(w, np.float32)
+    check(lib().fbgpu_set_labels(ctx.h, _lib.ptr(yy, C.c_float), _lib.ptr(ww, C.c_float), None, 0.0), ctx.h)
+    check(lib().fbgpu_set_outputs(ctx.h, K, _lib.ptr(margins, C.c_float)), ctx.h)
+    check(lib().fbgpu_multiclass_gradients(ctx.h, 0), ctx.h)
+    grads = oracle.softmax_gradients(np.repeat(margins[:, None], n, axis=1), y, w)
+    for rate, cls, tree in ((1.0, 0, 0), (1.0, 3, 3), (0.6, 2, 7)):
+        th = (1 << 64) - 1 if rate >= 1.0 else int(rate * (1 << 53))
+        sc = np.zeros(2, np.float64)
+        sm = np.zeros(2, np.int64)
+        check(lib().fbgpu_quantize_class(ctx.h, cls, th, 6, tree, 0, _lib.ptr(sc, C.c_double),
+                                         _lib.ptr(sm, C.c_int64)), ctx.h)
+        g = grads[cls].copy()
+        if rate < 1.0:  # data/subsample.rs:45-78 row hash keyed by the tree index
+            def mix(z):
+                z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9 & (2**64 - 1)
+                z = (z ^ (z >> 27)) * 0x94D049BB133111EB & (2**64 - 1)
+                return z ^ (z >> 31)
+            rot = lambda x, r: ((x << r) | (x >> (64 - r))) & (2**64 - 1)
+            for i in range(n):
+                hsh = mix(6 ^ rot(tree * 0x9E3779B97F4A7C15 & (2**64 - 1), 23) ^ (i * 0xD6E8FEB86659FD93 & (2**64 - 1)))
+                if (hsh >> 11) >= th:
+                    g[i] = 0.0
+        want_sc = oracle.quantizer(g.reshape(-1, 2), n)
+        _, want_sum = oracle.to_fixed(g.reshape(-1, 2), want_sc)
+        assert np.array_equal(sc, want_sc), (cls, sc, want_sc)
+        assert np.array_equal(sm, want_sum), (cls, sm, want_sum)
+    out = np.zeros((K, n), np.float32)
+    check(lib().fbgpu_download_margins(ctx.h, _lib.ptr(out, C.c_float)), ctx.h)
+    assert np.array_equal(out, np.repeat(margins[:, None], n, axis=1))
+    assert lib().fbgpu_set_output_column(ctx.h, K) != 0

@@ -302,3 +302,28 @@ def test_lossguide_fast_mode_within_tolerance(oracle):
         return -np.mean(y * np.log(pr) + (1 - y) * np.log(1 - pr))
 
     assert abs(logloss(a) - logloss(b)) < 1e-4
+
+
+def test_partition_leaf_path_byte_identical(oracle, tmp_path):
+    # the leaf values reach the margins through the partition chunks and the
+    # final-level pass (the path above 4M local rows) instead of the tree walk
+    import os
+    import subprocess
+    import sys
+    X, y = _synthetic(30000, 12, seed=77, missing=0.03)
+    np.save(tmp_path / "X.npy", X)
+    np.save(tmp_path / "y.npy", y)
+    p = dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=256)
+    code = (
+        "import sys, numpy as np, ferrisboost_b200 as fb\n"
+        f"X = np.load({str(tmp_path / 'X.npy')!r}); y = np.load({str(tmp_path / 'y.npy')!r})\n"
+        f"m = fb.train({p!r}, X, label=y, num_boost_round=6)\n"
+        f"open({str(tmp_path / 'm.json')!r}, 'wb').write(m.to_json())\n"
+        f"np.save({str(tmp_path / 'margin.npy')!r}, m.predict(X, output_margin=True))\n")
+    env = dict(os.environ, FBGPU_WALK="0")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=root)
+    ref = oracle.train(X, y, n_rounds=6, **p)
+    assert (tmp_path / "m.json").read_bytes() == ref.json()
+    walked = fb.train(p, X, label=y, num_boost_round=6)
+    assert walked.to_json() == ref.json()
