@@ -274,27 +274,44 @@ __global__ void k_gradient_quantize_exp(GradArgs a) {
 // reference's f32 order: wmax from the smallest positive normal f32, the
 // exps of (m_k - wmax) summed in f64, p = e / (f32)sum,
 // h = max(((2 p)(1 - p)) w, 1e-16), the label's class takes p - 1, g = p w.
-template <bool FAST>
+// KR > 0: K <= KR and each class's exp is kept in registers between the
+// sum and the division; KR = 0: any K, the exp evaluated again (same value).
+template <bool FAST, int KR>
 __global__ void k_softmax_grad(GradArgs a, uint32_t K, float* __restrict__ out) {
     const size_t n = a.n;
+    auto ex = [&](float x) { return FAST ? expf(x) : host_expf(x, a.exptab, a.exp_probes); };
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
         float wmax = FLT_MIN;
         for (uint32_t k = 0; k < K; k++) wmax = fmaxf(a.pred[k * n + i], wmax);
         double wsum = 0.0;
-        for (uint32_t k = 0; k < K; k++) {
-            const float x = __fsub_rn(a.pred[k * n + i], wmax);
-            wsum = __dadd_rn(wsum, (double)(FAST ? expf(x) : host_expf(x, a.exptab, a.exp_probes)));
+        float e[KR > 0 ? KR : 1];
+        if (KR > 0) {
+#pragma unroll
+            for (int k = 0; k < KR; k++) {
+                if ((uint32_t)k < K) {
+                    e[k] = ex(__fsub_rn(a.pred[k * n + i], wmax));
+                    wsum = __dadd_rn(wsum, (double)e[k]);
+                }
+            }
+        } else {
+            for (uint32_t k = 0; k < K; k++) wsum = __dadd_rn(wsum, (double)ex(__fsub_rn(a.pred[k * n + i], wmax)));
         }
         const float d = __double2float_rn(wsum);
         const float label = a.label[i];
         const float wt = a.weight ? a.weight[i] : 1.0f;
-        for (uint32_t k = 0; k < K; k++) {
-            const float x = __fsub_rn(a.pred[k * n + i], wmax);
-            float p = __fdiv_rn(FAST ? expf(x) : host_expf(x, a.exptab, a.exp_probes), d);
+        auto emit = [&](uint32_t k, float ek) {
+            float p = __fdiv_rn(ek, d);
             const float h = fmaxf(__fmul_rn(__fmul_rn(__fmul_rn(2.0f, p), __fsub_rn(1.0f, p)), wt), 1e-16f);
             if (label == (float)k) p = __fsub_rn(p, 1.0f);
             out[2 * (k * n + i)] = __fmul_rn(p, wt);
             out[2 * (k * n + i) + 1] = h;
+        };
+        if (KR > 0) {
+#pragma unroll
+            for (int k = 0; k < KR; k++)
+                if ((uint32_t)k < K) emit((uint32_t)k, e[k]);
+        } else {
+            for (uint32_t k = 0; k < K; k++) emit(k, ex(__fsub_rn(a.pred[k * n + i], wmax)));
         }
     }
 }
@@ -1567,10 +1584,17 @@ void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s) {
 void launch_quantize(const GradArgs& a, cudaStream_t s) { count_launch(); k_quantize<<<grad_grid(a.n), 256, 0, s>>>(a); }
 void launch_softmax_gradients(const GradArgs& a, uint32_t K, float* out, int fast, cudaStream_t s) {
     count_launch();
-    if (fast)
-        k_softmax_grad<true><<<grad_grid(a.n), 256, 0, s>>>(a, K, out);
-    else
-        k_softmax_grad<false><<<grad_grid(a.n), 256, 0, s>>>(a, K, out);
+    if (K <= 16) {
+        if (fast)
+            k_softmax_grad<true, 16><<<grad_grid(a.n), 256, 0, s>>>(a, K, out);
+        else
+            k_softmax_grad<false, 16><<<grad_grid(a.n), 256, 0, s>>>(a, K, out);
+    } else {
+        if (fast)
+            k_softmax_grad<true, 0><<<grad_grid(a.n), 256, 0, s>>>(a, K, out);
+        else
+            k_softmax_grad<false, 0><<<grad_grid(a.n), 256, 0, s>>>(a, K, out);
+    }
 }
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
                           cudaStream_t s) {
