@@ -278,6 +278,7 @@ class ExplainModel {
     void explain_host(int kind, const float* X, uint64_t n, float* out);
     uint64_t explain_width(int kind) const;
     uint32_t n_features() const { return F_; }
+    cudaStream_t stream() const { return s_; }
 
    private:
     int device_;

@@ -675,17 +675,25 @@ fbg::ExplainModel& device_model(Model& m, int device) {
 }
 
 // Per-class outputs of a multiclass model (tree.rs:468-480 predict_margins_upto,
-// explain.rs:704-727 one group per class): class k's device model writes
-// `width` values per row into a scratch block, interleaved into out[row][k][..].
+// explain.rs:704-727 one group per class): the rows go to the device once;
+// class k's device model writes `width` values per row into a device block,
+// copied with a pitch into out[row][k][..].
 template <class Fn>
-void per_class(Model& m, int device, uint64_t n, size_t width, float* out, Fn&& run) {
+void per_class(Model& m, int device, const float* X, uint64_t n, size_t width, float* out, Fn&& run) {
     ensure_device(m, device);
     const size_t K = m.class_margins.size();
-    std::vector<float> tmp(n * width);
+    if (n == 0) return;
+    FB_CUDA_CHECK(cudaSetDevice(device));
+    fbg::DevMem xd, od;
+    xd.alloc(n * m.n_features * sizeof(float));
+    od.alloc(n * width * sizeof(float));
+    FB_CUDA_CHECK(cudaMemcpy(xd.p, X, n * m.n_features * sizeof(float), cudaMemcpyHostToDevice));
     for (size_t k = 0; k < K; k++) {
-        run(m.dev_class[k]->impl, tmp.data());
-        for (uint64_t r = 0; r < n; r++)
-            std::memcpy(out + (r * K + k) * width, tmp.data() + r * width, width * sizeof(float));
+        fbg::ExplainModel& e = m.dev_class[k]->impl;
+        run(e, xd.as<float>(), od.as<float>(), e.stream());
+        FB_CUDA_CHECK(cudaMemcpy2DAsync(out + k * width, K * width * sizeof(float), od.p, width * sizeof(float),
+                                        width * sizeof(float), n, cudaMemcpyDeviceToHost, e.stream()));
+        FB_CUDA_CHECK(cudaStreamSynchronize(e.stream()));
     }
 }
 
@@ -1379,7 +1387,8 @@ int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* rig
 int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {
     return fbe::guarded([&]() -> int32_t {
         if (m->outputs() > 1)
-            fbe::per_class(*m, device, n, 1, out, [&](fbg::ExplainModel& e, float* o) { e.predict_host(X, n, o); });
+            fbe::per_class(*m, device, X, n, 1, out, [&](fbg::ExplainModel& e, const float* xd, float* od,
+                                                        cudaStream_t s) { e.predict_device(xd, n, od, s); });
         else
             fbe::device_model(*m, device).predict_host(X, n, out);
         return 0;
@@ -1425,8 +1434,10 @@ fbgpu_model* fb_model_device(fb_model* m, int32_t device) {
 int32_t fb_model_shap(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {
     return fbe::guarded([&]() -> int32_t {
         if (m->outputs() > 1)
-            fbe::per_class(*m, device, n, (size_t)m->n_features + 1, out,
-                           [&](fbg::ExplainModel& e, float* o) { e.shap_host(X, n, o); });
+            fbe::per_class(*m, device, X, n, (size_t)m->n_features + 1, out,
+                           [&](fbg::ExplainModel& e, const float* xd, float* od, cudaStream_t s) {
+                               e.shap_device(xd, n, od, s);
+                           });
         else
             fbe::device_model(*m, device).shap_host(X, n, out);
         return 0;
@@ -1437,8 +1448,10 @@ int32_t fb_model_explain(fb_model* m, int32_t kind, const float* X, uint64_t n, 
     return fbe::guarded([&]() -> int32_t {
         if (m->outputs() > 1 && (kind == 1 || kind == 2)) {  // per class: n x K x (F+1) [x (F+1)]
             const size_t nc = (size_t)m->n_features + 1;
-            fbe::per_class(*m, device, n, kind == 1 ? nc : nc * nc, out,
-                           [&](fbg::ExplainModel& e, float* o) { e.explain_host(kind, X, n, o); });
+            fbe::per_class(*m, device, X, n, kind == 1 ? nc : nc * nc, out,
+                           [&](fbg::ExplainModel& e, const float* xd, float* od, cudaStream_t s) {
+                               e.explain_device(kind, xd, n, od, s);
+                           });
         } else {
             fbe::device_model(*m, device).explain_host(kind, X, n, out);  // leaf indices: all trees in order
         }
