@@ -218,6 +218,7 @@ class Shard(NamedTuple):
     base_score: float     # label mean over all rows (fb_label_mean) or the given base_score
     timeout_ms: int = 120000
     comm: Any = None      # a distributed.Communicator started ahead (its initialization overlaps data preparation)
+    class_margins: Any = None  # multiclass: the K base margins over all rows (fb_class_margins)
 
 
 class Dataset:
@@ -334,12 +335,20 @@ class Booster:
                                               C.byref(fp))
         elif shard.comm is not None:
             fp.base_score = shard.base_score
+            if shard.class_margins is not None:
+                cm = np.ascontiguousarray(shard.class_margins, dtype=np.float32)
+                self._keep = self._keep + (cm,)
+                fp.class_margins = _lib.ptr(cm, C.c_float)
             self._keep = self._keep + (shard.comm,)
             self._h = lib().fb_booster_create_sharded_comm(
                 dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), C.byref(fp), shard.row_offset,
                 shard.n_rows_global, shard.comm.handle, shard.nranks, shard.rank)
         else:
             fp.base_score = shard.base_score
+            if shard.class_margins is not None:
+                cm = np.ascontiguousarray(shard.class_margins, dtype=np.float32)
+                self._keep = self._keep + (cm,)
+                fp.class_margins = _lib.ptr(cm, C.c_float)
             nid = np.frombuffer(shard.nccl_id, dtype=np.uint8).copy()
             self._h = lib().fb_booster_create_sharded(
                 dataset._h, _lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), C.byref(fp), shard.row_offset,

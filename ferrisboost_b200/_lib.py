@@ -31,6 +31,7 @@ class FbParams(C.Structure):
         ("colsample_bytree", C.c_float), ("base_score", C.c_float), ("seed", C.c_uint64),
         ("max_cat_to_onehot", C.c_uint32), ("max_cat_threshold", C.c_uint32), ("nthread", C.c_int32),
         ("gpu_math", C.c_int32), ("device", C.c_int32), ("monotone", i8p), ("num_class", C.c_uint32),
+        ("class_margins", f32p),
     ]
 
 
@@ -121,6 +122,7 @@ SIGNATURES = {
     "fb_sketch_features_device": (C.c_int64, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, u32p, C.c_uint32,
                                               C.c_int32, f32p, u32p, C.c_uint64]),
     "fb_label_mean": (C.c_float, [f32p, f32p, C.c_uint64]),
+    "fb_class_margins": (C.c_int32, [f32p, f32p, C.c_uint64, C.c_uint32, f32p]),
     "fb_dataset_free": (None, [P]),
     "fb_dataset_rows": (C.c_uint64, [P]),
     "fb_dataset_cuts": (C.c_int64, [P, f32p, u32p, C.c_uint64]),

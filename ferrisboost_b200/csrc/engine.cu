@@ -803,8 +803,10 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
                         const ShardInfo& sh = ShardInfo{}) {
     const fb_params& p = *pp;
     if (sh.nranks > 1) {
-        if (std::isnan(p.base_score))
-            throw InputError("a row-sharded booster needs base_score (the label mean over all rows)");
+        if (std::isnan(p.base_score) && !(p.objective >= 2 && p.class_margins))
+            throw InputError(p.objective >= 2
+                                 ? "a row-sharded multiclass booster needs class_margins (over all rows) or base_score"
+                                 : "a row-sharded booster needs base_score (the label mean over all rows)");
         if (!sh.nccl_id && !sh.comm) throw InputError("a row-sharded booster needs an NCCL unique id or communicator");
         if (sh.row_offset + d->n > sh.n_global) throw InputError("row_offset + rows exceeds n_rows_global");
     }
@@ -812,7 +814,6 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
         throw InputError("objective must be reg:squarederror, binary:logistic, multi:softprob or multi:softmax");
     const bool multi = p.objective >= 2;
     if (multi && p.num_class < 2) throw InputError("multi:softprob / multi:softmax need num_class >= 2");
-    if (multi && sh.nranks > 1) throw InputError("multiclass training runs on one GPU in this version");
     if (p.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     if (!(p.subsample > 0.0f && p.subsample <= 1.0f)) throw InputError("subsample must be in (0, 1]");
     if (!(p.colsample_bytree > 0.0f && p.colsample_bytree <= 1.0f)) throw InputError("colsample_bytree must be in (0, 1]");
@@ -850,8 +851,11 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     // objective.rs:41-61 label mean (FitInterceptGlmLike) when base_score is not given
     float base = p.base_score;
     if (multi) {  // mod.rs:1430-1450: per-class margins, the given base_score K times
-        b->model.class_margins = std::isnan(base) ? initial_class_margins(y, w, d->n, p.num_class)
-                                                  : std::vector<float>(p.num_class, base);
+        if (p.class_margins)
+            b->model.class_margins.assign(p.class_margins, p.class_margins + p.num_class);
+        else
+            b->model.class_margins = std::isnan(base) ? initial_class_margins(y, w, d->n, p.num_class)
+                                                      : std::vector<float>(p.num_class, base);
         base = b->model.class_margins[0];
     }
     if (std::isnan(base)) base = label_mean(y, w, d->n);
@@ -1203,6 +1207,18 @@ int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_
 
 float fb_label_mean(const float* labels, const float* weights, uint64_t n) {
     return fbe::label_mean(labels, weights, n);
+}
+
+int32_t fb_class_margins(const float* labels, const float* weights, uint64_t n, uint32_t K, float* out) {
+    return fbe::guarded([&]() -> int32_t {
+        if (K < 2) throw fbe::InputError("num_class must be >= 2");
+        for (uint64_t i = 0; i < n; i++)
+            if (!(labels[i] >= 0.0f && labels[i] < (float)K && labels[i] == std::trunc(labels[i])))
+                throw fbe::InputError("multiclass labels must be integers in [0, num_class=" + std::to_string(K) + ")");
+        const std::vector<float> v = fbe::initial_class_margins(labels, weights, n, K);
+        std::memcpy(out, v.data(), 4ull * K);
+        return 0;
+    }, 1);
 }
 
 void fb_dataset_free(fb_dataset* d) { delete d; }

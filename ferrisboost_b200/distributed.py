@@ -246,12 +246,21 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group, device=p["device_index"])
     lo, hi = shard_range(n, world, rank)
     base = p["base_score"]
-    if base is None:
+    class_margins = None
+    if p["objective"].startswith("multi:"):
+        # every rank holds all labels: the class base margins over all rows
+        if base is None:
+            class_margins = np.zeros(p["num_class"], np.float32)
+            if lib().fb_class_margins(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), n, p["num_class"],
+                                      _lib.ptr(class_margins, C.c_float)):
+                raise ValueError((lib().fb_last_error() or b"").decode())
+            base = float("nan")
+    elif base is None:
         base = float(lib().fb_label_mean(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), n))
     ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts,
                  device=p["device_index"])
     shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
-                  timeout_ms=timeout_ms, comm=comm)
+                  timeout_ms=timeout_ms, comm=comm, class_margins=class_margins)
     b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)
     if liveness is None:
         b.update(num_boost_round)

@@ -49,6 +49,9 @@ typedef struct fb_params {
     int32_t device;
     const int8_t* monotone;     /* n_features or NULL */
     uint32_t num_class;         /* multi:softprob / multi:softmax: classes, >= 2 (K trees per round) */
+    const float* class_margins; /* multiclass: the K base margins over all rows, or NULL (estimated from the
+                                   booster's labels, or base_score K times); a row-sharded multiclass
+                                   booster needs them or base_score (fb_class_margins on all labels) */
 } fb_params;
 
 void fb_default_params(fb_params* p);
@@ -105,6 +108,10 @@ int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32
  * (weighted when weights != NULL), summed in f64 in row order
  * (src/objective.rs:41-61). */
 float fb_label_mean(const float* labels, const float* weights, uint64_t n);
+/* The multiclass base margins (objective.rs:1225-1247 initial_class_margins):
+ * weighted class counts summed in f32 in row order, log(count / sum_w + 1e-6),
+ * minus their mean; K values to out.  Labels must be integers in [0, K). */
+int32_t fb_class_margins(const float* labels, const float* weights, uint64_t n, uint32_t K, float* out);
 void fb_dataset_free(fb_dataset* d);
 uint64_t fb_dataset_rows(const fb_dataset* d);
 /* Cuts: copies up to cap values; returns the total.  offsets: F+1 entries. */

@@ -1,7 +1,8 @@
 """Row-sharded training on 2 GPUs (one process per GPU, NCCL collectives on
 the training stream): every rank's model equals the single-GPU model byte for
-byte, in exact and in fast mode, with row and column sampling and a
-categorical feature.  Needs at least 2 GPUs; skipped otherwise."""
+byte, in exact and in fast mode, with row and column sampling, a
+categorical feature and a multiclass objective.  Needs at least 2 GPUs;
+skipped otherwise."""
 import os
 import socket
 
@@ -15,6 +16,8 @@ CASES = {
     "sampled_categorical": {"objective": "binary:logistic", "max_depth": 5, "eta": 0.2, "max_bin": 300,
                             "subsample": 0.8, "colsample_bytree": 0.7, "seed": 7},
     "sqerr_fast": {"objective": "reg:squarederror", "max_depth": 7, "eta": 0.1, "gpu_math": "fast"},
+    "multiclass": {"objective": "multi:softprob", "num_class": 4, "max_depth": 5, "eta": 0.3, "max_bin": 128,
+                   "subsample": 0.9, "seed": 3},
 }
 
 
@@ -31,6 +34,8 @@ def _data(case):
     z = X[:, 0] + 0.5 * np.nan_to_num(X[:, 1]) * np.nan_to_num(X[:, 2])
     if CASES[case]["objective"] == "binary:logistic":
         y = (rng.random(n) < 1 / (1 + np.exp(-np.nan_to_num(z)))).astype(np.float32)
+    elif CASES[case]["objective"].startswith("multi:"):
+        y = np.digitize(np.nan_to_num(z), [-1.0, 0.0, 1.0]).astype(np.float32)
     else:
         y = np.nan_to_num(z).astype(np.float32)
     return X, y, ft
