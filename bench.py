@@ -22,7 +22,7 @@ over ranks.  cpu_baseline / --impl reference: the C++ restatement of the
 reference CPU engine (oracle/), all host threads, a bounded sample of the same
 workload.
 
---config selects the other BASELINE configs (configs[0], [2], [3] and the
+--config selects the other benchmark configs (configs[0], [2], [3] and the
 max_depth 14 variant of [3], and [4]: TreeSHAP rows/s); they print the same
 JSON line for their own workload.
 """
@@ -87,7 +87,7 @@ def make_mixed(n, seed=0):
 
 
 def make_multiclass(n, seed=0, K=5):
-    """Multiclass workload (no BASELINE config names one): configs[1]'s 28
+    """Multiclass workload (none of the benchmark configs is multiclass): configs[1]'s 28
     N(0,1) features; the label is the argmax of K random linear scores plus
     Gumbel noise (a softmax model's draw)."""
     rng = np.random.default_rng(seed)

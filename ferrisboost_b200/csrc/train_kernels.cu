@@ -99,6 +99,26 @@ __device__ __forceinline__ uint32_t find_segment(const T* prefix, uint32_t n, T 
     return lo;
 }
 
+// find_segment by a whole warp: each round the 32 lanes probe 32 evenly
+// spaced entries at once and a ballot keeps the last one <= x, so a table of
+// up to 1024 entries takes two dependent loads instead of log2(n).  Every lane
+// of the warp calls it and gets the same answer.
+template <class T>
+__device__ __forceinline__ uint32_t find_segment_warp(const T* prefix, uint32_t n, T x) {
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t lo = 0, hi = n;  // invariant: prefix[lo] <= x, answer in [lo, hi)
+    while (hi - lo > 1) {
+        const uint32_t step = (hi - lo + 31u) / 32u;
+        const uint32_t i = lo + lane * step;
+        const bool le = i < hi && prefix[i] <= x;
+        const uint32_t mask = __ballot_sync(0xffffffffu, le);
+        const uint32_t last = 31u - (uint32_t)__clz(mask);  // lane 0 always holds (prefix[lo] <= x)
+        lo = lo + last * step;
+        hi = min(hi, lo + step);
+    }
+    return lo;
+}
+
 // ------------------------------------------------------------------ gradients
 // data/subsample.rs:45-78 row hash (SplitMix64 finalizer of seed, tree, row).
 __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
@@ -1107,7 +1127,7 @@ __device__ __forceinline__ void part_count_work(const LevelArgs& a) {
     const TreeState* st = a.st;
     if (c >= st->chunk_count) return;
     const uint32_t m = st->m;
-    const uint32_t j = find_segment(a.chunk_prefix, m, c);
+    const uint32_t j = find_segment_warp(a.chunk_prefix, m, c);
     const NodeInfo ni = a.nodes[j];
     const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
     const uint32_t cnt = min(kChunkRows, ni.len - r0);
@@ -1193,7 +1213,7 @@ __device__ __forceinline__ void part_scatter_work(const LevelArgs& a) {
     const TreeState* st = a.st;
     if (c >= st->chunk_count) return;
     const uint32_t m = st->m;
-    const uint32_t j = find_segment(a.chunk_prefix, m, c);
+    const uint32_t j = find_segment_warp(a.chunk_prefix, m, c);
     const SplitDesc sd = a.split[j];
     if (sd.child_slot < 0) return;
     const NodeInfo ni = a.nodes[j];
@@ -1332,7 +1352,7 @@ __global__ void __launch_bounds__(kPartThreads) k_leaf_final(LevelArgs a) {
     const uint32_t c = blockIdx.x;
     const TreeState* st = a.st;
     if (c >= st->chunk_count) return;
-    const uint32_t j = find_segment(a.chunk_prefix, st->m, c);
+    const uint32_t j = find_segment_warp(a.chunk_prefix, st->m, c);
     const NodeInfo ni = a.nodes[j];
     const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
     const uint32_t cnt = min(kChunkRows, ni.len - r0);
