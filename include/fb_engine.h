@@ -183,7 +183,10 @@ uint32_t fb_model_num_outputs(const fb_model* m);
 int32_t fb_model_transform(const fb_model* m, float* margins, uint64_t n, float* classes);
 /* The model's device copy on `device` as an include/fbgpu.h handle (owned by
  * the model, valid until the model is freed or gains trees), for
- * fbgpu_predict_device / fbgpu_shap_device on device-resident rows. */
+ * fbgpu_predict_device / fbgpu_shap_device on device-resident rows.  For a
+ * multiclass model the handle holds all trees in order with a zero base margin
+ * (what fbgpu_explain's leaf indices need); per-class margins and SHAP groups
+ * come from fb_model_predict / fb_model_shap. */
 struct fbgpu_model* fb_model_device(fb_model* m, int32_t device);
 /* SHAP contributions n x (F+1) on the device; n x K x (F+1) for a
  * multiclass model (one group per class, src/model/explain.rs:704-727). */
