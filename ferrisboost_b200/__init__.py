@@ -452,6 +452,105 @@ class Model:
             out = out.replace(b'"feature_names":[]', b'"feature_names":' + names.encode("utf-8"), 1)
         return out
 
+    @staticmethod
+    def load_model(source: "str | os.PathLike | bytes", device=None) -> "Model":
+        """A model from XGBoost-compatible JSON: a path or the JSON bytes (the
+        reference's ``Model.load_model``, src/model/tree.rs:760-960).  Models
+        of this engine and XGBoost models of its objectives (reg:squarederror,
+        binary:logistic, multi:softprob, multi:softmax) load; ``save_model`` of
+        the result writes the same JSON back."""
+        if isinstance(source, (bytes, bytearray)):
+            doc = json.loads(source)
+        else:
+            with open(os.fspath(source), "rb") as f:
+                doc = json.load(f)
+        learner = doc["learner"]
+        obj = learner["objective"]["name"]
+        if obj not in _OBJECTIVES:
+            raise ValueError(f"objective {obj!r} is not supported on this engine; supported objectives: "
+                             f"{', '.join(_OBJECTIVES)}")
+        lp = learner["learner_model_param"]
+        F = int(lp["num_feature"])
+        raw = str(lp["base_score"]).strip()
+        margins = [np.float32(float(v)) for v in raw.strip("[]").split(",") if v.strip()] if raw.startswith("[") \
+            else [np.float32(float(raw))]
+        K = int(lp.get("num_class", "0") or 0)
+        multi = obj.startswith("multi:")
+        if multi and (K < 2 or len(margins) != K):
+            raise ValueError(f"{obj} model with num_class {K} and {len(margins)} base margins")
+        spw = float(learner["objective"].get("reg_loss_param", {}).get("scale_pos_weight", "1"))
+        ftypes = learner.get("feature_types") or []
+        if ftypes and len(ftypes) != F:
+            raise ValueError(f"feature_types has {len(ftypes)} entries, the model has {F} features")
+        gbm = learner["gradient_booster"]["model"]
+        trees = gbm["trees"]
+        info = gbm.get("tree_info", [0] * len(trees))
+        k_out = K if multi else 1
+        if any(int(c) != t % k_out for t, c in enumerate(info)):
+            raise ValueError("tree_info must assign tree t to output t % num_class")
+        off = [0]
+        cols = {k: [] for k in ("left", "right", "feat", "cond", "dl", "leaf", "gain", "hess", "cat", "coff", "clen")}
+        words: list[int] = []
+        for t in trees:
+            n = len(t["left_children"])
+            cats_of = {}
+            for pos, node in enumerate(t.get("categories_nodes", [])):
+                seg, size = t["categories_segments"][pos], t["categories_sizes"][pos]
+                cats_of[int(node)] = [int(c) for c in t["categories"][seg:seg + size]]
+            split_type = t.get("split_type", [0] * n)
+            for i in range(n):
+                cols["left"].append(int(t["left_children"][i]))
+                cols["right"].append(int(t["right_children"][i]))
+                cols["feat"].append(int(t["split_indices"][i]))
+                cols["cond"].append(float(t["split_conditions"][i]))
+                cols["dl"].append(int(bool(t["default_left"][i])))
+                cols["leaf"].append(float(t["base_weights"][i]) if int(t["left_children"][i]) >= 0
+                                    else float(t["split_conditions"][i]))
+                cols["gain"].append(float(t["loss_changes"][i]))
+                cols["hess"].append(float(t["sum_hessian"][i]))
+                is_cat = int(split_type[i]) == 1
+                cols["cat"].append(int(is_cat))
+                cols["coff"].append(len(words))
+                if is_cat:
+                    cs = cats_of.get(i, [])
+                    w = [0] * ((max(cs) >> 5) + 1 if cs else 0)
+                    for c in cs:
+                        w[c >> 5] |= 1 << (c & 31)
+                    words.extend(w)
+                    cols["clen"].append(len(w))
+                else:
+                    cols["clen"].append(0)
+            off.append(off[-1] + n)
+        arr = {
+            "left": np.array(cols["left"], np.int32), "right": np.array(cols["right"], np.int32),
+            "feat": np.array(cols["feat"], np.uint32), "cond": np.array(cols["cond"], np.float32),
+            "dl": np.array(cols["dl"], np.uint8), "leaf": np.array(cols["leaf"], np.float32),
+            "gain": np.array(cols["gain"], np.float32), "hess": np.array(cols["hess"], np.float32),
+            "cat": np.array(cols["cat"], np.uint8), "coff": np.array(cols["coff"], np.uint32),
+            "clen": np.array(cols["clen"], np.uint32),
+        }
+        off_a = np.array(off, np.uint32)
+        wa = np.array(words if words else [0], np.uint32)
+        cm = np.array(margins, np.float32) if multi else None
+        ft = np.array([t == "c" for t in ftypes], np.uint8) if ftypes else None
+        h = lib().fb_model_create(F, _OBJECTIVES[obj], float(margins[0]), spw, K if multi else 0,
+                                  _lib.ptr(cm, C.c_float), _lib.ptr(ft, C.c_uint8), len(trees),
+                                  _lib.ptr(off_a, C.c_uint32), _lib.ptr(arr["left"], C.c_int32),
+                                  _lib.ptr(arr["right"], C.c_int32), _lib.ptr(arr["feat"], C.c_uint32),
+                                  _lib.ptr(arr["cond"], C.c_float), _lib.ptr(arr["dl"], C.c_uint8),
+                                  _lib.ptr(arr["leaf"], C.c_float), _lib.ptr(arr["gain"], C.c_float),
+                                  _lib.ptr(arr["hess"], C.c_float), _lib.ptr(arr["cat"], C.c_uint8),
+                                  _lib.ptr(arr["coff"], C.c_uint32), _lib.ptr(arr["clen"], C.c_uint32),
+                                  _lib.ptr(wa, C.c_uint32))
+        if not h:
+            raise ValueError(_err())
+        params = {"objective": obj, "num_class": K if multi else 0, "missing": float("nan")}
+        if device is not None:
+            params["device"] = device
+        m = Model(h, params)
+        m.feature_names = list(learner.get("feature_names") or []) or None
+        return m
+
     def save_model(self, path: str | os.PathLike) -> None:
         """XGBoost-compatible JSON (reference src/model/model_io.rs: atomic write)."""
         path = os.fspath(path)

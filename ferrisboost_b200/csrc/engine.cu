@@ -1380,6 +1380,72 @@ int64_t fb_model_json(const fb_model* m, char* buf, int64_t cap) {
     return (int64_t)s.size();
 }
 
+fb_model* fb_model_create(uint32_t n_features, int32_t objective, float base_score, float scale_pos_weight,
+                          uint32_t num_class, const float* class_margins, const uint8_t* feature_types,
+                          uint32_t n_trees, const uint32_t* tree_off, const int32_t* left, const int32_t* right,
+                          const uint32_t* feat, const float* cond, const uint8_t* default_left, const float* leaf,
+                          const float* gain, const float* hess, const uint8_t* is_cat, const uint32_t* cat_off,
+                          const uint32_t* cat_len, const uint32_t* cat_words) {
+    return fbe::guarded([&]() -> fb_model* {
+        if (n_features == 0) throw fbe::InputError("a model needs at least one feature");
+        if (objective < 0 || objective > 3) throw fbe::InputError("unsupported objective code");
+        if (objective >= 2 && (num_class < 2 || !class_margins))
+            throw fbe::InputError("a multiclass model needs num_class >= 2 and its class margins");
+        if (tree_off[0] != 0) throw fbe::InputError("tree offsets must start at 0");
+        std::unique_ptr<fb_model> m(new fb_model());
+        m->n_features = n_features;
+        m->objective = objective;
+        m->base_score = base_score;
+        m->scale_pos_weight = scale_pos_weight;
+        if (objective >= 2) {
+            m->class_margins.assign(class_margins, class_margins + num_class);
+            m->base_score = class_margins[0];
+        }
+        if (feature_types) {
+            m->feature_types.assign(feature_types, feature_types + n_features);
+            if (std::none_of(m->feature_types.begin(), m->feature_types.end(), [](uint8_t c) { return c != 0; }))
+                m->feature_types.clear();
+        }
+        m->trees.resize(n_trees);
+        for (uint32_t t = 0; t < n_trees; t++) {
+            const uint32_t b = tree_off[t], e = tree_off[t + 1];
+            if (e <= b) throw fbe::InputError("tree " + std::to_string(t) + " has no nodes");
+            const int32_t nn = (int32_t)(e - b);
+            auto& N = m->trees[t].nodes;
+            N.resize(nn);
+            for (int32_t i = 0; i < nn; i++) {
+                const uint32_t g = b + (uint32_t)i;
+                fbe::Node& nd = N[i];
+                nd.gain = gain ? gain[g] : 0.0f;
+                nd.hess = hess ? hess[g] : 0.0f;
+                nd.leaf = leaf[g];
+                nd.default_left = default_left[g] != 0;
+                if (left[g] < 0) {
+                    nd.is_leaf = true;
+                    continue;
+                }
+                if (left[g] >= nn || right[g] < 0 || right[g] >= nn || left[g] == i || right[g] == i)
+                    throw fbe::InputError("tree " + std::to_string(t) + " node " + std::to_string(i) +
+                                          " has a child outside the tree");
+                if (feat[g] >= n_features)
+                    throw fbe::InputError("tree " + std::to_string(t) + " splits on feature " +
+                                          std::to_string(feat[g]) + ", the model has " + std::to_string(n_features));
+                nd.is_leaf = false;
+                nd.left = left[g];
+                nd.right = right[g];
+                nd.feat = feat[g];
+                nd.cond = cond[g];
+                nd.is_cat = is_cat && is_cat[g];
+                if (nd.is_cat) {
+                    nd.cats.assign(cat_words + cat_off[g], cat_words + cat_off[g] + cat_len[g]);
+                    while (!nd.cats.empty() && nd.cats.back() == 0) nd.cats.pop_back();
+                }
+            }
+        }
+        return m.release();
+    }, nullptr);
+}
+
 int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* right, uint32_t* feat, float* cond,
                       uint8_t* default_left, float* leaf, uint8_t* is_leaf, float* gain, float* hess, uint32_t* cats) {
     if (t >= m->trees.size()) return -1;
