@@ -355,7 +355,9 @@ def run_ours(args, rank, world):
     depth = p.get("max_depth", 6)
     leaves = p.get("max_leaves", 0) or 2 ** depth
     tree_readback = 32 * min(2 ** (depth + 1), 2 * leaves + 1) + 64
-    bin_bytes = F * (2 if p["max_bin"] > 255 else 1)
+    # host -> device per e2e run: the f32 rows (the device sketches and bins
+    # them) and the f32 labels; spread over its 100 rounds
+    e2e_h2d = rows_local * (F * 4 + 4)
     line = {
         "metric": "train s/100 rounds", "value": round(s100, 4), "unit": "s/100 rounds", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": False,
@@ -365,7 +367,7 @@ def run_ours(args, rank, world):
                    if n * ((F * (2 if p["max_bin"] > 255 else 1) + 15) // 16 * 16 + 16) > 126e6
                    else "inputs smaller than L2"},
         "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds",
-                "h2d_bytes_per_step": int((rows_local * (bin_bytes + 4)) / E2E_ROUNDS),
+                "h2d_bytes_per_step": int(e2e_h2d / E2E_ROUNDS),
                 "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / E2E_ROUNDS),
                 "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "
                             "per-rank bytes; wall clock, max over ranks"},
