@@ -639,12 +639,13 @@ class Model:
 
 
 def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
-          feature_types: Sequence[str] | None = None, quiet: bool = True) -> Model:
+          feature_types: Sequence[str] | None = None, quiet: bool = True, header: bool = True) -> Model:
     """Train a model (reference python/ferrisboost/__init__.py:1090 ``train``).
 
     ``data`` is a 2-D array with ``label`` (and ``weight``) arrays; a
-    ``.parquet`` path, a list of paths, a directory or a glob pattern with
-    ``label`` (and ``weight``) naming columns of the files; or a pyarrow
+    ``.parquet`` / ``.csv`` path, a list of paths, a directory or a glob
+    pattern with ``label`` (and ``weight``) naming columns of the files (a
+    headerless CSV, ``header=False``: column indices); or a pyarrow
     Table / RecordBatch / RecordBatchReader with ``label`` an array
     (``columnar`` has the decode rules).  Columnar inputs record their column
     names as the model's feature names."""
@@ -652,11 +653,13 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     specs = columnar.path_specs(data)
     table = None if specs is not None else columnar.arrow_table(data)
     if specs is not None:
-        if not isinstance(label, str):
-            raise ValueError("for file input, label must be the name of a column of the file")
-        if weight is not None and not isinstance(weight, str):
-            raise ValueError("for file input, weight must be the name of a column of the file")
-        data = columnar.read_files(specs, label, weight, feature_types, p["missing"])
+        col = str if header else int
+        kind = "the name" if header else "the index"
+        if not isinstance(label, col) or isinstance(label, bool):
+            raise ValueError(f"for file input, label must be {kind} of a column of the file")
+        if weight is not None and (not isinstance(weight, col) or isinstance(weight, bool)):
+            raise ValueError(f"for file input, weight must be {kind} of a column of the file")
+        data = columnar.read_files(specs, label, weight, feature_types, p["missing"], header=header)
         label, weight, feature_types = data.label, data.weight, None
     elif table is not None:
         data = columnar.read_table(table, p["enable_categorical"], feature_types, p["missing"])
@@ -669,5 +672,5 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     b.update(num_boost_round)
     m = b.model()
     m.params = p
-    m.feature_names = ds.feature_names
+    m.feature_names = ds.feature_names or None
     return m

@@ -1,4 +1,4 @@
-"""Columnar ingest: Parquet files and pyarrow tables into device-resident bins.
+"""Columnar ingest: Parquet / CSV files and pyarrow tables into device-resident bins.
 
 The reference reads Parquet column chunks in Rust (src/source/parquet_source.rs,
 decode rules in src/source/arrow_source.rs:121-200) and pyarrow tables in
@@ -17,6 +17,11 @@ Decode rules (the reference's, value for value):
   f32 range) is an error for features, labels and weights.  Without
   ``feature_types``, dictionary columns are categorical
   (parquet_source.rs:472-500).  Other column types are errors.
+- CSV files (src/source/csv_source.rs): Arrow's CSV reader infers each
+  column's type (integers -> Int64, decimals -> Float64) and only an empty
+  field is null; the values then follow the Parquet rules above.  With
+  ``header=False`` the label (and weight) are column indices and the model
+  records no feature names.
 - pyarrow tables: a dictionary column needs ``enable_categorical`` and
   contributes its dictionary indices as category codes (null -> NaN); other
   columns convert with ``to_numpy`` then ``float32``.
@@ -69,14 +74,14 @@ def arrow_table(obj: Any):
 
 def expand_paths(specs: Sequence[str]) -> list[str]:
     """Files of the given specs in order: a directory contributes its
-    ``.parquet`` / ``.pq`` files sorted by name, a pattern with ``*``, ``?`` or
-    ``[`` its sorted matches, anything else itself."""
+    ``.parquet`` / ``.pq`` / ``.csv`` files sorted by name, a pattern with
+    ``*``, ``?`` or ``[`` its sorted matches, anything else itself."""
     out: list[str] = []
     for s in specs:
         if os.path.isdir(s):
-            files = sorted(f for f in os.listdir(s) if f.lower().endswith((".parquet", ".pq")))
+            files = sorted(f for f in os.listdir(s) if f.lower().endswith((".parquet", ".pq", ".csv")))
             if not files:
-                raise ValueError(f"directory {s!r} holds no .parquet files")
+                raise ValueError(f"directory {s!r} holds no .parquet or .csv files")
             out.extend(os.path.join(s, f) for f in files)
         elif any(c in s for c in "*?["):
             files = sorted(glob.glob(s))
@@ -85,8 +90,8 @@ def expand_paths(specs: Sequence[str]) -> list[str]:
             out.extend(files)
         else:
             lower = s.lower()
-            if not (lower.endswith(".parquet") or lower.endswith(".pq")):
-                raise ValueError(f"cannot tell the format of {s!r} from its extension; supported: .parquet")
+            if not (lower.endswith(".parquet") or lower.endswith(".pq") or lower.endswith(".csv")):
+                raise ValueError(f"cannot tell the format of {s!r} from its extension; supported: .parquet / .csv")
             if not os.path.exists(s):
                 raise FileNotFoundError(s)
             out.append(s)
@@ -115,6 +120,35 @@ def file_schema(path: str):
         except (ValueError, pa.ArrowException):
             pass
     return pq.read_schema(path)
+
+
+def _is_csv(path: str) -> bool:
+    return path.lower().endswith(".csv")
+
+
+def _read_csv(path: str, header: bool = True):
+    """A CSV file as a pyarrow Table with Arrow's type inference; only an empty
+    field is null (csv_source.rs:193-195).  Headerless columns are named
+    "0", "1", ... by position."""
+    import pyarrow.csv as pcsv
+
+    ro = pcsv.ReadOptions(autogenerate_column_names=not header, use_threads=True)
+    co = pcsv.ConvertOptions(null_values=[""], strings_can_be_null=True, quoted_strings_can_be_null=True)
+    table = pcsv.read_csv(path, read_options=ro, convert_options=co)
+    if not header:
+        table = table.rename_columns([str(i) for i in range(table.num_columns)])
+    return table
+
+
+def _open(path: str, header: bool = True):
+    """(schema, reader of named columns) of a Parquet or CSV file."""
+    import pyarrow.parquet as pq
+
+    if _is_csv(path):
+        table = _read_csv(path, header)
+        return table.schema, (lambda cols: table.select(list(cols))), table.num_rows
+    return file_schema(path), (lambda cols: pq.read_table(path, columns=list(cols), use_threads=True)), \
+        pq.ParquetFile(path).metadata.num_rows
 
 
 def _file_column_f32(col, name: str, missing: float, out: np.ndarray, allow_inf: bool = False,
@@ -167,29 +201,36 @@ def _file_column_f32(col, name: str, missing: float, out: np.ndarray, allow_inf:
         out[out == np.float32(missing)] = np.float32("nan")
 
 
-def read_files(specs: Sequence[str], label: str | None, weight: str | None, feature_types=None,
-               missing: float = float("nan")) -> Columns:
-    """Parquet file(s) -> feature columns, label and weight columns by name
-    (parquet_source.rs:36-90 LabeledSource, 447-500 feature_columns and
-    resolve_categorical_flags).  Files are concatenated in order; every file
-    must hold the first file's columns (bound by name)."""
+def read_files(specs: Sequence[str], label: "str | int | None", weight: "str | int | None", feature_types=None,
+               missing: float = float("nan"), header: bool = True) -> Columns:
+    """Parquet / CSV file(s) -> feature columns, label and weight columns by
+    name (parquet_source.rs:36-90 LabeledSource, 447-500 feature_columns and
+    resolve_categorical_flags; a headerless CSV names them by index).  Files
+    are concatenated in order; every file must hold the first file's columns
+    (bound by name)."""
     import pyarrow as pa
-    import pyarrow.parquet as pq
 
     files = expand_paths(specs)
-    schema = file_schema(files[0])
+    if not header:
+        if any(not _is_csv(f) for f in files):
+            raise ValueError("header=False applies to CSV files only")
+        label = None if label is None else str(int(label))
+        weight = None if weight is None else str(int(weight))
+    opened = [_open(f, header) for f in files]
+    schema = opened[0][0]
     names_all = list(schema.names)
     if len(set(names_all)) != len(names_all):
         raise ValueError(f"{files[0]} has duplicate column names")
     for what, col in (("label", label), ("weight", weight)):
         if col is not None and col not in names_all:
-            raise ValueError(f"{what} column {col!r} is not in {files[0]} (columns: {names_all})")
+            where = f"column index {col}" if not header else f"column {col!r}"
+            raise ValueError(f"{what} {where} is not in {files[0]} (columns: {names_all})")
     if label is None:
         raise ValueError("label must name a column of the file")
     feats = [c for c in names_all if c not in (label, weight)]
     if not feats:
         raise ValueError("the file has no feature columns besides the label")
-    counts = [pq.ParquetFile(f).metadata.num_rows for f in files]
+    counts = [o[2] for o in opened]
     n = int(sum(counts))
     if n == 0:
         raise ValueError("training data must have at least one row")
@@ -199,13 +240,12 @@ def read_files(specs: Sequence[str], label: str | None, weight: str | None, feat
     w = np.empty(n, np.float32) if weight is not None else None
     dict_cols = np.zeros(F, bool)
     r0 = 0
-    for f_path, cnt in zip(files, counts):
+    for f_path, (sch, read, cnt) in zip(files, opened):
         want = feats + [label] + ([weight] if weight is not None else [])
-        sch = file_schema(f_path)
         miss = [c for c in want if c not in sch.names]
         if miss:
             raise ValueError(f"{f_path} lacks the columns {miss} of {files[0]}")
-        table = pq.read_table(f_path, columns=want, use_threads=True)
+        table = read(want)
         for i, name in enumerate(feats):
             dict_cols[i] |= pa.types.is_dictionary(sch.field(name).type)
         # columns convert in parallel (the numpy copies release the GIL)
@@ -225,24 +265,22 @@ def read_files(specs: Sequence[str], label: str | None, weight: str | None, feat
         cat = np.array([t == "c" for t in ft], np.uint8)
     else:
         cat = dict_cols.astype(np.uint8)
-    return Columns(X, feats, cat if cat.any() else None, y, w)
+    # a headerless CSV has no column names to record (tree.rs:247)
+    return Columns(X, feats if header else [], cat if cat.any() else None, y, w)
 
 
 def read_file_features(specs: Sequence[str], names: Sequence[str], missing: float = float("nan")) -> np.ndarray:
-    """Prediction input from Parquet file(s): the named columns, bound by
-    name, as (F, n) float32 with the file decode rules (+-inf kept)."""
-    import pyarrow.parquet as pq
-
+    """Prediction input from Parquet / CSV file(s): the named columns, bound
+    by name, as (F, n) float32 with the file decode rules (+-inf kept)."""
     files = expand_paths(specs)
-    counts = [pq.ParquetFile(f).metadata.num_rows for f in files]
-    X = np.empty((len(names), int(sum(counts))), np.float32)
+    opened = [_open(f) for f in files]
+    X = np.empty((len(names), int(sum(o[2] for o in opened))), np.float32)
     r0 = 0
-    for f_path, cnt in zip(files, counts):
-        sch = file_schema(f_path)
+    for f_path, (sch, read, cnt) in zip(files, opened):
         miss = [c for c in names if c not in sch.names]
         if miss:
             raise ValueError(f"{f_path} lacks the model's feature columns {miss}")
-        table = pq.read_table(f_path, columns=list(names), use_threads=True)
+        table = read(names)
         with ThreadPoolExecutor(max(1, min(len(names), os.cpu_count() or 1))) as ex:
             list(ex.map(lambda i: _file_column_f32(table.column(names[i]), names[i], missing, X[i, r0:r0 + cnt],
                                                    allow_inf=True, file_type=sch.field(names[i]).type),

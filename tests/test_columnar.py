@@ -92,7 +92,7 @@ def test_parquet_missing_sentinel_inf_and_types(tmp_path):
     with pytest.raises(ValueError, match="label column 'nope'"):
         columnar.read_files([str(p)], "nope", None)
     with pytest.raises(ValueError, match="format"):
-        columnar.expand_paths([str(tmp_path / "x.csv")])
+        columnar.expand_paths([str(tmp_path / "x.txt")])
 
 
 def test_parquet_prediction_keeps_inf(tmp_path):
@@ -141,3 +141,59 @@ def test_arrow_table_rules():
     assert columnar.arrow_table(rb).num_rows == rb.num_rows
     assert columnar.arrow_table(np.zeros((2, 2))) is None
     assert columnar.path_specs("x.parquet") == ["x.parquet"] and columnar.path_specs(np.zeros(2)) is None
+
+
+def test_csv_decode_rules(tmp_path):
+    # csv_source.rs: Arrow's inference (integers -> Int64, decimals -> Float64)
+    # and only an empty field is null; then the Parquet decode rules
+    rng = np.random.default_rng(7)
+    n = 300
+    ints = rng.integers(-2**40, 2**40, n)
+    dec = rng.standard_normal(n) * 100
+    y = rng.integers(0, 2, n)
+    lines = ["a,b,label,c"]
+    for i in range(n):
+        b = "" if i % 17 == 0 else repr(float(dec[i]))
+        c = "NaN" if i % 23 == 0 else "0.1"
+        lines.append(f"{ints[i]},{b},{y[i]},{c}")
+    path = tmp_path / "d.csv"
+    path.write_text("\n".join(lines) + "\n")
+    c = columnar.read_files([str(path)], "label", None)
+    assert c.names == ["a", "b", "c"]
+    assert np.array_equal(c.X[0], ints.astype(np.float32))  # one rounding, int64 -> f32
+    want_b = np.where(np.arange(n) % 17 == 0, np.nan, dec).astype(np.float32)
+    assert np.array_equal(c.X[1], want_b, equal_nan=True)
+    want_c = np.where(np.arange(n) % 23 == 0, np.nan, 0.1).astype(np.float32)
+    assert np.array_equal(c.X[2], want_c, equal_nan=True)
+    assert np.array_equal(c.label, y.astype(np.float32))
+    # headerless: label and weight by column index, no feature names
+    hp = tmp_path / "h.csv"
+    hp.write_text("\n".join(lines[1:]) + "\n")
+    h = columnar.read_files([str(hp)], 2, None, header=False)
+    assert h.names == [] and np.array_equal(h.X, c.X, equal_nan=True) and np.array_equal(h.label, c.label)
+    with pytest.raises(ValueError, match="column index 9"):
+        columnar.read_files([str(hp)], 9, None, header=False)
+    bad = tmp_path / "s.csv"
+    bad.write_text("a,label\nx,1\ny,0\n")
+    with pytest.raises(ValueError, match="only numeric columns"):
+        columnar.read_files([str(bad)], "label", None)
+
+
+def test_csv_columns_bin_like_the_array():
+    import ferrisboost_b200 as fb
+    import tempfile, os
+    rng = np.random.default_rng(8)
+    X = rng.standard_normal((2000, 4)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "t.csv")
+        with open(path, "w") as f:
+            f.write("f0,f1,f2,f3,y\n")
+            for r in range(len(X)):
+                f.write(",".join("" if np.isnan(v) else repr(float(v)) for v in X[r]) + ",0\n")
+        c = columnar.read_files([path], "y", None)
+    a = fb.Dataset(X, max_bin=64)
+    b = fb.Dataset(c, max_bin=64)
+    assert all(np.array_equal(u, v) for u, v in zip(a.cuts(), b.cuts()))
+    assert all(np.array_equal(a.column(f), b.column(f)) for f in range(4))
+    assert b.feature_names == ["f0", "f1", "f2", "f3"]

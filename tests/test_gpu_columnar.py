@@ -101,3 +101,21 @@ def test_arrow_table_training_and_multi_file(oracle, tmp_path):
     m2 = fb.train(pr, str(d), label="y", weight="w", num_boost_round=6)
     ref2 = oracle.train(X, y, w, n_rounds=6, categorical=np.array([0, 0, 0, 0, 1], np.uint8), **pr)
     assert m2.to_json() == _named(ref2.json(), ["a", "b", "c", "d", "k"])
+
+
+def test_csv_training_matches_array(oracle, tmp_path):
+    rng = np.random.default_rng(9)
+    X = rng.standard_normal((20000, 5)).astype(np.float32)
+    X[rng.random(X.shape) < 0.03] = np.nan
+    y = (np.nan_to_num(X[:, 0]) - np.nan_to_num(X[:, 3]) > 0).astype(np.float32)
+    rows = [",".join("" if np.isnan(v) else repr(float(v)) for v in X[r]) + f",{int(y[r])}" for r in range(len(X))]
+    path = tmp_path / "t.csv"
+    path.write_text("a,b,c,d,e,y\n" + "\n".join(rows) + "\n")
+    p = dict(objective="binary:logistic", max_depth=5, eta=0.3, max_bin=64)
+    m = fb.train(p, str(path), label="y", num_boost_round=5)
+    ref = oracle.train(X, y, n_rounds=5, **p)
+    assert m.to_json() == _named(ref.json(), ["a", "b", "c", "d", "e"])
+    hp = tmp_path / "h.csv"
+    hp.write_text("\n".join(rows) + "\n")
+    mh = fb.train(p, str(hp), label=5, num_boost_round=5, header=False)
+    assert mh.to_json() == ref.json() and mh.feature_names is None
