@@ -133,3 +133,22 @@ def test_multiclass_base_score_and_label_checks(oracle):
         oracle.train(X, y + 0.5, objective="multi:softprob", num_class=3, n_rounds=1)
     with pytest.raises(RuntimeError, match="num_class"):
         oracle.train(X, y, objective="multi:softprob", num_class=1, n_rounds=1)
+
+
+def test_engine_class_margins_equal_the_oracle(oracle):
+    # the engine's host restatement (fb_class_margins, used by row-sharded
+    # multiclass training) against the oracle's, bit for bit
+    import ctypes as C
+    from ferrisboost_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(11)
+    for K, weighted in ((2, False), (5, True), (9, True)):
+        y = rng.integers(0, K, 20000).astype(np.float32)
+        w = rng.uniform(0, 3, 20000).astype(np.float32) if weighted else None
+        out = np.zeros(K, np.float32)
+        assert lib.fb_class_margins(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), len(y), K,
+                                    _lib.ptr(out, C.c_float)) == 0
+        assert np.array_equal(out.view(np.uint32), oracle.class_margins(y, K, w).view(np.uint32))
+    bad = np.array([0, 1, 2.5], np.float32)
+    out = np.zeros(3, np.float32)
+    assert lib.fb_class_margins(_lib.ptr(bad, C.c_float), None, 3, 3, _lib.ptr(out, C.c_float)) != 0
