@@ -931,10 +931,9 @@ void booster_round_multi(Booster& b) {
     const int fast = p.gpu_math == 1 ? 1 : 0;
     auto t0 = std::chrono::steady_clock::now();
     ctx.softmax_gradients(fast);
-    double t_grad = 0, t_tree = 0;
+    double t_tree = 0;  // tree growth; the rest of the round counts as gradient time
     for (uint32_t k = 0; k < K; k++) {
         const uint64_t tree = (uint64_t)b.rounds_done * K + k;
-        auto ta = std::chrono::steady_clock::now();
         ctx.quantize_class(k, th, p.seed, tree, fast);
         std::vector<uint8_t> en = sample_features(b.d->F, p.colsample_bytree, p.seed, tree);
         fbgpu_tree_params tp = tree_params(b);
@@ -944,14 +943,12 @@ void booster_round_multi(Booster& b) {
         ctx.build_tree(tp, p.colsample_bytree < 1.0f ? en.data() : nullptr, &out);
         auto tc = std::chrono::steady_clock::now();
         b.model.trees.push_back(assemble_tree(b, out));
-        t_grad += std::chrono::duration<double, std::milli>(tb - ta).count();
         t_tree += std::chrono::duration<double, std::milli>(tc - tb).count();
     }
     ctx.set_pred_column(0);
     b.rounds_done++;
     b.t_grad += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count() - t_tree;
     b.t_tree += t_tree;
-    (void)t_grad;
 }
 
 // One boosting round (training/mod.rs:1895-2311).
