@@ -15,6 +15,10 @@
 // Parity is pinned by the XGBoost 3.4.1 golden margins the reference ships in
 // tests/fixtures (tests/bit_exact_vs_xgboost.rs:213-554): 18 unweighted, 13
 // weighted and 13 monotone cases, checked bit for bit by tests/test_oracle.py.
+// The multiclass objectives have no golden vectors in the reference: their
+// restatement (softmax gradients, class base margins, K trees per round) is
+// pinned piecewise against independent statements (tests/test_multiclass_oracle.py)
+// and otherwise reuses the pinned single-output tree builder.
 #include "refcpu.h"
 
 #include <algorithm>
