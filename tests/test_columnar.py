@@ -197,3 +197,44 @@ def test_csv_columns_bin_like_the_array():
     assert all(np.array_equal(u, v) for u, v in zip(a.cuts(), b.cuts()))
     assert all(np.array_equal(a.column(f), b.column(f)) for f in range(4))
     assert b.feature_names == ["f0", "f1", "f2", "f3"]
+
+
+def test_parquet_decode_property(tmp_path):
+    # random numeric columns (every accepted type, nulls, a missing sentinel)
+    # decode like an independent numpy statement of the rules
+    from hypothesis import given, settings, strategies as st
+
+    types = [pa.float32(), pa.float64(), pa.int32(), pa.int64()]
+
+    @settings(max_examples=25, deadline=None)
+    @given(st.integers(1, 200), st.lists(st.integers(0, 3), min_size=1, max_size=5), st.integers(0, 2**31 - 1),
+           st.booleans())
+    def check(n, kinds, seed, sentinel):
+        rng = np.random.default_rng(seed)
+        cols, want = {}, []
+        miss = -7.0 if sentinel else float("nan")
+        for j, k in enumerate(kinds):
+            t = types[k]
+            nulls = rng.random(n) < 0.2
+            if pa.types.is_integer(t):
+                lim = 2**31 - 1 if t == pa.int32() else 2**62
+                v = rng.integers(-lim, lim, n).astype(np.int64)
+                v[rng.random(n) < 0.1] = -7
+                cols[f"c{j}"] = pa.array(v.astype(np.int32) if t == pa.int32() else v, t, mask=nulls)
+                exp = v.astype(np.float32)
+            else:
+                v = rng.standard_normal(n) * 1e3
+                v[rng.random(n) < 0.1] = -7.0
+                cols[f"c{j}"] = pa.array(v.astype(np.float32) if t == pa.float32() else v, t, mask=nulls)
+                exp = v.astype(np.float32)
+            exp = np.where(nulls, np.nan, exp).astype(np.float32)
+            if sentinel:
+                exp[exp == np.float32(-7.0)] = np.nan
+            want.append(exp)
+        cols["y"] = pa.array(np.zeros(n, np.float32))
+        path = tmp_path / f"p{seed}.parquet"
+        pq.write_table(pa.table(cols), path)
+        c = columnar.read_files([str(path)], "y", None, missing=miss)
+        assert np.array_equal(c.X, np.stack(want), equal_nan=True)
+
+    check()
