@@ -84,6 +84,153 @@ def build(force: bool = False):
     return _build(force=force)
 
 
+def _int_param(name: str, raw: Any) -> int:
+    """XGBoost writes every parameter as a string (tree.rs:1082-1095 parse_param)."""
+    try:
+        return int(str(raw).strip())
+    except ValueError:
+        raise ValueError(f"{name} = {raw!r} is not an integer") from None
+
+
+def _base_scores(raw: Any, multi: bool) -> list:
+    """tree.rs:1034-1080: "5E-1" (1.x / 2.x) or "[5E-1]" (3.x); a vector
+    "[a,b,c]" only for multiclass models."""
+    t = str(raw).strip()
+    inner = t[1:-1] if t.startswith("[") and t.endswith("]") else t
+    parts = [p.strip() for p in inner.split(",") if p.strip()]
+    if not parts:
+        raise ValueError(f"base_score is empty: {raw!r}")
+    if len(parts) > 1 and not multi:
+        raise ValueError(f"base_score is a vector ({raw!r}); multi-target models are not supported")
+    try:
+        return [np.float32(float(p)) for p in parts]
+    except ValueError:
+        raise ValueError(f"base_score = {raw!r} is not a number") from None
+
+
+def _parse_xgb_model(doc: Mapping) -> dict:
+    """The flat arrays ``fb_model_create`` takes, from an XGBoost JSON document,
+    with the reference loader's checks (src/model/tree.rs:765-890 for the
+    learner, :1258-1362 for each tree's arrays and category segments)."""
+    learner = doc["learner"]
+    booster = learner["gradient_booster"]
+    if booster.get("name", "gbtree") != "gbtree":
+        raise ValueError(f"only gbtree is supported, this model is {booster.get('name')}")
+    objective = learner["objective"]
+    obj = objective["name"]
+    if obj not in _OBJECTIVES:
+        raise ValueError(f"objective {obj!r} is not supported on this engine; supported objectives: "
+                         f"{', '.join(_OBJECTIVES)}")
+    multi = obj.startswith("multi:")
+    lp = learner["learner_model_param"]
+    num_class = max(_int_param("num_class", lp.get("num_class", "0") or "0"), 1)
+    nt_raw = str(lp.get("num_target", "")).strip()
+    num_target = max(_int_param("num_target", nt_raw), 1) if nt_raw else 1
+    if num_target > 1:
+        raise ValueError(f"multi-target models are not supported (num_target = {num_target})")
+    K = max(num_class, num_target)
+    gbm = booster["model"]
+    trees = gbm["trees"]
+    for i, g in enumerate(gbm.get("tree_info", [])):
+        if int(g) != i % K:
+            raise ValueError(f"tree {i} has tree_info = {g}, not {i} % num_class ({K}); this output group "
+                             "layout is not supported")
+    for t in trees:
+        leaf_vec = str(t.get("tree_param", {}).get("size_leaf_vector", "")).strip()
+        if leaf_vec and _int_param("size_leaf_vector", leaf_vec) > 1:
+            raise ValueError(f"tree {t.get('id')} has vector leaves (size_leaf_vector = {leaf_vec}); only scalar "
+                             "leaves are supported")
+    npt = gbm.get("gbtree_model_param", {}).get("num_parallel_tree", "1")
+    if _int_param("num_parallel_tree", npt) != 1:
+        raise ValueError(f"num_parallel_tree = {npt} (random forest mode) is not supported")
+    outputs = _int_param("num_class", objective.get("softmax_multiclass_param", {}).get("num_class", K)) \
+        if multi else 1
+    if K != outputs or (multi and K < 2):
+        raise ValueError(f"num_class = {K} is inconsistent with objective {obj}")
+    F = _int_param("num_feature", lp["num_feature"])
+    margins = _base_scores(lp["base_score"], multi)
+    if multi:
+        margins = margins * K if len(margins) == 1 else margins  # an old scalar: K copies
+        if len(margins) != K:
+            raise ValueError(f"base_score has {len(margins)} values, but num_class = {K}")
+    spw = float(objective.get("reg_loss_param", {}).get("scale_pos_weight", "1"))
+    ftypes = learner.get("feature_types") or []
+    if "c" in ftypes and len(ftypes) != F:
+        raise ValueError(f"feature_types has {len(ftypes)} entries, but the model has {F} features")
+    cols = {k: [] for k in ("left", "right", "feat", "cond", "dl", "leaf", "gain", "hess", "cat", "coff", "clen")}
+    words: list = []
+    off = [0]
+    for ti, t in enumerate(trees):
+        tid = t.get("id", ti)
+        n = len(t["left_children"])
+        if n == 0:
+            raise ValueError(f"tree {tid} has no root node")
+        for name in ("right_children", "split_conditions", "split_indices", "default_left"):
+            if len(t[name]) != n:
+                raise ValueError(f"tree {tid}: {name} length {len(t[name])} does not match node count {n}")
+        split_type = [int(v) for v in t.get("split_type") or []]
+        if split_type and len(split_type) != n:
+            raise ValueError(f"tree {tid}: split_type length {len(split_type)} does not match node count {n}")
+        if any(v not in (0, 1) for v in split_type):
+            raise ValueError(f"tree {tid}: unknown split_type (0 = numerical, 1 = categorical)")
+        split_type = split_type or [0] * n
+        nodes, segs, sizes = (t.get(k, []) for k in ("categories_nodes", "categories_segments", "categories_sizes"))
+        if not len(nodes) == len(segs) == len(sizes):
+            raise ValueError(f"tree {tid}: categories_nodes / segments / sizes have different lengths")
+        categories = t.get("categories", [])
+        cats_of: dict = {}
+        for node, seg, size in zip(nodes, segs, sizes):
+            node, seg, size = int(node), int(seg), int(size)
+            if seg < 0 or size < 0 or seg + size > len(categories):
+                raise ValueError(f"tree {tid}: category segment [{seg}, +{size}) is out of bounds, categories has "
+                                 f"{len(categories)} entries")
+            if not 0 <= node < n or split_type[node] != 1:
+                raise ValueError(f"tree {tid}: categories_nodes contains {node}, which is not a categorical split "
+                                 "node")
+            cs = [int(c) for c in categories[seg:seg + size]]
+            if any(c < 0 for c in cs):
+                raise ValueError(f"tree {tid}: node {node} contains a negative category value")
+            if any(c >= 1 << 24 for c in cs):
+                raise ValueError(f"tree {tid}: node {node} contains a category value above 2^24")
+            if node in cats_of:
+                raise ValueError(f"tree {tid}: node {node} appears more than once in categories_nodes")
+            cats_of[node] = cs
+        gains, hesses = t.get("loss_changes", []), t.get("sum_hessian", [])
+        for i in range(n):
+            left = int(t["left_children"][i])
+            is_cat = split_type[i] == 1
+            if is_cat and i not in cats_of:
+                raise ValueError(f"tree {tid}: node {i} is a categorical split but has no category segment")
+            cols["left"].append(left)
+            cols["right"].append(int(t["right_children"][i]))
+            cols["feat"].append(int(t["split_indices"][i]))
+            cols["cond"].append(float(t["split_conditions"][i]))
+            cols["dl"].append(int(bool(t["default_left"][i])))
+            cols["leaf"].append(float(t["split_conditions"][i]) if left < 0 else 0.0)  # leaves live in split_conditions
+            cols["gain"].append(float(gains[i]) if i < len(gains) else 0.0)
+            cols["hess"].append(float(hesses[i]) if i < len(hesses) else 0.0)
+            cols["cat"].append(int(is_cat))
+            cols["coff"].append(len(words))
+            w = []
+            if is_cat:
+                cs = cats_of[i]
+                w = [0] * ((max(cs) >> 5) + 1 if cs else 0)
+                for c in cs:
+                    w[c >> 5] |= 1 << (c & 31)
+            words.extend(w)
+            cols["clen"].append(len(w))
+        off.append(off[-1] + n)
+    dt = {"left": np.int32, "right": np.int32, "feat": np.uint32, "cond": np.float32, "dl": np.uint8,
+          "leaf": np.float32, "gain": np.float32, "hess": np.float32, "cat": np.uint8, "coff": np.uint32,
+          "clen": np.uint32}
+    out = {k: np.array(v, dt[k]) for k, v in cols.items()}
+    out.update(F=F, objective=obj, K=K if multi else 0, margins=margins, spw=spw, off=np.array(off, np.uint32),
+               words=np.array(words if words else [0], np.uint32), n_words=len(words),
+               class_margins=np.array(margins, np.float32) if multi else None,
+               ftypes=np.array([v == "c" for v in ftypes], np.uint8) if "c" in ftypes else None)
+    return out
+
+
 def _err() -> str:
     return (lib().fb_last_error() or b"").decode()
 
@@ -455,100 +602,37 @@ class Model:
     @staticmethod
     def load_model(source: "str | os.PathLike | bytes", device=None) -> "Model":
         """A model from XGBoost-compatible JSON: a path or the JSON bytes (the
-        reference's ``Model.load_model``, src/model/tree.rs:760-960).  Models
+        reference's ``Model.load_model``, src/model/tree.rs:754-1460).  Models
         of this engine and XGBoost models of its objectives (reg:squarederror,
         binary:logistic, multi:softprob, multi:softmax) load; ``save_model`` of
-        the result writes the same JSON back."""
+        the result writes the same JSON back.  What the reference rejects is
+        rejected here with ValueError: another booster, forests, multi-target
+        models and vector leaves, a num_class that disagrees with the
+        objective, trees out of the t % num_class order, malformed arrays or
+        category segments, and anything that is not a tree (checked by
+        ``fb_model_create``)."""
         if isinstance(source, (bytes, bytearray)):
             doc = json.loads(source)
         else:
             with open(os.fspath(source), "rb") as f:
                 doc = json.load(f)
-        learner = doc["learner"]
-        obj = learner["objective"]["name"]
-        if obj not in _OBJECTIVES:
-            raise ValueError(f"objective {obj!r} is not supported on this engine; supported objectives: "
-                             f"{', '.join(_OBJECTIVES)}")
-        lp = learner["learner_model_param"]
-        F = int(lp["num_feature"])
-        raw = str(lp["base_score"]).strip()
-        margins = [np.float32(float(v)) for v in raw.strip("[]").split(",") if v.strip()] if raw.startswith("[") \
-            else [np.float32(float(raw))]
-        K = int(lp.get("num_class", "0") or 0)
-        multi = obj.startswith("multi:")
-        if multi and (K < 2 or len(margins) != K):
-            raise ValueError(f"{obj} model with num_class {K} and {len(margins)} base margins")
-        spw = float(learner["objective"].get("reg_loss_param", {}).get("scale_pos_weight", "1"))
-        ftypes = learner.get("feature_types") or []
-        if ftypes and len(ftypes) != F:
-            raise ValueError(f"feature_types has {len(ftypes)} entries, the model has {F} features")
-        gbm = learner["gradient_booster"]["model"]
-        trees = gbm["trees"]
-        info = gbm.get("tree_info", [0] * len(trees))
-        k_out = K if multi else 1
-        if any(int(c) != t % k_out for t, c in enumerate(info)):
-            raise ValueError("tree_info must assign tree t to output t % num_class")
-        off = [0]
-        cols = {k: [] for k in ("left", "right", "feat", "cond", "dl", "leaf", "gain", "hess", "cat", "coff", "clen")}
-        words: list[int] = []
-        for t in trees:
-            n = len(t["left_children"])
-            cats_of = {}
-            for pos, node in enumerate(t.get("categories_nodes", [])):
-                seg, size = t["categories_segments"][pos], t["categories_sizes"][pos]
-                cats_of[int(node)] = [int(c) for c in t["categories"][seg:seg + size]]
-            split_type = t.get("split_type", [0] * n)
-            for i in range(n):
-                cols["left"].append(int(t["left_children"][i]))
-                cols["right"].append(int(t["right_children"][i]))
-                cols["feat"].append(int(t["split_indices"][i]))
-                cols["cond"].append(float(t["split_conditions"][i]))
-                cols["dl"].append(int(bool(t["default_left"][i])))
-                cols["leaf"].append(float(t["base_weights"][i]) if int(t["left_children"][i]) >= 0
-                                    else float(t["split_conditions"][i]))
-                cols["gain"].append(float(t["loss_changes"][i]))
-                cols["hess"].append(float(t["sum_hessian"][i]))
-                is_cat = int(split_type[i]) == 1
-                cols["cat"].append(int(is_cat))
-                cols["coff"].append(len(words))
-                if is_cat:
-                    cs = cats_of.get(i, [])
-                    w = [0] * ((max(cs) >> 5) + 1 if cs else 0)
-                    for c in cs:
-                        w[c >> 5] |= 1 << (c & 31)
-                    words.extend(w)
-                    cols["clen"].append(len(w))
-                else:
-                    cols["clen"].append(0)
-            off.append(off[-1] + n)
-        arr = {
-            "left": np.array(cols["left"], np.int32), "right": np.array(cols["right"], np.int32),
-            "feat": np.array(cols["feat"], np.uint32), "cond": np.array(cols["cond"], np.float32),
-            "dl": np.array(cols["dl"], np.uint8), "leaf": np.array(cols["leaf"], np.float32),
-            "gain": np.array(cols["gain"], np.float32), "hess": np.array(cols["hess"], np.float32),
-            "cat": np.array(cols["cat"], np.uint8), "coff": np.array(cols["coff"], np.uint32),
-            "clen": np.array(cols["clen"], np.uint32),
-        }
-        off_a = np.array(off, np.uint32)
-        wa = np.array(words if words else [0], np.uint32)
-        cm = np.array(margins, np.float32) if multi else None
-        ft = np.array([t == "c" for t in ftypes], np.uint8) if ftypes else None
-        h = lib().fb_model_create(F, _OBJECTIVES[obj], float(margins[0]), spw, K if multi else 0,
-                                  _lib.ptr(cm, C.c_float), _lib.ptr(ft, C.c_uint8), len(trees),
-                                  _lib.ptr(off_a, C.c_uint32), _lib.ptr(arr["left"], C.c_int32),
-                                  _lib.ptr(arr["right"], C.c_int32), _lib.ptr(arr["feat"], C.c_uint32),
-                                  _lib.ptr(arr["cond"], C.c_float), _lib.ptr(arr["dl"], C.c_uint8),
-                                  _lib.ptr(arr["leaf"], C.c_float), _lib.ptr(arr["gain"], C.c_float),
-                                  _lib.ptr(arr["hess"], C.c_float), _lib.ptr(arr["cat"], C.c_uint8),
-                                  _lib.ptr(arr["coff"], C.c_uint32), _lib.ptr(arr["clen"], C.c_uint32),
-                                  _lib.ptr(wa, C.c_uint32))
+        a = _parse_xgb_model(doc)
+        h = lib().fb_model_create(a["F"], _OBJECTIVES[a["objective"]], float(a["margins"][0]), a["spw"], a["K"],
+                                  _lib.ptr(a["class_margins"], C.c_float), _lib.ptr(a["ftypes"], C.c_uint8),
+                                  len(a["off"]) - 1, _lib.ptr(a["off"], C.c_uint32), _lib.ptr(a["left"], C.c_int32),
+                                  _lib.ptr(a["right"], C.c_int32), _lib.ptr(a["feat"], C.c_uint32),
+                                  _lib.ptr(a["cond"], C.c_float), _lib.ptr(a["dl"], C.c_uint8),
+                                  _lib.ptr(a["leaf"], C.c_float), _lib.ptr(a["gain"], C.c_float),
+                                  _lib.ptr(a["hess"], C.c_float), _lib.ptr(a["cat"], C.c_uint8),
+                                  _lib.ptr(a["coff"], C.c_uint32), _lib.ptr(a["clen"], C.c_uint32),
+                                  _lib.ptr(a["words"], C.c_uint32), a["n_words"])
         if not h:
             raise ValueError(_err())
-        params = {"objective": obj, "num_class": K if multi else 0, "missing": float("nan")}
+        params = {"objective": a["objective"], "num_class": a["K"], "missing": float("nan")}
         if device is not None:
             params["device"] = device
         m = Model(h, params)
-        m.feature_names = list(learner.get("feature_names") or []) or None
+        m.feature_names = list(doc["learner"].get("feature_names") or []) or None
         return m
 
     def save_model(self, path: str | os.PathLike) -> None:

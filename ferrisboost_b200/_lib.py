@@ -149,7 +149,7 @@ SIGNATURES = {
     "fb_model_json": (C.c_int64, [P, C.c_char_p, C.c_int64]),
     "fb_model_tree": (C.c_int64, [P, C.c_uint32, i32p, i32p, u32p, f32p, u8p, f32p, u8p, f32p, f32p, u32p]),
     "fb_model_create": (P, [C.c_uint32, C.c_int32, C.c_float, C.c_float, C.c_uint32, f32p, u8p, C.c_uint32, u32p,
-                            i32p, i32p, u32p, f32p, u8p, f32p, f32p, f32p, u8p, u32p, u32p, u32p]),
+                            i32p, i32p, u32p, f32p, u8p, f32p, f32p, f32p, u8p, u32p, u32p, u32p, C.c_uint64]),
     "fb_model_predict": (C.c_int32, [P, f32p, C.c_uint64, f32p, C.c_int32]),
     "fb_model_num_outputs": (C.c_uint32, [P]),
     "fb_model_transform": (C.c_int32, [P, f32p, C.c_uint64, f32p]),

@@ -1382,7 +1382,7 @@ fb_model* fb_model_create(uint32_t n_features, int32_t objective, float base_sco
                           uint32_t n_trees, const uint32_t* tree_off, const int32_t* left, const int32_t* right,
                           const uint32_t* feat, const float* cond, const uint8_t* default_left, const float* leaf,
                           const float* gain, const float* hess, const uint8_t* is_cat, const uint32_t* cat_off,
-                          const uint32_t* cat_len, const uint32_t* cat_words) {
+                          const uint32_t* cat_len, const uint32_t* cat_words, uint64_t n_cat_words) {
     return fbe::guarded([&]() -> fb_model* {
         if (n_features == 0) throw fbe::InputError("a model needs at least one feature");
         if (objective < 0 || objective > 3) throw fbe::InputError("unsupported objective code");
@@ -1410,6 +1410,10 @@ fb_model* fb_model_create(uint32_t n_features, int32_t objective, float base_sco
             const int32_t nn = (int32_t)(e - b);
             auto& N = m->trees[t].nodes;
             N.resize(nn);
+            std::vector<uint8_t> parents(nn, 0);
+            auto bad = [&](int32_t i, const std::string& what) {
+                return fbe::InputError("tree " + std::to_string(t) + " node " + std::to_string(i) + " " + what);
+            };
             for (int32_t i = 0; i < nn; i++) {
                 const uint32_t g = b + (uint32_t)i;
                 fbe::Node& nd = N[i];
@@ -1417,13 +1421,17 @@ fb_model* fb_model_create(uint32_t n_features, int32_t objective, float base_sco
                 nd.hess = hess ? hess[g] : 0.0f;
                 nd.leaf = leaf[g];
                 nd.default_left = default_left[g] != 0;
-                if (left[g] < 0) {
+                if (left[g] < 0) {  // tree.rs:1363-1374: a leaf has no child on either side
+                    if (right[g] >= 0) throw bad(i, "has only one child");
                     nd.is_leaf = true;
                     continue;
                 }
-                if (left[g] >= nn || right[g] < 0 || right[g] >= nn || left[g] == i || right[g] == i)
-                    throw fbe::InputError("tree " + std::to_string(t) + " node " + std::to_string(i) +
-                                          " has a child outside the tree");
+                // tree.rs:1375-1399: children inside the tree, distinct, each with one parent
+                if (right[g] < 0) throw bad(i, "has only one child");
+                if (left[g] >= nn || right[g] >= nn || left[g] == right[g])
+                    throw bad(i, "has invalid child indices (a child outside the tree, or the same child twice)");
+                for (int32_t c : {left[g], right[g]})
+                    if (++parents[c] > 1) throw bad(c, "has more than one parent");
                 if (feat[g] >= n_features)
                     throw fbe::InputError("tree " + std::to_string(t) + " splits on feature " +
                                           std::to_string(feat[g]) + ", the model has " + std::to_string(n_features));
@@ -1434,10 +1442,25 @@ fb_model* fb_model_create(uint32_t n_features, int32_t objective, float base_sco
                 nd.cond = cond[g];
                 nd.is_cat = is_cat && is_cat[g];
                 if (nd.is_cat) {
+                    if ((uint64_t)cat_off[g] + cat_len[g] > n_cat_words) throw bad(i, "has a category set out of range");
                     nd.cats.assign(cat_words + cat_off[g], cat_words + cat_off[g] + cat_len[g]);
                     while (!nd.cats.empty() && nd.cats.back() == 0) nd.cats.pop_back();
                 }
             }
+            // tree.rs:1418-1447: the root has no parent, and a walk from it
+            // meets every node exactly once (no cycle, nothing unreachable)
+            if (parents[0]) throw bad(0, "(the root) is a child of another node");
+            std::vector<uint8_t> seen(nn, 0);
+            std::vector<int32_t> stack{0};
+            while (!stack.empty()) {
+                const int32_t i = stack.back();
+                stack.pop_back();
+                if (seen[i]) throw fbe::InputError("tree " + std::to_string(t) + " contains a cycle");
+                seen[i] = 1;
+                if (!N[i].is_leaf) { stack.push_back(N[i].left); stack.push_back(N[i].right); }
+            }
+            for (int32_t i = 0; i < nn; i++)
+                if (!seen[i]) throw bad(i, "is unreachable from the root");
         }
         return m.release();
     }, nullptr);

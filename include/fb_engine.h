@@ -167,16 +167,19 @@ fb_model* fb_train(const float* X, uint64_t n, uint32_t F, const float* y, const
  * (left < 0: a leaf, whose value is leaf[i]); a split's condition is cond[i]
  * and its default direction default_left[i]; a categorical split (is_cat[i])
  * sends the categories of its bitset cat_words[cat_off[i] .. + cat_len[i]]
- * right.  objective: 0 reg:squarederror, 1 binary:logistic, 2
- * multi:softprob, 3 multi:softmax (num_class >= 2 and K class_margins; tree t
- * belongs to class t % K).  feature_types may be NULL (all numeric).  Returns
- * NULL with fb_last_error on an inconsistent model. */
+ * right (n_cat_words words in all).  objective: 0 reg:squarederror, 1
+ * binary:logistic, 2 multi:softprob, 3 multi:softmax (num_class >= 2 and K
+ * class_margins; tree t belongs to class t % K).  feature_types may be NULL
+ * (all numeric).  Returns NULL with fb_last_error on an inconsistent model:
+ * besides ranges, every tree must be a tree (tree.rs:1363-1447): a node has
+ * both children or none, each node at most one parent, the root none, and
+ * every node is reached from the root exactly once. */
 fb_model* fb_model_create(uint32_t n_features, int32_t objective, float base_score, float scale_pos_weight,
                           uint32_t num_class, const float* class_margins, const uint8_t* feature_types,
                           uint32_t n_trees, const uint32_t* tree_off, const int32_t* left, const int32_t* right,
                           const uint32_t* feat, const float* cond, const uint8_t* default_left, const float* leaf,
                           const float* gain, const float* hess, const uint8_t* is_cat, const uint32_t* cat_off,
-                          const uint32_t* cat_len, const uint32_t* cat_words);
+                          const uint32_t* cat_len, const uint32_t* cat_words, uint64_t n_cat_words);
 void fb_model_free(fb_model* m);
 uint32_t fb_model_num_trees(const fb_model* m);
 uint32_t fb_model_num_features(const fb_model* m);
