@@ -254,6 +254,7 @@ def _normalize_params(params: Mapping[str, Any], num_boost_round: int) -> dict[s
     for key in ("max_depth", "max_leaves", "max_bin", "nthread", "seed", "max_cat_to_onehot", "max_cat_threshold",
                 "num_class"):
         out[key] = int(out[key])
+    out["missing"] = _validate_missing(out["missing"])
     if out["objective"].startswith("multi:") and out["num_class"] < 2:  # objective.rs:331-337
         raise ValueError(f"{out['objective']} requires num_class >= 2, got {out['num_class']}")
     if out["max_leaves"] < 0:
@@ -333,10 +334,28 @@ def _fb_params(p: Mapping[str, Any]) -> _lib.FbParams:
     return fp
 
 
+def _validate_missing(missing: Any) -> float:
+    """src/source/mod.rs:218-235 validate_missing: NaN (no sentinel) or a
+    finite float32 other than f32::MAX.  +-inf and f32::MAX never occur in
+    features (they are rejected there), so a sentinel equal to one of them, or
+    one that overflows float32, is refused."""
+    m = float(missing)
+    if math.isnan(m):
+        return m
+    with np.errstate(over="ignore"):
+        narrowed = np.float32(m)
+    if not np.isfinite(narrowed) or narrowed == np.finfo(np.float32).max:
+        raise ValueError(f"missing={missing} is not allowed: it must be NaN or a finite float32 value (+/-inf and "
+                         "f32::MAX are reserved and rejected in features, so they cannot be the missing marker; "
+                         "pick a different sentinel)")
+    return float(narrowed)
+
+
 def _as_matrix(x: Any, missing: float = float("nan")) -> np.ndarray:
     a = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
     if a.ndim != 2:
         raise ValueError(f"data must be a 2-D array, got shape {a.shape}")
+    missing = _validate_missing(missing)
     if not math.isnan(missing):
         a = np.where(a == np.float32(missing), np.float32("nan"), a).astype(np.float32)
     return a
@@ -658,7 +677,7 @@ class Model:
 
     def _rows(self, data: Any) -> np.ndarray:
         """Row-major f32 rows for the prediction entry points."""
-        missing = self.params.get("missing", float("nan"))
+        missing = _validate_missing(self.params.get("missing", float("nan")))
         specs = columnar.path_specs(data)
         table = None if specs is not None else columnar.arrow_table(data)
         if specs is None and table is None:

@@ -58,6 +58,23 @@ def test_unknown_and_cpu_parameters_raise():
     assert p["eta"] == 0.1 and p["lambda"] == 2.0
 
 
+def test_missing_sentinel_rules():
+    """src/source/mod.rs:449-475: NaN and finite float32 sentinels are taken
+    (f32::MIN too); +-inf, f32::MAX and values that overflow float32 are
+    refused, in training parameters and in host data."""
+    import ferrisboost_b200 as fb
+    assert np.isnan(fb._normalize_params({}, 1)["missing"])
+    for ok in (-999.0, 0.0, float(np.finfo(np.float32).min)):
+        assert fb._normalize_params({"missing": ok}, 1)["missing"] == np.float32(ok)
+    for bad in (float("inf"), float("-inf"), float(np.finfo(np.float32).max), 1e39, -1e39):
+        with pytest.raises(ValueError, match="missing"):
+            fb._normalize_params({"missing": bad}, 1)
+        with pytest.raises(ValueError, match="missing"):
+            fb._as_matrix(np.zeros((2, 2)), bad)
+    got = fb._as_matrix(np.array([[1.0, -999.0], [np.nan, 2.0]]), -999.0)
+    assert np.isnan(got[0, 1]) and np.isnan(got[1, 0]) and got[0, 0] == 1.0 and got[1, 1] == 2.0
+
+
 @pytest.mark.parametrize("max_bin", [16, 255, 256, 1024])
 def test_dataset_cuts_and_bins_match_oracle(oracle, max_bin):
     import ferrisboost_b200 as fb
