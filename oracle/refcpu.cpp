@@ -1882,4 +1882,15 @@ void rc_best_split(const int64_t* hist, uint32_t F, const uint32_t* feat_offsets
     for (size_t i = 0; i < c.cats.size() && i < 8; i++) out->cats[i] = c.cats[i];
 }
 
+uint32_t rc_sample_features(uint32_t nf, float rate, uint64_t seed, uint64_t round, uint32_t* out) {
+    std::vector<uint32_t> ids = sample_features(nf, rate, seed, round);
+    std::copy(ids.begin(), ids.end(), out);
+    return (uint32_t)ids.size();
+}
+
+void rc_rows_selected(uint64_t n, float rate, uint64_t seed, uint64_t tree, uint8_t* out) {
+    const uint64_t th = threshold_for(rate);
+    for (uint64_t r = 0; r < n; r++) out[r] = th == UINT64_MAX || (row_hash(r, seed, tree) >> 11) < th;
+}
+
 }  // extern "C"

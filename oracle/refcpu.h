@@ -126,6 +126,12 @@ void rc_best_split(const int64_t* hist, uint32_t F, const uint32_t* feat_offsets
                    const int64_t* node_sum, const double* scales,
                    const rc_params* p, float lower, float upper,
                    const uint8_t* enabled, rc_split* out);
+/* colsample_bytree of one tree (data/colsample.rs:29-104): the sampled
+ * feature ids, ascending, into out (nf entries of room); returns how many. */
+uint32_t rc_sample_features(uint32_t nf, float rate, uint64_t seed, uint64_t round, uint32_t* out);
+/* subsample of one tree (data/subsample.rs:45-78): out[r] = 1 when row r
+ * keeps its gradient. */
+void rc_rows_selected(uint64_t n, float rate, uint64_t seed, uint64_t tree, uint8_t* out);
 
 #ifdef __cplusplus
 }

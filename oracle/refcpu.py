@@ -92,6 +92,9 @@ class RefCPU:
                                       C.POINTER(C.c_int64), C.POINTER(C.c_double), C.POINTER(rc_params),
                                       C.c_float, C.c_float, C.POINTER(C.c_uint8), C.POINTER(rc_split)]
         lib.rc_default_params.argtypes = [C.POINTER(rc_params)]
+        lib.rc_sample_features.argtypes = [C.c_uint32, C.c_float, C.c_uint64, C.c_uint64, C.POINTER(C.c_uint32)]
+        lib.rc_sample_features.restype = C.c_uint32
+        lib.rc_rows_selected.argtypes = [C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.POINTER(C.c_uint8)]
         self.lib = lib
 
     # ---------------------------------------------------------------- params
@@ -212,6 +215,16 @@ class RefCPU:
                          _ptr(g, C.c_int64), _ptr(r, C.c_uint32), 0 if r is None else r.shape[0],
                          _ptr(out, C.c_int64))
         return out
+
+    def sample_features(self, nf, rate, seed, round_):
+        out = np.zeros(max(nf, 1), dtype=np.uint32)
+        k = self.lib.rc_sample_features(nf, rate, seed, round_, _ptr(out, C.c_uint32))
+        return out[:k].copy()
+
+    def rows_selected(self, n, rate, seed, tree):
+        out = np.zeros(n, dtype=np.uint8)
+        self.lib.rc_rows_selected(n, rate, seed, tree, _ptr(out, C.c_uint8))
+        return out.astype(bool)
 
     def best_split(self, hist, feat_offsets, node_sum, scales, lower=-3.4028234663852886e38,
                    upper=3.4028234663852886e38, enabled=None, **kw):
