@@ -3,8 +3,10 @@ CPU oracle's histogram and quantizer: a per-row scalar reference, row
 subsets, row order, missing rows kept out of every bin but inside the node
 sum, sibling subtraction, 8- and 16-bit codes alike, and fixed point that
 neither overflows nor loses the signal when gradients grow or shrink by six
-orders of magnitude.  The device histogram kernels equal the oracle's bit for
-bit (the GPU kernel tests), so these properties hold for them too."""
+orders of magnitude; and the quantizer's known answers and its refusal of
+non-finite pairs (tests/numerical_guards.rs).  The device histogram and
+quantize kernels equal the oracle's bit for bit (the GPU kernel tests), so
+these properties hold for them too."""
 import numpy as np
 import pytest
 
@@ -123,3 +125,26 @@ def test_extreme_gradient_magnitudes_neither_overflow_nor_lose_the_signal(oracle
     tol = 1e-9 * max(abs(want_h), 1e-30 * mult)
     assert abs(grad - want_g) <= max(tol, 1e-9 * abs(want_g)), (mult, grad, want_g)
     assert abs(hess - want_h) <= max(tol, 1e-9 * abs(want_h)), (mult, hess, want_h)
+
+
+def test_quantizer_known_answers(oracle):
+    """tests/numerical_guards.rs:119-149: scale = 2^floor(log2((2^62 / n_rows)
+    / max|v|)) per channel; with 4 rows, max|g| = 2 and max|h| = 0.25 that is
+    2^59 and 2^62, and the fixed-point values are exact."""
+    g = np.array([[1.5, 0.125], [-2.0, 0.25]], np.float32)
+    scales = oracle.quantizer(g, 4)
+    assert scales[0] == 2.0 ** 59 and scales[1] == 2.0 ** 62
+    fixed, _ = oracle.to_fixed(g, scales)
+    assert fixed.tolist() == [[864_691_128_455_135_232, 576_460_752_303_423_488],
+                              [-1_152_921_504_606_846_976, 1_152_921_504_606_846_976]]
+    tiny = np.array([[np.finfo(np.float32).tiny, np.finfo(np.float32).tiny]], np.float32)
+    s = oracle.quantizer(tiny, 1)
+    assert np.all(np.isfinite(s)) and np.all(s > 0)
+
+
+@pytest.mark.parametrize("bad", [np.nan, np.inf, -np.inf])
+def test_quantizer_rejects_nonfinite_pairs(oracle, bad):
+    """tests/numerical_guards.rs:77-101."""
+    for pair in ([bad, 1.0], [1.0, bad]):
+        with pytest.raises(ValueError, match="non-finite"):
+            oracle.quantizer(np.array([pair], np.float32), 1)
