@@ -81,3 +81,16 @@ def test_exact_f32_max_is_rejected_by_dense_entry_points():
     given = (np.array([0.0], np.float32), np.array([0, 1], np.uint32))
     with pytest.raises(ValueError, match="f32::MAX"):
         fb.Dataset(X, max_bin=1, cuts=given)
+
+
+def test_find_bin_does_not_wrap_above_255_bins(oracle):
+    """columns.rs width_grouping_tests find_bin_does_not_wrap_above_255_bins:
+    599 cuts (600 bins, 16-bit codes); 0.5, 300 and 1e9 fall in bins 0, 300
+    and 599, with the cuts given, in the engine and the oracle."""
+    cuts = np.arange(1, 600, dtype=np.float32)
+    off = np.array([0, 599], np.uint32)
+    X = np.array([[0.5], [300.0], [1e9], [np.nan]], np.float32)
+    ds = fb.Dataset(X, cuts=(cuts, off))
+    col = ds.column(0)
+    assert col[:3].tolist() == [0, 300, 599]
+    assert np.array_equal(col, oracle.quantize(X, cuts, off)[0])
