@@ -1,0 +1,125 @@
+"""The reference's training unit tests (src/training/mod.rs tests) on the
+CPU oracle and the engine's host base score: the default base score is the
+label mean (f64, row order) or the weighted mean, 0.5 when every weight is
+zero, and 1 for all-positive logistic labels with a finite margin; a
+root-only round feeds the next round's gradients; leaf Hessians sum back to
+the root; trees keep max_depth; nothing to learn gives a single leaf; and
+training is reproducible."""
+import json
+
+import numpy as np
+import pytest
+
+import ferrisboost_b200 as fb
+from ferrisboost_b200 import _lib
+
+
+def _learner(ref):
+    return json.loads(ref.json())["learner"]
+
+
+def _base_score(ref):
+    return np.float32(float(_learner(ref)["learner_model_param"]["base_score"]))
+
+
+def _trees(ref):
+    return _learner(ref)["gradient_booster"]["model"]["trees"]
+
+
+def _label_mean(y, w=None):
+    """objective.rs:41-61 FitInterceptGlmLike: sum of y/n (or y/sw * w) in
+    f64, row order, rounded to f32; 0.5 when the weights sum to zero."""
+    if w is None:
+        acc = 0.0
+        for v in y:
+            acc += float(v) / len(y)
+        return np.float32(acc)
+    sw = 0.0
+    for v in w:
+        sw += float(v)
+    if sw <= 0.0:
+        return np.float32(0.5)
+    acc = 0.0
+    for v, wi in zip(y, w):
+        acc += float(v) / sw * float(wi)
+    return np.float32(acc)
+
+
+def _engine_mean(y, w=None):
+    y = np.ascontiguousarray(y, np.float32)
+    w = None if w is None else np.ascontiguousarray(w, np.float32)
+    return np.float32(fb.lib().fb_label_mean(_lib.ptr(y, _lib.C.c_float), _lib.ptr(w, _lib.C.c_float), len(y)))
+
+
+@pytest.mark.parametrize("objective", ["reg:squarederror", "binary:logistic"])
+def test_default_base_score_is_the_weighted_label_mean(oracle, objective):
+    """mod.rs:5597-5649."""
+    i = np.arange(40)
+    X = (i % 7).astype(np.float32)[:, None]
+    y = (i % 3 == 0).astype(np.float32)
+    w = np.where(i % 3 == 0, 3.0, 0.5 + (i % 4)).astype(np.float32)
+    m = oracle.train(X, y, objective=objective, max_depth=2, n_rounds=1, max_bin=255)
+    assert _base_score(m) == _label_mean(y) == _engine_mean(y)
+    mw = oracle.train(X, y, w, objective=objective, max_depth=2, n_rounds=1, max_bin=255)
+    assert _base_score(mw) == _label_mean(y, w) == _engine_mean(y, w)
+    assert _base_score(mw) != _label_mean(y)
+    assert _label_mean(y, np.zeros(40, np.float32)) == _engine_mean(y, np.zeros(40, np.float32)) == 0.5
+
+
+def test_all_positive_logistic_labels_give_a_clamped_finite_margin(oracle):
+    X = (np.arange(40) % 7).astype(np.float32)[:, None]
+    m = oracle.train(X, np.ones(40, np.float32), objective="binary:logistic", max_depth=2, n_rounds=1)
+    assert _base_score(m) == 1.0
+    assert np.isfinite(m.predict_margin(X)).all()
+
+
+def test_root_only_tree_updates_the_next_round(oracle):
+    """mod.rs:5651-5674: with max_depth 0 the root is the leaf; round two
+    sees round one's predictions, so its leaf is smaller but still positive."""
+    X = np.zeros((8, 1), np.float32)
+    m = oracle.train(X, np.ones(8, np.float32), objective="reg:squarederror", max_depth=0, n_rounds=2, eta=0.3,
+                     base_score=0.5)
+    t0, t1 = _trees(m)
+    first, second = t0["split_conditions"][0], t1["split_conditions"][0]
+    assert 0.0 < second < first
+
+
+def _step_data(n):
+    rng = np.random.default_rng(0)
+    X = rng.uniform(0, 1, (n, 3)).astype(np.float32)
+    y = (X[:, 0] > 0.5).astype(np.float32)
+    return X, y
+
+
+def test_leaf_hessians_sum_back_to_the_root(oracle):
+    X, y = _step_data(100)
+    m = oracle.train(X, y, objective="binary:logistic", max_depth=4, n_rounds=3)
+    for k, t in enumerate(_trees(m)):
+        root = t["sum_hessian"][0]
+        leaves = sum(h for h, c in zip(t["sum_hessian"], t["left_children"]) if c == -1)
+        assert abs(leaves - root) < 1e-3 * max(root, 1.0), k
+
+
+def _depth(t, i=0):
+    if t["left_children"][i] == -1:
+        return 0
+    return 1 + max(_depth(t, t["left_children"][i]), _depth(t, t["right_children"][i]))
+
+
+def test_respects_max_depth(oracle):
+    X, y = _step_data(100)
+    for d in (0, 1, 2, 4):
+        m = oracle.train(X, y, objective="binary:logistic", max_depth=d, n_rounds=2)
+        assert all(_depth(t) <= d for t in _trees(m)), d
+
+
+def test_nothing_to_learn_gives_a_single_leaf(oracle):
+    X = np.random.default_rng(1).standard_normal((64, 3)).astype(np.float32)
+    m = oracle.train(X, np.full(64, 0.7, np.float32), objective="reg:squarederror", max_depth=4, n_rounds=2)
+    assert all(len(t["left_children"]) == 1 for t in _trees(m))
+
+
+def test_training_is_reproducible(oracle):
+    X, y = _step_data(500)
+    kw = dict(objective="binary:logistic", max_depth=4, n_rounds=4, subsample=0.7, colsample_bytree=0.67, seed=3)
+    assert oracle.train(X, y, **kw).json() == oracle.train(X, y, **kw).json()
