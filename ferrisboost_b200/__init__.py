@@ -118,6 +118,8 @@ def _parse_xgb_model(doc: Mapping) -> dict:
         raise ValueError(f"only gbtree is supported, this model is {booster.get('name')}")
     objective = learner["objective"]
     obj = objective["name"]
+    if obj == "reg:linear":  # objective.rs:144
+        obj = "reg:squarederror"
     if obj not in _OBJECTIVES:
         raise ValueError(f"objective {obj!r} is not supported on this engine; supported objectives: "
                          f"{', '.join(_OBJECTIVES)}")
@@ -244,6 +246,8 @@ def _normalize_params(params: Mapping[str, Any], num_boost_round: int) -> dict[s
             known = ", ".join(sorted(_DEFAULTS) + sorted(_ALIASES))
             raise ValueError(f"unknown parameter {key!r}; supported parameters: {known}")
         out[canon] = value
+    if out["objective"] == "reg:linear":  # objective.rs:144: XGBoost's old name of squared error
+        out["objective"] = "reg:squarederror"
     if out["objective"] not in _OBJECTIVES:
         raise ValueError(f"objective {out['objective']!r} is not supported on this engine; supported objectives: "
                          f"{', '.join(_OBJECTIVES)}")

@@ -56,6 +56,10 @@ def test_unknown_and_cpu_parameters_raise():
         fb._normalize_params({"max_depth": 15}, 10)
     p = fb._normalize_params({"learning_rate": 0.1, "reg_lambda": 2.0}, 5)
     assert p["eta"] == 0.1 and p["lambda"] == 2.0
+    # objective.rs:144 / :1346 names_round_trip: reg:linear is squared error
+    assert fb._normalize_params({"objective": "reg:linear"}, 1)["objective"] == "reg:squarederror"
+    with pytest.raises(ValueError, match="not supported"):
+        fb._normalize_params({"objective": "rank:bogus"}, 1)
 
 
 def test_missing_sentinel_rules():
