@@ -267,3 +267,18 @@ def test_loaded_models_predict_like_the_oracle(oracle):
     rows = np.array([[0.0, 2.0, 0.0], [0.0, np.nan, 0.0], [0.0, 9.0, 0.0], [0.0, 2.5, 0.0]], np.float32)
     got = xm.predict(rows, output_margin=True)
     assert np.array_equal(got, np.array([-0.3, -0.3, 0.15, 0.15], np.float32))
+
+
+@pytest.mark.parametrize("objective", ["binary:logistic", "reg:squarederror"])
+def test_transform_inverts_base_margin(objective):
+    """objective.rs:1348-1358 transform_inverts_base_margin: the engine's
+    base margin (logit for logistic, identity for squared error) maps back to
+    base_score within 1e-6."""
+    for bs in (0.1, 0.5, 0.9):
+        d = _xgb_dump()
+        d["learner"]["objective"]["name"] = objective
+        d["learner"]["learner_model_param"]["base_score"] = repr(bs)
+        m = fb.Model.load_model(json.dumps(d).encode())
+        margin = fb.lib().fb_model_base_margin(m._h)
+        back = 1.0 / (1.0 + np.exp(-np.float64(margin))) if objective == "binary:logistic" else margin
+        assert abs(back - bs) < 1e-6, (objective, bs, back)
