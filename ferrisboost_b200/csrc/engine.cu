@@ -32,6 +32,13 @@ namespace fbe {
 using fbg::InputError;
 thread_local std::string g_err;
 
+// Training features never hold +-inf or f32::MAX: f32::MAX is the upper split
+// sentinel (dense.rs:300) and infinities are refused like XGBoost refuses them
+// (python/mod.rs:4063-4073 reject_inf).  Prediction input may hold infinities.
+const char* const kReservedValue =
+    "features cannot be +-inf or the reserved f32::MAX, which marks missing-value split boundaries (use NaN for "
+    "missing values; rescale extreme values)";
+
 // ---------------------------------------------------------------- sketch
 // sketch.rs:28-435: log-structured merge of compressed weighted summaries.
 struct SEntry {
@@ -264,15 +271,15 @@ void build_blocks(Dataset& d, const fbg::HostMatrix& X, int nth) {
             const uint32_t miss = d.missing(f);
             for (uint64_t r = 0; r < d.n; r++) {
                 const float v = X.at(r, f);
-                if (v == std::numeric_limits<float>::max()) reserved = 1;
+                if (v == std::numeric_limits<float>::max() || std::isinf(v)) reserved = 1;
                 const uint32_t bin = std::isnan(v) ? miss : d.bin_of(f, v);
                 if (b.width == 2) reinterpret_cast<uint16_t*>(b.data.data())[(size_t)i * d.n + r] = (uint16_t)bin;
                 else b.data[(size_t)i * d.n + r] = (uint8_t)bin;
             }
         }
     }
-    if (reserved)  // dense.rs:300
-        throw InputError("feature contains f32::MAX, reserved for missing-value split boundaries; rescale this feature");
+    if (reserved)  // dense.rs:300; python/mod.rs:4063-4073 reject_inf
+        throw InputError(kReservedValue);
 }
 
 int threads(int32_t nthread) { return nthread > 0 ? nthread : omp_get_max_threads(); }
@@ -455,8 +462,8 @@ Dataset* dataset_on_device(const fbg::HostMatrix& X, uint64_t n, uint32_t F, uin
                                 d_off.as<uint32_t>(), d_cat.as<uint8_t>(), b.dev->as<uint8_t>(), b.stride);
     }
     phase("binning");
-    if (reserved)  // dense.rs:300
-        throw InputError("feature contains f32::MAX, reserved for missing-value split boundaries; rescale this feature");
+    if (reserved)  // dense.rs:300; python/mod.rs:4063-4073 reject_inf
+        throw InputError(kReservedValue);
     return d.release();
 }
 

@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(256) k_bin_block(const float* __restrict__ X, 
             const uint32_t i = lane + 32u * q;
             if (i >= nf) break;
             const float x = X[r * rs + fid[q] * cs];
-            if (x == FLT_MAX) res = 1;
+            if (x == FLT_MAX || isinf(x)) res = 1;
             uint32_t bin;
             if (isnan(x)) bin = miss;
             else if (iscat[q]) bin = (x >= 0.0f && x < (float)(nc[q] + 1)) ? (uint32_t)x : miss - 1;

@@ -50,8 +50,8 @@ class DeviceMatrix {
     // `dst` (stride bytes, zero padded) holds the bins of feats[0..n_feats)
     // at byte i x width.  Cuts are the dataset's flat cuts and F+1 offsets
     // (device copies); NaN -> the missing sentinel (255 / 65535), categorical
-    // codes -> their bin.  Returns true if any value of these features equals
-    // f32::MAX (reserved, dense.rs:300).
+    // codes -> their bin.  Returns true if any value of these features is
+    // +-inf or f32::MAX (reserved: dense.rs:300, python/mod.rs:4063 reject_inf).
     bool bin_block(const uint32_t* feats, uint32_t n_feats, uint32_t width, const float* d_cuts,
                    const uint32_t* d_offsets, const uint8_t* d_cat, uint8_t* dst, uint32_t stride);
     // Features holding at least one NaN (1) or none (0), F entries.

@@ -2,9 +2,9 @@
 oracle and the engine's host data path: a feature of one bin whose values
 sit next to f32::MAX (or at f32::MIN) still splits from its missing values,
 with the same gain, covers and leaf values; the engine bins such values as
-the oracle does; f32::MAX itself, reserved as the upper split sentinel, is
-refused by every dense entry point; the models load and write back byte for
-byte."""
+the oracle does; f32::MAX itself, reserved as the upper split sentinel, and
++-inf are refused by every dense entry point; the models load and write back
+byte for byte."""
 import json
 
 import numpy as np
@@ -81,6 +81,17 @@ def test_exact_f32_max_is_rejected_by_dense_entry_points():
     given = (np.array([0.0], np.float32), np.array([0, 1], np.uint32))
     with pytest.raises(ValueError, match="f32::MAX"):
         fb.Dataset(X, max_bin=1, cuts=given)
+
+
+def test_infinite_training_features_are_rejected():
+    """python/mod.rs:4063-4073 reject_inf: training data (and validation sets,
+    binned with given cuts) cannot hold +-inf; missing values are NaN."""
+    for v in (np.inf, -np.inf):
+        X = np.array([[1.0], [2.0], [v], [np.nan]], np.float32)
+        with pytest.raises(ValueError, match="inf"):
+            fb.Dataset(X, max_bin=4)
+        with pytest.raises(ValueError, match="inf"):
+            fb.Dataset(X, cuts=(np.array([1.5], np.float32), np.array([0, 1], np.uint32)))
 
 
 def test_find_bin_does_not_wrap_above_255_bins(oracle):

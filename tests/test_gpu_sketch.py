@@ -22,15 +22,15 @@ def _cases():
     # exact multiples of the chunk size and one past them
     for n in (4096, 4097, 8192, 3 * 4096, 3 * 4096 + 1, 1):
         out.append((f"n{n}", rng.standard_normal((n, 2)).astype(np.float32), 256, None))
-    # NaNs, all-NaN and constant columns, infinities, heavy ties
+    # NaNs, all-NaN and constant columns, extreme magnitudes, heavy ties
     X = rng.standard_normal((60_000, 7)).astype(np.float32)
     X[rng.random(60_000) < 0.3, 0] = np.nan
     X[:, 1] = np.nan
     X[:, 2] = 1.5
     X[:, 3] = np.round(X[:, 3] * 4) / 4                             # low cardinality: midpoints
     X[rng.random(60_000) < 0.5, 4] = 0.0                            # half the values tie
-    X[::97, 5] = np.inf
-    X[::89, 5] = -np.inf
+    X[::97, 5] = 1e30                                               # extreme finite magnitudes
+    X[::89, 5] = -1e30
     X[:, 6] = np.where(X[:, 6] > 0, -0.0, X[:, 6])                  # one signed zero, many times
     out.append(("edges", X, 64, None))
     out.append(("edges_mb256", X, 256, None))
@@ -99,6 +99,11 @@ def test_device_dataset_rejects_reserved_and_invalid_values():
     X[7, 1] = np.finfo(np.float32).max
     with pytest.raises(ValueError, match="f32::MAX"):
         fb.Dataset(X, device=0)
+    for v in (np.inf, -np.inf):  # python/mod.rs:4063-4073 reject_inf
+        Xi = np.zeros((100, 2), np.float32)
+        Xi[9, 0] = v
+        with pytest.raises(ValueError, match="inf"):
+            fb.Dataset(Xi, device=0)
     Xc = np.array([[0.0], [1.5]], dtype=np.float32)
     with pytest.raises(ValueError, match="invalid category"):
         fb.Dataset(Xc, feature_types=["c"], device=0)
