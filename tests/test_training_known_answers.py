@@ -123,3 +123,35 @@ def test_training_is_reproducible(oracle):
     X, y = _step_data(500)
     kw = dict(objective="binary:logistic", max_depth=4, n_rounds=4, subsample=0.7, colsample_bytree=0.67, seed=3)
     assert oracle.train(X, y, **kw).json() == oracle.train(X, y, **kw).json()
+
+
+def _weight_toy(n=400, m=5, seed=0):
+    """python/tests/test_weights.py toy: integer features, so dropping rows
+    or zeroing their weights leaves the bins unchanged."""
+    rng = np.random.default_rng(seed)
+    x = rng.integers(0, 8, size=(n, m)).astype(np.float32)
+    y = (x[:, 0] - x[:, 1] + rng.normal(0, 0.5, n) > 0).astype(np.float32)
+    w = rng.uniform(0.1, 3.0, n).astype(np.float32)
+    return x, y, w
+
+
+_WKW = dict(objective="binary:logistic", max_depth=3, eta=0.3, nthread=1, n_rounds=5)
+
+
+def test_all_ones_weight_is_byte_identical_and_weights_change_the_model(oracle):
+    """test_weights.py:34-46."""
+    x, y, w = _weight_toy()
+    plain = oracle.train(x, y, **_WKW).json()
+    assert oracle.train(x, y, np.ones(len(y), np.float32), **_WKW).json() == plain
+    assert oracle.train(x, y, w, **_WKW).json() != plain
+
+
+def test_zero_weight_rows_match_dropping_them(oracle):
+    """test_weights.py:48-55: predictions equal (here the models are equal
+    byte for byte too)."""
+    x, y, w = _weight_toy()
+    keep = np.arange(len(y)) % 3 != 0
+    zeroed = oracle.train(x, y, np.where(keep, w, 0.0).astype(np.float32), **_WKW)
+    dropped = oracle.train(x[keep], y[keep], w[keep], **_WKW)
+    assert np.array_equal(zeroed.predict_margin(x), dropped.predict_margin(x))
+    assert zeroed.json() == dropped.json()
