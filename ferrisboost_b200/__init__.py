@@ -300,14 +300,66 @@ def _normalize_params(params: Mapping[str, Any], num_boost_round: int) -> dict[s
     for key in ("max_cat_to_onehot", "max_cat_threshold"):
         if out[key] < 1:
             raise ValueError(f"{key} must be >= 1, got {out[key]}")
-    mc = out["monotone_constraints"]
-    if isinstance(mc, str):
-        mc = [int(t) for t in mc.strip("()[] ").split(",") if t.strip()]
-    if mc is not None:
-        mc = [int(np.sign(v)) for v in mc]
-    out["monotone_constraints"] = mc
+    out["monotone_constraints"] = _normalize_monotone(out["monotone_constraints"])
     out["num_boost_round"] = int(num_boost_round)
     return out
+
+
+def _monotone_sign(value: Any, where: str) -> int:
+    """python/ferrisboost/__init__.py:386-390: an integer (not a bool), of
+    which only the sign counts (XGBoost reads 2 as 1 and -3 as -1)."""
+    if isinstance(value, bool) or not isinstance(value, (int, np.integer)):
+        raise ValueError(f"monotone_constraints {where} must be an integer (1 / 0 / -1), got {value!r}")
+    return int(np.sign(int(value)))
+
+
+def _normalize_monotone(mc: Any) -> "list[int] | dict[str, int] | None":
+    """python/ferrisboost/__init__.py:393-419: a tuple / list / array by
+    position, a "(1,0,-1)" string, or {column name: direction}; shorter than
+    the feature count means 0 for the rest, and all zeros is no constraint."""
+    if mc is None:
+        return None
+    if isinstance(mc, str):
+        text = mc.strip()
+        if not (text.startswith("(") and text.endswith(")")):
+            raise ValueError(f'a monotone_constraints string must look like "(1,0,-1)", got {mc!r}')
+        body = text[1:-1].strip()
+        try:
+            values = [int(v) for v in body.split(",")] if body else []
+        except ValueError:
+            raise ValueError(f"monotone_constraints string contains a non-integer: {mc!r}") from None
+        return [_monotone_sign(v, "element") for v in values]
+    if isinstance(mc, Mapping):
+        for name in mc:
+            if not isinstance(name, str):
+                raise ValueError(f"monotone_constraints dict keys must be column name strings, got {name!r}")
+        return {name: _monotone_sign(v, f"value for column {name!r}") for name, v in mc.items()}
+    if isinstance(mc, (list, tuple, np.ndarray)):
+        return [_monotone_sign(v, "element") for v in np.asarray(mc, dtype=object).ravel()]
+    raise ValueError('monotone_constraints must be a tuple/list, a "(1,0,-1)" string or a {column name: direction} '
+                     f"dict, got {type(mc).__name__}")
+
+
+def _positional_monotone(mc: "list[int] | dict[str, int] | None", names, n_features: int):
+    """Constraints by feature position (python/ferrisboost/__init__.py:
+    422-426 and :1344-1350 for names; training/mod.rs:1508-1512 for the
+    length)."""
+    if isinstance(mc, dict):
+        if not names:
+            raise ValueError("monotone_constraints given by column name needs column names: a numpy array has none; "
+                             "use a positional tuple, or a pyarrow Table / a file with a header")
+        unknown = [k for k in mc if k not in names]
+        if unknown:
+            raise ValueError(f"monotone_constraints columns {unknown} are not feature columns; feature columns: "
+                             f"{list(names)}")
+        mc = [mc.get(n, 0) for n in names]
+    if mc is None:
+        return None
+    if len(mc) > n_features:
+        raise ValueError(f"monotone_constraints has {len(mc)} entries, but there are only {n_features} features")
+    mono = np.zeros(n_features, dtype=np.int8)
+    mono[:len(mc)] = mc
+    return mono
 
 
 def _fb_params(p: Mapping[str, Any]) -> _lib.FbParams:
@@ -490,14 +542,9 @@ class Booster:
         w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
         self.params = p
         fp = _fb_params(p)
-        mono = None
-        if p["monotone_constraints"] is not None:
-            mc = p["monotone_constraints"]
-            if len(mc) > dataset.n_features:
-                raise ValueError(f"monotone_constraints has {len(mc)} entries, but there are only "
-                                 f"{dataset.n_features} features")
-            mono = np.zeros(dataset.n_features, dtype=np.int8)
-            mono[:len(mc)] = mc
+        mono = _positional_monotone(p["monotone_constraints"], getattr(dataset, "feature_names", None),
+                                    dataset.n_features)
+        if mono is not None:
             fp.monotone = _lib.ptr(mono, C.c_int8)
         self._keep = (y, w, mono, dataset)
         if shard is None:

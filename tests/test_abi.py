@@ -125,3 +125,44 @@ def test_host_expf_table_is_verified_on_this_host():
     from ferrisboost_b200 import _lib
     why = C.c_char_p()
     assert _lib.load().fbgpu_exact_exp_available(C.byref(why)) == 1, why.value
+
+
+@pytest.mark.parametrize("form", [
+    (1, -1, 0, 0), [1, -1, 0, 0], "(1,-1,0,0)", "(1, -1, 0, 0)", np.array([1, -1, 0, 0]), (1, -1), (5, -2, 0, 0),
+])
+def test_monotone_forms_are_equivalent(form):
+    """python/tests/test_monotone.py:61-72: tuple, list, string, numpy,
+    shorter than the feature count (zeros after), sign only (5 == 1)."""
+    import ferrisboost_b200 as fb
+    mc = fb._normalize_params({"monotone_constraints": form}, 1)["monotone_constraints"]
+    assert fb._positional_monotone(mc, None, 4).tolist() == [1, -1, 0, 0]
+
+
+@pytest.mark.parametrize("bad,match", [
+    ((1, 0, 0, 0, 1), "only 4 features"), ((1.5, 0), "integer"), ((True, 0), "integer"),
+    ("1,0,-1", "string must look like"), ("(1,x)", "non-integer"), (3.0, "tuple"),
+])
+def test_invalid_monotone_constraints_are_rejected(bad, match):
+    """python/tests/test_monotone.py:86-99."""
+    import ferrisboost_b200 as fb
+    with pytest.raises(ValueError, match=match):
+        mc = fb._normalize_params({"monotone_constraints": bad}, 1)["monotone_constraints"]
+        fb._positional_monotone(mc, None, 4)
+
+
+def test_named_monotone_constraints():
+    """python/ferrisboost/__init__.py:422-426, 1344-1350: by column name when
+    the data has names; unknown names and nameless data are refused; all
+    zeros and empty mean no constraint."""
+    import ferrisboost_b200 as fb
+    mc = fb._normalize_params({"monotone_constraints": {"b": -1, "d": 3}}, 1)["monotone_constraints"]
+    assert fb._positional_monotone(mc, ["a", "b", "c", "d"], 4).tolist() == [0, -1, 0, 1]
+    with pytest.raises(ValueError, match="column names"):
+        fb._positional_monotone(mc, None, 4)
+    with pytest.raises(ValueError, match="not feature columns"):
+        fb._positional_monotone({"z": 1}, ["a", "b"], 2)
+    with pytest.raises(ValueError, match="keys must be column name strings"):
+        fb._normalize_params({"monotone_constraints": {0: 1}}, 1)
+    for zeros in [(0, 0, 0, 0), (0,), "(0,0)", []]:
+        mc = fb._normalize_params({"monotone_constraints": zeros}, 1)["monotone_constraints"]
+        assert not fb._positional_monotone(mc, None, 4).any()
