@@ -758,6 +758,30 @@ float label_mean(const float* y, const float* w, uint64_t n) {
     return (float)acc;
 }
 
+// objective.rs:403-493 initial_base_score for squared error and logistic.
+// With |scale_pos_weight - 1| > 1e-6 (compared in f32) it is one Newton step
+// from margin 0 over the gradient weights (XGBoost FitIntercept,
+// objective.rs:480-493): each row's pair at margin 0 times its gradient weight
+// (sample weight, times scale_pos_weight on positives) in f32, summed in f64;
+// the step -G / max(H, 1e-6f) rounded to f32 and mapped through the transform
+// (sigmoid for logistic, objective.rs:37).  Otherwise the label mean.
+float initial_base_score(int objective, const float* y, const float* w, uint64_t n, float spw) {
+    if (!(std::fabs(spw - 1.0f) > 1e-6f)) return label_mean(y, w, n);
+    double sg = 0.0, sh = 0.0;
+    const float s0 = 1.0f / (1.0f + std::exp(-0.0f));
+    for (uint64_t i = 0; i < n; i++) {
+        const float gw = (w ? w[i] : 1.0f) * (y[i] == 1.0f ? spw : 1.0f);  // mod.rs:5470-5495
+        float g = objective == 1 ? s0 - y[i] : 0.0f - y[i];
+        float h = objective == 1 ? std::max(s0 * (1.0f - s0), 1e-16f) : 1.0f;
+        g = g * gw;
+        h = h * gw;
+        sg = sg + (double)g;
+        sh = sh + (double)h;
+    }
+    const float m = (float)(-sg / std::max(sh, (double)1e-6f));
+    return objective == 1 ? 1.0f / (1.0f + std::exp(-m)) : m;
+}
+
 // Row shard of a booster trained on several GPUs (one process per GPU).
 struct ShardInfo {
     uint64_t row_offset = 0, n_global = 0;
@@ -865,7 +889,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
                                                       : std::vector<float>(p.num_class, base);
         base = b->model.class_margins[0];
     }
-    if (std::isnan(base)) base = label_mean(y, w, d->n);
+    if (std::isnan(base)) base = initial_base_score(p.objective, y, w, d->n, p.scale_pos_weight);
     if (p.objective == 1 && !(base >= 0.0f && base <= 1.0f))
         throw InputError("logistic base_score is a probability and must be in [0, 1]");
     b->model.base_score = base;
@@ -1207,6 +1231,11 @@ int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_
         }
         return (int64_t)total;
     }, (int64_t)-1);
+}
+
+float fb_initial_base_score(int32_t objective, const float* labels, const float* weights, uint64_t n,
+                            float scale_pos_weight) {
+    return fbe::initial_base_score(objective, labels, weights, n, scale_pos_weight);
 }
 
 float fb_label_mean(const float* labels, const float* weights, uint64_t n) {

@@ -28,7 +28,8 @@ from typing import Any, Mapping, Sequence
 
 import numpy as np
 
-from . import (Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params, lib)
+from . import (_OBJECTIVES, Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params,
+               lib)
 
 __all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost", "Communicator"]
 
@@ -255,8 +256,9 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
                                       _lib.ptr(class_margins, C.c_float)):
                 raise ValueError((lib().fb_last_error() or b"").decode())
             base = float("nan")
-    elif base is None:
-        base = float(lib().fb_label_mean(_lib.ptr(y, C.c_float), _lib.ptr(w, C.c_float), n))
+    elif base is None:  # over all rows, as a single process would (objective.rs:403-493)
+        base = float(lib().fb_initial_base_score(_OBJECTIVES[p["objective"]], _lib.ptr(y, C.c_float),
+                                                 _lib.ptr(w, C.c_float), n, p["scale_pos_weight"]))
     ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts,
                  device=p["device_index"])
     shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,

@@ -108,6 +108,12 @@ int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32
  * (weighted when weights != NULL), summed in f64 in row order
  * (src/objective.rs:41-61). */
 float fb_label_mean(const float* labels, const float* weights, uint64_t n);
+/* The base score a booster takes when base_score is not given (objective.rs:
+ * 403-493 initial_base_score; objective 0 squared error, 1 logistic): the
+ * label mean, or with |scale_pos_weight - 1| > 1e-6 one Newton step from
+ * margin 0 over the gradient weights (weights may be NULL). */
+float fb_initial_base_score(int32_t objective, const float* labels, const float* weights, uint64_t n,
+                            float scale_pos_weight);
 /* The multiclass base margins (objective.rs:1225-1247 initial_class_margins):
  * weighted class counts summed in f32 in row order, log(count / sum_w + 1e-6),
  * minus their mean; K values to out.  Labels must be integers in [0, K). */

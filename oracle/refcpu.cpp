@@ -654,6 +654,27 @@ float estimate_base_score(const float* y, uint64_t n, const float* w) {
     return (float)acc;
 }
 
+// objective.rs:403-493 initial_base_score for squared error and logistic:
+// with |scale_pos_weight - 1| > 1e-6 (f32) one Newton step from margin 0 over
+// the gradient weights (XGBoost FitIntercept; objective.rs:480-493
+// newton_base_score), else the label mean.  Per row the pair at margin 0 is
+// weighted in f32 and summed in f64; the step -G / max(H, 1e-6f) is rounded to
+// f32 and mapped through the objective's transform (sigmoid, objective.rs:37).
+float initial_base_score(int objective, const float* y, uint64_t n, const float* w, const float* gw, float spw) {
+    if (!(std::fabs(spw - 1.0f) > 1e-6f)) return estimate_base_score(y, n, w);
+    double sg = 0.0, sh = 0.0;
+    const float s0 = 1.0f / (1.0f + std::exp(-0.0f));
+    for (uint64_t i = 0; i < n; i++) {
+        float g = objective == 1 ? s0 - y[i] : 0.0f - y[i];
+        float h = objective == 1 ? std::max(s0 * (1.0f - s0), 1e-16f) : 1.0f;
+        if (gw) { g = g * gw[i]; h = h * gw[i]; }
+        sg = sg + (double)g;
+        sh = sh + (double)h;
+    }
+    const float m = (float)(-sg / std::max(sh, (double)1e-6f));
+    return objective == 1 ? 1.0f / (1.0f + std::exp(-m)) : m;
+}
+
 // data/subsample.rs:45-78
 inline uint64_t mix64(uint64_t z) {
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -1100,7 +1121,10 @@ Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const 
         train_multiclass(C, m, y, w, n, F);
         return m;
     }
-    m->base_score = std::isnan(p.base_score) ? estimate_base_score(y, n, w) : p.base_score;
+    m->base_score = std::isnan(p.base_score)
+                        ? initial_base_score(p.objective, y, n, w, p.scale_pos_weight != 1.0f ? gwp : w,
+                                             p.scale_pos_weight)
+                        : p.base_score;
     float margin = base_margin(p.objective, m->base_score);
     std::vector<float> preds(n, margin);
     std::vector<GP> gp(n);

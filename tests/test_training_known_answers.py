@@ -6,6 +6,7 @@ root-only round feeds the next round's gradients; leaf Hessians sum back to
 the root; trees keep max_depth; nothing to learn gives a single leaf; and
 training is reproducible."""
 import json
+import math
 
 import numpy as np
 import pytest
@@ -155,3 +156,48 @@ def test_zero_weight_rows_match_dropping_them(oracle):
     dropped = oracle.train(x[keep], y[keep], w[keep], **_WKW)
     assert np.array_equal(zeroed.predict_margin(x), dropped.predict_margin(x))
     assert zeroed.json() == dropped.json()
+
+
+def _newton_base_score(objective, y, w, spw):
+    """objective.rs:403-493 with scale_pos_weight != 1: pairs at margin 0
+    times the gradient weights in f32, summed in f64; -G / max(H, 1e-6f) to
+    f32, through the transform."""
+    y = np.asarray(y, np.float32)
+    gw = (np.ones_like(y) if w is None else np.asarray(w, np.float32)) * np.where(y == 1.0, np.float32(spw),
+                                                                               np.float32(1.0)).astype(np.float32)
+    gw = gw.astype(np.float32)
+    if objective == "binary:logistic":
+        g, h = (np.float32(0.5) - y), np.full_like(y, np.float32(0.25))
+    else:
+        g, h = (np.float32(0.0) - y), np.ones_like(y)
+    sg = sh = 0.0
+    for gi, hi in zip((g * gw).astype(np.float32), (h * gw).astype(np.float32)):
+        sg += float(gi)
+        sh += float(hi)
+    m = np.float32(-sg / max(sh, float(np.float32(1e-6))))
+    if objective == "binary:logistic":
+        e = np.float32(math.exp(-float(m)))  # expf, correctly rounded (glibc's, which Rust's f32::exp calls)
+        return np.float32(np.float32(1.0) / (np.float32(1.0) + e))
+    return m
+
+
+@pytest.mark.parametrize("objective", ["binary:logistic", "reg:squarederror"])
+@pytest.mark.parametrize("spw", [0.3, 4.0, 1.0])
+@pytest.mark.parametrize("weighted", [False, True])
+def test_scale_pos_weight_base_score(oracle, objective, spw, weighted):
+    """python/tests/test_regularization.py:79-91: with scale_pos_weight != 1
+    the default base score is XGBoost's one-step Newton estimate
+    (FitIntercept), with 1 it is the label mean; the oracle's model, the
+    engine's host estimate and an independent statement agree bit for bit."""
+    rng = np.random.default_rng(5)
+    n = 2001
+    X = rng.integers(0, 6, (n, 3)).astype(np.float32)
+    y = (X[:, 0] + rng.normal(0, 1, n) > 2.5).astype(np.float32)
+    w = rng.uniform(0.2, 3, n).astype(np.float32) if weighted else None
+    want = _newton_base_score(objective, y, w, spw) if spw != 1.0 else _label_mean(y, w)
+    m = oracle.train(X, y, w, objective=objective, scale_pos_weight=spw, max_depth=2, n_rounds=1)
+    got = fb.lib().fb_initial_base_score(1 if objective == "binary:logistic" else 0, _lib.ptr(y, _lib.C.c_float),
+                                         _lib.ptr(w, _lib.C.c_float), n, spw)
+    assert _base_score(m) == np.float32(got) == want, (_base_score(m), got, want)
+    if spw != 1.0:
+        assert want != _label_mean(y, w)
