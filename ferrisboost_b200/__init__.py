@@ -295,6 +295,8 @@ def _normalize_params(params: Mapping[str, Any], num_boost_round: int) -> dict[s
     if not 0.0 < out["colsample_bytree"] <= 1.0:
         raise ValueError(f"colsample_bytree must be in (0, 1], got {out['colsample_bytree']}")
     out["max_delta_step"] = 0.0 if out["max_delta_step"] is None else float(out["max_delta_step"])
+    if not math.isfinite(out["max_delta_step"]) or out["max_delta_step"] < 0:
+        raise ValueError(f"max_delta_step must be finite and non-negative, got {out['max_delta_step']}")
     if out["base_score"] is not None:
         out["base_score"] = float(out["base_score"])
     for key in ("max_cat_to_onehot", "max_cat_threshold"):

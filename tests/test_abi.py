@@ -166,3 +166,17 @@ def test_named_monotone_constraints():
     for zeros in [(0, 0, 0, 0), (0,), "(0,0)", []]:
         mc = fb._normalize_params({"monotone_constraints": zeros}, 1)["monotone_constraints"]
         assert not fb._positional_monotone(mc, None, 4).any()
+
+
+@pytest.mark.parametrize("bad", [{"alpha": -1.0}, {"max_delta_step": -0.1}, {"scale_pos_weight": -2.0},
+                                 {"alpha": float("inf")}, {"max_delta_step": float("nan")}])
+def test_invalid_regularization_values_are_rejected(bad):
+    """python/tests/test_regularization.py:118-124."""
+    import ferrisboost_b200 as fb
+    with pytest.raises(ValueError, match=next(iter(bad))):
+        fb._normalize_params(bad, 1)
+    # reg_alpha is alpha; neutral values equal the defaults (test_regularization.py:64-78)
+    assert fb._normalize_params({"reg_alpha": 2.0}, 1)["alpha"] == 2.0
+    d = fb._normalize_params({}, 1)
+    n = fb._normalize_params({"alpha": 0.0, "max_delta_step": 0.0, "scale_pos_weight": 1.0}, 1)
+    assert all(d[k] == n[k] for k in ("alpha", "max_delta_step", "scale_pos_weight"))
