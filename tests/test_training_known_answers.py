@@ -201,3 +201,17 @@ def test_scale_pos_weight_base_score(oracle, objective, spw, weighted):
     assert _base_score(m) == np.float32(got) == want, (_base_score(m), got, want)
     if spw != 1.0:
         assert want != _label_mean(y, w)
+
+
+def test_max_delta_step_bounds_every_leaf(oracle):
+    """python/tests/test_regularization.py:104-115: |leaf| <= max_delta_step x
+    eta with lambda 0."""
+    rng = np.random.default_rng(6)
+    X = rng.integers(0, 5, (2000, 4)).astype(np.float32)
+    y = (X[:, 0] - X[:, 1] + rng.normal(0, 1, 2000) > 0).astype(np.float32)
+    eta, mds = 0.3, 0.2
+    m = oracle.train(X, y, objective="binary:logistic", max_delta_step=mds, eta=eta, reg_lambda=0.0, n_rounds=5,
+                     max_depth=6)
+    for t in _trees(m):
+        leaves = [v for v, c in zip(t["split_conditions"], t["left_children"]) if c == -1]
+        assert max(abs(v) for v in leaves) <= mds * eta * (1 + 1e-6)
