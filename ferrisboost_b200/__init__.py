@@ -439,7 +439,7 @@ class Shard(NamedTuple):
     nccl_id: bytes        # fbgpu_nccl_unique_id of rank 0, 128 bytes
     nranks: int
     rank: int
-    base_score: float     # label mean over all rows (fb_label_mean) or the given base_score
+    base_score: float     # over all rows (fb_initial_base_score) or the given base_score
     timeout_ms: int = 120000
     comm: Any = None      # a distributed.Communicator started ahead (its initialization overlaps data preparation)
     class_margins: Any = None  # multiclass: the K base margins over all rows (fb_class_margins)
