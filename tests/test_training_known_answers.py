@@ -215,3 +215,42 @@ def test_max_delta_step_bounds_every_leaf(oracle):
     for t in _trees(m):
         leaves = [v for v, c in zip(t["split_conditions"], t["left_children"]) if c == -1]
         assert max(abs(v) for v in leaves) <= mds * eta * (1 + 1e-6)
+
+
+def _wiggly(n=800, m=4, seed=0, missing=0.08):
+    """python/tests/test_monotone.py:8-15: a non-monotone truth."""
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(-2, 2, size=(n, m)).astype(np.float32)
+    signal = np.sin(1.7 * x[:, 0]) + 0.8 * np.cos(3 * x[:, 1]) - 0.5 * x[:, 2]
+    y = (signal + rng.normal(0, 0.3, n) > 0).astype(np.float32)
+    x[rng.random(x.shape) < missing] = np.nan
+    return x, y
+
+
+def _sweep_is_monotone(m, x, constraints):
+    grid = np.linspace(-2.2, 2.2, 61, dtype=np.float32)
+    for base in x[::23][:30]:
+        for f, c in enumerate(constraints):
+            if c == 0:
+                continue
+            rows = np.repeat(base[None, :], len(grid), axis=0)
+            rows[:, f] = grid
+            d = np.diff(m.predict_margin(rows))
+            if (c > 0 and (d < 0).any()) or (c < 0 and (d > 0).any()):
+                return False
+    return True
+
+
+def test_monotone_constraints_hold_and_zeros_change_nothing(oracle):
+    """python/tests/test_monotone.py:41-58: the unconstrained model breaks
+    monotonicity on this data, the constrained one keeps it; all-zero
+    constraints give the unconstrained bytes."""
+    x, y = _wiggly()
+    kw = dict(objective="binary:logistic", max_depth=5, eta=0.3, nthread=1)
+    mc = [1, -1, 0, 0]
+    free = oracle.train(x, y, n_rounds=20, **kw)
+    tied = oracle.train(x, y, n_rounds=20, monotone_constraints=mc, **kw)
+    assert not _sweep_is_monotone(free, x, mc)
+    assert _sweep_is_monotone(tied, x, mc)
+    assert oracle.train(x, y, n_rounds=4, monotone_constraints=[0, 0, 0, 0], **kw).json() == \
+        oracle.train(x, y, n_rounds=4, **kw).json()
