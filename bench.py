@@ -22,6 +22,16 @@ over ranks.  cpu_baseline / --impl reference: the C++ restatement of the
 reference CPU engine (oracle/), all host threads, a bounded sample of the same
 workload.
 
+Beside the timing, every run prints evidence that the timed engine computes
+the reference's models: model_sha256 (the e2e model's JSON, identical at every
+GPU count in exact mode), parity (at N=1: the engine's model against the
+oracle's on the same arrays, JSON bytes and margins bit for bit; for
+configs[1] 3 rounds on all 11M rows plus configs[0]'s full 100 rounds),
+fast_mode (gpu_math="fast" against exact after 100 rounds) and, for
+configs[1], treeshap: configs[4] (TreeSHAP of a 500-tree model of this
+workload on 1M fresh rows), rows/s and its largest difference from the
+oracle's SHAP values.
+
 --config selects the other benchmark configs (configs[0], [2], [3] and the
 max_depth 14 variant of [3], and [4]: TreeSHAP rows/s); they print the same
 JSON line for their own workload.
@@ -42,10 +52,14 @@ sys.path.insert(0, ROOT)
 N_FEATURES = 28
 PARAMS = {"objective": "binary:logistic", "max_depth": 8, "eta": 0.1, "lambda": 1.0, "max_bin": 256}
 E2E_ROUNDS = 100
-# DRAM bytes / algorithmic bytes of k_hist_stage over one tree, from an ncu
-# capture (profiles/k_hist_stage_c1_4Mrows_traffic.md); roofline.traffic =
-# this x the algorithmic bytes per launch measured live
+# DRAM bytes / algorithmic bytes of k_hist_stage over one tree: one ncu
+# capture of a 4M-row configs[1]-shaped tree (dram__bytes_read.sum +
+# dram__bytes_write.sum over its 8 histogram launches); roofline.traffic =
+# this ratio x the algorithmic bytes per launch measured live
 HIST_TRAFFIC_RATIO = 1800.9 / 8 / 84.44
+# oracle rounds compared with the engine's model at N=1 (a few seconds to
+# about half a minute of CPU per config)
+PARITY_ROUNDS = {"c0": 100, "c1": 3, "c2": 5, "c3": 3, "c3d14": 2, "c1mc": 2}
 
 
 def make_data(n, seed=0):
@@ -176,44 +190,46 @@ def cpu_threads():
     return len(os.sched_getaffinity(0))
 
 
-def reference_rounds(X, y, params, rounds, warmup, feature_types=None):
+def oracle_train(X, y, params, rounds, feature_types=None, nthread=0):
     """Oracle (C++ restatement of the reference CPU engine) on the workload:
-    set-up seconds and per-round wall seconds of the rounds after `warmup`,
-    all host threads."""
+    its model, set-up seconds and per-round wall seconds, `nthread` host
+    threads (0 = all)."""
     from oracle import RefCPU
     rc = RefCPU()
     kw = dict(params)
     if feature_types is not None:
         kw["categorical"] = np.array([t == "c" for t in feature_types], np.uint8)
-    rc.train(X, y, n_rounds=warmup + rounds, nthread=0, **kw)
+    model = rc.train(X, y, n_rounds=rounds, nthread=nthread, **kw)
     setup, per_round = rc.last_timing()
-    return setup, per_round[warmup:]
+    return model, setup, per_round
 
 
 def run_reference(args, rank, world):
     """The reference's CPU engine (the oracle restatement) on the same
-    workload: rank 0 alone; `value` = mean round x 100, `e2e` = set-up +
-    100 rounds."""
+    workload: rank 0 alone; W untimed warm-up rounds, then K timed rounds of
+    the same training run; `value` = mean timed round x 100, `e2e` = set-up +
+    100 x the mean round."""
     if rank != 0:
         return
     cfg = CONFIGS[args.config]
     n = args.rows or cfg["rows"]
     X, y, ft = cfg["make"](n)
-    steps = min(args.steps, 10)  # bounded sample: at most 10 timed rounds
-    warm = min(args.warmup, 1)
-    setup, rs = reference_rounds(X, y, cfg["params"], steps, warm, ft)
-    mean = float(np.mean(rs))
+    t0 = time.perf_counter()
+    _, setup, rs = oracle_train(X, y, cfg["params"], args.warmup + args.steps, ft)
+    wall = time.perf_counter() - t0
+    timed = rs[args.warmup:]
+    mean = float(np.mean(timed))
     line = {
         "metric": "train s/100 rounds", "value": round(mean * 100.0, 4), "unit": "s/100 rounds", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * mean, 3),
+        "steps": len(timed), "warmup": args.warmup, "ms_per_step": round(1000 * mean, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": cfg["workload"].replace(", gpu_math exact", ""), "rows": n,
-                   "features": int(X.shape[1])},
+        "config": {"workload": cfg["workload"], "rows": n, "features": int(X.shape[1])},
         "cpu_baseline": {"value": round(mean * 100.0, 4), "unit": "s/100 rounds", "cores": cpu_threads(),
                          "kind": "port",
-                         "sample": f"{steps} timed rounds after {warm} warm-up round(s) on the full {n}-row "
-                                   f"workload; sketch + quantize set-up {setup:.2f} s"},
+                         "sample": f"{len(timed)} timed rounds after {args.warmup} warm-up rounds of one training run "
+                                   f"on the full {n}-row workload; sketch + quantize set-up {setup:.2f} s; "
+                                   f"{wall:.1f} s wall in all"},
         "e2e": {"value": round(setup + mean * E2E_ROUNDS, 4), "unit": "s/100 rounds", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0, "includes": "set-up + 100 x the mean timed round"},
     }
@@ -257,6 +273,151 @@ def _peaks():
     return float(peaks.get("hbm_gbs", 6650.0)), "measured" if "hbm_gbs" in peaks else "fallback"
 
 
+def _sha256(b):
+    import hashlib
+    return hashlib.sha256(b).hexdigest()
+
+
+def _bits_equal(a, b):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    return a.shape == b.shape and bool(np.array_equal(a.view(np.uint32), b.view(np.uint32)))
+
+
+def parity_vs_oracle(model, oracle_model, X):
+    """The engine's model against the oracle's, trained on the same arrays
+    with the same parameters: JSON bytes and margins on the training rows,
+    bit for bit."""
+    ours, ref = model.to_json(), oracle_model.json()
+    mo = model.predict(X, output_margin=True)
+    mr = oracle_model.predict_margin(X)
+    out = {"rounds": int(model.num_trees // max(model.num_outputs, 1)), "rows": int(X.shape[0]),
+           "json_equal": ours == ref, "margins_equal": _bits_equal(mo, mr)}
+    if not out["margins_equal"]:
+        d = np.abs(mo.astype(np.float64) - mr.astype(np.float64))
+        out["max_abs_margin_diff"] = float(np.max(d))
+        out["rows_differing"] = int(np.count_nonzero(d.reshape(d.shape[0], -1).max(axis=1)))
+    if ours != ref:
+        k = min(len(ours), len(ref))
+        diff = np.nonzero(np.frombuffer(ours[:k], np.uint8) != np.frombuffer(ref[:k], np.uint8))[0]
+        out["first_json_difference_at"] = int(diff[0]) if diff.size else k
+    return out
+
+
+def fast_vs_exact(exact, fast, X, y, objective):
+    """gpu_math="fast" against the exact model after the same rounds, on the
+    training rows: the largest relative prediction error and the loss
+    difference (north_star: predictions within 1e-5 relative, logloss within
+    1e-4)."""
+    a = exact.predict(X, output_margin=True).astype(np.float64)
+    b = fast.predict(X, output_margin=True).astype(np.float64)
+    if objective == "binary:logistic":
+        pa, pb = 1.0 / (1.0 + np.exp(-a)), 1.0 / (1.0 + np.exp(-b))
+
+        def loss(p):
+            p = np.clip(p, 1e-15, 1 - 1e-15)
+            return float(-np.mean(y * np.log(p) + (1 - y) * np.log(1 - p)))
+        name = "logloss"
+    elif objective.startswith("multi:"):
+        def softmax(m):
+            e = np.exp(m - m.max(axis=1, keepdims=True))
+            return e / e.sum(axis=1, keepdims=True)
+        pa, pb = softmax(a), softmax(b)
+        yi = y.astype(np.int64)
+
+        def loss(p):
+            return float(-np.mean(np.log(np.clip(p[np.arange(p.shape[0]), yi], 1e-15, 1.0))))
+        name = "mlogloss"
+    else:
+        pa, pb = a, b
+
+        def loss(p):
+            return float(np.sqrt(np.mean((p - y) ** 2)))
+        name = "rmse"
+    rel = (np.abs(pb - pa) / np.maximum(np.abs(pa), 1e-30)).ravel()
+    return {"rounds": int(exact.num_trees // max(exact.num_outputs, 1)), "rows": int(X.shape[0]),
+            "max_rel_pred_err": float(np.max(rel)), "p99_rel_pred_err": float(np.quantile(rel, 0.99)),
+            "median_rel_pred_err": float(np.median(rel)), "preds_over_1e-5": int(np.count_nonzero(rel > 1e-5)),
+            f"{name}_exact": loss(pa), f"{name}_fast": loss(pb), f"{name}_diff": abs(loss(pb) - loss(pa)),
+            "max_abs_margin_diff": float(np.max(np.abs(b - a)))}
+
+
+def treeshap_leg(dist, rank, world, device, lib, model, steps, warmup, check_oracle):
+    """TreeSHAP and prediction of `model` on 1M fresh N(0,1) rows
+    (seed 1), rows sharded over the ranks.  e2e through the public
+    Model.predict from host rows; `value` from CUDA events with rows and
+    outputs resident.  At N=1 the oracle explains the first 2000 rows with the
+    same model (loaded from its JSON): max |SHAP - oracle|, and its rows/s."""
+    import torch
+    from ferrisboost_b200 import distributed as fbd
+    n = 1_000_000
+    Xe = np.random.default_rng(1).standard_normal((n, N_FEATURES), dtype=np.float32)
+    lo, hi = fbd.shard_range(n, world, rank)
+    Xs = np.ascontiguousarray(Xe[lo:hi])
+    model.predict(Xs[:1000], pred_contribs=True)
+    _fence(dist)
+    t0 = time.perf_counter()
+    phi = model.predict(Xs, pred_contribs=True)
+    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    t0 = time.perf_counter()
+    margin = model.predict(Xs, output_margin=True)
+    pred_e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    rowsum_err = float(np.max(np.abs(phi.astype(np.float64).sum(axis=1) - margin.astype(np.float64))))
+    xd = torch.from_numpy(Xs).cuda()
+    od = torch.empty((hi - lo, N_FEATURES + 1), dtype=torch.float32, device="cuda")
+    pd = torch.empty(hi - lo, dtype=torch.float32, device="cuda")
+    h = model.device_handle(device)
+    s = torch.cuda.current_stream()
+    for _ in range(warmup):
+        if lib.fbgpu_shap_device(h, xd.data_ptr(), hi - lo, od.data_ptr(), s.cuda_stream):
+            raise RuntimeError(lib.fbgpu_last_error(None).decode())
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    l0 = lib.fbgpu_launch_count()
+    with ClockSampler(device) as clk:
+        _fence(dist)
+        ev[0].record(s)
+        for _ in range(steps):
+            lib.fbgpu_shap_device(h, xd.data_ptr(), hi - lo, od.data_ptr(), s.cuda_stream)
+        ev[1].record(s)
+        ev[2].record(s)
+        for _ in range(steps):
+            lib.fbgpu_predict_device(h, xd.data_ptr(), hi - lo, pd.data_ptr(), s.cuda_stream)
+        ev[3].record(s)
+        _fence(dist)
+    launches = lib.fbgpu_launch_count() - l0
+    shap_ms = _max_over_ranks(dist, ev[0].elapsed_time(ev[1]) / steps)
+    pred_ms = _max_over_ranks(dist, ev[2].elapsed_time(ev[3]) / steps)
+    out = {
+        "metric": "TreeSHAP rows/s", "value": round(n / (shap_ms / 1000.0), 1), "unit": "rows/s",
+        "ms_per_step": round(shap_ms, 3), "steps": steps, "warmup": warmup, "rows": n, "trees": model.num_trees,
+        "e2e": {"value": round(n / e2e_s, 1), "unit": "rows/s", "h2d_bytes_per_step": int((hi - lo) * 4 * N_FEATURES),
+                "d2h_bytes_per_step": int((hi - lo) * 4 * (N_FEATURES + 1)),
+                "includes": "public Model.predict(pred_contribs=True) from host rows"},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+        "predict_rows_per_s": round(n / (pred_ms / 1000.0), 1), "predict_e2e_rows_per_s": round(n / pred_e2e_s, 1),
+        "max_abs_rowsum_minus_margin": rowsum_err,
+        "device_equals_public": bool(np.array_equal(od.cpu().numpy(), phi)),
+    }
+    del xd, od, pd
+    if check_oracle and world == 1:
+        from oracle import RefCPU
+        doc = model.to_json()
+        ref = RefCPU().load_json(doc)
+        rows = Xe[:2000]
+        ref.shap(rows[:64])
+        t0 = time.perf_counter()
+        want = ref.shap(rows)
+        cpu_s = time.perf_counter() - t0
+        out["oracle"] = {"rows": len(rows), "max_abs_err": float(np.max(np.abs(phi[:2000] - want))),
+                         "margins_equal": _bits_equal(margin[:2000], ref.predict_margin(rows)),
+                         "model_json_round_trip": ref.json() == doc}
+        out["cpu_baseline"] = {"value": round(len(rows) / cpu_s, 1), "unit": "rows/s", "cores": cpu_threads(),
+                               "kind": "port",
+                               "sample": f"oracle TreeSHAP of {len(rows)} of the rows with the same "
+                                         f"{model.num_trees}-tree model (loaded from its JSON), all host threads"}
+    return out
+
+
 def run_ours(args, rank, world):
     import torch
     import ferrisboost_b200 as fb
@@ -274,16 +435,18 @@ def run_ours(args, rank, world):
     p = dict(cfg["params"], device=f"cuda:{device}")
     F = int(X.shape[1])
     lo, hi = fbd.shard_range(n, world, rank)
+    cpu_legs = rank == 0 and world == 1 and not args.no_cpu
 
-    def train_public(params, rounds, booster=False):
+    def train_public(params, rounds, booster=False, data=None):
+        Xt, yt = data if data is not None else (X, y)
         if world == 1:
             if booster:
-                ds = fb.Dataset(X, max_bin=params["max_bin"], feature_types=ft, device=device)
-                b = fb.Booster(params, ds, y)
+                ds = fb.Dataset(Xt, max_bin=params["max_bin"], feature_types=ft, device=device)
+                b = fb.Booster(params, ds, yt)
                 b.update(rounds)
                 return b
-            return fb.train(params, X, label=y, num_boost_round=rounds, feature_types=ft)
-        return fbd.train(params, X, label=y, num_boost_round=rounds, feature_types=ft, timeout_s=300,
+            return fb.train(params, Xt, label=yt, num_boost_round=rounds, feature_types=ft)
+        return fbd.train(params, Xt, label=yt, num_boost_round=rounds, feature_types=ft, timeout_s=300,
                          return_booster=booster)
 
     # untimed: the process's first CUDA work (context creation, module
@@ -296,10 +459,9 @@ def run_ours(args, rank, world):
     _fence(dist)
     t0 = time.perf_counter()
     m = train_public(p, E2E_ROUNDS)
-    json_bytes = len(m.to_json())
+    model_json = m.to_json()
     e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
-    ref_json = m.to_json() if args.parquet else None
-    del m
+    exact_model = m
     e2e_parquet = None
     if args.parquet and world == 1:
         # the same 100 rounds from a Parquet file of the workload (written
@@ -316,7 +478,7 @@ def run_ours(args, rank, world):
         t0 = time.perf_counter()
         m = fb.train(p, path, label="label", num_boost_round=E2E_ROUNDS, feature_types=ft)
         pq_s = time.perf_counter() - t0
-        same = m.to_json() == ref_json.replace(b'"feature_names":[]', b'"feature_names":' + json.dumps(
+        same = m.to_json() == model_json.replace(b'"feature_names":[]', b'"feature_names":' + json.dumps(
             names, separators=(",", ":")).encode(), 1)
         del m
         os.remove(path)
@@ -344,13 +506,16 @@ def run_ours(args, rank, world):
     t = b.timing()
     dev_ms = _max_over_ranks(dist, t["device_ms"])
     fast_ms = _max_over_ranks(dist, fast.timing()["device_ms"])
-    del fast
+    comm_ms = _max_over_ranks(dist, t.get("comm_ms", 0.0))
+    del fast, b
     ms_step = dev_ms / args.steps
     s100 = ms_step * 100.0 / 1000.0
 
     hbm_peak, peak_src = _peaks()
     hist_launches = max(t["hist_launches"], 1.0)
-    hist_gbs = t["hist_bytes"] / (t["hist_ms"] / 1000.0) / 1e9 if t["hist_ms"] > 0 else None
+    # the histogram kernels alone: the phase's all-reduces (sharded) excluded
+    hist_kernel_ms = t["hist_ms"] - t["comm_ms"]
+    hist_gbs = t["hist_bytes"] / (hist_kernel_ms / 1000.0) / 1e9 if hist_kernel_ms > 0 else None
     rows_local = hi - lo
     depth = p.get("max_depth", 6)
     leaves = p.get("max_leaves", 0) or 2 ** depth
@@ -368,10 +533,11 @@ def run_ours(args, rank, world):
                    else "inputs smaller than L2"},
         "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds",
                 "h2d_bytes_per_step": int(e2e_h2d / E2E_ROUNDS),
-                "d2h_bytes_per_step": int(tree_readback + 16 + json_bytes / E2E_ROUNDS),
+                "d2h_bytes_per_step": int(tree_readback + 16 + len(model_json) / E2E_ROUNDS),
                 "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "
                             "per-rank bytes; wall clock, max over ranks"},
         **({"e2e_parquet": e2e_parquet} if e2e_parquet else {}),
+        "model_sha256": _sha256(model_json),
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(hist_gbs, 1) if hist_gbs else None, "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(hist_gbs / hbm_peak, 4) if hist_gbs else None,
@@ -380,21 +546,72 @@ def run_ours(args, rank, world):
                                        f"{HIST_TRAFFIC_RATIO:.2f}), scaled to this launch",
                      "kernel": "k_hist_stage (the histogram kernels of one level), rank 0",
                      "note": None if hist_gbs else "histogram timing is collected on level-wise trees only",
-                     "per_launch_ms": round(t["hist_ms"] / hist_launches, 4),
+                     "per_launch_ms": round(hist_kernel_ms / hist_launches, 4),
                      "alg_bytes_per_launch": int(t["hist_bytes"] / hist_launches), "peak_source": peak_src},
         "clocks": clk.summary(),
         "breakdown": {"hist_share_of_device": round(t["hist_ms"] / t["device_ms"], 4) if t["device_ms"] else None,
                       "fast_mode_s_per_100_rounds": round(fast_ms / args.steps * 100 / 1000, 4),
                       "setup_s": {"datagen": round(gen_s, 2), "sketch_bin_upload_warmup": round(setup_s, 2)}},
     }
-    if rank == 0 and world == 1 and not args.no_cpu:
-        csteps = 2
-        setup, rs = reference_rounds(X, y, cfg["params"], csteps, 1, ft)
-        line["cpu_baseline"] = {"value": round(float(np.mean(rs)) * 100, 4), "unit": "s/100 rounds",
+    if world > 1:
+        # device ms per round of the per-level histogram all-reduces (the
+        # limiting collective), beside the histogram kernels' own ms
+        line["breakdown"]["collective_ms_per_round"] = round(comm_ms / args.steps, 4)
+        line["breakdown"]["hist_kernel_ms_per_round"] = round(hist_kernel_ms / args.steps, 4)
+
+    # gpu_math="fast" after the same 100 rounds, against the exact model
+    objective = p.get("objective", "binary:logistic")
+    fast_model = train_public(dict(p, gpu_math="fast"), E2E_ROUNDS)
+    if rank == 0:
+        line["fast_mode"] = fast_vs_exact(exact_model, fast_model, X, y, objective)
+    del fast_model
+
+    # configs[4] rides on the configs[1] run: TreeSHAP of a 500-tree model of
+    # this workload (trained through the public train())
+    if args.config == "c1" and not args.no_shap:
+        trees = 50 if args.rows else 500
+        t0 = time.perf_counter()
+        shap_model = train_public(p, trees)
+        shap_train_s = _max_over_ranks(dist, time.perf_counter() - t0)
+        line["treeshap"] = treeshap_leg(dist, rank, world, device, lib, shap_model, steps=min(args.steps, 3),
+                                        warmup=1, check_oracle=cpu_legs)
+        line["treeshap"]["config"] = {"workload": f"configs[4] TreeSHAP of the {trees}-tree depth-8 configs[1] "
+                                                  f"model on 1M N(0,1) rows (seed 1)",
+                                      "train_s_for_model": round(shap_train_s, 2)}
+        del shap_model
+
+    if cpu_legs:
+        # the oracle on the same arrays: its timed rounds are the CPU baseline
+        # and its model is compared with the engine's, bit for bit
+        R = PARITY_ROUNDS.get(args.config, 3)
+        ref, setup, rs = oracle_train(X, y, cfg["params"], R, ft)
+        ours = train_public(p, R)
+        line["parity"] = {args.config: parity_vs_oracle(ours, ref, X)}
+        del ours
+        timed = rs[1:] if len(rs) > 1 else rs
+        line["cpu_baseline"] = {"value": round(float(np.mean(timed)) * 100, 4), "unit": "s/100 rounds",
                                 "cores": cpu_threads(), "kind": "port",
-                                "sample": f"{csteps} rounds after 1 warm-up round on the full {n}-row workload "
-                                          f"(oracle C++ restatement, all host threads)"}
-    del b
+                                "sample": f"{len(timed)} rounds after 1 warm-up round on the full {n}-row workload "
+                                          f"(oracle C++ restatement, all host threads); set-up {setup:.2f} s"}
+        del ref
+        if args.config == "c1" and not args.rows:
+            # configs[0] in full: 100 rounds on 1M rows, engine and oracle
+            c0 = CONFIGS["c0"]
+            X0, y0, _ = c0["make"](c0["rows"])
+            p0 = dict(c0["params"], device=f"cuda:{device}")
+            ref0, setup0, rs0 = oracle_train(X0, y0, c0["params"], PARITY_ROUNDS["c0"])
+            ours0 = train_public(p0, PARITY_ROUNDS["c0"], data=(X0, y0))
+            line["parity"]["c0"] = parity_vs_oracle(ours0, ref0, X0)
+            line["parity"]["c0"]["oracle_s_per_100_rounds"] = round(float(np.sum(rs0)) * 100 / len(rs0), 4)
+            del ours0, ref0
+            # the reference CPU engine on one core: 1 warm-up + 2 rounds
+            _, setup1, rs1 = oracle_train(X0, y0, c0["params"], 3, nthread=1)
+            line["cpu_baseline_1core"] = {"value": round(float(np.mean(rs1[1:])) * 100, 4), "unit": "s/100 rounds",
+                                          "cores": 1, "kind": "port", "config": "configs[0]",
+                                          "sample": f"2 rounds after 1 warm-up round on configs[0] (1M x 28, depth 6), "
+                                                    f"one host thread; set-up {setup1:.2f} s",
+                                          "all_cores_value": line["parity"]["c0"]["oracle_s_per_100_rounds"]}
+    del exact_model
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -415,81 +632,29 @@ def run_shap(args, rank, world):
     lib = _lib.load()
     trees = 50 if args.rows else 500
     Xtr, ytr, _ = make_data(args.rows or 11_000_000)
+    p = dict(PARAMS, device=f"cuda:{device}")
     t0 = time.perf_counter()
-    model = fb.train(dict(PARAMS, device=f"cuda:{device}"), Xtr, label=ytr, num_boost_round=trees)
+    if world == 1:
+        model = fb.train(p, Xtr, label=ytr, num_boost_round=trees)
+    else:
+        model = fbd.train(p, Xtr, label=ytr, num_boost_round=trees, timeout_s=300)
     train_s = time.perf_counter() - t0
     del Xtr, ytr
-    n = 1_000_000
-    Xe = np.random.default_rng(1).standard_normal((n, N_FEATURES), dtype=np.float32)
-    lo, hi = fbd.shard_range(n, world, rank)
-    Xs = np.ascontiguousarray(Xe[lo:hi])
-    # e2e: public predict(pred_contribs=True) from host rows, results on the host
-    model.predict(Xs[:1000], pred_contribs=True)
-    _fence(dist)
-    t0 = time.perf_counter()
-    phi = model.predict(Xs, pred_contribs=True)
-    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
-    t0 = time.perf_counter()
-    margin = model.predict(Xs, output_margin=True)
-    pred_e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
-    err = float(np.max(np.abs(phi.astype(np.float64).sum(axis=1) - margin.astype(np.float64))))
-    # device-resident: rows and outputs in HBM, CUDA events on the launching stream
-    xd = torch.from_numpy(Xs).cuda()
-    od = torch.empty((hi - lo, N_FEATURES + 1), dtype=torch.float32, device="cuda")
-    pd = torch.empty(hi - lo, dtype=torch.float32, device="cuda")
-    h = model.device_handle(device)
-    s = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        if lib.fbgpu_shap_device(h, xd.data_ptr(), hi - lo, od.data_ptr(), s.cuda_stream):
-            raise RuntimeError(lib.fbgpu_last_error(None).decode())
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    l0 = lib.fbgpu_launch_count()
-    with ClockSampler(device) as clk:
-        _fence(dist)
-        ev[0].record(s)
-        for _ in range(args.steps):
-            lib.fbgpu_shap_device(h, xd.data_ptr(), hi - lo, od.data_ptr(), s.cuda_stream)
-        ev[1].record(s)
-        ev[2].record(s)
-        for _ in range(args.steps):
-            lib.fbgpu_predict_device(h, xd.data_ptr(), hi - lo, pd.data_ptr(), s.cuda_stream)
-        ev[3].record(s)
-        _fence(dist)
-    launches = lib.fbgpu_launch_count() - l0
-    shap_ms = _max_over_ranks(dist, ev[0].elapsed_time(ev[1]) / args.steps)
-    pred_ms = _max_over_ranks(dist, ev[2].elapsed_time(ev[3]) / args.steps)
-    same = bool(np.array_equal(od.cpu().numpy(), phi))
+    leg = treeshap_leg(dist, rank, world, device, lib, model, args.steps, args.warmup,
+                       check_oracle=rank == 0 and world == 1 and not args.no_cpu)
     line = {
-        "metric": "TreeSHAP rows/s", "value": round(n / (shap_ms / 1000.0), 1), "unit": "rows/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(shap_ms, 3), "higher_is_better": True,
+        "metric": leg.pop("metric"), "value": leg.pop("value"), "unit": leg.pop("unit"), "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": leg.pop("ms_per_step"), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"configs[4] TreeSHAP of the {trees}-tree depth-8 configs[1] model on 1M N(0,1) "
-                               "rows (seed 1)", "rows": n, "trees": trees, "parallelism": f"row shards x{world}"},
-        "e2e": {"value": round(n / e2e_s, 1), "unit": "rows/s",
-                "h2d_bytes_per_step": int((hi - lo) * 4 * N_FEATURES),
-                "d2h_bytes_per_step": int((hi - lo) * 4 * (N_FEATURES + 1)),
-                "includes": "public Model.predict(pred_contribs=True) from host rows"},
-        "gpu_launches": int(launches),
-        "clocks": clk.summary(),
-        "breakdown": {"predict_rows_per_s": round(n / (pred_ms / 1000.0), 1),
-                      "predict_e2e_rows_per_s": round(n / pred_e2e_s, 1),
-                      "max_abs_rowsum_minus_margin": err, "device_equals_public": same,
-                      "train_s_for_model": round(train_s, 2)},
+                               "rows (seed 1)", "rows": leg.pop("rows"), "trees": leg.pop("trees"),
+                   "parallelism": f"row shards x{world}"},
+        "e2e": leg.pop("e2e"), "gpu_launches": leg.pop("gpu_launches"), "clocks": leg.pop("clocks"),
+        **({"cpu_baseline": leg.pop("cpu_baseline")} if "cpu_baseline" in leg else {}),
+        **({"oracle": leg.pop("oracle")} if "oracle" in leg else {}),
+        "model_sha256": _sha256(model.to_json()),
+        "breakdown": dict(leg, train_s_for_model=round(train_s, 2)),
     }
-    if rank == 0 and world == 1 and not args.no_cpu:
-        from oracle import RefCPU
-        rc = RefCPU()
-        Xs_tr, ys_tr, _ = make_data(200_000)
-        ref = rc.train(Xs_tr, ys_tr, n_rounds=20, nthread=0, **PARAMS)
-        rows = Xe[:2000]
-        ref.shap(rows[:100])
-        t0 = time.perf_counter()
-        ref.shap(rows)
-        cpu_s = time.perf_counter() - t0
-        rps = len(rows) / cpu_s * 20.0 / trees
-        line["cpu_baseline"] = {"value": round(rps, 1), "unit": "rows/s", "cores": cpu_threads(), "kind": "port",
-                                "sample": f"oracle TreeSHAP of 2000 rows with a 20-tree depth-8 model (200k "
-                                          f"training rows), scaled linearly to {trees} trees"}
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -506,6 +671,7 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["c4"])
     ap.add_argument("--rows", type=int, default=0, help="override the config's row count (smaller runs)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-shap", action="store_true", help="skip the configs[4] TreeSHAP leg of the configs[1] run")
     ap.add_argument("--parquet", action="store_true",
                     help="also time the e2e leg from a Parquet file of the workload (1 GPU)")
     args = ap.parse_args()

@@ -595,7 +595,10 @@ class Booster:
         t = np.zeros(8, dtype=np.float64)
         lib().fb_booster_timing(self._h, _lib.ptr(t, C.c_double))
         keys = ("wall_ms", "gradient_ms", "tree_ms", "device_ms", "hist_ms", "hist_launches", "hist_bytes", "trees")
-        return {k: float(v) for k, v in zip(keys, t)}
+        out = {k: float(v) for k, v in zip(keys, t)}
+        # of hist_ms: the per-level histogram all-reduces of a row-sharded run
+        out["comm_ms"] = float(lib().fb_booster_collective_ms(self._h))
+        return out
 
     def margins(self) -> np.ndarray:
         """Training margins: n values, or K x n (class-major) for multiclass."""

@@ -96,8 +96,8 @@ SIGNATURES = {
     "fbgpu_eval_split": (C.c_int, [P, i64p, i64p, f64p, C.POINTER(FbgpuTreeParams), C.c_float, C.c_float, u8p,
                                    C.POINTER(FbgpuSplit)]),
     "fbgpu_partition": (C.c_int, [P, u32p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_int32, u32p, u32p, u64p]),
-    "fbgpu_partition_noalloc": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint64, C.c_uint32,
-                                         C.c_int32, u32p, P, P, P]),
+    "fbgpu_partition_noalloc": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint64,
+                                         C.c_uint32, C.c_int32, u32p, P, P, P]),
     "fbgpu_model_create": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, u32p, i32p, i32p, u32p, f32p, u8p, f32p,
                                      u32p, u32p, u32p, C.c_uint64, C.c_float, C.POINTER(P)]),
     "fbgpu_model_destroy": (None, [P]),
@@ -139,6 +139,7 @@ SIGNATURES = {
     "fb_booster_free": (None, [P]),
     "fb_booster_update": (C.c_int32, [P, C.c_uint32]),
     "fb_booster_timing": (None, [P, f64p]),
+    "fb_booster_collective_ms": (C.c_double, [P]),
     "fb_booster_set_stats": (None, [P, C.c_int32]),
     "fb_booster_model": (P, [P]),
     "fb_booster_margins": (C.c_int32, [P, f32p]),

@@ -206,6 +206,7 @@ TrainCtx::TrainCtx(const fbgpu_config& cfg) : cfg_(cfg) {
     FB_CUDA_CHECK(cudaEventCreate(&ev0_));
     FB_CUDA_CHECK(cudaEventCreate(&ev1_));
     for (auto& e : hev_) FB_CUDA_CHECK(cudaEventCreate(&e));
+    for (auto& e : hevc_) FB_CUDA_CHECK(cudaEventCreate(&e));
     level_stats_.alloc(16 * 16);
     n_ = cfg.n_rows;
     F_ = cfg.n_features;
@@ -246,6 +247,7 @@ TrainCtx::~TrainCtx() {
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
     for (auto& e : hev_) if (e) cudaEventDestroy(e);
+    for (auto& e : hevc_) if (e) cudaEventDestroy(e);
     if (s_) cudaStreamDestroy(s_);
 }
 
@@ -310,12 +312,8 @@ std::unique_ptr<TrainCtx::Block> TrainCtx::new_block(const uint32_t* feat_ids, u
 }
 
 void TrainCtx::register_block(std::unique_ptr<Block> b) {
-    // column-major copy for the partition passes (FBGPU_PART=rec keeps them on the records)
-    static const bool part_rec = [] {
-        const char* e = std::getenv("FBGPU_PART");
-        return e && std::string(e) == "rec";
-    }();
-    if (!part_rec && n_ > 0) {
+    // column-major copy for the partition passes, which read one bin per row
+    if (n_ > 0) {
         b->cols.alloc((size_t)n_ * b->feats.size() * b->width);
         launch_records_to_columns((int)b->width, b->base, b->stride, n_, (uint32_t)b->feats.size(), b->cols.as<uint8_t>(),
                                   s_);
@@ -633,22 +631,8 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     const uint32_t kLpfMaxBins = 440;    // 440 x 32 lanes x 16 B = 220 KiB
     const uint32_t kWideMaxBins = 1024;  // 1028 x 8 lanes x 16 B = 128.5 KiB
     const uint32_t kWideMaxChunks = 4;
-    static const bool force_tpr = [] {
-        const char* e = std::getenv("FBGPU_HIST");
-        return e && std::string(e) == "tpr";
-    }();
-    // FBGPU_HIST=lpf selects the unstaged lane-per-feature kernel (and no wide tiles)
-    static const bool no_stage = [] {
-        const char* e = std::getenv("FBGPU_HIST");
-        return e && std::string(e) == "lpf";
-    }();
-    static const bool no_wide = [] {
-        const char* e = std::getenv("FBGPU_WIDE");
-        return e && std::string(e) == "0";
-    }();
     auto is_wide = [&](uint32_t f, uint32_t width) {
-        return !force_tpr && !no_stage && !no_wide && width == 2 && nbins_[f] > kLpfMaxBins &&
-               nbins_[f] <= kWideMaxBins;
+        return width == 2 && nbins_[f] > kLpfMaxBins && nbins_[f] <= kWideMaxBins;
     };
     std::vector<TileDesc> gen[2], lpf[2], wide;
     std::vector<TileFeat> tf;
@@ -681,7 +665,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
             maxb = 0;
         };
         for (uint32_t f : b.feats) {
-            if (!en[f] || force_tpr || nbins_[f] > kLpfMaxBins) continue;
+            if (!en[f] || nbins_[f] > kLpfMaxBins) continue;
             if (cur.n_feat == 32) flush_lpf();
             tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
             maxb = std::max(maxb, nbins_[f]);
@@ -728,7 +712,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
             g.local_bins = 0;
         };
         for (uint32_t f : b.feats) {
-            if (!en[f] || !(force_tpr || nbins_[f] > kLpfMaxBins) || is_wide(f, b.width)) continue;
+            if (!en[f] || nbins_[f] <= kLpfMaxBins || is_wide(f, b.width)) continue;
             if (g.n_feat == 64 || g.local_bins + nbins_[f] > max_local) flush_gen();
             tf.push_back(TileFeat{feat_byte_[f], g.local_bins, nbins_[f], hoff_[f]});
             g.local_bins += nbins_[f];
@@ -758,7 +742,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     const size_t kMaxSmem = 227 * 1024;
     hist_stages_ = 0;
     tile_smem_stage_ = 0;
-    if (!no_stage && max_chunks > 0) {
+    if (max_chunks > 0) {
         for (int st : {4, 2}) {
             // + one discard row of 4 planes x 32 lanes
             const size_t need = smem_lpf + 512 + hist_stage_bytes(max_chunks, st);
@@ -916,17 +900,12 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         return;
     }
     LevelArgs a = level_args(tp);
-    static const bool no_fuse = [] {
-        const char* e = std::getenv("FBGPU_FUSE");
-        return e && std::string(e) == "0";
-    }();
-    if (!no_fuse) {
-        if (!fuse_.p) {
-            fuse_.alloc(16);
-            FB_CUDA_CHECK(cudaMemsetAsync(fuse_.p, 0, 16, s_));
-        }
-        a.fuse = fuse_.as<unsigned int>();
+    // the one-CTA level steps ride in the last CTA of the kernel before them
+    if (!fuse_.p) {
+        fuse_.alloc(16);
+        FB_CUDA_CHECK(cudaMemsetAsync(fuse_.p, 0, 16, s_));
     }
+    a.fuse = fuse_.as<unsigned int>();
     // Leaf values reach the margins either by one walk of the finished tree
     // per row (k_tree_walk; the last level then needs no partition) or per
     // partition chunk and k_leaf_final.  Measured on B200: the walk is faster
@@ -984,6 +963,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             FB_CUDA_CHECK(cudaMemcpyAsync(hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, sums_.p, 16,
                                           cudaMemcpyDeviceToDevice, s_));
         launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
+        if (stats_ && comm_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hevc_[d], s_));
         allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc + (root_rides ? 2 : 0), false);
         if (root_rides) {
             FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, 16,
@@ -994,24 +974,10 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         }
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
-        if (a.walk && a.last_level) {  // the last level's children are leaves: no partition
-            if (a.fuse) {
-                launch_split_decide(a, max_m, s_);
-            } else {
-                launch_split(a, max_m, s_);
-                launch_decide(a, s_);
-            }
-        } else if (a.fuse) {  // the one-CTA steps ride in the last CTA of the kernel before them
-            launch_split_decide(a, max_m, s_);
+        launch_split_decide(a, max_m, s_);
+        if (!(a.walk && a.last_level)) {  // with the walk, the last level's children need no partition
             launch_part_count(a, max_chunks, s_);
             launch_part_scatter(a, max_chunks, s_);
-        } else {
-            launch_split(a, max_m, s_);
-            launch_decide(a, s_);
-            launch_part_count(a, max_chunks, s_);
-            launch_part_scan(a, s_);
-            launch_part_scatter(a, max_chunks, s_);
-            launch_next_level(a, s_);
         }
         cur = 1 - cur;
     }
@@ -1042,6 +1008,11 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         for (uint32_t d = 0; d < std::min<uint32_t>(maxd, 15); d++) {
             float ms = 0.0f;
             FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
+            if (comm_) {
+                float cms = 0.0f;
+                FB_CUDA_CHECK(cudaEventElapsedTime(&cms, hevc_[d], hev_[2 * d + 1]));
+                comm_ms_ += cms;
+            }
             const uint64_t acc_nodes = lvl[2 * d] >> 32, rows = lvl[2 * d + 1];
             hist_ms_ += ms;
             hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) + (n_wide_ ? 1 : 0);

@@ -145,8 +145,10 @@ class TrainCtx {
     // (enabled by set_stats): device time, launches and algorithmic bytes
     // (rows x (bin bytes + 16 B gradient + 4 B row id) + bins x 16 B flushed).
     void set_stats(bool on) { stats_ = on; }
-    void reset_stats() { hist_ms_ = 0; hist_launches_ = 0; hist_bytes_ = 0; }
+    void reset_stats() { hist_ms_ = 0; hist_launches_ = 0; hist_bytes_ = 0; comm_ms_ = 0; }
     double hist_ms() const { return hist_ms_; }
+    // Of hist_ms: the device time of the per-level histogram all-reduces (sharded contexts).
+    double comm_ms() const { return comm_ms_; }
     double hist_launches() const { return hist_launches_; }
     double hist_bytes() const { return hist_bytes_; }
 
@@ -234,9 +236,10 @@ class TrainCtx {
     float last_tree_ms_ = 0.0f;
     bool stats_ = false;
     cudaEvent_t hev_[32] = {};
+    cudaEvent_t hevc_[16] = {};  // per level: histogram kernels done, all-reduce starts
     DevMem level_stats_;
     DevMem fuse_;  // last-CTA counters of the fused level kernels (depthwise)
-    double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0;
+    double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0, comm_ms_ = 0;
 };
 
 // Root-to-leaf path form of a model's trees for the path TreeSHAP kernel

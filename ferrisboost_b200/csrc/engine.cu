@@ -907,7 +907,6 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     cfg.max_depth = p.max_depth;
     cfg.max_leaves = p.max_leaves;
     cfg.gpu_math = p.gpu_math;
-    if (const char* e = std::getenv("FBGPU_HIST_SMEM")) cfg.hist_smem_bytes = (uint32_t)std::atoi(e);
     b->ctx.reset(new fbg::TrainCtx(cfg));
     if (sh.nranks > 1) {
         if (sh.comm) {
@@ -1369,6 +1368,8 @@ void fb_booster_timing(const fb_booster* h, double* out8) {
     out8[6] = b->ctx->hist_bytes();
     out8[7] = (double)b->rounds_done;
 }
+
+double fb_booster_collective_ms(const fb_booster* h) { return h->b->ctx->comm_ms(); }
 
 void fb_booster_set_stats(fb_booster* h, int32_t on) { h->b->ctx->set_stats(on != 0); }
 

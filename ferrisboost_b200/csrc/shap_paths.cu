@@ -504,11 +504,6 @@ void ShapPaths::upload(cudaStream_t s) {
         FB_CUDA_CHECK(cudaMemcpyAsync(d_masks.p, masks.data(), masks.size() * 4, cudaMemcpyHostToDevice, s));
 }
 
-// rows per thread of the launch (FBGPU_SHAP_ROWS=1 or 2)
-static int path_rows() {
-    const char* e = std::getenv("FBGPU_SHAP_ROWS");
-    return e && std::atoi(e) == 1 ? 1 : 2;
-}
 
 size_t ShapPaths::inter_smem_bytes(uint32_t F, uint32_t warps) {
     const size_t nc = F + 1;
@@ -556,7 +551,10 @@ void ShapPaths::launch_inter(const float* X, uint64_t n, uint32_t F, float bias,
 #undef FB_SI
 }
 
-size_t ShapPaths::smem_bytes(uint32_t F) { return (size_t)F * kPathThreads * path_rows() * (8 + 4) + kChunkBytes; }
+// two rows per thread: the path data read from shared memory serves two product chains
+constexpr int kPathRows = 2;
+
+size_t ShapPaths::smem_bytes(uint32_t F) { return (size_t)F * kPathThreads * kPathRows * (8 + 4) + kChunkBytes; }
 
 void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out,
                        cudaStream_t s) const {
@@ -566,7 +564,7 @@ void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int R = path_rows();
+    const int R = kPathRows;
     const uint64_t tiles = (n + (uint64_t)kPathThreads * R - 1) / ((uint64_t)kPathThreads * R);
 #define FB_SP(MM, KK, RR)                                                                                            \
     do {                                                                                                             \
@@ -579,11 +577,8 @@ void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float
             X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(), bias, root_mean, \
             out);                                                                                                    \
     } while (0)
-    if (M == 4) {
-        if (R == 2) FB_SP(4, 8, 2); else FB_SP(4, 8, 1);
-    } else {
-        if (R == 2) FB_SP(8, 14, 2); else FB_SP(8, 14, 1);
-    }
+    if (M == 4) FB_SP(4, 8, kPathRows);
+    else FB_SP(8, 14, kPathRows);
 #undef FB_SP
 }
 

@@ -1057,13 +1057,8 @@ __device__ void decide_body(const LevelArgs& a, uint32_t* wt) {
     }
 }
 
-__global__ void __launch_bounds__(1024) k_decide(LevelArgs a) {
-    __shared__ uint32_t wt[32];
-    decide_body<1024>(a, wt);
-}
-
 // k_split_node for 8 nodes per CTA (one warp each) with the level's decisions
-// (k_decide) run by the last CTA.
+// (decide_body) run by the last CTA.
 __global__ void __launch_bounds__(256) k_split_node_decide(LevelArgs a) {
     __shared__ uint32_t wt[32];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1321,15 +1316,9 @@ __device__ void next_level_body(const LevelArgs& a, unsigned long long* wt64, ui
     }
 }
 
-__global__ void __launch_bounds__(1024) k_next_level(LevelArgs a) {
-    __shared__ unsigned long long wt64[32];
-    __shared__ uint32_t wt[32];
-    next_level_body<1024>(a, wt64, wt);
-}
-
 // Partition passes; with a.fuse set (depthwise growth) the last CTA of the
 // count pass also scans the chunk counts (k_part_scan) and the last CTA of
-// the scatter pass builds the next level (k_next_level).
+// the scatter pass builds the next level (next_level_body).
 __global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
     part_count_work(a);
     if (a.fuse && last_block_done(a.fuse + 1)) {
@@ -1705,7 +1694,6 @@ void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
     count_launch();
     k_split_node<<<max_m, 32, 0, s>>>(a);
 }
-void launch_decide(const LevelArgs& a, cudaStream_t s) { count_launch(); k_decide<<<1, 1024, 0, s>>>(a); }
 void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
     dim3 grid(max_m, a.n_features);
     count_launch();
@@ -1722,7 +1710,6 @@ void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s
     count_launch();
     k_part_scatter<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
-void launch_next_level(const LevelArgs& a, cudaStream_t s) { count_launch(); k_next_level<<<1, 1024, 0, s>>>(a); }
 void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s) {
     if (n_rows == 0) return;
     count_launch();

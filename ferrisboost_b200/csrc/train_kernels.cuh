@@ -198,13 +198,11 @@ void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_
                        const unsigned long long* acc_prefix, const TreeState* st, Pair* hist_acc,
                        unsigned long long slot_pairs, uint32_t grid_x, size_t smem, cudaStream_t s);
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
-void launch_decide(const LevelArgs& a, cudaStream_t s);
 // k_split_feat, then per-node reduction and decisions in one launch (a.fuse set)
 void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_part_scan(const LevelArgs& a, cudaStream_t s);
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
-void launch_next_level(const LevelArgs& a, cudaStream_t s);
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 // Every local row walks the finished tree (a.trec / a.tcats) on its record's
 // bins and adds its leaf's value to its margin (training/mod.rs:5020-5063,

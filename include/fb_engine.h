@@ -158,6 +158,10 @@ int32_t fb_booster_update(fb_booster* b, uint32_t n_rounds);
  * while statistics are on (fb_booster_set_stats), which adds CUDA events
  * around every histogram phase. */
 void fb_booster_timing(const fb_booster* b, double* out8);
+/* Of the histogram device ms above: the device ms of the per-level histogram
+ * all-reduces of a row-sharded booster (0 on one GPU), while statistics are
+ * on.  No counterpart in the reference (it has no multi-GPU path). */
+double fb_booster_collective_ms(const fb_booster* b);
 void fb_booster_set_stats(fb_booster* b, int32_t on);
 fb_model* fb_booster_model(fb_booster* b);
 /* Current training margins of the booster's rows (host copy). */

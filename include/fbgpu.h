@@ -293,20 +293,28 @@ fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, u
  * callers that own every device allocation themselves and cannot call
  * cudaMalloc (the reference's Rust host keeps all allocation on its side,
  * src/backend/mod.rs:7-10).  All pointers are device pointers except `cats`
- * (8 host words, the right-going categories, or NULL for a numeric split
- * `bin < split bin goes left`).  `bins` is a row-major record matrix: the
- * feature's bin of row r is the `width`-byte value at bins + r*stride +
- * byte_off (missing = 255 / 65535).  Writes the left rows then the right rows
- * of `rows` to `out_rows` in input order, and the left count to *n_left.
- * Work is enqueued on `stream` (a cudaStream_t, NULL = default stream).
- * The kernels' scratch is one fixed 512 KiB static device array per device,
- * so at most 268435456 rows per call (larger requests fail with
- * FBGPU_EINPUT).  The first call on a device looks the array up
- * (cudaGetSymbolAddress); make that first call before any stream capture.
- * Every call shares the array: calls that overlap on the GPU race. */
+ * (8 host words, the right-going categories < 256, or NULL for a numeric
+ * split `bin < split bin goes left`).  `bins` is a row-major record matrix:
+ * the feature's bin of row r is the `width`-byte value at
+ * bins + r*stride + byte_off, and a row whose bin equals `missing_bin` is
+ * missing (the reference's layout: 255 for one byte, 65535 for two bytes;
+ * 0xFFFFFFFF for a feature that holds no missing value, such as a 256-bin
+ * feature stored in one byte).  For two-byte bins the records' address,
+ * stride and byte_off must be even; rows, out_rows and n_left 4-byte aligned;
+ * rows and out_rows must not overlap (no in-place partition).  Writes the left
+ * rows then the right rows of `rows` to `out_rows` in input order, and the
+ * left count to *n_left.  Work is enqueued on `stream` (a cudaStream_t of the
+ * current device, NULL = default stream).  The kernels' scratch is one fixed
+ * 512 KiB static device array per device, so at most 268435456 rows per call
+ * (larger requests, like every rule above, fail with FBGPU_EINPUT).  The
+ * first call on a device looks the array up (cudaGetSymbolAddress), and again
+ * the first call after the device's context was replaced (cudaDeviceReset);
+ * make those calls before any stream capture.  Every call shares the array:
+ * calls that overlap on the GPU race. */
 fbgpu_status fbgpu_partition_noalloc(const void* bins, uint32_t stride, uint32_t width, uint32_t byte_off,
-                                     const uint32_t* rows, uint64_t n, uint32_t bin, int32_t missing_left,
-                                     const uint32_t* cats, uint32_t* out_rows, uint32_t* n_left, void* stream);
+                                     uint32_t missing_bin, const uint32_t* rows, uint64_t n, uint32_t bin,
+                                     int32_t missing_left, const uint32_t* cats, uint32_t* out_rows,
+                                     uint32_t* n_left, void* stream);
 
 /* ---------------------------------------------------------- explanation models */
 

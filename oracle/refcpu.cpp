@@ -29,6 +29,7 @@
 #include <cstdint>
 #include <cstring>
 #include <limits>
+#include <memory>
 #include <queue>
 #include <stdexcept>
 #include <string>
@@ -1626,6 +1627,59 @@ uint32_t rc_model_num_outputs(void* m) {
     return M->class_margins.empty() ? 1u : (uint32_t)M->class_margins.size();
 }
 float rc_model_base_margin(void* m) { Model* M = (Model*)m; return base_margin(M->objective, M->base_score); }
+
+void* rc_model_load(uint32_t n_trees, const uint32_t* tree_off, const int32_t* left, const int32_t* right,
+                    const uint32_t* feat, const float* value, const uint8_t* default_left, const float* gain,
+                    const float* hess, const uint64_t* cat_off, const uint32_t* cat_len, const uint32_t* cats,
+                    uint32_t n_features, int32_t objective, float base_score, const float* class_margins,
+                    uint32_t num_class, float scale_pos_weight, const uint8_t* feature_types) {
+    try {
+        auto m = std::make_unique<Model>();
+        m->objective = objective;
+        m->base_score = base_score;
+        m->n_features = n_features;
+        m->scale_pos_weight = scale_pos_weight;
+        if (class_margins && num_class >= 2) m->class_margins.assign(class_margins, class_margins + num_class);
+        if (feature_types) m->feature_types.assign(feature_types, feature_types + n_features);
+        for (uint32_t t = 0; t < n_trees; t++) {
+            const uint32_t b = tree_off[t], e = tree_off[t + 1];
+            if (e <= b) throw std::runtime_error("a tree has no nodes");
+            Tree T;
+            T.nodes.resize(e - b);
+            for (uint32_t i = b; i < e; i++) {
+                Node& nd = T.nodes[i - b];
+                nd.left = left[i];
+                nd.right = right[i];
+                nd.is_leaf = left[i] < 0;
+                nd.default_left = default_left[i] != 0;
+                nd.gain = gain[i];
+                nd.hess = hess[i];
+                if (nd.is_leaf) {
+                    nd.leaf = value[i];
+                    continue;
+                }
+                if (left[i] >= (int32_t)(e - b) || right[i] < 0 || right[i] >= (int32_t)(e - b))
+                    throw std::runtime_error("child index out of range");
+                if (feat[i] >= n_features) throw std::runtime_error("split feature out of range");
+                nd.feat = feat[i];
+                nd.cond = value[i];
+                if (cat_len && cat_len[i]) {  // categorical.rs bitset: right-going codes
+                    nd.is_cat = true;
+                    for (uint32_t k = 0; k < cat_len[i]; k++) {
+                        const uint32_t c = cats[cat_off[i] + k];
+                        if (nd.cats.size() <= c / 32) nd.cats.resize(c / 32 + 1, 0u);
+                        nd.cats[c / 32] |= 1u << (c % 32);
+                    }
+                }
+            }
+            m->trees.push_back(std::move(T));
+        }
+        return m.release();
+    } catch (const std::exception& ex) {
+        g_err = ex.what();
+        return nullptr;
+    }
+}
 
 int64_t rc_model_json(void* m, char* buf, int64_t cap) {
     std::string s = model_json(*(Model*)m);

@@ -73,6 +73,19 @@ int64_t rc_model_tree(void* model, uint32_t t, uint32_t* feat, float* cond,
                       int32_t* left, int32_t* right, uint8_t* default_left,
                       float* leaf, uint8_t* is_leaf, float* gain, float* hess);
 float rc_model_base_margin(void* model);
+/* A model from the flat arrays of an XGBoost JSON document (parsed by the
+ * caller; model/tree.rs:760-960 is the reference's loader).  Tree t holds
+ * nodes [tree_off[t], tree_off[t+1]); a node with left < 0 is a leaf whose
+ * value is value[i], otherwise value[i] is its threshold.  Node i's
+ * right-going category codes are cats[cat_off[i] .. cat_off[i] + cat_len[i]]
+ * (cat_len 0: a numeric split).  class_margins holds num_class base margins
+ * for a multiclass model (else NULL).  feature_types: n_features flags
+ * (1 = categorical) or NULL.  Returns NULL with rc_last_error on bad input. */
+void* rc_model_load(uint32_t n_trees, const uint32_t* tree_off, const int32_t* left, const int32_t* right,
+                    const uint32_t* feat, const float* value, const uint8_t* default_left, const float* gain,
+                    const float* hess, const uint64_t* cat_off, const uint32_t* cat_len, const uint32_t* cats,
+                    uint32_t n_features, int32_t objective, float base_score, const float* class_margins,
+                    uint32_t num_class, float scale_pos_weight, const uint8_t* feature_types);
 void rc_predict_margin(void* model, const float* X, uint64_t n, float* out,
                        int32_t nthread);
 /* QuadratureTreeSHAP contributions: n x (F+1), bias last. */

@@ -1,5 +1,6 @@
 """ctypes binding of oracle/_build/librefcpu.so (test infrastructure only)."""
 import ctypes as C
+import json
 import math
 import os
 import pathlib
@@ -95,6 +96,12 @@ class RefCPU:
         lib.rc_sample_features.argtypes = [C.c_uint32, C.c_float, C.c_uint64, C.c_uint64, C.POINTER(C.c_uint32)]
         lib.rc_sample_features.restype = C.c_uint32
         lib.rc_rows_selected.argtypes = [C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.POINTER(C.c_uint8)]
+        lib.rc_model_load.restype = _P
+        lib.rc_model_load.argtypes = [C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                      C.POINTER(C.c_uint32), C.POINTER(C.c_float), C.POINTER(C.c_uint8),
+                                      C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_uint64),
+                                      C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.c_uint32, C.c_int32, C.c_float,
+                                      C.POINTER(C.c_float), C.c_uint32, C.c_float, C.POINTER(C.c_uint8)]
         self.lib = lib
 
     # ---------------------------------------------------------------- params
@@ -139,6 +146,72 @@ class RefCPU:
         if not h:
             raise RuntimeError(self.lib.rc_last_error().decode())
         return RefModel(self, h, X.shape[1])
+
+    def load_json(self, doc):
+        """A model from XGBoost JSON text (bytes or str): the document's tree
+        arrays are parsed here and handed to rc_model_load.  Used to explain or
+        predict with a model trained elsewhere (the device engine) on the
+        oracle; writing it back with json() reproduces the document."""
+        d = json.loads(doc)
+        learner = d["learner"]
+        trees = learner["gradient_booster"]["model"]["trees"]
+        obj_name = learner["objective"]["name"]
+        objective = OBJECTIVES.get(obj_name, 0 if obj_name == "reg:linear" else None)
+        if objective is None:
+            raise ValueError(f"objective {obj_name!r} is not supported by the oracle")
+        nf = int(learner["learner_model_param"]["num_feature"])
+        num_class = int(learner["learner_model_param"].get("num_class", "0"))
+        base = learner["learner_model_param"]["base_score"]
+        margins = None
+        if base.startswith("["):
+            margins = np.array([float(v) for v in base.strip("[]").split(",")], dtype=np.float32)
+            base_score = 0.5
+        else:
+            base_score = float(base)
+        spw = float(learner["objective"].get("reg_loss_param", {}).get("scale_pos_weight", "1"))
+        ft = learner.get("feature_types") or []
+        ftypes = np.array([t == "c" for t in ft], np.uint8) if ft else None
+        off = [0]
+        cols = {k: [] for k in ("left", "right", "feat", "value", "dl", "gain", "hess")}
+        cat_off, cat_len, cats = [], [], []
+        for t in trees:
+            nn = len(t["left_children"])
+            off.append(off[-1] + nn)
+            cols["left"] += t["left_children"]
+            cols["right"] += t["right_children"]
+            cols["feat"] += t["split_indices"]
+            cols["value"] += t["split_conditions"]
+            cols["dl"] += t["default_left"]
+            cols["gain"] += t["loss_changes"]
+            cols["hess"] += t["sum_hessian"]
+            per_node = {}
+            for node, seg, size in zip(t["categories_nodes"], t["categories_segments"], t["categories_sizes"]):
+                per_node[node] = t["categories"][seg:seg + size]
+            for i in range(nn):
+                codes = per_node.get(i, [])
+                cat_off.append(len(cats))
+                cat_len.append(len(codes))
+                cats += codes
+        arr = {
+            "left": np.array(cols["left"], np.int32), "right": np.array(cols["right"], np.int32),
+            "feat": np.array(cols["feat"], np.uint32), "value": np.array(cols["value"], np.float32),
+            "dl": np.array(cols["dl"], np.uint8), "gain": np.array(cols["gain"], np.float32),
+            "hess": np.array(cols["hess"], np.float32),
+        }
+        toff = np.array(off, np.uint32)
+        coff = np.array(cat_off, np.uint64)
+        clen = np.array(cat_len, np.uint32)
+        carr = np.array(cats if cats else [0], np.uint32)
+        h = self.lib.rc_model_load(len(trees), _ptr(toff, C.c_uint32), _ptr(arr["left"], C.c_int32),
+                                   _ptr(arr["right"], C.c_int32), _ptr(arr["feat"], C.c_uint32),
+                                   _ptr(arr["value"], C.c_float), _ptr(arr["dl"], C.c_uint8),
+                                   _ptr(arr["gain"], C.c_float), _ptr(arr["hess"], C.c_float),
+                                   _ptr(coff, C.c_uint64), _ptr(clen, C.c_uint32), _ptr(carr, C.c_uint32), nf,
+                                   objective, base_score, _ptr(margins, C.c_float),
+                                   num_class if margins is not None else 0, spw, _ptr(ftypes, C.c_uint8))
+        if not h:
+            raise ValueError(self.lib.rc_last_error().decode())
+        return RefModel(self, h, nf)
 
     def softmax_gradients(self, margins, y, w=None):
         """margins K x n (class-major) -> K x n x 2 (g, h)."""

@@ -128,7 +128,10 @@ def test_fast_mode_within_tolerance(oracle):
 
     assert abs(logloss(a) - logloss(b)) < 1e-4
     pa, pb = 1 / (1 + np.exp(-a)), 1 / (1 + np.exp(-b))
-    assert np.median(np.abs(pa - pb) / np.abs(pb)) < 1e-5
+    rel = np.abs(pa - pb) / np.abs(pb)
+    # north_star: fast-mode predictions within 1e-5 relative of exact mode, every row
+    assert rel.max() <= 1e-5, (f"max {rel.max():.3e}, p99 {np.quantile(rel, 0.99):.3e}, "
+                               f"median {np.median(rel):.3e}, rows over {np.count_nonzero(rel > 1e-5)}")
 
 
 def test_predict_and_shap_match_oracle(oracle):

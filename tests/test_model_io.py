@@ -46,6 +46,12 @@ def test_oracle_model_round_trips(oracle, kind):
     assert m.to_json() == js
     assert m.num_trees == ref.num_trees
     assert m.num_outputs == ref.num_outputs
+    # the oracle's own loader (used to explain device-trained models on the
+    # CPU) reads the document back to the same trees
+    back = oracle.load_json(js)
+    assert back.json() == js
+    assert np.array_equal(back.predict_margin(X).view(np.uint32), ref.predict_margin(X).view(np.uint32))
+    assert np.array_equal(back.shap(X[:200]).view(np.uint32), ref.shap(X[:200]).view(np.uint32))
 
 
 def test_feature_names_and_file_round_trip(oracle, tmp_path):
