@@ -56,6 +56,7 @@ class FbgpuTreeOut(C.Structure):
     _fields_ = [
         ("capacity", C.c_uint32), ("n_nodes", C.c_uint32), ("left", i32p), ("right", i32p), ("feat", u32p),
         ("bin", u32p), ("gain", f32p), ("leaf", f32p), ("hess", f32p), ("flags", u32p), ("cats", u32p),
+        ("cat_words", C.c_uint32), ("reserved", C.c_uint32),
     ]
 
 
@@ -96,6 +97,9 @@ SIGNATURES = {
     "fbgpu_eval_split": (C.c_int, [P, i64p, i64p, f64p, C.POINTER(FbgpuTreeParams), C.c_float, C.c_float, u8p,
                                    C.POINTER(FbgpuSplit)]),
     "fbgpu_partition": (C.c_int, [P, u32p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_int32, u32p, u32p, u64p]),
+    "fbgpu_partition_set": (C.c_int, [P, u32p, C.c_uint64, C.c_uint32, C.c_int32, u32p, C.c_uint32, u32p, u64p]),
+    "fbgpu_ctx_cat_words": (C.c_uint32, [P]),
+    "fbgpu_split_cats": (C.c_int, [P, u32p, C.c_uint32]),
     "fbgpu_partition_noalloc": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint64,
                                          C.c_uint32, C.c_int32, u32p, P, P, P]),
     "fbgpu_model_create": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, u32p, i32p, i32p, u32p, f32p, u8p, f32p,
@@ -149,6 +153,7 @@ SIGNATURES = {
     "fb_model_num_features": (C.c_uint32, [P]),
     "fb_model_base_margin": (C.c_float, [P]),
     "fb_model_json": (C.c_int64, [P, C.c_char_p, C.c_int64]),
+    "fb_model_node_cats": (C.c_int64, [P, C.c_uint32, C.c_uint32, u32p, C.c_uint32]),
     "fb_model_tree": (C.c_int64, [P, C.c_uint32, i32p, i32p, u32p, f32p, u8p, f32p, u8p, f32p, f32p, u32p]),
     "fb_model_create": (P, [C.c_uint32, C.c_int32, C.c_float, C.c_float, C.c_uint32, f32p, u8p, C.c_uint32, u32p,
                             i32p, i32p, u32p, f32p, u8p, f32p, f32p, f32p, u8p, u32p, u32p, u32p, C.c_uint64]),

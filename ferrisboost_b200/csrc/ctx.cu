@@ -263,15 +263,27 @@ void TrainCtx::set_features(const uint32_t* n_bins, const uint8_t* width, const 
         }
     }
     hoff_.assign(F_ + 1, 0);
+    cat_slot_.assign(F_, 0);
+    n_cat_ = 0;
+    cat_words_ = 8;
     for (uint32_t f = 0; f < F_; f++) {
         if (width_[f] != 1 && width_[f] != 2) throw InputError("bin width must be 1 or 2 bytes");
         if (width_[f] == 1 && nbins_[f] > 256) throw InputError("one-byte bins hold at most 256 bins");
         if (nbins_[f] == 0) throw InputError("a feature has at least one bin");
-        if (nbins_[f] > 1024) throw InputError("device split search supports at most 1024 bins per feature");
-        if (cat_[f] && nbins_[f] > 256) throw InputError("device categorical splits support at most 256 categories");
+        if (cat_[f]) {
+            // codes 0..65533 (categorical.rs:19-28 MAX_CAT_CODE_WIDE); 65535 is the missing sentinel
+            if (nbins_[f] > 65534) throw InputError("a categorical feature has at most 65534 bins (codes 0..65533)");
+            cat_slot_[f] = n_cat_++;
+            cat_words_ = std::max<uint32_t>(cat_words_, (nbins_[f] + 31) / 32);
+        } else if (nbins_[f] > 1024) {
+            throw InputError("device split search supports at most 1024 bins per numeric feature");
+        }
         hoff_[f + 1] = hoff_[f] + nbins_[f];
     }
     total_bins_ = hoff_[F_];
+    d_cat_slot_.alloc(4ull * F_);
+    FB_CUDA_CHECK(cudaMemcpyAsync(d_cat_slot_.p, cat_slot_.data(), 4ull * F_, cudaMemcpyHostToDevice, s_));
+    last_split_cats_.assign(cat_words_, 0u);
     d_hoff_.alloc(4 * (F_ + 1));
     FB_CUDA_CHECK(cudaMemcpyAsync(d_hoff_.p, hoff_.data(), 4 * (F_ + 1), cudaMemcpyHostToDevice, s_));
     d_cat_.alloc(F_);
@@ -282,7 +294,8 @@ void TrainCtx::set_features(const uint32_t* n_bins, const uint8_t* width, const 
     d_floc_.alloc(sizeof(FeatLoc) * F_);
     d_floc_rec_.alloc(sizeof(FeatLoc) * F_);
     tiles_valid_ = false;
-    buf_depth_ = 0xffffffffu;  // histogram slots depend on total_bins
+    buf_depth_ = 0xffffffffu;  // histogram slots and category sets depend on the features
+    lg_leaves_ = 0xffffffffu;
     ensure_tree_buffers(cfg_.max_depth, cfg_.max_leaves);
     sync();
 }
@@ -598,10 +611,11 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
         hist_[i].alloc(lossguide && i == 1 ? 16 : 16 * tb * split_nodes);
     }
     hist_acc_.alloc(16 * tb * acc + 16);  // + the root sum riding on the root's allreduce
+    const uint64_t set_bytes = 4ull * cat_words_;
     feat_best_.alloc(sizeof(SplitRec) * split_nodes * F_);
-    feat_cats_.alloc(32 * split_nodes * F_);
+    feat_cats_.alloc(set_bytes * split_nodes * std::max<uint32_t>(n_cat_, 1));
     node_best_.alloc(sizeof(SplitRec) * split_nodes);
-    node_cats_.alloc(32 * std::max<uint64_t>(lvl, 1));
+    node_cats_.alloc(set_bytes * std::max<uint64_t>(lvl, 1));
     FB_CUDA_CHECK(cudaMemsetAsync(node_cats_.p, 0, node_cats_.bytes, s_));
     split_.alloc(sizeof(SplitDesc) * lvl);
     chunk_left_.alloc(4 * (uint64_t)max_chunks_);
@@ -610,9 +624,9 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
     node_left_.alloc(4 * lvl);
     node_left_global_.alloc(4 * lvl);
     trec_.alloc(sizeof(TreeRec) * tree_nodes);
-    tcats_.alloc(32 * tree_nodes);
+    tcats_.alloc(set_bytes * tree_nodes);
     state_.alloc(sizeof(TreeState));
-    h_tree_.reserve(sizeof(TreeRec) * tree_nodes + 32 * tree_nodes + sizeof(TreeState));
+    h_tree_.reserve(sizeof(TreeRec) * tree_nodes + set_bytes * tree_nodes + sizeof(TreeState));
     buf_depth_ = max_depth;
     buf_leaves_ = max_leaves;
     buf_lossguide_ = lossguide;
@@ -634,7 +648,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     auto is_wide = [&](uint32_t f, uint32_t width) {
         return width == 2 && nbins_[f] > kLpfMaxBins && nbins_[f] <= kWideMaxBins;
     };
-    std::vector<TileDesc> gen[2], lpf[2], wide;
+    std::vector<TileDesc> gen[2], lpf[2], wide, direct[2];
     std::vector<TileFeat> tf;
     size_t smem_gen = 16, smem_lpf = 16, smem_wide = 16;
     uint32_t max_chunks = 0, max_chunks_wide = 0;
@@ -712,20 +726,38 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
             g.local_bins = 0;
         };
         for (uint32_t f : b.feats) {
-            if (!en[f] || nbins_[f] <= kLpfMaxBins || is_wide(f, b.width)) continue;
+            if (!en[f] || nbins_[f] <= kLpfMaxBins || nbins_[f] > max_local || is_wide(f, b.width)) continue;
             if (g.n_feat == 64 || g.local_bins + nbins_[f] > max_local) flush_gen();
             tf.push_back(TileFeat{feat_byte_[f], g.local_bins, nbins_[f], hoff_[f]});
             g.local_bins += nbins_[f];
             g.n_feat++;
         }
         flush_gen();
+        // features with more bins than the shared-memory budget (categorical
+        // features of many codes): tiles without a shared histogram, updates
+        // added to the node histogram directly
+        TileDesc dt{b.base, b.stride, b.width, (uint32_t)tf.size(), 0, 0, miss};
+        for (uint32_t f : b.feats) {
+            if (!en[f] || nbins_[f] <= max_local || is_wide(f, b.width)) continue;
+            if (dt.n_feat == 64) {
+                direct[wi].push_back(dt);
+                dt.feat_begin = (uint32_t)tf.size();
+                dt.n_feat = 0;
+            }
+            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
+            dt.n_feat++;
+        }
+        if (dt.n_feat) direct[wi].push_back(dt);
     }
+    for (int w = 0; w < 2; w++)
+        for (const TileDesc& t : direct[w]) smem_gen = std::max(smem_gen, (size_t)t.n_feat * sizeof(TileFeat));
     std::vector<TileDesc> all;
     for (int w = 0; w < 2; w++) { tile_off_gen_[w] = (uint32_t)all.size(); n_gen_[w] = (uint32_t)gen[w].size(); all.insert(all.end(), gen[w].begin(), gen[w].end()); }
     for (int w = 0; w < 2; w++) { tile_off_lpf_[w] = (uint32_t)all.size(); n_lpf_[w] = (uint32_t)lpf[w].size(); all.insert(all.end(), lpf[w].begin(), lpf[w].end()); }
     tile_off_wide_ = (uint32_t)all.size();
     n_wide_ = (uint32_t)wide.size();
     all.insert(all.end(), wide.begin(), wide.end());
+    for (int w = 0; w < 2; w++) { tile_off_direct_[w] = (uint32_t)all.size(); n_direct_[w] = (uint32_t)direct[w].size(); all.insert(all.end(), direct[w].begin(), direct[w].end()); }
     d_tiles_.alloc(sizeof(TileDesc) * std::max<size_t>(all.size(), 1));
     d_tfeat_.alloc(sizeof(TileFeat) * std::max<size_t>(tf.size(), 1));
     if (!all.empty())
@@ -788,6 +820,10 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
                             acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf, tile_smem_lpf_,
                             s_);
     }
+    for (int w = 0; w < 2; w++)
+        if (n_direct_[w])
+            launch_hist(w + 1, T + tile_off_direct_[w], n_direct_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
+                        acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_gen, tile_smem_, s_);
     if (n_wide_) {
         const uint32_t grid_wide = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u));
         launch_hist_wide(wide_stages_, T + tile_off_wide_, n_wide_, TF, rows, fixed_.as<Pair>(), nodes, acc_list,
@@ -814,6 +850,9 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.hist_acc = hist_acc_.as<Pair>();
     a.slot_pairs = std::max<uint64_t>(total_bins_, 1);
     a.feat_best = feat_best_.as<SplitRec>();
+    a.cat_words = cat_words_;
+    a.cat_slot = d_cat_slot_.as<uint32_t>();
+    a.n_cat = n_cat_;
     a.feat_cats = feat_cats_.as<uint32_t>();
     a.node_best = node_best_.as<SplitRec>();
     a.node_cats = node_cats_.as<uint32_t>();
@@ -991,12 +1030,14 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
     FB_CUDA_CHECK(cudaGetLastError());
     FB_CUDA_CHECK(cudaEventRecord(ev1_, s_));
+    const uint32_t W = cat_words_;
     TreeRec* hrec = h_tree_.as<TreeRec>();
     uint32_t* hcats = reinterpret_cast<uint32_t*>(hrec + max_tree_nodes_);
-    TreeState* hst = reinterpret_cast<TreeState*>(hcats + 8ull * max_tree_nodes_);
+    TreeState* hst = reinterpret_cast<TreeState*>(hcats + (size_t)W * max_tree_nodes_);
     FB_CUDA_CHECK(cudaMemcpyAsync(hst, state_.p, sizeof(TreeState), cudaMemcpyDeviceToHost, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(hrec, trec_.p, sizeof(TreeRec) * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
-    if (has_cat_) FB_CUDA_CHECK(cudaMemcpyAsync(hcats, tcats_.p, 32ull * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
+    if (has_cat_)
+        FB_CUDA_CHECK(cudaMemcpyAsync(hcats, tcats_.p, 4ull * W * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
     uint64_t* lvl = h_small_.as<uint64_t>() + 32;  // 16 levels x 16 bytes
     if (stats_) FB_CUDA_CHECK(cudaMemcpyAsync(lvl, level_stats_.p, 16 * 16, cudaMemcpyDeviceToHost, s_));
     sync();
@@ -1015,7 +1056,8 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             }
             const uint64_t acc_nodes = lvl[2 * d] >> 32, rows = lvl[2 * d + 1];
             hist_ms_ += ms;
-            hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) + (n_wide_ ? 1 : 0);
+            hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) +
+                              (n_wide_ ? 1 : 0) + (n_direct_[0] ? 1 : 0) + (n_direct_[1] ? 1 : 0);
             hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
         }
     }
@@ -1023,6 +1065,9 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     if (nn == 0 || nn > max_tree_nodes_) throw std::runtime_error("device tree has an invalid node count");
     if (!out) return;
     if (out->capacity < nn) throw InputError("fbgpu_tree_out capacity is smaller than the tree");
+    const uint32_t out_w = out->cat_words ? out->cat_words : 8u;
+    if (out->cats && out_w < W)
+        throw InputError("fbgpu_tree_out.cat_words is smaller than the context's category sets (fbgpu_ctx_cat_words)");
     out->n_nodes = nn;
     // lossguide: the same splits, numbered in best-first pop order
     std::vector<uint32_t> old_of_new, new_of_old;
@@ -1040,7 +1085,8 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         if (out->hess) out->hess[i] = r.hess;
         if (out->flags) out->flags[i] = r.flags;
         if (out->cats) {
-            for (int w = 0; w < 8; w++) out->cats[i * 8 + w] = (r.flags & 4u) ? hcats[ci * 8 + w] : 0u;
+            for (uint32_t w = 0; w < out_w; w++)
+                out->cats[(size_t)i * out_w + w] = (r.flags & 4u) && w < W ? hcats[(size_t)ci * W + w] : 0u;
         }
     }
 }
@@ -1113,10 +1159,12 @@ void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const do
     launch_split(a, 1, s_);
     FB_CUDA_CHECK(cudaGetLastError());
     SplitRec r;
-    uint32_t cats[8];
+    last_split_cats_.assign(cat_words_, 0u);
     FB_CUDA_CHECK(cudaMemcpyAsync(&r, node_best_.p, sizeof r, cudaMemcpyDeviceToHost, s_));
-    FB_CUDA_CHECK(cudaMemcpyAsync(cats, node_cats_.p, 32, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(last_split_cats_.data(), node_cats_.p, 4ull * cat_words_, cudaMemcpyDeviceToHost,
+                                  s_));
     sync();
+    const uint32_t* cats = last_split_cats_.data();
     std::memset(out, 0, sizeof *out);
     out->found = r.flags & 1u;
     if (!out->found) return;
@@ -1128,10 +1176,11 @@ void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const do
     out->left_grad = r.left.g; out->left_hess = r.left.h;
     out->right_grad = r.right.g; out->right_hess = r.right.h;
     if (out->categorical) std::memcpy(out->cats, cats, 32);
+    else std::fill(last_split_cats_.begin(), last_split_cats_.end(), 0u);
 }
 
 void TrainCtx::partition(const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin, int missing_left,
-                         const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left) {
+                         const uint32_t* cats, uint32_t n_cat_words, uint32_t* out_rows, uint64_t* n_left) {
     ensure_features();
     if (feat >= F_) throw InputError("feature id out of range");
     if (n > n_) throw InputError("more rows than the context holds");
@@ -1140,14 +1189,17 @@ void TrainCtx::partition(const uint32_t* rows, uint64_t n, uint32_t feat, uint32
     NodeInfo ni{};
     ni.start = 0; ni.len = (uint32_t)n; ni.tree_id = 0; ni.parent_slot = -1;
     SplitDesc sd{0, feat, bin, (missing_left ? 2u : 0u) | (cats ? 4u : 0u)};
-    uint32_t cw[8] = {0};
-    if (cats) std::memcpy(cw, cats, 32);
+    if (cats && n_cat_words > cat_words_)
+        for (uint32_t w = cat_words_; w < n_cat_words; w++)
+            if (cats[w]) throw InputError("the category set holds codes beyond this context's widest feature");
+    std::vector<uint32_t> cw(cat_words_, 0u);
+    if (cats) std::memcpy(cw.data(), cats, 4ull * std::min(n_cat_words, cat_words_));
     uint32_t cp[2] = {0, ceil_div(n, kChunkRows)};
     TreeState st{};
     st.m = 1; st.chunk_count = cp[1];
     FB_CUDA_CHECK(cudaMemcpyAsync(nodes_[0].p, &ni, sizeof ni, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(split_.p, &sd, sizeof sd, cudaMemcpyHostToDevice, s_));
-    FB_CUDA_CHECK(cudaMemcpyAsync(node_cats_.p, cw, 32, cudaMemcpyHostToDevice, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(node_cats_.p, cw.data(), 4ull * cat_words_, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(chunk_prefix_[0].p, cp, 8, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(state_.p, &st, sizeof st, cudaMemcpyHostToDevice, s_));
     fbgpu_tree_params tp{};
@@ -1354,7 +1406,6 @@ void ExplainModel::explain_device(int kind, const float* X, uint64_t n, float* o
     if (kind == 0) {
         launch_pred_leaf(dm_, X, n, out, s);
     } else if (kind == 1) {
-        if (approx_smem_bytes(F_) > 227 * 1024) throw InputError("approx_contribs on the device supports at most 221 features");
         if (!means_.p) {
             std::vector<float> means(std::max<size_t>(h_nodes_.size(), 1), 0.0f);
             for (uint32_t t = 0; t < T_; t++) node_means(h_nodes_, h_tree_off_[t], 0, means);
@@ -1366,8 +1417,7 @@ void ExplainModel::explain_device(int kind, const float* X, uint64_t n, float* o
     } else {
         ensure_paths();
         if (!paths_.supported)
-            throw InputError("pred_interactions on the device supports category sets below 256 codes and at most 14 "
-                             "features on a path");
+            throw InputError("pred_interactions on the device supports at most 14 features on a path");
         paths_.launch_inter(X, n, F_, base_margin_, root_mean_, out, s);
     }
     FB_CUDA_CHECK(cudaGetLastError());
@@ -1526,7 +1576,23 @@ fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t
 }
 fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
                              int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left) {
-    return guard(ctx, [&] { ctx->impl.partition(rows, n, feat, bin, missing_left, cats, out_rows, n_left); });
+    return guard(ctx, [&] { ctx->impl.partition(rows, n, feat, bin, missing_left, cats, 8, out_rows, n_left); });
+}
+fbgpu_status fbgpu_partition_set(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, int32_t missing_left,
+                                 const uint32_t* cats, uint32_t n_words, uint32_t* out_rows, uint64_t* n_left) {
+    return guard(ctx, [&] {
+        if (!cats) throw fbg::InputError("a category set is required");
+        ctx->impl.partition(rows, n, feat, 0, missing_left, cats, n_words, out_rows, n_left);
+    });
+}
+uint32_t fbgpu_ctx_cat_words(const fbgpu_ctx* ctx) { return ctx ? ctx->impl.cat_words() : 0u; }
+fbgpu_status fbgpu_split_cats(fbgpu_ctx* ctx, uint32_t* out, uint32_t n_words) {
+    return guard(ctx, [&] {
+        const std::vector<uint32_t>& c = ctx->impl.last_split_cats();
+        for (uint32_t w = 0; w < n_words; w++) out[w] = w < c.size() ? c[w] : 0u;
+        for (size_t w = n_words; w < c.size(); w++)
+            if (c[w]) throw fbg::InputError("the category set needs fbgpu_ctx_cat_words words");
+    });
 }
 
 uint64_t fbgpu_launch_count(void) { return fbg::g_launches.load(std::memory_order_relaxed); }

@@ -130,8 +130,14 @@ class TrainCtx {
     void histogram(const uint32_t* rows, uint64_t n_sel, const int64_t* fixed, int64_t* out);
     void eval_split(const int64_t* hist, const int64_t* node_sum, const double* scales, const fbgpu_tree_params& tp,
                     float lower, float upper, const uint8_t* enabled, fbgpu_split* out);
+    // cats: n_cat_words words (NULL: numeric split); words beyond them are zero
     void partition(const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin, int missing_left,
-                   const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left);
+                   const uint32_t* cats, uint32_t n_cat_words, uint32_t* out_rows, uint64_t* n_left);
+    // Words of a category set in this context: 8, or enough for the widest
+    // categorical feature (a bit per code).
+    uint32_t cat_words() const { return cat_words_; }
+    // The full category set of the last eval_split (cat_words() words).
+    const std::vector<uint32_t>& last_split_cats() const { return last_split_cats_; }
 
     // Internal access for the engine (same library).
     cudaStream_t stream() const { return s_; }
@@ -187,9 +193,12 @@ class TrainCtx {
     std::vector<int> feat_block_;
     std::vector<uint32_t> feat_byte_;
     bool has_cat_ = false;
+    uint32_t cat_words_ = 8, n_cat_ = 0;  // set width (words) and categorical feature count
+    std::vector<uint32_t> cat_slot_;      // per feature: index among the categorical features
+    std::vector<uint32_t> last_split_cats_;
 
     // feature tables
-    DevMem d_hoff_, d_floc_, d_floc_rec_, d_enabled_, d_mono_, d_cat_;
+    DevMem d_hoff_, d_floc_, d_floc_rec_, d_enabled_, d_mono_, d_cat_, d_cat_slot_;
     std::vector<uint8_t> last_enabled_;
     std::vector<int8_t> last_mono_;
     bool tiles_valid_ = false;
@@ -198,6 +207,7 @@ class TrainCtx {
     size_t tile_smem_ = 0, tile_smem_lpf_ = 0, tile_smem_stage_ = 0;
     int hist_stages_ = 0;  // staged lane-per-feature histogram: cp.async stages, 0 = unstaged kernel
     uint32_t tile_off_wide_ = 0, n_wide_ = 0;  // wide tiles (8 lanes per row)
+    uint32_t tile_off_direct_[2] = {0, 0}, n_direct_[2] = {0, 0};  // global-atomic tiles (no shared histogram)
     size_t tile_smem_wide_ = 0;
     int wide_stages_ = 4;
     int smem_budget_ = 0;
@@ -249,6 +259,7 @@ struct ShapPaths {
     int M = 4, KMAX = 8;              // quadrature points, features per path (kernel template)
     bool supported = false;           // false: a path the kernel cannot represent (use the DFS kernel)
     uint32_t n_elems = 0;
+    uint32_t mask_words = 8;          // words of a category mask (a bit per code)
     std::vector<uint32_t> words, chunk_off, masks;
     DevMem d_words, d_chunks, d_masks;
     void build(const std::vector<DevNode>& nodes, const uint32_t* tree_off, uint32_t n_trees, uint32_t F,
@@ -260,6 +271,7 @@ struct ShapPaths {
     // SHAP interaction values over the same paths (warp per row)
     float rule_w8[8] = {};
     DevMem d_rule_w;
+    DevMem d_inter_scratch;           // interactions of models too wide for a shared-memory matrix
     static size_t inter_smem_bytes(uint32_t F, uint32_t warps);
     static uint32_t inter_warps(uint32_t F);
     void launch_inter(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out, cudaStream_t s);

@@ -938,7 +938,8 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     }
     const uint32_t cap = (2u << p.max_depth);
     b->o_left.resize(cap); b->o_right.resize(cap); b->o_feat.resize(cap); b->o_bin.resize(cap);
-    b->o_flags.resize(cap); b->o_cats.resize(8ull * cap); b->o_gain.resize(cap); b->o_leaf.resize(cap);
+    b->o_flags.resize(cap); b->o_cats.resize((size_t)b->ctx->cat_words() * cap); b->o_gain.resize(cap);
+    b->o_leaf.resize(cap);
     b->o_hess.resize(cap);
     return b.release();
 }
@@ -1058,7 +1059,10 @@ fbgpu_tree_out tree_out(Booster& b) {
     out.capacity = (uint32_t)b.o_left.size();
     out.left = b.o_left.data(); out.right = b.o_right.data(); out.feat = b.o_feat.data(); out.bin = b.o_bin.data();
     out.gain = b.o_gain.data(); out.leaf = b.o_leaf.data(); out.hess = b.o_hess.data(); out.flags = b.o_flags.data();
+    const uint32_t W = b.ctx->cat_words();
+    if (b.o_cats.size() != (size_t)W * out.capacity) b.o_cats.assign((size_t)W * out.capacity, 0u);
     out.cats = b.o_cats.data();
+    out.cat_words = W;
     return out;
 }
 
@@ -1075,7 +1079,7 @@ Tree assemble_tree(const Booster& b, const fbgpu_tree_out& out) {
         nd.default_left = (fl & 2u) != 0; nd.gain = out.gain[i]; nd.leaf = 0.0f;
         nd.is_cat = (fl & 4u) != 0;
         if (nd.is_cat) {
-            nd.cats.assign(out.cats + 8ull * i, out.cats + 8ull * i + 8);
+            nd.cats.assign(out.cats + (size_t)out.cat_words * i, out.cats + (size_t)out.cat_words * (i + 1));
             while (!nd.cats.empty() && nd.cats.back() == 0) nd.cats.pop_back();
             nd.cond = std::numeric_limits<float>::denorm_min();  // tree.rs:22 CATEGORICAL_SPLIT_COND
         } else {
@@ -1521,6 +1525,14 @@ int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* rig
         if (cats) for (int w = 0; w < 8; w++) cats[i * 8 + w] = w < (int)nd.cats.size() ? nd.cats[w] : 0u;
     }
     return (int64_t)N.size();
+}
+
+int64_t fb_model_node_cats(const fb_model* m, uint32_t t, uint32_t node, uint32_t* out, uint32_t cap) {
+    if (t >= m->trees.size() || node >= m->trees[t].nodes.size()) return -1;
+    const fbe::Node& nd = m->trees[t].nodes[node];
+    if (!nd.is_cat) return 0;
+    for (uint32_t w = 0; w < cap && w < nd.cats.size(); w++) out[w] = nd.cats[w];
+    return (int64_t)nd.cats.size();
 }
 
 int32_t fb_model_predict(fb_model* m, const float* X, uint64_t n, float* out, int32_t device) {

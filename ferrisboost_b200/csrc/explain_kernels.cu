@@ -270,10 +270,74 @@ void launch_pred_leaf(const DevModel& m, const float* X, uint64_t n, float* out,
     k_pred_leaf<<<(unsigned)blocks, 256, 0, s>>>(m, X, n, out);
 }
 
+// The same for models with more features than shared memory holds per row:
+// the row's totals accumulate in its output row (global memory, the same f32
+// additions in the same order) and a tree's deltas in a few per-thread slots,
+// one per feature on the path, visited in the order the shared-memory kernel
+// visits its columns.
+__global__ void __launch_bounds__(kApproxThreads) k_pred_approx_wide(DevModel m, const float* __restrict__ means,
+                                                                     const float* __restrict__ X, uint64_t n,
+                                                                     float bias, float* __restrict__ out) {
+    const uint32_t F = m.n_features, nc = F + 1;
+    for (uint64_t r = (uint64_t)blockIdx.x * kApproxThreads + threadIdx.x; r < n;
+         r += (uint64_t)gridDim.x * kApproxThreads) {
+        const float* x = X + r * F;
+        float* o = out + r * nc;
+        for (uint32_t c = 0; c < F; c++) o[c] = 0.0f;
+        float pb = 0.0f;  // bias column total
+        for (uint32_t tr = 0; tr < m.n_trees; tr++) {
+            const uint32_t base = m.tree_off[tr];
+            float node_value = means[base];
+            const float tb = __fadd_rn(0.0f, node_value);
+            uint32_t touched[kMaxShapDepth + 1];
+            uint32_t slot_feat[kMaxShapDepth + 1];
+            float slot_val[kMaxShapDepth + 1];
+            uint32_t nt = 0, ns = 0;
+            auto slot_of = [&](uint32_t f) {
+                for (uint32_t q = 0; q < ns; q++)
+                    if (slot_feat[q] == f) return q;
+                slot_feat[ns] = f;
+                slot_val[ns] = 0.0f;
+                return ns++;
+            };
+            DevNode nd = m.nodes[base];
+            if (!((nd.meta >> 24) & kNodeLeaf)) {
+                uint32_t i = 0, split = 0, q = 0;
+                while (!((nd.meta >> 24) & kNodeLeaf)) {
+                    split = nd.meta & 0xffffffu;
+                    i = (uint32_t)(node_goes_left(nd, m, base + i, x[split]) ? nd.left : nd.right);
+                    const float nv = means[base + i];
+                    if (nt > (uint32_t)kMaxShapDepth) break;  // trees are at most kMaxShapDepth deep
+                    q = slot_of(split);
+                    slot_val[q] = __fadd_rn(slot_val[q], __fsub_rn(nv, node_value));
+                    touched[nt++] = split;
+                    node_value = nv;
+                    nd = m.nodes[base + i];
+                }
+                slot_val[q] = __fadd_rn(slot_val[q], __fsub_rn(nd.val, node_value));
+            }
+            for (uint32_t k = 0; k < nt; k++) {
+                const uint32_t q = slot_of(touched[k]);
+                o[touched[k]] = __fadd_rn(o[touched[k]], slot_val[q]);
+                slot_val[q] = 0.0f;
+            }
+            pb = __fadd_rn(pb, tb);
+        }
+        o[F] = __fadd_rn(pb, bias);
+    }
+}
+
 void launch_pred_approx(const DevModel& m, const float* means, const float* X, uint64_t n, float bias, float* out,
                         cudaStream_t s) {
     if (n == 0) return;
     const size_t smem = 2ull * (m.n_features + 1) * kApproxThreads * sizeof(float);
+    if (smem > 227 * 1024) {
+        uint64_t blocks = (n + kApproxThreads - 1) / kApproxThreads;
+        if (blocks > 148ull * 16) blocks = 148ull * 16;
+        count_launch();
+        k_pred_approx_wide<<<(unsigned)blocks, kApproxThreads, 0, s>>>(m, means, X, n, bias, out);
+        return;
+    }
     cudaFuncSetAttribute(k_pred_approx, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     uint64_t blocks = (n + kApproxThreads - 1) / kApproxThreads;
     if (blocks > 148ull * 16) blocks = 148ull * 16;

@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(1024) k_wave_setup(LevelArgs a, LgArgs g) {
             a.nodes[k] = ni;
             const SplitRec b = g.slot_best[s];
             a.split[k] = SplitDesc{(int32_t)(2 * k), b.feat, b.bin, b.flags & 6u};
-            for (int w = 0; w < 8; w++) a.node_cats[k * 8 + w] = g.slot_cats[(size_t)s * 8 + w];
+            for (uint32_t w = 0; w < a.cat_words; w++)
+                a.node_cats[(size_t)k * a.cat_words + w] = g.slot_cats[(size_t)s * a.cat_words + w];
             chunks = (ni.len + kChunkRows - 1) / kChunkRows;
         }
         uint32_t tot;
@@ -266,7 +267,8 @@ __global__ void k_wave_store(LevelArgs a, LgArgs g) {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < m; i += gridDim.x * blockDim.x) {
         const uint32_t s = g.eval_slot[i];
         g.slot_best[s] = a.node_best[i];
-        for (int w = 0; w < 8; w++) g.slot_cats[(size_t)s * 8 + w] = a.node_cats[i * 8 + w];
+        for (uint32_t w = 0; w < a.cat_words; w++)
+            g.slot_cats[(size_t)s * a.cat_words + w] = a.node_cats[(size_t)i * a.cat_words + w];
     }
 }
 
@@ -310,7 +312,7 @@ struct HostSlot {
     bool expanded = false;
     float gain = 0.0f;
     SplitRec best{};
-    uint32_t cats[8] = {0};
+    std::vector<uint32_t> cats;  // right-going set (cat_words words) of a categorical best split
     uint32_t child[2] = {0, 0};
     float cvalue[2] = {0, 0}, chess[2] = {0, 0};
     float value = 0.0f;  // own leaf value (set when its parent is split)
@@ -361,7 +363,8 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
     WaveOut* h_out = reinterpret_cast<WaveOut*>(h_wave + lg_kmax_);
     SplitRec* h_best = reinterpret_cast<SplitRec*>(h_out + lg_kmax_);
     uint32_t* h_cats = reinterpret_cast<uint32_t*>(h_best + 2 * lg_kmax_);
-    TreeRec* h_root = reinterpret_cast<TreeRec*>(h_cats + 16 * lg_kmax_);
+    const uint32_t W = cat_words_;
+    TreeRec* h_root = reinterpret_cast<TreeRec*>(h_cats + 2ull * W * lg_kmax_);
     uint32_t* h_fslot = reinterpret_cast<uint32_t*>(h_root + 1);
     float* h_fval = reinterpret_cast<float*>(h_fslot + max_leaves + 1);
 
@@ -391,14 +394,15 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
         count_launch();
         k_wave_store<<<ceil_div(m, 256), 256, 0, s_>>>(a, g);
         FB_CUDA_CHECK(cudaMemcpyAsync(h_best, node_best_.p, sizeof(SplitRec) * m, cudaMemcpyDeviceToHost, s_));
-        if (has_cat_) FB_CUDA_CHECK(cudaMemcpyAsync(h_cats, node_cats_.p, 32ull * m, cudaMemcpyDeviceToHost, s_));
+        if (has_cat_)
+            FB_CUDA_CHECK(cudaMemcpyAsync(h_cats, node_cats_.p, 4ull * W * m, cudaMemcpyDeviceToHost, s_));
     };
     auto absorb = [&](uint32_t pos, uint32_t slot) {
         HostSlot& hs = slots[slot];
         hs.best = h_best[pos];
         hs.found = (hs.best.flags & 1u) != 0;
         hs.gain = hs.best.gain;
-        if (has_cat_ && (hs.best.flags & 4u)) std::memcpy(hs.cats, h_cats + 8ull * pos, 32);
+        if (has_cat_ && (hs.best.flags & 4u)) hs.cats.assign(h_cats + (size_t)W * pos, h_cats + (size_t)W * (pos + 1));
     };
     auto release = [&](HostSlot& hs) {
         if (hs.hist >= 0) free_hist.push_back(hs.hist);
@@ -426,8 +430,7 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
     slots[0].tree_id = 0;
     if (!root_only) absorb(0, 0);
     std::vector<TreeRec> tree(1, *h_root);
-    std::vector<std::array<uint32_t, 8>> tree_cats(1);
-    tree_cats[0].fill(0);
+    std::vector<std::vector<uint32_t>> tree_cats(1);
     struct E {
         int32_t key;
         int32_t id;
@@ -545,15 +548,11 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
         node.gain = p.best.gain;
         node.leaf = 0.0f;
         node.flags = ((p.best.flags & 2u) ? 2u : 0u) | ((p.best.flags & 4u) ? 4u : 0u);
-        std::array<uint32_t, 8> cw;
-        for (int w = 0; w < 8; w++) cw[w] = (p.best.flags & 4u) ? p.cats[w] : 0u;
-        tree_cats[p.tree_id] = cw;
+        if (p.best.flags & 4u) tree_cats[p.tree_id] = p.cats;
         tree.push_back(TreeRec{-1, -1, 0, 0, 0.0f, p.cvalue[0], p.chess[0], 1u});
         tree.push_back(TreeRec{-1, -1, 0, 0, 0.0f, p.cvalue[1], p.chess[1], 1u});
         tree_cats.emplace_back();
-        tree_cats.back().fill(0);
         tree_cats.emplace_back();
-        tree_cats.back().fill(0);
         leaf_count++;
         const uint32_t c0 = p.child[0], c1 = p.child[1];
         const uint32_t depth = p.depth + 1;
@@ -595,6 +594,9 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
     const uint32_t nn = (uint32_t)tree.size();
     if (!out) return;
     if (out->capacity < nn) throw InputError("fbgpu_tree_out capacity is smaller than the tree");
+    const uint32_t out_w = out->cat_words ? out->cat_words : 8u;
+    if (out->cats && out_w < W)
+        throw InputError("fbgpu_tree_out.cat_words is smaller than the context's category sets (fbgpu_ctx_cat_words)");
     out->n_nodes = nn;
     for (uint32_t i = 0; i < nn; i++) {
         const TreeRec& t = tree[i];
@@ -607,7 +609,8 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
         if (out->hess) out->hess[i] = t.hess;
         if (out->flags) out->flags[i] = t.flags;
         if (out->cats)
-            for (int w = 0; w < 8; w++) out->cats[i * 8 + w] = tree_cats[i][w];
+            for (uint32_t w = 0; w < out_w; w++)
+                out->cats[(size_t)i * out_w + w] = w < tree_cats[i].size() ? tree_cats[i][w] : 0u;
     }
     (void)enabled;
 }
@@ -620,7 +623,7 @@ void TrainCtx::ensure_lossguide_buffers(uint32_t max_leaves) {
     lg_slots_.alloc(sizeof(NodeInfo) * lg_slot_cap_);
     lg_slot_hist_.alloc(4ull * lg_slot_cap_);
     lg_slot_best_.alloc(sizeof(SplitRec) * lg_slot_cap_);
-    lg_slot_cats_.alloc(32ull * lg_slot_cap_);
+    lg_slot_cats_.alloc(4ull * cat_words_ * lg_slot_cap_);
     FB_CUDA_CHECK(cudaMemsetAsync(lg_slot_cats_.p, 0, lg_slot_cats_.bytes, s_));
     lg_wave_.alloc(sizeof(WaveEntry) * lg_kmax_);
     lg_wave_out_.alloc(sizeof(WaveOut) * lg_kmax_);
@@ -629,7 +632,7 @@ void TrainCtx::ensure_lossguide_buffers(uint32_t max_leaves) {
     lg_final_slot_.alloc(4ull * (max_leaves + 1));
     lg_final_value_.alloc(4ull * (max_leaves + 1));
     h_lg_.reserve(sizeof(WaveEntry) * lg_kmax_ + sizeof(WaveOut) * lg_kmax_ + sizeof(SplitRec) * 2 * lg_kmax_ +
-                  64ull * lg_kmax_ + sizeof(TreeRec) + 8ull * (max_leaves + 1) + 64);
+                  8ull * cat_words_ * lg_kmax_ + sizeof(TreeRec) + 8ull * (max_leaves + 1) + 64);
     lg_leaves_ = max_leaves;
 }
 

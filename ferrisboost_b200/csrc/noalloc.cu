@@ -178,6 +178,7 @@ extern "C" fbgpu_status fbgpu_partition_noalloc(const void* bins, uint32_t strid
         a.floc = &scr->floc;
         a.chunk_prefix = scr->chunk_prefix;
         a.node_cats = scr->cats;
+        a.cat_words = 8;
         a.chunk_left = scr->chunk_left;
         a.chunk_off = scr->chunk_off;
         a.node_left = n_left;

@@ -54,13 +54,14 @@ template <int M> __host__ __device__ constexpr uint32_t elem_words() { return 4 
 // merged into lo <= x < hi (hi = NaN when no edge bounds it above); NaN rows
 // follow the default directions; categorical rows test the intersection of
 // the edges' category sets (data/categorical.rs:330-345).
-__device__ __forceinline__ bool elem_test(uint4 h, float x, const uint32_t* __restrict__ cat_masks) {
+__device__ __forceinline__ bool elem_test(uint4 h, float x, const uint32_t* __restrict__ cat_masks, uint32_t mw) {
     const uint32_t fl = h.x >> 24;
     if (x != x) return (fl & kElemNanOk) != 0;
     if (fl & kElemCat) {
         if (x < 0.0f || x >= 16777216.0f) return (fl & kElemOutOk) != 0;
         const uint32_t code = (uint32_t)x;
-        return code < 256u ? ((cat_masks[h.y * 8u + (code >> 5)] >> (code & 31u)) & 1u) != 0 : (fl & kElemOutOk) != 0;
+        return code < 32u * mw ? ((cat_masks[h.y * mw + (code >> 5)] >> (code & 31u)) & 1u) != 0
+                               : (fl & kElemOutOk) != 0;
     }
     return !(x < __uint_as_float(h.y)) && !(x >= __uint_as_float(h.z));
 }
@@ -81,7 +82,8 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
                                                              const uint4* __restrict__ elems,
                                                              const uint32_t* __restrict__ chunk_off,
                                                              uint32_t n_chunks, const uint32_t* __restrict__ cat_masks,
-                                                             float bias, float root_mean, float* __restrict__ out) {
+                                                             uint32_t mask_words, float bias, float root_mean,
+                                                             float* __restrict__ out) {
     constexpr uint32_t EW = elem_words<M>();
     constexpr uint32_t TR = kPathThreads * R;  // rows per CTA tile
     extern __shared__ __align__(16) uint32_t smem[];
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
                         load_vec<M>(E + 4 + M, a1);
 #pragma unroll
                         for (int r = 0; r < R; r++) {
-                            const bool o = elem_test(h, xs[f * TR + t + r * kPathThreads], cat_masks);
+                            const bool o = elem_test(h, xs[f * TR + t + r * kPathThreads], cat_masks, mask_words);
                             obits[r] |= (o ? 1u : 0u) << j;
 #pragma unroll
                             for (int i = 0; i < M; i++) P[r][i] = __fmul_rn(P[r][i], o ? a1[i] : a0[i]);
@@ -192,6 +194,7 @@ __global__ void __launch_bounds__(kInterWarps * 32) k_shap_inter(const float* __
                                                                  const uint32_t* __restrict__ chunk_off,
                                                                  uint32_t n_chunks,
                                                                  const uint32_t* __restrict__ cat_masks,
+                                                                 uint32_t mask_words,
                                                                  const float* __restrict__ rule_w, uint32_t warps,
                                                                  float bias, float root_mean, float* __restrict__ out) {
     constexpr uint32_t EW = elem_words<M>();
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(kInterWarps * 32) k_shap_inter(const float* __
                 const uint32_t* E = ch + (e + (mine ? lane : 0)) * EW;
                 const uint4 h = *reinterpret_cast<const uint4*>(E);
                 const uint32_t f = h.x & 0xffffffu;
-                const bool o = mine && elem_test(h, x[f], cat_masks);
+                const bool o = mine && elem_test(h, x[f], cat_masks, mask_words);
                 float a[M], b[M], P[M];
                 load_vec<M>(E + 4 + (o ? M : 0), a);
                 load_vec<M>(E + 4 + 2 * M + (o ? M : 0), b);
@@ -288,6 +291,120 @@ __global__ void __launch_bounds__(kInterWarps * 32) k_shap_inter(const float* __
     }
 }
 
+// Interaction values of models with too many features for a shared-memory
+// matrix ((F+1)^2 f64 per row): the arithmetic of k_shap_inter, one warp (one
+// CTA) per row of a batch, the row's off-diagonal sums ([nc][nc]) and SHAP
+// values ([nc]) in global f64 scratch zeroed by the caller; k_inter_finish
+// then forms the diagonal and writes the f32 matrix.  Within a path no entry
+// is updated twice, and __syncwarp orders one path's updates before the
+// next's.
+template <int M>
+__global__ void __launch_bounds__(32) k_shap_inter_global(const float* __restrict__ X, uint64_t r0, uint32_t rows,
+                                                          uint32_t F, const uint4* __restrict__ elems,
+                                                          const uint32_t* __restrict__ chunk_off, uint32_t n_chunks,
+                                                          const uint32_t* __restrict__ cat_masks, uint32_t mask_words,
+                                                          const float* __restrict__ rule_w, double* __restrict__ scratch) {
+    constexpr uint32_t EW = elem_words<M>();
+    extern __shared__ __align__(16) uint32_t smem[];
+    const uint32_t nc = F + 1, lane = threadIdx.x;
+    const size_t mat = (size_t)nc * nc;
+    float* x = reinterpret_cast<float*>(smem);                   // [F]
+    uint32_t* ch = smem + ((F + 3u) & ~3u);                      // path chunk (16-byte aligned)
+    float inv_w[M];
+#pragma unroll
+    for (int i = 0; i < M; i++) inv_w[i] = 1.0f / rule_w[i];
+    for (uint32_t rr = blockIdx.x; rr < rows; rr += gridDim.x) {
+        const uint64_t r = r0 + rr;
+        double* m = scratch + (size_t)rr * (mat + nc);
+        double* dg = m + mat;
+        __syncwarp();
+        for (uint32_t i = lane; i < F; i += 32) x[i] = X[r * F + i];
+        for (uint32_t c = 0; c < n_chunks; c++) {
+            const uint32_t e0 = chunk_off[c], e1 = chunk_off[c + 1];
+            __syncwarp();
+            const uint4* src = elems + (size_t)e0 * (EW / 4);
+            uint4* dst = reinterpret_cast<uint4*>(ch);
+            for (uint32_t i = lane; i < (e1 - e0) * (EW / 4); i += 32) dst[i] = src[i];
+            __syncwarp();
+            uint32_t e = 0;
+            while (e < e1 - e0) {
+                const uint32_t k = ch[e * EW + 3];
+                const bool mine = lane < k;
+                const uint32_t* E = ch + (e + (mine ? lane : 0)) * EW;
+                const uint4 h = *reinterpret_cast<const uint4*>(E);
+                const uint32_t f = h.x & 0xffffffu;
+                const bool o = mine && elem_test(h, x[f], cat_masks, mask_words);
+                float a[M], b[M], P[M];
+                load_vec<M>(E + 4 + (o ? M : 0), a);
+                load_vec<M>(E + 4 + 2 * M + (o ? M : 0), b);
+                const float cj = __uint_as_float(E[4 + 4 * M + (o ? 1 : 0)]);
+                const float dj = __fsub_rn(o ? 1.0f : 0.0f, __uint_as_float(E[4 + 4 * M + 2]));
+#pragma unroll
+                for (int i = 0; i < M; i++) P[i] = mine ? a[i] : 1.0f;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                    for (int i = 0; i < M; i++) P[i] = __fmul_rn(P[i], __shfl_xor_sync(0xffffffffu, P[i], off));
+                if (mine) {
+                    float sacc = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < M; i++) sacc = __fmaf_rn(b[i], P[i], sacc);
+                    dg[f] = __dadd_rn(dg[f], (double)__fmul_rn(cj, sacc));
+                }
+                for (uint32_t l = 1; l < k; l++) {
+                    float bl[M];
+#pragma unroll
+                    for (int i = 0; i < M; i++) bl[i] = __shfl_sync(0xffffffffu, b[i], l);
+                    const float dl = __shfl_sync(0xffffffffu, dj, l);
+                    const uint32_t fl = __shfl_sync(0xffffffffu, f, l);
+                    if (lane < l) {
+                        float sacc = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < M; i++)
+                            sacc = __fmaf_rn(__fmul_rn(b[i], bl[i]), __fmul_rn(P[i], inv_w[i]), sacc);
+                        const double t = 0.5 * (double)cj * (double)dl * (double)sacc;
+                        m[(size_t)f * nc + fl] = __dadd_rn(m[(size_t)f * nc + fl], t);
+                        m[(size_t)fl * nc + f] = __dadd_rn(m[(size_t)fl * nc + f], t);
+                    }
+                }
+                __syncwarp();
+                e += k;
+            }
+        }
+    }
+}
+
+// Diagonal (the SHAP value minus the row's interactions; the bias row takes
+// the bias) and f32 output of k_shap_inter_global's rows: a warp per matrix
+// row.
+__global__ void __launch_bounds__(256) k_inter_finish(uint64_t r0, uint32_t rows, uint32_t F, float bias,
+                                                      float root_mean, const double* __restrict__ scratch,
+                                                      float* __restrict__ out) {
+    const uint32_t nc = F + 1, lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const size_t mat = (size_t)nc * nc;
+    const uint64_t total = (uint64_t)rows * nc;
+    for (uint64_t g = (uint64_t)blockIdx.x * 8 + warp; g < total; g += (uint64_t)gridDim.x * 8) {
+        const uint32_t rr = (uint32_t)(g / nc), i = (uint32_t)(g % nc);
+        const double* m = scratch + (size_t)rr * (mat + nc);
+        const double* mi = m + (size_t)i * nc;
+        float* o = out + (r0 + rr) * mat + (size_t)i * nc;
+        double off = 0.0;
+        for (uint32_t j = lane; j < nc; j += 32) {
+            const double v = mi[j];
+            if (j != i) {
+                off += v;
+                o[j] = __double2float_rn(v);
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) off += __shfl_xor_sync(0xffffffffu, off, d);
+        if (lane == 0) {
+            const double base = i == F ? (double)__fadd_rn(__fadd_rn(0.0f, root_mean), bias) : m[mat + i];
+            o[i] = __double2float_rn(base - off);
+        }
+    }
+}
+
 }  // namespace
 
 // Gauss-Legendre rule with m points on [0, 1] (Golub-Welsch-free Newton on
@@ -321,13 +438,18 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
         double z;
         float lo, hi;
         bool nan_ok, cat, out_ok;
-        uint32_t mask[8];
+        std::vector<uint32_t> mask;  // categorical: codes the row may hold (mask_words words)
     };
     struct Path {
         float v;
         std::vector<El> els;
     };
     supported = true;
+    // words of a category mask: every set of the model fits (a bit per code)
+    mask_words = 8;
+    for (uint32_t t = 0; t < n_trees; t++)
+        for (uint32_t i = tree_off[t]; i < tree_off[t + 1]; i++)
+            if ((nodes[i].meta >> 24) & kNodeCategorical) mask_words = std::max(mask_words, cat_len[i]);
     std::vector<Path> paths;
     std::vector<int> pos(F, -1);
     std::vector<El> st;
@@ -393,7 +515,7 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
                 e.nan_ok = true;
                 e.cat = (flags & kNodeCategorical) != 0;
                 e.out_ok = true;
-                for (auto& w : e.mask) w = 0xffffffffu;
+                e.mask.assign(mask_words, 0xffffffffu);
                 st.push_back(e);
                 slot = (int)st.size() - 1;
                 pos[f] = slot;
@@ -406,11 +528,7 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
             e.nan_ok = e.nan_ok && (((flags & kNodeDefaultLeft) != 0) == left);
             if (flags & kNodeCategorical) {
                 const uint32_t co = cat_off[a + fr.i], cl = cat_len[a + fr.i];
-                if (cl > 8) {  // codes >= 256 in a set: the 8-word masks cannot hold it
-                    supported = false;
-                    return;
-                }
-                for (uint32_t wi = 0; wi < 8; wi++) {
+                for (uint32_t wi = 0; wi < mask_words; wi++) {
                     const uint32_t s = wi < cl ? cat_words[co + wi] : 0u;
                     e.mask[wi] &= left ? ~s : s;
                 }
@@ -462,8 +580,8 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
             const uint32_t fl = (e.nan_ok ? kElemNanOk : 0u) | (e.cat ? kElemCat : 0u) | (e.out_ok ? kElemOutOk : 0u);
             rec[0] = (e.feat & 0xffffffu) | (fl << 24);
             if (e.cat) {
-                rec[1] = (uint32_t)(masks.size() / 8);
-                masks.insert(masks.end(), e.mask, e.mask + 8);
+                rec[1] = (uint32_t)(masks.size() / mask_words);
+                masks.insert(masks.end(), e.mask.begin(), e.mask.end());
                 rec[2] = 0;
             } else {
                 // no upper bound: hi = NaN, so the test !(x >= hi) always passes (x = +inf included)
@@ -496,7 +614,7 @@ void ShapPaths::build(const std::vector<DevNode>& nodes, const uint32_t* tree_of
 void ShapPaths::upload(cudaStream_t s) {
     d_words.alloc(std::max<size_t>(words.size(), 4) * 4);
     d_chunks.alloc(chunk_off.size() * 4);
-    d_masks.alloc(std::max<size_t>(masks.size(), 8) * 4);
+    d_masks.alloc(std::max<size_t>(masks.size(), mask_words) * 4);
     if (!words.empty())
         FB_CUDA_CHECK(cudaMemcpyAsync(d_words.p, words.data(), words.size() * 4, cudaMemcpyHostToDevice, s));
     FB_CUDA_CHECK(cudaMemcpyAsync(d_chunks.p, chunk_off.data(), chunk_off.size() * 4, cudaMemcpyHostToDevice, s));
@@ -520,7 +638,6 @@ void ShapPaths::launch_inter(const float* X, uint64_t n, uint32_t F, float bias,
                              cudaStream_t s) {
     if (n == 0) return;
     const uint32_t warps = inter_warps(F);
-    if (warps == 0) throw InputError("pred_interactions on the device supports at most 160 features");
     if (!d_rule_w.p) {
         double y[8], w[8];
         float wf[8];
@@ -530,10 +647,41 @@ void ShapPaths::launch_inter(const float* X, uint64_t n, uint32_t F, float bias,
         FB_CUDA_CHECK(cudaMemcpyAsync(d_rule_w.p, wf, sizeof(float) * M, cudaMemcpyHostToDevice, s));
     }
     const uint32_t n_chunks = (uint32_t)chunk_off.size() - 1;
-    const size_t smem = inter_smem_bytes(F, warps);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (warps == 0) {
+        // the matrix does not fit shared memory: global f64 scratch, rows in
+        // batches of at most 1 GiB of scratch
+        const size_t nc = (size_t)F + 1;
+        const size_t per_row = (nc * nc + nc) * 8;
+        const size_t gsmem = (size_t)((F + 3u) & ~3u) * 4 + kChunkBytes;
+        if (gsmem > 227 * 1024) throw InputError("pred_interactions on the device supports at most 51000 features");
+        const uint64_t R = std::max<uint64_t>(1, std::min<uint64_t>(n, (1ull << 30) / per_row));
+        if (d_inter_scratch.bytes < R * per_row) d_inter_scratch.alloc(R * per_row);
+        double* scr = d_inter_scratch.as<double>();
+        for (uint64_t r0 = 0; r0 < n; r0 += R) {
+            const uint32_t rows = (uint32_t)std::min<uint64_t>(R, n - r0);
+            FB_CUDA_CHECK(cudaMemsetAsync(scr, 0, rows * per_row, s));
+#define FB_SG(MM)                                                                                                  \
+    do {                                                                                                           \
+        cudaFuncSetAttribute(k_shap_inter_global<MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem);    \
+        count_launch();                                                                                            \
+        k_shap_inter_global<MM><<<rows, 32, gsmem, s>>>(X, r0, rows, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), \
+                                                        n_chunks, d_masks.as<uint32_t>(), mask_words,              \
+                                                        d_rule_w.as<float>(), scr);                                \
+    } while (0)
+            if (M == 4) FB_SG(4);
+            else FB_SG(8);
+#undef FB_SG
+            const uint64_t warps_total = (uint64_t)rows * nc;
+            const uint32_t grid = (uint32_t)std::min<uint64_t>((warps_total + 7) / 8, (uint64_t)sms * 8);
+            count_launch();
+            k_inter_finish<<<grid, 256, 0, s>>>(r0, rows, F, bias, root_mean, scr, out);
+        }
+        return;
+    }
+    const size_t smem = inter_smem_bytes(F, warps);
     const uint64_t groups = (n + warps - 1) / warps;
 #define FB_SI(MM)                                                                                                  \
     do {                                                                                                           \
@@ -543,7 +691,7 @@ void ShapPaths::launch_inter(const float* X, uint64_t n, uint32_t F, float bias,
         const uint64_t grid = std::min<uint64_t>(groups, (uint64_t)sms * std::max(per_sm, 1));                     \
         count_launch();                                                                                            \
         k_shap_inter<MM><<<(unsigned)grid, kInterWarps * 32, smem, s>>>(                                          \
-            X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(),               \
+            X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(), mask_words,   \
             d_rule_w.as<float>(), warps, bias, root_mean, out);                                                    \
     } while (0)
     if (M == 4) FB_SI(4);
@@ -574,8 +722,8 @@ void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float
         const uint64_t grid = std::min<uint64_t>(tiles, (uint64_t)sms * std::max(per_sm, 1));                        \
         count_launch();                                                                                              \
         k_shap_paths<MM, KK, RR><<<(unsigned)grid, kPathThreads, smem, s>>>(                                        \
-            X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(), bias, root_mean, \
-            out);                                                                                                    \
+            X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(), mask_words,    \
+            bias, root_mean, out);                                                                                   \
     } while (0)
     if (M == 4) FB_SP(4, 8, kPathRows);
     else FB_SP(8, 14, kPathRows);

@@ -214,8 +214,10 @@ __global__ void k_mask_max(GradArgs a) {
 }
 
 // objective.rs:37-39,513-526: the gradient of one row, in the reference's f32
-// operation order.  Logistic takes e = expf(-pred) (computed by the host's
-// glibc in exact mode, by CUDA's expf in fast mode).
+// operation order.  Logistic takes e = expf(-pred): the host's glibc expf in
+// exact mode (reproduced on the device); in fast mode fexp_core alone (fexp.h:
+// an f64 evaluation rounded once to f32, which differs from glibc on about
+// 0.004 % of the inputs, by one unit in the last place).
 __device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, float e, float& g, float& h) {
     float y = a.label[i];
     if (a.objective == 1) {
@@ -263,7 +265,7 @@ __global__ void k_gradient_max(GradArgs a, int mode) {
         float e = 0.0f;
         if (a.objective == 1) {
             const float x = -a.pred[i];
-            e = mode == 1 ? expf(x) : (mode == 2 ? host_expf(x, a.exptab, a.exp_probes) : a.host_exp[i]);
+            e = mode == 1 ? fbx::fexp_core(x) : (mode == 2 ? host_expf(x, a.exptab, a.exp_probes) : a.host_exp[i]);
         }
         float g, h;
         row_gradient(a, i, e, g, h);
@@ -299,7 +301,7 @@ __global__ void k_gradient_quantize_exp(GradArgs a) {
 template <bool FAST, int KR>
 __global__ void k_softmax_grad(GradArgs a, uint32_t K, float* __restrict__ out) {
     const size_t n = a.n;
-    auto ex = [&](float x) { return FAST ? expf(x) : host_expf(x, a.exptab, a.exp_probes); };
+    auto ex = [&](float x) { return FAST ? fbx::fexp_core(x) : host_expf(x, a.exptab, a.exp_probes); };
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
         float wmax = FLT_MIN;
         for (uint32_t k = 0; k < K; k++) wmax = fmaxf(a.pred[k * n + i], wmax);
@@ -406,6 +408,11 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
     for (uint32_t j = threadIdx.x; j < 4 * LB; j += blockDim.x) sm[j] = 0u;
     __syncthreads();
     const uint32_t nf = td.n_feat;
+    // a tile with no shared histogram (features wider than the shared-memory
+    // budget, e.g. categorical features of tens of thousands of codes) adds
+    // every update straight to the node histogram: 64-bit global atomics,
+    // exact modulo 2^64 like the shared planes
+    const bool direct = LB == 0;
     uint32_t k = find_segment(acc_prefix, n_acc, a);
     while (a < b) {
         const uint32_t node = acc_list[k];
@@ -413,6 +420,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
         const unsigned long long seg_end = min(b, acc_prefix[k + 1]);
         const uint32_t base = ni.start + (uint32_t)(a - acc_prefix[k]);
         const uint32_t cnt = (uint32_t)(seg_end - a);
+        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
         for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
             const uint32_t r = rows[base + i];
             const Pair gp = gpair[r];
@@ -422,14 +430,24 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
                 uint32_t bin = W == 2 ? (uint32_t)(*reinterpret_cast<const uint16_t*>(rec + f.byte_off))
                                       : (uint32_t)rec[f.byte_off];
                 if (bin >= f.nbins) continue;  // missing sentinels lie at or above every feature's bin count
+                if (direct) {
+                    Pair* o = out + f.global_off + bin;
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&o->g), (unsigned long long)gp.g);
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&o->h), (unsigned long long)gp.h);
+                    continue;
+                }
                 const uint32_t idx = f.local_off + bin;
                 plane_add(glo, ghi, idx, gp.g);
                 plane_add(hlo, hhi, idx, gp.h);
             }
         }
+        if (direct) {
+            a = seg_end;
+            k++;
+            continue;
+        }
         __syncthreads();
         // flush: one 64-bit global atomic per non-zero word, then clear
-        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
         for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
             unsigned long long g = ((unsigned long long)ghi[j] << 32) | glo[j];
             unsigned long long h = ((unsigned long long)hhi[j] << 32) | hlo[j];
@@ -733,13 +751,37 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
 }
 
 // ------------------------------------------------------------------ split
+// Wide categorical features (more codes than the split CTA has threads, up to
+// 65534 codes: categorical.rs:19-28 MAX_CAT_CODE_WIDE).  The reference sorts
+// all codes stably by weight and scans the first and the last n_scan - 1 of
+// that order (split.rs:484-617).  Only those codes take part, so instead of
+// sorting every code the CTA selects them by rank: a code's order key is its
+// f32 weight mapped to an order-preserving u32 (-0 and +0 one key, as `<`
+// sees them) with the code as the tie break; the key of a given rank comes
+// from a 4-pass radix select over the weight keys and a search in code order
+// among equal weights; each tile of kCatTile ranks is gathered into shared
+// memory, sorted, and scanned with the carry of the tiles before it.
+constexpr uint32_t kCatTile = 512;
+
+struct CatWideSmem {
+    unsigned long long key[kCatTile];  // a tile's composite keys (weight key << 32 | code)
+    uint32_t digit[256];
+    uint32_t count, sel_digit, sel_before, sel_code;
+};
+
 struct SplitSmem {
     Pair warp_tot[32];
     SplitRec best[kSplitThreads];
-    float w[kSplitThreads];
-    uint32_t idx[kSplitThreads];
-    Pair x[kSplitThreads];       // categorical: the finished histogram (parent and child may share memory)
+    union {
+        struct {
+            float w[kSplitThreads];
+            uint32_t idx[kSplitThreads];
+            Pair x[kSplitThreads];  // the finished histogram (parent and child may share memory)
+        } c;                        // categorical features of at most kSplitThreads codes
+        CatWideSmem wide;           // wider categorical features
+    } u;
     uint32_t set_words[8];
+    uint32_t wt[32];
 };
 
 __device__ __forceinline__ void consider(SplitRec& best, float gain, uint32_t ord, uint32_t bin, uint32_t flags,
@@ -758,6 +800,199 @@ __device__ __forceinline__ void block_best(SplitSmem& s, SplitRec& mine) {
         if ((int)threadIdx.x < stride && rec_better(s.best[threadIdx.x + stride], s.best[threadIdx.x]))
             s.best[threadIdx.x] = s.best[threadIdx.x + stride];
         __syncthreads();
+    }
+}
+
+// A category's sort key: its weight (CalcWeightCat, split.rs:520-530) as an
+// order-preserving u32.
+__device__ __forceinline__ uint32_t cat_weight_key(Pair x, const ScoreParams& sp) {
+    float w = xgb_weight(to_f64(x.g, sp.inv_g), to_f64(x.h, sp.inv_h), sp);
+    if (w == 0.0f) w = 0.0f;  // -0 and +0 compare equal under the sort's `<`: one key
+    const uint32_t b = __float_as_uint(w);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long cat_order_key(const Pair* hx, uint32_t c, const ScoreParams& sp) {
+    return ((unsigned long long)cat_weight_key(hx[c], sp) << 32) | c;
+}
+
+// The order key of the code with exactly r codes before it in the stable
+// weight order (0 <= r < n).  Every thread of the CTA calls it.
+__device__ unsigned long long cat_select(const Pair* hx, uint32_t n, const ScoreParams& sp, uint32_t r,
+                                         SplitSmem& s) {
+    CatWideSmem& ws = s.u.wide;
+    uint32_t prefix = 0, mask = 0, rem = r;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        ws.digit[threadIdx.x] = 0u;  // blockDim == 256 == digits
+        __syncthreads();
+        for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
+            const uint32_t k = cat_weight_key(hx[c], sp);
+            if ((k & mask) == prefix) atomicAdd(&ws.digit[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        const uint32_t cnt = ws.digit[threadIdx.x];
+        uint32_t tot;
+        const uint32_t before = block_excl_scan_u32<kSplitThreads>(cnt, s.wt, tot);
+        if (before <= rem && rem < before + cnt) {
+            ws.sel_digit = threadIdx.x;
+            ws.sel_before = before;
+        }
+        __syncthreads();
+        rem -= ws.sel_before;
+        prefix |= ws.sel_digit << shift;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    // the rem-th code, in code order, among those whose weight key is `prefix`
+    uint32_t seen = 0;
+    for (uint32_t base = 0; base < n; base += blockDim.x) {
+        const uint32_t c = base + threadIdx.x;
+        const bool match = c < n && cat_weight_key(hx[c], sp) == prefix;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan_u32<kSplitThreads>(match ? 1u : 0u, s.wt, tot);
+        if (match && seen + ex == rem) ws.sel_code = c;
+        seen += tot;
+        if (seen > rem) break;  // uniform: every thread holds the same `seen`
+    }
+    __syncthreads();
+    const uint32_t code = ws.sel_code;
+    __syncthreads();
+    return ((unsigned long long)prefix << 32) | code;
+}
+
+// Gathers the codes whose order keys lie in [lo, hi) (at most kCatTile) into
+// ws.key, sorted ascending; returns how many.
+__device__ uint32_t cat_gather(const Pair* hx, uint32_t n, const ScoreParams& sp, unsigned long long lo,
+                               unsigned long long hi, SplitSmem& s) {
+    CatWideSmem& ws = s.u.wide;
+    if (threadIdx.x == 0) ws.count = 0u;
+    __syncthreads();
+    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
+        const unsigned long long k = cat_order_key(hx, c, sp);
+        if (k >= lo && k < hi) {
+            const uint32_t at = atomicAdd(&ws.count, 1u);
+            if (at < kCatTile) ws.key[at] = k;
+        }
+    }
+    __syncthreads();
+    const uint32_t cnt = min(ws.count, kCatTile);
+    for (uint32_t i = cnt + threadIdx.x; i < kCatTile; i += blockDim.x) ws.key[i] = ~0ull;
+    __syncthreads();
+    for (uint32_t size = 2; size <= kCatTile; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = threadIdx.x; i < kCatTile; i += blockDim.x) {
+                const uint32_t j = i ^ stride;
+                if (j > i) {
+                    const unsigned long long x = ws.key[i], y = ws.key[j];
+                    if ((x > y) == ((i & size) == 0)) { ws.key[i] = y; ws.key[j] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    return cnt;
+}
+
+// Best categorical split of a feature with n > kSplitThreads codes whose
+// finished histogram is hx[0..n) (split.rs:484-617: one-hot below
+// max_cat_to_onehot, else the partition scans), and its right-going set
+// written to cw (cat_words words).
+__device__ void split_cat_wide(const LevelArgs& a, SplitSmem& s, const Pair* hx, uint32_t n, Pair sum,
+                               float parent_gain, int cons, const NodeInfo& ni, const ScoreParams& sp, SplitRec& mine,
+                               uint32_t* cw) {
+    const uint32_t W = a.cat_words;
+    if (n < a.max_onehot) {
+        Pair loc{0, 0};
+        for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) loc = padd(loc, hx[c]);
+        Pair tot;
+        (void)block_excl_scan_pair<kSplitThreads>(loc, s.warp_tot, tot);
+        const Pair missing = psub(sum, tot);
+        for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
+            const Pair x = hx[c];
+            float gain;
+            Pair l = psub(sum, x);
+            if (split_gain(parent_gain, l, x, cons, ni.lower, ni.upper, sp, gain))
+                consider(mine, gain, 2 * c, c, 2u | 4u, l, x);
+            const Pair r = padd(x, missing);
+            l = psub(sum, r);
+            if (split_gain(parent_gain, l, r, cons, ni.lower, ni.upper, sp, gain))
+                consider(mine, gain, 2 * c + 1, c, 4u, l, r);
+        }
+        block_best(s, mine);
+        const SplitRec b = s.best[0];
+        for (uint32_t w = threadIdx.x; w < W; w += blockDim.x)
+            cw[w] = (b.flags & 1u) && w == (b.bin >> 5) ? 1u << (b.bin & 31) : 0u;
+        return;
+    }
+    const uint32_t n_scan = min(a.max_cat_threshold, n);
+    const uint32_t K = n_scan >= 2 ? n_scan - 1 : 0u;
+    // forward: the first t+1 codes of the order go right, missing left
+    Pair carry{0, 0};
+    unsigned long long t_lo = 0ull;
+    for (uint32_t lo = 0; lo < K; lo += kCatTile) {
+        const uint32_t hi = min(lo + kCatTile, K);
+        const unsigned long long t_hi = cat_select(hx, n, sp, hi, s);
+        const uint32_t cnt = cat_gather(hx, n, sp, t_lo, t_hi, s);
+        const uint32_t i0 = 2 * threadIdx.x;
+        const Pair x0 = i0 < cnt ? hx[(uint32_t)s.u.wide.key[i0]] : Pair{0, 0};
+        const Pair x1 = i0 + 1 < cnt ? hx[(uint32_t)s.u.wide.key[i0 + 1]] : Pair{0, 0};
+        Pair tot;
+        const Pair ex = block_excl_scan_pair<kSplitThreads>(padd(x0, x1), s.warp_tot, tot);
+        Pair run = padd(carry, ex);
+        for (uint32_t q = 0; q < 2; q++) {
+            const uint32_t i = i0 + q;
+            run = padd(run, q ? x1 : x0);
+            if (i < cnt) {
+                const uint32_t rank = lo + i;
+                const Pair r = run, l = psub(sum, r);
+                float gain;
+                if (split_gain(parent_gain, l, r, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, rank, rank + 1, 2u | 4u, l, r);
+            }
+        }
+        carry = padd(carry, tot);
+        t_lo = t_hi;
+        __syncthreads();
+    }
+    // backward: the order's tail from rank t goes left, missing right
+    carry = Pair{0, 0};
+    unsigned long long t_hi = ~0ull;
+    for (uint32_t hi = n; K && hi > n - K;) {
+        const uint32_t lo = max(n - K, hi > kCatTile ? hi - kCatTile : 0u);
+        const unsigned long long t_lo2 = cat_select(hx, n, sp, lo, s);
+        const uint32_t cnt = cat_gather(hx, n, sp, t_lo2, t_hi, s);
+        const uint32_t i0 = 2 * threadIdx.x;
+        const Pair x0 = i0 < cnt ? hx[(uint32_t)s.u.wide.key[i0]] : Pair{0, 0};
+        const Pair x1 = i0 + 1 < cnt ? hx[(uint32_t)s.u.wide.key[i0 + 1]] : Pair{0, 0};
+        Pair tot;
+        const Pair ex = block_excl_scan_pair<kSplitThreads>(padd(x0, x1), s.warp_tot, tot);
+        Pair before = ex;  // this tile's codes ranked before element i
+        for (uint32_t q = 0; q < 2; q++) {
+            const uint32_t i = i0 + q;
+            if (i < cnt) {
+                const uint32_t rank = lo + i;
+                const Pair l = padd(carry, psub(tot, before)), r = psub(sum, l);
+                float gain;
+                if (split_gain(parent_gain, l, r, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, (n_scan - 1) + (n - 1 - rank), rank, 4u, l, r);
+            }
+            before = padd(before, q ? x1 : x0);
+        }
+        carry = padd(carry, tot);
+        t_hi = t_lo2;
+        hi = lo;
+        __syncthreads();
+    }
+    block_best(s, mine);
+    const SplitRec b = s.best[0];
+    // the right-going set: the b.bin codes first in the order
+    const unsigned long long cut = (b.flags & 1u) ? cat_select(hx, n, sp, b.bin, s) : 0ull;
+    for (uint32_t w = threadIdx.x; w < W; w += blockDim.x) {
+        uint32_t word = 0u;
+        for (uint32_t k = 0; k < 32; k++) {
+            const uint32_t c = 32 * w + k;
+            if (c < n && cat_order_key(hx, c, sp) < cut) word |= 1u << k;
+        }
+        cw[w] = word;
     }
 }
 
@@ -791,6 +1026,21 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
     mine.left = Pair{0, 0}; mine.right = Pair{0, 0};
 
     if (a.is_cat && a.is_cat[f]) {
+        const uint32_t W = a.cat_words;
+        uint32_t* cw = a.feat_cats + ((size_t)node * a.n_cat + a.cat_slot[f]) * W;
+        if (nb > kSplitThreads) {
+            // ---- wide categorical: the finished histogram goes to h first (each bin
+            // read and written by one thread), then the rank-selected scans read it
+            for (uint32_t c = threadIdx.x; c < nb; c += blockDim.x) h[c] = par ? psub(par[c], acc[c]) : acc[c];
+            __syncthreads();
+            split_cat_wide(a, s, h, nb, sum, parent_gain, cons, ni, sp, mine, cw);
+            if (threadIdx.x == 0) {
+                SplitRec b = s.best[0];
+                b.feat = f;
+                *out = b;
+            }
+            return;
+        }
         // ---- categorical: one bin per category code, n <= 256 (one per thread)
         const uint32_t n = nb, t = threadIdx.x;
         Pair x{0, 0};
@@ -813,42 +1063,42 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
                     consider(mine, gain, 2 * t + 1, t, 4u, l, r);
             }
             block_best(s, mine);
+            const SplitRec b = s.best[0];
+            for (uint32_t w = threadIdx.x; w < W; w += blockDim.x)
+                cw[w] = (b.flags & 1u) && w == (b.bin >> 5) ? 1u << (b.bin & 31) : 0u;
             if (threadIdx.x == 0) {
-                SplitRec b = s.best[0];
-                b.feat = f;
-                *out = b;
-                uint32_t* cw = a.feat_cats + ((size_t)node * F + f) * 8;
-                for (int w = 0; w < 8; w++) cw[w] = 0u;
-                if (b.flags & 1u) cw[b.bin >> 5] = 1u << (b.bin & 31);
+                SplitRec bf = b;
+                bf.feat = f;
+                *out = bf;
             }
             return;
         }
         // partition mode: stable sort of categories by weight (CalcWeightCat)
         float w = __int_as_float(0x7f800000);
         if (t < n) w = xgb_weight(to_f64(x.g, sp.inv_g), to_f64(x.h, sp.inv_h), sp);
-        s.w[t] = w;
-        s.idx[t] = t;
-        s.x[t] = x;
+        s.u.c.w[t] = w;
+        s.u.c.idx[t] = t;
+        s.u.c.x[t] = x;
         __syncthreads();
         for (uint32_t size = 2; size <= kSplitThreads; size <<= 1) {
             for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
                 uint32_t partner = t ^ stride;
                 if (partner > t) {
                     bool up = (t & size) == 0;
-                    float wa = s.w[t], wb = s.w[partner];
-                    uint32_t ia = s.idx[t], ib = s.idx[partner];
+                    float wa = s.u.c.w[t], wb = s.u.c.w[partner];
+                    uint32_t ia = s.u.c.idx[t], ib = s.u.c.idx[partner];
                     // (weight, index) order == std::stable_sort by `<` on weight
                     bool a_gt_b = (wb < wa) || (!(wa < wb) && ib < ia);
                     if (a_gt_b == up) {
-                        s.w[t] = wb; s.w[partner] = wa;
-                        s.idx[t] = ib; s.idx[partner] = ia;
+                        s.u.c.w[t] = wb; s.u.c.w[partner] = wa;
+                        s.u.c.idx[t] = ib; s.u.c.idx[partner] = ia;
                     }
                 }
                 __syncthreads();
             }
         }
-        const uint32_t cat = s.idx[t];
-        Pair xs = t < n ? s.x[cat] : Pair{0, 0};
+        const uint32_t cat = s.u.c.idx[t];
+        Pair xs = t < n ? s.u.c.x[cat] : Pair{0, 0};
         Pair tot;
         Pair excl = block_excl_scan_pair<kSplitThreads>(xs, s.warp_tot, tot);
         const uint32_t n_scan = min(a.max_cat_threshold, n);
@@ -873,11 +1123,10 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
         __syncthreads();
         if ((b.flags & 1u) && t < b.bin) atomicOr(&s.set_words[cat >> 5], 1u << (cat & 31));
         __syncthreads();
+        for (uint32_t wi = t; wi < W; wi += blockDim.x) cw[wi] = wi < 8 ? s.set_words[wi] : 0u;
         if (t == 0) {
             b.feat = f;
             *out = b;
-            uint32_t* cw = a.feat_cats + ((size_t)node * F + f) * 8;
-            for (int wi = 0; wi < 8; wi++) cw[wi] = s.set_words[wi];
         }
         return;
     }
@@ -977,8 +1226,11 @@ __global__ void k_split_node(LevelArgs a) {
         }
         a.node_best[node] = r;
     }
-    if (have && lane < 8 && a.is_cat && a.is_cat[bf])
-        a.node_cats[node * 8 + lane] = a.feat_cats[((size_t)node * F + bf) * 8 + lane];
+    if (have && a.is_cat && a.is_cat[bf]) {
+        const uint32_t W = a.cat_words;
+        const uint32_t* src = a.feat_cats + ((size_t)node * a.n_cat + a.cat_slot[bf]) * W;
+        for (uint32_t w = lane; w < W; w += 32) a.node_cats[(size_t)node * W + w] = src[w];
+    }
 }
 
 // Depthwise decisions of one level (one CTA): the max_leaves budget in node
@@ -1027,9 +1279,7 @@ __device__ void decide_body(const LevelArgs& a, uint32_t* wt) {
                 p.left = L; p.right = Rt; p.feat = b.feat; p.bin = b.bin; p.gain = b.gain; p.leaf = 0.0f;
                 p.hess = a.trec[ni.tree_id].hess;
                 p.flags = ((b.flags & 2u) ? 2u : 0u) | (is_cat ? 4u : 0u);
-                a.trec[ni.tree_id] = p;
-                if (is_cat)
-                    for (int w = 0; w < 8; w++) a.tcats[(size_t)ni.tree_id * 8 + w] = __ldcg(&a.node_cats[i * 8 + w]);
+                a.trec[ni.tree_id] = p;  // a categorical node's set is in tcats already (k_split_node_decide)
                 TreeRec cl{-1, -1, 0, 0, 0.0f, __fmul_rn(wl, sp.eta), __double2float_rn(lh), 1u};
                 TreeRec cr{-1, -1, 0, 0, 0.0f, __fmul_rn(wr, sp.eta), __double2float_rn(rh), 1u};
                 a.trec[L] = cl;
@@ -1092,21 +1342,44 @@ __global__ void __launch_bounds__(256) k_split_node_decide(LevelArgs a) {
             }
             a.node_best[node] = r;
         }
-        if (have && lane < 8 && a.is_cat && a.is_cat[bf])
-            a.node_cats[node * 8 + lane] = a.feat_cats[((size_t)node * F + bf) * 8 + lane];
+        if (have && a.is_cat && a.is_cat[bf]) {
+            // the set goes to the node's tree record too (read only if decide_body splits the node)
+            const uint32_t W = a.cat_words;
+            const uint32_t* src = a.feat_cats + ((size_t)node * a.n_cat + a.cat_slot[bf]) * W;
+            const size_t tid = (size_t)a.nodes[node].tree_id;
+            for (uint32_t w = lane; w < W; w += 32) {
+                const uint32_t v = src[w];
+                a.node_cats[(size_t)node * W + w] = v;
+                a.tcats[tid * W + w] = v;
+            }
+        }
     }
     if (last_block_done(a.fuse + 0)) decide_body<256>(a, wt);
 }
 
 // ------------------------------------------------------------------ partition
+// categorical.rs:330-345: a code in the set goes right; codes beyond the set's words go left
+__device__ __forceinline__ bool cat_left(const uint32_t* cats, uint32_t words, uint32_t bin) {
+    return bin >= 32u * words || ((cats[bin >> 5] >> (bin & 31)) & 1u) == 0u;
+}
+
 __device__ __forceinline__ bool goes_left(const LevelArgs& a, const SplitDesc& sd, const uint32_t* cats,
                                           uint32_t row) {
     const FeatLoc fl = a.floc[sd.feat];
     const uint8_t* p = fl.base + (size_t)row * fl.stride + fl.byte_off;
     uint32_t bin = fl.width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
     if (bin == fl.missing) return (sd.flags & 2u) != 0;
-    if (sd.flags & 4u) return bin >= 256u || ((cats[bin >> 5] >> (bin & 31)) & 1u) == 0u;
+    if (sd.flags & 4u) return cat_left(cats, a.cat_words, bin);
     return bin < sd.bin;
+}
+
+// The category set of node j of the level: copied to shared memory when it
+// is the usual 8 words (cats_s), else read in place.
+__device__ __forceinline__ const uint32_t* node_set(const LevelArgs& a, uint32_t j, uint32_t* cats_s) {
+    const uint32_t* g = a.node_cats + (size_t)j * a.cat_words;
+    if (a.cat_words != 8u) return g;
+    if (threadIdx.x < 8) cats_s[threadIdx.x] = g[threadIdx.x];
+    return cats_s;
 }
 
 // Count the left rows of every chunk of a split node; add the leaf value to
@@ -1142,7 +1415,7 @@ __device__ __forceinline__ void part_count_work(const LevelArgs& a) {
         if (threadIdx.x == 0) a.chunk_left[c] = 0u;
         return;
     }
-    if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
+    const uint32_t* set = node_set(a, j, cats);
     const FeatLoc fl = a.floc[sd.feat];
     __syncthreads();
     uint32_t bin[kPartItems];
@@ -1159,7 +1432,7 @@ __device__ __forceinline__ void part_count_work(const LevelArgs& a) {
     for (int k = 0; k < kPartItems; k++) {
         bool left;
         if (bin[k] == fl.missing) left = (sd.flags & 2u) != 0;
-        else if (sd.flags & 4u) left = bin[k] >= 256u || ((cats[bin[k] >> 5] >> (bin[k] & 31)) & 1u) == 0u;
+        else if (sd.flags & 4u) left = cat_left(set, a.cat_words, bin[k]);
         else left = bin[k] < sd.bin;
         if (i0 + k < cnt && left) flags |= 1u << k;
     }
@@ -1223,11 +1496,11 @@ __device__ __forceinline__ void part_scatter_work(const LevelArgs& a) {
     if (a.dirflags) {
         flags = a.dirflags[(size_t)c * kPartThreads + threadIdx.x];
     } else {
-        if (threadIdx.x < 8) cats[threadIdx.x] = a.node_cats[j * 8 + threadIdx.x];
+        const uint32_t* set = node_set(a, j, cats);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < kPartItems; k++)
-            if (i0 + k < cnt && goes_left(a, sd, cats, r[k])) flags |= 1u << k;
+            if (i0 + k < cnt && goes_left(a, sd, set, r[k])) flags |= 1u << k;
     }
     const uint32_t nl = (uint32_t)__popc(flags);
     uint32_t L;
@@ -1484,7 +1757,7 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
                 }
                 bool left;
                 if (bin == missing) left = (flags & 2u) != 0;
-                else if (flags & 4u) left = bin >= 256u || ((a.tcats[(size_t)node * 8 + (bin >> 5)] >> (bin & 31)) & 1u) == 0u;
+                else if (flags & 4u) left = cat_left(a.tcats + (size_t)node * a.cat_words, a.cat_words, bin);
                 else left = bin < sbin;
                 node = left ? left_id : right_id;
             }

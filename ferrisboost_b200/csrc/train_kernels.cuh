@@ -98,9 +98,14 @@ struct LevelArgs {
     const Pair* hist_prev;       // full histograms of the previous level
     unsigned long long slot_pairs; // pairs per histogram slot (total bins)
     SplitRec* feat_best;         // [node * F + f]
-    uint32_t* feat_cats;         // [node * F + f][8]
+    // category sets: cat_words 32-bit words each (>= 8; a bit per code, set =
+    // right-going); codes at or beyond 32 * cat_words go left
+    uint32_t cat_words;
+    const uint32_t* cat_slot;    // per feature: its index among the categorical features
+    uint32_t n_cat;              // categorical features
+    uint32_t* feat_cats;         // [node * n_cat + cat_slot[f]][cat_words]
     SplitRec* node_best;         // [node]
-    uint32_t* node_cats;         // [node][8]
+    uint32_t* node_cats;         // [node][cat_words]
     SplitDesc* split;            // [node]
     uint32_t* chunk_left;        // per chunk left count
     uint32_t* chunk_off;         // per chunk left offset within its node
@@ -111,7 +116,7 @@ struct LevelArgs {
     uint32_t* rows_next;
     float* pred;
     TreeRec* trec;
-    uint32_t* tcats;             // [tree node][8]
+    uint32_t* tcats;             // [tree node][cat_words]
     const uint32_t* node_hist;   // lossguide: histogram-pool slot of each node (null: level slots)
     unsigned int* fuse;          // depthwise: 3 zeroed counters; the one-CTA steps run in the last CTA
                                  // of the kernel before them (null: separate launches)
@@ -149,7 +154,7 @@ struct GradArgs {
 
 // Host-side launchers (train_kernels.cu).
 void launch_mask_max(const GradArgs& a, cudaStream_t s);
-// mode 0: e from host_exp (or squared error), 1: CUDA expf (fast mode),
+// mode 0: e from host_exp (or squared error), 1: fexp_core alone (fast mode),
 // 2: the host C library's expf reproduced on the device (fexp_core + exptab).
 void launch_gradient_max(const GradArgs& a, int mode, cudaStream_t s);
 void launch_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint32_t count, uint32_t* out,
@@ -158,7 +163,7 @@ void launch_gradient_quantize_exp(const GradArgs& a, cudaStream_t s);
 void launch_quantize(const GradArgs& a, cudaStream_t s);
 // objective.rs:1175-1219 softmax gradients of K classes: margins a.pred
 // (K x a.n, class-major), labels, optional weights -> out (K x a.n f32 pairs,
-// class-major).  fast: CUDA expf; else the host expf (a.exptab).
+// class-major).  fast: fexp_core alone; else the host expf (a.exptab).
 void launch_softmax_gradients(const GradArgs& a, uint32_t K, float* out, int fast, cudaStream_t s);
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
                           cudaStream_t s);

@@ -199,6 +199,11 @@ int64_t fb_model_json(const fb_model* m, char* buf, int64_t cap);
  * receives 8 words per node (the right-going category set). */
 int64_t fb_model_tree(const fb_model* m, uint32_t t, int32_t* left, int32_t* right, uint32_t* feat, float* cond,
                       uint8_t* default_left, float* leaf, uint8_t* is_leaf, float* gain, float* hess, uint32_t* cats);
+/* The right-going category set of node `node` of tree t: returns its length
+ * in 32-bit words (0 for a numeric split or a leaf, -1 for a bad index) and
+ * copies at most cap words to out.  fb_model_tree's cats holds only the
+ * first 8 words (codes < 256). */
+int64_t fb_model_node_cats(const fb_model* m, uint32_t t, uint32_t node, uint32_t* out, uint32_t cap);
 /* Raw margins of host rows, computed on the device: n values, or n x K
  * (row-major) for a multiclass model of K outputs (src/model/tree.rs:468-480
  * predict_margins_upto). */

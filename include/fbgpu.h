@@ -78,7 +78,9 @@ typedef struct fbgpu_tree_params {
 /* A grown tree (model/tree.rs:52-79 Node, arrays by node id).  The caller
  * provides arrays of `capacity` entries (2^(max_depth+1) - 1 suffices);
  * `bin` is the right-boundary bin of a numeric split (split.rs:17-52) and
- * cats holds 8 words (the right-going category set) per node. */
+ * cats holds cat_words words (the right-going category set, a bit per code)
+ * per node: at least fbgpu_ctx_cat_words(ctx), which is 8 unless a
+ * categorical feature has more than 256 codes (0 is read as 8). */
 typedef struct fbgpu_tree_out {
     uint32_t capacity;
     uint32_t n_nodes;
@@ -90,11 +92,15 @@ typedef struct fbgpu_tree_out {
     float* leaf;
     float* hess;
     uint32_t* flags;            /* bit0 leaf, bit1 default_left, bit2 categorical */
-    uint32_t* cats;             /* 8 words per node, may be NULL */
+    uint32_t* cats;             /* cat_words words per node, may be NULL */
+    uint32_t cat_words;
+    uint32_t reserved;
 } fbgpu_tree_out;
 
 /* Result of one node's split search (split.rs:17-52 SplitCandidate;
- * backend/cuda/histogram.cu:6-11 SplitPacket). */
+ * backend/cuda/histogram.cu:6-11 SplitPacket).  cats: the first 8 words of
+ * a categorical split's right-going set (codes < 256); fbgpu_split_cats
+ * returns the whole set. */
 typedef struct fbgpu_split {
     uint32_t found;
     uint32_t feat;
@@ -204,8 +210,12 @@ fbgpu_status fbgpu_round_from_exp(fbgpu_ctx* ctx, int32_t objective, const float
                                   uint64_t sub_threshold, uint64_t seed, uint64_t tree, const double* scales);
 
 /* Round start with the gradient computed on the device from the resident
- * margins.  fast = 1 is gpu_math="fast" (CUDA expf; replaces
- * fast_gradient_and_quantize, src/backend/mod.rs:220-228); fast = 0 is exact
+ * margins.  fast = 1 is gpu_math="fast" (replaces fast_gradient_and_quantize,
+ * src/backend/mod.rs:220-228): no host synchronisation, the power-of-two
+ * scales taken on the device, and exp evaluated in f64 and rounded once to
+ * f32 (within one unit in the last place of the host expf, equal on all but
+ * about 0.004 % of the inputs; the reference's fast mode uses CUDA's expf,
+ * which differs on about 7 %); fast = 0 is exact
  * mode with the scales taken by the host's libm: squared error is pure f32
  * arithmetic, logistic uses the device reproduction of the host expf
  * (fbgpu_exact_exp_available must be 1).
@@ -287,6 +297,24 @@ fbgpu_status fbgpu_eval_split(fbgpu_ctx* ctx, const int64_t* hist, const int64_t
  * (src/backend/mod.rs:468-483). cats: 8 words or NULL. */
 fbgpu_status fbgpu_partition(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat, uint32_t bin,
                              int32_t missing_left, const uint32_t* cats, uint32_t* out_rows, uint64_t* n_left);
+
+/* fbgpu_partition by a category set of any width: n_words words, a bit per
+ * code (codes beyond them go left).  Replaces
+ * GpuPartitionSession::partition_categorical (src/backend/mod.rs:476-483)
+ * for features of up to 65534 codes (src/data/categorical.rs:19-28). */
+fbgpu_status fbgpu_partition_set(fbgpu_ctx* ctx, const uint32_t* rows, uint64_t n, uint32_t feat,
+                                 int32_t missing_left, const uint32_t* cats, uint32_t n_words, uint32_t* out_rows,
+                                 uint64_t* n_left);
+
+/* Words of a category set in this context: 8, or ceil(bins / 32) of its
+ * widest categorical feature (fbgpu_tree_out.cat_words must be at least
+ * this).  No counterpart in the reference, whose bitsets are Vec<u32>. */
+uint32_t fbgpu_ctx_cat_words(const fbgpu_ctx* ctx);
+
+/* The whole right-going category set of the last fbgpu_eval_split (n_words
+ * words; FBGPU_EINPUT if the set does not fit).  Completes fbgpu_split.cats
+ * for features of more than 256 codes. */
+fbgpu_status fbgpu_split_cats(fbgpu_ctx* ctx, uint32_t* out, uint32_t n_words);
 
 /* Stable partition of device row ids by one numeric or categorical split,
  * allocating no device memory.  No counterpart in the reference: it exists for

@@ -87,6 +87,20 @@ class Ctx:
         return out, nl.value
 
 
+    def cat_words(self):
+        return lib().fbgpu_ctx_cat_words(self.h)
+
+    def partition_set(self, rows, feat, missing_left, words):
+        rows = np.ascontiguousarray(rows, dtype=np.uint32)
+        out = np.zeros_like(rows)
+        nl = C.c_uint64()
+        cw = np.ascontiguousarray(words, dtype=np.uint32)
+        check(lib().fbgpu_partition_set(self.h, _lib.ptr(rows, C.c_uint32), len(rows), feat, int(missing_left),
+                                        _lib.ptr(cw, C.c_uint32), len(cw), _lib.ptr(out, C.c_uint32),
+                                        C.byref(nl)), self.h)
+        return out, nl.value
+
+
 def random_bins(rng, n, nbins, miss_rate=0.05):
     """Column-major random bins with per-width missing sentinels."""
     F = len(nbins)

@@ -99,3 +99,42 @@ def test_device_explain_entry_point_matches_host():
     bad = np.zeros(1, np.float32)
     assert lib.fbgpu_explain(h, 7, _lib.ptr(np.zeros((1, 10), np.float32), C.c_float), 1,
                              _lib.ptr(bad, C.c_float)) != 0
+
+
+def test_wide_models_explain_like_the_oracle(oracle):
+    # configs[2]-shaped (2000 features, colsample_bytree 0.5): interaction
+    # matrices of 2001 x 2001 per row are accumulated in global memory, and
+    # Saabas values of rows wider than shared memory in the output rows
+    rng = np.random.default_rng(11)
+    n, F = 20000, 2000
+    X = rng.uniform(-1.0, 1.0, (n, F)).astype(np.float32)
+    idx = rng.choice(F, 50, replace=False)
+    y = ((X[:, idx] @ rng.standard_normal(50) + rng.normal(0.0, 0.1, n)) > 0).astype(np.float32)
+    p = dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=64, colsample_bytree=0.5)
+    m = fb.train(p, X, label=y, num_boost_round=8)
+    ref = oracle.train(X, y, n_rounds=8, **p)
+    assert m.to_json() == ref.json()
+    Xt = rng.uniform(-1.0, 1.0, (6, F)).astype(np.float32)
+    Xt[0, idx[:5]] = np.nan
+    got = m.predict(Xt, pred_interactions=True)
+    want = ref.interactions(Xt)
+    assert got.shape == (6, F + 1, F + 1)
+    assert np.max(np.abs(got - want)) <= 1e-5
+    np.testing.assert_allclose(got.sum(axis=2), m.predict(Xt, pred_contribs=True), atol=1e-4)
+    Xa = rng.uniform(-1.0, 1.0, (300, F)).astype(np.float32)
+    approx = m.predict(Xa, pred_contribs=True, approx_contribs=True)
+    assert np.array_equal(approx.view(np.uint32), ref.approx_contribs(Xa).view(np.uint32))
+
+
+def test_interactions_with_wide_category_sets(oracle):
+    from test_gpu_wide_categorical import wide_data
+    X, y, ft = wide_data(30000, [1200], seed=12)
+    p = dict(objective="reg:squarederror", max_depth=5, eta=0.3, max_bin=64)
+    m = fb.train(p, X, label=y, num_boost_round=4, feature_types=ft)
+    ref = oracle.train(X, y, n_rounds=4, categorical=np.array([t == "c" for t in ft], np.uint8), **p)
+    assert m.to_json() == ref.json()
+    Xt, _, _ = wide_data(300, [1200], seed=13)
+    Xt[:4, -1] = [5000.0, -1.0, 0.5, np.nan]
+    got = m.predict(Xt, pred_interactions=True)
+    assert np.max(np.abs(got - ref.interactions(Xt))) <= 1e-5
+    assert np.max(np.abs(m.predict(Xt, pred_contribs=True) - ref.shap(Xt))) <= 1e-5
