@@ -102,6 +102,7 @@ SIGNATURES = {
     "fbgpu_split_cats": (C.c_int, [P, u32p, C.c_uint32]),
     "fbgpu_partition_noalloc": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint64,
                                          C.c_uint32, C.c_int32, u32p, P, P, P]),
+    "fbgpu_hist_atomic_ceiling": (C.c_int, [C.c_int32, C.c_int32, C.c_uint32, f64p]),
     "fbgpu_model_create": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, u32p, i32p, i32p, u32p, f32p, u8p, f32p,
                                      u32p, u32p, u32p, C.c_uint64, C.c_float, C.POINTER(P)]),
     "fbgpu_model_destroy": (None, [P]),

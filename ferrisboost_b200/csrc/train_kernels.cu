@@ -590,6 +590,17 @@ __device__ __forceinline__ void add64_planes(uint32_t* lo, uint32_t* hi, long lo
     atomicAdd(hi, hi_add);
 }
 
+// The high-word addend of a 64-bit add whose low word went through a
+// returning atomic that found `old`: the addend's high word plus the carry.
+__device__ __forceinline__ uint32_t carry_into_high(uint32_t old, long long v) {
+    const uint32_t vl = (uint32_t)v, vh = (uint32_t)((unsigned long long)v >> 32);
+    uint32_t sum, hi_add;
+    asm("add.cc.u32 %0, %2, %3;\n\taddc.u32 %1, %4, 0;" : "=r"(sum), "=r"(hi_add) : "r"(old), "r"(vl), "r"(vh));
+    (void)sum;
+    return hi_add;
+}
+constexpr uint32_t kHistGroup = 4;
+
 template <int W, int S, int LPR>
 __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* __restrict__ tiles,
                                                                  const TileFeat* __restrict__ tfeat,
@@ -712,8 +723,34 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
             };
             if (LPR == 32) {
                 if (kq == kStageRows) {
+                    // kHistGroup rows at a time: their returning low-word atomics
+                    // first, then the high words with the carries, so several
+                    // returns are in flight instead of one chain per row (the
+                    // carries are per atomic, so any interleaving sums exactly)
 #pragma unroll
-                    for (uint32_t q = 0; q < kStageRows; q++) row(q);
+                    for (uint32_t q0 = 0; q0 < kStageRows; q0 += kHistGroup) {
+                        uint32_t* wq[kHistGroup];
+                        Pair gq[kHistGroup];
+                        uint32_t og[kHistGroup], oh[kHistGroup];
+#pragma unroll
+                        for (uint32_t u = 0; u < kHistGroup; u++) {
+                            const uint8_t* p = pr + (q0 + u) * rec_bytes;
+                            uint32_t bin = W == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+                            bin = bin < nbins ? bin : discard;
+                            wq[u] = hlane + bin * 128u;
+                            gq[u] = gps[q0 + u];
+                        }
+#pragma unroll
+                        for (uint32_t u = 0; u < kHistGroup; u++) {
+                            og[u] = atomicAdd(wq[u], (uint32_t)gq[u].g);
+                            oh[u] = atomicAdd(wq[u] + 64, (uint32_t)gq[u].h);
+                        }
+#pragma unroll
+                        for (uint32_t u = 0; u < kHistGroup; u++) {
+                            atomicAdd(wq[u] + 32, carry_into_high(og[u], gq[u].g));
+                            atomicAdd(wq[u] + 96, carry_into_high(oh[u], gq[u].h));
+                        }
+                    }
                 } else {
                     for (uint32_t q = 0; q < kq; q++) row(q);
                 }

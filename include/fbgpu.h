@@ -344,6 +344,17 @@ fbgpu_status fbgpu_partition_noalloc(const void* bins, uint32_t stride, uint32_t
                                      int32_t missing_left, const uint32_t* cats, uint32_t* out_rows,
                                      uint32_t* n_left, void* stream);
 
+/* Updates per second of the exact histogram update alone (no reference
+ * counterpart: a measurement of this engine's shared-memory atomic ceiling).
+ * Every (row, feature) update adds a gradient pair as two 64-bit sums modulo
+ * 2^64 to a 256-bin shared histogram, with rows generated in registers, on
+ * every SM of `device`; scheme 0 is the histogram kernel's (returning
+ * low-word atomic, carry into the high word), 1 the same with the low-word
+ * atomics of 4 updates issued first, 2 native 64-bit shared atomics, 3 four
+ * non-returning 32-bit atomics (not exact: the pipe's ceiling).  iters:
+ * updates per thread, a multiple of 8. */
+fbgpu_status fbgpu_hist_atomic_ceiling(int32_t device, int32_t scheme, uint32_t iters, double* updates_per_s);
+
 /* ---------------------------------------------------------- explanation models */
 
 /* A model for device prediction and SHAP.  Node arrays of all trees back to
