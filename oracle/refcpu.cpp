@@ -33,6 +33,7 @@
 #include <queue>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 #ifdef _OPENMP
 #include <omp.h>
@@ -903,6 +904,175 @@ Tree build_tree_depthwise(Ctx& C, const std::vector<FX>& gpair, FX root_sum, con
     return t;
 }
 
+// Row-sharded depthwise growth with threads as ranks: the device engine's
+// multi-GPU design restated on the CPU, to show it grows the reference's
+// trees.  Rank r holds rows [n r / N, n (r + 1) / N) and its own row buffers;
+// per level every rank (a thread) builds partial histograms of the accumulate
+// nodes over its own rows, a fake collective sums them modulo 2^64 in rank
+// order, and each rank partitions its own rows.  No row counts are
+// exchanged: the accumulated child is the one with the smaller global
+// hessian sum (left on ties), which changes which histogram is built, never
+// its integers.  With feature_sharded the sum is a reduce-scatter by feature
+// range: rank r scores splits on its own features only, and the per-node
+// winners are gathered in rank order, a strictly greater gain replacing the
+// current winner, so equal gains keep the lower feature as best_split does.
+struct ShardMode {
+    int ranks = 0;
+    bool feature_sharded = false;
+};
+thread_local ShardMode g_shard;
+
+Tree build_tree_depthwise_sharded(Ctx& C, const std::vector<FX>& gpair, FX root_sum, const Quantizer& q,
+                                  std::vector<float>& preds, const uint8_t* enabled, int N, bool feat_shard) {
+    const rc_params& p = C.P.p;
+    const uint32_t F = C.cuts.n_feats();
+    Tree t;
+    int root = t.push_leaf(leaf_of(root_sum, q, p), q.hess_f32(root_sum));
+    std::vector<uint64_t> lo(N + 1);
+    for (int r = 0; r <= N; r++) lo[r] = C.n * (uint64_t)r / (uint64_t)N;
+    std::vector<std::vector<uint32_t>> cur(N), nxt(N);
+    for (int r = 0; r < N; r++) {
+        for (uint64_t i = lo[r]; i < lo[r + 1]; i++) cur[r].push_back((uint32_t)i);
+        nxt[r].resize(cur[r].size());
+    }
+    struct SNode {
+        int node;
+        std::vector<size_t> start, len;  // per rank
+        FX sum;
+        int hist_from, sibling;
+        Bounds bounds;
+    };
+    std::vector<SNode> level(1);
+    level[0].node = root;
+    level[0].sum = root_sum;
+    level[0].hist_from = level[0].sibling = -1;
+    level[0].bounds = kUnbounded;
+    for (int r = 0; r < N; r++) {
+        level[0].start.push_back(0);
+        level[0].len.push_back(cur[r].size());
+    }
+    std::vector<std::vector<FX>> parent_hists;
+    uint32_t leaf_count = 1;
+    std::vector<uint32_t> feat_lo(N + 1);
+    for (int r = 0; r <= N; r++) feat_lo[r] = (uint32_t)((uint64_t)F * r / N);
+    for (uint32_t depth = 0; depth < p.max_depth; depth++) {
+        if (level.empty() || (p.max_leaves != 0 && leaf_count >= p.max_leaves)) break;
+        std::vector<size_t> acc;
+        for (size_t i = 0; i < level.size(); i++)
+            if (level[i].hist_from < 0) acc.push_back(i);
+        // every rank: partial histograms of the accumulate nodes over its rows
+        std::vector<std::vector<std::vector<FX>>> part(N);
+        std::vector<std::thread> ranks;
+        for (int r = 0; r < N; r++) {
+            ranks.emplace_back([&, r] {
+                part[r].assign(acc.size(), std::vector<FX>(C.total_bins, FX{0, 0}));
+                std::vector<const uint32_t*> rows;
+                std::vector<size_t> lens;
+                std::vector<FX*> outs;
+                for (size_t k = 0; k < acc.size(); k++) {
+                    rows.push_back(cur[r].data() + level[acc[k]].start[r]);
+                    lens.push_back(level[acc[k]].len[r]);
+                    outs.push_back(part[r][k].data());
+                }
+                hist_nodes(C.bins, C.n, C.cuts, C.hoff, gpair, rows, lens, outs, 1);
+            });
+        }
+        for (auto& th : ranks) th.join();
+        // the collective: sums in rank order (all-reduce; a reduce-scatter
+        // delivers the same sums for each rank's own feature range)
+        std::vector<std::vector<FX>> hists(level.size());
+        for (size_t k = 0; k < acc.size(); k++) {
+            std::vector<FX>& h = hists[acc[k]];
+            h = std::move(part[0][k]);
+            for (int r = 1; r < N; r++)
+                for (uint32_t b = 0; b < C.total_bins; b++) h[b] = fx_add(h[b], part[r][k][b]);
+        }
+        for (size_t i = 0; i < level.size(); i++) {
+            if (level[i].hist_from >= 0) {
+                std::vector<FX>& ph = parent_hists[level[i].hist_from];
+                const std::vector<FX>& sib = hists[level[i].sibling];
+                for (uint32_t b = 0; b < C.total_bins; b++) ph[b] = fx_sub(ph[b], sib[b]);
+                hists[i] = std::move(ph);
+            }
+        }
+        std::vector<Cand> chosen(level.size());
+        for (size_t i = 0; i < level.size(); i++) {
+            if (!feat_shard) {
+                chosen[i] = best_split(hists[i].data(), F, C.hoff.data(), level[i].sum, q, C.P, level[i].bounds,
+                                       enabled);
+                continue;
+            }
+            Cand best;
+            for (int r = 0; r < N; r++) {  // gather of the per-rank winners, in rank order
+                std::vector<uint8_t> own(F, 0);
+                for (uint32_t f = feat_lo[r]; f < feat_lo[r + 1]; f++) own[f] = enabled ? enabled[f] : 1;
+                Cand c = best_split(hists[i].data(), F, C.hoff.data(), level[i].sum, q, C.P, level[i].bounds,
+                                    own.data());
+                if (c.found && (!best.found || c.gain > best.gain)) best = c;
+            }
+            chosen[i] = best;
+        }
+        if (p.max_leaves != 0) {
+            uint32_t remaining = p.max_leaves > leaf_count ? p.max_leaves - leaf_count : 0;
+            for (Cand& c : chosen) {
+                if (!c.found) continue;
+                if (remaining == 0) c.found = false; else remaining--;
+            }
+        }
+        std::vector<SNode> next;
+        for (size_t i = 0; i < level.size(); i++) {
+            SNode& ln = level[i];
+            Cand& c = chosen[i];
+            if (!c.found) {
+                float v = t.nodes[ln.node].leaf;
+                for (int r = 0; r < N; r++)
+                    for (size_t k = 0; k < ln.len[r]; k++) preds[cur[r][ln.start[r] + k]] += v;
+                continue;
+            }
+            const uint16_t* col = C.bins.data() + (size_t)c.feat * C.n;
+            SNode L, Rn;
+            for (int r = 0; r < N; r++) {  // each rank partitions its own rows
+                size_t nl = partition_rows(cur[r].data() + ln.start[r], ln.len[r], nxt[r].data() + ln.start[r], col,
+                                           C.cuts.missing(c.feat), c);
+                L.start.push_back(ln.start[r]);
+                L.len.push_back(nl);
+                Rn.start.push_back(ln.start[r] + nl);
+                Rn.len.push_back(ln.len[r] - nl);
+            }
+            leaf_count++;
+            float lv, rv;
+            Bounds lb, rb;
+            child_values(c, q, p, ln.bounds, C.P.mono_of(c.feat), lv, rv, lb, rb);
+            int l, r;
+            t.split_leaf(ln.node, c.feat, c.is_cat ? 0.0f : C.cuts.threshold(c.feat, c.bin), c.missing_left, c.gain,
+                         lv, q.hess_f32(c.left), rv, q.hess_f32(c.right), l, r);
+            if (c.is_cat) {
+                t.nodes[ln.node].is_cat = true;
+                t.nodes[ln.node].cats = c.cats;
+                t.nodes[ln.node].cond = std::numeric_limits<float>::denorm_min();
+            }
+            // the smaller child by global hessian sum (signed compare, as the device does)
+            const int small = c.left.h <= c.right.h ? 0 : 1;
+            const int slot = (int)next.size();
+            L.node = l; L.sum = c.left; L.bounds = lb; L.hist_from = L.sibling = -1;
+            Rn.node = r; Rn.sum = c.right; Rn.bounds = rb; Rn.hist_from = Rn.sibling = -1;
+            if (small == 0) { Rn.hist_from = (int)i; Rn.sibling = slot; }
+            else { L.hist_from = (int)i; L.sibling = slot + 1; }
+            next.push_back(std::move(L));
+            next.push_back(std::move(Rn));
+        }
+        parent_hists = std::move(hists);
+        std::swap(cur, nxt);
+        level = std::move(next);
+    }
+    for (const SNode& ln : level) {
+        float v = t.nodes[ln.node].leaf;
+        for (int r = 0; r < N; r++)
+            for (size_t k = 0; k < ln.len[r]; k++) preds[cur[r][ln.start[r] + k]] += v;
+    }
+    return t;
+}
+
 // training/lossguide.rs:506-700 grow (best-first).
 Tree build_tree_lossguide(Ctx& C, const std::vector<FX>& gpair, FX root_sum, const Quantizer& q,
                           std::vector<float>& preds, const uint8_t* enabled) {
@@ -1163,7 +1333,10 @@ Model* train_impl(const float* X, uint64_t n, uint32_t F, const float* y, const 
         }
         const uint8_t* en = enabled.empty() ? nullptr : enabled.data();
         Tree t = p.grow_policy == 1 ? build_tree_lossguide(C, fixed, root_sum, q, preds, en)
-                                    : build_tree_depthwise(C, fixed, root_sum, q, preds, en);
+                 : g_shard.ranks > 1
+                     ? build_tree_depthwise_sharded(C, fixed, root_sum, q, preds, en, g_shard.ranks,
+                                                    g_shard.feature_sharded)
+                     : build_tree_depthwise(C, fixed, root_sum, q, preds, en);
         m->trees.push_back(std::move(t));
         g_round_s.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t_round).count());
     }
@@ -1600,6 +1773,16 @@ void* rc_train(const float* X, uint64_t n, uint32_t F, const float* y, const flo
         g_err = e.what();
         return nullptr;
     }
+}
+
+void* rc_train_sharded(const float* X, uint64_t n, uint32_t F, const float* y, const float* w, const rc_params* p,
+                       int32_t n_ranks, int32_t feature_sharded) {
+    if (n_ranks < 1 || (uint64_t)n_ranks > n) { g_err = "n_ranks must be in 1..=n"; return nullptr; }
+    g_shard.ranks = n_ranks;
+    g_shard.feature_sharded = feature_sharded != 0;
+    void* m = rc_train(X, n, F, y, w, p);
+    g_shard = ShardMode{};
+    return m;
 }
 
 void rc_model_free(void* m) { delete (Model*)m; }

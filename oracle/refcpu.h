@@ -54,6 +54,13 @@ void rc_default_params(rc_params* p);
 void* rc_train(const float* X, uint64_t n, uint32_t F, const float* y,
                const float* w, const rc_params* p);
 const char* rc_last_error(void);
+/* rc_train with rows sharded over n_ranks threads as ranks (depthwise growth;
+ * lossguide trains unsharded): partial histograms per rank summed by a fake
+ * collective, the accumulated child chosen by global hessian sums, and with
+ * feature_sharded the split search split by feature range with the
+ * winners gathered.  The models must equal rc_train's. */
+void* rc_train_sharded(const float* X, uint64_t n, uint32_t F, const float* y, const float* w, const rc_params* p,
+                       int32_t n_ranks, int32_t feature_sharded);
 /* Wall seconds of the last rc_train on this thread: setup (sketch, bins) and
  * each round.  Returns the number of rounds. */
 int32_t rc_last_timing(double* setup_s, double* round_s, int32_t cap);

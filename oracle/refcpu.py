@@ -57,6 +57,9 @@ class RefCPU:
         lib.rc_train.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.c_uint32, C.POINTER(C.c_float),
                                  C.POINTER(C.c_float), C.POINTER(rc_params)]
         lib.rc_last_error.restype = C.c_char_p
+        lib.rc_train_sharded.restype = _P
+        lib.rc_train_sharded.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.c_uint32, C.POINTER(C.c_float),
+                                         C.POINTER(C.c_float), C.POINTER(rc_params), C.c_int32, C.c_int32]
         lib.rc_last_timing.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_int32]
         lib.rc_last_timing.restype = C.c_int32
         lib.rc_model_free.argtypes = [_P]
@@ -143,6 +146,19 @@ class RefCPU:
         p = self.params(**kw)
         h = self.lib.rc_train(_ptr(X, C.c_float), X.shape[0], X.shape[1], _ptr(y, C.c_float),
                               _ptr(w, C.c_float), C.byref(p))
+        if not h:
+            raise RuntimeError(self.lib.rc_last_error().decode())
+        return RefModel(self, h, X.shape[1])
+
+    def train_sharded(self, X, y, w=None, ranks=2, feature_sharded=False, **kw):
+        """train() with rows sharded over `ranks` threads as ranks (the device
+        engine's multi-GPU algorithm on the CPU); must give train()'s model."""
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        w = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+        p = self.params(**kw)
+        h = self.lib.rc_train_sharded(_ptr(X, C.c_float), X.shape[0], X.shape[1], _ptr(y, C.c_float),
+                                      _ptr(w, C.c_float), C.byref(p), ranks, int(feature_sharded))
         if not h:
             raise RuntimeError(self.lib.rc_last_error().decode())
         return RefModel(self, h, X.shape[1])
