@@ -401,9 +401,8 @@ void TrainCtx::set_labels(const float* labels, const float* weights, const float
     if (base_rows) {
         FB_CUDA_CHECK(cudaMemcpyAsync(pred_.p, base_rows, n_ * 4, cudaMemcpyHostToDevice, s_));
     } else {
-        std::vector<float> v(n_, base_margin);
-        FB_CUDA_CHECK(cudaMemcpyAsync(pred_.p, v.data(), n_ * 4, cudaMemcpyHostToDevice, s_));
-        sync();
+        launch_fill(pred_.as<float>(), n_, base_margin, s_);
+        FB_CUDA_CHECK(cudaGetLastError());
     }
     sync();
 }

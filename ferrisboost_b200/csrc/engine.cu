@@ -13,6 +13,8 @@
 #include <algorithm>
 #include <charconv>
 #include <chrono>
+#include <future>
+#include <mutex>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -28,6 +30,24 @@
 #include "sketch.cuh"
 
 namespace fbe {
+
+// FBGPU_TRACE=1: the wall time of each phase of dataset and booster
+// preparation on stderr (phase(name) closes the phase that started at the
+// previous call).
+struct PhaseTrace {
+    const char* what;
+    bool on;
+    std::chrono::steady_clock::time_point t;
+    explicit PhaseTrace(const char* w)
+        : what(w), on(std::getenv("FBGPU_TRACE") != nullptr), t(std::chrono::steady_clock::now()) {}
+    void operator()(const char* name) {
+        if (!on) return;
+        const auto now = std::chrono::steady_clock::now();
+        std::fprintf(stderr, "[fbgpu] %s %-14s %8.3f ms\n", what, name,
+                     std::chrono::duration<double, std::milli>(now - t).count());
+        t = now;
+    }
+};
 
 using fbg::InputError;
 thread_local std::string g_err;
@@ -414,16 +434,7 @@ Dataset* dataset_on_device(const fbg::HostMatrix& X, uint64_t n, uint32_t F, uin
     d->device = device;
     d->cat.assign(F, 0);
     if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
-    // FBGPU_TRACE=1: wall time of each preparation phase on stderr
-    static const bool trace = std::getenv("FBGPU_TRACE") != nullptr;
-    auto tp = std::chrono::steady_clock::now();
-    auto phase = [&](const char* what) {
-        if (!trace) return;
-        const auto now = std::chrono::steady_clock::now();
-        std::fprintf(stderr, "[fbgpu] dataset %-14s %8.3f ms\n", what,
-                     std::chrono::duration<double, std::milli>(now - tp).count());
-        tp = now;
-    };
+    PhaseTrace phase("dataset");
     fbg::DeviceMatrix M(X, n, F, s);
     phase("rows to device");
     if (cuts) {
@@ -552,9 +563,72 @@ std::string display_f32(float v) {  // Rust Display for f32
     return o;
 }
 
-std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order of tree.rs:1167-1257
+static void json_iarr(std::string& o, const std::vector<int64_t>& v) {
+    o.push_back('[');
+    for (size_t i = 0; i < v.size(); i++) { if (i) o.push_back(','); o += std::to_string(v[i]); }
+    o.push_back(']');
+}
+static void json_farr(std::string& o, const std::vector<float>& v) {
+    o.push_back('[');
+    for (size_t i = 0; i < v.size(); i++) { if (i) o.push_back(','); o += json_f32(v[i]); }
+    o.push_back(']');
+}
+
+// One tree's JSON object (tree.rs:600-750, serde field order of tree.rs:1167-1257).
+static std::string tree_json(const Model& m, size_t ti) {
+    const std::vector<Node>& N = m.trees[ti].nodes;
+    const size_t nn = N.size();
     std::string o;
-    o.reserve(256 + m.trees.size() * 4096);
+    o.reserve(64 + nn * 96);
+    std::vector<float> bw(nn), lc(nn), sc(nn), sh(nn);
+    std::vector<int64_t> dl(nn), lch(nn), rch(nn), par(nn, 2147483647), si(nn), st(nn, 0), cats, cnodes, cseg, csz;
+    for (size_t i = 0; i < nn; i++) {
+        const Node& nd = N[i];
+        lch[i] = nd.left; rch[i] = nd.right; dl[i] = nd.default_left; lc[i] = nd.gain; sh[i] = nd.hess;
+        if (nd.is_leaf) { sc[i] = nd.leaf; si[i] = 0; bw[i] = nd.leaf; continue; }
+        sc[i] = nd.cond; si[i] = nd.feat; bw[i] = 0.0f;
+        par[nd.left] = (int64_t)i; par[nd.right] = (int64_t)i;
+        if (nd.is_cat) {
+            st[i] = 1;
+            cnodes.push_back((int64_t)i);
+            cseg.push_back((int64_t)cats.size());
+            int64_t c = 0;
+            for (size_t w = 0; w < nd.cats.size(); w++)
+                for (int b = 0; b < 32; b++)
+                    if ((nd.cats[w] >> b) & 1u) { cats.push_back((int64_t)(w * 32 + b)); c++; }
+            csz.push_back(c);
+        }
+    }
+    o += "{\"base_weights\":"; json_farr(o, bw);
+    o += ",\"categories\":"; json_iarr(o, cats);
+    o += ",\"categories_nodes\":"; json_iarr(o, cnodes);
+    o += ",\"categories_segments\":"; json_iarr(o, cseg);
+    o += ",\"categories_sizes\":"; json_iarr(o, csz);
+    o += ",\"default_left\":"; json_iarr(o, dl);
+    o += ",\"id\":" + std::to_string(ti);
+    o += ",\"left_children\":"; json_iarr(o, lch);
+    o += ",\"loss_changes\":"; json_farr(o, lc);
+    o += ",\"parents\":"; json_iarr(o, par);
+    o += ",\"right_children\":"; json_iarr(o, rch);
+    o += ",\"split_conditions\":"; json_farr(o, sc);
+    o += ",\"split_indices\":"; json_iarr(o, si);
+    o += ",\"split_type\":"; json_iarr(o, st);
+    o += ",\"sum_hessian\":"; json_farr(o, sh);
+    o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
+         "\",\"num_nodes\":\"" + std::to_string(nn) + "\",\"size_leaf_vector\":\"1\"}}";
+    return o;
+}
+
+std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order of tree.rs:1167-1257
+    const size_t nt = m.trees.size(), K = m.outputs();
+    // the trees' objects are independent: formatted in parallel, joined in order
+    std::vector<std::string> parts(nt);
+#pragma omp parallel for schedule(dynamic, 4) if (nt >= 16)
+    for (int64_t ti = 0; ti < (int64_t)nt; ti++) parts[ti] = tree_json(m, (size_t)ti);
+    size_t total = 1024;
+    for (const std::string& t : parts) total += t.size() + 1;
+    std::string o;
+    o.reserve(total + 16 * nt);
     o += "{\"version\":[2,0,0],\"learner\":{\"attributes\":{},\"feature_names\":[],\"feature_types\":[";
     bool any = std::any_of(m.feature_types.begin(), m.feature_types.end(), [](uint8_t c) { return c != 0; });
     if (any)
@@ -562,7 +636,6 @@ std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order 
             if (f) o.push_back(',');
             o += m.feature_types[f] ? "\"c\"" : "\"q\"";
         }
-    const size_t nt = m.trees.size(), K = m.outputs();
     o += "],\"gradient_booster\":{\"name\":\"gbtree\",\"model\":{\"gbtree_model_param\":{\"num_trees\":\"" +
          std::to_string(nt) + "\",\"num_parallel_tree\":\"1\"},\"iteration_indptr\":[";
     // tree.rs:688-697: K trees per round, tree t belongs to output t % K
@@ -571,56 +644,9 @@ std::string model_json(const Model& m) {  // tree.rs:600-750, serde field order 
     o += "],\"tree_info\":[";
     for (size_t i = 0; i < nt; i++) { if (i) o.push_back(','); o += std::to_string(i % K); }
     o += "],\"trees\":[";
-    auto iarr = [&](const std::vector<int64_t>& v) {
-        o.push_back('[');
-        for (size_t i = 0; i < v.size(); i++) { if (i) o.push_back(','); o += std::to_string(v[i]); }
-        o.push_back(']');
-    };
-    auto farr = [&](const std::vector<float>& v) {
-        o.push_back('[');
-        for (size_t i = 0; i < v.size(); i++) { if (i) o.push_back(','); o += json_f32(v[i]); }
-        o.push_back(']');
-    };
     for (size_t ti = 0; ti < nt; ti++) {
-        const std::vector<Node>& N = m.trees[ti].nodes;
-        const size_t nn = N.size();
-        std::vector<float> bw(nn), lc(nn), sc(nn), sh(nn);
-        std::vector<int64_t> dl(nn), lch(nn), rch(nn), par(nn, 2147483647), si(nn), st(nn, 0), cats, cnodes, cseg, csz;
-        for (size_t i = 0; i < nn; i++) {
-            const Node& nd = N[i];
-            lch[i] = nd.left; rch[i] = nd.right; dl[i] = nd.default_left; lc[i] = nd.gain; sh[i] = nd.hess;
-            if (nd.is_leaf) { sc[i] = nd.leaf; si[i] = 0; bw[i] = nd.leaf; continue; }
-            sc[i] = nd.cond; si[i] = nd.feat; bw[i] = 0.0f;
-            par[nd.left] = (int64_t)i; par[nd.right] = (int64_t)i;
-            if (nd.is_cat) {
-                st[i] = 1;
-                cnodes.push_back((int64_t)i);
-                cseg.push_back((int64_t)cats.size());
-                int64_t c = 0;
-                for (size_t w = 0; w < nd.cats.size(); w++)
-                    for (int b = 0; b < 32; b++)
-                        if ((nd.cats[w] >> b) & 1u) { cats.push_back((int64_t)(w * 32 + b)); c++; }
-                csz.push_back(c);
-            }
-        }
         if (ti) o.push_back(',');
-        o += "{\"base_weights\":"; farr(bw);
-        o += ",\"categories\":"; iarr(cats);
-        o += ",\"categories_nodes\":"; iarr(cnodes);
-        o += ",\"categories_segments\":"; iarr(cseg);
-        o += ",\"categories_sizes\":"; iarr(csz);
-        o += ",\"default_left\":"; iarr(dl);
-        o += ",\"id\":" + std::to_string(ti);
-        o += ",\"left_children\":"; iarr(lch);
-        o += ",\"loss_changes\":"; farr(lc);
-        o += ",\"parents\":"; iarr(par);
-        o += ",\"right_children\":"; iarr(rch);
-        o += ",\"split_conditions\":"; farr(sc);
-        o += ",\"split_indices\":"; iarr(si);
-        o += ",\"split_type\":"; iarr(st);
-        o += ",\"sum_hessian\":"; farr(sh);
-        o += ",\"tree_param\":{\"num_deleted\":\"0\",\"num_feature\":\"" + std::to_string(m.n_features) +
-             "\",\"num_nodes\":\"" + std::to_string(nn) + "\",\"size_leaf_vector\":\"1\"}}";
+        o += parts[ti];
     }
     std::string base = display_f32(m.base_score);
     if (!m.class_margins.empty()) {  // tree.rs:704-720: the vector form "[a,b,c]", margin space
@@ -850,23 +876,44 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     if (!(p.colsample_bytree > 0.0f && p.colsample_bytree <= 1.0f)) throw InputError("colsample_bytree must be in (0, 1]");
     if (!(p.eta >= 0.0f) || !(p.lambda >= 0.0f) || !(p.gamma >= 0.0f) || !(p.min_child_weight >= 0.0f))
         throw InputError("learning_rate, lambda, gamma and min_child_weight must be finite and non-negative");
-    for (uint64_t i = 0; i < d->n; i++)
-        if (!std::isfinite(y[i])) throw InputError("labels must all be finite");
-    if (p.objective == 1)
-        for (uint64_t i = 0; i < d->n; i++)
-            if (y[i] < 0.0f || y[i] > 1.0f) throw InputError("binary:logistic labels must be in [0, 1]");
-    if (multi)  // objective.rs:681-688
-        for (uint64_t i = 0; i < d->n; i++)
-            if (!(y[i] >= 0.0f && y[i] < (float)p.num_class && y[i] == std::trunc(y[i])))
-                throw InputError("multiclass labels must be integers in [0, num_class=" + std::to_string(p.num_class) +
-                                 ")");
+    PhaseTrace phase("booster");
+    {
+        // the label rules, checked in parallel (the first failing rule in this order is reported)
+        int bad_finite = 0, bad_range = 0, bad_class = 0;
+        const float K = (float)p.num_class;
+        const int nth = threads(p.nthread);
+#pragma omp parallel for schedule(static) reduction(| : bad_finite, bad_range, bad_class) num_threads(nth)
+        for (int64_t i = 0; i < (int64_t)d->n; i++) {
+            const float v = y[i];
+            bad_finite |= !std::isfinite(v);
+            bad_range |= v < 0.0f || v > 1.0f;
+            bad_class |= !(v >= 0.0f && v < K && v == std::trunc(v));
+        }
+        if (bad_finite) throw InputError("labels must all be finite");
+        if (p.objective == 1 && bad_range) throw InputError("binary:logistic labels must be in [0, 1]");
+        if (multi && bad_class)  // objective.rs:681-688
+            throw InputError("multiclass labels must be integers in [0, num_class=" + std::to_string(p.num_class) +
+                             ")");
+    }
+    // the default base score is a sequential f64 sum over the rows (its
+    // rounding order is the reference's): computed on a host thread while the
+    // device context is set up
+    std::future<float> base_later;
+    if (!multi && std::isnan(p.base_score))
+        base_later = std::async(std::launch::async, [=] {
+            return initial_base_score(p.objective, y, w, d->n, p.scale_pos_weight);
+        });
+    phase("label checks");
     auto b = std::make_unique<Booster>();
     b->d = d;
     b->p = p;
     b->row0 = sh.nranks > 1 ? sh.row_offset : 0;
     b->n_global = sh.nranks > 1 ? sh.n_global : d->n;
     if (p.monotone) b->mono.assign(p.monotone, p.monotone + d->F);
-    b->labels.assign(y, y + d->n);
+    b->labels.resize(d->n);
+#pragma omp parallel for schedule(static) num_threads(threads(p.nthread))
+    for (int64_t c = 0; c < (int64_t)d->n; c += (1 << 18))
+        std::memcpy(b->labels.data() + c, y + c, 4 * std::min<uint64_t>(1 << 18, d->n - (uint64_t)c));
     if (w) b->weights.assign(w, w + d->n);
     // mod.rs:5470-5495 gradient weights (sample weight x scale_pos_weight on
     // positives; objective.rs uses_scale_pos_weight: not for multiclass)
@@ -889,10 +936,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
                                                       : std::vector<float>(p.num_class, base);
         base = b->model.class_margins[0];
     }
-    if (std::isnan(base)) base = initial_base_score(p.objective, y, w, d->n, p.scale_pos_weight);
-    if (p.objective == 1 && !(base >= 0.0f && base <= 1.0f))
-        throw InputError("logistic base_score is a probability and must be in [0, 1]");
-    b->model.base_score = base;
+    phase("labels");
     b->model.objective = p.objective;
     b->model.n_features = d->F;
     b->model.scale_pos_weight = p.scale_pos_weight;
@@ -908,6 +952,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     cfg.max_leaves = p.max_leaves;
     cfg.gpu_math = p.gpu_math;
     b->ctx.reset(new fbg::TrainCtx(cfg));
+    phase("context");
     if (sh.nranks > 1) {
         if (sh.comm) {
             if (sh.comm->impl.nranks != sh.nranks || sh.comm->impl.rank != sh.rank)
@@ -930,7 +975,14 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
         else
             b->ctx->upload_block(blk.feats.data(), (uint32_t)blk.feats.size(), blk.width, blk.data.data());
     }
+    phase("features, blocks");
+    if (base_later.valid()) base = base_later.get();
+    if (p.objective == 1 && !(base >= 0.0f && base <= 1.0f))
+        throw InputError("logistic base_score is a probability and must be in [0, 1]");
+    b->model.base_score = base;
+    phase("base score");
     b->ctx->set_labels(y, b->grad_w.empty() ? nullptr : b->grad_w.data(), nullptr, base_margin(p.objective, base));
+    phase("labels upload");
     if (multi) {
         if (p.gpu_math != 1 && !b->ctx->has_exact_exp())
             throw InputError("exact multiclass training needs the verified host-expf table on the device");
@@ -1107,7 +1159,12 @@ struct fb_dataset {
 struct fb_booster {
     std::unique_ptr<fbe::Booster> b;
 };
-struct fb_model : fbe::Model {};
+struct fb_model : fbe::Model {
+    // fb_model_json's text between a size query (buf NULL) and the call that
+    // copies it out, so the usual two-call pattern formats the model once
+    mutable std::string json_pending;
+    mutable std::mutex json_mu;
+};
 
 extern "C" {
 
@@ -1413,8 +1470,14 @@ uint32_t fb_model_num_features(const fb_model* m) { return m->n_features; }
 float fb_model_base_margin(const fb_model* m) { return fbe::base_margin(m->objective, m->base_score); }
 
 int64_t fb_model_json(const fb_model* m, char* buf, int64_t cap) {
-    std::string s = fbe::model_json(*m);
-    if (buf && cap > 0) std::memcpy(buf, s.data(), (size_t)std::min<int64_t>(cap, (int64_t)s.size()));
+    std::lock_guard<std::mutex> lock(m->json_mu);
+    if (!buf || cap <= 0) {
+        m->json_pending = fbe::model_json(*m);
+        return (int64_t)m->json_pending.size();
+    }
+    std::string s = m->json_pending.empty() ? fbe::model_json(*m) : std::move(m->json_pending);
+    m->json_pending.clear();
+    std::memcpy(buf, s.data(), (size_t)std::min<int64_t>(cap, (int64_t)s.size()));
     return (int64_t)s.size();
 }
 

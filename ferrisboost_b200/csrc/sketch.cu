@@ -29,6 +29,7 @@
 // - cuts: the same binary search as the host's partition_point per target,
 //   then the order-dependent de-duplication in one thread.
 #include <algorithm>
+#include <mutex>
 #include <cfloat>
 #include <climits>
 #include <cstring>
@@ -586,13 +587,17 @@ DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cud
     const size_t bytes = (size_t)n * F * sizeof(float);
     FB_CUDA_CHECK(cudaMalloc(&x_, std::max<size_t>(bytes, 16)));
     // pageable source: pinned staging in slabs, two buffers so the host copy
-    // of one slab overlaps the transfer of the other
+    // of one slab overlaps the transfer of the other.  The two 64 MiB buffers
+    // are allocated once per process and kept (pinned allocation costs tens
+    // of milliseconds); one upload uses them at a time.
     const size_t slab = std::min<size_t>(bytes, 64ull << 20);
     if (bytes) {
-        PinnedMem stage[2];
+        static std::mutex stage_mu;
+        static PinnedMem stage[2];
+        std::lock_guard<std::mutex> stage_lock(stage_mu);
         cudaEvent_t done[2];
         for (int i = 0; i < 2; i++) {
-            stage[i].reserve(slab);
+            stage[i].reserve(64ull << 20);
             FB_CUDA_CHECK(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
         }
         const char* src = reinterpret_cast<const char*>(X_host.p);

@@ -587,6 +587,7 @@ __device__ __forceinline__ void add64_planes(uint32_t* lo, uint32_t* hi, long lo
     const uint32_t old = atomicAdd(lo, vl);
     uint32_t sum, hi_add;
     asm("add.cc.u32 %0, %2, %3;\n\taddc.u32 %1, %4, 0;" : "=r"(sum), "=r"(hi_add) : "r"(old), "r"(vl), "r"(vh));
+    (void)sum;
     atomicAdd(hi, hi_add);
 }
 
@@ -2035,6 +2036,15 @@ void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, c
                       cudaStream_t s) {
     count_launch();
     k_tree_init<<<1, 32, 0, s>>>(a, n_local, n_global, root_sum);
+}
+__global__ void k_fill(float* p, uint64_t n, float v) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        p[i] = v;
+}
+void launch_fill(float* p, uint64_t n, float v, cudaStream_t s) {
+    if (n == 0) return;
+    count_launch();
+    k_fill<<<(unsigned)std::min<uint64_t>((n + 255) / 256, 148ull * 16), 256, 0, s>>>(p, n, v);
 }
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s) {
     count_launch();

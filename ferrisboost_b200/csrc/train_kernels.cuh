@@ -216,6 +216,8 @@ void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s);
 void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
                       cudaStream_t s);
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s);
+// p[0..n) = v
+void launch_fill(float* p, uint64_t n, float v, cudaStream_t s);
 void launch_records_to_columns(int width, const uint8_t* rec, uint32_t stride, uint64_t n_rows, uint32_t n_feats,
                                uint8_t* cols, cudaStream_t s);
 void launch_transpose(int width, const uint8_t* src, uint8_t* dst, uint32_t n_rows, uint32_t n_feats,
