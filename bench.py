@@ -418,6 +418,24 @@ def treeshap_leg(dist, rank, world, device, lib, model, steps, warmup, check_ora
     return out
 
 
+def atomic_ceiling(lib, device, updates, kernel_ms):
+    """The histogram kernels' (row, feature) update rate against the rate the
+    same exact update scheme reaches alone (fbgpu_hist_atomic_ceiling: rows
+    generated in registers, shared-memory atomics only, every SM), measured
+    here on this device."""
+    import ctypes as C
+    v = C.c_double()
+    best = 0.0
+    for _ in range(3):
+        if lib.fbgpu_hist_atomic_ceiling(device, 0, 8192, C.byref(v)) == 0:
+            best = max(best, v.value)
+    rate = updates / (kernel_ms / 1000.0)
+    return {"unit": "G updates/s", "achieved": round(rate / 1e9, 1), "ceiling": round(best / 1e9, 1),
+            "frac": round(rate / best, 4) if best else None,
+            "what": "(row, feature) histogram updates per second of the histogram kernels against the same four "
+                    "32-bit shared atomics + carry per update with no memory traffic (scheme 0)"}
+
+
 def run_ours(args, rank, world):
     import torch
     import ferrisboost_b200 as fb
@@ -549,6 +567,7 @@ def run_ours(args, rank, world):
                      "per_launch_ms": round(hist_kernel_ms / hist_launches, 4),
                      "alg_bytes_per_launch": int(t["hist_bytes"] / hist_launches), "peak_source": peak_src},
         "clocks": clk.summary(),
+        **({"atomic_ceiling": atomic_ceiling(lib, device, t["hist_updates"], hist_kernel_ms)} if hist_gbs else {}),
         "breakdown": {"hist_share_of_device": round(t["hist_ms"] / t["device_ms"], 4) if t["device_ms"] else None,
                       "fast_mode_s_per_100_rounds": round(fast_ms / args.steps * 100 / 1000, 4),
                       "setup_s": {"datagen": round(gen_s, 2), "sketch_bin_upload_warmup": round(setup_s, 2)}},

@@ -598,6 +598,7 @@ class Booster:
         out = {k: float(v) for k, v in zip(keys, t)}
         # of hist_ms: the per-level histogram all-reduces of a row-sharded run
         out["comm_ms"] = float(lib().fb_booster_collective_ms(self._h))
+        out["hist_updates"] = float(lib().fb_booster_hist_updates(self._h))
         return out
 
     def margins(self) -> np.ndarray:

@@ -145,6 +145,7 @@ SIGNATURES = {
     "fb_booster_update": (C.c_int32, [P, C.c_uint32]),
     "fb_booster_timing": (None, [P, f64p]),
     "fb_booster_collective_ms": (C.c_double, [P]),
+    "fb_booster_hist_updates": (C.c_double, [P]),
     "fb_booster_set_stats": (None, [P, C.c_int32]),
     "fb_booster_model": (P, [P]),
     "fb_booster_margins": (C.c_int32, [P, f32p]),

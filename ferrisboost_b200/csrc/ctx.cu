@@ -1042,9 +1042,9 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     sync();
     FB_CUDA_CHECK(cudaEventElapsedTime(&last_tree_ms_, ev0_, ev1_));
     if (stats_) {
-        uint64_t row_bytes = 0, bins = 0;  // enabled features of this tree
+        uint64_t row_bytes = 0, bins = 0, feats = 0;  // enabled features of this tree
         for (uint32_t f = 0; f < F_; f++)
-            if (last_enabled_[f]) { row_bytes += width_[f]; bins += nbins_[f]; }
+            if (last_enabled_[f]) { row_bytes += width_[f]; bins += nbins_[f]; feats++; }
         for (uint32_t d = 0; d < std::min<uint32_t>(maxd, 15); d++) {
             float ms = 0.0f;
             FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
@@ -1058,6 +1058,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) +
                               (n_wide_ ? 1 : 0) + (n_direct_[0] ? 1 : 0) + (n_direct_[1] ? 1 : 0);
             hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
+            hist_updates_ += (double)rows * (double)feats;
         }
     }
     const uint32_t nn = hst->n_tree_nodes;

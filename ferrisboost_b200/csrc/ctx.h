@@ -151,7 +151,9 @@ class TrainCtx {
     // (enabled by set_stats): device time, launches and algorithmic bytes
     // (rows x (bin bytes + 16 B gradient + 4 B row id) + bins x 16 B flushed).
     void set_stats(bool on) { stats_ = on; }
-    void reset_stats() { hist_ms_ = 0; hist_launches_ = 0; hist_bytes_ = 0; comm_ms_ = 0; }
+    void reset_stats() { hist_ms_ = 0; hist_launches_ = 0; hist_bytes_ = 0; comm_ms_ = 0; hist_updates_ = 0; }
+    // (row, feature) histogram updates of those trees
+    double hist_updates() const { return hist_updates_; }
     double hist_ms() const { return hist_ms_; }
     // Of hist_ms: the device time of the per-level histogram all-reduces (sharded contexts).
     double comm_ms() const { return comm_ms_; }
@@ -249,7 +251,7 @@ class TrainCtx {
     cudaEvent_t hevc_[16] = {};  // per level: histogram kernels done, all-reduce starts
     DevMem level_stats_;
     DevMem fuse_;  // last-CTA counters of the fused level kernels (depthwise)
-    double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0, comm_ms_ = 0;
+    double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0, comm_ms_ = 0, hist_updates_ = 0;
 };
 
 // Root-to-leaf path form of a model's trees for the path TreeSHAP kernel

@@ -1431,6 +1431,7 @@ void fb_booster_timing(const fb_booster* h, double* out8) {
 }
 
 double fb_booster_collective_ms(const fb_booster* h) { return h->b->ctx->comm_ms(); }
+double fb_booster_hist_updates(const fb_booster* h) { return h->b->ctx->hist_updates(); }
 
 void fb_booster_set_stats(fb_booster* h, int32_t on) { h->b->ctx->set_stats(on != 0); }
 

@@ -162,6 +162,11 @@ void fb_booster_timing(const fb_booster* b, double* out8);
  * all-reduces of a row-sharded booster (0 on one GPU), while statistics are
  * on.  No counterpart in the reference (it has no multi-GPU path). */
 double fb_booster_collective_ms(const fb_booster* b);
+/* The (row, feature) updates the histogram kernels made while statistics
+ * were on: accumulated rows x enabled features, summed over the levels (no
+ * reference counterpart; the histogram's work in the unit of
+ * fbgpu_hist_atomic_ceiling). */
+double fb_booster_hist_updates(const fb_booster* b);
 void fb_booster_set_stats(fb_booster* b, int32_t on);
 fb_model* fb_booster_model(fb_booster* b);
 /* Current training margins of the booster's rows (host copy). */
