@@ -50,6 +50,10 @@ CONFIGS = [
     dict(objective="binary:logistic", max_depth=7, eta=0.2, max_bin=1024, max_leaves=40, min_child_weight=5.0,
          gamma=0.2, reg_lambda=2.0),
     dict(objective="reg:squarederror", max_depth=4, eta=0.5, max_bin=255, alpha=0.5, max_delta_step=0.3),
+    # scale_pos_weight: positives' gradients weighted, and the default base
+    # score one Newton step from margin 0 (objective.rs:403-493)
+    dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=256, scale_pos_weight=0.3),
+    dict(objective="binary:logistic", max_depth=5, eta=0.3, max_bin=128, scale_pos_weight=4.0, subsample=0.8, seed=5),
 ]
 
 
@@ -59,7 +63,7 @@ def test_synthetic_models_byte_identical(oracle, k):
     X, y = _synthetic(30000, 28, seed=k, missing=0.03 if k % 2 else 0.0)
     if p["objective"] == "reg:squarederror":
         y = (np.nan_to_num(X[:, 0]) * 2 + np.nan_to_num(X[:, 3]) ** 2).astype(np.float32)
-    w = np.random.default_rng(k).uniform(0.2, 2.0, len(y)).astype(np.float32) if k == 3 else None
+    w = np.random.default_rng(k).uniform(0.2, 2.0, len(y)).astype(np.float32) if k in (3, 6) else None
     m = fb.train(p, X, label=y, num_boost_round=12, weight=w)
     ref = oracle.train(X, y, w, n_rounds=12, **p)
     a, b = m.to_json(), ref.json()
