@@ -468,9 +468,11 @@ def run_ours(args, rank, world):
                          return_booster=booster)
 
     # untimed: the process's first CUDA work (context creation, module
-    # loading) on a few rows, so the e2e leg times the workload, not start-up
-    wn = min(n, 4096)  # every rank, on its own device: no collectives
-    fb.train(p, X[:wn], label=y[:wn], num_boost_round=2, feature_types=ft)
+    # loading) on a few rows, so the e2e leg times the workload, not start-up;
+    # when sharded also the process's first NCCL communicator (library
+    # loading and topology discovery take seconds once per process)
+    wn = min(n, 4096 * world)
+    train_public(p, 2, data=(X[:wn], y[:wn]))
 
     # e2e: 100 rounds through the public train() from host arrays (sketch,
     # binning, uploads, rounds, model JSON); wall clock, max over ranks

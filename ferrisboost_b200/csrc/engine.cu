@@ -435,7 +435,7 @@ Dataset* dataset_on_device(const fbg::HostMatrix& X, uint64_t n, uint32_t F, uin
     d->cat.assign(F, 0);
     if (categorical) for (uint32_t f = 0; f < F; f++) d->cat[f] = categorical[f] ? 1 : 0;
     PhaseTrace phase("dataset");
-    fbg::DeviceMatrix M(X, n, F, s);
+    fbg::DeviceMatrix M(X, n, F, s, fbe::threads(nthread));
     phase("rows to device");
     if (cuts) {
         check_cuts(offsets, F);
@@ -1237,10 +1237,10 @@ fb_dataset* fb_dataset_on_device_columns(const float* X, uint64_t n, uint32_t F,
 int32_t fb_dataset_device(const fb_dataset* h) { return h->d->device; }
 
 int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* w,
-                                  const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t device,
-                                  float* cuts, uint32_t* counts, uint64_t cap) {
+                                  const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
+                                  int32_t device, float* cuts, uint32_t* counts, uint64_t cap) {
     if (w || max_bin * 16ull > fbg::kSketchMaxLimit)
-        return fb_sketch_features(X, n, F, max_bin, w, categorical, feats, n_feats, 0, cuts, counts, cap);
+        return fb_sketch_features(X, n, F, max_bin, w, categorical, feats, n_feats, nthread, cuts, counts, cap);
     return fbe::guarded([&]() -> int64_t {
         if (n == 0 || F == 0) throw fbe::InputError("training data must have at least one row and one feature");
         if (max_bin == 0) throw fbe::InputError("max_bin must be in 1..=65535");
@@ -1250,7 +1250,7 @@ int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32
         std::vector<std::vector<float>> per;
         {
             fbe::PrepStream ps(device);
-            fbg::DeviceMatrix M(fbg::HostMatrix{X, F, 1}, n, F, ps.s);
+            fbg::DeviceMatrix M(fbg::HostMatrix{X, F, 1}, n, F, ps.s, fbe::threads(nthread));
             per = fbe::device_sketch(M, max_bin, categorical, fs);
         }
         uint64_t total = 0;

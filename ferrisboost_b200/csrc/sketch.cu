@@ -28,6 +28,8 @@
 //   if it does not hold, one thread runs the sequential loop instead.
 // - cuts: the same binary search as the host's partition_point per target,
 //   then the order-dependent de-duplication in one thread.
+#include <omp.h>
+
 #include <algorithm>
 #include <mutex>
 #include <cfloat>
@@ -580,8 +582,9 @@ template <class T> void upload(DevMem& d, const std::vector<T>& h, cudaStream_t 
 
 }  // namespace
 
-DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cudaStream_t stream)
+DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cudaStream_t stream, int threads)
     : n_(n), F_(F), rs_(X_host.rs), cs_(X_host.cs), s_(stream) {
+    const int nth = threads > 0 ? threads : omp_get_max_threads();
     if (!((rs_ == F && cs_ == 1) || (rs_ == 1 && cs_ == n)))
         throw std::invalid_argument("DeviceMatrix: the host matrix must be contiguous row-major or column-major");
     const size_t bytes = (size_t)n * F * sizeof(float);
@@ -608,7 +611,7 @@ DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cud
                 const size_t len = std::min(slab, bytes - off);
                 if (used[k]) FB_CUDA_CHECK(cudaEventSynchronize(done[k]));
                 char* dst = stage[k].as<char>();
-#pragma omp parallel for schedule(static)
+#pragma omp parallel for schedule(static) num_threads(nth)
                 for (int64_t p = 0; p < (int64_t)len; p += (1 << 20))
                     std::memcpy(dst + p, src + off + p, std::min<size_t>(1 << 20, len - (size_t)p));
                 FB_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<char*>(x_) + off, dst, len, cudaMemcpyHostToDevice, s_));

@@ -33,7 +33,8 @@ struct HostMatrix {
 // `stream` of the current device.
 class DeviceMatrix {
    public:
-    DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cudaStream_t stream);
+    // threads: host threads copying into the pinned staging (0: the OpenMP default)
+    DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cudaStream_t stream, int threads = 0);
     ~DeviceMatrix();
     DeviceMatrix(const DeviceMatrix&) = delete;
     DeviceMatrix& operator=(const DeviceMatrix&) = delete;

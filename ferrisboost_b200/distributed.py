@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import sys
 from typing import Any, Mapping, Sequence
 
 import numpy as np
@@ -145,7 +146,7 @@ def sketch_features(X: np.ndarray, feats: Sequence[int], max_bin: int, weight=No
     else:
         n = lib().fb_sketch_features_device(_lib.ptr(X, C.c_float), X.shape[0], X.shape[1], max_bin,
                                             _lib.ptr(w, C.c_float), _lib.ptr(cat, C.c_uint8), _lib.ptr(fs, C.c_uint32),
-                                            len(fs), int(device), _lib.ptr(cuts, C.c_float),
+                                            len(fs), nthread, int(device), _lib.ptr(cuts, C.c_float),
                                             _lib.ptr(counts, C.c_uint32), cap)
     if n < 0:
         raise ValueError(_err())
@@ -196,6 +197,22 @@ def _broadcast(obj, group=None):
     return box[0]
 
 
+class _PhaseTrace:
+    """FBGPU_TRACE=1: wall time of each phase of a sharded train() on stderr."""
+
+    def __init__(self, what: str):
+        import time
+        self.what, self.on, self.clock = what, bool(os.environ.get("FBGPU_TRACE")), time.perf_counter
+        self.t = self.clock()
+
+    def __call__(self, name: str) -> None:
+        if not self.on:
+            return
+        now = self.clock()
+        sys.stderr.write(f"[fbgpu] {self.what} {name:<30} {1000 * (now - self.t):9.3f} ms\n")
+        self.t = now
+
+
 def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
           feature_types: Sequence[str] | None = None, group=None, timeout_s: float = 120.0,
           return_booster: bool = False, liveness: Liveness | None = None):
@@ -232,6 +249,7 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     if n < world:  # the same on every rank: all raise before any collective
         raise ValueError(f"{n} rows cannot be sharded over {world} ranks")
     cat = _feature_flags(feature_types, F)
+    trace = _PhaseTrace(f"rank {rank}")
     nid = None
     if rank == 0:  # a failure on rank 0 is sent to every rank, which all raise
         try:
@@ -244,7 +262,9 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     timeout_ms = int(max(1.0, timeout_s) * 1000)
     # the communicator initializes while the cuts are sketched and the rows binned
     comm = Communicator(nid, world, rank, p["device_index"], timeout_ms)
+    trace("id, communicator start")
     cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group, device=p["device_index"])
+    trace("sketch + all-gather of cuts")
     lo, hi = shard_range(n, world, rank)
     base = p["base_score"]
     class_margins = None
@@ -259,13 +279,17 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     elif base is None:  # over all rows, as a single process would (objective.rs:403-493)
         base = float(lib().fb_initial_base_score(_OBJECTIVES[p["objective"]], _lib.ptr(y, C.c_float),
                                                  _lib.ptr(w, C.c_float), n, p["scale_pos_weight"]))
+    trace("base score")
     ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts,
                  device=p["device_index"])
+    trace("shard binning")
     shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
                   timeout_ms=timeout_ms, comm=comm, class_margins=class_margins)
     b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)
+    trace("booster (communicator ready)")
     if liveness is None:
         b.update(num_boost_round)
+        trace("rounds")
     else:
         for _ in range(num_boost_round):
             liveness.beat()

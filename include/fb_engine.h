@@ -99,11 +99,12 @@ int64_t fb_sketch_features(const float* X, uint64_t n, uint32_t F, uint32_t max_
                            const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
                            float* cuts, uint32_t* counts, uint64_t cap);
 /* fb_sketch_features computed on CUDA device `device` (the rows are copied
- * there once); the same cuts, bit for bit.  With weights, or max_bin > 1024,
- * the host sketch runs instead. */
+ * there once, copied by nthread host threads, 0 = the OpenMP default); the
+ * same cuts, bit for bit.  With weights, or max_bin > 1024, the host sketch
+ * runs instead. */
 int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32_t max_bin, const float* weights,
-                                  const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t device,
-                                  float* cuts, uint32_t* counts, uint64_t cap);
+                                  const uint8_t* categorical, const uint32_t* feats, uint32_t n_feats, int32_t nthread,
+                                  int32_t device, float* cuts, uint32_t* counts, uint64_t cap);
 /* The base_score estimated from the labels when none is given: the label mean
  * (weighted when weights != NULL), summed in f64 in row order
  * (src/objective.rs:41-61). */
