@@ -78,7 +78,11 @@ struct TreeState {
     uint32_t chunk_count;  // row chunks over the current level's nodes
     uint32_t kept;         // nodes split in the current level
     uint32_t error;        // nonzero: a kernel detected an inconsistency
-    uint32_t pad[7];
+    uint32_t pad0;
+    // feature-sharded split search: pairs between two ranks' blocks of the
+    // level's accumulate histograms (0 otherwise; see acc_bin)
+    unsigned long long rank_stride;
+    uint32_t pad[4];
 };
 
 __device__ __forceinline__ double to_f64(long long x, double inv) { return __dmul_rn(__ll2double_rn(x), inv); }

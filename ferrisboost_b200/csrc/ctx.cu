@@ -637,10 +637,17 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
 // 8 two-byte features of at most kWideMaxBins bins whose bins lie within 4
 // record chunks (the staged kernel with 8 lanes per row); the remaining
 // features go to row-per-thread tiles sized by the shared-memory budget.
-void TrainCtx::plan_tiles(const uint8_t* enabled) {
+void TrainCtx::plan_tiles(const uint8_t* enabled, bool rank_major) {
     std::vector<uint8_t> en(F_, 1);
     if (enabled) for (uint32_t f = 0; f < F_; f++) en[f] = enabled[f] ? 1 : 0;
-    if (tiles_valid_ && en == last_enabled_) return;
+    if (tiles_valid_ && en == last_enabled_ && rank_major == tiles_rank_major_) return;
+    // a feature's bin index in the accumulate histograms: its offset, or for
+    // the rank-major layout its rank (top 8 bits) and offset in the rank's block
+    auto gbin = [&](uint32_t f) -> uint32_t {
+        if (!rank_major) return hoff_[f];
+        const uint32_t r = feat_rank_[f];
+        return (r << 24) | (hoff_[f] - rank_bin_lo_[r]);
+    };
     const uint32_t kLpfMaxBins = 440;    // 440 x 32 lanes x 16 B = 220 KiB
     const uint32_t kWideMaxBins = 1024;  // 1028 x 8 lanes x 16 B = 128.5 KiB
     const uint32_t kWideMaxChunks = 4;
@@ -680,7 +687,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
         for (uint32_t f : b.feats) {
             if (!en[f] || nbins_[f] > kLpfMaxBins) continue;
             if (cur.n_feat == 32) flush_lpf();
-            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
+            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], gbin(f)});
             maxb = std::max(maxb, nbins_[f]);
             cur.n_feat++;
         }
@@ -709,7 +716,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
             if (wd.n_feat == kWideLanes || (hi + 15) / 16 - lo / 16 > kWideMaxChunks) flush_wide();
             wlo = std::min(wlo, feat_byte_[f]);
             whi = std::max(whi, feat_byte_[f] + 2);
-            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
+            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], gbin(f)});
             maxb = std::max(maxb, nbins_[f]);
             wd.n_feat++;
         }
@@ -727,7 +734,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
         for (uint32_t f : b.feats) {
             if (!en[f] || nbins_[f] <= kLpfMaxBins || nbins_[f] > max_local || is_wide(f, b.width)) continue;
             if (g.n_feat == 64 || g.local_bins + nbins_[f] > max_local) flush_gen();
-            tf.push_back(TileFeat{feat_byte_[f], g.local_bins, nbins_[f], hoff_[f]});
+            tf.push_back(TileFeat{feat_byte_[f], g.local_bins, nbins_[f], gbin(f)});
             g.local_bins += nbins_[f];
             g.n_feat++;
         }
@@ -743,7 +750,7 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
                 dt.feat_begin = (uint32_t)tf.size();
                 dt.n_feat = 0;
             }
-            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], hoff_[f]});
+            tf.push_back(TileFeat{feat_byte_[f], 0, nbins_[f], gbin(f)});
             dt.n_feat++;
         }
         if (dt.n_feat) direct[wi].push_back(dt);
@@ -792,15 +799,18 @@ void TrainCtx::plan_tiles(const uint8_t* enabled) {
     if (n_wide_) set_hist_wide_smem_limit((int)tile_smem_wide_);
     sync();
     last_enabled_ = en;
+    tiles_rank_major_ = rank_major;
     tiles_valid_ = true;
 }
 
 // One histogram pass over the accumulate rows of the current level (all tiles).
 void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, const uint32_t* acc_list,
-                                 const unsigned long long* acc_prefix, uint64_t rows_upper) {
+                                 const unsigned long long* acc_prefix, uint64_t rows_upper, Pair* out,
+                                 unsigned long long slot) {
     const TileDesc* T = d_tiles_.as<TileDesc>();
     const TileFeat* TF = d_tfeat_.as<TileFeat>();
-    const unsigned long long slot = std::max<uint64_t>(total_bins_, 1);
+    if (!out) out = hist_acc_.as<Pair>();
+    if (!slot) slot = std::max<uint64_t>(total_bins_, 1);
     const uint32_t grid_gen = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 1024), 148 * 2));
     const size_t lpf_smem = hist_stages_ ? tile_smem_stage_ : tile_smem_lpf_;
     const int per_sm = lpf_smem + 1024 <= 113 * 1024 ? 2 : 1;
@@ -809,24 +819,24 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
     const uint32_t grid_lpf = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u * per_sm));
     for (int w = 0; w < 2; w++) {
         launch_hist(w + 1, T + tile_off_gen_[w], n_gen_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list, acc_prefix,
-                    state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_gen, tile_smem_, s_);
+                    state_.as<TreeState>(), out, slot, grid_gen, tile_smem_, s_);
         if (hist_stages_)
             launch_hist_stage(w + 1, hist_stages_, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes,
-                              acc_list, acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf,
+                              acc_list, acc_prefix, state_.as<TreeState>(), out, slot, grid_lpf,
                               lpf_smem, s_);
         else
             launch_hist_lpf(w + 1, T + tile_off_lpf_[w], n_lpf_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
-                            acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_lpf, tile_smem_lpf_,
+                            acc_prefix, state_.as<TreeState>(), out, slot, grid_lpf, tile_smem_lpf_,
                             s_);
     }
     for (int w = 0; w < 2; w++)
         if (n_direct_[w])
             launch_hist(w + 1, T + tile_off_direct_[w], n_direct_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
-                        acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_gen, tile_smem_, s_);
+                        acc_prefix, state_.as<TreeState>(), out, slot, grid_gen, tile_smem_, s_);
     if (n_wide_) {
         const uint32_t grid_wide = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u));
         launch_hist_wide(wide_stages_, T + tile_off_wide_, n_wide_, TF, rows, fixed_.as<Pair>(), nodes, acc_list,
-                         acc_prefix, state_.as<TreeState>(), hist_acc_.as<Pair>(), slot, grid_wide, tile_smem_wide_,
+                         acc_prefix, state_.as<TreeState>(), out, slot, grid_wide, tile_smem_wide_,
                          s_);
     }
 }
@@ -848,6 +858,9 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.st = state_.as<TreeState>();
     a.hist_acc = hist_acc_.as<Pair>();
     a.slot_pairs = std::max<uint64_t>(total_bins_, 1);
+    a.feat_lo = 0;
+    a.feat_hi = F_;
+    a.bin_lo = 0;
     a.feat_best = feat_best_.as<SplitRec>();
     a.cat_words = cat_words_;
     a.cat_slot = d_cat_slot_.as<uint32_t>();
@@ -867,6 +880,30 @@ LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     a.trec = trec_.as<TreeRec>();
     a.tcats = tcats_.as<uint32_t>();
     return a;
+}
+
+// Contiguous feature ranges, one per rank, with about total_bins / N bins
+// each: rank r scores the features from the first one whose bins start at or
+// after r / N of all bins.  chunk_pairs_ is the largest range's bin count.
+void TrainCtx::setup_split_shards() {
+    const uint32_t N = (uint32_t)nranks_;
+    if (total_bins_ >= (1u << 24)) throw InputError("the feature-sharded split search packs bin offsets in 24 bits");
+    rank_feat_lo_.assign(N + 1, F_);
+    rank_bin_lo_.assign(N + 1, (uint32_t)total_bins_);
+    uint32_t f = 0;
+    for (uint32_t r = 0; r < N; r++) {
+        const uint64_t target = total_bins_ * r / N;
+        while (f < F_ && hoff_[f] < target) f++;
+        rank_feat_lo_[r] = f;
+        rank_bin_lo_[r] = hoff_[f];
+    }
+    feat_rank_.assign(F_, 0);
+    chunk_pairs_ = 1;
+    for (uint32_t r = 0; r < N; r++) {
+        for (uint32_t g = rank_feat_lo_[r]; g < rank_feat_lo_[r + 1]; g++) feat_rank_[g] = r;
+        chunk_pairs_ = std::max<uint64_t>(chunk_pairs_, rank_bin_lo_[r + 1] - rank_bin_lo_[r]);
+    }
+    split_shard_ = true;
 }
 
 // Lossguide grows the same tree as depthwise growth when max_leaves cannot
@@ -924,7 +961,29 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     if (n_ == 0) throw InputError("training data must have at least one row");
     const bool best_first = lossguide && !lossguide_is_levelwise(tp);
     ensure_tree_buffers(tp.max_depth, tp.max_leaves, best_first);
-    plan_tiles(enabled);
+    // Row-sharded depthwise trees with large level histograms score splits
+    // per rank on its own features: a reduce-scatter of the level's
+    // histograms (half the bytes of an all-reduce) and a gather of the
+    // per-node winners (one more collective and a merge kernel per level).
+    // FBGPU_SPLIT_SHARD=1 / 0 forces either form.
+    static const int split_shard_env = [] {
+        const char* e = std::getenv("FBGPU_SPLIT_SHARD");
+        return e ? (std::string(e) == "0" ? 0 : 1) : -1;
+    }();
+    const bool wide_levels = 16ull * max_acc_ * total_bins_ >= (32ull << 20);
+    const bool rs_mode = comm_ && nranks_ > 1 && !best_first &&
+                         (split_shard_env >= 0 ? split_shard_env == 1 : wide_levels);
+    if (rs_mode) {
+        if (!split_shard_) setup_split_shards();
+        const uint64_t lvl = max_level_nodes_;
+        const uint64_t block = (uint64_t)max_acc_ * chunk_pairs_;
+        if (hist_acc_.bytes < 16ull * nranks_ * block + 16) hist_acc_.alloc(16ull * nranks_ * block + 16);
+        if (hist_rs_.bytes < 16ull * block) hist_rs_.alloc(16ull * block);
+        if (best_all_.bytes < sizeof(SplitRec) * nranks_ * lvl) best_all_.alloc(sizeof(SplitRec) * nranks_ * lvl);
+        if (cats_all_.bytes < 4ull * cat_words_ * nranks_ * lvl) cats_all_.alloc(4ull * cat_words_ * nranks_ * lvl);
+        h_stride_.reserve(8 * 16);
+    }
+    plan_tiles(enabled, rs_mode);
     if (tp.monotone) {
         std::vector<int8_t> m(tp.monotone, tp.monotone + F_);
         if (m != last_mono_) {
@@ -967,7 +1026,16 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     a.acc_prefix = acc_prefix_[0].as<unsigned long long>();
     a.chunk_prefix = chunk_prefix_[0].as<uint32_t>();
     a.rows_cur = rows_[0].as<uint32_t>();
-    if (root_pending_ && maxd == 0) reduce_root_sum(true);
+    if (rs_mode) {
+        // the split reads this rank's block of the reduce-scattered histograms,
+        // its node slots hold this rank's bins only
+        a.hist_acc = hist_rs_.as<Pair>();
+        a.slot_pairs = chunk_pairs_;
+        a.feat_lo = rank_feat_lo_[rank_];
+        a.feat_hi = rank_feat_lo_[rank_ + 1];
+        a.bin_lo = rank_bin_lo_[rank_];
+    }
+    if (root_pending_ && (maxd == 0 || rs_mode)) reduce_root_sum(true);
     launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
     for (uint32_t d = 0; d < maxd; d++) {
         const uint32_t max_m = (uint32_t)std::min<uint64_t>(1ull << d, max_level_nodes_);
@@ -986,7 +1054,9 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         a.hist_prev = hist_[(d + 1) & 1].as<Pair>();
         a.rows_cur = rows_[cur].as<uint32_t>();
         a.rows_next = rows_[1 - cur].as<uint32_t>();
-        FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, 16ull * a.slot_pairs * max_acc, s_));
+        const uint64_t block = (uint64_t)max_acc * chunk_pairs_;  // rs_mode: pairs of one rank's block
+        FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, rs_mode ? 16ull * nranks_ * block : 16ull * a.slot_pairs * max_acc,
+                                      s_));
         if (stats_ && d < 15) {
             // this level's accumulate nodes and rows: TreeState bytes [8, 24) hold
             // leaf_count, acc_count (u32 each) and acc_total (u64)
@@ -1000,9 +1070,21 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         if (root_rides)
             FB_CUDA_CHECK(cudaMemcpyAsync(hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, sums_.p, 16,
                                           cudaMemcpyDeviceToDevice, s_));
-        launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
-        if (stats_ && comm_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hevc_[d], s_));
-        allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc + (root_rides ? 2 : 0), false);
+        if (rs_mode) {
+            // rank-major accumulate histograms ([rank][slot][rank's bins]); each
+            // rank receives the sums of its own block
+            uint64_t* hs = h_stride_.as<uint64_t>() + (d & 15);
+            *hs = block;
+            FB_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(state_.p) + offsetof(TreeState, rank_stride), hs,
+                                          8, cudaMemcpyHostToDevice, s_));
+            launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_, hist_acc_.as<Pair>(), chunk_pairs_);
+            if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hevc_[d], s_));
+            comm_->reduce_scatter_u64(hist_acc_.p, hist_rs_.p, 2 * block, s_);
+        } else {
+            launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
+            if (stats_ && comm_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hevc_[d], s_));
+            allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc + (root_rides ? 2 : 0), false);
+        }
         if (root_rides) {
             FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, 16,
                                           cudaMemcpyDeviceToDevice, s_));
@@ -1012,7 +1094,16 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         }
         if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
-        launch_split_decide(a, max_m, s_);
+        if (rs_mode) {
+            // this rank's best split per node over its features, every rank's
+            // winners gathered, merged and decided
+            launch_split(a, max_m, s_);
+            comm_->all_gather_bytes(node_best_.p, best_all_.p, sizeof(SplitRec) * max_m, s_);
+            if (has_cat_) comm_->all_gather_bytes(node_cats_.p, cats_all_.p, 4ull * cat_words_ * max_m, s_);
+            launch_merge_decide(a, best_all_.as<SplitRec>(), cats_all_.as<uint32_t>(), (uint32_t)nranks_, max_m, s_);
+        } else {
+            launch_split_decide(a, max_m, s_);
+        }
         if (!(a.walk && a.last_level)) {  // with the walk, the last level's children need no partition
             launch_part_count(a, max_chunks, s_);
             launch_part_scatter(a, max_chunks, s_);

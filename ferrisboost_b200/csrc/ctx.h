@@ -174,9 +174,13 @@ class TrainCtx {
     std::unique_ptr<Block> new_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t width);
     void register_block(std::unique_ptr<Block> b);
     void ensure_features() const;
-    void plan_tiles(const uint8_t* enabled);
+    void plan_tiles(const uint8_t* enabled, bool rank_major = false);
     void launch_histograms(const uint32_t* rows, const NodeInfo* nodes, const uint32_t* acc_list,
-                           const unsigned long long* acc_prefix, uint64_t rows_upper);
+                           const unsigned long long* acc_prefix, uint64_t rows_upper, Pair* out = nullptr,
+                           unsigned long long slot = 0);
+    // Feature-sharded split search of a row-sharded depthwise tree: feature
+    // ranges per rank (balanced by bins), this rank's range and block size.
+    void setup_split_shards();
     void ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide = false);
     void ensure_lossguide_buffers(uint32_t max_leaves);
     void build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
@@ -204,6 +208,7 @@ class TrainCtx {
     std::vector<uint8_t> last_enabled_;
     std::vector<int8_t> last_mono_;
     bool tiles_valid_ = false;
+    bool tiles_rank_major_ = false;  // the plan's packed bin indices carry ranks (feature-sharded split search)
     DevMem d_tiles_, d_tfeat_;
     uint32_t tile_off_gen_[2] = {0, 0}, n_gen_[2] = {0, 0}, tile_off_lpf_[2] = {0, 0}, n_lpf_[2] = {0, 0};
     size_t tile_smem_ = 0, tile_smem_lpf_ = 0, tile_smem_stage_ = 0;
@@ -223,6 +228,15 @@ class TrainCtx {
     std::unique_ptr<NcclComm> comm_;
     int nranks_ = 1, rank_ = 0;
     DevMem node_left_global_, comm_scratch_;
+    // feature-sharded split search (row-sharded depthwise trees): rank r
+    // scores features [rank_feat_lo_[r], rank_feat_lo_[r + 1]) whose bins are
+    // [rank_bin_lo_[r], rank_bin_lo_[r + 1]); a rank's block holds chunk_pairs_
+    // pairs per accumulate slot
+    bool split_shard_ = false;
+    std::vector<uint32_t> rank_feat_lo_, rank_bin_lo_, feat_rank_;
+    uint64_t chunk_pairs_ = 0;
+    DevMem hist_rs_, best_all_, cats_all_;
+    PinnedMem h_stride_;
     void allreduce_u64(void* buf, size_t count, bool max_op);
     void allreduce_u32(const void* src, void* dst, size_t count);
     void reduce_root_sum(bool now);

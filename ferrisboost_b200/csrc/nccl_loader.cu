@@ -22,6 +22,8 @@ struct Api {
     decltype(&ncclCommDestroy) destroy = nullptr;
     decltype(&ncclCommAbort) abort = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclReduceScatter) reduce_scatter = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
     std::string why;
 };
@@ -51,6 +53,8 @@ const Api& api() {
         bind(r.handle, r.destroy, "ncclCommDestroy", r.why);
         bind(r.handle, r.abort, "ncclCommAbort", r.why);
         bind(r.handle, r.all_reduce, "ncclAllReduce", r.why);
+        bind(r.handle, r.reduce_scatter, "ncclReduceScatter", r.why);
+        bind(r.handle, r.all_gather, "ncclAllGather", r.why);
         bind(r.handle, r.error_string, "ncclGetErrorString", r.why);
         return r;
     }();
@@ -148,6 +152,22 @@ void NcclComm::allreduce(const void* src, void* dst, size_t count, bool u64, boo
                                              static_cast<ncclComm_t>(comm_), s);
     if (rc != ncclSuccess && rc != ncclInProgress) fail(nccl_msg("ncclAllReduce", rc), false);
     wait_ready("ncclAllReduce");
+}
+
+void NcclComm::reduce_scatter_u64(const void* src, void* dst, size_t recv_count, cudaStream_t s) {
+    if (failed_) throw NcclError("the NCCL communicator was aborted by an earlier error");
+    const ncclResult_t rc =
+        api().reduce_scatter(src, dst, recv_count, ncclUint64, ncclSum, static_cast<ncclComm_t>(comm_), s);
+    if (rc != ncclSuccess && rc != ncclInProgress) fail(nccl_msg("ncclReduceScatter", rc), false);
+    wait_ready("ncclReduceScatter");
+}
+
+void NcclComm::all_gather_bytes(const void* src, void* dst, size_t send_bytes, cudaStream_t s) {
+    if (failed_) throw NcclError("the NCCL communicator was aborted by an earlier error");
+    const ncclResult_t rc =
+        api().all_gather(src, dst, send_bytes, ncclUint8, static_cast<ncclComm_t>(comm_), s);
+    if (rc != ncclSuccess && rc != ncclInProgress) fail(nccl_msg("ncclAllGather", rc), false);
+    wait_ready("ncclAllGather");
 }
 
 void NcclComm::sync(cudaStream_t s) {

@@ -37,6 +37,10 @@ public:
 
     // In place when src == dst.  u64: ncclUint64 with sum or max; otherwise ncclUint32 sum.
     void allreduce(const void* src, void* dst, size_t count, bool u64, bool max_op, cudaStream_t s);
+    // ncclReduceScatter (u64 sum): rank r receives the sum of block r (recv_count words) of every rank's src.
+    void reduce_scatter_u64(const void* src, void* dst, size_t recv_count, cudaStream_t s);
+    // ncclAllGather: dst holds every rank's send_bytes, in rank order.
+    void all_gather_bytes(const void* src, void* dst, size_t send_bytes, cudaStream_t s);
     // Waits for the stream, polling the communicator; aborts it after the time limit.
     void sync(cudaStream_t s);
     bool failed() const { return failed_; }

@@ -5,6 +5,19 @@
 
 namespace fbg {
 
+// The pair of (accumulate slot, packed bin index) in a level's accumulate
+// histograms.  Unsharded, slot * slot_pairs + bin.  For the feature-sharded
+// split search of a row-sharded run the histograms are laid out rank-major,
+// [rank][accumulate slot][that rank's features' bins], so one reduce-scatter
+// hands each rank the sums of its own features; a feature's packed index
+// carries its rank in the top 8 bits and rank_stride (TreeState) is the size
+// of a rank's block.
+__device__ __forceinline__ Pair* acc_bin(Pair* hist_acc, uint32_t acc_slot, unsigned long long slot_pairs,
+                                         unsigned long long rank_stride, uint32_t packed) {
+    return hist_acc + (unsigned long long)(packed >> 24) * rank_stride + (unsigned long long)acc_slot * slot_pairs +
+           (packed & 0xffffffu);
+}
+
 // ------------------------------------------------------------------ scans
 template <int NT>
 __device__ __forceinline__ Pair block_excl_scan_pair(Pair v, Pair* warp_tot, Pair& total) {
@@ -420,7 +433,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
         const unsigned long long seg_end = min(b, acc_prefix[k + 1]);
         const uint32_t base = ni.start + (uint32_t)(a - acc_prefix[k]);
         const uint32_t cnt = (uint32_t)(seg_end - a);
-        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
+        const unsigned long long rs = st->rank_stride;
         for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
             const uint32_t r = rows[base + i];
             const Pair gp = gpair[r];
@@ -431,7 +444,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
                                       : (uint32_t)rec[f.byte_off];
                 if (bin >= f.nbins) continue;  // missing sentinels lie at or above every feature's bin count
                 if (direct) {
-                    Pair* o = out + f.global_off + bin;
+                    Pair* o = acc_bin(hist_acc, ni.acc_slot, slot_pairs, rs, f.global_off + bin);
                     atomicAdd(reinterpret_cast<unsigned long long*>(&o->g), (unsigned long long)gp.g);
                     atomicAdd(reinterpret_cast<unsigned long long*>(&o->h), (unsigned long long)gp.h);
                     continue;
@@ -457,9 +470,9 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const TileDesc* __restric
                     uint32_t mid = (lo + hi) >> 1;
                     if (tf[mid].local_off <= j) lo = mid; else hi = mid;
                 }
-                const uint32_t gidx = tf[lo].global_off + (j - tf[lo].local_off);
-                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
-                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
+                Pair* o = acc_bin(hist_acc, ni.acc_slot, slot_pairs, rs, tf[lo].global_off + (j - tf[lo].local_off));
+                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&o->g), g);
+                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&o->h), h);
                 glo[j] = 0u; ghi[j] = 0u; hlo[j] = 0u; hhi[j] = 0u;
             }
         }
@@ -542,16 +555,16 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_lpf(const TileDesc* __
             }
         }
         __syncthreads();
-        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
+        const unsigned long long rs = st->rank_stride;
         for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
             const unsigned long long g = ((unsigned long long)ghi[j] << 32) | glo[j];
             const unsigned long long h = ((unsigned long long)hhi[j] << 32) | hlo[j];
             if (g | h) {
                 const uint32_t t = j & 31u, bb = j >> 5;
                 const TileFeat ft = tfeat[td.feat_begin + t];
-                const uint32_t gidx = ft.global_off + bb;
-                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
-                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
+                Pair* o = acc_bin(hist_acc, ni.acc_slot, slot_pairs, rs, ft.global_off + bb);
+                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&o->g), g);
+                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&o->h), h);
                 glo[j] = 0u; ghi[j] = 0u; hlo[j] = 0u; hhi[j] = 0u;
             }
         }
@@ -767,7 +780,7 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
         }
         cp_async_wait<0>();
         __syncthreads();
-        Pair* out = hist_acc + (unsigned long long)ni.acc_slot * slot_pairs;
+        const unsigned long long rs = st->rank_stride;
         for (uint32_t j = threadIdx.x; j < LB; j += blockDim.x) {
             const uint32_t t = j % LPR, bb = j / LPR;
             uint32_t* w = LPR == 32 ? sm + bb * 128u + t : sm + bb * LPR + t;
@@ -776,9 +789,9 @@ __global__ void __launch_bounds__(kHistLpfThreads) k_hist_stage(const TileDesc* 
             const unsigned long long h = ((unsigned long long)w[o3] << 32) | w[o2];
             if (g | h) {
                 const TileFeat ft = tfeat[td.feat_begin + t];
-                const uint32_t gidx = ft.global_off + bb;
-                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].g), g);
-                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&out[gidx].h), h);
+                Pair* o = acc_bin(hist_acc, ni.acc_slot, slot_pairs, rs, ft.global_off + bb);
+                if (g) atomicAdd(reinterpret_cast<unsigned long long*>(&o->g), g);
+                if (h) atomicAdd(reinterpret_cast<unsigned long long*>(&o->h), h);
                 w[0] = 0u; w[o1] = 0u; w[o2] = 0u; w[o3] = 0u;
             }
         }
@@ -1038,16 +1051,17 @@ __device__ void split_cat_wide(const LevelArgs& a, SplitSmem& s, const Pair* hx,
 // sibling), scan it, score every candidate and keep the first maximum in the
 // reference's enumeration order (split.rs:331-461; categorical :484-617).
 __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
-    const uint32_t node = blockIdx.x, f = blockIdx.y, F = a.n_features;
+    // features feat_lo.. (all features, unless the split search is feature-sharded)
+    const uint32_t node = blockIdx.x, f = a.feat_lo + blockIdx.y, F = a.n_features;
     if (node >= a.st->m) return;
     SplitRec* out = a.feat_best + (size_t)node * F + f;
-    if (!a.enabled[f]) {
+    if (!a.enabled[f] || f >= a.feat_hi) {
         if (threadIdx.x == 0) out->flags = 0;
         return;
     }
     __shared__ SplitSmem s;
     const NodeInfo ni = a.nodes[node];
-    const uint32_t off = a.hoff[f], nb = a.hoff[f + 1] - off;
+    const uint32_t off = a.hoff[f] - a.bin_lo, nb = a.hoff[f + 1] - a.hoff[f];
     const Pair* acc = a.hist_acc + (unsigned long long)ni.acc_slot * a.slot_pairs + off;
     const Pair* par = ni.parent_slot >= 0 ? a.hist_prev + (unsigned long long)ni.parent_slot * a.slot_pairs + off
                                           : nullptr;
@@ -1240,7 +1254,7 @@ __global__ void k_split_node(LevelArgs a) {
     float bg = 0.0f;
     uint32_t bf = 0xffffffffu;
     bool have = false;
-    for (uint32_t f = lane; f < F; f += 32) {
+    for (uint32_t f = a.feat_lo + lane; f < a.feat_hi; f += 32) {
         const SplitRec& r = a.feat_best[(size_t)node * F + f];
         if (!(r.flags & 1u)) continue;
         if (!have || r.gain > bg) { bg = r.gain; bf = f; have = true; }
@@ -1356,7 +1370,7 @@ __global__ void __launch_bounds__(256) k_split_node_decide(LevelArgs a) {
         float bg = 0.0f;
         uint32_t bf = 0xffffffffu;
         bool have = false;
-        for (uint32_t f = lane; f < F; f += 32) {
+        for (uint32_t f = a.feat_lo + lane; f < a.feat_hi; f += 32) {
             const SplitRec& r = a.feat_best[(size_t)node * F + f];
             if (!(r.flags & 1u)) continue;
             if (!have || r.gain > bg) { bg = r.gain; bf = f; have = true; }
@@ -1389,6 +1403,46 @@ __global__ void __launch_bounds__(256) k_split_node_decide(LevelArgs a) {
                 const uint32_t v = src[w];
                 a.node_cats[(size_t)node * W + w] = v;
                 a.tcats[tid * W + w] = v;
+            }
+        }
+    }
+    if (last_block_done(a.fuse + 0)) decide_body<256>(a, wt);
+}
+
+// Feature-sharded split search of a row-sharded run: each rank's per-node
+// winner over its own features (k_split_node), gathered in rank order, is
+// merged into the node's best split.  A strictly greater gain replaces the
+// current winner, so equal gains keep the lower rank's, which is the lower
+// feature (ranks own ascending feature ranges; split.rs:631-642).  The
+// winner's category set goes to the node and its tree record, then the last
+// CTA runs the level's decisions.
+__global__ void __launch_bounds__(256) k_merge_decide(LevelArgs a, const SplitRec* __restrict__ all_best,
+                                                      const uint32_t* __restrict__ all_cats, uint32_t n_ranks,
+                                                      uint32_t stride) {
+    __shared__ uint32_t wt[32];
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < a.st->m) {
+        int best = -1;
+        float bg = 0.0f;
+        for (uint32_t r = 0; r < n_ranks; r++) {
+            const SplitRec& rec = all_best[(size_t)r * stride + i];
+            if (!(rec.flags & 1u)) continue;
+            if (best < 0 || rec.gain > bg) { best = (int)r; bg = rec.gain; }
+        }
+        SplitRec out;
+        if (best >= 0) {
+            out = all_best[(size_t)best * stride + i];
+        } else {
+            out.flags = 0;
+        }
+        a.node_best[i] = out;
+        if (best >= 0 && (out.flags & 4u)) {
+            const uint32_t W = a.cat_words;
+            const uint32_t* src = all_cats + ((size_t)best * stride + i) * W;
+            const size_t tid = (size_t)a.nodes[i].tree_id;
+            for (uint32_t w = 0; w < W; w++) {
+                a.node_cats[(size_t)i * W + w] = src[w];
+                a.tcats[tid * W + w] = src[w];
             }
         }
     }
@@ -1824,6 +1878,7 @@ __global__ void k_tree_init(LevelArgs a, uint32_t n_local, uint32_t n_global, co
     TreeState* st = a.st;
     st->m = 1; st->n_tree_nodes = 1; st->leaf_count = 1; st->acc_count = 1; st->acc_total = n_local;
     st->chunk_count = (n_local + kChunkRows - 1) / kChunkRows; st->kept = 0; st->error = 0;
+    st->rank_stride = 0;
 }
 
 __global__ void k_iota(uint32_t* rows, uint32_t n) {
@@ -1999,18 +2054,27 @@ void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_
 #undef FB_HS
 }
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
-    dim3 grid(max_m, a.n_features);
-    count_launch();
-    k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    if (a.feat_hi > a.feat_lo) {
+        dim3 grid(max_m, a.feat_hi - a.feat_lo);
+        count_launch();
+        k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    }
     count_launch();
     k_split_node<<<max_m, 32, 0, s>>>(a);
 }
 void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
-    dim3 grid(max_m, a.n_features);
-    count_launch();
-    k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    if (a.feat_hi > a.feat_lo) {
+        dim3 grid(max_m, a.feat_hi - a.feat_lo);
+        count_launch();
+        k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+    }
     count_launch();
     k_split_node_decide<<<(max_m + 7) / 8, 256, 0, s>>>(a);
+}
+void launch_merge_decide(const LevelArgs& a, const SplitRec* all_best, const uint32_t* all_cats, uint32_t n_ranks,
+                         uint32_t max_m, cudaStream_t s) {
+    count_launch();
+    k_merge_decide<<<(max_m + 255) / 256, 256, 0, s>>>(a, all_best, all_cats, n_ranks, max_m);
 }
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
     count_launch();

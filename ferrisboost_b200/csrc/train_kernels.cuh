@@ -96,7 +96,9 @@ struct LevelArgs {
     Pair* hist_acc;              // accumulate-node histograms (acc index slots)
     Pair* hist_cur;              // full histograms of this level (node slots)
     const Pair* hist_prev;       // full histograms of the previous level
-    unsigned long long slot_pairs; // pairs per histogram slot (total bins)
+    unsigned long long slot_pairs; // pairs per histogram slot (total bins; a rank's block when feature-sharded)
+    uint32_t feat_lo, feat_hi;   // features this rank scores (all unless the split search is feature-sharded)
+    uint32_t bin_lo;             // first bin of feat_lo in the node histograms (their slots hold bins from here)
     SplitRec* feat_best;         // [node * F + f]
     // category sets: cat_words 32-bit words each (>= 8; a bit per code, set =
     // right-going); codes at or beyond 32 * cat_words go left
@@ -205,6 +207,10 @@ void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_
 void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
 // k_split_feat, then per-node reduction and decisions in one launch (a.fuse set)
 void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s);
+// Feature-sharded split search: merge the n_ranks gathered per-node winners
+// (all_best / all_cats: [rank][max_m] records / sets) and decide the level.
+void launch_merge_decide(const LevelArgs& a, const SplitRec* all_best, const uint32_t* all_cats, uint32_t n_ranks,
+                         uint32_t max_m, cudaStream_t s);
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_part_scan(const LevelArgs& a, cudaStream_t s);
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
