@@ -621,6 +621,8 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
     dirflags_.alloc((uint64_t)max_chunks_ * kPartThreads);
     chunk_off_.alloc(4 * (uint64_t)max_chunks_);
     node_left_.alloc(4 * lvl);
+    part_cnt_.alloc(8 * lvl);
+    FB_CUDA_CHECK(cudaMemsetAsync(part_cnt_.p, 0, part_cnt_.bytes, s_));
     node_left_global_.alloc(4 * lvl);
     trec_.alloc(sizeof(TreeRec) * tree_nodes);
     tcats_.alloc(set_bytes * tree_nodes);
@@ -1003,6 +1005,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         FB_CUDA_CHECK(cudaMemsetAsync(fuse_.p, 0, 16, s_));
     }
     a.fuse = fuse_.as<unsigned int>();
+    a.part_cnt = part_cnt_.as<unsigned long long>();
     // Leaf values reach the margins either by one walk of the finished tree
     // per row (k_tree_walk; the last level then needs no partition) or per
     // partition chunk and k_leaf_final.  Measured on B200: the walk is faster
@@ -1105,8 +1108,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             launch_split_decide(a, max_m, s_);
         }
         if (!(a.walk && a.last_level)) {  // with the walk, the last level's children need no partition
-            launch_part_count(a, max_chunks, s_);
-            launch_part_scatter(a, max_chunks, s_);
+            launch_part_level(a, max_chunks, s_);
         }
         cur = 1 - cur;
     }

@@ -265,6 +265,7 @@ class TrainCtx {
     cudaEvent_t hevc_[16] = {};  // per level: histogram kernels done, all-reduce starts
     DevMem level_stats_;
     DevMem fuse_;  // last-CTA counters of the fused level kernels (depthwise)
+    DevMem part_cnt_;  // k_part_level reservation counters, zero between levels
     double hist_ms_ = 0, hist_launches_ = 0, hist_bytes_ = 0, comm_ms_ = 0, hist_updates_ = 0;
 };
 

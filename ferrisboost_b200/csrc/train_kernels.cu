@@ -1681,22 +1681,104 @@ __device__ void next_level_body(const LevelArgs& a, unsigned long long* wt64, ui
     }
 }
 
-// Partition passes; with a.fuse set (depthwise growth) the last CTA of the
-// count pass also scans the chunk counts (k_part_scan) and the last CTA of
-// the scatter pass builds the next level (next_level_body).
-__global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) {
-    part_count_work(a);
-    if (a.fuse && last_block_done(a.fuse + 1)) {
-        __shared__ uint32_t wt_scan[32];
-        part_scan_body<kPartThreads>(a, wt_scan);
+// Stable partition passes (count, k_part_scan, scatter): the single-node
+// partition entry points and lossguide growth.
+__global__ void __launch_bounds__(kPartThreads) k_part_count(LevelArgs a) { part_count_work(a); }
+
+__global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) { part_scatter_work(a); }
+
+// Depthwise growth: the whole level partition in one pass.  Each chunk CTA
+// finds its rows' directions, reserves room with one 64-bit atomic on its
+// node's counter pair (left rows counted up from the node's start in the low
+// word, right rows counted down from its end in the high word; a node holds
+// fewer than 2^32 rows, so the low word never carries) and writes its rows
+// there in row order.  Chunks of one node land in the order their
+// reservations happen, so a child's span is a run of row-ordered pieces
+// rather than one row-ordered run: nothing downstream depends on the order
+// (histograms are exact integer sums, leaf values are added per row, the
+// child sizes are the same).  Rows of nodes that stop growing get their leaf
+// value as in k_part_count.
+__device__ __forceinline__ void part_level_work(const LevelArgs& a) {
+    __shared__ uint32_t wt[32];
+    __shared__ uint32_t cats[8];
+    __shared__ uint32_t stage[kChunkRows];
+    __shared__ unsigned long long base;
+    const uint32_t c = blockIdx.x;
+    const TreeState* st = a.st;
+    if (c >= st->chunk_count) return;
+    const uint32_t m = st->m;
+    const uint32_t j = find_segment_warp(a.chunk_prefix, m, c);
+    const NodeInfo ni = a.nodes[j];
+    const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
+    const uint32_t cnt = min(kChunkRows, ni.len - r0);
+    const uint32_t* rows = a.rows_cur + ni.start + r0;
+    const SplitDesc sd = a.split[j];
+    const uint32_t i0 = threadIdx.x * kPartItems;
+    uint32_t r[kPartItems];
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) r[k] = i0 + k < cnt ? rows[i0 + k] : 0u;
+    if (sd.child_slot < 0) {
+        if (!a.walk) {
+            const float leaf = a.trec[ni.tree_id].leaf;
+#pragma unroll
+            for (int k = 0; k < kPartItems; k++)
+                if (i0 + k < cnt) a.pred[r[k]] = __fadd_rn(a.pred[r[k]], leaf);
+        }
+        return;
+    }
+    const uint32_t* set = node_set(a, j, cats);
+    const FeatLoc fl = a.floc[sd.feat];
+    __syncthreads();
+    uint32_t flags = 0;
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        uint32_t bin = fl.missing;
+        if (i0 + k < cnt) {
+            const uint8_t* p = fl.base + (size_t)r[k] * fl.stride + fl.byte_off;
+            bin = fl.width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+        }
+        bool left;
+        if (bin == fl.missing) left = (sd.flags & 2u) != 0;
+        else if (sd.flags & 4u) left = cat_left(set, a.cat_words, bin);
+        else left = bin < sd.bin;
+        if (i0 + k < cnt && left) flags |= 1u << k;
+    }
+    uint32_t L;
+    const uint32_t lpos = block_excl_scan_u32<kPartThreads>((uint32_t)__popc(flags), wt, L);
+    if (threadIdx.x == 0)
+        base = atomicAdd(&a.part_cnt[j], (unsigned long long)L | ((unsigned long long)(cnt - L) << 32));
+    uint32_t li = lpos, ri = L + (min(i0, cnt) - lpos);
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        if (i0 + k < cnt) {
+            if (flags & (1u << k)) stage[li++] = r[k];
+            else stage[ri++] = r[k];
+        }
+    }
+    __syncthreads();
+    const uint32_t lbase = (uint32_t)base, rbase = (uint32_t)(base >> 32);
+    uint32_t* dst_l = a.rows_next + ni.start + lbase;
+    // this chunk's right rows end where the rows reserved before them begin
+    uint32_t* dst_r = a.rows_next + ni.start + (ni.len - rbase - (cnt - L));
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+        if (i < L) dst_l[i] = stage[i];
+        else dst_r[i - L] = stage[i];
     }
 }
 
-__global__ void __launch_bounds__(kPartThreads) k_part_scatter(LevelArgs a) {
-    part_scatter_work(a);
-    if (a.fuse && last_block_done(a.fuse + 2)) {
+// The last CTA turns the counter pairs into the per-node left counts, clears
+// them for the next level and builds the next level (next_level_body).
+__global__ void __launch_bounds__(kPartThreads) k_part_level(LevelArgs a) {
+    part_level_work(a);
+    if (last_block_done(a.fuse + 1)) {
         __shared__ unsigned long long wt64_next[32];
         __shared__ uint32_t wt_next[32];
+        const uint32_t m = a.st->m;
+        for (uint32_t j = threadIdx.x; j < m; j += blockDim.x) {
+            a.node_left[j] = (uint32_t)__ldcg(&a.part_cnt[j]);
+            a.part_cnt[j] = 0ull;
+        }
+        __syncthreads();
         next_level_body<kPartThreads>(a, wt64_next, wt_next);
     }
 }
@@ -1905,8 +1987,9 @@ __global__ void k_transpose_block(const uint8_t* __restrict__ src, uint8_t* __re
 
 // Column-major copy of a block's row records (feature i of the block at
 // cols + i * n_rows * W): the partition passes gather one bin per row, and
-// the rows of a node are ascending ids, so at the shallow levels neighbouring
-// rows of a node share the 32-byte sectors of a column but never a record's.
+// the rows of a node come in runs of ascending ids, so at the shallow levels
+// neighbouring rows of a node share the 32-byte sectors of a column but never
+// a record's.
 // Tiled transpose: a CTA stages kTrRows records in shared memory with
 // coalesced word loads (row pitch stride + 4 bytes, so the column reads hit
 // distinct banks), then writes each feature's kTrRows bins contiguously.
@@ -2084,6 +2167,10 @@ void launch_part_scan(const LevelArgs& a, cudaStream_t s) { count_launch(); k_pa
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
     count_launch();
     k_part_scatter<<<max_chunks, kPartThreads, 0, s>>>(a);
+}
+void launch_part_level(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    count_launch();
+    k_part_level<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
 void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s) {
     if (n_rows == 0) return;

@@ -120,8 +120,10 @@ struct LevelArgs {
     TreeRec* trec;
     uint32_t* tcats;             // [tree node][cat_words]
     const uint32_t* node_hist;   // lossguide: histogram-pool slot of each node (null: level slots)
-    unsigned int* fuse;          // depthwise: 3 zeroed counters; the one-CTA steps run in the last CTA
+    unsigned int* fuse;          // depthwise: zeroed counters; the one-CTA steps run in the last CTA
                                  // of the kernel before them (null: separate launches)
+    unsigned long long* part_cnt; // depthwise: per node (left rows, right rows) reserved by k_part_level;
+                                  // zero between levels
 };
 
 #ifdef __CUDACC__
@@ -214,6 +216,9 @@ void launch_merge_decide(const LevelArgs& a, const SplitRec* all_best, const uin
 void launch_part_count(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_part_scan(const LevelArgs& a, cudaStream_t s);
 void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
+// Depthwise: one-pass partition of every node of the level, then the next
+// level's tables (last CTA).  Needs a.fuse and a.part_cnt.
+void launch_part_level(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 // Every local row walks the finished tree (a.trec / a.tcats) on its record's
 // bins and adds its leaf's value to its margin (training/mod.rs:5020-5063,
