@@ -469,8 +469,9 @@ def run_ours(args, rank, world):
 
     # untimed: the process's first CUDA work (context creation, module
     # loading) on a few rows, so the e2e leg times the workload, not start-up;
-    # when sharded also the process's first NCCL communicator (library
-    # loading and topology discovery take seconds once per process)
+    # when sharded also the process's NCCL communicator, which
+    # distributed.train keeps for the process group's later trainings (its
+    # start takes from a fraction of a second to seconds, once per process)
     wn = min(n, 4096 * world)
     train_public(p, 2, data=(X[:wn], y[:wn]))
 
@@ -555,7 +556,8 @@ def run_ours(args, rank, world):
                 "h2d_bytes_per_step": int(e2e_h2d / E2E_ROUNDS),
                 "d2h_bytes_per_step": int(tree_readback + 16 + len(model_json) / E2E_ROUNDS),
                 "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "
-                            "per-rank bytes; wall clock, max over ranks"},
+                            "per-rank bytes; wall clock, max over ranks"
+                            + ("; the NCCL communicator kept from the untimed warm-up training" if world > 1 else "")},
         **({"e2e_parquet": e2e_parquet} if e2e_parquet else {}),
         "model_sha256": _sha256(model_json),
         "gpu_launches": int(launches),

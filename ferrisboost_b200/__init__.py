@@ -436,7 +436,7 @@ class Shard(NamedTuple):
     """One rank's part of a row-sharded run (see ``ferrisboost_b200.distributed``)."""
     row_offset: int       # global index of this rank's first row
     n_rows_global: int    # rows over all ranks
-    nccl_id: bytes        # fbgpu_nccl_unique_id of rank 0, 128 bytes
+    nccl_id: bytes        # fbgpu_nccl_unique_id of rank 0, 128 bytes (unused with comm)
     nranks: int
     rank: int
     base_score: float     # over all rows (fb_initial_base_score) or the given base_score

@@ -140,6 +140,8 @@ SIGNATURES = {
                                            C.c_int32, C.c_int32]),
     "fbgpu_comm_begin": (C.c_int, [u8p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32, C.POINTER(P)]),
     "fbgpu_comm_free": (None, [P]),
+    "fbgpu_comm_usable": (C.c_int32, [P]),
+    "fbgpu_comm_abort": (None, [P]),
     "fbgpu_ctx_adopt_comm": (C.c_int, [P, P]),
     "fb_booster_free": (None, [P]),
     "fb_booster_update": (C.c_int32, [P, C.c_uint32]),

@@ -144,7 +144,7 @@ void TrainCtx::set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t
     rank_ = rank;
 }
 
-void TrainCtx::adopt_comm(std::unique_ptr<NcclComm> comm, int nranks, int rank) {
+void TrainCtx::adopt_comm(std::shared_ptr<NcclComm> comm, int nranks, int rank) {
     if (nranks < 1 || rank < 0 || rank >= nranks) throw InputError("invalid rank / world size");
     if (comm_) throw InputError("the context already has a communicator");
     if (nranks == 1) return;
@@ -1732,10 +1732,20 @@ fbgpu_status fbgpu_comm_begin(const uint8_t* unique_id, int32_t nranks, int32_t 
 
 void fbgpu_comm_free(fbgpu_comm* c) { delete c; }
 
+int32_t fbgpu_comm_usable(fbgpu_comm* c) {
+    if (!c) return 0;
+    if (c->impl.worker.joinable()) return 0;  // still starting: not yet joined by any context
+    return c->impl.usable() ? 1 : 0;
+}
+
+void fbgpu_comm_abort(fbgpu_comm* c) {
+    if (c && !c->impl.worker.joinable() && c->impl.comm) c->impl.comm->abort();
+}
+
 fbgpu_status fbgpu_ctx_adopt_comm(fbgpu_ctx* ctx, fbgpu_comm* c) {
     return guard(ctx, [&] {
         if (!c) throw fbg::InputError("null communicator");
-        ctx->impl.adopt_comm(c->impl.take(), c->impl.nranks, c->impl.rank);
+        ctx->impl.adopt_comm(c->impl.share(), c->impl.nranks, c->impl.rank);
     });
 }
 

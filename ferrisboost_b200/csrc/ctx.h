@@ -118,7 +118,7 @@ class TrainCtx {
     // communicator per context (ranks in the same order on every GPU).
     void set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t timeout_ms);
     // A communicator initialized ahead of time (fbgpu_comm_begin).
-    void adopt_comm(std::unique_ptr<NcclComm> comm, int nranks, int rank);
+    void adopt_comm(std::shared_ptr<NcclComm> comm, int nranks, int rank);
     int nranks() const { return nranks_; }
     // Waits for the training stream; when sharded, a bounded poll that aborts
     // the communicator if a peer stops answering.
@@ -225,7 +225,7 @@ class TrainCtx {
     DevMem gp_multi_;                 // multiclass: K x n f32 gradient pairs of the round
     DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double)
     DevMem exptab_;  // host-expf exception table (fexp.h), empty when unverified
-    std::unique_ptr<NcclComm> comm_;
+    std::shared_ptr<NcclComm> comm_;
     int nranks_ = 1, rank_ = 0;
     DevMem node_left_global_, comm_scratch_;
     // feature-sharded split search (row-sharded depthwise trees): rank r
@@ -334,19 +334,23 @@ class ExplainModel {
 // training will use, run on a background host thread while the caller
 // prepares its data (fbgpu_comm_begin).  take() waits for it.
 struct PendingComm {
-    std::unique_ptr<NcclComm> comm;
+    std::shared_ptr<NcclComm> comm;
     std::thread worker;
     std::exception_ptr error;
     int nranks = 1, rank = 0;
     ~PendingComm() {
         if (worker.joinable()) worker.join();
     }
-    std::unique_ptr<NcclComm> take() {
+    // The communicator, shared with the context that joins it; the handle
+    // keeps its reference, so a later context can join it again.
+    std::shared_ptr<NcclComm> share() {
         if (worker.joinable()) worker.join();
         if (error) std::rethrow_exception(error);
-        if (!comm) throw InputError("the communicator was already taken by a context");
-        return std::move(comm);
+        if (!comm || comm->failed()) throw NcclError("the communicator failed or was aborted");
+        return comm;
     }
+    // Started without error, not failed, and no context holds it.
+    bool usable() const { return !worker.joinable() && !error && comm && !comm->failed() && comm.use_count() == 1; }
 };
 
 // Sets the message fbgpu_last_error(NULL) returns on this thread.

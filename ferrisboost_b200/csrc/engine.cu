@@ -957,7 +957,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
         if (sh.comm) {
             if (sh.comm->impl.nranks != sh.nranks || sh.comm->impl.rank != sh.rank)
                 throw InputError("the communicator was started for another rank / world size");
-            b->ctx->adopt_comm(sh.comm->impl.take(), sh.nranks, sh.rank);
+            b->ctx->adopt_comm(sh.comm->impl.share(), sh.nranks, sh.rank);
         } else {
             b->ctx->set_comm(sh.nccl_id, sh.nranks, sh.rank, sh.timeout_ms);
         }

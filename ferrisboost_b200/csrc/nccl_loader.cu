@@ -120,6 +120,12 @@ NcclComm::~NcclComm() {
     a.abort(c);
 }
 
+void NcclComm::abort() {
+    if (comm_ && !failed_) api().abort(static_cast<ncclComm_t>(comm_));
+    comm_ = nullptr;
+    failed_ = true;
+}
+
 void NcclComm::fail(const std::string& msg, bool timeout) {
     // abort ends the communicator's kernels still waiting on a peer
     if (comm_ && !failed_) api().abort(static_cast<ncclComm_t>(comm_));

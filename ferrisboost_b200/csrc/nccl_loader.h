@@ -44,6 +44,9 @@ public:
     // Waits for the stream, polling the communicator; aborts it after the time limit.
     void sync(cudaStream_t s);
     bool failed() const { return failed_; }
+    // Ends the communicator at once, without waiting for the peers (exit
+    // paths; nothing may be in flight on it); later calls fail.
+    void abort();
 
 private:
     void* comm_ = nullptr;  // ncclComm_t

@@ -19,10 +19,17 @@ module is the multi-GPU replacement for that trait.
 
 ``torch.distributed`` (any backend; gloo is enough) only carries the NCCL id,
 the cuts and the label mean between the ranks before training.
+
+The NCCL communicator is made by the first ``train`` of a process group and
+kept for the next ones (starting one takes from a fraction of a second to
+seconds, like the process group itself); ``release_communicators`` ends the
+kept ones.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes as C
+import hashlib
 import os
 import sys
 from typing import Any, Mapping, Sequence
@@ -32,7 +39,8 @@ import numpy as np
 from . import (_OBJECTIVES, Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params,
                lib)
 
-__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost", "Communicator"]
+__all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost", "Communicator",
+           "release_communicators"]
 
 
 class Communicator:
@@ -40,7 +48,8 @@ class Communicator:
     (fbgpu_comm_begin): its initialization and a warm-up of the collectives
     run on a background thread of the library while this rank sketches and
     bins its rows.  Every rank creates one with the same unique id; a
-    Booster built with ``Shard(comm=...)`` takes it over."""
+    Booster built with ``Shard(comm=...)`` shares it; the communicator ends
+    when this object and every booster holding it are gone."""
 
     def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int, timeout_ms: int = 120000):
         nid = np.frombuffer(unique_id, dtype=np.uint8).copy()
@@ -49,6 +58,17 @@ class Communicator:
         if st:
             raise RuntimeError(lib().fbgpu_last_error(None).decode())
         self.handle = h
+        self.timeout_ms = timeout_ms
+
+    def usable(self) -> bool:
+        """Started without error, not failed, and held by no live booster."""
+        return bool(self.handle) and lib().fbgpu_comm_usable(self.handle) == 1
+
+    def abort(self) -> None:
+        """Ends the communicator without waiting for the peers (nothing may be
+        in flight on it)."""
+        if self.handle:
+            lib().fbgpu_comm_abort(self.handle)
 
     def __del__(self):
         h = getattr(self, "handle", None)
@@ -58,6 +78,60 @@ class Communicator:
             except TypeError:  # interpreter shutdown: module globals already cleared
                 pass
             self.handle = None
+
+
+# Communicators kept between trainings: (group, world, rank, device) ->
+# (Communicator, generation).  The generation names the unique id the
+# communicator was made from, the same on every rank that made it together.
+_COMMS: dict = {}
+
+
+def release_communicators() -> None:
+    """Ends every communicator this process keeps (at exit too).  Call it on
+    every rank; boosters still holding one fail their next collective."""
+    while _COMMS:
+        _, (comm, _gen) = _COMMS.popitem()
+        comm.abort()
+        del comm
+
+
+atexit.register(release_communicators)
+
+
+def _all_gather(obj, group=None) -> list:
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, obj, group=group)
+    return out
+
+
+def _communicator(key, world: int, rank: int, device: int, timeout_ms: int, group=None):
+    """The kept communicator of ``key`` when every rank holds the same usable
+    one, else a new one from a unique id of rank 0 (kept for the next
+    training).  Every rank takes the same branch: one all-gather of the kept
+    generations decides, before any NCCL call."""
+    kept = _COMMS.get(key)
+    mine = kept[1] if kept is not None and kept[0].timeout_ms == timeout_ms and kept[0].usable() else None
+    gens = _all_gather(mine, group)
+    if mine is not None and all(g == mine for g in gens):
+        return kept[0]
+    if kept is not None:
+        del _COMMS[key]
+        if mine is not None:  # a peer cannot use it: end it here without waiting for that peer
+            kept[0].abort()
+        del kept
+    nid = None
+    if rank == 0:  # a failure on rank 0 is sent to every rank, which all raise
+        try:
+            nid = nccl_unique_id()
+        except RuntimeError as e:
+            nid = "error: " + str(e)
+    nid = _broadcast(nid, group)
+    if isinstance(nid, str):
+        raise RuntimeError(f"rank 0 could not create an NCCL id ({nid})")
+    comm = Communicator(nid, world, rank, device, timeout_ms)
+    _COMMS[key] = (comm, hashlib.blake2b(nid, digest_size=8).hexdigest())
+    return comm
 
 
 class PeerLost(RuntimeError):
@@ -250,18 +324,10 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
         raise ValueError(f"{n} rows cannot be sharded over {world} ranks")
     cat = _feature_flags(feature_types, F)
     trace = _PhaseTrace(f"rank {rank}")
-    nid = None
-    if rank == 0:  # a failure on rank 0 is sent to every rank, which all raise
-        try:
-            nid = nccl_unique_id()
-        except RuntimeError as e:
-            nid = "error: " + str(e)
-    nid = _broadcast(nid, group)
-    if isinstance(nid, str):
-        raise RuntimeError(f"rank 0 could not create an NCCL id ({nid})")
     timeout_ms = int(max(1.0, timeout_s) * 1000)
-    # the communicator initializes while the cuts are sketched and the rows binned
-    comm = Communicator(nid, world, rank, p["device_index"], timeout_ms)
+    # a new communicator initializes while the cuts are sketched and the rows binned
+    comm = _communicator((id(group) if group is not None else 0, world, rank, p["device_index"]), world, rank,
+                         p["device_index"], timeout_ms, group)
     trace("id, communicator start")
     cuts = sketch_cuts(X, p["max_bin"], w, cat, p["nthread"], group, device=p["device_index"])
     trace("sketch + all-gather of cuts")
@@ -283,7 +349,7 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     ds = Dataset(X[lo:hi], max_bin=p["max_bin"], feature_types=feature_types, nthread=p["nthread"], cuts=cuts,
                  device=p["device_index"])
     trace("shard binning")
-    shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=nid, nranks=world, rank=rank, base_score=base,
+    shard = Shard(row_offset=lo, n_rows_global=n, nccl_id=b"", nranks=world, rank=rank, base_score=base,
                   timeout_ms=timeout_ms, comm=comm, class_margins=class_margins)
     b = Booster(params, ds, y[lo:hi], None if w is None else w[lo:hi], shard=shard)
     trace("booster (communicator ready)")

@@ -143,8 +143,9 @@ fb_booster* fb_booster_create_sharded(const fb_dataset* shard, const float* labe
                                       const uint8_t* nccl_id, int32_t nranks, int32_t rank, uint32_t timeout_ms);
 /* fb_booster_create_sharded with a communicator already started by
  * fbgpu_comm_begin (include/fbgpu.h), so its initialization overlapped the
- * data preparation; the booster takes the communicator over (the handle is
- * still freed with fbgpu_comm_free). */
+ * data preparation, or kept from an earlier training; the booster shares
+ * the communicator with the handle (which is still freed with
+ * fbgpu_comm_free). */
 struct fbgpu_comm;
 fb_booster* fb_booster_create_sharded_comm(const fb_dataset* shard, const float* labels, const float* weights,
                                            const fb_params* p, uint64_t row_offset, uint64_t n_rows_global,

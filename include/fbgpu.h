@@ -155,13 +155,23 @@ fbgpu_status fbgpu_ctx_set_comm(fbgpu_ctx* ctx, const uint8_t* unique_id, int32_
  * set up NCCL's connections) run on a background host thread while the
  * caller sketches and bins its data; fbgpu_ctx_adopt_comm joins it to a
  * context (waiting for it if needed) and fbgpu_comm_free releases the
- * handle.  Every rank calls fbgpu_comm_begin, with the same unique id.  No
- * counterpart in the reference. */
+ * handle.  Every rank calls fbgpu_comm_begin, with the same unique id.  The
+ * handle and the contexts that joined it share the communicator, which ends
+ * when the last of them is released, so a process can keep one handle and
+ * join it to the contexts of successive trainings (every rank the same
+ * ones, one context at a time).  No counterpart in the reference. */
 typedef struct fbgpu_comm fbgpu_comm;
 fbgpu_status fbgpu_comm_begin(const uint8_t* unique_id, int32_t nranks, int32_t rank, int32_t device,
                               uint32_t timeout_ms, fbgpu_comm** out);
 fbgpu_status fbgpu_ctx_adopt_comm(fbgpu_ctx* ctx, fbgpu_comm* comm);
 void fbgpu_comm_free(fbgpu_comm* comm);
+/* 1 when the communicator started without error, has not failed or been
+ * aborted, and no live context holds it (it may join a new one); else 0. */
+int32_t fbgpu_comm_usable(fbgpu_comm* comm);
+/* Aborts the communicator now, without waiting for the peers (exit paths;
+ * nothing may be in flight on it).  Contexts holding it fail their next
+ * collective; the handle is still freed with fbgpu_comm_free. */
+void fbgpu_comm_abort(fbgpu_comm* comm);
 
 /* Feature metadata: bins per feature (cuts + 1), storage width in bytes
  * (bins.rs:58-66 BinWidth::for_feature) and categorical flags (may be NULL).

@@ -158,3 +158,61 @@ def test_liveness_detects_a_lost_peer_before_the_next_round(tmp_path, scenario):
         assert "left" in r0
     else:
         assert "has not answered" in r0
+
+
+class _FakeComm:
+    """Stands in for distributed.Communicator: no NCCL, no GPU."""
+
+    def __init__(self, nid, world, rank, device, timeout_ms):
+        self.nid, self.timeout_ms, self.held, self.aborted = bytes(nid), timeout_ms, False, False
+
+    def usable(self):
+        return not self.held and not self.aborted
+
+    def abort(self):
+        self.aborted = True
+
+
+def _comm_cache_worker(rank, world, port, out_dir):
+    import json
+    import torch.distributed as dist
+    from ferrisboost_b200 import distributed as fbd
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    fbd.Communicator = _FakeComm
+    fbd.nccl_unique_id = lambda: os.urandom(128)
+    try:
+        key = (0, world, rank, 0)
+        first = fbd._communicator(key, world, rank, 0, 5000)
+        again = fbd._communicator(key, world, rank, 0, 5000)  # every rank holds the same usable one
+        if rank == 1:
+            again.held = True  # a live booster still holds rank 1's communicator
+        third = fbd._communicator(key, world, rank, 0, 5000)
+        other_timeout = fbd._communicator(key, world, rank, 0, 9000)
+        ids = [None] * world
+        dist.all_gather_object(ids, (first.nid, third.nid, other_timeout.nid))
+        res = {"reused": again is first, "replaced": third is not again,
+               "first_aborted": first.aborted, "third_aborted": third.aborted,
+               "same_ids": all(i == ids[0] for i in ids),
+               "new_on_timeout": other_timeout is not third, "kept": len(fbd._COMMS)}
+        fbd.release_communicators()
+        res["released"] = other_timeout.aborted and not fbd._COMMS
+        with open(os.path.join(out_dir, f"c{rank}.json"), "w") as f:
+            json.dump(res, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_communicator_kept_between_trainings_only_when_every_rank_can_use_it(tmp_path):
+    import json
+    import torch.multiprocessing as mp
+    world, port = 2, _free_port()
+    mp.start_processes(_comm_cache_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    r0 = json.loads((tmp_path / "c0.json").read_text())
+    r1 = json.loads((tmp_path / "c1.json").read_text())
+    for r in (r0, r1):
+        assert r["reused"] and r["replaced"] and r["same_ids"] and r["new_on_timeout"]
+        assert r["kept"] == 1 and r["released"] and not r["third_aborted"]
+    # rank 0 could use its copy but rank 1 could not: rank 0 ends it without waiting
+    # for rank 1; rank 1's copy stays with the booster that holds it
+    assert r0["first_aborted"] and not r1["first_aborted"]

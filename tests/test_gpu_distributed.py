@@ -69,11 +69,17 @@ def _worker(rank, world, port, out_dir, split_shard):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
     try:
+        gens = []
         for case, params in CASES.items():
             X, y, ft = _data(case)
             m = fbd.train(params, X, label=y, num_boost_round=6, feature_types=ft, timeout_s=60)
             with open(os.path.join(out_dir, f"{case}_r{rank}.json"), "wb") as f:
                 f.write(m.to_json())
+            gens += [g for _, g in fbd._COMMS.values()]
+        # one communicator, made by the first training and kept for the others
+        with open(os.path.join(out_dir, f"gens_r{rank}.txt"), "w") as f:
+            f.write(" ".join(gens))
+        fbd.release_communicators()
     finally:
         dist.destroy_process_group()
 
@@ -94,3 +100,5 @@ def test_two_gpu_models_equal_single_gpu(tmp_path, split_shard):
         for r in range(world):
             got = (tmp_path / f"{case}_r{r}.json").read_bytes()
             assert got == want, f"{case}: rank {r} model differs from the single-GPU model"
+    gens = [(tmp_path / f"gens_r{r}.txt").read_text().split() for r in range(world)]
+    assert len(gens[0]) == len(CASES) and len(set(gens[0])) == 1 and gens[0] == gens[1]
