@@ -52,6 +52,7 @@ sys.path.insert(0, ROOT)
 N_FEATURES = 28
 PARAMS = {"objective": "binary:logistic", "max_depth": 8, "eta": 0.1, "lambda": 1.0, "max_bin": 256}
 E2E_ROUNDS = 100
+E2E_RUNS = 3  # e2e runs per bench line; the median is reported
 # DRAM bytes / algorithmic bytes of k_hist_stage over one tree: one ncu
 # capture of a 4M-row configs[1]-shaped tree (dram__bytes_read.sum +
 # dram__bytes_write.sum over its 8 histogram launches); roofline.traffic =
@@ -476,12 +477,18 @@ def run_ours(args, rank, world):
     train_public(p, 2, data=(X[:wn], y[:wn]))
 
     # e2e: 100 rounds through the public train() from host arrays (sketch,
-    # binning, uploads, rounds, model JSON); wall clock, max over ranks
-    _fence(dist)
-    t0 = time.perf_counter()
-    m = train_public(p, E2E_ROUNDS)
-    model_json = m.to_json()
-    e2e_s = _max_over_ranks(dist, time.perf_counter() - t0)
+    # binning, uploads, rounds, model JSON); wall clock, max over ranks; the
+    # median of E2E_RUNS runs (the host cores are shared with other jobs, so
+    # a single run can catch a stall of the multithreaded set-up), every run
+    # listed beside it
+    e2e_runs = []
+    for _ in range(E2E_RUNS):
+        _fence(dist)
+        t0 = time.perf_counter()
+        m = train_public(p, E2E_ROUNDS)
+        model_json = m.to_json()
+        e2e_runs.append(_max_over_ranks(dist, time.perf_counter() - t0))
+    e2e_s = float(np.median(e2e_runs))
     exact_model = m
     e2e_parquet = None
     if args.parquet and world == 1:
@@ -552,7 +559,7 @@ def run_ours(args, rank, world):
                    "l2": "inputs larger than L2 (bin records and fixed-point gradients exceed 126 MB)"
                    if n * ((F * (2 if p["max_bin"] > 255 else 1) + 15) // 16 * 16 + 16) > 126e6
                    else "inputs smaller than L2"},
-        "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds",
+        "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds", "runs": [round(v, 4) for v in e2e_runs],
                 "h2d_bytes_per_step": int(e2e_h2d / E2E_ROUNDS),
                 "d2h_bytes_per_step": int(tree_readback + 16 + len(model_json) / E2E_ROUNDS),
                 "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "

@@ -1008,18 +1008,26 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     a.part_cnt = part_cnt_.as<unsigned long long>();
     // Leaf values reach the margins either by one walk of the finished tree
     // per row (k_tree_walk; the last level then needs no partition) or per
-    // partition chunk and k_leaf_final.  Measured on B200: the walk is faster
-    // up to a few million local rows (C0, 1M rows: -3 %), the partition path
-    // beyond (C1, 11M rows: the walk is +2 %).  FBGPU_WALK=0 / 1 forces one.
+    // partition chunk (k_part_level for nodes that stop early, k_part_final
+    // for the last level).  The walk streams every row's record once and
+    // updates the margins in row order; the partition path updates them in
+    // arena order, one scattered sector per row.  Measured on B200: the walk
+    // is faster up to a few million local rows, and beyond when its fast form
+    // applies (the tree in shared memory, every feature in one staged record
+    // block): C1, 11M rows, 0.265 against 0.273 s / 100 rounds.
+    // FBGPU_WALK=0 / 1 forces one.
     static const int walk_env = [] {
         const char* e = std::getenv("FBGPU_WALK");
         return e ? std::atoi(e) : -1;
     }();
-    a.walk = walk_env >= 0 ? (walk_env ? 1u : 0u) : (n_ <= (4ull << 20) ? 1u : 0u);
     if (blocks_.size() == 1 && blocks_[0]->stride <= 64 && blocks_[0]->stride % 4 == 0) {
         a.walk_rec = blocks_[0]->base;
         a.walk_stride = blocks_[0]->stride;
     }
+    uint64_t max_nodes = (2ull << tp.max_depth) - 1;  // max_depth <= 14
+    if (tp.max_leaves) max_nodes = std::min<uint64_t>(max_nodes, 2ull * tp.max_leaves - 1);
+    const bool walk_fast = a.walk_rec != nullptr && max_nodes <= kWalkNodes;
+    a.walk = walk_env >= 0 ? (walk_env ? 1u : 0u) : ((n_ <= (4ull << 20) || walk_fast) ? 1u : 0u);
     const uint32_t maxd = tp.max_depth;
     FB_CUDA_CHECK(cudaEventRecord(ev0_, s_));
     int cur = 0;
@@ -1107,9 +1115,10 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         } else {
             launch_split_decide(a, max_m, s_);
         }
-        if (!(a.walk && a.last_level)) {  // with the walk, the last level's children need no partition
-            launch_part_level(a, max_chunks, s_);
-        }
+        // the last level's children are final leaves: with the walk they need
+        // nothing here, otherwise their leaf values go to the margins now
+        if (!a.last_level) launch_part_level(a, max_chunks, s_);
+        else if (!a.walk) launch_part_final(a, max_chunks, s_);
         cur = 1 - cur;
     }
     a.nodes = nodes_[cur].as<NodeInfo>();
@@ -1118,7 +1127,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     const uint32_t last_m = (uint32_t)std::min<uint64_t>(1ull << maxd, max_level_nodes_);
     if (a.walk)
         launch_tree_walk(a, (uint32_t)n_, s_);
-    else
+    else if (maxd == 0)  // the root is the only leaf
         launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
     FB_CUDA_CHECK(cudaGetLastError());
     FB_CUDA_CHECK(cudaEventRecord(ev1_, s_));

@@ -822,7 +822,8 @@ struct Booster {
     uint64_t row0 = 0, n_global = 0;  // global index of row 0, rows over all ranks
     fb_params p{};
     std::vector<int8_t> mono;
-    std::vector<float> labels, weights, grad_w;
+    std::vector<float> labels;  // host copy, kept only for the host-expf logistic rounds
+    std::vector<float> grad_w;
     std::unique_ptr<fbg::TrainCtx> ctx;
     Model model;
     uint32_t rounds_done = 0;
@@ -910,11 +911,6 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     b->row0 = sh.nranks > 1 ? sh.row_offset : 0;
     b->n_global = sh.nranks > 1 ? sh.n_global : d->n;
     if (p.monotone) b->mono.assign(p.monotone, p.monotone + d->F);
-    b->labels.resize(d->n);
-#pragma omp parallel for schedule(static) num_threads(threads(p.nthread))
-    for (int64_t c = 0; c < (int64_t)d->n; c += (1 << 18))
-        std::memcpy(b->labels.data() + c, y + c, 4 * std::min<uint64_t>(1 << 18, d->n - (uint64_t)c));
-    if (w) b->weights.assign(w, w + d->n);
     // mod.rs:5470-5495 gradient weights (sample weight x scale_pos_weight on
     // positives; objective.rs uses_scale_pos_weight: not for multiclass)
     if (p.scale_pos_weight != 1.0f && !multi) {
@@ -924,7 +920,7 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
             b->grad_w[i] = y[i] == 1.0f ? wi * p.scale_pos_weight : wi;
         }
     } else if (w) {
-        b->grad_w = b->weights;
+        b->grad_w.assign(w, w + d->n);
     }
     // objective.rs:41-61 label mean (FitInterceptGlmLike) when base_score is not given
     float base = p.base_score;
@@ -982,6 +978,13 @@ Booster* booster_create(const Dataset* d, const float* y, const float* w, const 
     b->model.base_score = base;
     phase("base score");
     b->ctx->set_labels(y, b->grad_w.empty() ? nullptr : b->grad_w.data(), nullptr, base_margin(p.objective, base));
+    if (p.objective == 1 && p.gpu_math != 1 && !b->ctx->has_exact_exp()) {
+        // the host-expf rounds read the labels on the host
+        b->labels.resize(d->n);
+#pragma omp parallel for schedule(static) num_threads(threads(p.nthread))
+        for (int64_t c = 0; c < (int64_t)d->n; c += (1 << 18))
+            std::memcpy(b->labels.data() + c, y + c, 4 * std::min<uint64_t>(1 << 18, d->n - (uint64_t)c));
+    }
     phase("labels upload");
     if (multi) {
         if (p.gpu_math != 1 && !b->ctx->has_exact_exp())

@@ -265,6 +265,20 @@ __device__ __forceinline__ float host_expf(float x, const uint2* tab, uint32_t p
     return fbx::fexp_core(x);
 }
 
+// host_expf with its first probe already loaded (t = tab[exp_slot(key)]).
+__device__ __forceinline__ float host_expf_from(float x, uint32_t key, uint2 t, const uint2* tab, uint32_t probes) {
+    if (t.x == fbx::kEmptyKey) return fbx::fexp_core(x);
+    if (t.x == key) return __uint_as_float(t.y);
+    uint32_t slot = fbx::exp_slot(key);
+    for (uint32_t i = 1; i < probes; i++) {
+        slot = (slot + 1) & (fbx::kExpTableSlots - 1);
+        const uint2 e = __ldg(&tab[slot]);
+        if (e.x == fbx::kEmptyKey) break;
+        if (e.x == key) return __uint_as_float(e.y);
+    }
+    return fbx::fexp_core(x);
+}
+
 __global__ void k_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin, uint32_t count, uint32_t* out) {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x)
         out[i] = __float_as_uint(host_expf(__uint_as_float(begin + i), tab, probes));
@@ -272,20 +286,52 @@ __global__ void k_expf_emulate(const uint2* tab, uint32_t probes, uint32_t begin
 
 // Gradient pass that only folds bounds and stores the f32 pairs (exact
 // squared error, exact logistic with the emulated host expf, fast mode).
-__global__ void k_gradient_max(GradArgs a, int mode) {
+// Each thread takes kGradRows rows a step (a grid stride apart, so every load
+// is coalesced) and issues their margin loads, then their first probes of the
+// exception table, before it needs any of them: the pass is bound by the
+// latency of those two dependent loads, not by their bytes.
+constexpr int kGradRows = 4;
+__global__ void __launch_bounds__(256) k_gradient_max(GradArgs a, int mode) {
     double mg = 0.0, mh = 0.0;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
-        float e = 0.0f;
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x, n = a.n;
+    for (uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += kGradRows * stride) {
+        float e[kGradRows];
+#pragma unroll
+        for (int k = 0; k < kGradRows; k++) e[k] = 0.0f;
         if (a.objective == 1) {
-            const float x = -a.pred[i];
-            e = mode == 1 ? fbx::fexp_core(x) : (mode == 2 ? host_expf(x, a.exptab, a.exp_probes) : a.host_exp[i]);
+            float x[kGradRows];
+#pragma unroll
+            for (int k = 0; k < kGradRows; k++) {
+                const uint64_t i = i0 + k * stride;
+                x[k] = i < n ? -a.pred[i] : 0.0f;
+            }
+            if (mode == 2) {
+                uint2 t[kGradRows];
+#pragma unroll
+                for (int k = 0; k < kGradRows; k++)
+                    t[k] = __ldg(&a.exptab[fbx::exp_slot(__float_as_uint(x[k]))]);
+#pragma unroll
+                for (int k = 0; k < kGradRows; k++)
+                    e[k] = host_expf_from(x[k], __float_as_uint(x[k]), t[k], a.exptab, a.exp_probes);
+            } else {
+#pragma unroll
+                for (int k = 0; k < kGradRows; k++) {
+                    const uint64_t i = i0 + k * stride;
+                    e[k] = mode == 1 ? fbx::fexp_core(x[k]) : (i < n ? a.host_exp[i] : 0.0f);
+                }
+            }
         }
-        float g, h;
-        row_gradient(a, i, e, g, h);
-        a.gpair_f32[2ull * i] = g;
-        a.gpair_f32[2ull * i + 1] = h;
-        mg = fmax(mg, bound_of(g));
-        mh = fmax(mh, bound_of(h));
+#pragma unroll
+        for (int k = 0; k < kGradRows; k++) {
+            const uint64_t i = i0 + k * stride;
+            if (i < n) {
+                float g, h;
+                row_gradient(a, (uint32_t)i, e[k], g, h);
+                reinterpret_cast<float2*>(a.gpair_f32)[i] = make_float2(g, h);
+                mg = fmax(mg, bound_of(g));
+                mh = fmax(mh, bound_of(h));
+            }
+        }
     }
     fold_max(mg, mh, a.maxbits);
 }
@@ -1767,8 +1813,11 @@ __device__ __forceinline__ void part_level_work(const LevelArgs& a) {
 }
 
 // The last CTA turns the counter pairs into the per-node left counts, clears
-// them for the next level and builds the next level (next_level_body).
-__global__ void __launch_bounds__(kPartThreads) k_part_level(LevelArgs a) {
+// them for the next level and builds the next level (next_level_body).  At
+// 32 registers four 512-thread CTAs fit an SM (three at the 40 the compiler
+// takes unbounded): the pass waits on its dependent loads, so residency is
+// what hides them.
+__global__ void __launch_bounds__(kPartThreads, 4) k_part_level(LevelArgs a) {
     part_level_work(a);
     if (last_block_done(a.fuse + 1)) {
         __shared__ unsigned long long wt64_next[32];
@@ -1780,6 +1829,61 @@ __global__ void __launch_bounds__(kPartThreads) k_part_level(LevelArgs a) {
         }
         __syncthreads();
         next_level_body<kPartThreads>(a, wt64_next, wt_next);
+    }
+}
+
+// Depthwise, the last level without the tree walk: the children are final
+// leaves, so each row's leaf value goes to its margin here instead of after a
+// partition into the children (k_part_level, then k_leaf_final): a row of a
+// split node takes its child's value (the same direction test as
+// k_part_level), a row of a node that stops here takes the node's own.  One
+// f32 addition per row, as on the other path; no row is written.
+__global__ void __launch_bounds__(kPartThreads) k_part_final(LevelArgs a) {
+    __shared__ uint32_t cats[8];
+    const uint32_t c = blockIdx.x;
+    const TreeState* st = a.st;
+    if (c >= st->chunk_count) return;
+    const uint32_t j = find_segment_warp(a.chunk_prefix, st->m, c);
+    const NodeInfo ni = a.nodes[j];
+    const uint32_t r0 = (c - a.chunk_prefix[j]) * kChunkRows;
+    const uint32_t cnt = min(kChunkRows, ni.len - r0);
+    const uint32_t* rows = a.rows_cur + ni.start + r0;
+    const SplitDesc sd = a.split[j];
+    const uint32_t i0 = threadIdx.x * kPartItems;
+    uint32_t r[kPartItems];
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) r[k] = i0 + k < cnt ? rows[i0 + k] : 0u;
+    if (sd.child_slot < 0) {
+        const float leaf = a.trec[ni.tree_id].leaf;
+#pragma unroll
+        for (int k = 0; k < kPartItems; k++)
+            if (i0 + k < cnt) a.pred[r[k]] = __fadd_rn(a.pred[r[k]], leaf);
+        return;
+    }
+    const uint32_t* set = node_set(a, j, cats);
+    const FeatLoc fl = a.floc[sd.feat];
+    const float leaf_l = a.trec[a.next_nodes[sd.child_slot].tree_id].leaf;
+    const float leaf_r = a.trec[a.next_nodes[sd.child_slot + 1].tree_id].leaf;
+    __syncthreads();
+    uint32_t bin[kPartItems];
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        bin[k] = fl.missing;
+        if (i0 + k < cnt) {
+            const uint8_t* p = fl.base + (size_t)r[k] * fl.stride + fl.byte_off;
+            bin[k] = fl.width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
+        }
+    }
+    float pv[kPartItems];
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) pv[k] = i0 + k < cnt ? a.pred[r[k]] : 0.0f;
+#pragma unroll
+    for (int k = 0; k < kPartItems; k++) {
+        bool left;
+        if (bin[k] == fl.missing) left = (sd.flags & 2u) != 0;
+        else if (sd.flags & 4u) left = cat_left(set, a.cat_words, bin[k]);
+        else left = bin[k] < sd.bin;
+        if (i0 + k < cnt) a.pred[r[k]] = __fadd_rn(pv[k], left ? leaf_l : leaf_r);
     }
 }
 
@@ -1811,25 +1915,28 @@ __global__ void __launch_bounds__(kPartThreads) k_leaf_final(LevelArgs a) {
 // memory with coalesced word loads (pitch + 4 bytes, so the 32 lanes' rows
 // fall in different banks) and the steps read bins from there; otherwise each
 // step reads its byte from the records in global memory.
-constexpr uint32_t kWalkNodes = 512;
 constexpr uint32_t kWalkThreads = 256;
 constexpr uint32_t kWalkStageBytes = 64;
-struct WalkNode {
-    const uint8_t* p;  // split: record base + the feature's byte offset
-    uint32_t stride;   // split: record stride
+// One 16-byte entry per node, read with one shared load per step.
+struct alignas(16) WalkNode {
     uint32_t lr;       // split: left | right << 16 (tree-local ids)
     uint32_t bin_fl;   // split bin | node flags << 16 | bin width << 24
     uint32_t val;      // split: missing sentinel; leaf: the leaf value's bits
-    uint32_t off;      // split: the feature's byte offset in the record
-    uint32_t pad;
+    uint32_t loc;      // split: the feature's byte offset in the staged record, or its id (unstaged)
 };
-static_assert(sizeof(WalkNode) == 32, "WalkNode layout");
+static_assert(sizeof(WalkNode) == 16, "WalkNode layout");
 
+// WORDS: 32-bit words staged per row (records of up to 4 * WORDS bytes).
+template <uint32_t WORDS>
 __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_t n_rows) {
     __shared__ WalkNode wn[kWalkNodes];
-    __shared__ uint32_t stage[kWalkThreads * (kWalkStageBytes / 4 + 1)];
+    __shared__ uint32_t stage[kWalkThreads * (WORDS + 1)];
+    __shared__ uint32_t plain;  // every split numeric on one-byte bins, right child = left + 1
     const uint32_t nn = a.st->n_tree_nodes;
     const bool table = nn <= kWalkNodes;
+    const bool staged = table && a.walk_rec != nullptr;
+    if (threadIdx.x == 0) plain = 1u;
+    __syncthreads();
     if (table) {
         for (uint32_t i = threadIdx.x; i < nn; i += blockDim.x) {
             const TreeRec t = a.trec[i];
@@ -1839,23 +1946,21 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
                 w.val = __float_as_uint(t.leaf);
             } else {
                 const FeatLoc fl = a.floc_rec[t.feat];
-                w.p = fl.base + fl.byte_off;
-                w.stride = fl.stride;
                 w.lr = (uint32_t)t.left | ((uint32_t)t.right << 16);
                 w.bin_fl = (t.bin & 0xffffu) | ((t.flags & 0xffu) << 16) | (fl.width << 24);
                 w.val = fl.missing;
-                w.off = fl.byte_off;
+                w.loc = staged ? fl.byte_off : t.feat;
+                if ((t.flags & 4u) || fl.width != 1 || t.right != t.left + 1) plain = 0u;
             }
             wn[i] = w;
         }
     }
-    const bool staged = table && a.walk_rec != nullptr;
     const uint32_t words = a.walk_stride / 4, pitch = words + 1;
     const uint8_t* srow = reinterpret_cast<const uint8_t*>(stage + threadIdx.x * pitch);
     // staged: the next step's records are loaded into registers (word i of
     // the step's contiguous block at i = threadIdx.x + k * blockDim.x) while
     // the current step walks, then stored to shared memory
-    constexpr uint32_t kWalkWords = kWalkStageBytes / 4;
+    constexpr uint32_t kWalkWords = WORDS;
     uint32_t nxt[kWalkWords];
     const uint32_t step = blockDim.x * gridDim.x;
     auto load_next = [&](uint32_t base) {
@@ -1868,6 +1973,14 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
         }
     };
     auto store_next = [&]() {
+        if (words == kWalkWords) {  // records of exactly kWalkWords words: no runtime division
+#pragma unroll
+            for (uint32_t k = 0; k < kWalkWords; k++) {
+                const uint32_t i = threadIdx.x + k * blockDim.x;
+                stage[(i / kWalkWords) * (kWalkWords + 1) + i % kWalkWords] = nxt[k];
+            }
+            return;
+        }
 #pragma unroll
         for (uint32_t k = 0; k < kWalkWords; k++) {
             const uint32_t i = threadIdx.x + k * blockDim.x;
@@ -1879,6 +1992,10 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
     };
     if (staged) load_next(blockIdx.x * blockDim.x);
     __syncthreads();
+    // the common tree: one 16-byte node load, one staged byte, a compare and
+    // an add per level
+    const bool fast = staged && plain != 0u;
+    const uint4* wn4 = reinterpret_cast<const uint4*>(wn);
     for (uint32_t base = blockIdx.x * blockDim.x; base < n_rows; base += step) {
         const uint32_t r = base + threadIdx.x;
         if (staged) {
@@ -1887,13 +2004,24 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
             load_next(base + step);
         }
         const float pv = r < n_rows ? a.pred[r] : 0.0f;  // in flight during the walk
-        if (r < n_rows) {
+        if (fast) {
+            if (r < n_rows) {
+                uint4 q = wn4[0];
+                for (uint32_t depth = 0; depth < 64 && !(q.y & (1u << 16)); depth++) {
+                    const uint32_t bin = srow[q.w];
+                    const bool left = bin == q.z ? (q.y & (2u << 16)) != 0u : bin < (q.y & 0xffffu);
+                    q = wn4[(q.x & 0xffffu) + (left ? 0u : 1u)];
+                }
+                if (q.y & (1u << 16)) a.pred[r] = __fadd_rn(pv, __uint_as_float(q.z));
+            }
+        } else if (r < n_rows) {
             uint32_t node = 0;
             for (uint32_t depth = 0; depth < 64; depth++) {  // trees are at most 15 levels deep
                 uint32_t flags, sbin, missing, width, left_id, right_id, bin;
                 float leaf = 0.0f;
                 if (table) {
-                    const WalkNode w = wn[node];
+                    const uint4 q = wn4[node];
+                    const WalkNode w{q.x, q.y, q.z, q.w};
                     flags = (w.bin_fl >> 16) & 0xffu;
                     if (flags & 1u) leaf = __uint_as_float(w.val);
                     sbin = w.bin_fl & 0xffffu;
@@ -1902,11 +2030,12 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
                     left_id = w.lr & 0xffffu;
                     right_id = w.lr >> 16;
                     if (!(flags & 1u)) {
-                        if (staged)
-                            bin = width == 2 ? (uint32_t)srow[w.off] | ((uint32_t)srow[w.off + 1] << 8)
-                                             : (uint32_t)srow[w.off];
-                        else {
-                            const uint8_t* p = w.p + (size_t)r * w.stride;
+                        if (staged) {
+                            bin = width == 2 ? (uint32_t)srow[w.loc] | ((uint32_t)srow[w.loc + 1] << 8)
+                                             : (uint32_t)srow[w.loc];
+                        } else {
+                            const FeatLoc fl = a.floc_rec[w.loc];
+                            const uint8_t* p = fl.base + (size_t)r * fl.stride + fl.byte_off;
                             bin = width == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(p) : (uint32_t)*p;
                         }
                     }
@@ -2021,6 +2150,19 @@ __global__ void __launch_bounds__(256) k_records_to_columns(const uint8_t* __res
 }
 
 // ------------------------------------------------------------------ launchers
+// CTAs of `threads` threads (static shared memory only) that the device's
+// SMs hold at once for `kernel` (a failed query gives one CTA per SM of a
+// B200: a smaller grid, never a wrong result; the launch reports the error).
+static uint32_t resident_grid(const void* kernel, uint32_t threads) {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, (int)threads, 0) != cudaSuccess || per_sm <= 0)
+        per_sm = 1;
+    return (uint32_t)(sms * per_sm);
+}
+
 static unsigned grad_grid(uint32_t n) {
     unsigned b = (n + 255) / 256;
     return b < 148u * 8u ? (b ? b : 1u) : 148u * 8u;
@@ -2175,9 +2317,18 @@ void launch_part_level(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) 
 void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s) {
     if (n_rows == 0) return;
     count_launch();
-    // one resident wave (shared memory allows 6 CTAs per SM)
-    const uint32_t blocks = std::min<uint32_t>((n_rows + kWalkThreads - 1) / kWalkThreads, 148u * 6u);
-    k_tree_walk<<<blocks, kWalkThreads, 0, s>>>(a, n_rows);
+    // one resident wave: every CTA takes the same number of steps, so a grid
+    // beyond what the SMs hold at once would run a second, nearly empty wave
+    static const uint32_t wave8 = resident_grid(reinterpret_cast<const void*>(k_tree_walk<8>), kWalkThreads);
+    static const uint32_t wave16 = resident_grid(reinterpret_cast<const void*>(k_tree_walk<16>), kWalkThreads);
+    const bool narrow = a.walk_rec == nullptr || a.walk_stride <= 32;
+    const uint32_t blocks = std::min<uint32_t>((n_rows + kWalkThreads - 1) / kWalkThreads, narrow ? wave8 : wave16);
+    if (narrow) k_tree_walk<8><<<blocks, kWalkThreads, 0, s>>>(a, n_rows);
+    else k_tree_walk<16><<<blocks, kWalkThreads, 0, s>>>(a, n_rows);
+}
+void launch_part_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
+    count_launch();
+    k_part_final<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
     count_launch();

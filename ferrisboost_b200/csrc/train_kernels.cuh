@@ -23,6 +23,7 @@ constexpr int kMaxBinsPerThread = 4;  // features up to 1024 bins per CTA scan
 constexpr uint32_t kChunkRows = 4096; // partition / leaf chunk
 constexpr int kPartThreads = 512;
 constexpr int kPartItems = kChunkRows / kPartThreads;
+constexpr uint32_t kWalkNodes = 512;  // k_tree_walk keeps trees of up to this many nodes in shared memory
 constexpr int kHistThreads = 512;
 constexpr int kHistLpfThreads = 1024;
 
@@ -219,6 +220,9 @@ void launch_part_scatter(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s
 // Depthwise: one-pass partition of every node of the level, then the next
 // level's tables (last CTA).  Needs a.fuse and a.part_cnt.
 void launch_part_level(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
+// Depthwise, last level: every row's final leaf value added to its margin
+// (no partition into the children, no k_leaf_final after it).
+void launch_part_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 // Every local row walks the finished tree (a.trec / a.tcats) on its record's
 // bins and adds its leaf's value to its margin (training/mod.rs:5020-5063,

@@ -311,26 +311,38 @@ def test_lossguide_fast_mode_within_tolerance(oracle):
     assert abs(logloss(a) - logloss(b)) < 1e-4
 
 
-def test_partition_leaf_path_byte_identical(oracle, tmp_path):
+@pytest.mark.parametrize("case", ["numeric", "categorical"])
+def test_partition_leaf_path_byte_identical(oracle, tmp_path, case):
     # the leaf values reach the margins through the partition chunks and the
-    # final-level pass (the path above 4M local rows) instead of the tree walk
+    # final-level pass (FBGPU_WALK=0) instead of the tree walk: the same
+    # models and bit-identical training margins; "numeric" trees take the
+    # walk's fast form, "categorical" ones its general form
     import os
     import subprocess
     import sys
     X, y = _synthetic(30000, 12, seed=77, missing=0.03)
+    ft = None
+    if case == "categorical":
+        X[:, 5] = np.random.default_rng(5).integers(0, 20, len(X))
+        ft = ["q"] * 12
+        ft[5] = "c"
     np.save(tmp_path / "X.npy", X)
     np.save(tmp_path / "y.npy", y)
     p = dict(objective="binary:logistic", max_depth=6, eta=0.3, max_bin=256)
     code = (
         "import sys, numpy as np, ferrisboost_b200 as fb\n"
         f"X = np.load({str(tmp_path / 'X.npy')!r}); y = np.load({str(tmp_path / 'y.npy')!r})\n"
-        f"m = fb.train({p!r}, X, label=y, num_boost_round=6)\n"
-        f"open({str(tmp_path / 'm.json')!r}, 'wb').write(m.to_json())\n"
-        f"np.save({str(tmp_path / 'margin.npy')!r}, m.predict(X, output_margin=True))\n")
+        f"b = fb.Booster({p!r}, fb.Dataset(X, max_bin=256, feature_types={ft!r}), y)\n"
+        "b.update(6)\n"
+        f"open({str(tmp_path / 'm.json')!r}, 'wb').write(b.model().to_json())\n"
+        f"np.save({str(tmp_path / 'margin.npy')!r}, b.margins())\n")
     env = dict(os.environ, FBGPU_WALK="0")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=root)
-    ref = oracle.train(X, y, n_rounds=6, **p)
+    cat = None if ft is None else np.array([c == "c" for c in ft], np.uint8)
+    ref = oracle.train(X, y, n_rounds=6, categorical=cat, **p)
     assert (tmp_path / "m.json").read_bytes() == ref.json()
-    walked = fb.train(p, X, label=y, num_boost_round=6)
-    assert walked.to_json() == ref.json()
+    walked = fb.Booster(p, fb.Dataset(X, max_bin=256, feature_types=ft), y)
+    walked.update(6)
+    assert walked.model().to_json() == ref.json()
+    assert np.array_equal(walked.margins().view(np.uint32), np.load(tmp_path / "margin.npy").view(np.uint32))
