@@ -279,6 +279,7 @@ struct ShapPaths {
     uint32_t mask_words = 8;          // words of a category mask (a bit per code)
     std::vector<uint32_t> words, chunk_off, masks;
     DevMem d_words, d_chunks, d_masks;
+    mutable DevMem d_acc;             // k_shap_paths: per-CTA f64 totals of phi
     void build(const std::vector<DevNode>& nodes, const uint32_t* tree_off, uint32_t n_trees, uint32_t F,
                const std::vector<uint32_t>& cat_off, const std::vector<uint32_t>& cat_len, const uint32_t* cat_words,
                const float* rule_nodes, const float* rule_weights);

@@ -25,10 +25,14 @@
 // c_{o_f} sum_i b_{o_f,i} P_i to phi_f: no division, no recursion, no
 // per-thread stack.
 //
-// Layout: one thread per row; the CTA's rows keep x and phi in shared memory
-// ([feature][thread], conflict-free), and the path elements stream through
-// shared memory in chunks of whole paths, read by every thread at the same
-// address (broadcast).
+// Layout: one thread per row; the CTA's rows keep x and an f32 partial of phi
+// in shared memory ([feature][thread], conflict-free), and the path elements
+// stream through shared memory in chunks of whole paths, read by every thread
+// at the same address (broadcast).  Every kFlushChunks chunks (about one
+// depth-8 tree's paths) each thread adds its rows' partials into f64 totals
+// in a per-CTA global scratch block ([feature][thread], coalesced, resident
+// in L2) and clears them: a partial sums at most one term per path, like the
+// reference's per-tree f32 sums, and the totals over trees stay f64.
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -42,7 +46,8 @@ namespace fbg {
 namespace {
 
 constexpr int kPathThreads = 128;
-constexpr uint32_t kChunkBytes = 24 * 1024;
+constexpr uint32_t kChunkBytes = 16 * 1024;
+constexpr uint32_t kFlushChunks = 8;
 
 // Element record, in 32-bit words: [0] feature | flags << 24, [1] lo (f32) or
 // category-mask index, [2] hi (f32), [3] elements in the path (first element
@@ -83,16 +88,16 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
                                                              const uint32_t* __restrict__ chunk_off,
                                                              uint32_t n_chunks, const uint32_t* __restrict__ cat_masks,
                                                              uint32_t mask_words, float bias, float root_mean,
-                                                             float* __restrict__ out) {
+                                                             double* __restrict__ acc, float* __restrict__ out) {
     constexpr uint32_t EW = elem_words<M>();
     constexpr uint32_t TR = kPathThreads * R;  // rows per CTA tile
     extern __shared__ __align__(16) uint32_t smem[];
-    // phi accumulates in f64: a value receives one term per path that tests
-    // its feature (tens of thousands per row), where the reference adds one
-    // per-tree sum per tree; f32 accumulation would drift past the 1e-5 bar
-    double* ph = reinterpret_cast<double*>(smem);                       // [F][TR]
-    float* xs = reinterpret_cast<float*>(ph + (size_t)F * TR);          // [F][TR]
+    // a value receives one term per path that tests its feature (tens of
+    // thousands per row): f32 partials over kFlushChunks chunks, f64 totals
+    float* ph = reinterpret_cast<float*>(smem);                         // [F][TR]
+    float* xs = ph + (size_t)F * TR;                                    // [F][TR]
     uint32_t* ch = reinterpret_cast<uint32_t*>(xs + (size_t)F * TR);    // chunk of elements
+    double* tot = acc + (size_t)blockIdx.x * F * TR;                    // [F][TR] f64 totals
     const uint32_t t = threadIdx.x;
     for (uint64_t r0 = (uint64_t)blockIdx.x * TR; r0 < n; r0 += (uint64_t)gridDim.x * TR) {
         const uint32_t rows = (uint32_t)min((uint64_t)TR, n - r0);
@@ -101,8 +106,24 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
             const uint32_t rr = i / F, f = i - rr * F;
             xs[f * TR + rr] = X[r0 * F + i];
         }
-        for (uint32_t i = t; i < F * TR; i += kPathThreads) ph[i] = 0.0;
+        for (uint32_t i = t; i < F * TR; i += kPathThreads) ph[i] = 0.0f;
+        bool flushed = false;  // uniform: the flushes follow the chunk count
         for (uint32_t c = 0; c < n_chunks; c++) {
+            if (c > 0 && c % kFlushChunks == 0) {
+                // each thread moves its own rows' partials (no other thread touches them)
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const uint32_t rr = t + r * kPathThreads;
+                    if (rr < rows)
+                        for (uint32_t f = 0; f < F; f++) {
+                            float* p = ph + f * TR + rr;
+                            double* q = tot + f * TR + rr;
+                            *q = flushed ? __dadd_rn(*q, (double)*p) : (double)*p;
+                            *p = 0.0f;
+                        }
+                }
+                flushed = true;
+            }
             const uint32_t e0 = chunk_off[c], e1 = chunk_off[c + 1];
             __syncthreads();
             const uint4* src = elems + (size_t)e0 * (EW / 4);
@@ -154,8 +175,8 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
                             float sacc = 0.0f;
 #pragma unroll
                             for (int i = 0; i < M; i++) sacc = __fmaf_rn(o ? b1[i] : b0[i], P[r][i], sacc);
-                            double* p = ph + feats[j] * TR + t + r * kPathThreads;
-                            *p = __dadd_rn(*p, (double)__fmul_rn(o ? cc.y : cc.x, sacc));
+                            float* p = ph + feats[j] * TR + t + r * kPathThreads;
+                            *p = __fadd_rn(*p, __fmul_rn(o ? cc.y : cc.x, sacc));
                         }
                     }
                 }
@@ -168,7 +189,10 @@ __global__ void __launch_bounds__(kPathThreads) k_shap_paths(const float* __rest
             const uint32_t rr = t + r * kPathThreads;
             if (rr < rows) {
                 float* o = out + (r0 + rr) * (uint64_t)(F + 1);
-                for (uint32_t f = 0; f < F; f++) o[f] = __double2float_rn(ph[f * TR + rr]);
+                for (uint32_t f = 0; f < F; f++) {
+                    const double v = (double)ph[f * TR + rr];
+                    o[f] = __double2float_rn(flushed ? __dadd_rn(tot[f * TR + rr], v) : v);
+                }
                 o[F] = __fadd_rn(__fadd_rn(0.0f, root_mean), bias);  // explain.rs:725-726
             }
         }
@@ -702,7 +726,7 @@ void ShapPaths::launch_inter(const float* X, uint64_t n, uint32_t F, float bias,
 // two rows per thread: the path data read from shared memory serves two product chains
 constexpr int kPathRows = 2;
 
-size_t ShapPaths::smem_bytes(uint32_t F) { return (size_t)F * kPathThreads * kPathRows * (8 + 4) + kChunkBytes; }
+size_t ShapPaths::smem_bytes(uint32_t F) { return (size_t)F * kPathThreads * kPathRows * (4 + 4) + kChunkBytes; }
 
 void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float root_mean, float* out,
                        cudaStream_t s) const {
@@ -720,10 +744,12 @@ void ShapPaths::launch(const float* X, uint64_t n, uint32_t F, float bias, float
         int per_sm = 1;                                                                                              \
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_shap_paths<MM, KK, RR>, kPathThreads, smem);        \
         const uint64_t grid = std::min<uint64_t>(tiles, (uint64_t)sms * std::max(per_sm, 1));                        \
+        const size_t acc_bytes = grid * F * (size_t)kPathThreads * RR * 8;                                           \
+        if (d_acc.bytes < acc_bytes) d_acc.alloc(acc_bytes);                                                         \
         count_launch();                                                                                              \
         k_shap_paths<MM, KK, RR><<<(unsigned)grid, kPathThreads, smem, s>>>(                                        \
             X, n, F, d_words.as<uint4>(), d_chunks.as<uint32_t>(), n_chunks, d_masks.as<uint32_t>(), mask_words,    \
-            bias, root_mean, out);                                                                                   \
+            bias, root_mean, d_acc.as<double>(), out);                                                               \
     } while (0)
     if (M == 4) FB_SP(4, 8, kPathRows);
     else FB_SP(8, 14, kPathRows);

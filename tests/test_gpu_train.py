@@ -339,8 +339,8 @@ def test_partition_leaf_path_byte_identical(oracle, tmp_path, case):
     env = dict(os.environ, FBGPU_WALK="0")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     subprocess.run([sys.executable, "-c", code], check=True, env=env, cwd=root)
-    cat = None if ft is None else np.array([c == "c" for c in ft], np.uint8)
-    ref = oracle.train(X, y, n_rounds=6, categorical=cat, **p)
+    cat = {} if ft is None else {"categorical": np.array([c == "c" for c in ft], np.uint8)}
+    ref = oracle.train(X, y, n_rounds=6, **cat, **p)
     assert (tmp_path / "m.json").read_bytes() == ref.json()
     walked = fb.Booster(p, fb.Dataset(X, max_bin=256, feature_types=ft), y)
     walked.update(6)
