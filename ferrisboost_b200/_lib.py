@@ -141,6 +141,8 @@ SIGNATURES = {
     "fbgpu_comm_begin": (C.c_int, [u8p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32, C.POINTER(P)]),
     "fbgpu_comm_free": (None, [P]),
     "fbgpu_comm_usable": (C.c_int32, [P]),
+    "fbgpu_quantizer_scales": (C.c_int, [C.c_int32, f32p, C.c_uint64, C.c_uint64, C.POINTER(C.c_double)]),
+    "fbgpu_quantizer_scale_digest": (C.c_uint64, [C.c_uint32, C.c_uint32, C.c_uint64]),
     "fbgpu_comm_abort": (None, [P]),
     "fbgpu_ctx_adopt_comm": (C.c_int, [P, P]),
     "fb_booster_free": (None, [P]),

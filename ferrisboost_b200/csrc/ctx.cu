@@ -133,6 +133,36 @@ double pow2_scale_host(double max_abs, uint64_t n_rows) {
     return std::ldexp(1.0, k);
 }
 
+std::vector<fbx::ScaleExc> build_scale_exceptions(uint64_t n_rows) {
+    // max_abs = budget / 2^k makes raw exactly 2^k; the f32 values around it
+    // are the only ones whose raw can sit just below a power of two
+    const double budget = fbx::scale_budget(n_rows);
+    const int e = std::ilogb(budget);
+    std::vector<fbx::ScaleExc> out;
+    for (int k = e - 131; k <= e + 151; k++) {
+        const float c = (float)std::ldexp(budget, -k);
+        if (!std::isfinite(c)) continue;
+        float lo = c;
+        for (int i = 0; i < 3 && lo > 0.0f; i++) lo = std::nextafter(lo, 0.0f);
+        if (!(lo > 0.0f)) lo = std::nextafter(0.0f, 1.0f);
+        float f = lo;
+        for (int i = 0; i < 7 && std::isfinite(f); i++, f = std::nextafter(f, INFINITY)) {
+            const double m = (double)f;
+            const double host = pow2_scale_host(m, n_rows);
+            if (host != fbx::scale_of_exp(fbx::scale_exp_ilogb(m, n_rows))) {
+                uint64_t bits;
+                std::memcpy(&bits, &m, 8);
+                out.push_back({bits, std::ilogb(host), 0});
+            }
+        }
+    }
+    std::sort(out.begin(), out.end(), [](const fbx::ScaleExc& a, const fbx::ScaleExc& b) { return a.bits < b.bits; });
+    out.erase(std::unique(out.begin(), out.end(),
+                          [](const fbx::ScaleExc& a, const fbx::ScaleExc& b) { return a.bits == b.bits; }),
+              out.end());
+    return out;
+}
+
 // ======================================================================= TrainCtx
 void TrainCtx::set_comm(const uint8_t* unique_id, int nranks, int rank, uint32_t timeout_ms) {
     if (!unique_id) throw InputError("unique_id is null");
@@ -202,11 +232,16 @@ TrainCtx::TrainCtx(const fbgpu_config& cfg) : cfg_(cfg) {
     if (cfg.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     FB_CUDA_CHECK(cudaSetDevice(cfg.device));
     FB_CUDA_CHECK(cudaStreamCreateWithFlags(&s_, cudaStreamNonBlocking));
-    h_small_.reserve(512);
+    h_small_.reserve(1024);  // words 0..9 round values, 32..63 level stats, 80 the scale error word
     FB_CUDA_CHECK(cudaEventCreate(&ev0_));
     FB_CUDA_CHECK(cudaEventCreate(&ev1_));
-    for (auto& e : hev_) FB_CUDA_CHECK(cudaEventCreate(&e));
-    for (auto& e : hevc_) FB_CUDA_CHECK(cudaEventCreate(&e));
+    for (ReadSlot& sl : slot_) {
+        FB_CUDA_CHECK(cudaEventCreate(&sl.ev0));
+        FB_CUDA_CHECK(cudaEventCreate(&sl.ev1));
+        FB_CUDA_CHECK(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+        for (auto& e : sl.hev) FB_CUDA_CHECK(cudaEventCreate(&e));
+        for (auto& e : sl.hevc) FB_CUDA_CHECK(cudaEventCreate(&e));
+    }
     level_stats_.alloc(16 * 16);
     n_ = cfg.n_rows;
     F_ = cfg.n_features;
@@ -246,8 +281,11 @@ TrainCtx::~TrainCtx() {
     if (s_) cudaStreamSynchronize(s_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
-    for (auto& e : hev_) if (e) cudaEventDestroy(e);
-    for (auto& e : hevc_) if (e) cudaEventDestroy(e);
+    for (ReadSlot& sl : slot_) {
+        for (cudaEvent_t e : {sl.ev0, sl.ev1, sl.done}) if (e) cudaEventDestroy(e);
+        for (auto& e : sl.hev) if (e) cudaEventDestroy(e);
+        for (auto& e : sl.hevc) if (e) cudaEventDestroy(e);
+    }
     if (s_) cudaStreamDestroy(s_);
 }
 
@@ -479,6 +517,34 @@ void TrainCtx::round_from_exp(int objective, const float* host_exp, uint64_t th,
     reduce_root_sum(false);
 }
 
+void TrainCtx::launch_scales(const unsigned long long* maxbits, bool fast) {
+    double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
+    unsigned long long* err = sums_.as<unsigned long long>() + 6;
+    if (fast) {
+        launch_device_scales(maxbits, cfg_.n_rows_global, dscales, err, s_);
+    } else {
+        if (scale_exc_rows_ != cfg_.n_rows_global) {
+            const std::vector<fbx::ScaleExc> exc = build_scale_exceptions(cfg_.n_rows_global);
+            d_scale_exc_.alloc(sizeof(fbx::ScaleExc) * std::max<size_t>(exc.size(), 1));
+            if (!exc.empty())
+                FB_CUDA_CHECK(cudaMemcpyAsync(d_scale_exc_.p, exc.data(), sizeof(fbx::ScaleExc) * exc.size(),
+                                              cudaMemcpyHostToDevice, s_));
+            n_scale_exc_ = (uint32_t)exc.size();
+            scale_exc_rows_ = cfg_.n_rows_global;
+            sync();  // the host vector goes out of scope
+        }
+        launch_device_scales_exact(maxbits, cfg_.n_rows_global, d_scale_exc_.as<fbx::ScaleExc>(), n_scale_exc_,
+                                   dscales, err, s_);
+    }
+    scale_err_pending_ = true;
+}
+
+void TrainCtx::check_scale_error(const unsigned long long* host_err) {
+    if (!scale_err_pending_) return;
+    scale_err_pending_ = false;
+    if (*host_err) throw InputError("non-finite gradient or Hessian");
+}
+
 void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
                             int64_t* sum_out) {
     FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 32, s_));
@@ -490,32 +556,22 @@ void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed,
                          "use fbgpu_round_from_exp with host exp values");
     launch_gradient_max(a, fast ? 1 : (objective == 1 ? 2 : 0), s_);
     allreduce_u64(a.maxbits, 2, true);
-    double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
-    if (fast) {
-        launch_device_scales(a.maxbits, cfg_.n_rows_global, dscales, s_);
-    } else {
-        unsigned long long* mb = h_small_.as<unsigned long long>();
-        FB_CUDA_CHECK(cudaMemcpyAsync(mb, a.maxbits, 16, cudaMemcpyDeviceToHost, s_));
-        sync();
-        double mg, mh;
-        std::memcpy(&mg, &mb[0], 8);
-        std::memcpy(&mh, &mb[1], 8);
-        if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
-        double* sc = h_small_.as<double>() + 2;
-        sc[0] = pow2_scale_host(mg, cfg_.n_rows_global);
-        sc[1] = pow2_scale_host(mh, cfg_.n_rows_global);
-        FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
-    }
+    launch_scales(a.maxbits, fast != 0);
     launch_quantize(a, s_);
     reduce_root_sum(sum_out != nullptr);
-    if (scales_out || sum_out) {
-        unsigned long long* hs = h_small_.as<unsigned long long>() + 4;
-        FB_CUDA_CHECK(cudaMemcpyAsync(hs, dscales, 16, cudaMemcpyDeviceToHost, s_));
-        FB_CUDA_CHECK(cudaMemcpyAsync(hs + 2, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
-        sync();
-        if (scales_out) std::memcpy(scales_out, hs, 16);
-        if (sum_out) std::memcpy(sum_out, hs + 2, 16);
-    }
+    read_scales_sum(scales_out, sum_out);
+}
+
+// Scales and root sum of the round to the host (when asked for: a sync).
+void TrainCtx::read_scales_sum(double* scales_out, int64_t* sum_out) {
+    if (!scales_out && !sum_out) return;
+    unsigned long long* hs = h_small_.as<unsigned long long>() + 4;
+    FB_CUDA_CHECK(cudaMemcpyAsync(hs, sums_.as<unsigned long long>() + 4, 24, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaMemcpyAsync(hs + 3, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
+    sync();
+    check_scale_error(hs + 2);
+    if (scales_out) std::memcpy(scales_out, hs, 16);
+    if (sum_out) std::memcpy(sum_out, hs + 3, 16);
 }
 
 void TrainCtx::set_outputs(uint32_t K, const float* class_margins) {
@@ -547,32 +603,10 @@ void TrainCtx::quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t t
     a.gpair_in = gp_multi_.as<float>() + 2ull * k * n_;
     launch_mask_max(a, s_);  // mod.rs:4811-4842 mask_and_bounds
     allreduce_u64(a.maxbits, 2, true);
-    double* dscales = reinterpret_cast<double*>(sums_.as<unsigned long long>() + 4);
-    if (fast) {
-        launch_device_scales(a.maxbits, cfg_.n_rows_global, dscales, s_);
-    } else {
-        unsigned long long* mb = h_small_.as<unsigned long long>();
-        FB_CUDA_CHECK(cudaMemcpyAsync(mb, a.maxbits, 16, cudaMemcpyDeviceToHost, s_));
-        sync();
-        double mg, mh;
-        std::memcpy(&mg, &mb[0], 8);
-        std::memcpy(&mh, &mb[1], 8);
-        if (!std::isfinite(mg) || !std::isfinite(mh)) throw InputError("non-finite gradient or Hessian");
-        double* sc = h_small_.as<double>() + 2;
-        sc[0] = pow2_scale_host(mg, cfg_.n_rows_global);
-        sc[1] = pow2_scale_host(mh, cfg_.n_rows_global);
-        FB_CUDA_CHECK(cudaMemcpyAsync(dscales, sc, 16, cudaMemcpyHostToDevice, s_));
-    }
+    launch_scales(a.maxbits, fast != 0);
     launch_quantize(a, s_);
     reduce_root_sum(sum_out != nullptr);
-    if (scales_out || sum_out) {
-        unsigned long long* hs = h_small_.as<unsigned long long>() + 4;
-        FB_CUDA_CHECK(cudaMemcpyAsync(hs, dscales, 16, cudaMemcpyDeviceToHost, s_));
-        FB_CUDA_CHECK(cudaMemcpyAsync(hs + 2, sums_.p, 16, cudaMemcpyDeviceToHost, s_));
-        sync();
-        if (scales_out) std::memcpy(scales_out, hs, 16);
-        if (sum_out) std::memcpy(sum_out, hs + 2, 16);
-    }
+    read_scales_sum(scales_out, sum_out);
 }
 
 void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide) {
@@ -627,7 +661,6 @@ void TrainCtx::ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool
     trec_.alloc(sizeof(TreeRec) * tree_nodes);
     tcats_.alloc(set_bytes * tree_nodes);
     state_.alloc(sizeof(TreeState));
-    h_tree_.reserve(sizeof(TreeRec) * tree_nodes + set_bytes * tree_nodes + sizeof(TreeState));
     buf_depth_ = max_depth;
     buf_leaves_ = max_leaves;
     buf_lossguide_ = lossguide;
@@ -956,7 +989,31 @@ void lossguide_order(const TreeRec* rec, uint32_t nn, std::vector<uint32_t>& old
     if (next != nn) throw std::runtime_error("device tree is malformed");
 }
 
+bool TrainCtx::tree_async(const fbgpu_tree_params& tp) const {
+    return tp.grow_policy == 0 || lossguide_is_levelwise(tp);
+}
+
+void TrainCtx::wait_event(cudaEvent_t ev) {
+    if (comm_) comm_->wait_event(ev);
+    else FB_CUDA_CHECK(cudaEventSynchronize(ev));
+}
+
 void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out) {
+    if (!tree_async(tp)) {
+        build_tree_launch(tp, enabled, out);  // best-first: grown and read back here
+        return;
+    }
+    if (slots_pending_) throw InputError("collect the launched trees before building one synchronously");
+    build_tree_launch(tp, enabled, nullptr);
+    build_tree_collect(out);
+}
+
+void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* enabled) {
+    if (!tree_async(tp)) throw InputError("this tree needs the host while it grows (best-first lossguide)");
+    build_tree_launch(tp, enabled, nullptr);
+}
+
+void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* lg_out) {
     ensure_features();
     if (tp.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     const bool lossguide = tp.grow_policy != 0;
@@ -994,10 +1051,13 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
         }
     }
     if (best_first) {
+        if (slots_pending_) throw InputError("collect the launched trees before growing a best-first tree");
         ensure_lossguide_buffers(tp.max_leaves);
-        build_tree_lossguide(tp, enabled, out);
+        build_tree_lossguide(tp, enabled, lg_out);
         return;
     }
+    if (slots_pending_ == 2) throw InputError("two trees are in flight: collect one before launching another");
+    ReadSlot& S = slot_[slot_next_];
     LevelArgs a = level_args(tp);
     // the one-CTA level steps ride in the last CTA of the kernel before them
     if (!fuse_.p) {
@@ -1029,7 +1089,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     const bool walk_fast = a.walk_rec != nullptr && max_nodes <= kWalkNodes;
     a.walk = walk_env >= 0 ? (walk_env ? 1u : 0u) : ((n_ <= (4ull << 20) || walk_fast) ? 1u : 0u);
     const uint32_t maxd = tp.max_depth;
-    FB_CUDA_CHECK(cudaEventRecord(ev0_, s_));
+    FB_CUDA_CHECK(cudaEventRecord(S.ev0, s_));
     int cur = 0;
     launch_iota(rows_[0].as<uint32_t>(), (uint32_t)n_, s_);
     a.nodes = nodes_[0].as<NodeInfo>();
@@ -1075,7 +1135,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
                           "TreeState layout");
             FB_CUDA_CHECK(cudaMemcpyAsync(level_stats_.as<uint8_t>() + 16 * d,
                                           reinterpret_cast<uint8_t*>(state_.p) + 8, 16, cudaMemcpyDeviceToDevice, s_));
-            FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d], s_));
+            FB_CUDA_CHECK(cudaEventRecord(S.hev[2 * d], s_));
         }
         const bool root_rides = d == 0 && root_pending_;
         if (root_rides)
@@ -1089,11 +1149,11 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             FB_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(state_.p) + offsetof(TreeState, rank_stride), hs,
                                           8, cudaMemcpyHostToDevice, s_));
             launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_, hist_acc_.as<Pair>(), chunk_pairs_);
-            if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hevc_[d], s_));
+            if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(S.hevc[d], s_));
             comm_->reduce_scatter_u64(hist_acc_.p, hist_rs_.p, 2 * block, s_);
         } else {
             launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
-            if (stats_ && comm_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hevc_[d], s_));
+            if (stats_ && comm_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(S.hevc[d], s_));
             allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc + (root_rides ? 2 : 0), false);
         }
         if (root_rides) {
@@ -1103,7 +1163,7 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
             launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
             root_pending_ = false;
         }
-        if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(hev_[2 * d + 1], s_));
+        if (stats_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(S.hev[2 * d + 1], s_));
         const uint32_t max_chunks = ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + max_m;
         if (rs_mode) {
             // this rank's best split per node over its features, every rank's
@@ -1130,41 +1190,73 @@ void TrainCtx::build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, f
     else if (maxd == 0)  // the root is the only leaf
         launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
     FB_CUDA_CHECK(cudaGetLastError());
-    FB_CUDA_CHECK(cudaEventRecord(ev1_, s_));
+    FB_CUDA_CHECK(cudaEventRecord(S.ev1, s_));
+    // the result into this slot's pinned buffers, in stream order (the next
+    // tree's kernels overwrite the device copies only after these)
     const uint32_t W = cat_words_;
-    TreeRec* hrec = h_tree_.as<TreeRec>();
+    S.tree.reserve(sizeof(TreeRec) * max_tree_nodes_ + 4ull * W * max_tree_nodes_ + sizeof(TreeState));
+    S.small.reserve(16 * 16 + 8);
+    TreeRec* hrec = S.tree.as<TreeRec>();
     uint32_t* hcats = reinterpret_cast<uint32_t*>(hrec + max_tree_nodes_);
     TreeState* hst = reinterpret_cast<TreeState*>(hcats + (size_t)W * max_tree_nodes_);
     FB_CUDA_CHECK(cudaMemcpyAsync(hst, state_.p, sizeof(TreeState), cudaMemcpyDeviceToHost, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(hrec, trec_.p, sizeof(TreeRec) * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
     if (has_cat_)
         FB_CUDA_CHECK(cudaMemcpyAsync(hcats, tcats_.p, 4ull * W * max_tree_nodes_, cudaMemcpyDeviceToHost, s_));
-    uint64_t* lvl = h_small_.as<uint64_t>() + 32;  // 16 levels x 16 bytes
+    uint64_t* lvl = S.small.as<uint64_t>();  // 16 levels x 16 bytes
     if (stats_) FB_CUDA_CHECK(cudaMemcpyAsync(lvl, level_stats_.p, 16 * 16, cudaMemcpyDeviceToHost, s_));
-    sync();
-    FB_CUDA_CHECK(cudaEventElapsedTime(&last_tree_ms_, ev0_, ev1_));
+    S.scale_err = scale_err_pending_;
+    scale_err_pending_ = false;
+    if (S.scale_err)
+        FB_CUDA_CHECK(cudaMemcpyAsync(lvl + 32, sums_.as<unsigned long long>() + 6, 8, cudaMemcpyDeviceToHost, s_));
+    FB_CUDA_CHECK(cudaEventRecord(S.done, s_));
+    S.lossguide = lossguide;
+    S.max_nodes = max_tree_nodes_;
+    S.stats = stats_;
+    S.maxd = maxd;
+    S.W = W;
     if (stats_) {
-        uint64_t row_bytes = 0, bins = 0, feats = 0;  // enabled features of this tree
+        S.row_bytes = S.bins = S.feats = 0;  // enabled features of this tree
         for (uint32_t f = 0; f < F_; f++)
-            if (last_enabled_[f]) { row_bytes += width_[f]; bins += nbins_[f]; feats++; }
-        for (uint32_t d = 0; d < std::min<uint32_t>(maxd, 15); d++) {
+            if (last_enabled_[f]) { S.row_bytes += width_[f]; S.bins += nbins_[f]; S.feats += 1; }
+        S.launches_per_level = (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) +
+                               (n_wide_ ? 1 : 0) + (n_direct_[0] ? 1 : 0) + (n_direct_[1] ? 1 : 0);
+    }
+    slot_next_ = 1 - slot_next_;
+    slots_pending_++;
+}
+
+void TrainCtx::build_tree_collect(fbgpu_tree_out* out) {
+    if (slots_pending_ == 0) throw InputError("no launched tree to collect");
+    ReadSlot& S = slot_[(slot_next_ + 2 - slots_pending_) % 2];
+    slots_pending_--;
+    wait_event(S.done);
+    const uint32_t W = S.W;
+    const TreeRec* hrec = S.tree.as<TreeRec>();
+    const uint32_t* hcats = reinterpret_cast<const uint32_t*>(hrec + S.max_nodes);
+    const TreeState* hst = reinterpret_cast<const TreeState*>(hcats + (size_t)W * S.max_nodes);
+    const uint64_t* lvl = S.small.as<uint64_t>();
+    FB_CUDA_CHECK(cudaEventElapsedTime(&last_tree_ms_, S.ev0, S.ev1));
+    if (S.scale_err && lvl[32]) throw InputError("non-finite gradient or Hessian");
+    if (S.stats) {
+        for (uint32_t d = 0; d < std::min<uint32_t>(S.maxd, 15); d++) {
             float ms = 0.0f;
-            FB_CUDA_CHECK(cudaEventElapsedTime(&ms, hev_[2 * d], hev_[2 * d + 1]));
+            FB_CUDA_CHECK(cudaEventElapsedTime(&ms, S.hev[2 * d], S.hev[2 * d + 1]));
             if (comm_) {
                 float cms = 0.0f;
-                FB_CUDA_CHECK(cudaEventElapsedTime(&cms, hevc_[d], hev_[2 * d + 1]));
+                FB_CUDA_CHECK(cudaEventElapsedTime(&cms, S.hevc[d], S.hev[2 * d + 1]));
                 comm_ms_ += cms;
             }
             const uint64_t acc_nodes = lvl[2 * d] >> 32, rows = lvl[2 * d + 1];
             hist_ms_ += ms;
-            hist_launches_ += (n_gen_[0] ? 1 : 0) + (n_gen_[1] ? 1 : 0) + (n_lpf_[0] ? 1 : 0) + (n_lpf_[1] ? 1 : 0) +
-                              (n_wide_ ? 1 : 0) + (n_direct_[0] ? 1 : 0) + (n_direct_[1] ? 1 : 0);
-            hist_bytes_ += (double)rows * (double)(row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * bins * 16.0;
-            hist_updates_ += (double)rows * (double)feats;
+            hist_launches_ += S.launches_per_level;
+            hist_bytes_ += (double)rows * (S.row_bytes + 16 + (d ? 4 : 0)) + (double)acc_nodes * S.bins * 16.0;
+            hist_updates_ += (double)rows * S.feats;
         }
     }
+    const bool lossguide = S.lossguide;
     const uint32_t nn = hst->n_tree_nodes;
-    if (nn == 0 || nn > max_tree_nodes_) throw std::runtime_error("device tree has an invalid node count");
+    if (nn == 0 || nn > S.max_nodes) throw std::runtime_error("device tree has an invalid node count");
     if (!out) return;
     if (out->capacity < nn) throw InputError("fbgpu_tree_out capacity is smaller than the tree");
     const uint32_t out_w = out->cat_words ? out->cat_words : 8u;

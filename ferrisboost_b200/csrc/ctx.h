@@ -99,6 +99,23 @@ class TrainCtx {
                       int64_t* sum_out);
 
     void build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
+    // A tree in two halves, for trees that need no host decision while they
+    // grow (depthwise, and lossguide whose cap cannot bind): launch enqueues
+    // the tree and the copy of its result into a pinned slot and returns;
+    // collect waits for the oldest launched tree and fills `out`.  Two slots:
+    // a caller can launch the next round's gradients and tree before it
+    // collects this one, so the host's work between rounds overlaps the
+    // device's.  build_tree() is launch + collect.
+    bool tree_async(const fbgpu_tree_params& tp) const;
+    void build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* enabled);
+    void build_tree_collect(fbgpu_tree_out* out);
+    uint32_t trees_in_flight() const { return slots_pending_; }
+    // Waits for the stream and drops the launched trees (after an error).
+    void abandon_trees() {
+        slots_pending_ = 0;
+        scale_err_pending_ = false;
+        sync();
+    }
 
     // Multiclass (multi:softprob / multi:softmax, training/mod.rs:2564-2800):
     // K margin columns, class-major, each starting at its class's base margin.
@@ -184,6 +201,8 @@ class TrainCtx {
     void ensure_tree_buffers(uint32_t max_depth, uint32_t max_leaves, bool lossguide = false);
     void ensure_lossguide_buffers(uint32_t max_leaves);
     void build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
+    // the launch half; a best-first tree is grown and read back into lg_out here
+    void build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* lg_out);
     LevelArgs level_args(const fbgpu_tree_params& tp) const;
     GradArgs grad_args() const;
 
@@ -223,7 +242,15 @@ class TrainCtx {
     DevMem label_, weight_, pred_, gpair_f32_, host_exp_, fixed_;
     uint32_t K_ = 1, pred_col_ = 0;  // margin columns (classes) and the one the tree updates
     DevMem gp_multi_;                 // multiclass: K x n f32 gradient pairs of the round
-    DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double)
+    DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double), [6] scale error word
+    // exact scales on the device: the row count's exception list (qscale.h)
+    DevMem d_scale_exc_;
+    uint32_t n_scale_exc_ = 0;
+    uint64_t scale_exc_rows_ = ~0ull;
+    bool scale_err_pending_ = false;  // a device scale kernel ran; its error word is checked at the next readback
+    void launch_scales(const unsigned long long* maxbits, bool fast);
+    void check_scale_error(const unsigned long long* host_err);
+    void read_scales_sum(double* scales_out, int64_t* sum_out);
     DevMem exptab_;  // host-expf exception table (fexp.h), empty when unverified
     std::shared_ptr<NcclComm> comm_;
     int nranks_ = 1, rank_ = 0;
@@ -257,12 +284,22 @@ class TrainCtx {
     DevMem rows_[2], nodes_[2], acc_list_[2], acc_prefix_[2], chunk_prefix_[2];
     DevMem dirflags_, hist_acc_, hist_[2], feat_best_, feat_cats_, node_best_, node_cats_, split_, chunk_left_, chunk_off_,
         node_left_, trec_, tcats_, state_;
-    PinnedMem h_tree_;
+    // readback slots of launched depthwise trees (build_tree_launch / _collect)
+    struct ReadSlot {
+        PinnedMem tree;   // TreeRec[max_tree_nodes_] | category sets | TreeState
+        PinnedMem small;  // 16 levels x 16 B of level statistics, then the scale error word
+        cudaEvent_t ev0 = nullptr, ev1 = nullptr, done = nullptr;  // tree start, tree end, readback copied
+        cudaEvent_t hev[32] = {}, hevc[16] = {};
+        bool lossguide = false, stats = false, scale_err = false;
+        uint32_t maxd = 0, W = 8, max_nodes = 0;
+        double launches_per_level = 0, row_bytes = 0, bins = 0, feats = 0;  // statistics of the launch's plan
+    };
+    ReadSlot slot_[2];
+    uint32_t slot_next_ = 0, slots_pending_ = 0;  // the oldest pending slot is (slot_next_ + 2 - pending) % 2
+    void wait_event(cudaEvent_t ev);
     PinnedMem h_small_;  // 512 B of pinned readback: no pageable copy waits behind a collective
     float last_tree_ms_ = 0.0f;
     bool stats_ = false;
-    cudaEvent_t hev_[32] = {};
-    cudaEvent_t hevc_[16] = {};  // per level: histogram kernels done, all-reduce starts
     DevMem level_stats_;
     DevMem fuse_;  // last-CTA counters of the fused level kernels (depthwise)
     DevMem part_cnt_;  // k_part_level reservation counters, zero between levels
@@ -362,6 +399,9 @@ void make_shap_rule(float* nodes, float* weights);
 
 // types.rs:366-385 pow2_scale with the host libm (exact mode).
 double pow2_scale_host(double max_abs, uint64_t n_rows);
+// The f32 bounds whose reference scale is not 2^(binary exponent of raw) for
+// n_rows rows, sorted (qscale.h).
+std::vector<fbx::ScaleExc> build_scale_exceptions(uint64_t n_rows);
 
 }  // namespace fbg
 

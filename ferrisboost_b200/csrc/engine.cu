@@ -828,6 +828,7 @@ struct Booster {
     Model model;
     uint32_t rounds_done = 0;
     fbg::PinnedMem h_margin, h_exp;
+    std::string failed;  // set when a pipelined update failed after the next round was launched
     double t_wall = 0, t_grad = 0, t_tree = 0, t_dev = 0;
     std::vector<int32_t> o_left, o_right;
     std::vector<uint32_t> o_feat, o_bin, o_flags, o_cats;
@@ -1096,6 +1097,58 @@ void booster_round(Booster& b) {
     b.rounds_done++;
     b.t_grad += std::chrono::duration<double, std::milli>(t1 - t0).count();
     b.t_tree += std::chrono::duration<double, std::milli>(t2 - t1).count();
+}
+
+// Pipelined rounds: round r+1's gradients and tree are enqueued before tree
+// r is read back, so the host's work between rounds (waiting for and reading
+// tree r, assembling it, sampling the next round's features, launching) runs
+// while the device computes.  It applies when a round needs no host value
+// while it runs: gradients and scales on the device (fast mode, squared
+// error, or exact logistic with the device expf table), one output, and
+// trees that grow without the host (TrainCtx::tree_async).  The model is the
+// same: each round reads the margins the previous round's tree left, in
+// stream order, and takes its own round index for sampling.
+bool pipelinable(const Booster& b) {
+    const fb_params& p = b.p;
+    if (p.objective >= 2) return false;
+    if (!(p.gpu_math == 1 || p.objective == 0 || b.ctx->has_exact_exp())) return false;
+    return b.ctx->tree_async(tree_params(b));
+}
+
+void launch_round(Booster& b, uint32_t round) {
+    const fb_params& p = b.p;
+    fbg::TrainCtx& ctx = *b.ctx;
+    ctx.round_device(p.objective, p.gpu_math == 1 ? 1 : 0, threshold_for(p.subsample), p.seed, round, nullptr,
+                     nullptr);
+    std::vector<uint8_t> en = sample_features(b.d->F, p.colsample_bytree, p.seed, round);
+    ctx.build_tree_launch(tree_params(b), p.colsample_bytree < 1.0f ? en.data() : nullptr);
+}
+
+void collect_round(Booster& b) {
+    fbgpu_tree_out out = tree_out(b);
+    b.ctx->build_tree_collect(&out);
+    b.model.trees.push_back(assemble_tree(b, out));
+    b.rounds_done++;
+}
+
+void update_pipelined(Booster& b, uint32_t n_rounds) {
+    fbg::TrainCtx& ctx = *b.ctx;
+    try {
+        for (uint32_t r = 0; r < n_rounds; r++) {
+            launch_round(b, b.rounds_done + ctx.trees_in_flight());
+            if (ctx.trees_in_flight() == 2) collect_round(b);
+        }
+        while (ctx.trees_in_flight()) collect_round(b);
+    } catch (const std::exception& e) {
+        // a round after the failing one may have run: the margins no longer
+        // match the model, so the booster takes no further rounds
+        b.failed = e.what();
+        try {
+            ctx.abandon_trees();
+        } catch (...) {
+        }
+        throw;
+    }
 }
 
 fbgpu_tree_params tree_params(const Booster& b) {
@@ -1400,6 +1453,8 @@ void fb_booster_free(fb_booster* b) { delete b; }
 int32_t fb_booster_update(fb_booster* h, uint32_t n_rounds) {
     fbe::Booster* b = h->b.get();
     return fbe::guarded([&]() -> int32_t {
+        if (!b->failed.empty())
+            throw fbe::InputError("the booster stopped after an error in an earlier update: " + b->failed);
         b->t_grad = b->t_tree = 0.0;
         b->ctx->reset_stats();
         cudaEvent_t e0, e1;
@@ -1408,7 +1463,10 @@ int32_t fb_booster_update(fb_booster* h, uint32_t n_rounds) {
         b->ctx->sync();
         auto t0 = std::chrono::steady_clock::now();
         FB_CUDA_CHECK(cudaEventRecord(e0, b->ctx->stream()));
-        for (uint32_t r = 0; r < n_rounds; r++) fbe::booster_round(*b);
+        if (fbe::pipelinable(*b))
+            fbe::update_pipelined(*b, n_rounds);
+        else
+            for (uint32_t r = 0; r < n_rounds; r++) fbe::booster_round(*b);
         FB_CUDA_CHECK(cudaEventRecord(e1, b->ctx->stream()));
         b->ctx->sync();
         b->t_wall = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();

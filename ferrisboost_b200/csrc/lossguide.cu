@@ -424,7 +424,11 @@ void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* 
     }
     if (!root_only) evaluate(1, 1);
     FB_CUDA_CHECK(cudaMemcpyAsync(h_root, trec_.p, sizeof(TreeRec), cudaMemcpyDeviceToHost, s_));
+    unsigned long long* herr = h_small_.as<unsigned long long>() + 80;
+    if (scale_err_pending_)
+        FB_CUDA_CHECK(cudaMemcpyAsync(herr, sums_.as<unsigned long long>() + 6, 8, cudaMemcpyDeviceToHost, s_));
     sync();
+    check_scale_error(herr);
     slots[0].hist = 0;
     slots[0].value = h_root->leaf;
     slots[0].tree_id = 0;

@@ -176,13 +176,13 @@ void NcclComm::all_gather_bytes(const void* src, void* dst, size_t send_bytes, c
     wait_ready("ncclAllGather");
 }
 
-void NcclComm::sync(cudaStream_t s) {
+template <class Q> void NcclComm::wait(Q query) {
     if (failed_) throw NcclError("the NCCL communicator was aborted by an earlier error");
     const Api& a = api();
     ncclComm_t c = static_cast<ncclComm_t>(comm_);
     const auto t0 = Clock::now();
     for (;;) {
-        const cudaError_t e = cudaStreamQuery(s);
+        const cudaError_t e = query();
         if (e == cudaSuccess) return;
         if (e != cudaErrorNotReady) {
             (void)cudaGetLastError();
@@ -198,5 +198,9 @@ void NcclComm::sync(cudaStream_t s) {
         std::this_thread::yield();
     }
 }
+
+void NcclComm::sync(cudaStream_t s) { wait([s] { return cudaStreamQuery(s); }); }
+
+void NcclComm::wait_event(cudaEvent_t ev) { wait([ev] { return cudaEventQuery(ev); }); }
 
 }  // namespace fbg

@@ -41,8 +41,10 @@ public:
     void reduce_scatter_u64(const void* src, void* dst, size_t recv_count, cudaStream_t s);
     // ncclAllGather: dst holds every rank's send_bytes, in rank order.
     void all_gather_bytes(const void* src, void* dst, size_t send_bytes, cudaStream_t s);
-    // Waits for the stream, polling the communicator; aborts it after the time limit.
+    // Waits for the stream (or an event), polling the communicator; aborts it
+    // after the time limit.
     void sync(cudaStream_t s);
+    void wait_event(cudaEvent_t ev);
     bool failed() const { return failed_; }
     // Ends the communicator at once, without waiting for the peers (exit
     // paths; nothing may be in flight on it); later calls fail.
@@ -53,6 +55,7 @@ private:
     uint32_t timeout_ms_;
     bool failed_ = false;
     void wait_ready(const char* what);  // until the last call is no longer in progress
+    template <class Q> void wait(Q query);
     [[noreturn]] void fail(const std::string& msg, bool timeout);
 };
 

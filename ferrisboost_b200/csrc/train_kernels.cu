@@ -397,11 +397,14 @@ __global__ void k_softmax_grad(GradArgs a, uint32_t K, float* __restrict__ out) 
     }
 }
 
+// Zero scales (a non-finite bound, k_device_scales_exact) quantize every
+// row to zero.
 __global__ void k_quantize(GradArgs a) {
     Pair s{0, 0};
     double gs = a.scales[0], hs = a.scales[1];
+    const bool zero = gs == 0.0 || hs == 0.0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += blockDim.x * gridDim.x) {
-        Pair f = to_fixed(a.gpair_f32[2ull * i], a.gpair_f32[2ull * i + 1], gs, hs);
+        Pair f = zero ? Pair{0, 0} : to_fixed(a.gpair_f32[2ull * i], a.gpair_f32[2ull * i + 1], gs, hs);
         a.fixed[i] = f;
         s = padd(s, f);
     }
@@ -420,9 +423,46 @@ __device__ double d_pow2_scale(double max_abs, unsigned long long n_rows) {
     k = k < -1000 ? -1000 : (k > 1000 ? 1000 : k);
     return ldexp(1.0, k);
 }
-__global__ void k_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales) {
-    scales[0] = d_pow2_scale(__longlong_as_double((long long)maxbits[0]), n_rows);
-    scales[1] = d_pow2_scale(__longlong_as_double((long long)maxbits[1]), n_rows);
+// A non-finite bound: zero scales and *err = 1, as k_device_scales_exact.
+__global__ void k_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
+                                unsigned long long* err) {
+    const double mg = __longlong_as_double((long long)maxbits[0]), mh = __longlong_as_double((long long)maxbits[1]);
+    if (!isfinite(mg) || !isfinite(mh)) {
+        scales[0] = 0.0;
+        scales[1] = 0.0;
+        *err = 1ull;
+        return;
+    }
+    scales[0] = d_pow2_scale(mg, n_rows);
+    scales[1] = d_pow2_scale(mh, n_rows);
+    *err = 0ull;
+}
+
+// Exact mode: the reference's scales (types.rs:366-385, the host's log2;
+// qscale.h) from the bounds, so the round needs no host round trip.  A
+// non-finite bound sets *err and zero scales: every fixed-point gradient is
+// then zero (k_quantize), the tree grown from them adds nothing to the
+// margins, and the host raises the error when it reads the tree back.
+__global__ void k_device_scales_exact(const unsigned long long* maxbits, unsigned long long n_rows,
+                                      const fbx::ScaleExc* exc, uint32_t n_exc, double* scales,
+                                      unsigned long long* err) {
+    const double mg = __longlong_as_double((long long)maxbits[0]), mh = __longlong_as_double((long long)maxbits[1]);
+    if (!isfinite(mg) || !isfinite(mh)) {
+        scales[0] = 0.0;
+        scales[1] = 0.0;
+        *err = 1ull;
+        return;
+    }
+    scales[0] = fbx::scale_of_exp(fbx::scale_exp_exact(mg, n_rows, exc, n_exc));
+    scales[1] = fbx::scale_of_exp(fbx::scale_exp_exact(mh, n_rows, exc, n_exc));
+    *err = 0ull;
+}
+
+// The same scale of each value (the exactness tests).
+__global__ void k_quantizer_scales(const float* vals, uint64_t count, unsigned long long n_rows,
+                                   const fbx::ScaleExc* exc, uint32_t n_exc, double* out) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)blockDim.x * gridDim.x)
+        out[i] = fbx::scale_of_exp(fbx::scale_exp_exact((double)vals[i], n_rows, exc, n_exc));
 }
 
 // ------------------------------------------------------------------ histogram
@@ -2197,9 +2237,22 @@ void launch_softmax_gradients(const GradArgs& a, uint32_t K, float* out, int fas
     }
 }
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
-                          cudaStream_t s) {
+                          unsigned long long* err, cudaStream_t s) {
     count_launch();
-    k_device_scales<<<1, 1, 0, s>>>(maxbits, n_rows, scales);
+    k_device_scales<<<1, 1, 0, s>>>(maxbits, n_rows, scales, err);
+}
+void launch_device_scales_exact(const unsigned long long* maxbits, unsigned long long n_rows,
+                                const fbx::ScaleExc* exc, uint32_t n_exc, double* scales, unsigned long long* err,
+                                cudaStream_t s) {
+    count_launch();
+    k_device_scales_exact<<<1, 1, 0, s>>>(maxbits, n_rows, exc, n_exc, scales, err);
+}
+void launch_quantizer_scales(const float* vals, uint64_t count, unsigned long long n_rows, const fbx::ScaleExc* exc,
+                             uint32_t n_exc, double* out, cudaStream_t s) {
+    if (count == 0) return;
+    count_launch();
+    const uint64_t blocks = std::min<uint64_t>((count + 255) / 256, 148ull * 8);
+    k_quantizer_scales<<<(unsigned)blocks, 256, 0, s>>>(vals, count, n_rows, exc, n_exc, out);
 }
 void set_hist_smem_limit(int bytes) {
     cudaFuncSetAttribute(k_hist<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

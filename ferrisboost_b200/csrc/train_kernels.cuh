@@ -15,6 +15,7 @@
 #pragma once
 #include "common.cuh"
 #include "fexp.h"
+#include "qscale.h"
 
 namespace fbg {
 
@@ -171,7 +172,14 @@ void launch_quantize(const GradArgs& a, cudaStream_t s);
 // class-major).  fast: fexp_core alone; else the host expf (a.exptab).
 void launch_softmax_gradients(const GradArgs& a, uint32_t K, float* out, int fast, cudaStream_t s);
 void launch_device_scales(const unsigned long long* maxbits, unsigned long long n_rows, double* scales,
-                          cudaStream_t s);
+                          unsigned long long* err, cudaStream_t s);
+// Exact mode: the reference's scales (qscale.h) and the error word (1: a
+// non-finite bound, scales zero).
+void launch_device_scales_exact(const unsigned long long* maxbits, unsigned long long n_rows,
+                                const fbx::ScaleExc* exc, uint32_t n_exc, double* scales, unsigned long long* err,
+                                cudaStream_t s);
+void launch_quantizer_scales(const float* vals, uint64_t count, unsigned long long n_rows, const fbx::ScaleExc* exc,
+                             uint32_t n_exc, double* out, cudaStream_t s);
 void set_hist_smem_limit(int bytes);
 void launch_hist(int width, const TileDesc* tiles, uint32_t n_tiles, const TileFeat* tfeat, const uint32_t* rows,
                  const Pair* gpair, const NodeInfo* nodes, const uint32_t* acc_list,

@@ -365,6 +365,22 @@ fbgpu_status fbgpu_partition_noalloc(const void* bins, uint32_t stride, uint32_t
  * updates per thread, a multiple of 8. */
 fbgpu_status fbgpu_hist_atomic_ceiling(int32_t device, int32_t scheme, uint32_t iters, double* updates_per_s);
 
+/* The power-of-two quantizer scale of each bound `max_abs[i]` (the largest
+ * |gradient| or |Hessian| of a round, an f32 value) for `n_rows` rows, as
+ * exact-mode training computes it on the device: the reference's pow2_scale
+ * (src/types.rs:366-385, 2^floor(log2((2^62 / n_rows) / max_abs)) with the
+ * host's log2, clamped to 2^-1000..2^1000, 1.0 when that is not a positive
+ * finite number).  device >= 0 evaluates on that GPU, device < 0 on the host;
+ * both use the same code.  No reference counterpart as an entry point: the
+ * reference computes this on the host inside each round. */
+fbgpu_status fbgpu_quantizer_scales(int32_t device, const float* max_abs, uint64_t count, uint64_t n_rows,
+                                    double* out);
+/* Sum modulo 2^64 of mix(b, scale(f32 with bits b)) over b in [lo_bits,
+ * hi_bits), host, all cores: compared with the same digest of the
+ * reference's pow2_scale over every positive f32 (tests).  mix is the
+ * SplitMix64 finalizer of (scale bits) ^ (b * 0x9E3779B97F4A7C15). */
+uint64_t fbgpu_quantizer_scale_digest(uint32_t lo_bits, uint32_t hi_bits, uint64_t n_rows);
+
 /* ---------------------------------------------------------- explanation models */
 
 /* A model for device prediction and SHAP.  Node arrays of all trees back to

@@ -2090,6 +2090,31 @@ int rc_quantizer(const float* gpair, uint64_t n, uint64_t n_rows, double* scales
     return 0;
 }
 
+void rc_pow2_scales(const float* max_abs, uint64_t count, uint64_t n_rows, double* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)count; i++) out[i] = pow2_scale((double)max_abs[i], n_rows);
+}
+
+// Sum modulo 2^64 of the SplitMix64 finalizer of (scale bits) ^ (b * golden)
+// over the f32 bit patterns b in [lo_bits, hi_bits).
+uint64_t rc_pow2_scale_digest(uint32_t lo_bits, uint32_t hi_bits, uint64_t n_rows) {
+    uint64_t sum = 0;
+#pragma omp parallel for schedule(static) reduction(+ : sum)
+    for (int64_t b = (int64_t)lo_bits; b < (int64_t)hi_bits; b++) {
+        const uint32_t u = (uint32_t)b;
+        float f;
+        std::memcpy(&f, &u, 4);
+        const double s = pow2_scale((double)f, n_rows);
+        uint64_t z;
+        std::memcpy(&z, &s, 8);
+        z ^= (uint64_t)u * 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        sum += z ^ (z >> 31);
+    }
+    return sum;
+}
+
 void rc_to_fixed(const float* gpair, uint64_t n, const double* scales, int64_t* out, int64_t* sum) {
     Quantizer q = Quantizer::from_scales(scales[0], scales[1]);
     FX s{0, 0};

@@ -121,6 +121,11 @@ void rc_quantize(const float* X, uint64_t n, uint32_t F, const float* cuts,
 /* Power-of-two quantizer scales (grad, hess) for n_rows rows. */
 int rc_quantizer(const float* gpair, uint64_t n, uint64_t n_rows,
                  double* scales);
+/* types.rs:366-385 pow2_scale of each f32 bound, and a digest of it over the
+ * f32 bit patterns [lo_bits, hi_bits): the sum modulo 2^64 of the SplitMix64
+ * finalizer of (scale bits) ^ (b * 0x9E3779B97F4A7C15). */
+void rc_pow2_scales(const float* max_abs, uint64_t count, uint64_t n_rows, double* out);
+uint64_t rc_pow2_scale_digest(uint32_t lo_bits, uint32_t hi_bits, uint64_t n_rows);
 /* Fixed-point gradients round(v * scale) and their sum. */
 void rc_to_fixed(const float* gpair, uint64_t n, const double* scales,
                  int64_t* out, int64_t* sum);

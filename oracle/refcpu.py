@@ -87,6 +87,10 @@ class RefCPU:
                                     C.POINTER(C.c_uint32), C.POINTER(C.c_uint8), C.POINTER(C.c_uint16)]
         lib.rc_quantizer.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.c_uint64, C.POINTER(C.c_double)]
         lib.rc_quantizer.restype = C.c_int
+        lib.rc_pow2_scales.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.c_uint64, C.POINTER(C.c_double)]
+        lib.rc_pow2_scales.restype = None
+        lib.rc_pow2_scale_digest.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64]
+        lib.rc_pow2_scale_digest.restype = C.c_uint64
         lib.rc_to_fixed.argtypes = [C.POINTER(C.c_float), C.c_uint64, C.POINTER(C.c_double),
                                     C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
         lib.rc_hist.argtypes = [C.POINTER(C.c_uint16), C.c_uint64, C.c_uint32, C.POINTER(C.c_uint32),
@@ -282,6 +286,17 @@ class RefCPU:
         if rc:
             raise ValueError("non-finite gradient or Hessian")
         return s
+
+    def pow2_scales(self, max_abs, n_rows):
+        """types.rs:366-385 pow2_scale of each f32 bound."""
+        v = np.ascontiguousarray(max_abs, dtype=np.float32)
+        out = np.zeros(v.shape[0], dtype=np.float64)
+        self.lib.rc_pow2_scales(_ptr(v, C.c_float), v.shape[0], n_rows, _ptr(out, C.c_double))
+        return out
+
+    def pow2_scale_digest(self, lo_bits, hi_bits, n_rows):
+        """Digest of pow2_scale over the f32 bit patterns [lo_bits, hi_bits)."""
+        return int(self.lib.rc_pow2_scale_digest(lo_bits, hi_bits, n_rows))
 
     def to_fixed(self, gpair, scales):
         g = np.ascontiguousarray(gpair, dtype=np.float32)

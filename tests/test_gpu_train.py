@@ -346,3 +346,18 @@ def test_partition_leaf_path_byte_identical(oracle, tmp_path, case):
     walked.update(6)
     assert walked.model().to_json() == ref.json()
     assert np.array_equal(walked.margins().view(np.uint32), np.load(tmp_path / "margin.npy").view(np.uint32))
+
+
+def test_non_finite_gradient_stops_the_booster():
+    # w * scale_pos_weight overflows to +inf on the positive rows: the
+    # gradient bounds are not finite, the round raises (the scales are
+    # computed on the device and the error is read back with the tree), and
+    # the booster takes no further rounds
+    X, y = _synthetic(5000, 6, seed=4)
+    w = np.full(len(y), 1e37, np.float32)
+    b = fb.Booster(dict(objective="binary:logistic", max_depth=3, scale_pos_weight=100.0, base_score=0.5),
+                   fb.Dataset(X, max_bin=64, weight=w), y, w)
+    with pytest.raises(Exception, match="non-finite gradient or Hessian"):
+        b.update(3)
+    with pytest.raises(Exception, match="non-finite|stopped after an error"):
+        b.update(1)
