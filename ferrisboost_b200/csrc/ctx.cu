@@ -876,6 +876,30 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
     }
 }
 
+// The split search's feature lists for [a.feat_lo, a.feat_hi): numeric
+// features of up to 256 bins (a warp each) and the rest (a CTA each).
+void TrainCtx::set_split_lists(LevelArgs& a) {
+    if (split_lists_lo_ != a.feat_lo || split_lists_hi_ != a.feat_hi || !d_split_lists_.p) {
+        std::vector<uint32_t> num, cta;
+        for (uint32_t f = a.feat_lo; f < a.feat_hi; f++)
+            ((nbins_[f] <= 256 && !cat_[f]) ? num : cta).push_back(f);
+        n_split_num_ = (uint32_t)num.size();
+        n_split_cta_ = (uint32_t)cta.size();
+        split_lists_host_ = num;
+        split_lists_host_.insert(split_lists_host_.end(), cta.begin(), cta.end());
+        d_split_lists_.alloc(4 * std::max<size_t>(split_lists_host_.size(), 1));
+        if (!split_lists_host_.empty())
+            FB_CUDA_CHECK(cudaMemcpyAsync(d_split_lists_.p, split_lists_host_.data(), 4 * split_lists_host_.size(),
+                                          cudaMemcpyHostToDevice, s_));
+        split_lists_lo_ = a.feat_lo;
+        split_lists_hi_ = a.feat_hi;
+    }
+    a.split_num = d_split_lists_.as<uint32_t>();
+    a.n_split_num = n_split_num_;
+    a.split_cta = d_split_lists_.as<uint32_t>() + n_split_num_;
+    a.n_split_cta = n_split_cta_;
+}
+
 LevelArgs TrainCtx::level_args(const fbgpu_tree_params& tp) const {
     LevelArgs a{};
     a.n_features = F_;
@@ -1106,6 +1130,7 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
         a.feat_hi = rank_feat_lo_[rank_ + 1];
         a.bin_lo = rank_bin_lo_[rank_];
     }
+    set_split_lists(a);
     if (root_pending_ && (maxd == 0 || rs_mode)) reduce_root_sum(true);
     launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
     for (uint32_t d = 0; d < maxd; d++) {
@@ -1346,6 +1371,7 @@ void TrainCtx::eval_split(const int64_t* hist, const int64_t* node_sum, const do
     FB_CUDA_CHECK(cudaMemcpyAsync(nodes_[0].p, &ni, sizeof ni, cudaMemcpyHostToDevice, s_));
     FB_CUDA_CHECK(cudaMemcpyAsync(state_.p, &st, sizeof st, cudaMemcpyHostToDevice, s_));
     LevelArgs a = level_args(tp);
+    set_split_lists(a);
     a.nodes = nodes_[0].as<NodeInfo>();
     a.hist_cur = hist_[0].as<Pair>();
     a.hist_prev = hist_[1].as<Pair>();

@@ -204,6 +204,10 @@ class TrainCtx {
     // the launch half; a best-first tree is grown and read back into lg_out here
     void build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* lg_out);
     LevelArgs level_args(const fbgpu_tree_params& tp) const;
+    void set_split_lists(LevelArgs& a);
+    DevMem d_split_lists_;  // [numeric features of <= 256 bins | the rest] of the cached range
+    std::vector<uint32_t> split_lists_host_;
+    uint32_t split_lists_lo_ = ~0u, split_lists_hi_ = ~0u, n_split_num_ = 0, n_split_cta_ = 0;
     GradArgs grad_args() const;
 
     fbgpu_config cfg_;

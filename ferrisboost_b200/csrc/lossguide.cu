@@ -330,6 +330,7 @@ int32_t total_key(float g) {
 void TrainCtx::build_tree_lossguide(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out) {
     const uint32_t max_leaves = tp.max_leaves, max_depth = tp.max_depth;
     LevelArgs a = level_args(tp);
+    set_split_lists(a);
     a.last_level = 0;
     Pair* pool = hist_[0].as<Pair>();
     a.hist_cur = pool;

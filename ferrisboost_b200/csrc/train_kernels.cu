@@ -1137,8 +1137,10 @@ __device__ void split_cat_wide(const LevelArgs& a, SplitSmem& s, const Pair* hx,
 // sibling), scan it, score every candidate and keep the first maximum in the
 // reference's enumeration order (split.rs:331-461; categorical :484-617).
 __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
-    // features feat_lo.. (all features, unless the split search is feature-sharded)
-    const uint32_t node = blockIdx.x, f = a.feat_lo + blockIdx.y, F = a.n_features;
+    // features feat_lo.. (all features, unless the split search is feature-sharded);
+    // with the warp kernel beside it, only the categorical and wide ones
+    const uint32_t node = blockIdx.x, F = a.n_features;
+    const uint32_t f = a.split_cta ? a.split_cta[blockIdx.y] : a.feat_lo + blockIdx.y;
     if (node >= a.st->m) return;
     SplitRec* out = a.feat_best + (size_t)node * F + f;
     if (!a.enabled[f] || f >= a.feat_hi) {
@@ -1311,6 +1313,102 @@ __global__ void __launch_bounds__(kSplitThreads) k_split_feat(LevelArgs a) {
         SplitRec b = s.best[0];
         b.feat = f;
         *out = b;
+    }
+}
+
+// Numeric features of at most kSplitWarpBins bins: one warp per (node,
+// feature), lane l holding bins [8l, 8l + 8).  The same candidates as the
+// numeric path of k_split_feat (forward with missing right at every bin,
+// then, when the node has missing values, reverse with missing left; the
+// same ordinals), the prefix sums and the arg-max by shuffles, so no block
+// barrier.  The arg-max order (gain, then ordinal) is total, so the winner
+// does not depend on how the candidates are reduced.
+// 128-thread CTAs (16 resident warps per SM at the kernel's ~110 registers;
+// bounding it further spills): a level's (node, feature) warps are spread
+// in finer steps than with 256-thread CTAs.
+constexpr uint32_t kSplitWarpBins = 256;
+constexpr uint32_t kSplitNumThreads = 128;
+__global__ void __launch_bounds__(kSplitNumThreads) k_split_num(LevelArgs a) {
+    const uint32_t node = blockIdx.x, lane = threadIdx.x & 31u;
+    const uint32_t item = blockIdx.y * (kSplitNumThreads / 32) + (threadIdx.x >> 5);
+    if (node >= a.st->m || item >= a.n_split_num) return;
+    const uint32_t f = a.split_num[item];
+    SplitRec* out = a.feat_best + (size_t)node * a.n_features + f;
+    if (!a.enabled[f]) {
+        if (lane == 0) out->flags = 0;
+        return;
+    }
+    const NodeInfo ni = a.nodes[node];
+    const uint32_t off = a.hoff[f] - a.bin_lo, nb = a.hoff[f + 1] - a.hoff[f];
+    const Pair* acc = a.hist_acc + (unsigned long long)ni.acc_slot * a.slot_pairs + off;
+    const Pair* par = ni.parent_slot >= 0 ? a.hist_prev + (unsigned long long)ni.parent_slot * a.slot_pairs + off
+                                          : nullptr;
+    Pair* h = a.hist_cur + (unsigned long long)(a.node_hist ? a.node_hist[node] : node) * a.slot_pairs + off;
+    const bool keep_hist = !a.last_level;
+    const Pair sum = ni.sum;
+    const ScoreParams sp = load_sp(a);
+    const float parent_gain = node_gain(sum, sp, ni.lower, ni.upper);
+    const int cons = a.mono ? (int)a.mono[f] : 0;
+    const uint32_t b0 = lane * 8;
+    Pair v[8];
+    Pair loc{0, 0};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t bidx = b0 + k;
+        Pair x{0, 0};
+        if (bidx < nb) {
+            x = par ? psub(par[bidx], acc[bidx]) : acc[bidx];
+            if (keep_hist) h[bidx] = x;
+        }
+        v[k] = x;
+        loc = padd(loc, x);
+    }
+    Pair incl = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const Pair t{__shfl_up_sync(0xffffffffu, incl.g, o), __shfl_up_sync(0xffffffffu, incl.h, o)};
+        if ((int)lane >= o) incl = padd(incl, t);
+    }
+    const Pair total{__shfl_sync(0xffffffffu, incl.g, 31), __shfl_sync(0xffffffffu, incl.h, 31)};
+    const bool reverse = !peq(total, sum);
+    SplitRec mine;
+    mine.flags = 0; mine.gain = 0.0f; mine.ord = 0xffffffffu; mine.bin = 0; mine.feat = f;
+    mine.left = Pair{0, 0}; mine.right = Pair{0, 0};
+    Pair run = psub(incl, loc);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t bidx = b0 + k;
+        if (bidx < nb) {
+            const Pair excl = run;
+            run = padd(run, v[k]);
+            float gain;
+            const Pair r = psub(sum, run);
+            if (split_gain(parent_gain, run, r, cons, ni.lower, ni.upper, sp, gain))
+                consider(mine, gain, bidx, bidx + 1, 0u, run, r);
+            if (reverse) {
+                const Pair rr = psub(total, excl);
+                const Pair ll = psub(sum, rr);
+                if (split_gain(parent_gain, ll, rr, cons, ni.lower, ni.upper, sp, gain))
+                    consider(mine, gain, nb + (nb - 1 - bidx), bidx, 2u, ll, rr);
+            }
+        }
+    }
+    // arg-max of (valid, gain, ordinal) over the warp; the lane holding the
+    // winning ordinal writes its record (ordinals are unique per candidate)
+    bool bv = (mine.flags & 1u) != 0;
+    float bg = mine.gain;
+    uint32_t bo = mine.ord;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const bool ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const float og = __shfl_xor_sync(0xffffffffu, bg, o);
+        const uint32_t oo = __shfl_xor_sync(0xffffffffu, bo, o);
+        if (ov && (!bv || og > bg || (og == bg && oo < bo))) { bv = true; bg = og; bo = oo; }
+    }
+    if (!bv) {
+        if (lane == 0) *out = mine;  // flags 0
+    } else if ((mine.flags & 1u) && mine.ord == bo) {
+        *out = mine;
     }
 }
 
@@ -2331,21 +2429,41 @@ void launch_hist_stage(int width, int stages, const TileDesc* tiles, uint32_t n_
     }
 #undef FB_HS
 }
-void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
-    if (a.feat_hi > a.feat_lo) {
-        dim3 grid(max_m, a.feat_hi - a.feat_lo);
-        count_launch();
-        k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
+// The per-feature searches.  From kSplitWarpNodes nodes on: numeric features
+// of up to kSplitWarpBins bins a warp each (k_split_num), the others a CTA
+// each (k_split_feat).  Below (or without the lists) every feature of
+// [feat_lo, feat_hi) a CTA: with few nodes, a warp's serial chain of 16 gain
+// evaluations takes longer than a CTA's one per thread (measured on B200, C1:
+// the warp form 15-18 us per level up to 16 nodes against 10-15, and 26 / 32
+// against 32 / 55 us at 64 / 128 nodes).
+constexpr uint32_t kSplitWarpNodes = 32;
+static void launch_split_feats(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
+    if (!a.split_cta || max_m < kSplitWarpNodes) {
+        if (a.feat_hi > a.feat_lo) {
+            LevelArgs all = a;
+            all.split_cta = nullptr;
+            count_launch();
+            k_split_feat<<<dim3(max_m, a.feat_hi - a.feat_lo), kSplitThreads, 0, s>>>(all);
+        }
+        return;
     }
+    if (a.n_split_num) {
+        count_launch();
+        k_split_num<<<dim3(max_m, (a.n_split_num + kSplitNumThreads / 32 - 1) / (kSplitNumThreads / 32)),
+                      kSplitNumThreads, 0, s>>>(a);
+    }
+    if (a.n_split_cta) {
+        count_launch();
+        k_split_feat<<<dim3(max_m, a.n_split_cta), kSplitThreads, 0, s>>>(a);
+    }
+}
+void launch_split(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
+    launch_split_feats(a, max_m, s);
     count_launch();
     k_split_node<<<max_m, 32, 0, s>>>(a);
 }
 void launch_split_decide(const LevelArgs& a, uint32_t max_m, cudaStream_t s) {
-    if (a.feat_hi > a.feat_lo) {
-        dim3 grid(max_m, a.feat_hi - a.feat_lo);
-        count_launch();
-        k_split_feat<<<grid, kSplitThreads, 0, s>>>(a);
-    }
+    launch_split_feats(a, max_m, s);
     count_launch();
     k_split_node_decide<<<(max_m + 7) / 8, 256, 0, s>>>(a);
 }

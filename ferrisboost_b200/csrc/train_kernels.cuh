@@ -101,6 +101,13 @@ struct LevelArgs {
     unsigned long long slot_pairs; // pairs per histogram slot (total bins; a rank's block when feature-sharded)
     uint32_t feat_lo, feat_hi;   // features this rank scores (all unless the split search is feature-sharded)
     uint32_t bin_lo;             // first bin of feat_lo in the node histograms (their slots hold bins from here)
+    // the features of [feat_lo, feat_hi) split by search kernel: numeric ones of
+    // up to 256 bins (a warp each, k_split_num) and the rest (a CTA each,
+    // k_split_feat); null split_cta: every feature a CTA
+    const uint32_t* split_num;
+    uint32_t n_split_num;
+    const uint32_t* split_cta;
+    uint32_t n_split_cta;
     SplitRec* feat_best;         // [node * F + f]
     // category sets: cat_words 32-bit words each (>= 8; a bit per code, set =
     // right-going); codes at or beyond 32 * cat_words go left
