@@ -1151,8 +1151,12 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
         a.rows_cur = rows_[cur].as<uint32_t>();
         a.rows_next = rows_[1 - cur].as<uint32_t>();
         const uint64_t block = (uint64_t)max_acc * chunk_pairs_;  // rs_mode: pairs of one rank's block
-        FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, rs_mode ? 16ull * nranks_ * block : 16ull * a.slot_pairs * max_acc,
-                                      s_));
+        // the level's accumulate histograms start at zero: the root level's
+        // here, the others zeroed by the previous level's k_part_level
+        auto acc_bytes = [&](uint64_t acc) {
+            return rs_mode ? 16ull * nranks_ * acc * chunk_pairs_ : 16ull * a.slot_pairs * acc;
+        };
+        if (d == 0) FB_CUDA_CHECK(cudaMemsetAsync(hist_acc_.p, 0, acc_bytes(max_acc), s_));
         if (stats_ && d < 15) {
             // this level's accumulate nodes and rows: TreeState bytes [8, 24) hold
             // leaf_count, acc_count (u32 each) and acc_total (u64)
@@ -1202,7 +1206,14 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
         }
         // the last level's children are final leaves: with the walk they need
         // nothing here, otherwise their leaf values go to the margins now
-        if (!a.last_level) launch_part_level(a, max_chunks, s_);
+        if (!a.last_level) {
+            const uint64_t next_acc = std::min<uint64_t>(1ull << d, max_acc_);
+            a.hist_zero = hist_acc_.as<unsigned long long>();
+            a.hist_zero_words = acc_bytes(next_acc) / 8;
+            launch_part_level(a, max_chunks, s_);
+            a.hist_zero = nullptr;
+            a.hist_zero_words = 0;
+        }
         else if (!a.walk) launch_part_final(a, max_chunks, s_);
         cur = 1 - cur;
     }

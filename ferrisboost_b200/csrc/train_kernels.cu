@@ -1956,6 +1956,15 @@ __device__ __forceinline__ void part_level_work(const LevelArgs& a) {
 // takes unbounded): the pass waits on its dependent loads, so residency is
 // what hides them.
 __global__ void __launch_bounds__(kPartThreads, 4) k_part_level(LevelArgs a) {
+    // the next level's accumulate histograms, read by this level's split
+    // search (finished before this kernel) and not again, start at zero
+    if (a.hist_zero) {
+        uint4* z = reinterpret_cast<uint4*>(a.hist_zero);
+        const unsigned long long n16 = a.hist_zero_words / 2;
+        for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+             i += (unsigned long long)gridDim.x * blockDim.x)
+            z[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
     part_level_work(a);
     if (last_block_done(a.fuse + 1)) {
         __shared__ unsigned long long wt64_next[32];

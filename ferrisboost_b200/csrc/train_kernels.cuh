@@ -133,6 +133,8 @@ struct LevelArgs {
                                  // of the kernel before them (null: separate launches)
     unsigned long long* part_cnt; // depthwise: per node (left rows, right rows) reserved by k_part_level;
                                   // zero between levels
+    unsigned long long* hist_zero; // depthwise: k_part_level zeroes the next level's accumulate
+    unsigned long long hist_zero_words; // histograms (a multiple of 2 words), or nothing when null
 };
 
 #ifdef __CUDACC__
