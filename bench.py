@@ -481,13 +481,16 @@ def run_ours(args, rank, world):
     # median of E2E_RUNS runs (the host cores are shared with other jobs, so
     # a single run can catch a stall of the multithreaded set-up), every run
     # listed beside it
-    e2e_runs = []
+    e2e_runs, e2e_split = [], []
     for _ in range(E2E_RUNS):
         _fence(dist)
         t0 = time.perf_counter()
         m = train_public(p, E2E_ROUNDS)
+        t1 = time.perf_counter()
         model_json = m.to_json()
-        e2e_runs.append(_max_over_ranks(dist, time.perf_counter() - t0))
+        t2 = time.perf_counter()
+        e2e_runs.append(_max_over_ranks(dist, t2 - t0))
+        e2e_split.append([round(t1 - t0, 4), round(t2 - t1, 4)])
     e2e_s = float(np.median(e2e_runs))
     exact_model = m
     e2e_parquet = None
@@ -560,6 +563,7 @@ def run_ours(args, rank, world):
                    if n * ((F * (2 if p["max_bin"] > 255 else 1) + 15) // 16 * 16 + 16) > 126e6
                    else "inputs smaller than L2"},
         "e2e": {"value": round(e2e_s, 4), "unit": "s/100 rounds", "runs": [round(v, 4) for v in e2e_runs],
+                "runs_train_json_s": e2e_split,
                 "h2d_bytes_per_step": int(e2e_h2d / E2E_ROUNDS),
                 "d2h_bytes_per_step": int(tree_readback + 16 + len(model_json) / E2E_ROUNDS),
                 "includes": "sketch + binning + upload + 100 rounds + model JSON through the public train(); "

@@ -826,11 +826,19 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
         feature_types = None
     if label is None:
         raise ValueError("label is required for array input")
+    from ._trace import PhaseTrace
+    trace = PhaseTrace("train")
     ds = Dataset(data, max_bin=p["max_bin"], weight=weight, feature_types=feature_types, nthread=p["nthread"],
                  missing=p["missing"], device=p["device_index"])
+    trace("dataset (upload, sketch, bins)")
     b = Booster(params, ds, label, weight)
+    trace("booster")
     b.update(num_boost_round)
+    trace("rounds")
     m = b.model()
     m.params = p
     m.feature_names = ds.feature_names or None
+    trace("model")
+    del b, ds
+    trace("release")
     return m

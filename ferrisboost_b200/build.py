@@ -18,7 +18,7 @@ HERE = pathlib.Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libfbgpu.so"
 SOURCES = ["train_kernels.cu", "explain_kernels.cu", "ctx.cu", "engine.cu", "noalloc.cu", "nccl_loader.cu", "lossguide.cu",
-           "sketch.cu", "shap_paths.cu", "hist_ceiling.cu", "qscale.cu"]
+           "sketch.cu", "shap_paths.cu", "hist_ceiling.cu", "qscale.cu", "devmem.cu"]
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 
 

@@ -31,28 +31,37 @@ struct InputError : std::runtime_error {
     using std::runtime_error::runtime_error;
 };
 
-// Owning device allocation.
+// Device blocks through the process-wide cache (devmem.cu): dev_alloc
+// returns a block of at least n bytes and its size in *cap; dev_free takes
+// the block back once its device is idle.
+void* dev_alloc(size_t n, size_t* cap);
+void dev_free(void* p, size_t cap);
+void* pinned_alloc(size_t n, size_t* cap);
+void pinned_free(void* p, size_t cap);
+
+// Owning device allocation; `bytes` is the size asked for.
 struct DevMem {
     void* p = nullptr;
-    size_t bytes = 0;
+    size_t bytes = 0, cap = 0;
     DevMem() = default;
     DevMem(const DevMem&) = delete;
     DevMem& operator=(const DevMem&) = delete;
     ~DevMem() { release(); }
     void release() {
-        if (p) cudaFree(p);
+        if (p) dev_free(p, cap);
         p = nullptr;
-        bytes = 0;
+        bytes = cap = 0;
     }
     void alloc(size_t n) {
         release();
         if (n == 0) n = 16;
-        FB_CUDA_CHECK(cudaMalloc(&p, n));
+        p = dev_alloc(n, &cap);
         bytes = n;
     }
     template <class T> T* as() const { return static_cast<T*>(p); }
 };
 
+// Pinned host buffer through the same cache; `bytes` is its capacity.
 struct PinnedMem {
     void* p = nullptr;
     size_t bytes = 0;
@@ -61,15 +70,14 @@ struct PinnedMem {
     PinnedMem& operator=(const PinnedMem&) = delete;
     ~PinnedMem() { release(); }
     void release() {
-        if (p) cudaFreeHost(p);
+        if (p) pinned_free(p, bytes);
         p = nullptr;
         bytes = 0;
     }
     void reserve(size_t n) {
         if (n <= bytes) return;
         release();
-        FB_CUDA_CHECK(cudaMallocHost(&p, n));
-        bytes = n;
+        p = pinned_alloc(n, &bytes);
     }
     template <class T> T* as() const { return static_cast<T*>(p); }
 };

@@ -588,7 +588,7 @@ DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cud
     if (!((rs_ == F && cs_ == 1) || (rs_ == 1 && cs_ == n)))
         throw std::invalid_argument("DeviceMatrix: the host matrix must be contiguous row-major or column-major");
     const size_t bytes = (size_t)n * F * sizeof(float);
-    FB_CUDA_CHECK(cudaMalloc(&x_, std::max<size_t>(bytes, 16)));
+    x_ = static_cast<float*>(dev_alloc(std::max<size_t>(bytes, 16), &x_cap_));
     // pageable source: pinned staging in slabs, two buffers so the host copy
     // of one slab overlaps the transfer of the other.  The two 64 MiB buffers
     // are allocated once per process and kept (pinned allocation costs tens
@@ -622,7 +622,7 @@ DeviceMatrix::DeviceMatrix(const HostMatrix& X_host, uint64_t n, uint32_t F, cud
         } catch (...) {
             cudaStreamSynchronize(s_);
             for (auto& e : done) cudaEventDestroy(e);
-            cudaFree(x_);
+            dev_free(x_, x_cap_);
             x_ = nullptr;
             throw;
         }
@@ -649,7 +649,7 @@ std::vector<uint8_t> DeviceMatrix::nan_features() {
 DeviceMatrix::~DeviceMatrix() {
     if (x_) {
         cudaStreamSynchronize(s_);
-        cudaFree(x_);
+        dev_free(x_, x_cap_);
     }
 }
 

@@ -64,6 +64,7 @@ class DeviceMatrix {
     uint64_t rs_, cs_;  // element (r, f) at x_[r * rs_ + f * cs_]
     cudaStream_t s_;
     float* x_ = nullptr;
+    size_t x_cap_ = 0;  // the block's size (dev_alloc)
 };
 
 }  // namespace fbg

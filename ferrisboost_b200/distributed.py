@@ -38,6 +38,7 @@ import numpy as np
 
 from . import (_OBJECTIVES, Booster, Dataset, Shard, _as_matrix, _err, _feature_flags, _lib, _normalize_params,
                lib)
+from ._trace import PhaseTrace
 
 __all__ = ["shard_range", "sketch_cuts", "nccl_unique_id", "train", "Liveness", "PeerLost", "Communicator",
            "release_communicators"]
@@ -271,22 +272,6 @@ def _broadcast(obj, group=None):
     return box[0]
 
 
-class _PhaseTrace:
-    """FBGPU_TRACE=1: wall time of each phase of a sharded train() on stderr."""
-
-    def __init__(self, what: str):
-        import time
-        self.what, self.on, self.clock = what, bool(os.environ.get("FBGPU_TRACE")), time.perf_counter
-        self.t = self.clock()
-
-    def __call__(self, name: str) -> None:
-        if not self.on:
-            return
-        now = self.clock()
-        sys.stderr.write(f"[fbgpu] {self.what} {name:<30} {1000 * (now - self.t):9.3f} ms\n")
-        self.t = now
-
-
 def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_round: int = 10, weight: Any = None,
           feature_types: Sequence[str] | None = None, group=None, timeout_s: float = 120.0,
           return_booster: bool = False, liveness: Liveness | None = None):
@@ -323,7 +308,7 @@ def train(params: Mapping[str, Any], data: Any, label: Any = None, num_boost_rou
     if n < world:  # the same on every rank: all raise before any collective
         raise ValueError(f"{n} rows cannot be sharded over {world} ranks")
     cat = _feature_flags(feature_types, F)
-    trace = _PhaseTrace(f"rank {rank}")
+    trace = PhaseTrace(f"rank {rank}")
     timeout_ms = int(max(1.0, timeout_s) * 1000)
     # a new communicator initializes while the cuts are sketched and the rows binned
     comm = _communicator((id(group) if group is not None else 0, world, rank, p["device_index"]), world, rank,
