@@ -793,6 +793,19 @@ void TrainCtx::plan_tiles(const uint8_t* enabled, bool rank_major) {
     for (int w = 0; w < 2; w++)
         for (const TileDesc& t : direct[w]) smem_gen = std::max(smem_gen, (size_t)t.n_feat * sizeof(TileFeat));
     std::vector<TileDesc> all;
+    // mean bins per tile of each launch (the fixed clear-and-flush work of a CTA)
+    auto mean_bins = [&](const std::vector<TileDesc>& v) -> uint64_t {
+        uint64_t b = 0;
+        for (const TileDesc& t : v)
+            for (uint32_t i = 0; i < t.n_feat; i++) b += tf[t.feat_begin + i].nbins;
+        return v.empty() ? 0 : b / v.size();
+    };
+    for (int w = 0; w < 2; w++) {
+        tile_bins_gen_[w] = mean_bins(gen[w]);
+        tile_bins_lpf_[w] = mean_bins(lpf[w]);
+        tile_bins_direct_[w] = mean_bins(direct[w]);
+    }
+    tile_bins_wide_ = mean_bins(wide);
     for (int w = 0; w < 2; w++) { tile_off_gen_[w] = (uint32_t)all.size(); n_gen_[w] = (uint32_t)gen[w].size(); all.insert(all.end(), gen[w].begin(), gen[w].end()); }
     for (int w = 0; w < 2; w++) { tile_off_lpf_[w] = (uint32_t)all.size(); n_lpf_[w] = (uint32_t)lpf[w].size(); all.insert(all.end(), lpf[w].begin(), lpf[w].end()); }
     tile_off_wide_ = (uint32_t)all.size();
@@ -846,13 +859,38 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
     const TileFeat* TF = d_tfeat_.as<TileFeat>();
     if (!out) out = hist_acc_.as<Pair>();
     if (!slot) slot = std::max<uint64_t>(total_bins_, 1);
-    const uint32_t grid_gen = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 1024), 148 * 2));
+    // CTAs per feature tile.  Each CTA clears and flushes (global atomics
+    // into the same node bins as its tile's other CTAs) a shared histogram of
+    // its tile's bins whatever its row count, so a CTA should get rows in
+    // proportion to its tile's bins: with many tiles and few rows (C2: 38
+    // tiles of 32 features, 400k rows) a full grid per tile made that fixed
+    // work dominate (5624 CTAs of ~2700 rows, 0.85 ms per level).  The
+    // launch still fills every SM once (the kernels are issue-bound: idle SMs
+    // cost more than extra flushes), and beyond one wave its CTAs are
+    // snapped to whole waves (a nearly empty last wave costs a full one).
+    // Rows per CTA per tile bin, measured on B200 (s / 100 rounds at factors
+    // 1 / 4 / 16): lane-per-feature tiles 4 (C2: 0.703 / 0.589 / 0.631), wide
+    // tiles 16 (C3: 1.003 / 1.002 / 0.844); C1 and C0 fill one wave at any.
+    auto per_tile = [&](uint32_t slots, uint32_t n_tiles, uint64_t tile_bins, uint64_t min_rows,
+                        uint64_t rows_per_bin) {
+        if (n_tiles == 0) return 1u;
+        const uint64_t want_rows = std::max<uint64_t>(min_rows, rows_per_bin * tile_bins);
+        const uint64_t by_rows = std::max<uint64_t>(1, ceil_div(rows_upper, std::max<uint64_t>(want_rows, 1)));
+        const uint64_t fill = std::min<uint64_t>(std::max<uint32_t>(1, slots / n_tiles),
+                                                 std::max<uint64_t>(1, ceil_div(rows_upper, min_rows)));
+        uint64_t g = std::min<uint64_t>(std::max(by_rows, fill), slots);
+        const uint64_t total = g * n_tiles;
+        if (total > slots) {
+            const uint64_t waves = std::max<uint64_t>(1, (total + slots / 2) / slots);
+            g = std::max<uint64_t>(1, waves * slots / n_tiles);
+        }
+        return (uint32_t)g;
+    };
     const size_t lpf_smem = hist_stages_ ? tile_smem_stage_ : tile_smem_lpf_;
     const int per_sm = lpf_smem + 1024 <= 113 * 1024 ? 2 : 1;
-    // every SM gets a CTA once there are ~512 rows per CTA: the kernel is
-    // issue-bound, so idle SMs cost more than the extra flushes
-    const uint32_t grid_lpf = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u * per_sm));
     for (int w = 0; w < 2; w++) {
+        const uint32_t grid_gen = per_tile(148 * 2, n_gen_[w], tile_bins_gen_[w], 1024, 4);
+        const uint32_t grid_lpf = per_tile(148u * per_sm, n_lpf_[w], tile_bins_lpf_[w], 512, 4);
         launch_hist(w + 1, T + tile_off_gen_[w], n_gen_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list, acc_prefix,
                     state_.as<TreeState>(), out, slot, grid_gen, tile_smem_, s_);
         if (hist_stages_)
@@ -867,9 +905,11 @@ void TrainCtx::launch_histograms(const uint32_t* rows, const NodeInfo* nodes, co
     for (int w = 0; w < 2; w++)
         if (n_direct_[w])
             launch_hist(w + 1, T + tile_off_direct_[w], n_direct_[w], TF, rows, fixed_.as<Pair>(), nodes, acc_list,
-                        acc_prefix, state_.as<TreeState>(), out, slot, grid_gen, tile_smem_, s_);
+                        acc_prefix, state_.as<TreeState>(), out, slot,
+                        per_tile(148 * 2, n_direct_[w], tile_bins_direct_[w], 1024, 4),
+                        tile_smem_, s_);
     if (n_wide_) {
-        const uint32_t grid_wide = std::max<uint32_t>(1, std::min<uint32_t>(ceil_div(rows_upper, 512), 148u));
+        const uint32_t grid_wide = per_tile(148u, n_wide_, tile_bins_wide_, 512, 16);
         launch_hist_wide(wide_stages_, T + tile_off_wide_, n_wide_, TF, rows, fixed_.as<Pair>(), nodes, acc_list,
                          acc_prefix, state_.as<TreeState>(), out, slot, grid_wide, tile_smem_wide_,
                          s_);

@@ -245,6 +245,8 @@ class TrainCtx {
     size_t tile_smem_ = 0, tile_smem_lpf_ = 0, tile_smem_stage_ = 0;
     int hist_stages_ = 0;  // staged lane-per-feature histogram: cp.async stages, 0 = unstaged kernel
     uint32_t tile_off_wide_ = 0, n_wide_ = 0;  // wide tiles (8 lanes per row)
+    uint64_t tile_bins_gen_[2] = {0, 0}, tile_bins_lpf_[2] = {0, 0}, tile_bins_wide_ = 0,
+             tile_bins_direct_[2] = {0, 0};  // mean bins per tile of each launch
     uint32_t tile_off_direct_[2] = {0, 0}, n_direct_[2] = {0, 0};  // global-atomic tiles (no shared histogram)
     size_t tile_smem_wide_ = 0;
     int wide_stages_ = 4;
