@@ -281,6 +281,8 @@ TrainCtx::~TrainCtx() {
     if (s_) cudaStreamSynchronize(s_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
+    for (cudaGraphExec_t& e : tree_exec_)
+        if (e) cudaGraphExecDestroy(e);
     for (ReadSlot& sl : slot_) {
         for (cudaEvent_t e : {sl.ev0, sl.ev1, sl.done}) if (e) cudaEventDestroy(e);
         for (auto& e : sl.hev) if (e) cudaEventDestroy(e);
@@ -1053,6 +1055,22 @@ void lossguide_order(const TreeRec* rec, uint32_t nn, std::vector<uint32_t>& old
     if (next != nn) throw std::runtime_error("device tree is malformed");
 }
 
+void TrainCtx::launch_graph(cudaGraph_t g, int slot) {
+    cudaGraphExec_t& e = tree_exec_[slot];
+    if (e) {
+        cudaGraphExecUpdateResultInfo info{};
+        if (cudaGraphExecUpdate(e, g, &info) != cudaSuccess) {  // another shape: instantiate anew
+            (void)cudaGetLastError();
+            cudaGraphExecDestroy(e);
+            e = nullptr;
+        }
+    }
+    const cudaError_t inst = e ? cudaSuccess : cudaGraphInstantiate(&e, g, 0);
+    cudaGraphDestroy(g);
+    FB_CUDA_CHECK(inst);
+    FB_CUDA_CHECK(cudaGraphLaunch(e, s_));
+}
+
 bool TrainCtx::tree_async(const fbgpu_tree_params& tp) const {
     return tp.grow_policy == 0 || lossguide_is_levelwise(tp);
 }
@@ -1153,14 +1171,7 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
     const bool walk_fast = a.walk_rec != nullptr && max_nodes <= kWalkNodes;
     a.walk = walk_env >= 0 ? (walk_env ? 1u : 0u) : ((n_ <= (4ull << 20) || walk_fast) ? 1u : 0u);
     const uint32_t maxd = tp.max_depth;
-    FB_CUDA_CHECK(cudaEventRecord(S.ev0, s_));
-    int cur = 0;
-    launch_iota(rows_[0].as<uint32_t>(), (uint32_t)n_, s_);
-    a.nodes = nodes_[0].as<NodeInfo>();
-    a.acc_list = acc_list_[0].as<uint32_t>();
-    a.acc_prefix = acc_prefix_[0].as<unsigned long long>();
-    a.chunk_prefix = chunk_prefix_[0].as<uint32_t>();
-    a.rows_cur = rows_[0].as<uint32_t>();
+    const uint32_t W = cat_words_;
     if (rs_mode) {
         // the split reads this rank's block of the reduce-scattered histograms,
         // its node slots hold this rank's bins only
@@ -1170,7 +1181,34 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
         a.feat_hi = rank_feat_lo_[rank_ + 1];
         a.bin_lo = rank_bin_lo_[rank_];
     }
+    // host-side set-up first: from here to the readback nothing allocates,
+    // uploads from pageable memory or waits, so that span can be captured
     set_split_lists(a);
+    S.tree.reserve(sizeof(TreeRec) * max_tree_nodes_ + 4ull * W * max_tree_nodes_ + sizeof(TreeState));
+    S.small.reserve(16 * 16 + 8);
+    // One GPU without per-level statistics: the tree's launches (about 40)
+    // are captured into a CUDA graph and launched as one, so the device runs
+    // them back to back.  The graph is captured again every tree and the
+    // slot's executable graph updated from it (cudaGraphExecUpdate), so it
+    // never replays stale arguments; the capture costs host time that the
+    // pipelined rounds overlap with the device's.  FBGPU_GRAPHS=0 launches
+    // the kernels one by one.
+    static const bool graphs_env = [] {
+        const char* e = std::getenv("FBGPU_GRAPHS");
+        return !(e && std::string(e) == "0");
+    }();
+    // the events and the readback copies stay outside the graph: the host
+    // waits on them, and an event recorded during a capture is a graph
+    // dependency, not one the host can wait for
+    FB_CUDA_CHECK(cudaEventRecord(S.ev0, s_));
+    CaptureGuard capture(s_, graphs_env && !comm_ && !stats_);
+    int cur = 0;
+    launch_iota(rows_[0].as<uint32_t>(), (uint32_t)n_, s_);
+    a.nodes = nodes_[0].as<NodeInfo>();
+    a.acc_list = acc_list_[0].as<uint32_t>();
+    a.acc_prefix = acc_prefix_[0].as<unsigned long long>();
+    a.chunk_prefix = chunk_prefix_[0].as<uint32_t>();
+    a.rows_cur = rows_[0].as<uint32_t>();
     if (root_pending_ && (maxd == 0 || rs_mode)) reduce_root_sum(true);
     launch_tree_init(a, (uint32_t)n_, (uint32_t)cfg_.n_rows_global, sums_.as<unsigned long long>(), s_);
     for (uint32_t d = 0; d < maxd; d++) {
@@ -1266,12 +1304,10 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
     else if (maxd == 0)  // the root is the only leaf
         launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
     FB_CUDA_CHECK(cudaGetLastError());
+    if (capture.on) launch_graph(capture.end(), slot_next_);
     FB_CUDA_CHECK(cudaEventRecord(S.ev1, s_));
     // the result into this slot's pinned buffers, in stream order (the next
     // tree's kernels overwrite the device copies only after these)
-    const uint32_t W = cat_words_;
-    S.tree.reserve(sizeof(TreeRec) * max_tree_nodes_ + 4ull * W * max_tree_nodes_ + sizeof(TreeState));
-    S.small.reserve(16 * 16 + 8);
     TreeRec* hrec = S.tree.as<TreeRec>();
     uint32_t* hcats = reinterpret_cast<uint32_t*>(hrec + max_tree_nodes_);
     TreeState* hst = reinterpret_cast<TreeState*>(hcats + (size_t)W * max_tree_nodes_);

@@ -39,6 +39,30 @@ void dev_free(void* p, size_t cap);
 void* pinned_alloc(size_t n, size_t* cap);
 void pinned_free(void* p, size_t cap);
 
+// Captures the work a stream is given while `on` (end() returns the graph);
+// a capture left open by an exception is ended and discarded.
+struct CaptureGuard {
+    cudaStream_t s;
+    bool on;
+    CaptureGuard(cudaStream_t st, bool enable) : s(st), on(enable) {
+        if (on) FB_CUDA_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+    }
+    cudaGraph_t end() {
+        cudaGraph_t g = nullptr;
+        on = false;
+        FB_CUDA_CHECK(cudaStreamEndCapture(s, &g));
+        return g;
+    }
+    ~CaptureGuard() {
+        if (!on) return;
+        cudaGraph_t g = nullptr;
+        if (cudaStreamEndCapture(s, &g) == cudaSuccess && g) cudaGraphDestroy(g);
+        (void)cudaGetLastError();
+    }
+    CaptureGuard(const CaptureGuard&) = delete;
+    CaptureGuard& operator=(const CaptureGuard&) = delete;
+};
+
 // Owning device allocation; `bytes` is the size asked for.
 struct DevMem {
     void* p = nullptr;
@@ -311,6 +335,8 @@ class TrainCtx {
     ReadSlot slot_[2];
     uint32_t slot_next_ = 0, slots_pending_ = 0;  // the oldest pending slot is (slot_next_ + 2 - pending) % 2
     void wait_event(cudaEvent_t ev);
+    cudaGraphExec_t tree_exec_[2] = {};  // per readback slot: the last captured tree's executable graph
+    void launch_graph(cudaGraph_t g, int slot);
     PinnedMem h_small_;  // 512 B of pinned readback: no pageable copy waits behind a collective
     float last_tree_ms_ = 0.0f;
     bool stats_ = false;
