@@ -102,3 +102,74 @@ def test_two_gpu_models_equal_single_gpu(tmp_path, split_shard):
             assert got == want, f"{case}: rank {r} model differs from the single-GPU model"
     gens = [(tmp_path / f"gens_r{r}.txt").read_text().split() for r in range(world)]
     assert len(gens[0]) == len(CASES) and len(set(gens[0])) == 1 and gens[0] == gens[1]
+
+
+def _stall_worker(rank, world, port, out_dir):
+    """Rank 1 stops taking part between rounds: it stays alive and keeps its
+    communicator and memory, but never calls the next round's collectives
+    (a stalled host).  Rank 0's next round then waits on its level
+    all-reduce until the library's bounded wait (timeout_s) gives up, aborts
+    the communicator (which ends the waiting NCCL kernel) and reports the
+    timeout; later calls report the failed communicator.  Both ranks leave
+    only after rank 0 has seen the error, so no rank's memory goes away
+    under a collective."""
+    import datetime
+    import time
+    import torch.distributed as dist
+    from ferrisboost_b200 import distributed as fbd
+    os.environ["LOCAL_RANK"] = str(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        X, y, _ = _data("logistic_exact")
+        b = fbd.train(CASES["logistic_exact"], X, label=y, num_boost_round=2, timeout_s=3,
+                      return_booster=True)
+        b.model()  # both rounds collected on both ranks
+        dist.barrier()
+        lines = []
+        if rank == 0:
+            t0 = time.monotonic()
+            try:
+                b.update(1)
+                b.model()
+                lines.append("no error")
+            except RuntimeError as e:
+                lines.append(f"first {time.monotonic() - t0:.2f} {e}")
+            try:
+                b.update(1)
+                b.model()
+                lines.append("no error")
+            except RuntimeError as e:
+                lines.append(f"second {e}")
+        dist.barrier()  # rank 1 waits here, outside any collective, until rank 0 is done
+        del b
+        fbd.release_communicators()
+        with open(os.path.join(out_dir, f"stall_r{rank}.txt"), "w") as f:
+            f.write("\n".join(lines))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_stalled_peer_ends_in_timeout_then_failed_communicator(tmp_path, monkeypatch):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import time
+    import torch.multiprocessing as mp
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")  # plain peer transport, no NVLink multicast objects
+    ctx = mp.start_processes(_stall_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.monotonic() + 240
+    while not ctx.join(timeout=5):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.kill()
+            pytest.fail("ranks did not finish within 240 s")
+    lines = (tmp_path / "stall_r0.txt").read_text().splitlines()
+    assert (tmp_path / "stall_r1.txt").exists()
+    assert lines[0].startswith("first "), lines
+    waited = float(lines[0].split()[1])
+    assert 2.5 <= waited <= 60.0, lines
+    assert "within 3000 ms" in lines[0], lines  # the bounded wait's timeout, not another failure
+    assert lines[1].startswith("second ") and "aborted" in lines[1], lines
