@@ -353,6 +353,68 @@ struct SlotArrays {
     uint32_t L;
 };
 
+// The bitonic network of k_chunk_summary over 4096 keys with 1024 threads,
+// thread t holding keys 4t .. 4t + 3 in registers: a compare-exchange at
+// distance j < 4 stays in the thread, 4 <= j <= 64 pairs lanes of one warp
+// (shuffles), and only j >= 128 goes through shared memory (15 of the 78
+// stages).  Every stage compares the same pairs in the same direction as the
+// shared-memory loop, so the sorted keys are the same.  Ends with the keys
+// in keys[0 .. 4096) and the CTA synced.
+__device__ void bitonic_sort_4096(const float* __restrict__ src, uint32_t cnt, uint32_t* keys) {
+    const uint32_t t = threadIdx.x, lane = t & 31u;
+    uint32_t x[4];
+#pragma unroll
+    for (uint32_t e = 0; e < 4; e++) {
+        const uint32_t i = 4 * t + e;
+        x[e] = i < cnt ? f2key(src[i]) : 0xffffffffu;
+    }
+    for (uint32_t k = 2; k <= 4096; k <<= 1) {
+        uint32_t j = k >> 1;
+        if (j >= 128) {
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) keys[4 * t + e] = x[e];
+            __syncthreads();
+            for (; j >= 128; j >>= 1) {
+#pragma unroll
+                for (uint32_t h = 0; h < 2; h++) {
+                    const uint32_t p = t + h * 1024u;
+                    const uint32_t i = 2 * p - (p & (j - 1)), ixj = i + j;
+                    const uint32_t a = keys[i], b = keys[ixj];
+                    const bool up = (i & k) == 0;
+                    if ((a > b) == up) { keys[i] = b; keys[ixj] = a; }
+                }
+                __syncthreads();
+            }
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) x[e] = keys[4 * t + e];
+        }
+        for (; j >= 4; j >>= 1) {
+            const uint32_t d = j >> 2;  // partner lane offset
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) {
+                const uint32_t i = 4 * t + e;
+                const uint32_t y = __shfl_xor_sync(0xffffffffu, x[e], d);
+                const bool lower = (i & j) == 0, up = (i & k) == 0;
+                x[e] = (lower == up) ? min(x[e], y) : max(x[e], y);
+            }
+        }
+        (void)lane;
+        for (; j >= 1; j >>= 1) {
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) {
+                if (e & j) continue;
+                const uint32_t i = 4 * t + e;
+                const bool up = (i & k) == 0;
+                const uint32_t a = x[e], b = x[e + j];
+                if ((a > b) == up) { x[e] = b; x[e + j] = a; }
+            }
+        }
+    }
+#pragma unroll
+    for (uint32_t e = 0; e < 4; e++) keys[4 * t + e] = x[e];
+    __syncthreads();
+}
+
 // build_summary (sketch.rs:305-329) of one chunk with unit weights: sorted,
 // equal values grouped, rmin = values before the group, rmax = rmin + count.
 __global__ void __launch_bounds__(kSkThreads) k_chunk_summary(const float* __restrict__ vals,
@@ -370,18 +432,23 @@ __global__ void __launch_bounds__(kSkThreads) k_chunk_summary(const float* __res
     uint32_t P = 1;
     while (P < cnt) P <<= 1;
     const float* src = vals + vbase[jb] + first;
+    if (P == 4 * kSkThreads && blockDim.x == kSkThreads) {
+        bitonic_sort_4096(src, cnt, keys);
+    } else {
     for (uint32_t i = threadIdx.x; i < P; i += blockDim.x) keys[i] = i < cnt ? f2key(src[i]) : 0xffffffffu;
     __syncthreads();
     for (uint32_t k = 2; k <= P; k <<= 1) {
         for (uint32_t j = k >> 1; j > 0; j >>= 1) {
             for (uint32_t p = threadIdx.x; p < (P >> 1); p += blockDim.x) {
-                const uint32_t i = (p / j) * 2 * j + (p % j), ixj = i + j;
+                // p = q j + r (r < j, j a power of two): i = 2 q j + r = 2 p - r
+                const uint32_t i = 2 * p - (p & (j - 1)), ixj = i + j;
                 const uint32_t a = keys[i], b = keys[ixj];
                 const bool up = (i & k) == 0;
                 if ((a > b) == up) { keys[i] = b; keys[ixj] = a; }
             }
             __syncthreads();
         }
+    }
     }
     const uint32_t slot = sbase[jb] + c;
     float* ov = S.v + (size_t)slot * L;
@@ -423,6 +490,41 @@ __global__ void __launch_bounds__(kSkThreads) k_merge_level(SlotArrays S, const 
         SumMut A = sum_at(S.v, S.lo, S.hi, (size_t)a * L);
         SumMut B = sum_at(S.v, S.lo, S.hi, (size_t)b * L);
         const uint32_t m = cta_merge(A.ref(), na, B.ref(), nb, M, tp, sh);
+        const uint32_t no = cta_prune(M.ref(), m, A, L, shi, &sflag);
+        if (threadIdx.x == 0) S.count[a] = no;
+        __syncthreads();
+    }
+}
+
+// The same level with each task's two summaries and its merge held in shared
+// memory (13 L + 1 words: L <= kMergeSmemMaxL), so the binary searches of the
+// merge and the compress read shared memory instead of L2.  One CTA per SM.
+constexpr uint32_t kMergeSmemMaxL = 4096;
+__global__ void __launch_bounds__(kSkThreads) k_merge_level_smem(SlotArrays S, const uint32_t* __restrict__ task_left,
+                                                                 const uint32_t* __restrict__ task_right,
+                                                                 uint32_t n_tasks) {
+    extern __shared__ float msm[];
+    __shared__ uint32_t sh[32];
+    __shared__ int shi[32];
+    __shared__ uint32_t sflag;
+    const uint32_t L = S.L;
+    SumMut As = sum_at(msm, msm + L, msm + 2 * L, 0);
+    SumMut Bs = sum_at(msm + 3 * L, msm + 4 * L, msm + 5 * L, 0);
+    SumMut M = sum_at(msm + 6 * L, msm + 8 * L, msm + 10 * L, 0);
+    uint32_t* tp = reinterpret_cast<uint32_t*>(msm + 12 * L);
+    for (uint32_t t = blockIdx.x; t < n_tasks; t += gridDim.x) {
+        const uint32_t a = task_left[t], b = task_right[t];
+        const uint32_t na = S.count[a], nb = S.count[b];
+        SumMut A = sum_at(S.v, S.lo, S.hi, (size_t)a * L);
+        const SumRef B = sum_at(S.v, S.lo, S.hi, (size_t)b * L).ref();
+        for (uint32_t i = threadIdx.x; i < na; i += blockDim.x) {
+            As.v[i] = A.v[i]; As.lo[i] = A.lo[i]; As.hi[i] = A.hi[i];
+        }
+        for (uint32_t i = threadIdx.x; i < nb; i += blockDim.x) {
+            Bs.v[i] = B.v[i]; Bs.lo[i] = B.lo[i]; Bs.hi[i] = B.hi[i];
+        }
+        __syncthreads();
+        const uint32_t m = cta_merge(As.ref(), na, Bs.ref(), nb, M, tp, sh);
         const uint32_t no = cta_prune(M.ref(), m, A, L, shi, &sflag);
         if (threadIdx.x == 0) S.count[a] = no;
         __syncthreads();
@@ -737,6 +839,16 @@ void DeviceMatrix::numeric_cuts(uint32_t max_bin, const std::vector<uint32_t>& f
         // levels 1..: node k of level l lives in the slot of its first chunk
         const uint32_t max_ch = *std::max_element(nch.begin(), nch.end());
         const uint32_t grid_cap = 148u * 2u;
+        // shared-memory merges when the summaries fit (max_bin <= 256)
+        int dev = 0, sms = 148, optin = 0;
+        FB_CUDA_CHECK(cudaGetDevice(&dev));
+        FB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        FB_CUDA_CHECK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        size_t merge_smem = (size_t)(13 * L + 1) * 4;
+        if (L > kMergeSmemMaxL || merge_smem + 1024 > (size_t)optin) merge_smem = 0;
+        if (merge_smem)
+            FB_CUDA_CHECK(cudaFuncSetAttribute(k_merge_level_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)merge_smem));
         DevMem d_scr, d_tscr, d_tl, d_tr;
         for (uint32_t l = 1; (1ull << l) <= max_ch; l++) {
             std::vector<uint32_t> tl, tr;
@@ -747,13 +859,17 @@ void DeviceMatrix::numeric_cuts(uint32_t max_bin, const std::vector<uint32_t>& f
                 }
             const uint32_t nt = (uint32_t)tl.size();
             const uint32_t grid = std::min(nt, grid_cap);
-            if (d_scr.bytes < (size_t)grid * 6 * L * 4) d_scr.alloc((size_t)grid * 6 * L * 4);
-            if (d_tscr.bytes < (size_t)grid * (L + 1) * 4) d_tscr.alloc((size_t)grid * (L + 1) * 4);
+            if (!merge_smem && d_scr.bytes < (size_t)grid * 6 * L * 4) d_scr.alloc((size_t)grid * 6 * L * 4);
+            if (!merge_smem && d_tscr.bytes < (size_t)grid * (L + 1) * 4) d_tscr.alloc((size_t)grid * (L + 1) * 4);
             upload(d_tl, tl, s_);
             upload(d_tr, tr, s_);
             count_launch();
-            k_merge_level<<<grid, kSkThreads, 0, s_>>>(S, d_tl.as<uint32_t>(), d_tr.as<uint32_t>(), nt,
-                                                       d_scr.as<float>(), d_tscr.as<uint32_t>());
+            if (merge_smem)
+                k_merge_level_smem<<<std::min(nt, (uint32_t)sms), kSkThreads, merge_smem, s_>>>(
+                    S, d_tl.as<uint32_t>(), d_tr.as<uint32_t>(), nt);
+            else
+                k_merge_level<<<grid, kSkThreads, 0, s_>>>(S, d_tl.as<uint32_t>(), d_tr.as<uint32_t>(), nt,
+                                                           d_scr.as<float>(), d_tscr.as<uint32_t>());
             FB_CUDA_CHECK(cudaGetLastError());
             FB_CUDA_CHECK(cudaStreamSynchronize(s_));  // the task lists are reused
         }
