@@ -127,6 +127,7 @@ SIGNATURES = {
     "fb_sketch_features_device": (C.c_int64, [f32p, C.c_uint64, C.c_uint32, C.c_uint32, f32p, u8p, u32p, C.c_uint32,
                                               C.c_int32, C.c_int32, f32p, u32p, C.c_uint64]),
     "fb_label_mean": (C.c_float, [f32p, f32p, C.c_uint64]),
+    "fb_label_mean_f64": (C.c_double, [f32p, C.c_uint64]),
     "fb_initial_base_score": (C.c_float, [C.c_int32, f32p, f32p, C.c_uint64, C.c_float]),
     "fb_class_margins": (C.c_int32, [f32p, f32p, C.c_uint64, C.c_uint32, f32p]),
     "fb_dataset_free": (None, [P]),

@@ -769,14 +769,77 @@ std::vector<uint8_t> sample_features(uint32_t nf, float rate, uint64_t seed, uin
 }
 
 // ---------------------------------------------------------------- booster
-// objective.rs:41-61 label mean (FitInterceptGlmLike), the base_score when
-// none is given: a sequential f64 sum in row order.
-float label_mean(const float* y, const float* w, uint64_t n) {
-    if (!w) {
-        double acc = 0.0, nn = (double)n;
-        for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / nn;
-        return (float)acc;
+// The f64 sequence a_0 = +0, a_(j+1) = a_j + t (each sum rounded to nearest,
+// ties to even), after k steps, without k dependent additions.  Inside one
+// binade [2^E, 2^(E+1)) every sum rounds to a multiple of u = 2^(E-52), so
+// a_(j+1) = a_j + RN(t / u) u: the increment r is the same at every step,
+// except when t / u is an odd multiple of 1/2 (a tie); then it depends on the
+// parity of a_j / u until one step has made a_j / u even, and is constant
+// after it.  So: single steps until two consecutive increments agree (which
+// rules out the parity case), then a jump of s steps of r while every
+// unrounded sum stays at least one u below the binade's top; the binade edges
+// and subnormal values take single steps.
+double repeated_sum(double t, uint64_t k) {
+    const bool neg = t < 0.0;
+    if (neg) t = -t;  // rounding to nearest is symmetric: the sequence of -t is the negated one
+    double a = 0.0;
+    while (k > 0) {
+        const double n1 = a + t;
+        k--;
+        if (n1 == a) break;  // a + t rounds back to a: so do all further steps
+        a = n1;
+        if (k == 0 || !std::isfinite(a) || a < std::numeric_limits<double>::min()) continue;
+        const double r1 = (a + t) - a;  // exact: both are multiples of u and r1 <= a
+        const double a1 = a + r1;
+        const int E = std::ilogb(a);
+        if (r1 <= 0.0 || std::ilogb(a1) != E || (a1 + t) - a1 != r1) continue;
+        const double u = std::ldexp(1.0, E - 52);
+        const double A = a / u, R = r1 / u, T = t / u;      // A, R integers below 2^53
+        const double X = 9007199254740991.0 - A;             // 2^53 - 1 - A, exact
+        const double sd = std::floor((X - T) / R) - 1.0;     // one fewer than the bound allows, and one
+        if (!(sd >= 1.0)) continue;                           // more for the rounding of the division
+        const uint64_t s = sd >= (double)k ? k : (uint64_t)sd;
+        a = a + (double)s * r1;  // a multiple of u below 2^(E+1): exact
+        k -= s;
     }
+    return neg ? -a : a;
+}
+
+// objective.rs:41-61 label mean (FitInterceptGlmLike), the base_score when
+// none is given: a sequential f64 sum in row order.  Labels that take one
+// value v besides zero (binary labels) make every term 0 or t = v / n, and
+// adding a zero term leaves the sum as it is, so the sum is the k-fold
+// sequence of t (k = rows labelled v): repeated_sum gives the same f64 value
+// as the row loop without its 11M dependent additions at configs[1].
+double label_mean_f64(const float* y, uint64_t n) {
+    const double nn = (double)n;
+    uint64_t first = 0;
+    uint32_t vb = 0;
+    for (; first < n; first++) {
+        std::memcpy(&vb, y + first, 4);
+        if (vb & 0x7fffffffu) break;
+    }
+    if (first == n) return 0.0;  // every term is a zero
+    const float v = y[first];
+    if (std::isfinite(v)) {
+        int other = 0;
+        long long k = 0;
+#pragma omp parallel for schedule(static) reduction(+ : k) reduction(| : other)
+        for (long long i = (long long)first; i < (long long)n; i++) {
+            uint32_t b;
+            std::memcpy(&b, y + i, 4);
+            k += b == vb;
+            other |= (b & 0x7fffffffu) != 0 && b != vb;
+        }
+        if (!other) return repeated_sum((double)v / nn, (uint64_t)k);
+    }
+    double acc = 0.0;
+    for (uint64_t i = 0; i < n; i++) acc = acc + (double)y[i] / nn;
+    return acc;
+}
+
+float label_mean(const float* y, const float* w, uint64_t n) {
+    if (!w) return (float)label_mean_f64(y, n);
     double sw = 0.0, acc = 0.0;
     for (uint64_t i = 0; i < n; i++) sw = sw + (double)w[i];
     if (sw <= 0.0) return 0.5f;
@@ -1357,6 +1420,8 @@ float fb_initial_base_score(int32_t objective, const float* labels, const float*
 float fb_label_mean(const float* labels, const float* weights, uint64_t n) {
     return fbe::label_mean(labels, weights, n);
 }
+
+double fb_label_mean_f64(const float* labels, uint64_t n) { return fbe::label_mean_f64(labels, n); }
 
 int32_t fb_class_margins(const float* labels, const float* weights, uint64_t n, uint32_t K, float* out) {
     return fbe::guarded([&]() -> int32_t {

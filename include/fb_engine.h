@@ -109,6 +109,11 @@ int64_t fb_sketch_features_device(const float* X, uint64_t n, uint32_t F, uint32
  * (weighted when weights != NULL), summed in f64 in row order
  * (src/objective.rs:41-61). */
 float fb_label_mean(const float* labels, const float* weights, uint64_t n);
+/* The unweighted label mean's f64 accumulator before its rounding to f32
+ * (objective.rs:41-61: acc = acc + label / n in row order), the value
+ * fb_label_mean rounds.  Exposed so that its exactness against the row loop
+ * can be checked at f64. */
+double fb_label_mean_f64(const float* labels, uint64_t n);
 /* The base score a booster takes when base_score is not given (objective.rs:
  * 403-493 initial_base_score; objective 0 squared error, 1 logistic): the
  * label mean, or with |scale_pos_weight - 1| > 1e-6 one Newton step from
