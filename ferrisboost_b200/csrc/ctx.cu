@@ -281,8 +281,9 @@ TrainCtx::~TrainCtx() {
     if (s_) cudaStreamSynchronize(s_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
-    for (cudaGraphExec_t& e : tree_exec_)
-        if (e) cudaGraphExecDestroy(e);
+    for (auto& slot : tree_exec_)
+        for (cudaGraphExec_t& e : slot)
+            if (e) cudaGraphExecDestroy(e);
     for (ReadSlot& sl : slot_) {
         for (cudaEvent_t e : {sl.ev0, sl.ev1, sl.done}) if (e) cudaEventDestroy(e);
         for (auto& e : sl.hev) if (e) cudaEventDestroy(e);
@@ -1055,8 +1056,9 @@ void lossguide_order(const TreeRec* rec, uint32_t nn, std::vector<uint32_t>& old
     if (next != nn) throw std::runtime_error("device tree is malformed");
 }
 
-void TrainCtx::launch_graph(cudaGraph_t g, int slot) {
-    cudaGraphExec_t& e = tree_exec_[slot];
+void TrainCtx::launch_graph(cudaGraph_t g, int slot, int segment) {
+    if (segment >= kTreeSegments) throw std::runtime_error("more graph segments than a tree has levels");
+    cudaGraphExec_t& e = tree_exec_[slot][segment];
     if (e) {
         cudaGraphExecUpdateResultInfo info{};
         if (cudaGraphExecUpdate(e, g, &info) != cudaSuccess) {  // another shape: instantiate anew
@@ -1186,13 +1188,14 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
     set_split_lists(a);
     S.tree.reserve(sizeof(TreeRec) * max_tree_nodes_ + 4ull * W * max_tree_nodes_ + sizeof(TreeState));
     S.small.reserve(16 * 16 + 8);
-    // One GPU without per-level statistics: the tree's launches (about 40)
-    // are captured into a CUDA graph and launched as one, so the device runs
-    // them back to back.  The graph is captured again every tree and the
-    // slot's executable graph updated from it (cudaGraphExecUpdate), so it
-    // never replays stale arguments; the capture costs host time that the
-    // pipelined rounds overlap with the device's.  FBGPU_GRAPHS=0 launches
-    // the kernels one by one.
+    // Without per-level statistics the tree's launches (about 40) are
+    // captured into CUDA graphs and launched as one graph per segment, so the
+    // device runs them back to back: one segment per tree on one GPU.  The
+    // graphs are captured again every tree and the slot's executable graphs
+    // updated from them (cudaGraphExecUpdate), so they never replay stale
+    // arguments; the capture costs host time that the pipelined rounds
+    // overlap with the device's.  FBGPU_GRAPHS=0 launches the kernels one by
+    // one.
     static const bool graphs_env = [] {
         const char* e = std::getenv("FBGPU_GRAPHS");
         return !(e && std::string(e) == "0");
@@ -1201,7 +1204,13 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
     // waits on them, and an event recorded during a capture is a graph
     // dependency, not one the host can wait for
     FB_CUDA_CHECK(cudaEventRecord(S.ev0, s_));
-    CaptureGuard capture(s_, graphs_env && !comm_ && !stats_);
+    // Sharded: the collectives stay outside the graphs.  Each span of kernels
+    // between two of them (the level's split, partition and the next level's
+    // histograms) is captured and launched as one segment.  The
+    // feature-sharded form and a root-only tree keep launching kernel by kernel.
+    const bool graphs = graphs_env && !stats_ && !rs_mode && !(comm_ && root_pending_ && maxd == 0);
+    CaptureGuard capture(s_, graphs);
+    int segment = 0;
     int cur = 0;
     launch_iota(rows_[0].as<uint32_t>(), (uint32_t)n_, s_);
     a.nodes = nodes_[0].as<NodeInfo>();
@@ -1261,7 +1270,9 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
         } else {
             launch_histograms(a.rows_cur, a.nodes, a.acc_list, a.acc_prefix, n_);
             if (stats_ && comm_ && d < 15) FB_CUDA_CHECK(cudaEventRecord(S.hevc[d], s_));
+            if (comm_ && capture.on) launch_graph(capture.end(), slot_next_, segment++);
             allreduce_u64(hist_acc_.p, 2ull * a.slot_pairs * max_acc + (root_rides ? 2 : 0), false);
+            if (comm_ && graphs) capture.begin();
         }
         if (root_rides) {
             FB_CUDA_CHECK(cudaMemcpyAsync(sums_.p, hist_acc_.as<unsigned long long>() + 2ull * a.slot_pairs, 16,
@@ -1304,7 +1315,7 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
     else if (maxd == 0)  // the root is the only leaf
         launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);
     FB_CUDA_CHECK(cudaGetLastError());
-    if (capture.on) launch_graph(capture.end(), slot_next_);
+    if (capture.on) launch_graph(capture.end(), slot_next_, segment);
     FB_CUDA_CHECK(cudaEventRecord(S.ev1, s_));
     // the result into this slot's pinned buffers, in stream order (the next
     // tree's kernels overwrite the device copies only after these)

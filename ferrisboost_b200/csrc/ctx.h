@@ -44,8 +44,12 @@ void pinned_free(void* p, size_t cap);
 struct CaptureGuard {
     cudaStream_t s;
     bool on;
-    CaptureGuard(cudaStream_t st, bool enable) : s(st), on(enable) {
-        if (on) FB_CUDA_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+    CaptureGuard(cudaStream_t st, bool enable) : s(st), on(false) {
+        if (enable) begin();
+    }
+    void begin() {
+        FB_CUDA_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+        on = true;
     }
     cudaGraph_t end() {
         cudaGraph_t g = nullptr;
@@ -335,8 +339,12 @@ class TrainCtx {
     ReadSlot slot_[2];
     uint32_t slot_next_ = 0, slots_pending_ = 0;  // the oldest pending slot is (slot_next_ + 2 - pending) % 2
     void wait_event(cudaEvent_t ev);
-    cudaGraphExec_t tree_exec_[2] = {};  // per readback slot: the last captured tree's executable graph
-    void launch_graph(cudaGraph_t g, int slot);
+    // per readback slot and graph segment (one per level's span between two
+    // collectives when sharded, else one per tree): the last captured
+    // executable graph
+    static constexpr int kTreeSegments = 17;
+    cudaGraphExec_t tree_exec_[2][kTreeSegments] = {};
+    void launch_graph(cudaGraph_t g, int slot, int segment);
     PinnedMem h_small_;  // 512 B of pinned readback: no pageable copy waits behind a collective
     float last_tree_ms_ = 0.0f;
     bool stats_ = false;
