@@ -433,6 +433,7 @@ void TrainCtx::upload_block(const uint32_t* feat_ids, uint32_t n_feats, uint32_t
 }
 
 void TrainCtx::set_labels(const float* labels, const float* weights, const float* base_rows, float base_margin) {
+    next_grad_.set = fused_grad_.set = false;
     FB_CUDA_CHECK(cudaMemcpyAsync(label_.p, labels, n_ * 4, cudaMemcpyHostToDevice, s_));
     has_weight_ = weights != nullptr;
     if (weights) {
@@ -548,16 +549,29 @@ void TrainCtx::check_scale_error(const unsigned long long* host_err) {
     if (*host_err) throw InputError("non-finite gradient or Hessian");
 }
 
+void TrainCtx::set_next_gradient(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree) {
+    next_grad_.set = K_ == 1 && (objective == 0 || objective == 1) && (fast || objective == 0 || exptab_.p);
+    next_grad_.objective = objective;
+    next_grad_.fast = fast ? 1 : 0;
+    next_grad_.th = th;
+    next_grad_.seed = seed;
+    next_grad_.tree = tree;
+}
+
 void TrainCtx::round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
                             int64_t* sum_out) {
-    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, 32, s_));
+    // the previous tree's walk already wrote this round's gradient pairs and
+    // their bounds (same parameters, margins untouched since)
+    const bool done = fused_grad_.same(objective, fast ? 1 : 0, th, seed, tree);
+    fused_grad_.set = false;
+    FB_CUDA_CHECK(cudaMemsetAsync(sums_.p, 0, done ? 16 : 32, s_));
     GradArgs a = grad_args();
     a.sub_th = th; a.sub_seed = seed; a.sub_tree = tree;
     a.objective = objective;
     if (!fast && objective == 1 && !a.exptab)
         throw InputError("exact logistic gradients on the device need the verified host-expf table; "
                          "use fbgpu_round_from_exp with host exp values");
-    launch_gradient_max(a, fast ? 1 : (objective == 1 ? 2 : 0), s_);
+    if (!done) launch_gradient_max(a, fast ? 1 : (objective == 1 ? 2 : 0), s_);
     allreduce_u64(a.maxbits, 2, true);
     launch_scales(a.maxbits, fast != 0);
     launch_quantize(a, s_);
@@ -578,6 +592,7 @@ void TrainCtx::read_scales_sum(double* scales_out, int64_t* sum_out) {
 }
 
 void TrainCtx::set_outputs(uint32_t K, const float* class_margins) {
+    next_grad_.set = fused_grad_.set = false;
     if (K < 2) throw InputError("a multiclass context needs at least 2 classes");
     K_ = K;
     pred_col_ = 0;
@@ -1098,6 +1113,9 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
 }
 
 void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* lg_out) {
+    const NextGrad ng = next_grad_;
+    next_grad_.set = false;
+    fused_grad_.set = false;
     ensure_features();
     if (tp.max_depth > 14) throw InputError("max_depth must be in 0..=14");
     const bool lossguide = tp.grow_policy != 0;
@@ -1310,7 +1328,16 @@ void TrainCtx::build_tree_launch(const fbgpu_tree_params& tp, const uint8_t* ena
     a.chunk_prefix = chunk_prefix_[cur].as<uint32_t>();
     a.rows_cur = rows_[cur].as<uint32_t>();
     const uint32_t last_m = (uint32_t)std::min<uint64_t>(1ull << maxd, max_level_nodes_);
-    if (a.walk)
+    if (a.walk && ng.set) {
+        // the next round's gradients from the new margins, in the walk; its
+        // bounds start from zero (this round's were read by its scales)
+        FB_CUDA_CHECK(cudaMemsetAsync(sums_.as<unsigned long long>() + 2, 0, 16, s_));
+        GradArgs ga = grad_args();
+        ga.sub_th = ng.th; ga.sub_seed = ng.seed; ga.sub_tree = ng.tree;
+        ga.objective = ng.objective;
+        launch_tree_walk(a, (uint32_t)n_, s_, &ga, ng.fast ? 1 : (ng.objective == 1 ? 2 : 0));
+        fused_grad_ = ng;
+    } else if (a.walk)
         launch_tree_walk(a, (uint32_t)n_, s_);
     else if (maxd == 0)  // the root is the only leaf
         launch_leaf_final(a, ceil_div(std::max<uint64_t>(n_, 1), kChunkRows) + last_m, s_);

@@ -133,6 +133,12 @@ class TrainCtx {
                         const double* scales);
     void round_device(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree, double* scales_out,
                       int64_t* sum_out);
+    // The parameters of the round_device call that will follow the next
+    // launched tree.  When that tree ends with the tree walk, the walk also
+    // computes that round's gradient pairs and bounds from the new margins,
+    // and the matching round_device call starts at its scales.  Applies to
+    // one output, squared error or logistic, with gradients on the device.
+    void set_next_gradient(int objective, int fast, uint64_t th, uint64_t seed, uint64_t tree);
 
     void build_tree(const fbgpu_tree_params& tp, const uint8_t* enabled, fbgpu_tree_out* out);
     // A tree in two halves, for trees that need no host decision while they
@@ -150,6 +156,7 @@ class TrainCtx {
     void abandon_trees() {
         slots_pending_ = 0;
         scale_err_pending_ = false;
+        next_grad_.set = fused_grad_.set = false;
         sync();
     }
 
@@ -165,7 +172,10 @@ class TrainCtx {
     void quantize_class(uint32_t k, uint64_t th, uint64_t seed, uint64_t tree, int fast, double* scales_out = nullptr,
                         int64_t* sum_out = nullptr);
     // The margin column the next build_tree adds its leaf values to.
-    void set_pred_column(uint32_t k) { pred_col_ = k; }
+    void set_pred_column(uint32_t k) {
+        pred_col_ = k;
+        next_grad_.set = fused_grad_.set = false;
+    }
 
     // Row sharding over several GPUs: one context per GPU, one NCCL
     // communicator per context (ranks in the same order on every GPU).
@@ -283,6 +293,16 @@ class TrainCtx {
     // rows / gradients
     DevMem label_, weight_, pred_, gpair_f32_, host_exp_, fixed_;
     uint32_t K_ = 1, pred_col_ = 0;  // margin columns (classes) and the one the tree updates
+    struct NextGrad {
+        bool set = false;
+        int objective = 0, fast = 0;
+        uint64_t th = 0, seed = 0, tree = 0;
+        bool same(int o, int f, uint64_t t, uint64_t s, uint64_t r) const {
+            return set && objective == o && fast == f && th == t && seed == s && tree == r;
+        }
+    };
+    NextGrad next_grad_;   // for the next launched tree's walk
+    NextGrad fused_grad_;  // the round whose gradients the last tree's walk computed
     DevMem gp_multi_;                 // multiclass: K x n f32 gradient pairs of the round
     DevMem sums_;  // [0..1] root sum, [2..3] max bits, [4..5] scales (double), [6] scale error word
     // exact scales on the device: the row count's exception list (qscale.h)

@@ -1183,6 +1183,8 @@ void launch_round(Booster& b, uint32_t round) {
     fbg::TrainCtx& ctx = *b.ctx;
     ctx.round_device(p.objective, p.gpu_math == 1 ? 1 : 0, threshold_for(p.subsample), p.seed, round, nullptr,
                      nullptr);
+    // the tree's walk may compute round + 1's gradients from its margins
+    ctx.set_next_gradient(p.objective, p.gpu_math == 1 ? 1 : 0, threshold_for(p.subsample), p.seed, round + 1);
     std::vector<uint8_t> en = sample_features(b.d->F, p.colsample_bytree, p.seed, round);
     ctx.build_tree_launch(tree_params(b), p.colsample_bytree < 1.0f ? en.data() : nullptr);
 }

@@ -231,7 +231,8 @@ __global__ void k_mask_max(GradArgs a) {
 // exact mode (reproduced on the device); in fast mode fexp_core alone (fexp.h:
 // an f64 evaluation rounded once to f32, which differs from glibc on about
 // 0.004 % of the inputs, by one unit in the last place).
-__device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, float e, float& g, float& h) {
+// `m` is the row's margin (read by squared error only).
+__device__ __forceinline__ void row_gradient_m(const GradArgs& a, uint32_t i, float e, float m, float& g, float& h) {
     float y = a.label[i];
     if (a.objective == 1) {
         float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
@@ -239,7 +240,7 @@ __device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, floa
         g = __fsub_rn(s, y);
         h = hh < 1e-16f ? 1e-16f : hh;
     } else {
-        g = __fsub_rn(a.pred[i], y);
+        g = __fsub_rn(m, y);
         h = 1.0f;
     }
     if (a.weight) {  // training/mod.rs:5498-5505 weighted
@@ -248,6 +249,9 @@ __device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, floa
         h = __fmul_rn(h, w);
     }
     if (!row_selected(a.row0 + i, a.sub_th, a.sub_seed, a.sub_tree)) { g = 0.0f; h = 0.0f; }
+}
+__device__ __forceinline__ void row_gradient(const GradArgs& a, uint32_t i, float e, float& g, float& h) {
+    row_gradient_m(a, i, e, a.objective == 1 ? 0.0f : a.pred[i], g, h);
 }
 
 // The host C library's expf on the device: fexp_core, except on the inputs the
@@ -2074,8 +2078,12 @@ struct alignas(16) WalkNode {
 static_assert(sizeof(WalkNode) == 16, "WalkNode layout");
 
 // WORDS: 32-bit words staged per row (records of up to 4 * WORDS bytes).
-template <uint32_t WORDS>
-__global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_t n_rows) {
+// GRAD: the walk also computes the next round's gradient pairs from the new
+// margins (what k_gradient_max would compute at the start of that round, in
+// mode gmode: 1 fexp_core alone, 2 the host expf reproduced) and folds their
+// bounds into ga.maxbits, so that round starts at its scales.
+template <uint32_t WORDS, bool GRAD>
+__global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_t n_rows, GradArgs ga, int gmode) {
     __shared__ WalkNode wn[kWalkNodes];
     __shared__ uint32_t stage[kWalkThreads * (WORDS + 1)];
     __shared__ uint32_t plain;  // every split numeric on one-byte bins, right child = left + 1
@@ -2143,6 +2151,19 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
     // an add per level
     const bool fast = staged && plain != 0u;
     const uint4* wn4 = reinterpret_cast<const uint4*>(wn);
+    double mg = 0.0, mh = 0.0;  // GRAD: bounds of this thread's gradient pairs
+    auto next_gradient = [&](uint32_t r, float m) {
+        float e = 0.0f;
+        if (ga.objective == 1) {
+            const float x = -m;
+            e = gmode == 2 ? host_expf(x, ga.exptab, ga.exp_probes) : fbx::fexp_core(x);
+        }
+        float g, h;
+        row_gradient_m(ga, r, e, m, g, h);
+        reinterpret_cast<float2*>(ga.gpair_f32)[r] = make_float2(g, h);
+        mg = fmax(mg, bound_of(g));
+        mh = fmax(mh, bound_of(h));
+    };
     for (uint32_t base = blockIdx.x * blockDim.x; base < n_rows; base += step) {
         const uint32_t r = base + threadIdx.x;
         if (staged) {
@@ -2159,9 +2180,15 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
                     const bool left = bin == q.z ? (q.y & (2u << 16)) != 0u : bin < (q.y & 0xffffu);
                     q = wn4[(q.x & 0xffffu) + (left ? 0u : 1u)];
                 }
-                if (q.y & (1u << 16)) a.pred[r] = __fadd_rn(pv, __uint_as_float(q.z));
+                float m = pv;
+                if (q.y & (1u << 16)) {
+                    m = __fadd_rn(pv, __uint_as_float(q.z));
+                    a.pred[r] = m;
+                }
+                if (GRAD) next_gradient(r, m);
             }
         } else if (r < n_rows) {
+            float m = pv;
             uint32_t node = 0;
             for (uint32_t depth = 0; depth < 64; depth++) {  // trees are at most 15 levels deep
                 uint32_t flags, sbin, missing, width, left_id, right_id, bin;
@@ -2202,7 +2229,8 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
                     }
                 }
                 if (flags & 1u) {
-                    a.pred[r] = __fadd_rn(pv, leaf);
+                    m = __fadd_rn(pv, leaf);
+                    a.pred[r] = m;
                     break;
                 }
                 bool left;
@@ -2211,9 +2239,11 @@ __global__ void __launch_bounds__(kWalkThreads) k_tree_walk(LevelArgs a, uint32_
                 else left = bin < sbin;
                 node = left ? left_id : right_id;
             }
+            if (GRAD) next_gradient(r, m);
         }
         if (staged) __syncthreads();
     }
+    if (GRAD) fold_max(mg, mh, ga.maxbits);
 }
 
 // Root of a new tree (training/mod.rs:3466-3469, 3499-3501).
@@ -2494,17 +2524,30 @@ void launch_part_level(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) 
     count_launch();
     k_part_level<<<max_chunks, kPartThreads, 0, s>>>(a);
 }
-void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s) {
+void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s, const GradArgs* next_grad, int gmode) {
     if (n_rows == 0) return;
     count_launch();
     // one resident wave: every CTA takes the same number of steps, so a grid
     // beyond what the SMs hold at once would run a second, nearly empty wave
-    static const uint32_t wave8 = resident_grid(reinterpret_cast<const void*>(k_tree_walk<8>), kWalkThreads);
-    static const uint32_t wave16 = resident_grid(reinterpret_cast<const void*>(k_tree_walk<16>), kWalkThreads);
+    static const uint32_t wave8 =
+        resident_grid(reinterpret_cast<const void*>(k_tree_walk<8, false>), kWalkThreads);
+    static const uint32_t wave16 =
+        resident_grid(reinterpret_cast<const void*>(k_tree_walk<16, false>), kWalkThreads);
+    static const uint32_t wave8g = resident_grid(reinterpret_cast<const void*>(k_tree_walk<8, true>), kWalkThreads);
+    static const uint32_t wave16g =
+        resident_grid(reinterpret_cast<const void*>(k_tree_walk<16, true>), kWalkThreads);
     const bool narrow = a.walk_rec == nullptr || a.walk_stride <= 32;
-    const uint32_t blocks = std::min<uint32_t>((n_rows + kWalkThreads - 1) / kWalkThreads, narrow ? wave8 : wave16);
-    if (narrow) k_tree_walk<8><<<blocks, kWalkThreads, 0, s>>>(a, n_rows);
-    else k_tree_walk<16><<<blocks, kWalkThreads, 0, s>>>(a, n_rows);
+    const uint32_t want = (n_rows + kWalkThreads - 1) / kWalkThreads;
+    if (next_grad) {
+        const uint32_t blocks = std::min<uint32_t>(want, narrow ? wave8g : wave16g);
+        if (narrow) k_tree_walk<8, true><<<blocks, kWalkThreads, 0, s>>>(a, n_rows, *next_grad, gmode);
+        else k_tree_walk<16, true><<<blocks, kWalkThreads, 0, s>>>(a, n_rows, *next_grad, gmode);
+        return;
+    }
+    const GradArgs none{};
+    const uint32_t blocks = std::min<uint32_t>(want, narrow ? wave8 : wave16);
+    if (narrow) k_tree_walk<8, false><<<blocks, kWalkThreads, 0, s>>>(a, n_rows, none, 0);
+    else k_tree_walk<16, false><<<blocks, kWalkThreads, 0, s>>>(a, n_rows, none, 0);
 }
 void launch_part_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s) {
     count_launch();

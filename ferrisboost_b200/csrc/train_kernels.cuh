@@ -244,7 +244,10 @@ void launch_leaf_final(const LevelArgs& a, uint32_t max_chunks, cudaStream_t s);
 // Every local row walks the finished tree (a.trec / a.tcats) on its record's
 // bins and adds its leaf's value to its margin (training/mod.rs:5020-5063,
 // one addition per row per tree as in the partition path).
-void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s);
+// next_grad: also the next round's gradient pairs and their bounds from the
+// new margins (gmode as launch_gradient_max's mode); null: the walk alone.
+void launch_tree_walk(const LevelArgs& a, uint32_t n_rows, cudaStream_t s, const GradArgs* next_grad = nullptr,
+                      int gmode = 0);
 void launch_tree_init(const LevelArgs& a, uint32_t n_local, uint32_t n_global, const unsigned long long* root_sum,
                       cudaStream_t s);
 void launch_iota(uint32_t* rows, uint32_t n, cudaStream_t s);
