@@ -720,7 +720,14 @@ void per_class(Model& m, int device, const float* X, uint64_t n, size_t width, f
     fbg::DevMem xd, od;
     xd.alloc(n * m.n_features * sizeof(float));
     od.alloc(n * width * sizeof(float));
-    FB_CUDA_CHECK(cudaMemcpy(xd.p, X, n * m.n_features * sizeof(float), cudaMemcpyHostToDevice));
+    // The class models run on their own non-blocking streams, which do not
+    // wait for the legacy default stream, and a plain cudaMemcpy from pageable
+    // memory may return before its DMA has landed.  So the rows go up on the
+    // first class's stream, and that stream is drained before any class reads
+    // them.
+    cudaStream_t s0 = m.dev_class[0]->impl.stream();
+    FB_CUDA_CHECK(cudaMemcpyAsync(xd.p, X, n * m.n_features * sizeof(float), cudaMemcpyHostToDevice, s0));
+    FB_CUDA_CHECK(cudaStreamSynchronize(s0));
     for (size_t k = 0; k < K; k++) {
         fbg::ExplainModel& e = m.dev_class[k]->impl;
         run(e, xd.as<float>(), od.as<float>(), e.stream());

@@ -128,3 +128,24 @@ def test_multiclass_input_errors():
         fb.train(_params(3), X, label=y + 0.5, num_boost_round=1)
     with pytest.raises(ValueError, match="integers"):
         fb.train(_params(2), X, label=y, num_boost_round=1)  # label 2 with num_class 2
+
+
+def test_repeated_predictions_on_alternating_rows_agree():
+    """The rows of a multiclass prediction go to the device once and every
+    class's model reads them on its own stream: each call must see its own
+    rows, also when the device block it gets last held another call's rows."""
+    K = 3
+    X, y, _ = fixture(40_000, 8, K, seed=4)
+    m = fb.train(_params(K), X, label=y, num_boost_round=4)
+    rng = np.random.default_rng(11)
+    X2 = rng.standard_normal(X.shape).astype(np.float32)
+    first = {0: m.predict(X, output_margin=True), 1: m.predict(X2, output_margin=True)}
+    for i in range(12):
+        which = i % 2
+        got = m.predict(X2 if which else X, output_margin=True)
+        assert np.array_equal(got, first[which]), f"call {i}"
+    # the probabilities are the softmax of the same call's margins
+    prob = m.predict(X)
+    e = np.exp((first[0] - first[0].max(axis=1, keepdims=True)).astype(np.float32))
+    want = e / e.astype(np.float64).sum(axis=1, keepdims=True).astype(np.float32)
+    np.testing.assert_allclose(prob, want, rtol=2e-6, atol=1e-7)
